@@ -1,0 +1,552 @@
+#!/usr/bin/env python3
+"""bench.py — throughput of the quantized-weight hot path on B200.
+
+One step = one E2B-shape quantized decode pass at M=1 token: every MATMUL_Q call
+of the 35 decoder layers at the BASELINE config-2 bit widths (I8 q/k/v/o and
+PLE gate/projection, 4-bit gate+up fused with GeGLU, 2-bit down) plus the I8
+lm_head [262144, 1536] with the logit soft-cap 30 fused. Synthetic seeded
+weights (uniform codes, scales ~U(0.005, 0.02)) and N(0,1) activations; the
+weights (~1.12 GB) are far larger than L2, so no flush is needed between steps.
+
+The step is recorded once through the C ABI (gq_graph_begin/end) and replayed.
+`value` is device-timed (CUDA events on the library's stream, inputs resident);
+`e2e` adds, every step, the host->device copy of the step's input activation
+from pinned memory and the device->host read of the step's logits, all through
+the same C ABI. Multi-GPU (torchrun): every rank runs an independent decode
+stream on its own weights (weak scaling, no collective on the data path);
+timings are the max over ranks.
+
+`--impl reference` times the CPU oracle — the C restatement of the reference's
+Rust CPU backend (oracle/gq_oracle.c) — on a bounded sample of the same step
+with all host threads.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "gemma-4-webgpu-kernels_b200"))
+sys.path.insert(0, ROOT)
+
+import numpy as np  # noqa: E402
+
+METRIC = "MATMUL_Q decode GB/s (E2B quantized decode step, M=1)"
+UNIT = "GB/s"
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["gq", "reference"], default="gq")
+    ap.add_argument("--m", type=int, default=1, help="tokens per step (decode batch)")
+    ap.add_argument("--no-extras", action="store_true", help="skip the per-config sub-measurements")
+    return ap.parse_args()
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+# ---- the decode-step workload -------------------------------------------------
+
+class DecodeStep:
+    """All MATMUL_Q calls of one E2B decode step, with pre-bound C-ABI arguments."""
+
+    def __init__(self, g, m: int, seed: int, with_lm_head: bool = True):
+        import torch
+        from gq import synth
+
+        self.g, self.m = g, m
+        lib, ctx = g.lib, g.ctx
+        dev = g.torch_device
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(seed)
+
+        def f32(*shape):
+            return torch.randn(*shape, generator=gen, device=dev, dtype=torch.float32)
+
+        self.x_hidden = f32(m, synth.HIDDEN)
+        self.x_attn = f32(m, synth.HEADS_Q * synth.HEAD_DIM_GLOBAL)
+        self.x_inter = f32(m, synth.INTER)
+        self.x_ple_in = f32(m, synth.PLE_DIM)
+        self.ple = f32(m, synth.LAYERS * synth.PLE_DIM)
+        self.keep = []
+        self.calls = []   # (label, fn, args, bytes)
+        self.bytes = 0
+        self.host_weights = {}
+        wseed = seed * 1000
+
+        def qweight(n, k, bits, signed):
+            nonlocal wseed
+            wseed += 1
+            rb = k if signed else k * bits // 8
+            payload = torch.randint(0, 256, (n * rb,), generator=gen, device=dev, dtype=torch.uint8)
+            scales = synth.uniform(wseed, n, 0.005, 0.02)
+            torch.cuda.synchronize(dev)
+            t = g.quant_tensor_from_device(payload, scales, (n, k), bits, signed, k)
+            return t, payload, scales
+
+        from ctypes import c_float, c_void_p
+        for i in range(synth.LAYERS):
+            for p in synth.layer_projections(i):
+                t, payload, scales = qweight(p.n, p.k, p.bits, p.signed)
+                if i in (0, 4):  # host copies of one local + one global layer (CPU sample)
+                    self.host_weights[(i, p.name, 0)] = (payload.cpu().numpy(), scales, p)
+                x = {synth.HIDDEN: self.x_hidden, synth.INTER: self.x_inter, synth.PLE_DIM: self.x_ple_in}.get(p.k)
+                if x is None:
+                    x = self.x_attn[:, : p.k].contiguous()
+                    self.keep.append(x)
+                y = torch.empty(m, p.n, device=dev, dtype=torch.float32)
+                self.keep += [t, y]
+                b = synth.proj_bytes(p, m)
+                self.bytes += b
+                if p.mode == 1:
+                    t2, payload2, scales2 = qweight(p.n, p.k, p.bits, p.signed)
+                    if i in (0, 4):
+                        self.host_weights[(i, p.name, 1)] = (payload2.cpu().numpy(), scales2, p)
+                    self.keep.append(t2)
+                    self.calls.append((p.name, lib.gq_linear_geglu,
+                                       (ctx, c_void_p(x.data_ptr()), m, p.k, c_void_p(t.qw), c_void_p(t2.qw),
+                                        c_void_p(y.data_ptr())), b, p))
+                elif p.mode == 2:
+                    self.calls.append((p.name, lib.gq_linear_gelu_mul_cols,
+                                       (ctx, c_void_p(x.data_ptr()), m, p.k, c_void_p(t.qw),
+                                        c_void_p(self.ple.data_ptr()), self.ple.shape[1], i * synth.PLE_DIM,
+                                        c_void_p(y.data_ptr())), b, p))
+                else:
+                    self.calls.append((p.name, lib.gq_linear,
+                                       (ctx, c_void_p(x.data_ptr()), m, p.k, c_void_p(t.qw), c_void_p(y.data_ptr())),
+                                       b, p))
+                self.last_out = y
+        if with_lm_head:
+            p = synth.Proj("lm_head", synth.VOCAB, synth.HIDDEN, 8, True)
+            t, payload, scales = qweight(p.n, p.k, 8, True)
+            self.logits = torch.empty(m, p.n, device=dev, dtype=torch.float32)
+            self.keep += [t, self.logits]
+            b = synth.proj_bytes(p, m)
+            self.bytes += b
+            self.calls.append(("lm_head", lib.gq_linear_softcap,
+                               (ctx, c_void_p(self.x_hidden.data_ptr()), m, p.k, c_void_p(t.qw), c_float(30.0),
+                                c_void_p(self.logits.data_ptr()), p.n, 0), b, p))
+            self.last_out = self.logits
+        self.launches = len(self.calls)
+
+    def run(self):
+        for label, fn, args, _, _ in self.calls:
+            rc = fn(*args)
+            if rc != 0:
+                self.g._check(rc, label)
+
+
+def cuda_events_time(torch, stream, fn, iters):
+    s = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    s.record(stream)
+    for _ in range(iters):
+        fn()
+    e.record(stream)
+    e.synchronize()
+    return s.elapsed_time(e)
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.dev = device_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
+                 "-i", str(self.dev)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def cpu_sample(step: DecodeStep, min_seconds: float = 10.0):
+    """Time the oracle (all host threads) on layers 0 and 4 of the step."""
+    from oracle import oracle
+    from gq import QuantWeight, synth
+
+    xs = {synth.HIDDEN: step.x_hidden.cpu().numpy(), synth.INTER: step.x_inter.cpu().numpy(),
+          synth.PLE_DIM: step.x_ple_in.cpu().numpy()}
+    xa = step.x_attn.cpu().numpy()
+    ple = step.ple.cpu().numpy()
+    work = []
+    nbytes = 0
+    byname = {}
+    for (i, name, h), (payload, scales, p) in sorted(step.host_weights.items()):
+        q = QuantWeight(payload, scales, (p.n, p.k), p.bits, p.signed, p.k)
+        byname.setdefault((i, name), [None, None, p])[h] = q
+    for (i, name), (q0, q1, p) in sorted(byname.items()):
+        x = xs.get(p.k, xa[:, : p.k])
+        x = np.ascontiguousarray(x)
+        if p.mode == 1:
+            work.append(lambda x=x, a=q0, b=q1: oracle.linear_geglu(x, a, b))
+        elif p.mode == 2:
+            work.append(lambda x=x, a=q0, i=i: oracle.linear_gelu_mul_cols(x, a, ple, i * synth.PLE_DIM))
+        else:
+            work.append(lambda x=x, a=q0: oracle.linear(x, a))
+        nbytes += synth.proj_bytes(p, step.m)
+    for w in work:  # warm-up
+        w()
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        for w in work:
+            w()
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds:
+            break
+    gbs = nbytes * reps / el / 1e9
+    return {"value": gbs, "unit": UNIT, "cores": oracle.default_threads(), "kind": "port",
+            "sample": f"layers 0 and 4 of the step ({len(work)} MATMUL_Q calls, {nbytes / 1e6:.1f} MB), "
+                      f"{reps} reps in {el:.1f} s; C restatement of the reference Rust CPU backend",
+            "seconds": el}
+
+
+def run_gq(args):
+    import torch
+    import torch.distributed as dist
+    from gq import CudaBackend, synth
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=torch.device("cuda", local))
+
+    hbm_peak, bf16_peak, peak_kind = peaks()
+    g = CudaBackend(local, own_stream=True)
+    stream = torch.cuda.ExternalStream(g.stream_ptr(), device=g.torch_device)
+    step = DecodeStep(g, args.m, seed=1234 + rank)
+    g.flush()
+    step.run()  # eager once (also sets kernel attributes before recording)
+    g.flush()
+    graph = g.record(step.run)
+
+    for _ in range(args.warmup):
+        g.replay(graph)
+    g.flush()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        ms_total = cuda_events_time(torch, stream, lambda: g.replay(graph), args.steps)
+    g.flush()
+    ms = ms_total / args.steps
+    t = torch.tensor([ms], device=g.torch_device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_max = float(t.item())
+    value = step.bytes * world / (ms_max / 1e3) / 1e9
+
+    # e2e: pinned host activation in, logits out, through the C ABI, each step.
+    from ctypes import c_void_p
+    hx = torch.randn(step.x_hidden.shape, dtype=torch.float32).pin_memory()
+    hy = torch.empty(step.last_out.shape, dtype=torch.float32).pin_memory()
+    h2d = hx.numel() * 4
+    d2h = hy.numel() * 4
+    lib, ctx = g.lib, g.ctx
+
+    def e2e_step():
+        g._check(lib.gq_memcpy_h2d(ctx, c_void_p(step.x_hidden.data_ptr()), c_void_p(hx.data_ptr()), h2d), "h2d")
+        g.replay(graph)
+        g._check(lib.gq_memcpy_d2h(ctx, c_void_p(hy.data_ptr()), c_void_p(step.last_out.data_ptr()), d2h), "d2h")
+        g.flush()
+
+    for _ in range(max(3, args.warmup // 4)):
+        e2e_step()
+    e2e_steps = max(10, min(args.steps, 500))
+    ms_e2e = cuda_events_time(torch, stream, e2e_step, e2e_steps) / e2e_steps
+    t = torch.tensor([ms_e2e], device=g.torch_device)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_e2e = float(t.item())
+
+    # per-launch durations (events around each launch) for the roofline of the
+    # dominant kernel family (the streaming GEMV)
+    per = [[] for _ in step.calls]
+    for _ in range(5):
+        evs = []
+        for (label, fn, a, b, p) in step.calls:
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            fn(*a)
+            e1.record(stream)
+            evs.append((e0, e1))
+        torch.cuda.synchronize()
+        for j, (e0, e1) in enumerate(evs):
+            per[j].append(e0.elapsed_time(e1))
+    med = [statistics.median(v) for v in per]
+    kern_ms = sum(med)
+    kern_bytes = sum(c[3] for c in step.calls)
+    achieved = kern_bytes / (kern_ms / 1e3) / 1e9
+    lm = [(c, mm) for c, mm in zip(step.calls, med) if c[0] == "lm_head"]
+    by_kind = {}
+    for c, mm in zip(step.calls, med):
+        key = f"{c[4].bits}b{'s' if c[4].signed else ''}_mode{c[4].mode}"
+        d = by_kind.setdefault(key, [0, 0.0, 0])
+        d[0] += c[3]
+        d[1] += mm
+        d[2] += 1
+    traffic = None
+    try:
+        with open(os.path.join(ROOT, "profiles", "gemv_traffic.json")) as f:
+            traffic = json.load(f).get("dram_bytes_per_step")
+    except Exception:
+        pass
+
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_max, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u8/i8 weights, f32 activations+accumulate", "data": "synthetic",
+        "config": {"workload": f"e2b_quantized_decode_step_m{args.m}", "layers": synth.LAYERS,
+                   "tokens_per_step": args.m, "lm_head": "i8 262144x1536 softcap 30",
+                   "bits": "q/k/v/o/ple i8, gate+up 4-bit (geglu fused), down 2-bit",
+                   "bytes_per_step": step.bytes, "l2": "weights 1.12 GB per step >> 126 MB L2; no flush",
+                   "parallelism": f"replicas x{world}" if world > 1 else "single"},
+        "tokens_per_s": round(args.m * world / (ms_max / 1e3), 1),
+        "frac_of_measured_hbm": round(value / world / hbm_peak, 4),
+        "frac_of_8tbs_nominal": round(value / world / 8000.0, 4),
+        "e2e": {"value": round(step.bytes * world / (ms_e2e / 1e3) / 1e9, 2), "unit": UNIT,
+                "ms_per_step": round(ms_e2e, 5), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": step.launches * args.steps,
+        "roofline": {"bound": "hbm", "kernel": "gemv_q (all MATMUL_Q launches of the step, events per launch)",
+                     "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                     "frac": round(achieved / hbm_peak, 4), "peak_kind": peak_kind, "traffic": traffic,
+                     "per_kind": {k: {"GB/s": round(v[0] / (v[1] / 1e3) / 1e9, 1), "launches": v[2],
+                                      "ms": round(v[1], 4)} for k, v in sorted(by_kind.items())}},
+    }
+    if lm:
+        (c, mm), = lm
+        line["lm_head"] = {"ms": round(mm, 4), "GB/s": round(c[3] / (mm / 1e3) / 1e9, 1),
+                           "frac_of_measured_hbm": round(c[3] / (mm / 1e3) / 1e9 / hbm_peak, 4)}
+    line["clocks"] = clk.summary()
+
+    if rank == 0 and world == 1 and not args.no_extras:
+        line["extras"] = extras(g, torch, stream, hbm_peak)
+    if rank == 0 and world == 1:
+        line["cpu_baseline"] = cpu_sample(step, min_seconds=10.0)
+    g.destroy_graph(graph)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    g.close()
+
+
+def extras(g, torch, stream, hbm_peak):
+    """Per-config sub-measurements (2 at M=8, 4)."""
+    from ctypes import c_float, c_void_p
+    from gq import synth
+
+    out = {}
+    lib, ctx = g.lib, g.ctx
+    dev = g.torch_device
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(99)
+
+    # config 1: 4-bit [6144,1536] GEMV, rotating 64 copies (302 MB) to defeat L2
+    copies = []
+    for c in range(64):
+        payload = torch.randint(0, 256, (6144 * 768,), generator=gen, device=dev, dtype=torch.uint8)
+        torch.cuda.synchronize()
+        copies.append(g.quant_tensor_from_device(payload, synth.uniform(500 + c, 6144, 0.005, 0.02), (6144, 1536), 4,
+                                                 False, 1536))
+    x = torch.randn(1, 1536, generator=gen, device=dev)
+    y = torch.empty(1, 6144, device=dev)
+    calls = [(c_void_p(x.data_ptr()), c_void_p(t.qw), c_void_p(y.data_ptr())) for t in copies]
+
+    def rot():
+        for a, w, yy in calls:
+            lib.gq_linear(ctx, a, 1, 1536, w, yy)
+
+    graph = g.record(rot)
+    for _ in range(5):
+        g.replay(graph)
+    reps = 50
+    ms = cuda_events_time(torch, stream, lambda: g.replay(graph), reps) / (reps * len(calls))
+    b = synth.proj_bytes(synth.Proj("c1", 6144, 1536, 4, False), 1)
+    out["config1_gemv_4bit_6144x1536"] = {"us_per_call": round(ms * 1e3, 3), "GB/s": round(b / (ms / 1e3) / 1e9, 1),
+                                          "frac_of_measured_hbm": round(b / (ms / 1e3) / 1e9 / hbm_peak, 4),
+                                          "note": "64 rotating copies, graph-replayed back to back"}
+    g.destroy_graph(graph)
+    for t in copies:
+        g.free_quant(t)
+
+    # config 2 at M=8 (whole step, graph-replayed)
+    step8 = DecodeStep(g, 8, seed=4321, with_lm_head=False)
+    step8.run()
+    g.flush()
+    graph = g.record(step8.run)
+    for _ in range(5):
+        g.replay(graph)
+    ms = cuda_events_time(torch, stream, lambda: g.replay(graph), 50) / 50
+    out["config2_sweep_m8"] = {"ms_per_step": round(ms, 4), "GB/s": round(step8.bytes / (ms / 1e3) / 1e9, 1),
+                               "bytes_per_step": step8.bytes}
+    g.destroy_graph(graph)
+    for t in step8.keep:
+        if getattr(t, "qw", None):
+            g.free_quant(t)
+    del step8
+
+    # config 4: EMBED_Q of 4096 ids over the 4-bit token table and the I8 PLE table
+    V, T = synth.VOCAB, 4096
+    tok = torch.randint(0, 256, (V * 768,), generator=gen, device=dev, dtype=torch.uint8)
+    plet = torch.randint(0, 256, (V * 8960,), generator=gen, device=dev, dtype=torch.uint8)
+    torch.cuda.synchronize()
+    t_tok = g.quant_tensor_from_device(tok, synth.uniform(601, V, 0.005, 0.02), (V, 1536), 4, False, 1536)
+    t_ple = g.quant_tensor_from_device(plet, synth.uniform(602, V * 35, 0.005, 0.02), (V, 8960), 8, True, 256)
+    del tok, plet
+    ids = torch.from_numpy(synth.int_codes(603, T, 0, V - 1).astype(np.int32)).to(dev)
+    o_tok = torch.empty(T, 1536, device=dev)
+    o_ple = torch.empty(T, 8960, device=dev)
+
+    def emb():
+        lib.gq_embed_rows(ctx, c_void_p(t_tok.qw), c_void_p(ids.data_ptr()), T, c_float(39.191835), c_void_p(o_tok.data_ptr()))
+        lib.gq_embed_rows(ctx, c_void_p(t_ple.qw), c_void_p(ids.data_ptr()), T, c_float(16.0), c_void_p(o_ple.data_ptr()))
+
+    emb()
+    g.flush()
+    graph = g.record(emb)
+    for _ in range(5):
+        g.replay(graph)
+    ms = cuda_events_time(torch, stream, lambda: g.replay(graph), 50) / 50
+    b = T * 768 + T * 4 + T * 1536 * 4 + T * 8960 + T * 35 * 4 + T * 8960 * 4 + T * 4
+    out["config4_embed_q_ple"] = {"us_per_step": round(ms * 1e3, 2), "GB/s": round(b / (ms / 1e3) / 1e9, 1),
+                                  "frac_of_measured_hbm": round(b / (ms / 1e3) / 1e9 / hbm_peak, 4),
+                                  "bytes": b}
+    g.destroy_graph(graph)
+    g.free_quant(t_tok)
+    g.free_quant(t_ple)
+    g.flush()
+    return out
+
+
+def run_reference(args):
+    """The reference arm: the CPU oracle on a bounded sample of the same step."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle import oracle
+    from gq import QuantWeight, synth
+
+    m = args.m
+    layers = (0, 4)
+    rng_x = {k: synth.normal(10 + k, m * k).reshape(m, k) for k in
+             (synth.HIDDEN, synth.INTER, synth.PLE_DIM, synth.HEADS_Q * synth.HEAD_DIM_GLOBAL,
+              synth.HEADS_Q * synth.HEAD_DIM_LOCAL)}
+    ple = synth.normal(20, m * synth.LAYERS * synth.PLE_DIM).reshape(m, -1)
+    work, nbytes, seed = [], 0, 7000
+    for i in layers:
+        for p in synth.layer_projections(i):
+            seed += 1
+            q = synth.random_qweight(seed, p.n, p.k, p.bits, p.signed)
+            x = rng_x[p.k]
+            if p.mode == 1:
+                q2 = synth.random_qweight(seed + 500, p.n, p.k, p.bits, p.signed)
+                work.append(lambda x=x, a=q, b=q2: oracle.linear_geglu(x, a, b))
+            elif p.mode == 2:
+                work.append(lambda x=x, a=q, i=i: oracle.linear_gelu_mul_cols(x, a, ple, i * synth.PLE_DIM))
+            else:
+                work.append(lambda x=x, a=q: oracle.linear(x, a))
+            nbytes += synth.proj_bytes(p, m)
+    for w in work:
+        w()
+    times = []
+    steps = max(1, min(args.steps, 20))
+    for _ in range(max(0, min(args.warmup, 2))):
+        for w in work:
+            w()
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        for w in work:
+            w()
+        times.append(time.perf_counter() - t0)
+    sec = statistics.median(times)
+    value = nbytes / sec / 1e9
+    sample = (f"layers {layers} of the E2B quantized decode step at M={m} ({len(work)} MATMUL_Q calls, "
+              f"{nbytes / 1e6:.1f} MB); C restatement of the reference Rust CPU backend, median of {steps}")
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": args.gpus, "steps": steps,
+        "warmup": args.warmup, "ms_per_step": round(sec * 1e3, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "u8/i8 weights, f32 activations+accumulate", "data": "synthetic",
+        "config": {"workload": f"e2b_quantized_decode_step_m{m}", "sampled_layers": list(layers)},
+        "impl": "reference",
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": oracle.default_threads(), "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gq(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,158 @@
+/*
+ * gq.h — C ABI of the B200 quantized-weight backend (libgq.so).
+ *
+ * This is the drop-in boundary for the quantized-weight hot path of the Gemma-4
+ * engine in Dhruba531/gemma-4-webgpu-kernels. Each entry point replaces one
+ * method of the Rust `Backend` trait (rust/src/backend.rs:88-180) for quantized
+ * tensors; a Rust `CudaBackend` binds these symbols through `extern "C"` (see
+ * INTEGRATION.md) and maps a non-zero status to `panic!`, which is what the
+ * trait's infallible signatures do today.
+ *
+ * Conventions
+ *  - Every function returns an int status (GQ_OK == 0). Nothing aborts or traps.
+ *  - Activation/output pointers are DEVICE pointers owned by the caller. A
+ *    gq_qweight owns its device copy of the packed bytes and scales until
+ *    gq_qweight_free (the reference's ownership rule, backend_wgpu.rs:25-35).
+ *  - All work is enqueued on the context's stream and returns immediately, like
+ *    the reference's recorded dispatches; gq_sync / gq_readback block
+ *    (backend.rs:169-173).
+ *  - One host thread per context (the reference backend is !Sync).
+ *  - f32 tensors are dense row-major. Outputs are fully overwritten; nothing
+ *    relies on zeroed buffers (backend_wgpu.rs:380-383).
+ *  - Kernel-detected errors (an embedding id >= rows, a pipeline wait that
+ *    timed out) set a device status word; the next gq_sync returns
+ *    GQ_ERR_DEVICE and gq_last_error says which.
+ */
+#ifndef GQ_H
+#define GQ_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GQ_ABI_VERSION 1
+
+typedef enum gq_status {
+  GQ_OK = 0,
+  GQ_ERR_INVALID_ARGUMENT = 1, /* null pointer, bad shape, K mismatch, bad offset */
+  GQ_ERR_UNSUPPORTED = 2,      /* bits not in {2,4,8}, K not a multiple of values/byte */
+  GQ_ERR_CUDA = 3,             /* CUDA runtime error; text in gq_last_error */
+  GQ_ERR_OUT_OF_MEMORY = 4,
+  GQ_ERR_DEVICE = 5            /* a kernel reported an error (see gq_last_error) */
+} gq_status;
+
+/* Device status bits reported through GQ_ERR_DEVICE. */
+#define GQ_DEVERR_BAD_ID 0x1u       /* embed id >= table rows (output row zeroed) */
+#define GQ_DEVERR_WAIT_TIMEOUT 0x2u /* a bounded pipeline wait gave up */
+
+typedef struct gq_ctx gq_ctx;         /* device + stream + error word + workspace */
+typedef struct gq_qweight gq_qweight; /* packed weight resident on the device */
+typedef struct gq_graph gq_graph;     /* a recorded, replayable sequence of ops */
+
+int gq_abi_version(void);
+const char *gq_status_string(int status);
+
+/* ---- context: replaces WgpuBackend::create (rust/src/backend_wgpu.rs:239-300) */
+int gq_ctx_create(int device, gq_ctx **out);
+int gq_ctx_destroy(gq_ctx *ctx);
+/* Use the caller's cudaStream_t (e.g. torch's current stream); NULL restores the
+ * context's own stream. */
+int gq_ctx_set_stream(gq_ctx *ctx, void *cuda_stream);
+void *gq_ctx_get_stream(gq_ctx *ctx);
+/* Number of SMs of the context's device (grid sizing; reported by bench tools). */
+int gq_ctx_num_sms(gq_ctx *ctx);
+const char *gq_last_error(gq_ctx *ctx);
+
+/* ---- sync / memory: replaces Backend::{tensor, zeros, readback, flush,
+ *      free_tensor} (rust/src/backend.rs:94-96, :169-179) */
+int gq_sync(gq_ctx *ctx);
+int gq_alloc(gq_ctx *ctx, size_t bytes, void **dptr);
+int gq_free(gq_ctx *ctx, void *dptr);
+int gq_memcpy_h2d(gq_ctx *ctx, void *dst_dev, const void *src_host, size_t bytes);
+int gq_memcpy_d2h(gq_ctx *ctx, void *dst_host, const void *src_dev, size_t bytes);
+int gq_memset(gq_ctx *ctx, void *dst_dev, int value, size_t bytes);
+/* Blocking f32 read (Backend::readback, rust/src/backend.rs:171). */
+int gq_readback(gq_ctx *ctx, float *dst_host, const float *src_dev, size_t count);
+
+/* ---- weights: replaces Backend::quant_tensor (rust/src/backend.rs:95;
+ *      wgpu upload at rust/src/backend_wgpu.rs:442-456). Arguments mirror
+ *      QuantWeight (rust/src/backend.rs:16-24): qbytes are the raw payload
+ *      (U8 sub-byte packed LSB-first offset-binary, or native I8), scales are
+ *      one f32 per (row, group), shape [n, k]. Host pointers; copied. */
+int gq_qweight_upload(gq_ctx *ctx, const uint8_t *qbytes, size_t nbytes, const float *scales,
+                      size_t nscales, int64_t n, int64_t k, int32_t bits, int32_t signed_i8,
+                      int64_t group_size, gq_qweight **out);
+/* Same, with the packed bytes already in DEVICE memory (copied device to
+ * device; scales are host f32) — WgpuBackend::quant_tensor_from_gpu
+ * (rust/src/backend_wgpu.rs:447-456), used when the payload was streamed to the
+ * GPU by another path. */
+int gq_qweight_upload_device(gq_ctx *ctx, const uint8_t *qbytes_dev, size_t nbytes,
+                             const float *scales, size_t nscales, int64_t n, int64_t k,
+                             int32_t bits, int32_t signed_i8, int64_t group_size,
+                             gq_qweight **out);
+int gq_qweight_free(gq_qweight *w);
+/* Shape/format of an uploaded weight (any out pointer may be NULL). */
+int gq_qweight_info(const gq_qweight *w, int64_t *n, int64_t *k, int32_t *bits,
+                    int32_t *signed_i8, int64_t *group_size);
+
+/* ---- record / replay: the reference records every op of a forward pass into
+ *      one command encoder and submits it at flush (rust/src/backend_wgpu.rs:
+ *      11-15, :562-594). Here the ops issued between gq_graph_begin and
+ *      gq_graph_end are captured from the context's stream into a CUDA graph
+ *      that gq_graph_launch replays with one call. The context's stream must be
+ *      a non-default stream while recording (the context's own stream is). No
+ *      synchronising call (gq_sync, gq_readback, uploads) may be made while
+ *      recording. */
+int gq_graph_begin(gq_ctx *ctx);
+int gq_graph_end(gq_ctx *ctx, gq_graph **out);
+int gq_graph_launch(gq_ctx *ctx, gq_graph *graph);
+int gq_graph_destroy(gq_graph *graph);
+
+/* ---- ops. x is [m, k] f32, y is [m, w.n] f32, all device pointers. */
+
+/* Backend::linear (rust/src/backend.rs:105-106): y = x · deq(W)ᵀ. The wgpu
+ * backend dispatches MATMUL_Q / MATMUL_Q_TILED / MATMUL_Q_SCALAR here
+ * (rust/src/backend_wgpu.rs:768-806). */
+int gq_linear(gq_ctx *ctx, const float *x, int64_t m, int64_t k, const gq_qweight *w,
+              float *y);
+
+/* Backend::linear_geglu (rust/src/backend.rs:155-160; MODE 1 at
+ * rust/src/backend_wgpu.rs:808-821): y = gelu_tanh(x·Wgᵀ) * (x·Wuᵀ). */
+int gq_linear_geglu(gq_ctx *ctx, const float *x, int64_t m, int64_t k, const gq_qweight *wg,
+                    const gq_qweight *wu, float *y);
+
+/* Backend::linear_gelu_mul_cols (rust/src/backend.rs:161-167; MODE 2 at
+ * rust/src/backend_wgpu.rs:823-835): y = gelu_tanh(x·Wᵀ) * b[:, off:off+n],
+ * b is [m, b_stride] f32. */
+int gq_linear_gelu_mul_cols(gq_ctx *ctx, const float *x, int64_t m, int64_t k,
+                            const gq_qweight *w, const float *b, int64_t b_stride,
+                            int64_t b_offset, float *y);
+
+/* lm_head with the final logit soft-cap fused: the composition
+ * softcap(linear(x, lm_head), cap) of rust/src/model.rs:192 and
+ * Backend::softcap (rust/src/backend.rs:116). cap <= 0 means no cap. The
+ * output row stride is ldy floats and the n results of each row are written at
+ * column y_col0 (a vocab shard writing into its slice of the full logits). */
+int gq_linear_softcap(gq_ctx *ctx, const float *x, int64_t m, int64_t k, const gq_qweight *w,
+                      float cap, float *y, int64_t ldy, int64_t y_col0);
+
+/* Backend::embed_rows for a quantized table (rust/src/backend.rs:101-102;
+ * CPU rust/src/backend_cpu.rs:127-137, wgpu EMBED_Q at
+ * rust/src/backend_wgpu.rs:734-754): out[i, d] = deq(table, ids[i], d) * scale.
+ * ids is a DEVICE array of t u32. An id >= table rows zeroes that output row
+ * and raises GQ_DEVERR_BAD_ID at the next gq_sync. */
+int gq_embed_rows(gq_ctx *ctx, const gq_qweight *table, const uint32_t *ids, int64_t t,
+                  float scale, float *out);
+
+/* Backend::softcap / geglu / gelu_tanh (rust/src/backend.rs:112-116) on n
+ * f32 elements. */
+int gq_softcap(gq_ctx *ctx, const float *x, int64_t n, float cap, float *y);
+int gq_geglu(gq_ctx *ctx, const float *gate, const float *up, int64_t n, float *y);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GQ_H */

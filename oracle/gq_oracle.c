@@ -1,0 +1,283 @@
+/*
+ * gq_oracle.c — CPU restatement of the reference's quantized-weight path.
+ * TEST INFRASTRUCTURE ONLY (see gq_oracle.h): the checker, never the product.
+ *
+ * Every function cites the Rust function it restates (paths relative to
+ * Dhruba531/gemma-4-webgpu-kernels). Compiled with -ffp-contract=off so each
+ * `a * b` and `+` rounds separately, as the Rust code does.
+ */
+#include "gq_oracle.h"
+
+#include <math.h>
+#include <pthread.h>
+#include <stdlib.h>
+#include <string.h>
+#include <unistd.h>
+
+/* rust/src/backend.rs:28-30 */
+int64_t gqo_per_byte(const gqo_qweight *w) { return w->signed_i8 ? 1 : (8 / w->bits); }
+
+/* rust/src/backend.rs:33-36 */
+int64_t gqo_row_bytes(const gqo_qweight *w) {
+  return w->signed_i8 ? w->k : w->k / gqo_per_byte(w);
+}
+
+/* rust/src/backend.rs:39-41 (div_ceil) */
+int64_t gqo_scale_stride(const gqo_qweight *w) {
+  return (w->k + w->group_size - 1) / w->group_size;
+}
+
+/* rust/src/backend.rs:46-54: the integer part of deq. Sub-byte and unsigned
+ * 8-bit codes are offset binary (raw - 2^(bits-1)); I8 is two's complement. */
+int32_t gqo_code(const gqo_qweight *w, int64_t n, int64_t k) {
+  if (w->signed_i8) {
+    return (int32_t)(int8_t)w->qbytes[n * gqo_row_bytes(w) + k];
+  }
+  int64_t per_byte = gqo_per_byte(w);
+  uint32_t b = w->qbytes[n * gqo_row_bytes(w) + k / per_byte];
+  uint32_t shift = (uint32_t)(k % per_byte) * (uint32_t)w->bits;
+  return (int32_t)((b >> shift) & ((1u << w->bits) - 1u)) - (1 << (w->bits - 1));
+}
+
+/* rust/src/backend.rs:45-56 */
+float gqo_deq(const gqo_qweight *w, int64_t n, int64_t k) {
+  return (float)gqo_code(w, n, k) * w->scales[n * gqo_scale_stride(w) + k / w->group_size];
+}
+
+/* rust/src/dequant.rs:16-33 */
+void gqo_unpack_int(const uint8_t *bytes, int32_t bits, size_t count, int32_t *out) {
+  if (bits == 8) {
+    for (size_t i = 0; i < count; i++) out[i] = (int32_t)(int8_t)bytes[i];
+    return;
+  }
+  size_t per_byte = (size_t)(8 / bits);
+  uint32_t mask = (1u << bits) - 1u;
+  int32_t zp = 1 << (bits - 1);
+  for (size_t i = 0; i < count; i++) {
+    uint32_t byte = bytes[i / per_byte];
+    uint32_t shift = (uint32_t)(i % per_byte) * (uint32_t)bits;
+    out[i] = (int32_t)((byte >> shift) & mask) - zp;
+  }
+}
+
+/* rust/src/dequant.rs:37-50 */
+size_t gqo_pack_int(const int32_t *values, size_t count, int32_t bits, uint8_t *out) {
+  if (bits == 8) {
+    for (size_t i = 0; i < count; i++) out[i] = (uint8_t)values[i];
+    return count;
+  }
+  size_t per_byte = (size_t)(8 / bits);
+  int32_t mask = (1 << bits) - 1;
+  int32_t zp = 1 << (bits - 1);
+  size_t nb = (count + per_byte - 1) / per_byte;
+  memset(out, 0, nb);
+  for (size_t i = 0; i < count; i++) {
+    uint32_t shift = (uint32_t)(i % per_byte) * (uint32_t)bits;
+    out[i / per_byte] |= (uint8_t)(((values[i] + zp) & mask) << shift);
+  }
+  return nb;
+}
+
+/* rust/src/dequant.rs:53-62 */
+size_t gqo_pack_unsigned(const uint32_t *values, size_t count, int32_t bits, uint8_t *out) {
+  size_t per_byte = (size_t)(8 / bits);
+  uint32_t mask = (1u << bits) - 1u;
+  size_t nb = (count + per_byte - 1) / per_byte;
+  memset(out, 0, nb);
+  for (size_t i = 0; i < count; i++) {
+    uint32_t shift = (uint32_t)(i % per_byte) * (uint32_t)bits;
+    out[i / per_byte] |= (uint8_t)((values[i] & mask) << shift);
+  }
+  return nb;
+}
+
+/* rust/src/dequant.rs:65-75 */
+void gqo_dequantize(const int32_t *q, const float *scales, size_t rows, size_t cols,
+                    size_t group_size, float *out) {
+  size_t groups_per_row = (cols + group_size - 1) / group_size;
+  for (size_t r = 0; r < rows; r++)
+    for (size_t c = 0; c < cols; c++)
+      out[r * cols + c] = (float)q[r * cols + c] * scales[r * groups_per_row + c / group_size];
+}
+
+/* rust/src/backend_cpu.rs:72-78: GEMMA_CPU_THREADS, else the core count. */
+int32_t gqo_default_threads(void) {
+  const char *e = getenv("GEMMA_CPU_THREADS");
+  if (e && *e) {
+    char *end = NULL;
+    long v = strtol(e, &end, 10);
+    if (end && *end == '\0' && v >= 1) return (int32_t)v;
+  }
+  long n = sysconf(_SC_NPROCESSORS_ONLN);
+  return n >= 1 ? (int32_t)n : 1;
+}
+
+/* ---- par_ranges: rust/src/backend_cpu.rs:63-91 ------------------------- */
+
+#define PAR_MIN_WORK (1u << 14)
+
+typedef void (*range_fn)(void *ctx, int64_t start, int64_t end);
+typedef struct {
+  range_fn f;
+  void *ctx;
+  int64_t start, end;
+} range_job;
+
+static void *range_thread(void *p) {
+  range_job *j = (range_job *)p;
+  j->f(j->ctx, j->start, j->end);
+  return NULL;
+}
+
+/* Contiguous chunks of ceil(n/threads) rows, one scoped thread each. Each chunk
+ * owns disjoint output rows, so results do not depend on the thread count. */
+static void par_ranges(int64_t n, uint64_t work, int32_t threads, range_fn f, void *ctx) {
+  if (threads <= 0) threads = gqo_default_threads();
+  if (threads > n) threads = (int32_t)n;
+  if (threads < 1) threads = 1;
+  if (threads == 1 || work < PAR_MIN_WORK) {
+    f(ctx, 0, n);
+    return;
+  }
+  int64_t chunk = (n + threads - 1) / threads;
+  int64_t njobs = (n + chunk - 1) / chunk;
+  pthread_t *tid = (pthread_t *)calloc((size_t)njobs, sizeof(pthread_t));
+  range_job *jobs = (range_job *)calloc((size_t)njobs, sizeof(range_job));
+  int *started = (int *)calloc((size_t)njobs, sizeof(int));
+  for (int64_t i = 0; i < njobs; i++) {
+    jobs[i].f = f;
+    jobs[i].ctx = ctx;
+    jobs[i].start = i * chunk;
+    jobs[i].end = (i + 1) * chunk < n ? (i + 1) * chunk : n;
+    started[i] = pthread_create(&tid[i], NULL, range_thread, &jobs[i]) == 0;
+    if (!started[i]) range_thread(&jobs[i]); /* no thread: run inline */
+  }
+  for (int64_t i = 0; i < njobs; i++)
+    if (started[i]) pthread_join(tid[i], NULL);
+  free(started);
+  free(jobs);
+  free(tid);
+}
+
+/* ---- linear: rust/src/backend_cpu.rs:174-222 ---------------------------- */
+
+typedef struct {
+  const float *x;
+  int64_t t, k;
+  const gqo_qweight *w; /* NULL for the f32 branch */
+  const float *wf;      /* f32 weight [n,k] */
+  float *out_t;         /* [n, t] transposed result */
+} linear_ctx;
+
+static void linear_rows(void *p, int64_t start, int64_t end) {
+  linear_ctx *c = (linear_ctx *)p;
+  const int64_t k = c->k, tt = c->t;
+  float *row = (float *)malloc((size_t)(k > 0 ? k : 1) * sizeof(float));
+  for (int64_t nn = start; nn < end; nn++) {
+    const float *wb;
+    if (c->w) {
+      /* dequantize the weight row once, reuse for every input row */
+      for (int64_t kk = 0; kk < k; kk++) row[kk] = gqo_deq(c->w, nn, kk);
+      wb = row;
+    } else {
+      wb = c->wf + nn * k;
+    }
+    for (int64_t i = 0; i < tt; i++) {
+      const float *xb = c->x + i * k;
+      float acc = 0.0f;
+      for (int64_t kk = 0; kk < k; kk++) acc += xb[kk] * wb[kk];
+      c->out_t[nn * tt + i] = acc;
+    }
+  }
+  free(row);
+}
+
+static int32_t linear_impl(const float *x, int64_t t, int64_t k, const gqo_qweight *w,
+                           const float *wf, int64_t n, float *y, int32_t threads) {
+  if (t < 0 || k < 0 || n < 0) return -1;
+  if (t == 0 || n == 0) return 0;
+  float *out_t = (t == 1) ? y : (float *)malloc((size_t)(n * t) * sizeof(float));
+  linear_ctx c = {x, t, k, w, wf, out_t};
+  par_ranges(n, (uint64_t)n * (uint64_t)k * (uint64_t)t, threads, linear_rows, &c);
+  if (t != 1) {
+    for (int64_t nn = 0; nn < n; nn++)
+      for (int64_t i = 0; i < t; i++) y[i * n + nn] = out_t[nn * t + i];
+    free(out_t);
+  }
+  return 0;
+}
+
+int32_t gqo_linear(const float *x, int64_t t, int64_t k, const gqo_qweight *w, float *y,
+                   int32_t threads) {
+  if (!w || w->k != k) return -1;
+  return linear_impl(x, t, k, w, NULL, w->n, y, threads);
+}
+
+int32_t gqo_linear_f32(const float *x, int64_t t, int64_t k, const float *w, int64_t n,
+                       float *y, int32_t threads) {
+  return linear_impl(x, t, k, NULL, w, n, y, threads);
+}
+
+/* ---- embed_rows: rust/src/backend_cpu.rs:127-137 ------------------------ */
+int32_t gqo_embed_rows(const gqo_qweight *table, const uint32_t *ids, int64_t t, float scale,
+                       float *out) {
+  const int64_t d = table->k;
+  for (int64_t i = 0; i < t; i++)
+    if ((int64_t)ids[i] >= table->n) return -1;
+  for (int64_t i = 0; i < t; i++)
+    for (int64_t dd = 0; dd < d; dd++)
+      out[i * d + dd] = gqo_deq(table, (int64_t)ids[i], dd) * scale;
+  return 0;
+}
+
+/* ---- elementwise: rust/src/backend_cpu.rs:55-58, 239-244, 343-350 ------- */
+float gqo_gelu_tanh(float v) {
+  const float c = sqrtf(2.0f / (float)M_PI);
+  return 0.5f * v * (1.0f + tanhf(c * (v + 0.044715f * v * v * v)));
+}
+
+void gqo_geglu(const float *gate, const float *up, size_t n, float *out) {
+  for (size_t i = 0; i < n; i++) out[i] = gqo_gelu_tanh(gate[i]) * up[i];
+}
+
+void gqo_softcap(const float *x, size_t n, float cap, float *out) {
+  for (size_t i = 0; i < n; i++) out[i] = cap * tanhf(x[i] / cap);
+}
+
+void gqo_slice_cols(const float *x, int64_t rows, int64_t stride, int64_t offset, int64_t width,
+                    float *out) {
+  for (int64_t r = 0; r < rows; r++)
+    memcpy(out + r * width, x + r * stride + offset, (size_t)width * sizeof(float));
+}
+
+/* ---- fused-op compositions: rust/src/backend.rs:155-167 ------------------ */
+int32_t gqo_linear_geglu(const float *x, int64_t t, int64_t k, const gqo_qweight *wg,
+                         const gqo_qweight *wu, float *y, int32_t threads) {
+  if (!wg || !wu || wg->n != wu->n) return -1;
+  size_t cnt = (size_t)(t * wg->n);
+  float *g = (float *)malloc((cnt ? cnt : 1) * sizeof(float));
+  float *u = (float *)malloc((cnt ? cnt : 1) * sizeof(float));
+  int32_t rc = gqo_linear(x, t, k, wg, g, threads);
+  if (rc == 0) rc = gqo_linear(x, t, k, wu, u, threads);
+  if (rc == 0) gqo_geglu(g, u, cnt, y);
+  free(g);
+  free(u);
+  return rc;
+}
+
+int32_t gqo_linear_gelu_mul_cols(const float *x, int64_t t, int64_t k, const gqo_qweight *w,
+                                 const float *b, int64_t b_stride, int64_t offset, float *y,
+                                 int32_t threads) {
+  if (!w || offset < 0 || offset + w->n > b_stride) return -1;
+  size_t cnt = (size_t)(t * w->n);
+  float *g = (float *)malloc((cnt ? cnt : 1) * sizeof(float));
+  float *s = (float *)malloc((cnt ? cnt : 1) * sizeof(float));
+  int32_t rc = gqo_linear(x, t, k, w, g, threads);
+  if (rc == 0) {
+    gqo_slice_cols(b, t, b_stride, offset, w->n, s);
+    gqo_geglu(g, s, cnt, y);
+  }
+  free(g);
+  free(s);
+  return rc;
+}

@@ -1,0 +1,147 @@
+"""The CPU oracle against the reference's own known-answer tests, and against an
+independent float64 restatement of the same algorithm (no GPU).
+
+Pins: rust/tests/weights.rs:32-52 (pack/unpack round trip, dequantize KAT).
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+
+from oracle import oracle
+from gq import QuantWeight
+from gq import synth
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+KAT = json.load(open(os.path.join(HERE, "golden", "kat.json")))
+
+
+@pytest.mark.parametrize("case", KAT["roundtrip"], ids=lambda c: f"{c['bits']}bit")
+def test_int_pack_unpack_roundtrip(case):
+    """rust/tests/weights.rs:32-42, plus the packed byte image."""
+    bits, vals = case["bits"], np.array(case["values"], dtype=np.int32)
+    packed = oracle.pack_int(vals, bits)
+    assert packed.tolist() == case["packed"]
+    back = oracle.unpack_int(packed, bits, vals.size)
+    assert back.tolist() == vals.tolist()
+    # the host packer used for synthetic weights agrees byte for byte
+    assert synth.pack_codes(vals, bits).tolist() == case["packed"]
+
+
+def test_dequantize_per_row():
+    """rust/tests/weights.rs:44-52: exact known answer, both routes."""
+    d = KAT["dequantize_per_row"]
+    out = oracle.dequantize(d["q"], d["scales"], d["rows"], d["cols"], d["group_size"])
+    assert out.tolist() == d["expected"]
+    packed = oracle.pack_int(d["q"], 4)
+    assert packed.tolist() == d["packed_4bit"]
+    q = oracle.unpack_int(packed, 4, len(d["q"]))
+    assert oracle.dequantize(q, d["scales"], 2, 4, 4).tolist() == d["expected"]
+    # QuantWeight::deq element by element
+    w = QuantWeight(qbytes=packed, scales=np.array(d["scales"], np.float32), shape=(2, 4), bits=4,
+                    signed_i8=False, group_size=4)
+    assert [oracle.deq(w, n, k) for n in range(2) for k in range(4)] == d["expected"]
+
+
+def _random_qw(rng, n, k, bits, signed=False, group=None):
+    g = group or k
+    if signed:
+        qbytes = rng.integers(0, 256, n * k, dtype=np.uint8)
+    else:
+        vals = rng.integers(0, 1 << bits, n * k, dtype=np.uint32)
+        qbytes = oracle.pack_unsigned(vals, bits)
+    ss = -(-k // g)
+    return QuantWeight(qbytes=qbytes, scales=rng.uniform(0.01, 0.06, n * ss).astype(np.float32),
+                       shape=(n, k), bits=bits, signed_i8=signed, group_size=g)
+
+
+@pytest.mark.parametrize("bits,signed", [(2, False), (4, False), (8, True), (8, False)])
+def test_codes_match_independent_unpack(bits, signed):
+    rng = np.random.default_rng(bits * 10 + signed)
+    w = _random_qw(rng, 7, 48, bits, signed)
+    ref = w.codes()  # numpy restatement in the host package
+    got = np.array([[oracle.code(w, n, k) for k in range(48)] for n in range(7)])
+    assert (got == ref).all()
+
+
+@pytest.mark.parametrize("bits,signed,n,k,t,group", [
+    (4, False, 40, 64, 5, None), (2, False, 40, 64, 1, None), (8, True, 30, 48, 4, None),
+    (4, False, 21, 52, 3, None), (4, False, 50, 32, 3, 16), (2, False, 70, 96, 9, None)])
+def test_linear_matches_float64(bits, signed, n, k, t, group):
+    rng = np.random.default_rng(n * k + t)
+    w = _random_qw(rng, n, k, bits, signed, group)
+    x = rng.standard_normal((t, k)).astype(np.float32)
+    y = oracle.linear(x, w)
+    g = w.group_size
+    s = w.scales.reshape(n, -1)[:, np.arange(k) // g]
+    wd = w.codes().astype(np.float64) * s.astype(np.float64)
+    ref = x.astype(np.float64) @ wd.T
+    rel = np.linalg.norm(y - ref) / np.linalg.norm(ref)
+    assert rel < 1e-6
+
+
+def test_linear_threads_bit_identical(monkeypatch):
+    """par_ranges splits rows; results must not depend on the thread count
+    (rust/src/backend_cpu.rs:66-69)."""
+    rng = np.random.default_rng(3)
+    w = _random_qw(rng, 300, 256, 4)
+    x = rng.standard_normal((3, 256)).astype(np.float32)
+    a = oracle.linear(x, w, threads=1)
+    b = oracle.linear(x, w, threads=7)
+    assert np.array_equal(a, b)
+
+
+def test_default_threads_env(monkeypatch):
+    monkeypatch.setenv("GEMMA_CPU_THREADS", "3")
+    assert oracle.default_threads() == 3
+    monkeypatch.setenv("GEMMA_CPU_THREADS", "0")  # invalid -> core count
+    assert oracle.default_threads() >= 1
+
+
+def test_fused_compositions():
+    rng = np.random.default_rng(5)
+    wg, wu = _random_qw(rng, 24, 32, 4), _random_qw(rng, 24, 32, 4)
+    x = rng.standard_normal((3, 32)).astype(np.float32)
+    g, u = oracle.linear(x, wg), oracle.linear(x, wu)
+    assert np.array_equal(oracle.linear_geglu(x, wg, wu), oracle.geglu(g, u))
+    b = rng.standard_normal((3, 96)).astype(np.float32)
+    w = _random_qw(rng, 24, 32, 8, signed=True)
+    got = oracle.linear_gelu_mul_cols(x, w, b, 48)
+    assert np.array_equal(got, oracle.geglu(oracle.linear(x, w), b[:, 48:72]))
+    with pytest.raises(ValueError):
+        oracle.linear_gelu_mul_cols(x, w, b, 80)
+
+
+def test_gelu_and_softcap_values():
+    v = np.linspace(-6, 6, 101).astype(np.float32)
+    c = np.float32(np.sqrt(np.float32(2.0) / np.float32(np.pi)))
+    ref = 0.5 * v.astype(np.float64) * (1 + np.tanh(np.float64(c) * (v + 0.044715 * v.astype(np.float64) ** 3)))
+    got = np.array([oracle.gelu_tanh(float(a)) for a in v])
+    assert np.max(np.abs(got - ref)) < 1e-6
+    sc = oracle.softcap(v * 10, 30.0)
+    assert np.max(np.abs(sc - 30 * np.tanh(v.astype(np.float64) * 10 / 30))) < 1e-5
+
+
+def test_embed_rows_and_bad_id():
+    rng = np.random.default_rng(11)
+    t = _random_qw(rng, 50, 32, 4, group=16)
+    ids = [3, 7, 49, 0, 21]
+    out = oracle.embed_rows(t, ids, float(np.sqrt(32)))
+    s = t.scales.reshape(50, 2)
+    codes = t.codes()
+    for i, idv in enumerate(ids):
+        for d in range(32):
+            exp = np.float32(np.float32(codes[idv, d]) * s[idv, d // 16]) * np.float32(np.sqrt(32))
+            assert out[i, d] == exp
+    with pytest.raises(IndexError):
+        oracle.embed_rows(t, [50], 1.0)
+
+
+def test_lcg_matches_reference_definition():
+    """rust/tests/common/mod.rs:29-42: state = (state*1103515245 + 12345) & 0x7fffffff."""
+    r = synth.Lcg(7)
+    s = 7
+    for _ in range(5):
+        s = (s * 1103515245 + 12345) & 0x7FFFFFFF
+        assert r.next() == np.float32(s) / np.float32(0x7FFFFFFF)
