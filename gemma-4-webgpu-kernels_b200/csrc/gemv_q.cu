@@ -7,7 +7,7 @@
 // weight, 2 gelu * column slice) plus MODE 3 (logit soft-cap).
 //
 // Design (B200, HBM-bound):
-//  * Persistent CTAs, one per SM, each owning a contiguous range of weight rows.
+//  * Persistent CTAs, two per SM, each owning a contiguous range of weight rows.
 //    Rows are contiguous in the packed layout, so a CTA's work is one contiguous
 //    byte range, streamed into shared memory by the TMA engine with 1-D bulk
 //    copies (cp.async.bulk) through a ring of mbarrier-tracked stages. Copies for
@@ -15,9 +15,9 @@
 //    programmatic dependent launch the weight stream of this kernel overlaps the
 //    tail of the kernel that produces x.
 //  * Inside a stage the work is balanced at 16-byte-chunk granularity: thread t
-//    takes chunks t, t+512, ... of the stage, whatever row they belong to, and
-//    writes one partial sum per chunk; a second pass adds the partials of each
-//    row and runs the epilogue.
+//    takes chunks t, t+256, ... of the stage, whatever row they belong to, and
+//    writes one partial sum per chunk; then one warp per row adds that row's
+//    partials with shuffles and runs the epilogue.
 //  * Dequantization costs one LOP3 + one FFMA per code. A code field masked in
 //    place, (word & (mask << pos)), read as an f32 bit pattern is the subnormal
 //    raw * 2^(pos-149); FFMA handles subnormal inputs at full rate and exactly.
@@ -35,8 +35,9 @@
 
 namespace {
 
-constexpr int kThreads = 512;
+constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
+constexpr int kCtasPerSm = 2;  // one CTA's epilogue overlaps the other's stream
 constexpr int kMaxStages = 4;
 
 struct GemvArgs {
@@ -79,26 +80,25 @@ __host__ __device__ constexpr int code_pos(int j) {
   return j < Fmt<BITS>::kSplit ? j * BITS : j * BITS - Fmt<BITS>::kShift;
 }
 
-// ---- block reductions ---------------------------------------------------------
-__device__ __forceinline__ double block_sum_d(double v, double *scratch) {
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+// ---- block reduction of (sum in double, max in float) in one pass --------------
+__device__ __forceinline__ void block_sum_max(double &sum, float &mx, double *dscr, float *fscr) {
+  for (int o = 16; o > 0; o >>= 1) {
+    sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   __syncthreads();
-  if (lane == 0) scratch[warp] = v;
+  if (lane == 0) {
+    dscr[warp] = sum;
+    fscr[warp] = mx;
+  }
   __syncthreads();
-  double r = 0.0;
-  for (int i = 0; i < kWarps; ++i) r += scratch[i];
-  return r;
-}
-__device__ __forceinline__ float block_max_f(float v, float *scratch) {
-  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  __syncthreads();
-  if (lane == 0) scratch[warp] = v;
-  __syncthreads();
-  float r = 0.0f;
-  for (int i = 0; i < kWarps; ++i) r = fmaxf(r, scratch[i]);
-  return r;
+  sum = 0.0;
+  mx = 0.0f;
+  for (int i = 0; i < kWarps; ++i) {
+    sum += dscr[i];
+    mx = fmaxf(mx, fscr[i]);
+  }
 }
 
 __device__ __forceinline__ float pow2f(int e) {  // exact 2^e for e in [-126, 127]
@@ -129,7 +129,7 @@ __host__ __device__ inline GemvSmem gemv_layout(int bits, int mt, int nw, int ro
 
 // ---- the kernel -----------------------------------------------------------------
 template <int BITS, bool SIGNED, int MT, int MODE>
-__global__ void __launch_bounds__(kThreads, 1) gemv_q_kernel(const GemvArgs a) {
+__global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q_kernel(const GemvArgs a) {
   using F = Fmt<BITS>;
   constexpr int NW = (MODE == 1) ? 2 : 1;  // weights streamed together
   constexpr int ACC = (MT == 1) ? 4 : (MT == 2 ? 2 : 1);
@@ -184,35 +184,40 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q_kernel(const GemvArgs a) {
   gqd::griddep_wait();
 
   // ---- stage x: x' = x - mu, scaled by 2^(S - pos) into the padded layout ----
+  // mu and S come from one (sum, max|x|) reduction; S leaves one bit of headroom
+  // for |x - mu| <= 2 max|x|. zp * sum(x') is taken as sum(x) - K*mu in double:
+  // the per-element rounding of x - mu it ignores is below 2^-24 relative.
   for (int m = 0; m < MT; ++m) {
     const bool live = (m0 + m) < a.M;
     const float *xr = a.x + (size_t)(m0 + m) * a.ldx;
     double sx = 0.0;
-    if (live)
-      for (int k = tid; k < a.K; k += kThreads) sx += (double)xr[k];
-    sx = block_sum_d(sx, dscr);
-    const float mu = live && a.K > 0 ? (float)(sx / (double)a.K) : 0.0f;
     float mx = 0.0f;
     if (live)
-      for (int k = tid; k < a.K; k += kThreads) mx = fmaxf(mx, fabsf(__fsub_rn(xr[k], mu)));
-    mx = block_max_f(mx, fscr);
+      for (int k = tid * 4; k < a.K; k += kThreads * 4) {
+        const float4 v = *reinterpret_cast<const float4 *>(xr + k);
+        sx += (double)v.x + (double)v.y + (double)v.z + (double)v.w;
+        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+      }
+    block_sum_max(sx, mx, dscr, fscr);
+    const float mu = live && a.K > 0 ? (float)(sx / (double)a.K) : 0.0f;
     int e = 0;
-    if (mx > 0.0f && isfinite(mx)) frexpf(mx, &e);  // mx < 2^e
-    int S = 126 - e;
+    if (mx > 0.0f && isfinite(mx)) frexpf(mx, &e);  // mx < 2^e, so |x - mu| < 2^(e+1)
+    int S = 125 - e;
     S = max(-100, min(126, S));
-    double sxp = 0.0;
     float *xm = xs + (size_t)m * C * F::kPad;
-    for (int k = tid; k < C * F::kPerChunk; k += kThreads) {
-      const float v = live ? __fsub_rn(xr[k], mu) : 0.0f;
-      sxp += (double)v;
-      const int j = k % F::kPerWord;
-      const int pos = code_pos<BITS>(j);
-      xm[(k / F::kPerChunk) * F::kPad + (k % F::kPerChunk)] = v * pow2f(S - pos);
+    for (int k = tid * 4; k < a.K; k += kThreads * 4) {
+      float4 v = live ? *reinterpret_cast<const float4 *>(xr + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+      float vv[4] = {__fsub_rn(v.x, mu), __fsub_rn(v.y, mu), __fsub_rn(v.z, mu), __fsub_rn(v.w, mu)};
+      if (!live) vv[0] = vv[1] = vv[2] = vv[3] = 0.0f;
+      float o[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) o[i] = vv[i] * pow2f(S - code_pos<BITS>((k + i) % F::kPerWord));
+      *reinterpret_cast<float4 *>(xm + (k / F::kPerChunk) * F::kPad + (k % F::kPerChunk)) =
+          make_float4(o[0], o[1], o[2], o[3]);
     }
-    sxp = block_sum_d(sxp, dscr);
     if (tid == 0) {
       mu_s[m] = mu;
-      // zp * sum(x') in the scaled domain (2^(S-149)), exact in double
+      const double sxp = live ? sx - (double)a.K * (double)mu : 0.0;
       corr_s[m] = (float)((double)F::kZp * sxp * ldexp(1.0, S - 149));
       pow2_s[m] = ldexp(1.0, 149 - S);
     }
@@ -236,9 +241,9 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q_kernel(const GemvArgs a) {
     const int nch = rows * C;
     const uint8_t *buf = stage_buf + (size_t)stage * NW * stage_bytes;
 
+    int r = tid / C, c = tid - (tid / C) * C;  // (row, chunk) of f, advanced without division
+    const int dr = kThreads / C, dc = kThreads - (kThreads / C) * C;
     for (int f = tid; f < nch; f += kThreads) {
-      const int r = f / C;
-      const int c = f - r * C;
       uint4 wv[NW];
 #pragma unroll
       for (int h = 0; h < NW; ++h)
@@ -291,23 +296,33 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_q_kernel(const GemvArgs a) {
           for (int q = 1; q < ACC; ++q) v += acc[h][m][q];
           red[((size_t)h * MT + m) * tile_chunks + f] = v;
         }
+      r += dr;
+      c += dc;
+      if (c >= C) {
+        c -= C;
+        ++r;
+      }
     }
     __syncthreads();  // partials written; stage buffer fully consumed
     if (tid == 0 && t + a.stages < ntiles) issue(t + a.stages);
 
-    for (int e = tid; e < rows * MT; e += kThreads) {
-      const int r = e / MT;
-      const int m = e - r * MT;
+    const int warp = tid >> 5, lane = tid & 31;
+    for (int e = warp; e < rows * MT; e += kWarps) {  // one warp per (row, m)
+      const int r2 = e / MT;
+      const int m = e - r2 * MT;
       if (m0 + m >= a.M) continue;
-      const int n = r0 + r;
+      const int n = r0 + r2;
       float dsum[NW];
 #pragma unroll
       for (int h = 0; h < NW; ++h) {
-        const float *p = red + ((size_t)h * MT + m) * tile_chunks + (size_t)r * C;
+        const float *p = red + ((size_t)h * MT + m) * tile_chunks + (size_t)r2 * C;
         float v = 0.0f;
-        for (int c = 0; c < C; ++c) v += p[c];
+        for (int cc = lane; cc < C; cc += 32) v += p[cc];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
         dsum[h] = v;
       }
+      if (lane != 0) continue;
       const double mu = (double)mu_s[m];
       const double corr = (double)corr_s[m];
       const double p2 = pow2_s[m];
@@ -388,7 +403,8 @@ bool gq_gemv_supported(gq_ctx *ctx, const gq_qweight *w, int64_t m, int nw) {
   if (w->row_bytes % 16 != 0 || w->row_bytes > 65536) return false;
   if (w->n > (1ll << 30)) return false;
   const int mt = m <= 1 ? 1 : (m == 2 ? 2 : 4);
-  return gemv_smem_bytes(w->bits, mt, nw, (int)w->row_bytes, 1, 2) <= ctx->smem_optin;
+  if (w->k % 4 != 0) return false;
+  return gemv_smem_bytes(w->bits, mt, nw, (int)w->row_bytes, 1, 2) <= ctx->smem_optin / kCtasPerSm - 1024;
 }
 
 // mode: 0 plain, 1 geglu (w2 = up), 2 gelu * bs slice, 3 soft-cap.
@@ -423,25 +439,26 @@ int gq_gemv_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq_qw
   a.row_bytes = rb;
   a.err = ctx->dev_err;
 
-  // Grid: one CTA per SM over contiguous row ranges.
-  const int gx_max = ctx->num_sms;
+  // Grid: kCtasPerSm CTAs per SM over contiguous row ranges.
+  const int gx_max = ctx->num_sms * kCtasPerSm;
   int rows_per_cta = (int)((w->n + gx_max - 1) / gx_max);
   if (rows_per_cta < 1) rows_per_cta = 1;
   const int gx = (int)((w->n + rows_per_cta - 1) / rows_per_cta);
-  // Stage size: about 2048 chunks (4 per thread) and <= 32 KB per weight.
-  int tile_rows = max(1, 2048 / C);
-  tile_rows = min(tile_rows, max(1, (32 * 1024) / rb));
+  // Stage size: about 1024 chunks (4 per thread) and <= 16 KB per weight.
+  int tile_rows = max(1, 1024 / C);
+  tile_rows = min(tile_rows, max(1, (16 * 1024) / rb));
   tile_rows = min(tile_rows, rows_per_cta);
   const int ntiles = (rows_per_cta + tile_rows - 1) / tile_rows;
   int stages = min(kMaxStages, ntiles);
+  const size_t smem_cap = ctx->smem_optin / kCtasPerSm - 1024;
   size_t smem = gemv_smem_bytes(w->bits, mt, nw, rb, tile_rows, stages);
-  while (smem > ctx->smem_optin && (stages > 1 || tile_rows > 1)) {
+  while (smem > smem_cap && (stages > 1 || tile_rows > 1)) {
     if (stages > 2) --stages;
     else if (tile_rows > 1) tile_rows = (tile_rows + 1) / 2;
     else --stages;
     smem = gemv_smem_bytes(w->bits, mt, nw, rb, tile_rows, stages);
   }
-  if (smem > ctx->smem_optin) return gq_fail(ctx, GQ_ERR_UNSUPPORTED, "gemv: shared memory");
+  if (smem > smem_cap) return gq_fail(ctx, GQ_ERR_UNSUPPORTED, "gemv: shared memory");
   a.rows_per_cta = rows_per_cta;
   a.tile_rows = tile_rows;
   a.stages = stages;

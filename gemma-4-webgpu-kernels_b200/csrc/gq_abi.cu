@@ -20,6 +20,10 @@ int gq_gemv_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq_qw
                    const gq_qweight *w2, const float *bs, int64_t b_stride, int64_t b_off,
                    float cap, float *y, int64_t ldy, int64_t y_col0);
 int gq_scalar_linear_launch(gq_ctx *ctx, const float *x, int64_t m, const gq_qweight *w, float *y);
+bool gq_prefill_supported(gq_ctx *ctx, const gq_qweight *w, int64_t m);
+int gq_prefill_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq_qweight *w, const gq_qweight *w2,
+                      const float *bs, int64_t b_stride, int64_t b_off, float cap, float *y, int64_t ldy,
+                      int64_t y_col0);
 int gq_qsum_launch(gq_ctx *ctx, const gq_qweight *w, float *out);
 int gq_embed_launch(gq_ctx *ctx, const gq_qweight *w, const uint32_t *ids, int64_t t, float emb,
                     float *out);
@@ -142,6 +146,7 @@ int gq_ctx_destroy(gq_ctx *ctx) {
   cudaStreamSynchronize(ctx->stream);
   for (int i = 0; i < 2; ++i)
     if (ctx->scratch[i]) cudaFree(ctx->scratch[i]);
+  if (ctx->ws) cudaFree(ctx->ws);
   if (ctx->dev_err) cudaFree(ctx->dev_err);
   if (ctx->own_stream) cudaStreamDestroy(ctx->own_stream);
   delete ctx;
@@ -344,6 +349,22 @@ int check_linear_args(gq_ctx *ctx, const char *op, const float *x, int64_t m, in
   return GQ_OK;
 }
 
+// Rows of activations from which the bf16 tensor-core path is used (prefill).
+// Below it the streaming CUDA-core kernel keeps f32 activations.
+int64_t prefill_min_m() {
+  static int64_t v = -1;
+  if (v < 0) {
+    const char *e = getenv("GQ_PREFILL_MIN_M");
+    v = (e && *e) ? atoll(e) : 128;
+    if (v < 16) v = 16;
+  }
+  return v;
+}
+
+bool use_prefill(gq_ctx *ctx, const float *x, int64_t m, const gq_qweight *w) {
+  return m >= prefill_min_m() && ((uintptr_t)x % 16 == 0) && gq_prefill_supported(ctx, w, m);
+}
+
 }  // namespace
 
 extern "C" {
@@ -352,6 +373,7 @@ int gq_linear(gq_ctx *ctx, const float *x, int64_t m, int64_t k, const gq_qweigh
   GQ_ENTER(ctx);
   int rc = check_linear_args(ctx, "linear", x, m, k, w, y);
   if (rc != GQ_OK || m == 0 || w->n == 0) return rc;
+  if (use_prefill(ctx, x, m, w)) return gq_prefill_launch(ctx, 0, x, m, w, nullptr, nullptr, 0, 0, 0.0f, y, w->n, 0);
   if (gq_gemv_supported(ctx, w, m, 1))
     return gq_gemv_launch(ctx, 0, x, m, w, nullptr, nullptr, 0, 0, 0.0f, y, w->n, 0);
   return gq_scalar_linear_launch(ctx, x, m, w, y);
@@ -367,6 +389,8 @@ int gq_linear_geglu(gq_ctx *ctx, const float *x, int64_t m, int64_t k, const gq_
   if (m == 0 || wg->n == 0) return GQ_OK;
   const bool same = wg->bits == wu->bits && wg->signed_i8 == wu->signed_i8 &&
                     wg->group_size == wu->group_size;
+  if (same && use_prefill(ctx, x, m, wg))
+    return gq_prefill_launch(ctx, 1, x, m, wg, wu, nullptr, 0, 0, 0.0f, y, wg->n, 0);
   if (same && gq_gemv_supported(ctx, wg, m, 2))
     return gq_gemv_launch(ctx, 1, x, m, wg, wu, nullptr, 0, 0, 0.0f, y, wg->n, 0);
   // composition of rust/src/backend.rs:156-160
@@ -388,6 +412,8 @@ int gq_linear_gelu_mul_cols(gq_ctx *ctx, const float *x, int64_t m, int64_t k, c
     return gq_fail(ctx, GQ_ERR_INVALID_ARGUMENT, "linear_gelu_mul_cols: offset + N exceeds b's row");
   if (m == 0 || w->n == 0) return GQ_OK;
   if (!b) return gq_fail(ctx, GQ_ERR_INVALID_ARGUMENT, "linear_gelu_mul_cols: null b");
+  if (use_prefill(ctx, x, m, w))
+    return gq_prefill_launch(ctx, 2, x, m, w, nullptr, b, b_stride, b_offset, 0.0f, y, w->n, 0);
   if (gq_gemv_supported(ctx, w, m, 1))
     return gq_gemv_launch(ctx, 2, x, m, w, nullptr, b, b_stride, b_offset, 0.0f, y, w->n, 0);
   // composition of rust/src/backend.rs:163-167
@@ -406,6 +432,7 @@ int gq_linear_softcap(gq_ctx *ctx, const float *x, int64_t m, int64_t k, const g
   if (ldy < 0 || y_col0 < 0 || y_col0 + w->n > ldy)
     return gq_fail(ctx, GQ_ERR_INVALID_ARGUMENT, "linear_softcap: y_col0 + N exceeds ldy");
   if (m == 0 || w->n == 0) return GQ_OK;
+  if (use_prefill(ctx, x, m, w)) return gq_prefill_launch(ctx, 3, x, m, w, nullptr, nullptr, 0, 0, cap, y, ldy, y_col0);
   if (gq_gemv_supported(ctx, w, m, 1))
     return gq_gemv_launch(ctx, 3, x, m, w, nullptr, nullptr, 0, 0, cap, y, ldy, y_col0);
   // composition: generic linear into scratch, then soft-cap into the strided output

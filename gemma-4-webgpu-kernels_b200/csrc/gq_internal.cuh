@@ -22,6 +22,9 @@ struct gq_ctx {
   // temporaries of the composed fallbacks (generic kernel + elementwise epilogue)
   float *scratch[2] = {nullptr, nullptr};
   size_t scratch_cap[2] = {0, 0};
+  // workspace of the tensor-core prefill path (bf16 copy of the activations)
+  void *ws = nullptr;
+  size_t ws_cap = 0;
 };
 
 struct gq_qweight {

@@ -1,0 +1,488 @@
+// prefill_tc.cu — prefill dequantizing GEMM on the 5th-generation tensor cores.
+//
+// Replaces the reference's MATMUL_Q_TILED shader (rust/src/kernels/matmul_q_tiled.wgsl:
+// 39-126, chosen for M >= 16 at rust/src/backend_wgpu.rs:663-673), whose W tile is
+// dequantized to f32 in workgroup memory and multiplied with f32 FMAs. Here:
+//   C[m, n] = epilogue( s[n] * sum_k bf16(x[m, k]) * q[n, k] )
+// with bf16 operands and fp32 accumulation in tensor memory (TMEM):
+//  * x is cast to bf16 once per call (a [M, K] workspace) and loaded tile by tile
+//    with TMA (cp.async.bulk.tensor, 128-byte swizzle);
+//  * 8 producer warps dequantize the packed weight rows straight into shared
+//    memory in the K-major 128-byte-swizzled layout tcgen05.mma reads (codes are
+//    exact in bf16; the per-row scale is applied in the epilogue);
+//  * one elected thread issues tcgen05.mma (M=128 tokens, N=256 weight rows,
+//    K=16) into a 128x256 fp32 accumulator in TMEM; tcgen05.commit releases
+//    each shared-memory stage and finally signals the epilogue;
+//  * 4 warps read the accumulator back with tcgen05.ld, apply the scale and the
+//    MODE epilogue (0 plain, 1 GeGLU, 2 gelu * column slice, 3 soft-cap) and
+//    store f32.
+// For MODE 1 the 256 MMA columns hold 128 gate rows followed by the same 128 up
+// rows, so one MMA computes both projections of a 128-wide output tile.
+//
+// Every wait is bounded (2 s); a timeout sets GQ_DEVERR_WAIT_TIMEOUT, drains,
+// frees TMEM and returns.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <type_traits>
+
+#include "gq_internal.cuh"
+
+namespace {
+
+constexpr int BM = 128;        // tokens per tile (MMA M)
+constexpr int BN = 256;        // MMA N (weight rows, or gate+up halves)
+constexpr int BK = 64;         // K per stage: one 128-byte swizzle row of bf16
+constexpr int STAGES = 4;
+constexpr int kThreads = 320;  // warp 0: TMA(A), warp 1: MMA + TMEM, warps 2-9: B producers
+constexpr int kProducers = 256;
+constexpr uint32_t A_STAGE = BM * BK * 2;  // 16 KB
+constexpr uint32_t B_STAGE = BN * BK * 2;  // 32 KB
+constexpr uint32_t TMEM_COLS = 256;
+
+struct PrefillArgs {
+  int M, N, K;
+  const uint8_t *w;
+  const float *s;
+  const uint8_t *w2;
+  const float *s2;
+  int row_bytes;
+  const float *bs;
+  int64_t b_stride, b_off;
+  float cap;
+  float *y;
+  int64_t ldy, y_col0;
+  uint32_t *err;
+};
+
+// ---- PTX wrappers (tcgen05 / TMA) ----------------------------------------------
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int c0, int c1, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          gqd::smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(gqd::smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(gqd::smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_commit(uint64_t *bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   gqd::smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// 32 lanes x 32 bits, 16 consecutive columns per thread.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 B apart.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
+  uint64_t d = (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)1 << 16;             // leading byte offset (unused for this layout)
+  d |= (uint64_t)(1024 >> 4) << 32;   // stride byte offset: next 8-row group
+  d |= (uint64_t)1 << 46;             // descriptor version for tcgen05
+  d |= (uint64_t)2 << 61;             // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor: bf16 x bf16 -> f32, both K-major, M=128, N=256.
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                            ((uint32_t)(BM >> 4) << 24);
+
+// ---- dequantization of 8 consecutive codes to 8 bf16 (natural K order) -------
+// Sub-byte codes use the bf16 pattern 0x4300|n (= 128 + n, exact), then subtract
+// 128 + zero point. Two codes at bit offsets a (low half) and a+16 (high half)
+// come out of one masked word; PRMT then pairs neighbours into natural order.
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+  return r;
+}
+__device__ __forceinline__ uint32_t bsub(uint32_t v, uint32_t c2) {  // bf16x2 v - c2 (exact here)
+  __nv_bfloat162 a = *reinterpret_cast<__nv_bfloat162 *>(&v);
+  __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162 *>(&c2);
+  __nv_bfloat162 r = __hsub2(a, b);
+  return *reinterpret_cast<uint32_t *>(&r);
+}
+
+// 4-bit: one 32-bit word = codes 0..7 (nibble j at bits 4j, offset binary).
+__device__ __forceinline__ uint4 deq8_b4(uint32_t w) {
+  const uint32_t A = (w & 0x000F000Fu) | 0x43004300u;          // (c0, c4)
+  const uint32_t B = ((w >> 4) & 0x000F000Fu) | 0x43004300u;   // (c1, c5)
+  const uint32_t C = ((w >> 8) & 0x000F000Fu) | 0x43004300u;   // (c2, c6)
+  const uint32_t D = ((w >> 12) & 0x000F000Fu) | 0x43004300u;  // (c3, c7)
+  const uint32_t zp = 0x43084308u;                              // 136 = 128 + 8
+  uint4 r;
+  r.x = bsub(prmt(A, B, 0x5410), zp);  // (c0, c1)
+  r.y = bsub(prmt(C, D, 0x5410), zp);  // (c2, c3)
+  r.z = bsub(prmt(A, B, 0x7632), zp);  // (c4, c5)
+  r.w = bsub(prmt(C, D, 0x7632), zp);  // (c6, c7)
+  return r;
+}
+// 2-bit: 16 bits = codes 0..7 (crumb j at bits 2j).
+__device__ __forceinline__ uint4 deq8_b2(uint32_t h) {
+  // E_j holds code j (low half) and code j+4 (high half)
+  const uint32_t v = (h & 0xFFu) | ((h & 0xFF00u) << 8);  // codes 0-3 at bits 0-7, codes 4-7 at bits 16-23
+  const uint32_t E0 = (v & 0x00030003u) | 0x43004300u;
+  const uint32_t E1 = ((v >> 2) & 0x00030003u) | 0x43004300u;
+  const uint32_t E2 = ((v >> 4) & 0x00030003u) | 0x43004300u;
+  const uint32_t E3 = ((v >> 6) & 0x00030003u) | 0x43004300u;
+  const uint32_t zp = 0x43024302u;  // 130 = 128 + 2
+  uint4 r;
+  r.x = bsub(prmt(E0, E1, 0x5410), zp);  // (c0, c1)
+  r.y = bsub(prmt(E2, E3, 0x5410), zp);  // (c2, c3)
+  r.z = bsub(prmt(E0, E1, 0x7632), zp);  // (c4, c5)
+  r.w = bsub(prmt(E2, E3, 0x7632), zp);  // (c6, c7)
+  return r;
+}
+// 8-bit: two words = codes 0..7. u = byte ^ XOR is offset binary (zp 128); the f32
+// 2^23 + u minus 2^23 + 128 is the exact code, and its upper half is its bf16.
+template <bool SIGNED>
+__device__ __forceinline__ uint32_t deq2_b8(uint32_t u, int j0) {
+  const uint32_t magic = 0x4B000000u;
+  const float f0 = __uint_as_float(prmt(u, magic, 0x7440u + j0)) - 8388736.0f;
+  const float f1 = __uint_as_float(prmt(u, magic, 0x7440u + j0 + 1)) - 8388736.0f;
+  return prmt(__float_as_uint(f0), __float_as_uint(f1), 0x7632);
+}
+template <bool SIGNED>
+__device__ __forceinline__ uint4 deq8_b8(uint2 q) {
+  const uint32_t x = SIGNED ? 0x80808080u : 0u;
+  const uint32_t u0 = q.x ^ x, u1 = q.y ^ x;
+  uint4 r;
+  r.x = deq2_b8<SIGNED>(u0, 0);
+  r.y = deq2_b8<SIGNED>(u0, 2);
+  r.z = deq2_b8<SIGNED>(u1, 0);
+  r.w = deq2_b8<SIGNED>(u1, 2);
+  return r;
+}
+
+// Packed bytes of 8 consecutive codes.
+template <int BITS>
+struct Pack8 {
+  using T = typename std::conditional<BITS == 8, uint2, typename std::conditional<BITS == 4, uint32_t, uint16_t>::type>::type;
+};
+
+template <int BITS, bool SIGNED>
+__device__ __forceinline__ uint4 deq8(typename Pack8<BITS>::T p) {
+  if constexpr (BITS == 4) return deq8_b4(p);
+  else if constexpr (BITS == 2) return deq8_b2(p);
+  else return deq8_b8<SIGNED>(p);
+}
+
+template <int BITS>
+__device__ __forceinline__ typename Pack8<BITS>::T load8(const uint8_t *row, int k) {
+  using T = typename Pack8<BITS>::T;
+  return *reinterpret_cast<const T *>(row + (size_t)k * BITS / 8);
+}
+
+// ---- the kernel -----------------------------------------------------------------
+template <int BITS, bool SIGNED, int MODE>
+__global__ void __launch_bounds__(kThreads, 1)
+    prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const PrefillArgs a) {
+  using P8 = typename Pack8<BITS>::T;
+  constexpr int OW = (MODE == 1) ? BN / 2 : BN;  // output columns per tile
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *sA = smem;                                       // [STAGES][BM x BK bf16], swizzled
+  uint8_t *sB = smem + STAGES * A_STAGE;                    // [STAGES][BN x BK bf16], swizzled
+  uint64_t *full_a = reinterpret_cast<uint64_t *>(sB + STAGES * B_STAGE);
+  uint64_t *full_b = full_a + STAGES;
+  uint64_t *empty = full_b + STAGES;
+  uint64_t *acc_full = empty + STAGES;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_full + 1);
+  volatile uint32_t *abort_flag = tmem_slot + 1;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * BM;
+  const int n0 = blockIdx.y * OW;
+  const int KT = a.K / BK;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      gqd::mbar_init(&full_a[i], 1);
+      gqd::mbar_init(&full_b[i], kProducers);
+      gqd::mbar_init(&empty[i], 1);
+    }
+    gqd::mbar_init(acc_full, 1);
+    *abort_flag = 0;
+    gqd::fence_mbar_init();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(gqd::smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  gqd::griddep_wait();  // x (the bf16 workspace) comes from the preceding cast kernel
+
+  if (warp == 0) {
+    // ---- A: TMA loads of the bf16 activation tile ----
+    if (lane == 0) {
+      int issued = 0;
+      for (int kt = 0; kt < KT && !*abort_flag; ++kt) {
+        const int s = kt % STAGES;
+        if (kt >= STAGES && !gqd::mbar_wait_bounded(&empty[s], ((kt / STAGES) - 1) & 1)) {
+          *abort_flag = 1;
+          break;
+        }
+        gqd::mbar_arrive_expect_tx(&full_a[s], A_STAGE);
+        tma_load_2d(sA + s * A_STAGE, &tmap_a, kt * BK, m0, &full_a[s]);
+        issued = kt + 1;
+      }
+      if (*abort_flag) {
+        // bounded drain of the loads still in flight before shared memory is released
+        for (int kt = issued > STAGES ? issued - STAGES : 0; kt < issued; ++kt)
+          (void)gqd::mbar_wait_bounded(&full_a[kt % STAGES], (kt / STAGES) & 1, 100000000ull);
+      }
+    }
+  } else if (warp == 1) {
+    // ---- MMA issue (one thread) ----
+    if (lane == 0) {
+      for (int kt = 0; kt < KT; ++kt) {
+        const int s = kt % STAGES;
+        const uint32_t ph = (kt / STAGES) & 1;
+        if (*abort_flag || !gqd::mbar_wait_bounded(&full_a[s], ph) || !gqd::mbar_wait_bounded(&full_b[s], ph)) {
+          *abort_flag = 1;
+          break;
+        }
+        tc_fence_after();
+        const uint64_t ad = sw128_desc(gqd::smem_u32(sA + s * A_STAGE));
+        const uint64_t bd = sw128_desc(gqd::smem_u32(sB + s * B_STAGE));
+#pragma unroll
+        for (int j = 0; j < BK / 16; ++j)  // 16 bf16 = 32 bytes per MMA along K
+          tc_mma(tmem, ad + (uint64_t)(2 * j), bd + (uint64_t)(2 * j), kIdesc, (kt | j) != 0);
+        tc_commit(&empty[s]);
+      }
+      tc_commit(acc_full);  // fires once every MMA issued above has completed
+    }
+  } else {
+    // ---- B: dequantize weight rows into the swizzled K-major tile ----
+    const int pt = threadIdx.x - 64;  // 0..255
+    for (int kt = 0; kt < KT; ++kt) {
+      const int s = kt % STAGES;
+      if (kt >= STAGES && (*abort_flag || !gqd::mbar_wait_bounded(&empty[s], ((kt / STAGES) - 1) & 1))) {
+        *abort_flag = 1;
+        break;
+      }
+      uint8_t *dst = sB + s * B_STAGE;
+#pragma unroll
+      for (int it = 0; it < (BN * 8) / kProducers; ++it) {
+        const int item = pt + it * kProducers;
+        const int r = item >> 3;  // tile row 0..255
+        const int c = item & 7;   // 16-byte chunk (8 codes) within the 128-byte row
+        int n;
+        const uint8_t *wp;
+        if (MODE == 1) {
+          n = n0 + (r & (BN / 2 - 1));
+          wp = (r < BN / 2) ? a.w : a.w2;
+        } else {
+          n = n0 + r;
+          wp = a.w;
+        }
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (n < a.N) v = deq8<BITS, SIGNED>(load8<BITS>(wp + (size_t)n * a.row_bytes, kt * BK + c * 8));
+        *reinterpret_cast<uint4 *>(dst + r * 128 + ((c ^ (r & 7)) << 4)) = v;
+      }
+      fence_proxy_async();  // make the generic-proxy stores visible to the tensor core
+      mbar_arrive(&full_b[s]);
+    }
+    // ---- epilogue: warps 2..5 read the accumulator back ----
+    if (warp < 6) {
+      const int q = warp & 3;  // TMEM lane quarter this warp may access
+      const int m = m0 + q * 32 + lane;
+      const bool ok = gqd::mbar_wait_bounded(acc_full, 0);
+      if (!ok) *abort_flag = 1;
+      tc_fence_after();
+      if (ok) {
+        for (int c0 = 0; c0 < OW; c0 += 16) {
+          float v[16], u[16];
+          tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + c0, v);
+          if (MODE == 1) tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + BN / 2 + c0, u);
+          if (m < a.M) {
+            float *yr = a.y + (size_t)m * a.ldy + a.y_col0;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int n = n0 + c0 + j;
+              if (n >= a.N) break;
+              float o = __fmul_rn(v[j], a.s[n]);
+              if (MODE == 1) {
+                o = __fmul_rn(gqd::gelu_tanh(o), __fmul_rn(u[j], a.s2[n]));
+              } else if (MODE == 2) {
+                o = __fmul_rn(gqd::gelu_tanh(o), a.bs[(size_t)m * a.b_stride + a.b_off + n]);
+              } else if (MODE == 3) {
+                if (a.cap > 0.0f) o = __fmul_rn(a.cap, tanhf(__fdiv_rn(o, a.cap)));
+              }
+              yr[n] = o;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+    }
+  }
+
+  __syncthreads();
+  if (threadIdx.x == 0 && *abort_flag) gqd::report(a.err, GQ_DEVERR_WAIT_TIMEOUT);
+  if (warp == 1) {
+    if (*abort_flag) {
+      // Outstanding MMAs (if any) signal acc_full through the final commit.
+      (void)gqd::mbar_wait_bounded(acc_full, 0, 100000000ull);
+    }
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS) : "memory");
+  }
+}
+
+// f32 -> bf16 (round to nearest even), [M, K] row-major, K % 4 == 0.
+__global__ void cast_bf16_kernel(const float *x, __nv_bfloat16 *xb, int64_t n4) {
+  gqd::griddep_wait();
+  gqd::griddep_launch_dependents();
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+    const float4 v = reinterpret_cast<const float4 *>(x)[i];
+    __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y);
+    __nv_bfloat162 hi = __floats2bfloat162_rn(v.z, v.w);
+    uint2 o;
+    o.x = *reinterpret_cast<uint32_t *>(&lo);
+    o.y = *reinterpret_cast<uint32_t *>(&hi);
+    reinterpret_cast<uint2 *>(xb)[i] = o;
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void *p = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+template <int BITS, bool SIGNED, int MODE>
+int launch_t(gq_ctx *ctx, const CUtensorMap &map, const PrefillArgs &a, dim3 grid, size_t smem) {
+  auto kern = prefill_tc_kernel<BITS, SIGNED, MODE>;
+  static bool attr_set[64] = {};
+  const int dev = ctx->device & 63;
+  if (!attr_set[dev]) {
+    GQ_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    attr_set[dev] = true;
+  }
+  GQ_CUDA_TRY(ctx, gq_launch(ctx, kern, grid, dim3(kThreads), smem, map, a));
+  return GQ_OK;
+}
+
+template <int BITS, bool SIGNED>
+int launch_mode(gq_ctx *ctx, int mode, const CUtensorMap &map, const PrefillArgs &a, dim3 grid, size_t smem) {
+  switch (mode) {
+    case 0: return launch_t<BITS, SIGNED, 0>(ctx, map, a, grid, smem);
+    case 1: return launch_t<BITS, SIGNED, 1>(ctx, map, a, grid, smem);
+    case 2: return launch_t<BITS, SIGNED, 2>(ctx, map, a, grid, smem);
+    default: return launch_t<BITS, SIGNED, 3>(ctx, map, a, grid, smem);
+  }
+}
+
+constexpr size_t kSmemBytes = 1024 + STAGES * (A_STAGE + B_STAGE) + (3 * STAGES + 1) * 8 + 16;
+
+}  // namespace
+
+// The tensor-core path applies to M >= 16 rows with K a multiple of 64, one
+// scale per row and a shape that packs whole bytes per 8 codes.
+bool gq_prefill_supported(gq_ctx *ctx, const gq_qweight *w, int64_t m) {
+  if (m < 16 || w->group_size != w->k || w->k % BK != 0 || w->k <= 0 || w->n <= 0) return false;
+  if (m > (1ll << 30) || w->n > (1ll << 30) || w->k > (1 << 24)) return false;
+  return kSmemBytes <= ctx->smem_optin && encode_fn() != nullptr;
+}
+
+// Workspace for the bf16 copy of x (grown on demand, stream-ordered).
+static int ws_get(gq_ctx *ctx, size_t bytes, void **out) {
+  if (ctx->ws_cap < bytes) {
+    if (ctx->ws) cudaFreeAsync(ctx->ws, ctx->stream);
+    ctx->ws = nullptr;
+    ctx->ws_cap = 0;
+    GQ_CUDA_TRY(ctx, cudaMallocAsync(&ctx->ws, bytes, ctx->stream));
+    ctx->ws_cap = bytes;
+  }
+  *out = ctx->ws;
+  return GQ_OK;
+}
+
+int gq_prefill_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq_qweight *w, const gq_qweight *w2,
+                      const float *bs, int64_t b_stride, int64_t b_off, float cap, float *y, int64_t ldy,
+                      int64_t y_col0) {
+  const int64_t K = w->k;
+  void *wsp = nullptr;
+  int rc = ws_get(ctx, (size_t)(m * K) * 2, &wsp);
+  if (rc != GQ_OK) return rc;
+  __nv_bfloat16 *xb = static_cast<__nv_bfloat16 *>(wsp);
+  {
+    const int64_t n4 = m * K / 4;
+    int64_t g = (n4 + 255) / 256;
+    if (g > (int64_t)ctx->num_sms * 8) g = (int64_t)ctx->num_sms * 8;
+    GQ_CUDA_TRY(ctx, gq_launch(ctx, cast_bf16_kernel, dim3((unsigned)g), dim3(256), 0, x, xb, n4));
+  }
+  CUtensorMap map;
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)m};
+  cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+  cuuint32_t box[2] = {BK, BM};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult cr = encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, xb, dims, strides, box, estr,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (cr != CUDA_SUCCESS) return gq_fail(ctx, GQ_ERR_CUDA, "prefill: cuTensorMapEncodeTiled failed");
+  PrefillArgs a = {};
+  a.M = (int)m;
+  a.N = (int)w->n;
+  a.K = (int)K;
+  a.w = w->bytes;
+  a.s = w->scales;
+  if (w2) {
+    a.w2 = w2->bytes;
+    a.s2 = w2->scales;
+  }
+  a.row_bytes = (int)w->row_bytes;
+  a.bs = bs;
+  a.b_stride = b_stride;
+  a.b_off = b_off;
+  a.cap = cap;
+  a.y = y;
+  a.ldy = ldy;
+  a.y_col0 = y_col0;
+  a.err = ctx->dev_err;
+  const int ow = (mode == 1) ? BN / 2 : BN;
+  dim3 grid((unsigned)((m + BM - 1) / BM), (unsigned)((w->n + ow - 1) / ow));
+  if (w->bits == 4) return launch_mode<4, false>(ctx, mode, map, a, grid, kSmemBytes);
+  if (w->bits == 2) return launch_mode<2, false>(ctx, mode, map, a, grid, kSmemBytes);
+  if (w->signed_i8) return launch_mode<8, true>(ctx, mode, map, a, grid, kSmemBytes);
+  return launch_mode<8, false>(ctx, mode, map, a, grid, kSmemBytes);
+}

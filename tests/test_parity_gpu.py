@@ -236,10 +236,14 @@ def test_embed_config4_shapes_bit_exact(g):
 
 
 def test_embed_odd_width_and_duplicates(g):
-    t = synth.make_qweight(81, 20, 18, 2)  # D % 4 != 0 -> per-element kernel
+    t = synth.make_qweight(81, 20, 18, 4)  # D % 4 != 0 -> per-element kernel
     ids = [0, 19, 19, 5, 0]
     got = g.readback(g.embed_rows(g.quant_tensor(t), ids, 0.5))
     assert np.array_equal(got.reshape(5, 18), oracle.embed_rows(t, ids, 0.5))
+    # K not a multiple of the values per byte cannot be packed (row_bytes = K / per_byte
+    # truncates in rust/src/backend.rs:33-36): rejected at upload
+    with pytest.raises(GqError):
+        g.quant_tensor(QuantWeight(np.zeros(40, np.uint8), np.ones(20, np.float32), (20, 18), 2, False, 18))
 
 
 def test_embed_bad_id_raises(g):

@@ -1,0 +1,96 @@
+"""The tcgen05 prefill GEMM (M >= 128) against the CPU oracle (needs a B200).
+
+Two bars per case:
+  * against the f32 oracle: relative L2 <= 1e-2 (the bf16 tensor-core bound);
+  * against the oracle run on the same bf16-rounded activations: relative
+    L2 <= 1e-5 — products of bf16 activations and integer codes are exact, so
+    only the accumulation order differs. This pins the dequantization, the
+    swizzled operand layout and the epilogue, not just the rounding budget.
+"""
+import numpy as np
+import pytest
+
+from oracle import oracle
+from gq import CudaBackend, GqError, QuantWeight
+from gq import synth
+
+pytestmark = pytest.mark.gpu
+
+
+def rel_l2(a, b):
+    a = np.asarray(a, np.float64).ravel()
+    b = np.asarray(b, np.float64).ravel()
+    return np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30)
+
+
+def bf16_round(x):
+    """Round-to-nearest-even to bf16, returned as f32."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16) << 16
+    return r.astype(np.uint32).view(np.float32).reshape(np.shape(x))
+
+
+@pytest.fixture(scope="module")
+def g():
+    be = CudaBackend(0)
+    yield be
+    be.close()
+
+
+CASES = [  # (m, n, k, bits, signed)
+    (512, 6144, 1536, 4, False),   # config 3 gate/up shape
+    (512, 1536, 6144, 2, False),   # config 3 down shape
+    (128, 256, 64, 8, True),
+    (130, 300, 128, 4, False),     # M and N tails
+    (200, 520, 192, 2, False),
+    (256, 2048, 1536, 8, True),    # I8 q_proj at prefill
+    (384, 96, 256, 8, False),      # U8 8-bit, N < one tile
+]
+
+
+@pytest.mark.parametrize("m,n,k,bits,signed", CASES)
+def test_prefill_linear(g, m, n, k, bits, signed):
+    w = synth.make_qweight(100 + n + k, n, k, bits, signed)
+    x = synth.normal(200 + m, m * k).reshape(m, k)
+    got = g.readback(g.linear(g.tensor(x, x.shape), g.quant_tensor(w))).reshape(m, n)
+    assert rel_l2(got, oracle.linear(x, w)) <= 1e-2
+    assert rel_l2(got, oracle.linear(bf16_round(x), w)) <= 1e-5
+
+
+@pytest.mark.parametrize("m,n,k,bits", [(512, 6144, 1536, 4), (160, 200, 128, 2)])
+def test_prefill_geglu(g, m, n, k, bits):
+    wg = synth.make_qweight(300 + n, n, k, bits)
+    wu = synth.make_qweight(301 + n, n, k, bits)
+    x = synth.normal(302, m * k).reshape(m, k)
+    got = g.readback(g.linear_geglu(g.tensor(x, x.shape), g.quant_tensor(wg), g.quant_tensor(wu))).reshape(m, n)
+    assert rel_l2(got, oracle.linear_geglu(x, wg, wu)) <= 1e-2
+    assert rel_l2(got, oracle.linear_geglu(bf16_round(x), wg, wu)) <= 1e-5
+
+
+def test_prefill_gelu_mul_cols_and_softcap(g):
+    m, n, k = 192, 256, 1536
+    w = synth.make_qweight(401, n, k, 8, True)
+    x = synth.normal(402, m * k).reshape(m, k)
+    ple = synth.normal(403, m * 8960).reshape(m, 8960)
+    got = g.readback(g.linear_gelu_mul_cols(g.tensor(x, x.shape), g.quant_tensor(w), g.tensor(ple, ple.shape),
+                                            7 * 256)).reshape(m, n)
+    assert rel_l2(got, oracle.linear_gelu_mul_cols(bf16_round(x), w, ple, 7 * 256)) <= 1e-5
+    wl = synth.make_qweight(404, 4096, k, 8, True)
+    xs = (4.0 * synth.normal(405, m * k)).reshape(m, k)
+    full = g.zeros((m, 3 * 4096))
+    g.linear_softcap(g.tensor(xs, xs.shape), g.quant_tensor(wl), 30.0, out=full, col0=4096)
+    got = g.readback(full).reshape(m, 3 * 4096)
+    ref = oracle.softcap(oracle.linear(bf16_round(xs), wl), 30.0)
+    assert rel_l2(got[:, 4096:8192], ref) <= 1e-5
+    assert not got[:, :4096].any() and not got[:, 8192:].any()
+
+
+def test_prefill_reference_tile_sizes(g):
+    """The reference's tiled-path cases (rust/tests/gpu.rs:335-349 shapes scaled to
+    K % 64 == 0): partial 128-row tiles and N not a multiple of the tile."""
+    for bits in (2, 4, 8):
+        w = synth.make_qweight(500 + bits, 70, 128, bits, bits == 8)
+        for m in (128, 129, 255):
+            x = synth.normal(600 + m, m * 128).reshape(m, 128)
+            got = g.readback(g.linear(g.tensor(x, x.shape), g.quant_tensor(w))).reshape(m, 70)
+            assert rel_l2(got, oracle.linear(bf16_round(x), w)) <= 1e-5, (bits, m)
