@@ -7,17 +7,19 @@
 // weight, 2 gelu * column slice) plus MODE 3 (logit soft-cap).
 //
 // Design (B200, HBM-bound):
-//  * Persistent CTAs, two per SM, each owning a contiguous range of weight rows.
+//  * Persistent CTAs, one per SM, each owning a contiguous range of weight rows;
+//    registers and shared memory are sized so the next kernel's CTA fits beside
+//    it and prefetches its own weights under programmatic dependent launch.
 //    Rows are contiguous in the packed layout, so a CTA's work is one contiguous
 //    byte range, streamed into shared memory by the TMA engine with 1-D bulk
 //    copies (cp.async.bulk) through a ring of mbarrier-tracked stages. Copies for
 //    the first stages are issued before griddepcontrol.wait, so under
 //    programmatic dependent launch the weight stream of this kernel overlaps the
 //    tail of the kernel that produces x.
-//  * Inside a stage the work is balanced at 16-byte-chunk granularity: thread t
-//    takes chunks t, t+256, ... of the stage, whatever row they belong to, and
-//    writes one partial sum per chunk; then one warp per row adds that row's
-//    partials with shuffles and runs the epilogue.
+//  * Inside a stage each row belongs to a group of lanes of one warp, which
+//    reduces its sum with shuffles and runs the epilogue; warps progress
+//    independently (no block barrier per stage) and the last warp to finish a
+//    stage issues its refill.
 //  * Dequantization costs one LOP3 + one FFMA per code. A code field masked in
 //    place, (word & (mask << pos)), read as an f32 bit pattern is the subnormal
 //    raw * 2^(pos-149); FFMA handles subnormal inputs at full rate and exactly.
@@ -37,7 +39,10 @@ namespace {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
-constexpr int kCtasPerSm = 2;  // one CTA's epilogue overlaps the other's stream
+// One CTA per SM is launched, but registers and shared memory are sized so that
+// two fit: the next kernel's CTA (programmatic dependent launch) becomes
+// resident while this one streams, and prefetches its own weights.
+constexpr int kResident = 2;
 constexpr int kMaxStages = 4;
 
 struct GemvArgs {
@@ -57,8 +62,9 @@ struct GemvArgs {
   int64_t ldy, y_col0;
   int row_bytes;    // bytes per packed row, multiple of 16
   int rows_per_cta; // contiguous rows per CTA
-  int tile_rows;    // rows per pipeline stage
+  int tile_rows;    // rows per pipeline stage (a multiple of the rows one pass covers)
   int stages;       // pipeline depth
+  int lanes;        // lanes per row (power of two dividing row_bytes/16)
   uint32_t *err;
 };
 
@@ -80,34 +86,13 @@ __host__ __device__ constexpr int code_pos(int j) {
   return j < Fmt<BITS>::kSplit ? j * BITS : j * BITS - Fmt<BITS>::kShift;
 }
 
-// ---- block reduction of (sum in double, max in float) in one pass --------------
-__device__ __forceinline__ void block_sum_max(double &sum, float &mx, double *dscr, float *fscr) {
-  for (int o = 16; o > 0; o >>= 1) {
-    sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  }
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  __syncthreads();
-  if (lane == 0) {
-    dscr[warp] = sum;
-    fscr[warp] = mx;
-  }
-  __syncthreads();
-  sum = 0.0;
-  mx = 0.0f;
-  for (int i = 0; i < kWarps; ++i) {
-    sum += dscr[i];
-    mx = fmaxf(mx, fscr[i]);
-  }
-}
-
 __device__ __forceinline__ float pow2f(int e) {  // exact 2^e for e in [-126, 127]
   return __int_as_float((e + 127) << 23);
 }
 
 // Shared-memory carve-up, identical on host (sizing) and device (addressing).
 struct GemvSmem {
-  size_t stage_off, xs_off, red_off, bar_off, dscr_off, fscr_off, par_off, total;
+  size_t stage_off, xs_off, bar_off, cnt_off, dscr_off, fscr_off, par_off, total;
 };
 __host__ __device__ inline size_t align16(size_t v) { return (v + 15) & ~size_t(15); }
 __host__ __device__ inline GemvSmem gemv_layout(int bits, int mt, int nw, int row_bytes,
@@ -118,47 +103,108 @@ __host__ __device__ inline GemvSmem gemv_layout(int bits, int mt, int nw, int ro
   size_t o = 0;
   L.stage_off = o; o = align16(o + (size_t)stages * nw * tile_rows * row_bytes);
   L.xs_off = o;    o = align16(o + (size_t)mt * C * (per_chunk + 4) * sizeof(float));
-  L.red_off = o;   o = align16(o + (size_t)nw * mt * tile_rows * C * sizeof(float));
   L.bar_off = o;   o = align16(o + kMaxStages * sizeof(uint64_t));
-  L.dscr_off = o;  o = align16(o + kWarps * sizeof(double));
-  L.fscr_off = o;  o = align16(o + kWarps * sizeof(float));
+  L.cnt_off = o;   o = align16(o + kMaxStages * sizeof(uint32_t));
+  L.dscr_off = o;  o = align16(o + (size_t)kWarps * mt * sizeof(double));
+  L.fscr_off = o;  o = align16(o + (size_t)kWarps * mt * sizeof(float));
   L.par_off = o;   o = align16(o + (size_t)mt * (sizeof(double) + 2 * sizeof(float)));
   L.total = o;
   return L;
 }
 
+__device__ __forceinline__ uint32_t lop3_xor_and(uint32_t a, uint32_t x, uint32_t m) {
+  uint32_t r;  // (a ^ x) & m in one instruction
+  asm("lop3.b32 %0, %1, %2, %3, 0x28;" : "=r"(r) : "r"(a), "r"(x), "r"(m));
+  return r;
+}
+
+// MAC of one 16-byte chunk (4 words) of NW weights against MT activation rows.
+// acc[h][m][q]: ACC independent accumulators per (weight, row). Each code costs
+// one LOP3 (mask, with the I8 sign flip folded in) and one FFMA per row.
+template <int BITS, bool SIGNED, int MT, int NW, int ACC>
+__device__ __forceinline__ void mac_chunk(const uint4 (&wv)[NW], const float *xc, int xs_mstride,
+                                          float (&acc)[NW][MT][ACC]) {
+  using F = Fmt<BITS>;
+  constexpr uint32_t kMask = (1u << BITS) - 1u;
+  constexpr uint32_t kXor = (BITS == 8 && SIGNED) ? 0x80808080u : 0u;
+#pragma unroll
+  for (int wi = 0; wi < 4; ++wi) {
+    uint32_t lo[NW], hi[NW];
+#pragma unroll
+    for (int h = 0; h < NW; ++h) {
+      lo[h] = (wi == 0 ? wv[h].x : wi == 1 ? wv[h].y : wi == 2 ? wv[h].z : wv[h].w);
+      hi[h] = lo[h] >> F::kShift;
+    }
+#pragma unroll
+    for (int j4 = 0; j4 < F::kPerWord; j4 += 4) {
+      float4 xv[MT];
+#pragma unroll
+      for (int m = 0; m < MT; ++m)
+        xv[m] = *reinterpret_cast<const float4 *>(xc + m * xs_mstride + wi * F::kPerWord + j4);
+#pragma unroll
+      for (int jj = 0; jj < 4; ++jj) {
+        const int j = j4 + jj;
+#pragma unroll
+        for (int h = 0; h < NW; ++h) {
+          const uint32_t src = (j < F::kSplit) ? lo[h] : hi[h];
+          const uint32_t mask = kMask << code_pos<BITS>(j);
+          const uint32_t xr = (j < F::kSplit) ? kXor : (kXor >> F::kShift);
+          const float fld = __uint_as_float(kXor ? lop3_xor_and(src, xr & mask, mask) : (src & mask));
+#pragma unroll
+          for (int m = 0; m < MT; ++m) {
+            const float xvj = jj == 0 ? xv[m].x : jj == 1 ? xv[m].y : jj == 2 ? xv[m].z : xv[m].w;
+            acc[h][m][j % ACC] = __fmaf_rn(xvj, fld, acc[h][m][j % ACC]);
+          }
+        }
+      }
+    }
+  }
+}
+
 // ---- the kernel -----------------------------------------------------------------
+// Work mapping: a row of C 16-byte chunks belongs to LANES consecutive lanes of
+// one warp (LANES = the largest power of two <= 32 dividing C); lane li of the
+// group takes chunks li, li+LANES, ... so a stage's rows are read as contiguous
+// 16*LANES-byte runs. A warp holds 32/LANES rows at once and walks the stage's
+// rows in passes of kWarps*32/LANES. Row sums are reduced with shuffles inside
+// the lane group; no block barrier is needed per stage: the last warp to finish
+// a stage refills it.
 template <int BITS, bool SIGNED, int MT, int MODE>
-__global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q_kernel(const GemvArgs a) {
+__global__ void __launch_bounds__(kThreads, kResident) gemv_q_kernel(const GemvArgs a) {
   using F = Fmt<BITS>;
   constexpr int NW = (MODE == 1) ? 2 : 1;  // weights streamed together
   constexpr int ACC = (MT == 1) ? 4 : (MT == 2 ? 2 : 1);
-  constexpr uint32_t kMask = (1u << BITS) - 1u;
-  constexpr uint32_t kXor = (BITS == 8 && SIGNED) ? 0x80808080u : 0u;
 
   extern __shared__ __align__(128) uint8_t smem[];
   const int C = a.row_bytes >> 4;  // chunks per row
   const int stage_bytes = a.tile_rows * a.row_bytes;
-  const int tile_chunks = a.tile_rows * C;
   const GemvSmem L = gemv_layout(BITS, MT, NW, a.row_bytes, a.tile_rows, a.stages);
   uint8_t *stage_buf = smem + L.stage_off;                        // [stages][NW][stage_bytes]
   float *xs = reinterpret_cast<float *>(smem + L.xs_off);         // [MT][C][kPad]
-  float *red = reinterpret_cast<float *>(smem + L.red_off);       // [NW][MT][tile_chunks]
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bar_off);  // [kMaxStages]
-  double *dscr = reinterpret_cast<double *>(smem + L.dscr_off);   // [kWarps]
-  float *fscr = reinterpret_cast<float *>(smem + L.fscr_off);     // [kWarps]
+  uint32_t *done = reinterpret_cast<uint32_t *>(smem + L.cnt_off);  // [kMaxStages]
+  double *dscr = reinterpret_cast<double *>(smem + L.dscr_off);   // [kWarps][MT]
+  float *fscr = reinterpret_cast<float *>(smem + L.fscr_off);     // [kWarps][MT]
   double *pow2_s = reinterpret_cast<double *>(smem + L.par_off);  // [MT]
   float *mu_s = reinterpret_cast<float *>(pow2_s + MT);           // [MT]
   float *corr_s = mu_s + MT;                                      // [MT]
 
   const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
   const int n_begin = blockIdx.x * a.rows_per_cta;
   const int n_end = min(a.N, n_begin + a.rows_per_cta);
   const int m0 = blockIdx.y * MT;
   const int nrows = n_end - n_begin;
   const int ntiles = nrows > 0 ? (nrows + a.tile_rows - 1) / a.tile_rows : 0;
+  const int xs_mstride = C * F::kPad;
+  const int lanes = a.lanes;                 // lanes per row (power of two)
+  const int li = lane & (lanes - 1);         // lane within the row group
+  const int grp = lane / lanes;              // row group within the warp
+  const int rpw = 32 / lanes;                // rows per warp per pass
+  const int rows_per_pass = kWarps * rpw;
+  const int cpl = C / lanes;                 // chunks per lane per row
 
-  int issued = 0;  // tiles whose copies thread 0 has issued
+  int issued = 0;  // tiles whose copies have been issued (meaningful in the issuing thread)
   auto issue = [&](int t) {
     issued = t + 1;
     const int stage = t % a.stages;
@@ -173,7 +219,10 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q_kernel(const Gemv
   };
 
   if (tid == 0) {
-    for (int i = 0; i < a.stages; ++i) gqd::mbar_init(&bars[i], 1);
+    for (int i = 0; i < a.stages; ++i) {
+      gqd::mbar_init(&bars[i], 1);
+      done[i] = 0;
+    }
     gqd::fence_mbar_init();
   }
   __syncthreads();
@@ -181,73 +230,139 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q_kernel(const Gemv
   if (tid == 0)
     for (int t = 0; t < min(a.stages, ntiles); ++t) issue(t);
 
+  // Let the next kernel's CTAs launch now: they co-reside (registers and shared
+  // memory are sized for two CTAs per SM) and prefetch their own weights while
+  // this grid streams; they wait for this grid's results in griddepcontrol.wait.
+  gqd::griddep_launch_dependents();
   gqd::griddep_wait();
 
   // ---- stage x: x' = x - mu, scaled by 2^(S - pos) into the padded layout ----
-  // mu and S come from one (sum, max|x|) reduction; S leaves one bit of headroom
-  // for |x - mu| <= 2 max|x|. zp * sum(x') is taken as sum(x) - K*mu in double:
-  // the per-element rounding of x - mu it ignores is below 2^-24 relative.
-  for (int m = 0; m < MT; ++m) {
-    const bool live = (m0 + m) < a.M;
-    const float *xr = a.x + (size_t)(m0 + m) * a.ldx;
-    double sx = 0.0;
-    float mx = 0.0f;
-    if (live)
-      for (int k = tid * 4; k < a.K; k += kThreads * 4) {
-        const float4 v = *reinterpret_cast<const float4 *>(xr + k);
-        sx += (double)v.x + (double)v.y + (double)v.z + (double)v.w;
-        mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-      }
-    block_sum_max(sx, mx, dscr, fscr);
-    const float mu = live && a.K > 0 ? (float)(sx / (double)a.K) : 0.0f;
-    int e = 0;
-    if (mx > 0.0f && isfinite(mx)) frexpf(mx, &e);  // mx < 2^e, so |x - mu| < 2^(e+1)
-    int S = 125 - e;
-    S = max(-100, min(126, S));
-    float *xm = xs + (size_t)m * C * F::kPad;
-    for (int k = tid * 4; k < a.K; k += kThreads * 4) {
-      float4 v = live ? *reinterpret_cast<const float4 *>(xr + k) : make_float4(0.f, 0.f, 0.f, 0.f);
-      float vv[4] = {__fsub_rn(v.x, mu), __fsub_rn(v.y, mu), __fsub_rn(v.z, mu), __fsub_rn(v.w, mu)};
-      if (!live) vv[0] = vv[1] = vv[2] = vv[3] = 0.0f;
-      float o[4];
+  // One global read of x (held in registers up to kXv float4 per thread and row),
+  // one (sum, max|x|) reduction for all MT rows giving mu and S (S leaves one
+  // bit of headroom for |x - mu| <= 2 max|x|), then the scaled write. zp*sum(x')
+  // is taken as sum(x) - K*mu in double (the per-element rounding of x - mu it
+  // ignores is below 2^-24 relative).
+  {
+    constexpr int kXv = (MT == 1) ? 6 : (MT == 2 ? 3 : 2);
+    float4 xv[MT][kXv];
+    double sx[MT];
+    float mx[MT];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) o[i] = vv[i] * pow2f(S - code_pos<BITS>((k + i) % F::kPerWord));
-      *reinterpret_cast<float4 *>(xm + (k / F::kPerChunk) * F::kPad + (k % F::kPerChunk)) =
-          make_float4(o[0], o[1], o[2], o[3]);
+    for (int m = 0; m < MT; ++m) {
+      sx[m] = 0.0;
+      mx[m] = 0.0f;
+      const bool live = m0 + m < a.M;
+      const float *xr = a.x + (size_t)(m0 + m) * a.ldx;
+#pragma unroll
+      for (int i = 0; i < kXv; ++i) {
+        const int k = (tid + i * kThreads) * 4;
+        xv[m][i] = (live && k < a.K) ? __ldg(reinterpret_cast<const float4 *>(xr + k)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      for (int k = (tid + kXv * kThreads) * 4; live && k < a.K; k += kThreads * 4) {
+        const float4 v = __ldg(reinterpret_cast<const float4 *>(xr + k));
+        sx[m] += ((double)v.x + (double)v.y) + ((double)v.z + (double)v.w);
+        mx[m] = fmaxf(mx[m], fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+      }
+#pragma unroll
+      for (int i = 0; i < kXv; ++i) {
+        const float4 v = xv[m][i];
+        sx[m] += ((double)v.x + (double)v.y) + ((double)v.z + (double)v.w);
+        mx[m] = fmaxf(mx[m], fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        sx[m] += __shfl_xor_sync(0xffffffffu, sx[m], o);
+        mx[m] = fmaxf(mx[m], __shfl_xor_sync(0xffffffffu, mx[m], o));
+      }
+      if (lane == 0) {
+        dscr[warp * MT + m] = sx[m];
+        fscr[warp * MT + m] = mx[m];
+      }
     }
-    if (tid == 0) {
-      mu_s[m] = mu;
-      const double sxp = live ? sx - (double)a.K * (double)mu : 0.0;
-      corr_s[m] = (float)((double)F::kZp * sxp * ldexp(1.0, S - 149));
-      pow2_s[m] = ldexp(1.0, 149 - S);
+    __syncthreads();
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      double sum = 0.0;
+      float mxx = 0.0f;
+      for (int i = 0; i < kWarps; ++i) {
+        sum += dscr[i * MT + m];
+        mxx = fmaxf(mxx, fscr[i * MT + m]);
+      }
+      const bool live = (m0 + m) < a.M;
+      const float mu = live && a.K > 0 ? (float)(sum / (double)a.K) : 0.0f;
+      int e = 0;
+      if (mxx > 0.0f && isfinite(mxx)) frexpf(mxx, &e);  // mx < 2^e, so |x - mu| < 2^(e+1)
+      int S = 125 - e;
+      S = max(22, min(126, S));  // 2^(149-S) stays a normal f32 for the epilogue
+      float *xm = xs + (size_t)m * xs_mstride;
+      const float *xr = a.x + (size_t)(m0 + m) * a.ldx;
+      auto put = [&](int k, float4 v) {
+        float o[4] = {0.f, 0.f, 0.f, 0.f};
+        if (live) {
+          const float vv[4] = {__fsub_rn(v.x, mu), __fsub_rn(v.y, mu), __fsub_rn(v.z, mu), __fsub_rn(v.w, mu)};
+#pragma unroll
+          for (int i = 0; i < 4; ++i) o[i] = vv[i] * pow2f(S - code_pos<BITS>((k + i) % F::kPerWord));
+        }
+        *reinterpret_cast<float4 *>(xm + (k / F::kPerChunk) * F::kPad + (k % F::kPerChunk)) =
+            make_float4(o[0], o[1], o[2], o[3]);
+      };
+#pragma unroll
+      for (int i = 0; i < kXv; ++i) {
+        const int k = (tid + i * kThreads) * 4;
+        if (k < a.K) put(k, xv[m][i]);
+      }
+      for (int k = (tid + kXv * kThreads) * 4; k < a.K; k += kThreads * 4)
+        put(k, live ? __ldg(reinterpret_cast<const float4 *>(xr + k)) : make_float4(0.f, 0.f, 0.f, 0.f));
+      if (tid == 0) {
+        mu_s[m] = mu;
+        const double sxp = live ? sum - (double)a.K * (double)mu : 0.0;
+        corr_s[m] = (float)((double)F::kZp * sxp * ldexp(1.0, S - 149));
+        pow2_s[m] = ldexp(1.0, 149 - S);
+      }
     }
   }
   __syncthreads();
-  gqd::griddep_launch_dependents();
+
+  float mu_r[MT], corr_r[MT], p2_r[MT];
+#pragma unroll
+  for (int m = 0; m < MT; ++m) {
+    mu_r[m] = mu_s[m];
+    corr_r[m] = corr_s[m];
+    p2_r[m] = (float)pow2_s[m];
+  }
 
   bool failed = false;
-  int t_fail = 0;
+  int t_fail = ntiles;
   for (int t = 0; t < ntiles; ++t) {
     const int stage = t % a.stages;
-    const uint32_t parity = (uint32_t)(t / a.stages) & 1u;
-    const bool ok = gqd::mbar_wait_bounded(&bars[stage], parity);
-    if (__syncthreads_or(!ok)) {
+    const int r0 = n_begin + t * a.tile_rows;
+    const int rows = min(a.tile_rows, n_end - r0);
+    const uint8_t *buf = stage_buf + (size_t)stage * NW * stage_bytes;
+    if (!gqd::mbar_wait_bounded(&bars[stage], (uint32_t)(t / a.stages) & 1u)) {
       failed = true;
       t_fail = t;
       break;
     }
-    const int r0 = n_begin + t * a.tile_rows;
-    const int rows = min(a.tile_rows, n_end - r0);
-    const int nch = rows * C;
-    const uint8_t *buf = stage_buf + (size_t)stage * NW * stage_bytes;
-
-    int r = tid / C, c = tid - (tid / C) * C;  // (row, chunk) of f, advanced without division
-    const int dr = kThreads / C, dc = kThreads - (kThreads / C) * C;
-    for (int f = tid; f < nch; f += kThreads) {
-      uint4 wv[NW];
+    for (int rr = warp * rpw + grp; rr - grp < rows; rr += rows_per_pass) {
+      const bool live_row = rr < rows;
+      const int n = r0 + rr;
+      // epilogue operands: issued now, used after the row's MAC work
+      float sc0 = 0.f, qs0 = 0.f, sc1 = 0.f, qs1 = 0.f, bsv[MT];
 #pragma unroll
-      for (int h = 0; h < NW; ++h)
-        wv[h] = *reinterpret_cast<const uint4 *>(buf + h * stage_bytes + (size_t)r * a.row_bytes + c * 16);
+      for (int m = 0; m < MT; ++m) bsv[m] = 0.f;
+      if (live_row && li == 0) {
+        sc0 = __ldg(a.s + n);
+        qs0 = __ldg(a.qsum + n);
+        if (NW == 2) {
+          sc1 = __ldg(a.s2 + n);
+          qs1 = __ldg(a.qsum2 + n);
+        }
+        if (MODE == 2) {
+#pragma unroll
+          for (int m = 0; m < MT; ++m)
+            if (m0 + m < a.M) bsv[m] = a.bs[(size_t)(m0 + m) * a.b_stride + a.b_off + n];
+        }
+      }
       float acc[NW][MT][ACC];
 #pragma unroll
       for (int h = 0; h < NW; ++h)
@@ -255,107 +370,87 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) gemv_q_kernel(const Gemv
         for (int m = 0; m < MT; ++m)
 #pragma unroll
           for (int q = 0; q < ACC; ++q) acc[h][m][q] = 0.0f;
-      const float *xc = xs + (size_t)c * F::kPad;
+      if (live_row) {
+        const uint8_t *rowp = buf + (size_t)rr * a.row_bytes;
+        int j = 0;
+        for (; j + 1 < cpl; j += 2) {  // two chunks in flight
+          const int ca = li + j * lanes, cb = ca + lanes;
+          uint4 wa[NW], wb[NW];
 #pragma unroll
-      for (int wi = 0; wi < 4; ++wi) {
-        uint32_t lo[NW], hi[NW];
-#pragma unroll
-        for (int h = 0; h < NW; ++h) {
-          const uint32_t word = (wi == 0 ? wv[h].x : wi == 1 ? wv[h].y : wi == 2 ? wv[h].z : wv[h].w) ^ kXor;
-          lo[h] = word;
-          hi[h] = word >> F::kShift;
-        }
-#pragma unroll
-        for (int j4 = 0; j4 < F::kPerWord; j4 += 4) {
-          float4 xv[MT];
-#pragma unroll
-          for (int m = 0; m < MT; ++m)
-            xv[m] = *reinterpret_cast<const float4 *>(xc + (size_t)m * C * F::kPad + wi * F::kPerWord + j4);
-#pragma unroll
-          for (int jj = 0; jj < 4; ++jj) {
-            const int j = j4 + jj;
-#pragma unroll
-            for (int h = 0; h < NW; ++h) {
-              const uint32_t src = (j < F::kSplit) ? lo[h] : hi[h];
-              const float fld = __uint_as_float(src & (kMask << code_pos<BITS>(j)));
-#pragma unroll
-              for (int m = 0; m < MT; ++m) {
-                const float xvj = jj == 0 ? xv[m].x : jj == 1 ? xv[m].y : jj == 2 ? xv[m].z : xv[m].w;
-                acc[h][m][j % ACC] = __fmaf_rn(xvj, fld, acc[h][m][j % ACC]);
-              }
-            }
+          for (int h = 0; h < NW; ++h) {
+            wa[h] = *reinterpret_cast<const uint4 *>(rowp + h * stage_bytes + ca * 16);
+            wb[h] = *reinterpret_cast<const uint4 *>(rowp + h * stage_bytes + cb * 16);
           }
+          mac_chunk<BITS, SIGNED, MT, NW, ACC>(wa, xs + (size_t)ca * F::kPad, xs_mstride, acc);
+          mac_chunk<BITS, SIGNED, MT, NW, ACC>(wb, xs + (size_t)cb * F::kPad, xs_mstride, acc);
+        }
+        if (j < cpl) {
+          const int ca = li + j * lanes;
+          uint4 wa[NW];
+#pragma unroll
+          for (int h = 0; h < NW; ++h) wa[h] = *reinterpret_cast<const uint4 *>(rowp + h * stage_bytes + ca * 16);
+          mac_chunk<BITS, SIGNED, MT, NW, ACC>(wa, xs + (size_t)ca * F::kPad, xs_mstride, acc);
         }
       }
+      float v[NW][MT];
 #pragma unroll
       for (int h = 0; h < NW; ++h)
 #pragma unroll
         for (int m = 0; m < MT; ++m) {
-          float v = acc[h][m][0];
+          float s = acc[h][m][0];
 #pragma unroll
-          for (int q = 1; q < ACC; ++q) v += acc[h][m][q];
-          red[((size_t)h * MT + m) * tile_chunks + f] = v;
+          for (int q = 1; q < ACC; ++q) s += acc[h][m][q];
+          for (int o = lanes >> 1; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+          v[h][m] = s;
         }
-      r += dr;
-      c += dc;
-      if (c >= C) {
-        c -= C;
-        ++r;
+      if (live_row && li == 0) {
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+          if (m0 + m >= a.M) break;
+          // ((sum - zp*sum(x')) * 2^(149-S) + mu * sum(q)) * scale, in f32: the
+          // power-of-two factor is exact and the two terms are of the size of
+          // the result
+          const float v0 = __fmul_rn(__fmaf_rn(mu_r[m], qs0, __fmul_rn(__fsub_rn(v[0][m], corr_r[m]), p2_r[m])), sc0);
+          float out;
+          if (MODE == 1) {
+            const float v1 =
+                __fmul_rn(__fmaf_rn(mu_r[m], qs1, __fmul_rn(__fsub_rn(v[NW - 1][m], corr_r[m]), p2_r[m])), sc1);
+            out = __fmul_rn(gqd::gelu_tanh(v0), v1);
+          } else if (MODE == 2) {
+            out = __fmul_rn(gqd::gelu_tanh(v0), bsv[m]);
+          } else if (MODE == 3) {
+            out = a.cap > 0.0f ? __fmul_rn(a.cap, tanhf(__fdiv_rn(v0, a.cap))) : v0;
+          } else {
+            out = v0;
+          }
+          a.y[(size_t)(m0 + m) * a.ldy + a.y_col0 + n] = out;
+        }
       }
     }
-    __syncthreads();  // partials written; stage buffer fully consumed
-    if (tid == 0 && t + a.stages < ntiles) issue(t + a.stages);
-
-    const int warp = tid >> 5, lane = tid & 31;
-    for (int e = warp; e < rows * MT; e += kWarps) {  // one warp per (row, m)
-      const int r2 = e / MT;
-      const int m = e - r2 * MT;
-      if (m0 + m >= a.M) continue;
-      const int n = r0 + r2;
-      float dsum[NW];
-#pragma unroll
-      for (int h = 0; h < NW; ++h) {
-        const float *p = red + ((size_t)h * MT + m) * tile_chunks + (size_t)r2 * C;
-        float v = 0.0f;
-        for (int cc = lane; cc < C; cc += 32) v += p[cc];
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        dsum[h] = v;
+    // This warp is done reading the stage; the last warp to finish refills it.
+    __syncwarp();
+    if (lane == 0) {
+      const uint32_t prev = atomicAdd(&done[stage], 1u);
+      if (prev == kWarps - 1) {
+        atomicExch(&done[stage], 0u);
+        if (t + a.stages < ntiles) issue(t + a.stages);
       }
-      if (lane != 0) continue;
-      const double mu = (double)mu_s[m];
-      const double corr = (double)corr_s[m];
-      const double p2 = pow2_s[m];
-      const float v0 = (float)((((double)dsum[0] - corr) * p2 + mu * (double)a.qsum[n]) * (double)a.s[n]);
-      float out;
-      if (MODE == 1) {
-        const float v1 = (float)((((double)dsum[NW - 1] - corr) * p2 + mu * (double)a.qsum2[n]) * (double)a.s2[n]);
-        out = __fmul_rn(gqd::gelu_tanh(v0), v1);
-      } else if (MODE == 2) {
-        out = __fmul_rn(gqd::gelu_tanh(v0), a.bs[(size_t)(m0 + m) * a.b_stride + a.b_off + n]);
-      } else if (MODE == 3) {
-        out = a.cap > 0.0f ? __fmul_rn(a.cap, tanhf(__fdiv_rn(v0, a.cap))) : v0;
-      } else {
-        out = v0;
-      }
-      a.y[(size_t)(m0 + m) * a.ldy + a.y_col0 + n] = out;
     }
-    // The partial buffer is rewritten by the next tile only after the barrier
-    // at the top of the next iteration.
-    __syncthreads();
   }
 
-  if (failed) {
+  // A timed-out wait leaves this warp; report it and drain (bounded) the copies
+  // this CTA may still have in flight before its shared memory is released.
+  const bool any_failed = __syncthreads_or(failed);
+  if (any_failed) {
     if (tid == 0) {
       gqd::report(a.err, GQ_DEVERR_WAIT_TIMEOUT);
-      // Drain copies still in flight (bounded) before the CTA's shared memory
-      // is released: tiles [t_fail, issued) each own a distinct stage.
-      for (int t = t_fail; t < issued; ++t)
-        (void)gqd::mbar_wait_bounded(&bars[t % a.stages], (uint32_t)(t / a.stages) & 1u,
-                                     100000000ull);
+      for (int s = 0; s < a.stages; ++s) (void)gqd::mbar_wait_bounded(&bars[s], 0u, 50000000ull);
+      for (int s = 0; s < a.stages; ++s) (void)gqd::mbar_wait_bounded(&bars[s], 1u, 50000000ull);
     }
     __syncthreads();
   }
+  (void)t_fail;
+  (void)issued;
 }
 
 template <int BITS, bool SIGNED, int MT, int MODE>
@@ -404,7 +499,10 @@ bool gq_gemv_supported(gq_ctx *ctx, const gq_qweight *w, int64_t m, int nw) {
   if (w->n > (1ll << 30)) return false;
   const int mt = m <= 1 ? 1 : (m == 2 ? 2 : 4);
   if (w->k % 4 != 0) return false;
-  return gemv_smem_bytes(w->bits, mt, nw, (int)w->row_bytes, 1, 2) <= ctx->smem_optin / kCtasPerSm - 1024;
+  int lanes = 32;
+  while ((w->row_bytes / 16) % lanes != 0) lanes >>= 1;
+  return gemv_smem_bytes(w->bits, mt, nw, (int)w->row_bytes, kWarps * (32 / lanes), 2) <=
+         ctx->smem_optin / kResident - 1024;
 }
 
 // mode: 0 plain, 1 geglu (w2 = up), 2 gelu * bs slice, 3 soft-cap.
@@ -439,29 +537,54 @@ int gq_gemv_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq_qw
   a.row_bytes = rb;
   a.err = ctx->dev_err;
 
-  // Grid: kCtasPerSm CTAs per SM over contiguous row ranges.
-  const int gx_max = ctx->num_sms * kCtasPerSm;
-  int rows_per_cta = (int)((w->n + gx_max - 1) / gx_max);
-  if (rows_per_cta < 1) rows_per_cta = 1;
+  // Grid: one CTA per SM over contiguous row ranges.
+  int rows_per_cta0 = (int)((w->n + ctx->num_sms - 1) / ctx->num_sms);
+  if (rows_per_cta0 < 1) rows_per_cta0 = 1;
+  // Lanes per row: a power of two dividing the chunk count. Fewer lanes per row
+  // amortise the row's shuffle reduction and epilogue over more chunks per lane
+  // and let row groups share the shared-memory reads of x; more lanes per row
+  // keep all warps busy when a CTA owns few rows. Take the fewest lanes (>= 4)
+  // whose passes are at least 85% occupied.
+  int lanes = 32;
+  while (C % lanes != 0) lanes >>= 1;
+  const int max_lanes = lanes;
+  for (int l = 4; l <= max_lanes; l <<= 1) {
+    if (C % l != 0) continue;
+    const int rpp = kWarps * (32 / l);
+    // two stages of one pass each, plus the staged x, must fit
+    if (l != max_lanes && ((size_t)rpp * rb * nw > 48 * 1024 ||
+                           gemv_smem_bytes(w->bits, mt, nw, rb, rpp, 2) > ctx->smem_optin / kResident - 1024))
+      continue;
+    const int passes = (rows_per_cta0 + rpp - 1) / rpp;
+    if (rows_per_cta0 >= (int)(0.85 * passes * rpp) || l == max_lanes) {
+      lanes = l;
+      break;
+    }
+  }
+  const int rows_per_pass = kWarps * (32 / lanes);
+  const int rows_per_cta = rows_per_cta0;
   const int gx = (int)((w->n + rows_per_cta - 1) / rows_per_cta);
-  // Stage size: about 1024 chunks (4 per thread) and <= 16 KB per weight.
-  int tile_rows = max(1, 1024 / C);
-  tile_rows = min(tile_rows, max(1, (16 * 1024) / rb));
-  tile_rows = min(tile_rows, rows_per_cta);
+  // Stage size: whole passes, >= 24 KB per copy where the rows allow (large bulk
+  // copies stream fastest), <= 32 KB per weight.
+  int passes = 1;
+  while ((passes + 1) * rows_per_pass * rb * nw <= 48 * 1024 && passes * rows_per_pass * rb < 24 * 1024) ++passes;
+  int tile_rows = passes * rows_per_pass;
+  if (tile_rows > rows_per_cta) tile_rows = ((rows_per_cta + rows_per_pass - 1) / rows_per_pass) * rows_per_pass;
   const int ntiles = (rows_per_cta + tile_rows - 1) / tile_rows;
   int stages = min(kMaxStages, ntiles);
-  const size_t smem_cap = ctx->smem_optin / kCtasPerSm - 1024;
+  const size_t smem_cap = ctx->smem_optin / kResident - 1024;
   size_t smem = gemv_smem_bytes(w->bits, mt, nw, rb, tile_rows, stages);
-  while (smem > smem_cap && (stages > 1 || tile_rows > 1)) {
+  while (smem > smem_cap && (stages > 2 || tile_rows > rows_per_pass)) {
     if (stages > 2) --stages;
-    else if (tile_rows > 1) tile_rows = (tile_rows + 1) / 2;
-    else --stages;
+    else tile_rows -= rows_per_pass;
     smem = gemv_smem_bytes(w->bits, mt, nw, rb, tile_rows, stages);
   }
-  if (smem > smem_cap) return gq_fail(ctx, GQ_ERR_UNSUPPORTED, "gemv: shared memory");
+  if (smem > smem_cap || tile_rows < 1 || stages < 1)
+    return gq_fail(ctx, GQ_ERR_UNSUPPORTED, "gemv: no stage configuration fits shared memory");
   a.rows_per_cta = rows_per_cta;
   a.tile_rows = tile_rows;
   a.stages = stages;
+  a.lanes = lanes;
   dim3 grid(gx, (unsigned)((m + mt - 1) / mt));
   if (w->bits == 4) return launch_mt<4, false>(ctx, mt, mode, a, grid, smem);
   if (w->bits == 2) return launch_mt<2, false>(ctx, mt, mode, a, grid, smem);

@@ -183,6 +183,17 @@ def test_lm_head_softcap_and_shard_slice(g, m):
     assert not got[:, :n].any() and not got[:, 2 * n:].any()
 
 
+@pytest.mark.parametrize("n,k,bits,signed", [(65536, 1536, 8, True), (32768, 1536, 8, True),
+                                              (40000, 1536, 4, False), (20000, 6144, 2, False)])
+def test_lm_head_scale_shapes(g, n, k, bits, signed):
+    """Row counts of a full or sharded vocab projection (thousands of rows per
+    CTA, deep pipelines, large stage sizes)."""
+    w = synth.random_qweight(900 + n, n, k, bits, signed)
+    x = synth.normal(901, k).reshape(1, k)
+    got = g.readback(g.linear(g.tensor(x, x.shape), g.quant_tensor(w)))
+    assert rel_l2(got, oracle.linear(x, w)) <= REL_L2_FFMA
+
+
 @pytest.mark.parametrize("kind", ["mean", "outlier", "tiny", "huge"])
 def test_precision_robustness(g, kind):
     """Activations with a large mean, an outlier channel, or extreme scale."""
