@@ -37,8 +37,9 @@
 
 namespace {
 
-constexpr int kThreads = 256;
-constexpr int kWarps = kThreads / 32;
+constexpr int kThreads = 256;        // narrow variant (two CTAs fit per SM)
+constexpr int kWideThreads = 512;    // wide variant for CTAs that own many rows
+constexpr int kMaxWarps = kWideThreads / 32;
 // One CTA per SM is launched, but registers and shared memory are sized so that
 // two fit: the next kernel's CTA (programmatic dependent launch) becomes
 // resident while this one streams, and prefetches its own weights.
@@ -65,6 +66,7 @@ struct GemvArgs {
   int tile_rows;    // rows per pipeline stage (a multiple of the rows one pass covers)
   int stages;       // pipeline depth
   int lanes;        // lanes per row (power of two dividing row_bytes/16)
+  double inv_k;     // 1 / K
   uint32_t *err;
 };
 
@@ -101,26 +103,22 @@ __host__ __device__ inline GemvSmem gemv_layout(int bits, int mt, int nw, int ro
   const int per_chunk = 4 * (32 / bits);
   GemvSmem L;
   size_t o = 0;
-  L.stage_off = o; o = align16(o + (size_t)stages * nw * tile_rows * row_bytes);
+  // per stage: NW packed weight tiles, then NW x {scale, code sum} per row
+  L.stage_off = o; o = align16(o + (size_t)stages * nw * ((size_t)tile_rows * row_bytes + 2 * tile_rows * sizeof(float)));
   L.xs_off = o;    o = align16(o + (size_t)mt * C * (per_chunk + 4) * sizeof(float));
   L.bar_off = o;   o = align16(o + kMaxStages * sizeof(uint64_t));
   L.cnt_off = o;   o = align16(o + kMaxStages * sizeof(uint32_t));
-  L.dscr_off = o;  o = align16(o + (size_t)kWarps * mt * sizeof(double));
-  L.fscr_off = o;  o = align16(o + (size_t)kWarps * mt * sizeof(float));
+  L.dscr_off = o;  o = align16(o + (size_t)kMaxWarps * mt * sizeof(double));
+  L.fscr_off = o;  o = align16(o + (size_t)kMaxWarps * mt * sizeof(float));
   L.par_off = o;   o = align16(o + (size_t)mt * (sizeof(double) + 2 * sizeof(float)));
   L.total = o;
   return L;
 }
 
-__device__ __forceinline__ uint32_t lop3_xor_and(uint32_t a, uint32_t x, uint32_t m) {
-  uint32_t r;  // (a ^ x) & m in one instruction
-  asm("lop3.b32 %0, %1, %2, %3, 0x28;" : "=r"(r) : "r"(a), "r"(x), "r"(m));
-  return r;
-}
-
 // MAC of one 16-byte chunk (4 words) of NW weights against MT activation rows.
-// acc[h][m][q]: ACC independent accumulators per (weight, row). Each code costs
-// one LOP3 (mask, with the I8 sign flip folded in) and one FFMA per row.
+// acc[h][m][q]: ACC independent accumulators per (weight, row). Per word: one
+// XOR (I8 sign flip to offset binary) and one shift; per code: one AND with an
+// immediate mask and one FFMA per activation row.
 template <int BITS, bool SIGNED, int MT, int NW, int ACC>
 __device__ __forceinline__ void mac_chunk(const uint4 (&wv)[NW], const float *xc, int xs_mstride,
                                           float (&acc)[NW][MT][ACC]) {
@@ -132,7 +130,7 @@ __device__ __forceinline__ void mac_chunk(const uint4 (&wv)[NW], const float *xc
     uint32_t lo[NW], hi[NW];
 #pragma unroll
     for (int h = 0; h < NW; ++h) {
-      lo[h] = (wi == 0 ? wv[h].x : wi == 1 ? wv[h].y : wi == 2 ? wv[h].z : wv[h].w);
+      lo[h] = (wi == 0 ? wv[h].x : wi == 1 ? wv[h].y : wi == 2 ? wv[h].z : wv[h].w) ^ kXor;
       hi[h] = lo[h] >> F::kShift;
     }
 #pragma unroll
@@ -146,10 +144,7 @@ __device__ __forceinline__ void mac_chunk(const uint4 (&wv)[NW], const float *xc
         const int j = j4 + jj;
 #pragma unroll
         for (int h = 0; h < NW; ++h) {
-          const uint32_t src = (j < F::kSplit) ? lo[h] : hi[h];
-          const uint32_t mask = kMask << code_pos<BITS>(j);
-          const uint32_t xr = (j < F::kSplit) ? kXor : (kXor >> F::kShift);
-          const float fld = __uint_as_float(kXor ? lop3_xor_and(src, xr & mask, mask) : (src & mask));
+          const float fld = __uint_as_float(((j < F::kSplit) ? lo[h] : hi[h]) & (kMask << code_pos<BITS>(j)));
 #pragma unroll
           for (int m = 0; m < MT; ++m) {
             const float xvj = jj == 0 ? xv[m].x : jj == 1 ? xv[m].y : jj == 2 ? xv[m].z : xv[m].w;
@@ -163,28 +158,32 @@ __device__ __forceinline__ void mac_chunk(const uint4 (&wv)[NW], const float *xc
 
 // ---- the kernel -----------------------------------------------------------------
 // Work mapping: a row of C 16-byte chunks belongs to LANES consecutive lanes of
-// one warp (LANES = the largest power of two <= 32 dividing C); lane li of the
-// group takes chunks li, li+LANES, ... so a stage's rows are read as contiguous
-// 16*LANES-byte runs. A warp holds 32/LANES rows at once and walks the stage's
-// rows in passes of kWarps*32/LANES. Row sums are reduced with shuffles inside
-// the lane group; no block barrier is needed per stage: the last warp to finish
-// a stage refills it.
-template <int BITS, bool SIGNED, int MT, int MODE>
-__global__ void __launch_bounds__(kThreads, kResident) gemv_q_kernel(const GemvArgs a) {
+// one warp (LANES a power of two dividing C); lane li of the group takes chunks
+// li, li+LANES, ... so a stage's rows are read as contiguous 16*LANES-byte runs.
+// A lane group holds R consecutive rows at once (the x value loaded for a code
+// position feeds all R rows), a warp holds 32/LANES groups, and the CTA walks
+// the stage's rows in passes of WARPS*R*32/LANES. Row sums are reduced with
+// shuffles inside the lane group; no block barrier is needed per stage: the last
+// warp to finish a stage refills it.
+template <int BITS, bool SIGNED, int MT, int MODE, int THREADS, int R>
+__global__ void __launch_bounds__(THREADS, THREADS == kThreads ? kResident : 1) gemv_q_kernel(const GemvArgs a) {
   using F = Fmt<BITS>;
+  constexpr int WARPS = THREADS / 32;
   constexpr int NW = (MODE == 1) ? 2 : 1;  // weights streamed together
-  constexpr int ACC = (MT == 1) ? 4 : (MT == 2 ? 2 : 1);
+  constexpr int NR = NW * R;               // packed rows per lane group
+  constexpr int ACC = (MT * NR == 1) ? 4 : ((MT * NR) == 2 ? 2 : 1);
 
   extern __shared__ __align__(128) uint8_t smem[];
   const int C = a.row_bytes >> 4;  // chunks per row
-  const int stage_bytes = a.tile_rows * a.row_bytes;
+  const int stage_bytes = a.tile_rows * a.row_bytes;                    // one weight's tile
+  const int stage_stride = NW * (stage_bytes + 2 * a.tile_rows * 4);    // weights + row operands
   const GemvSmem L = gemv_layout(BITS, MT, NW, a.row_bytes, a.tile_rows, a.stages);
   uint8_t *stage_buf = smem + L.stage_off;                        // [stages][NW][stage_bytes]
   float *xs = reinterpret_cast<float *>(smem + L.xs_off);         // [MT][C][kPad]
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bar_off);  // [kMaxStages]
   uint32_t *done = reinterpret_cast<uint32_t *>(smem + L.cnt_off);  // [kMaxStages]
-  double *dscr = reinterpret_cast<double *>(smem + L.dscr_off);   // [kWarps][MT]
-  float *fscr = reinterpret_cast<float *>(smem + L.fscr_off);     // [kWarps][MT]
+  double *dscr = reinterpret_cast<double *>(smem + L.dscr_off);   // [WARPS][MT]
+  float *fscr = reinterpret_cast<float *>(smem + L.fscr_off);     // [WARPS][MT]
   double *pow2_s = reinterpret_cast<double *>(smem + L.par_off);  // [MT]
   float *mu_s = reinterpret_cast<float *>(pow2_s + MT);           // [MT]
   float *corr_s = mu_s + MT;                                      // [MT]
@@ -200,22 +199,31 @@ __global__ void __launch_bounds__(kThreads, kResident) gemv_q_kernel(const GemvA
   const int lanes = a.lanes;                 // lanes per row (power of two)
   const int li = lane & (lanes - 1);         // lane within the row group
   const int grp = lane / lanes;              // row group within the warp
-  const int rpw = 32 / lanes;                // rows per warp per pass
-  const int rows_per_pass = kWarps * rpw;
+  const int gpw = 32 / lanes;                // row groups per warp
+  const int rows_per_pass = WARPS * gpw * R;
   const int cpl = C / lanes;                 // chunks per lane per row
 
-  int issued = 0;  // tiles whose copies have been issued (meaningful in the issuing thread)
+  // One stage = the packed rows of the tile plus their scales and code sums
+  // (contiguous per tile; r0 is a multiple of 4 so every copy is 16-byte
+  // aligned, and the allocations are padded past the last row).
   auto issue = [&](int t) {
-    issued = t + 1;
     const int stage = t % a.stages;
     const int r0 = n_begin + t * a.tile_rows;
     const int rows = min(a.tile_rows, n_end - r0);
     const uint32_t bytes = (uint32_t)rows * (uint32_t)a.row_bytes;
+    const uint32_t obytes = ((uint32_t)rows * 4u + 15u) & ~15u;
     uint64_t *bar = &bars[stage];
-    gqd::mbar_arrive_expect_tx(bar, bytes * NW);
-    uint8_t *dst = stage_buf + (size_t)stage * NW * stage_bytes;
+    gqd::mbar_arrive_expect_tx(bar, NW * (bytes + 2 * obytes));
+    uint8_t *dst = stage_buf + (size_t)stage * stage_stride;
+    float *ops = reinterpret_cast<float *>(dst + NW * stage_bytes);
     gqd::bulk_g2s(dst, a.w + (size_t)r0 * a.row_bytes, bytes, bar);
-    if (NW == 2) gqd::bulk_g2s(dst + stage_bytes, a.w2 + (size_t)r0 * a.row_bytes, bytes, bar);
+    gqd::bulk_g2s(ops, a.s + r0, obytes, bar);
+    gqd::bulk_g2s(ops + a.tile_rows, a.qsum + r0, obytes, bar);
+    if (NW == 2) {
+      gqd::bulk_g2s(dst + stage_bytes, a.w2 + (size_t)r0 * a.row_bytes, bytes, bar);
+      gqd::bulk_g2s(ops + 2 * a.tile_rows, a.s2 + r0, obytes, bar);
+      gqd::bulk_g2s(ops + 3 * a.tile_rows, a.qsum2 + r0, obytes, bar);
+    }
   };
 
   if (tid == 0) {
@@ -230,9 +238,10 @@ __global__ void __launch_bounds__(kThreads, kResident) gemv_q_kernel(const GemvA
   if (tid == 0)
     for (int t = 0; t < min(a.stages, ntiles); ++t) issue(t);
 
-  // Let the next kernel's CTAs launch now: they co-reside (registers and shared
-  // memory are sized for two CTAs per SM) and prefetch their own weights while
-  // this grid streams; they wait for this grid's results in griddepcontrol.wait.
+  // Let the next kernel's CTAs launch now: they co-reside (the narrow variant's
+  // registers and shared memory are sized for two CTAs per SM) and prefetch
+  // their own weights while this grid streams; they wait for this grid's
+  // results in griddepcontrol.wait.
   gqd::griddep_launch_dependents();
   gqd::griddep_wait();
 
@@ -243,7 +252,7 @@ __global__ void __launch_bounds__(kThreads, kResident) gemv_q_kernel(const GemvA
   // is taken as sum(x) - K*mu in double (the per-element rounding of x - mu it
   // ignores is below 2^-24 relative).
   {
-    constexpr int kXv = (MT == 1) ? 6 : (MT == 2 ? 3 : 2);
+    constexpr int kXv = (THREADS == kThreads ? 6 : 3) / MT > 0 ? (THREADS == kThreads ? 6 : 3) / MT : 1;
     float4 xv[MT][kXv];
     double sx[MT];
     float mx[MT];
@@ -255,10 +264,10 @@ __global__ void __launch_bounds__(kThreads, kResident) gemv_q_kernel(const GemvA
       const float *xr = a.x + (size_t)(m0 + m) * a.ldx;
 #pragma unroll
       for (int i = 0; i < kXv; ++i) {
-        const int k = (tid + i * kThreads) * 4;
+        const int k = (tid + i * THREADS) * 4;
         xv[m][i] = (live && k < a.K) ? __ldg(reinterpret_cast<const float4 *>(xr + k)) : make_float4(0.f, 0.f, 0.f, 0.f);
       }
-      for (int k = (tid + kXv * kThreads) * 4; live && k < a.K; k += kThreads * 4) {
+      for (int k = (tid + kXv * THREADS) * 4; live && k < a.K; k += THREADS * 4) {
         const float4 v = __ldg(reinterpret_cast<const float4 *>(xr + k));
         sx[m] += ((double)v.x + (double)v.y) + ((double)v.z + (double)v.w);
         mx[m] = fmaxf(mx[m], fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
@@ -284,12 +293,13 @@ __global__ void __launch_bounds__(kThreads, kResident) gemv_q_kernel(const GemvA
     for (int m = 0; m < MT; ++m) {
       double sum = 0.0;
       float mxx = 0.0f;
-      for (int i = 0; i < kWarps; ++i) {
+#pragma unroll
+      for (int i = 0; i < WARPS; ++i) {
         sum += dscr[i * MT + m];
         mxx = fmaxf(mxx, fscr[i * MT + m]);
       }
       const bool live = (m0 + m) < a.M;
-      const float mu = live && a.K > 0 ? (float)(sum / (double)a.K) : 0.0f;
+      const float mu = live ? (float)(sum * a.inv_k) : 0.0f;
       int e = 0;
       if (mxx > 0.0f && isfinite(mxx)) frexpf(mxx, &e);  // mx < 2^e, so |x - mu| < 2^(e+1)
       int S = 125 - e;
@@ -308,16 +318,17 @@ __global__ void __launch_bounds__(kThreads, kResident) gemv_q_kernel(const GemvA
       };
 #pragma unroll
       for (int i = 0; i < kXv; ++i) {
-        const int k = (tid + i * kThreads) * 4;
+        const int k = (tid + i * THREADS) * 4;
         if (k < a.K) put(k, xv[m][i]);
       }
-      for (int k = (tid + kXv * kThreads) * 4; k < a.K; k += kThreads * 4)
+      for (int k = (tid + kXv * THREADS) * 4; k < a.K; k += THREADS * 4)
         put(k, live ? __ldg(reinterpret_cast<const float4 *>(xr + k)) : make_float4(0.f, 0.f, 0.f, 0.f));
       if (tid == 0) {
         mu_s[m] = mu;
         const double sxp = live ? sum - (double)a.K * (double)mu : 0.0;
-        corr_s[m] = (float)((double)F::kZp * sxp * ldexp(1.0, S - 149));
-        pow2_s[m] = ldexp(1.0, 149 - S);
+        // 2^(S-149) and 2^(149-S) built exactly from their exponent bits
+        corr_s[m] = (float)((double)F::kZp * sxp * __longlong_as_double((long long)(1023 + S - 149) << 52));
+        pow2_s[m] = __longlong_as_double((long long)(1023 + 149 - S) << 52);
       }
     }
   }
@@ -332,98 +343,151 @@ __global__ void __launch_bounds__(kThreads, kResident) gemv_q_kernel(const GemvA
   }
 
   bool failed = false;
-  int t_fail = ntiles;
   for (int t = 0; t < ntiles; ++t) {
     const int stage = t % a.stages;
     const int r0 = n_begin + t * a.tile_rows;
     const int rows = min(a.tile_rows, n_end - r0);
-    const uint8_t *buf = stage_buf + (size_t)stage * NW * stage_bytes;
+    const uint8_t *buf = stage_buf + (size_t)stage * stage_stride;
+    const float *ops = reinterpret_cast<const float *>(buf + NW * stage_bytes);  // [NW][scale|qsum][tile_rows]
     if (!gqd::mbar_wait_bounded(&bars[stage], (uint32_t)(t / a.stages) & 1u)) {
       failed = true;
-      t_fail = t;
       break;
     }
-    for (int rr = warp * rpw + grp; rr - grp < rows; rr += rows_per_pass) {
-      const bool live_row = rr < rows;
-      const int n = r0 + rr;
-      // epilogue operands: issued now, used after the row's MAC work
-      float sc0 = 0.f, qs0 = 0.f, sc1 = 0.f, qs1 = 0.f, bsv[MT];
+    // rows rr0 .. rr0+R-1 of the stage belong to this lane group in this pass
+    for (int rr0 = (warp * gpw + grp) * R, base = warp * gpw * R; base < rows; rr0 += rows_per_pass,
+             base += rows_per_pass) {
+      // epilogue operands: scales and code sums arrived with the stage; the
+      // MODE-2 slice value is issued now and used after the rows' MAC work
+      float sc[NR], qs[NR], bsv[R][MT];
 #pragma unroll
-      for (int m = 0; m < MT; ++m) bsv[m] = 0.f;
-      if (live_row && li == 0) {
-        sc0 = __ldg(a.s + n);
-        qs0 = __ldg(a.qsum + n);
-        if (NW == 2) {
-          sc1 = __ldg(a.s2 + n);
-          qs1 = __ldg(a.qsum2 + n);
-        }
-        if (MODE == 2) {
+      for (int i = 0; i < R; ++i) {
+        const int rr = rr0 + i, n = r0 + rr;
+        const bool live_row = rr < rows;
 #pragma unroll
-          for (int m = 0; m < MT; ++m)
-            if (m0 + m < a.M) bsv[m] = a.bs[(size_t)(m0 + m) * a.b_stride + a.b_off + n];
+        for (int h = 0; h < NW; ++h) {
+          sc[i * NW + h] = live_row ? ops[(2 * h) * a.tile_rows + rr] : 0.f;
+          qs[i * NW + h] = live_row ? ops[(2 * h + 1) * a.tile_rows + rr] : 0.f;
         }
+#pragma unroll
+        for (int m = 0; m < MT; ++m)
+          bsv[i][m] = (MODE == 2 && live_row && (li & (lanes / R - 1)) == 0 && m0 + m < a.M)
+                          ? a.bs[(size_t)(m0 + m) * a.b_stride + a.b_off + n]
+                          : 0.f;
       }
-      float acc[NW][MT][ACC];
+      float acc[NR][MT][ACC];
 #pragma unroll
-      for (int h = 0; h < NW; ++h)
+      for (int h = 0; h < NR; ++h)
 #pragma unroll
         for (int m = 0; m < MT; ++m)
 #pragma unroll
           for (int q = 0; q < ACC; ++q) acc[h][m][q] = 0.0f;
-      if (live_row) {
-        const uint8_t *rowp = buf + (size_t)rr * a.row_bytes;
-        int j = 0;
-        for (; j + 1 < cpl; j += 2) {  // two chunks in flight
-          const int ca = li + j * lanes, cb = ca + lanes;
-          uint4 wa[NW], wb[NW];
+      // rows past the stage's end read (stale but in-bounds) stage bytes; their
+      // sums are discarded below
+      const uint8_t *rowp = buf + (size_t)min(rr0, a.tile_rows - R) * a.row_bytes;
+      int j = 0;
+      for (; j + 1 < cpl; j += 2) {  // two chunks in flight
+        const int ca = li + j * lanes, cb = ca + lanes;
+        uint4 wa[NR], wb[NR];
+#pragma unroll
+        for (int i = 0; i < R; ++i)
 #pragma unroll
           for (int h = 0; h < NW; ++h) {
-            wa[h] = *reinterpret_cast<const uint4 *>(rowp + h * stage_bytes + ca * 16);
-            wb[h] = *reinterpret_cast<const uint4 *>(rowp + h * stage_bytes + cb * 16);
+            const uint8_t *p = rowp + h * stage_bytes + (size_t)i * a.row_bytes;
+            wa[i * NW + h] = *reinterpret_cast<const uint4 *>(p + ca * 16);
+            wb[i * NW + h] = *reinterpret_cast<const uint4 *>(p + cb * 16);
           }
-          mac_chunk<BITS, SIGNED, MT, NW, ACC>(wa, xs + (size_t)ca * F::kPad, xs_mstride, acc);
-          mac_chunk<BITS, SIGNED, MT, NW, ACC>(wb, xs + (size_t)cb * F::kPad, xs_mstride, acc);
-        }
-        if (j < cpl) {
-          const int ca = li + j * lanes;
-          uint4 wa[NW];
-#pragma unroll
-          for (int h = 0; h < NW; ++h) wa[h] = *reinterpret_cast<const uint4 *>(rowp + h * stage_bytes + ca * 16);
-          mac_chunk<BITS, SIGNED, MT, NW, ACC>(wa, xs + (size_t)ca * F::kPad, xs_mstride, acc);
-        }
+        mac_chunk<BITS, SIGNED, MT, NR, ACC>(wa, xs + (size_t)ca * F::kPad, xs_mstride, acc);
+        mac_chunk<BITS, SIGNED, MT, NR, ACC>(wb, xs + (size_t)cb * F::kPad, xs_mstride, acc);
       }
-      float v[NW][MT];
+      if (j < cpl) {
+        const int ca = li + j * lanes;
+        uint4 wa[NR];
 #pragma unroll
-      for (int h = 0; h < NW; ++h)
+        for (int i = 0; i < R; ++i)
 #pragma unroll
-        for (int m = 0; m < MT; ++m) {
-          float s = acc[h][m][0];
+          for (int h = 0; h < NW; ++h)
+            wa[i * NW + h] =
+                *reinterpret_cast<const uint4 *>(rowp + h * stage_bytes + (size_t)i * a.row_bytes + ca * 16);
+        mac_chunk<BITS, SIGNED, MT, NR, ACC>(wa, xs + (size_t)ca * F::kPad, xs_mstride, acc);
+      }
+      // Row sums. The first log2(R) butterfly steps are transposing: the lanes
+      // with bit o set keep the upper half of the rows and send the lower half,
+      // so each step halves the values per lane; after them a lane holds one
+      // row's partial (row index from its o-bits) and the rest is a plain
+      // xor-reduction. R rows cost the shuffles of one, and R lanes run the
+      // epilogue in parallel.
+      float v[R][NW * MT];
 #pragma unroll
-          for (int q = 1; q < ACC; ++q) s += acc[h][m][q];
-          for (int o = lanes >> 1; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-          v[h][m] = s;
-        }
-      if (live_row && li == 0) {
+      for (int i = 0; i < R; ++i)
 #pragma unroll
-        for (int m = 0; m < MT; ++m) {
-          if (m0 + m >= a.M) break;
-          // ((sum - zp*sum(x')) * 2^(149-S) + mu * sum(q)) * scale, in f32: the
-          // power-of-two factor is exact and the two terms are of the size of
-          // the result
-          const float v0 = __fmul_rn(__fmaf_rn(mu_r[m], qs0, __fmul_rn(__fsub_rn(v[0][m], corr_r[m]), p2_r[m])), sc0);
-          float out;
-          if (MODE == 1) {
-            const float v1 =
-                __fmul_rn(__fmaf_rn(mu_r[m], qs1, __fmul_rn(__fsub_rn(v[NW - 1][m], corr_r[m]), p2_r[m])), sc1);
-            out = __fmul_rn(gqd::gelu_tanh(v0), v1);
-          } else if (MODE == 2) {
-            out = __fmul_rn(gqd::gelu_tanh(v0), bsv[m]);
-          } else if (MODE == 3) {
-            out = a.cap > 0.0f ? __fmul_rn(a.cap, tanhf(__fdiv_rn(v0, a.cap))) : v0;
-          } else {
-            out = v0;
+        for (int h = 0; h < NW; ++h)
+#pragma unroll
+          for (int m = 0; m < MT; ++m) {
+            float sum = acc[i * NW + h][m][0];
+#pragma unroll
+            for (int q = 1; q < ACC; ++q) sum += acc[i * NW + h][m][q];
+            v[i][h * MT + m] = sum;
           }
-          a.y[(size_t)(m0 + m) * a.ldy + a.y_col0 + n] = out;
+      int o = lanes >> 1;
+      int row_sel = 0;  // row (within the group's R) this lane ends up holding
+#pragma unroll
+      for (int nv = R; nv > 1; nv >>= 1) {
+        const bool upper = (li & o) != 0;
+#pragma unroll
+        for (int i = 0; i < nv / 2; ++i)
+#pragma unroll
+          for (int q = 0; q < NW * MT; ++q) {
+            const float send = upper ? v[i][q] : v[i + nv / 2][q];
+            const float keep = upper ? v[i + nv / 2][q] : v[i][q];
+            v[i][q] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+          }
+        if (upper) row_sel += nv / 2;
+        o >>= 1;
+      }
+      for (; o > 0; o >>= 1)
+#pragma unroll
+        for (int q = 0; q < NW * MT; ++q) v[0][q] += __shfl_xor_sync(0xffffffffu, v[0][q], o);
+      if ((li & (lanes / R - 1)) == 0) {
+        const int i = row_sel;
+        const int rr = rr0 + i, n = r0 + rr;
+        if (rr < rows) {
+          // the lane's operands for row i (registers indexed by a runtime row:
+          // select from the R candidates)
+          float sc0 = sc[0], qs0 = qs[0], sc1 = sc[NW - 1], qs1 = qs[NW - 1];
+          float bsr[MT];
+#pragma unroll
+          for (int m = 0; m < MT; ++m) bsr[m] = bsv[0][m];
+#pragma unroll
+          for (int k = 1; k < R; ++k)
+            if (k == i) {
+              sc0 = sc[k * NW];
+              qs0 = qs[k * NW];
+              sc1 = sc[k * NW + NW - 1];
+              qs1 = qs[k * NW + NW - 1];
+#pragma unroll
+              for (int m = 0; m < MT; ++m) bsr[m] = bsv[k][m];
+            }
+#pragma unroll
+          for (int m = 0; m < MT; ++m) {
+            if (m0 + m >= a.M) break;
+            // ((sum - zp*sum(x')) * 2^(149-S) + mu * sum(q)) * scale, in f32: the
+            // power-of-two factor is exact and the two terms are of the size of
+            // the result
+            const float v0 = __fmul_rn(__fmaf_rn(mu_r[m], qs0, __fmul_rn(__fsub_rn(v[0][m], corr_r[m]), p2_r[m])), sc0);
+            float out;
+            if (MODE == 1) {
+              const float v1 =
+                  __fmul_rn(__fmaf_rn(mu_r[m], qs1, __fmul_rn(__fsub_rn(v[0][MT + m], corr_r[m]), p2_r[m])), sc1);
+              out = __fmul_rn(gqd::gelu_tanh(v0), v1);
+            } else if (MODE == 2) {
+              out = __fmul_rn(gqd::gelu_tanh(v0), bsr[m]);
+            } else if (MODE == 3) {
+              out = a.cap > 0.0f ? __fmul_rn(a.cap, tanhf(__fdiv_rn(v0, a.cap))) : v0;
+            } else {
+              out = v0;
+            }
+            a.y[(size_t)(m0 + m) * a.ldy + a.y_col0 + n] = out;
+          }
         }
       }
     }
@@ -431,7 +495,7 @@ __global__ void __launch_bounds__(kThreads, kResident) gemv_q_kernel(const GemvA
     __syncwarp();
     if (lane == 0) {
       const uint32_t prev = atomicAdd(&done[stage], 1u);
-      if (prev == kWarps - 1) {
+      if (prev == WARPS - 1) {
         atomicExch(&done[stage], 0u);
         if (t + a.stages < ntiles) issue(t + a.stages);
       }
@@ -449,13 +513,11 @@ __global__ void __launch_bounds__(kThreads, kResident) gemv_q_kernel(const GemvA
     }
     __syncthreads();
   }
-  (void)t_fail;
-  (void)issued;
 }
 
-template <int BITS, bool SIGNED, int MT, int MODE>
+template <int BITS, bool SIGNED, int MT, int MODE, int THREADS, int R>
 int launch_t(gq_ctx *ctx, const GemvArgs &a, dim3 grid, size_t smem) {
-  auto kern = gemv_q_kernel<BITS, SIGNED, MT, MODE>;
+  auto kern = gemv_q_kernel<BITS, SIGNED, MT, MODE, THREADS, R>;
   static bool attr_set[64] = {};
   const int dev = ctx->device & 63;
   if (!attr_set[dev]) {
@@ -463,25 +525,33 @@ int launch_t(gq_ctx *ctx, const GemvArgs &a, dim3 grid, size_t smem) {
                                           (int)ctx->smem_optin));
     attr_set[dev] = true;
   }
-  GQ_CUDA_TRY(ctx, gq_launch(ctx, kern, grid, dim3(kThreads), smem, a));
+  GQ_CUDA_TRY(ctx, gq_launch(ctx, kern, grid, dim3(THREADS), smem, a));
   return GQ_OK;
 }
 
+template <int BITS, bool SIGNED, int MT, int MODE>
+int launch_v(gq_ctx *ctx, bool wide, const GemvArgs &a, dim3 grid, size_t smem) {
+  if constexpr (MT == 1) {
+    if (wide) return launch_t<BITS, SIGNED, MT, MODE, kWideThreads, 2>(ctx, a, grid, smem);
+  }
+  return launch_t<BITS, SIGNED, MT, MODE, kThreads, 1>(ctx, a, grid, smem);
+}
+
 template <int BITS, bool SIGNED, int MT>
-int launch_mode(gq_ctx *ctx, int mode, const GemvArgs &a, dim3 grid, size_t smem) {
+int launch_mode(gq_ctx *ctx, int mode, bool wide, const GemvArgs &a, dim3 grid, size_t smem) {
   switch (mode) {
-    case 0: return launch_t<BITS, SIGNED, MT, 0>(ctx, a, grid, smem);
-    case 1: return launch_t<BITS, SIGNED, MT, 1>(ctx, a, grid, smem);
-    case 2: return launch_t<BITS, SIGNED, MT, 2>(ctx, a, grid, smem);
-    default: return launch_t<BITS, SIGNED, MT, 3>(ctx, a, grid, smem);
+    case 0: return launch_v<BITS, SIGNED, MT, 0>(ctx, wide, a, grid, smem);
+    case 1: return launch_v<BITS, SIGNED, MT, 1>(ctx, wide, a, grid, smem);
+    case 2: return launch_v<BITS, SIGNED, MT, 2>(ctx, wide, a, grid, smem);
+    default: return launch_v<BITS, SIGNED, MT, 3>(ctx, wide, a, grid, smem);
   }
 }
 
 template <int BITS, bool SIGNED>
-int launch_mt(gq_ctx *ctx, int mt, int mode, const GemvArgs &a, dim3 grid, size_t smem) {
-  if (mt == 1) return launch_mode<BITS, SIGNED, 1>(ctx, mode, a, grid, smem);
-  if (mt == 2) return launch_mode<BITS, SIGNED, 2>(ctx, mode, a, grid, smem);
-  return launch_mode<BITS, SIGNED, 4>(ctx, mode, a, grid, smem);
+int launch_mt(gq_ctx *ctx, int mt, int mode, bool wide, const GemvArgs &a, dim3 grid, size_t smem) {
+  if (mt == 1) return launch_mode<BITS, SIGNED, 1>(ctx, mode, wide, a, grid, smem);
+  if (mt == 2) return launch_mode<BITS, SIGNED, 2>(ctx, mode, wide, a, grid, smem);
+  return launch_mode<BITS, SIGNED, 4>(ctx, mode, wide, a, grid, smem);
 }
 
 }  // namespace
@@ -501,7 +571,7 @@ bool gq_gemv_supported(gq_ctx *ctx, const gq_qweight *w, int64_t m, int nw) {
   if (w->k % 4 != 0) return false;
   int lanes = 32;
   while ((w->row_bytes / 16) % lanes != 0) lanes >>= 1;
-  return gemv_smem_bytes(w->bits, mt, nw, (int)w->row_bytes, kWarps * (32 / lanes), 2) <=
+  return gemv_smem_bytes(w->bits, mt, nw, (int)w->row_bytes, (kThreads / 32) * (32 / lanes), 2) <=
          ctx->smem_optin / kResident - 1024;
 }
 
@@ -521,11 +591,11 @@ int gq_gemv_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq_qw
   a.N = (int)w->n;
   a.w = w->bytes;
   a.s = w->scales;
-  a.qsum = w->scales + w->n * w->scale_stride;  // qsum follows the scales
+  a.qsum = w->scales + w->qsum_off;  // per-row code sums, 16-byte aligned after the scales
   if (w2) {
     a.w2 = w2->bytes;
     a.s2 = w2->scales;
-    a.qsum2 = w2->scales + w2->n * w2->scale_stride;
+    a.qsum2 = w2->scales + w2->qsum_off;
   }
   a.bs = bs;
   a.b_stride = b_stride;
@@ -538,56 +608,72 @@ int gq_gemv_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq_qw
   a.err = ctx->dev_err;
 
   // Grid: one CTA per SM over contiguous row ranges.
-  int rows_per_cta0 = (int)((w->n + ctx->num_sms - 1) / ctx->num_sms);
-  if (rows_per_cta0 < 1) rows_per_cta0 = 1;
-  // Lanes per row: a power of two dividing the chunk count. Fewer lanes per row
-  // amortise the row's shuffle reduction and epilogue over more chunks per lane
-  // and let row groups share the shared-memory reads of x; more lanes per row
-  // keep all warps busy when a CTA owns few rows. Take the fewest lanes (>= 4)
-  // whose passes are at least 85% occupied.
-  int lanes = 32;
-  while (C % lanes != 0) lanes >>= 1;
-  const int max_lanes = lanes;
-  for (int l = 4; l <= max_lanes; l <<= 1) {
-    if (C % l != 0) continue;
-    const int rpp = kWarps * (32 / l);
-    // two stages of one pass each, plus the staged x, must fit
-    if (l != max_lanes && ((size_t)rpp * rb * nw > 48 * 1024 ||
-                           gemv_smem_bytes(w->bits, mt, nw, rb, rpp, 2) > ctx->smem_optin / kResident - 1024))
-      continue;
-    const int passes = (rows_per_cta0 + rpp - 1) / rpp;
-    if (rows_per_cta0 >= (int)(0.85 * passes * rpp) || l == max_lanes) {
-      lanes = l;
-      break;
-    }
-  }
-  const int rows_per_pass = kWarps * (32 / lanes);
-  const int rows_per_cta = rows_per_cta0;
+  // (a multiple of 4 rows, so each tile's scale copy starts 16-byte aligned)
+  int rows_per_cta = (int)((w->n + ctx->num_sms - 1) / ctx->num_sms);
+  rows_per_cta = (rows_per_cta + 3) & ~3;
   const int gx = (int)((w->n + rows_per_cta - 1) / rows_per_cta);
-  // Stage size: whole passes, >= 24 KB per copy where the rows allow (large bulk
-  // copies stream fastest), <= 32 KB per weight.
-  int passes = 1;
-  while ((passes + 1) * rows_per_pass * rb * nw <= 48 * 1024 && passes * rows_per_pass * rb < 24 * 1024) ++passes;
-  int tile_rows = passes * rows_per_pass;
-  if (tile_rows > rows_per_cta) tile_rows = ((rows_per_cta + rows_per_pass - 1) / rows_per_pass) * rows_per_pass;
-  const int ntiles = (rows_per_cta + tile_rows - 1) / tile_rows;
-  int stages = min(kMaxStages, ntiles);
-  const size_t smem_cap = ctx->smem_optin / kResident - 1024;
-  size_t smem = gemv_smem_bytes(w->bits, mt, nw, rb, tile_rows, stages);
-  while (smem > smem_cap && (stages > 2 || tile_rows > rows_per_pass)) {
-    if (stages > 2) --stages;
-    else tile_rows -= rows_per_pass;
+  int max_lanes = 32;
+  while (C % max_lanes != 0) max_lanes >>= 1;
+
+  // Two variants: narrow (256 threads, one row per lane group, sized so the next
+  // kernel's CTA co-resides and prefetches under PDL) for CTAs that own few rows;
+  // wide (512 threads, two rows per lane group, the SM to itself) when a CTA owns
+  // hundreds of rows (vocab-sized projections), where latency hiding matters more.
+  auto plan = [&](bool wide, int &lanes, int &tile_rows, int &stages, size_t &smem) -> bool {
+    const int warps = (wide ? kWideThreads : kThreads) / 32;
+    const int R = wide ? 2 : 1;
+    const size_t cap = wide ? ctx->smem_optin - 1024 : ctx->smem_optin / kResident - 1024;
+    // Lanes per row: a power of two dividing the chunk count. Fewer lanes per
+    // row amortise the row's shuffle reduction and epilogue over more chunks per
+    // lane and let row groups share the shared-memory reads of x; more lanes per
+    // row keep all warps busy when a CTA owns few rows. Take the fewest lanes
+    // (>= 4) whose passes fit a 48 KB stage and are at least 85% occupied.
+    lanes = -1;
+    for (int l = 4; l <= max_lanes; l <<= 1) {
+      if (C % l != 0) continue;
+      const int rpp = warps * (32 / l) * R;
+      if ((size_t)rpp * rb * nw > 48 * 1024 || gemv_smem_bytes(w->bits, mt, nw, rb, rpp, 2) > cap) continue;
+      const int passes = (rows_per_cta + rpp - 1) / rpp;
+      if (rows_per_cta >= (int)(0.85 * passes * rpp) || l == max_lanes) {
+        lanes = l;
+        break;
+      }
+    }
+    if (lanes < 0) {  // nothing fits the 48 KB stage budget: one pass per stage at max lanes
+      lanes = max_lanes;
+      if (gemv_smem_bytes(w->bits, mt, nw, rb, warps * (32 / lanes) * R, 1) > cap) return false;
+    }
+    const int rows_per_pass = warps * (32 / lanes) * R;
+    // Stage size: whole passes, >= 24 KB per copy where the rows allow (large
+    // bulk copies stream fastest), <= 48 KB per stage.
+    int passes = 1;
+    while ((passes + 1) * rows_per_pass * rb * nw <= 48 * 1024 && passes * rows_per_pass * rb < 24 * 1024) ++passes;
+    tile_rows = passes * rows_per_pass;
+    if (tile_rows > rows_per_cta) tile_rows = ((rows_per_cta + rows_per_pass - 1) / rows_per_pass) * rows_per_pass;
+    const int ntiles = (rows_per_cta + tile_rows - 1) / tile_rows;
+    stages = min(kMaxStages, ntiles);
     smem = gemv_smem_bytes(w->bits, mt, nw, rb, tile_rows, stages);
-  }
-  if (smem > smem_cap || tile_rows < 1 || stages < 1)
+    while (smem > cap && (stages > 1 || tile_rows > rows_per_pass)) {
+      if (stages > 2 || (stages > 1 && tile_rows == rows_per_pass)) --stages;
+      else tile_rows -= rows_per_pass;
+      smem = gemv_smem_bytes(w->bits, mt, nw, rb, tile_rows, stages);
+    }
+    return smem <= cap && tile_rows >= 1 && stages >= 1;
+  };
+  int lanes = 0, tile_rows = 0, stages = 0;
+  size_t smem = 0;
+  bool wide = (mt == 1) && rows_per_cta >= 256 && max_lanes >= 4;  // wide holds 2 rows per >= 2-lane group
+  if (wide && !plan(true, lanes, tile_rows, stages, smem)) wide = false;
+  if (!wide && !plan(false, lanes, tile_rows, stages, smem))
     return gq_fail(ctx, GQ_ERR_UNSUPPORTED, "gemv: no stage configuration fits shared memory");
   a.rows_per_cta = rows_per_cta;
   a.tile_rows = tile_rows;
   a.stages = stages;
   a.lanes = lanes;
+  a.inv_k = 1.0 / (double)w->k;
   dim3 grid(gx, (unsigned)((m + mt - 1) / mt));
-  if (w->bits == 4) return launch_mt<4, false>(ctx, mt, mode, a, grid, smem);
-  if (w->bits == 2) return launch_mt<2, false>(ctx, mt, mode, a, grid, smem);
-  if (w->signed_i8) return launch_mt<8, true>(ctx, mt, mode, a, grid, smem);
-  return launch_mt<8, false>(ctx, mt, mode, a, grid, smem);
+  if (w->bits == 4) return launch_mt<4, false>(ctx, mt, mode, wide, a, grid, smem);
+  if (w->bits == 2) return launch_mt<2, false>(ctx, mt, mode, wide, a, grid, smem);
+  if (w->signed_i8) return launch_mt<8, true>(ctx, mt, mode, wide, a, grid, smem);
+  return launch_mt<8, false>(ctx, mt, mode, wide, a, grid, smem);
 }

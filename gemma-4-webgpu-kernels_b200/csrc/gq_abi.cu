@@ -259,7 +259,8 @@ static int qweight_upload_impl(gq_ctx *ctx, const uint8_t *qbytes, bool bytes_on
   // Packed bytes padded to a 16-byte multiple (+16) so vector loads of the last
   // row never leave the allocation; scales followed by per-row code sums.
   const size_t byte_alloc = ((w->nbytes + 15) & ~size_t(15)) + 16;
-  const size_t scale_alloc = (size_t)(n * ss + n + 4) * sizeof(float);
+  w->qsum_off = (n * ss + 3) & ~int64_t(3);
+  const size_t scale_alloc = (size_t)(w->qsum_off + n + 8) * sizeof(float);
   cudaError_t e;
   if ((e = cudaMalloc(reinterpret_cast<void **>(&w->bytes), byte_alloc)) != cudaSuccess ||
       (e = cudaMalloc(reinterpret_cast<void **>(&w->scales), scale_alloc)) != cudaSuccess) {
@@ -275,11 +276,12 @@ static int qweight_upload_impl(gq_ctx *ctx, const uint8_t *qbytes, bool bytes_on
                              bytes_on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice,
                              ctx->stream)) != cudaSuccess)
       break;
+    if ((e = cudaMemsetAsync(w->scales, 0, scale_alloc, ctx->stream)) != cudaSuccess) break;
     if (n * ss > 0 &&
         (e = cudaMemcpyAsync(w->scales, scales, (size_t)(n * ss) * sizeof(float), cudaMemcpyHostToDevice,
                              ctx->stream)) != cudaSuccess)
       break;
-    rc = gq_qsum_launch(ctx, w, w->scales + n * ss);
+    rc = gq_qsum_launch(ctx, w, w->scales + w->qsum_off);
     if (rc != GQ_OK) break;
     // The host buffers may be freed by the caller as soon as we return.
     e = cudaStreamSynchronize(ctx->stream);

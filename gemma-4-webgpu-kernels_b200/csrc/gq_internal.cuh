@@ -38,6 +38,7 @@ struct gq_qweight {
   int64_t group_size = 0;
   int64_t row_bytes = 0;       // bytes per packed row
   int64_t scale_stride = 0;    // scale entries per row
+  int64_t qsum_off = 0;        // float offset of the per-row code sums (16-byte aligned)
   size_t nbytes = 0;
 };
 
