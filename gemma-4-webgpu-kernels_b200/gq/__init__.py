@@ -112,6 +112,10 @@ class CudaBackend:
     # ---- plumbing ---------------------------------------------------------
     def _bind_stream(self) -> None:
         s = self._torch.cuda.current_stream(self.torch_device).cuda_stream
+        # torch's default stream is the legacy NULL stream (handle 0); pass it as
+        # cudaStreamLegacy (0x1), since NULL means "the context's own stream" here
+        if not s:
+            s = 1
         _abi.check(self.lib.gq_ctx_set_stream(self.ctx, c_void_p(s)), self.ctx, "set_stream")
 
     def _check(self, rc: int, what: str) -> None:

@@ -59,7 +59,8 @@ const char *gq_status_string(int status);
 int gq_ctx_create(int device, gq_ctx **out);
 int gq_ctx_destroy(gq_ctx *ctx);
 /* Use the caller's cudaStream_t (e.g. torch's current stream); NULL restores the
- * context's own stream. */
+ * context's own (non-blocking) stream. To run on the legacy default stream pass
+ * cudaStreamLegacy ((void*)0x1). */
 int gq_ctx_set_stream(gq_ctx *ctx, void *cuda_stream);
 void *gq_ctx_get_stream(gq_ctx *ctx);
 /* Number of SMs of the context's device (grid sizing; reported by bench tools). */
