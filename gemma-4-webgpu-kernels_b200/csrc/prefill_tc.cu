@@ -26,6 +26,7 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
 #include <type_traits>
 
 #include "gq_internal.cuh"
@@ -485,4 +486,107 @@ int gq_prefill_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq
   if (w->bits == 2) return launch_mode<2, false>(ctx, mode, map, a, grid, kSmemBytes);
   if (w->signed_i8) return launch_mode<8, true>(ctx, mode, map, a, grid, kSmemBytes);
   return launch_mode<8, false>(ctx, mode, map, a, grid, kSmemBytes);
+}
+
+// ---- allocation-free variant ---------------------------------------------------
+// For callers that cannot allocate device memory at call time: a serving process
+// that reserves its whole HBM budget at start-up and treats any later cudaMalloc
+// as an error, or an embedder whose buffers all come from its own arena. The
+// scratch this path needs (the bf16 copy of the activations) lives in this
+// file-scope array instead of a context workspace; every GPU that loads the
+// library holds it until the process exits.
+namespace {
+constexpr int64_t kStaticScratchElems = int64_t(4) << 20;  // 4 Mi bf16 (8 MiB): M*K <= 4,194,304
+static __device__ __align__(256) __nv_bfloat16 g_prefill_scratch[kStaticScratchElems];
+
+// Host-side device addresses of the array, one per device. Host code must not
+// pass the symbol itself to a kernel: in host code it names a host-side
+// stand-in, not device memory.
+struct StaticSetup {
+  void *scratch = nullptr;
+  int smem_optin = 0;
+  bool ready = false;
+};
+StaticSetup g_static_setup[64];
+
+cudaError_t static_setup(int dev, StaticSetup **out) {
+  StaticSetup &st = g_static_setup[dev & 63];
+  if (!st.ready) {
+    cudaError_t e = cudaGetSymbolAddress(&st.scratch, g_prefill_scratch);
+    if (e != cudaSuccess) return e;
+    if (st.scratch == nullptr) return cudaErrorInvalidSymbol;
+    e = cudaDeviceGetAttribute(&st.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    if (e != cudaSuccess) return e;
+    st.ready = true;
+  }
+  *out = &st;
+  return cudaSuccess;
+}
+
+template <int BITS, bool SIGNED>
+cudaError_t static_launch(cudaStream_t stream, const CUtensorMap &map, const PrefillArgs &a, dim3 grid) {
+  auto kern = prefill_tc_kernel<BITS, SIGNED, 0>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.stream = stream;
+  return cudaLaunchKernelEx(&cfg, kern, map, a);
+}
+}  // namespace
+
+extern "C" int gq_linear_prefill_static(void *cuda_stream, const float *x, int64_t m, int64_t k,
+                                        const uint8_t *qbytes, const float *scales, int64_t n, int32_t bits,
+                                        int32_t signed_i8, float *y) {
+  if (m < 0 || n < 0 || k <= 0) return GQ_ERR_INVALID_ARGUMENT;
+  if (m == 0 || n == 0) return GQ_OK;
+  if (!x || !qbytes || !scales || !y) return GQ_ERR_INVALID_ARGUMENT;
+  if (signed_i8 ? bits != 8 : (bits != 2 && bits != 4 && bits != 8)) return GQ_ERR_UNSUPPORTED;
+  if (k % BK != 0) return GQ_ERR_UNSUPPORTED;
+  if (m > kStaticScratchElems / k) return GQ_ERR_INVALID_ARGUMENT;  // M*K beyond the static scratch
+  if (n > (int64_t(1) << 30)) return GQ_ERR_UNSUPPORTED;
+  if ((uintptr_t)x % 16 != 0 || (uintptr_t)qbytes % 16 != 0 || (uintptr_t)scales % 4 != 0)
+    return GQ_ERR_INVALID_ARGUMENT;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return GQ_ERR_CUDA;
+  StaticSetup *st = nullptr;
+  if (static_setup(dev, &st) != cudaSuccess) return GQ_ERR_CUDA;
+  if ((size_t)st->smem_optin < kSmemBytes || encode_fn() == nullptr) return GQ_ERR_UNSUPPORTED;
+  cudaStream_t stream = static_cast<cudaStream_t>(cuda_stream);
+  __nv_bfloat16 *xb = static_cast<__nv_bfloat16 *>(st->scratch);
+  {
+    const int64_t n4 = m * k / 4;
+    const unsigned g = (unsigned)std::min<int64_t>((n4 + 255) / 256, 148 * 8);
+    cast_bf16_kernel<<<g, 256, 0, stream>>>(x, xb, n4);
+    if (cudaGetLastError() != cudaSuccess) return GQ_ERR_CUDA;
+  }
+  CUtensorMap map;
+  cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)m};
+  cuuint64_t strides[1] = {(cuuint64_t)k * 2};
+  cuuint32_t box[2] = {BK, BM};
+  cuuint32_t estr[2] = {1, 1};
+  if (encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, xb, dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return GQ_ERR_CUDA;
+  PrefillArgs a = {};
+  a.M = (int)m;
+  a.N = (int)n;
+  a.K = (int)k;
+  a.w = qbytes;
+  a.s = scales;
+  a.row_bytes = (int)(signed_i8 ? k : k * bits / 8);
+  a.y = y;
+  a.ldy = n;
+  a.y_col0 = 0;
+  a.err = nullptr;  // no context: a timed-out wait is still bounded, but not reported
+  const dim3 grid((unsigned)((m + BM - 1) / BM), (unsigned)((n + BN - 1) / BN));
+  cudaError_t e;
+  if (bits == 4) e = static_launch<4, false>(stream, map, a, grid);
+  else if (bits == 2) e = static_launch<2, false>(stream, map, a, grid);
+  else if (signed_i8) e = static_launch<8, true>(stream, map, a, grid);
+  else e = static_launch<8, false>(stream, map, a, grid);
+  return e == cudaSuccess ? GQ_OK : GQ_ERR_CUDA;
 }

@@ -73,6 +73,8 @@ SIGNATURES = {
     "gq_linear_softcap": (
         c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_float, c_void_p, c_int64, c_int64]),
     "gq_embed_rows": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_float, c_void_p]),
+    "gq_linear_prefill_static": (
+        c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int32, c_int32, c_void_p]),
     "gq_softcap": (c_int, [c_void_p, c_void_p, c_int64, c_float, c_void_p]),
     "gq_geglu": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
 }

@@ -148,6 +148,25 @@ int gq_linear_softcap(gq_ctx *ctx, const float *x, int64_t m, int64_t k, const g
 int gq_embed_rows(gq_ctx *ctx, const gq_qweight *table, const uint32_t *ids, int64_t t,
                   float scale, float *out);
 
+/* Allocation-free prefill linear. No counterpart in the reference: it exists for
+ * callers that cannot allocate device memory when they call (a serving process
+ * that reserves all of its HBM at start-up and must not cudaMalloc afterwards,
+ * or an embedder whose buffers all come from its own arena), and who therefore
+ * cannot create a gq_ctx either. y[m, n] = bf16(x) · deq(W)ᵀ with the same
+ * tensor-core kernel as gq_linear uses for m >= 128 (any m >= 1 is accepted).
+ * Weights are caller device pointers in the upload layout: qbytes [n, row_bytes]
+ * (16-byte aligned), one f32 scale per row. Requires k % 64 == 0 and
+ * m * k <= 4,194,304: the bf16 copy of x goes to a file-scope 8 MiB device array
+ * that every GPU loading the library holds until exit; larger sizes return
+ * GQ_ERR_INVALID_ARGUMENT. Nothing is allocated. The first call on a device
+ * looks up that array's device address (cudaGetSymbolAddress) and should come
+ * before any stream capture. All calls share the array: calls that overlap on
+ * the GPU (different streams, concurrent) race on it. Work is enqueued on
+ * cuda_stream (NULL = legacy default stream) of the current device. */
+int gq_linear_prefill_static(void *cuda_stream, const float *x, int64_t m, int64_t k,
+                             const uint8_t *qbytes, const float *scales, int64_t n, int32_t bits,
+                             int32_t signed_i8, float *y);
+
 /* Backend::softcap / geglu / gelu_tanh (rust/src/backend.rs:112-116) on n
  * f32 elements. */
 int gq_softcap(gq_ctx *ctx, const float *x, int64_t n, float cap, float *y);
