@@ -382,8 +382,10 @@ def run_gq(args):
                            "frac_of_measured_hbm": round(c[3] / (mm / 1e3) / 1e9 / hbm_peak, 4)}
     line["clocks"] = clk.summary()
 
+    if world > 1:
+        line["lm_head_sharded"] = sharded_lm_head(torch, dist, rank, world, local, args)
     if rank == 0 and world == 1 and not args.no_extras:
-        line["extras"] = extras(g, torch, stream, hbm_peak)
+        line["extras"] = extras(g, torch, stream, hbm_peak, bf16_peak)
     if rank == 0 and world == 1:
         line["cpu_baseline"] = cpu_sample(step, min_seconds=10.0)
     g.destroy_graph(graph)
@@ -395,7 +397,48 @@ def run_gq(args):
     g.close()
 
 
-def extras(g, torch, stream, hbm_peak):
+def sharded_lm_head(torch, dist, rank, world, local, args):
+    """The I8 lm_head [262144, 1536] + soft-cap split by vocab rows over the ranks,
+    shard GEMV then NCCL all-gather of the logits; max over ranks."""
+    from gq import CudaBackend, synth
+    from gq.parallel import ShardedLmHead, shard_rows
+
+    g2 = CudaBackend(local)  # torch's stream, so NCCL orders after the GEMV
+    V, K = synth.VOCAB, synth.HIDDEN
+    r0, r1 = shard_rows(V, world, rank)
+    gen = torch.Generator(device=g2.torch_device)
+    gen.manual_seed(55 + rank)
+    payload = torch.randint(0, 256, ((r1 - r0) * K,), generator=gen, device=g2.torch_device, dtype=torch.uint8)
+    torch.cuda.synchronize()
+    wt = g2.quant_tensor_from_device(payload, synth.uniform(56 + rank, r1 - r0, 0.005, 0.02), (r1 - r0, K), 8, True, K)
+
+    head = ShardedLmHead(g2, wt, V, rank, world, cap=30.0)
+    x = g2.tensor(synth.normal(57, K).reshape(1, K), (1, K))
+    for _ in range(max(3, args.warmup)):
+        head.forward(x)
+    torch.cuda.synchronize()
+    dist.barrier()
+    reps = max(20, min(args.steps, 200))
+    s = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(reps):
+        logits = head.forward(x)
+    e.record()
+    e.synchronize()
+    ms = torch.tensor([s.elapsed_time(e) / reps], device=g2.torch_device)
+    dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms = float(ms.item())
+    nbytes = V * K + 4 * V + 4 * K + 4 * V  # whole lm_head: weights, scales, x, logits
+    out = {"world": world, "ms": round(ms, 4), "GB/s_whole_head": round(nbytes / (ms / 1e3) / 1e9, 1),
+           "logits_shape": list(logits.shape), "collective": "NCCL all_gather_into_tensor",
+           "note": "strong scaling of one matrix: shard GEMV + all-gather, max over ranks"}
+    g2.free_quant(wt)
+    g2.close()
+    return out
+
+
+def extras(g, torch, stream, hbm_peak, bf16_peak):
     """Per-config sub-measurements (2 at M=8, 4)."""
     from ctypes import c_float, c_void_p
     from gq import synth
@@ -449,6 +492,46 @@ def extras(g, torch, stream, hbm_peak):
         if getattr(t, "qw", None):
             g.free_quant(t)
     del step8
+
+    # config 3: prefill GEMMs at M=512 (tcgen05, bf16 operands, fp32 accumulate)
+    M3 = 512
+    xg = torch.randn(M3, 1536, generator=gen, device=dev)
+    xd = torch.randn(M3, 6144, generator=gen, device=dev)
+    pg = torch.randint(0, 256, (6144 * 768,), generator=gen, device=dev, dtype=torch.uint8)
+    pu = torch.randint(0, 256, (6144 * 768,), generator=gen, device=dev, dtype=torch.uint8)
+    pd = torch.randint(0, 256, (1536 * 1536,), generator=gen, device=dev, dtype=torch.uint8)
+    torch.cuda.synchronize()
+    wg = g.quant_tensor_from_device(pg, synth.uniform(701, 6144, 0.005, 0.02), (6144, 1536), 4, False, 1536)
+    wu = g.quant_tensor_from_device(pu, synth.uniform(702, 6144, 0.005, 0.02), (6144, 1536), 4, False, 1536)
+    wd = g.quant_tensor_from_device(pd, synth.uniform(703, 1536, 0.005, 0.02), (1536, 6144), 2, False, 6144)
+    yg = torch.empty(M3, 6144, device=dev)
+    yd = torch.empty(M3, 1536, device=dev)
+    flop = 2.0 * M3 * 6144 * 1536
+    cases3 = {
+        "gate_4bit_512x1536x6144": lambda: lib.gq_linear(ctx, c_void_p(xg.data_ptr()), M3, 1536, c_void_p(wg.qw),
+                                                          c_void_p(yg.data_ptr())),
+        "gate_up_geglu_4bit": lambda: lib.gq_linear_geglu(ctx, c_void_p(xg.data_ptr()), M3, 1536, c_void_p(wg.qw),
+                                                          c_void_p(wu.qw), c_void_p(yg.data_ptr())),
+        "down_2bit_512x6144x1536": lambda: lib.gq_linear(ctx, c_void_p(xd.data_ptr()), M3, 6144, c_void_p(wd.qw),
+                                                         c_void_p(yd.data_ptr())),
+    }
+    c3 = {}
+    for name, fn in cases3.items():
+        fn()
+        g.flush()
+        graph = g.record(lambda: [fn() for _ in range(10)])
+        for _ in range(3):
+            g.replay(graph)
+        ms = cuda_events_time(torch, stream, lambda: g.replay(graph), 10) / 100
+        f = flop * (2 if "geglu" in name else 1)
+        tf = f / (ms / 1e3) / 1e12
+        c3[name] = {"us": round(ms * 1e3, 2), "TFLOP/s": round(tf, 1),
+                    "frac_of_measured_bf16": round(tf / bf16_peak, 4)}
+        g.destroy_graph(graph)
+    c3["note"] = "each call = bf16 cast of x + tcgen05 GEMM; 10 calls per graph replay"
+    out["config3_prefill_m512"] = c3
+    for t in (wg, wu, wd):
+        g.free_quant(t)
 
     # config 4: EMBED_Q of 4096 ids over the 4-bit token table and the I8 PLE table
     V, T = synth.VOCAB, 4096

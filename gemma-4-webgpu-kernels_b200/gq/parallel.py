@@ -55,8 +55,9 @@ class ShardedLmHead:
 
     forward(x) returns the full soft-capped logits [M, V] on every rank."""
 
-    def __init__(self, backend, shard: QuantWeight, vocab: int, rank: int, world: int, cap: float = 30.0,
-                 group=None):
+    def __init__(self, backend, shard, vocab: int, rank: int, world: int, cap: float = 30.0, group=None):
+        """shard: this rank's rows as a QuantWeight (uploaded here) or an already
+        uploaded GqTensor."""
         import torch
         import torch.distributed as dist
 
@@ -66,7 +67,10 @@ class ShardedLmHead:
         self.r0, self.r1 = shard_rows(vocab, world, rank)
         self.per = -(-vocab // world)
         assert shard.shape[0] == self.r1 - self.r0
-        self.w = backend.quant_tensor(shard) if shard.shape[0] else None
+        if getattr(shard, "qw", None) is not None:
+            self.w = shard
+        else:
+            self.w = backend.quant_tensor(shard) if shard.shape[0] else None
         self._bufs = {}
 
     def _buffers(self, m: int):
