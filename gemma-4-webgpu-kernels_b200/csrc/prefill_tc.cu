@@ -36,11 +36,12 @@ namespace {
 constexpr int BM = 128;        // tokens per tile (MMA M)
 constexpr int BN = 256;        // MMA N (weight rows, or gate+up halves)
 constexpr int BK = 64;         // K per stage: one 128-byte swizzle row of bf16
-constexpr int STAGES = 4;
+constexpr int STAGES = 3;
 constexpr int kThreads = 320;  // warp 0: TMA(A), warp 1: MMA + TMEM, warps 2-9: B producers
 constexpr int kProducers = 256;
 constexpr uint32_t A_STAGE = BM * BK * 2;  // 16 KB
 constexpr uint32_t B_STAGE = BN * BK * 2;  // 32 KB
+constexpr uint32_t P_STAGE = BN * BK;      // packed weight tile, <= 16 KB (8-bit)
 constexpr uint32_t TMEM_COLS = 256;
 
 struct PrefillArgs {
@@ -202,14 +203,16 @@ __device__ __forceinline__ typename Pack8<BITS>::T load8(const uint8_t *row, int
 // ---- the kernel -----------------------------------------------------------------
 template <int BITS, bool SIGNED, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
-    prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const PrefillArgs a) {
+    prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_w,
+                      const __grid_constant__ CUtensorMap tmap_w2, const PrefillArgs a) {
   using P8 = typename Pack8<BITS>::T;
   constexpr int OW = (MODE == 1) ? BN / 2 : BN;  // output columns per tile
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t *sA = smem;                                       // [STAGES][BM x BK bf16], swizzled
   uint8_t *sB = smem + STAGES * A_STAGE;                    // [STAGES][BN x BK bf16], swizzled
-  uint64_t *full_a = reinterpret_cast<uint64_t *>(sB + STAGES * B_STAGE);
+  uint8_t *sP = sB + STAGES * B_STAGE;                      // [STAGES][BN rows x BK codes packed]
+  uint64_t *full_a = reinterpret_cast<uint64_t *>(sP + STAGES * P_STAGE);
   uint64_t *full_b = full_a + STAGES;
   uint64_t *empty = full_b + STAGES;
   uint64_t *acc_full = empty + STAGES;
@@ -254,8 +257,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           *abort_flag = 1;
           break;
         }
-        gqd::mbar_arrive_expect_tx(&full_a[s], A_STAGE);
+        constexpr uint32_t pk = BK * BITS / 8;  // packed bytes of one row per stage
+        gqd::mbar_arrive_expect_tx(&full_a[s], A_STAGE + BN * pk);
         tma_load_2d(sA + s * A_STAGE, &tmap_a, kt * BK, m0, &full_a[s]);
+        if (MODE == 1) {  // gate rows then the same up rows
+          tma_load_2d(sP + s * P_STAGE, &tmap_w, kt * (int)pk, n0, &full_a[s]);
+          tma_load_2d(sP + s * P_STAGE + (BN / 2) * pk, &tmap_w2, kt * (int)pk, n0, &full_a[s]);
+        } else {
+          tma_load_2d(sP + s * P_STAGE, &tmap_w, kt * (int)pk, n0, &full_a[s]);
+        }
         issued = kt + 1;
       }
       if (*abort_flag) {
@@ -285,31 +295,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_commit(acc_full);  // fires once every MMA issued above has completed
     }
   } else {
-    // ---- B: dequantize weight rows into the swizzled K-major tile ----
+    // ---- B: dequantize the TMA-staged packed rows into the swizzled K-major tile ----
     const int pt = threadIdx.x - 64;  // 0..255
+    constexpr int pk = BK * BITS / 8;  // packed bytes per row per stage
     for (int kt = 0; kt < KT; ++kt) {
       const int s = kt % STAGES;
       if (kt >= STAGES && (*abort_flag || !gqd::mbar_wait_bounded(&empty[s], ((kt / STAGES) - 1) & 1))) {
         *abort_flag = 1;
         break;
       }
+      if (*abort_flag || !gqd::mbar_wait_bounded(&full_a[s], (kt / STAGES) & 1)) {
+        *abort_flag = 1;
+        break;
+      }
       uint8_t *dst = sB + s * B_STAGE;
+      const uint8_t *src = sP + s * P_STAGE;
 #pragma unroll
       for (int it = 0; it < (BN * 8) / kProducers; ++it) {
         const int item = pt + it * kProducers;
-        const int r = item >> 3;  // tile row 0..255
+        const int r = item >> 3;  // tile row 0..255 (rows past N arrive zero-filled; discarded later)
         const int c = item & 7;   // 16-byte chunk (8 codes) within the 128-byte row
-        int n;
-        const uint8_t *wp;
-        if (MODE == 1) {
-          n = n0 + (r & (BN / 2 - 1));
-          wp = (r < BN / 2) ? a.w : a.w2;
-        } else {
-          n = n0 + r;
-          wp = a.w;
-        }
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (n < a.N) v = deq8<BITS, SIGNED>(load8<BITS>(wp + (size_t)n * a.row_bytes, kt * BK + c * 8));
+        const uint4 v = deq8<BITS, SIGNED>(*reinterpret_cast<const P8 *>(src + r * pk + c * (8 * BITS / 8)));
         *reinterpret_cast<uint4 *>(dst + r * 128 + ((c ^ (r & 7)) << 4)) = v;
       }
       fence_proxy_async();  // make the generic-proxy stores visible to the tensor core
@@ -391,7 +397,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 }
 
 template <int BITS, bool SIGNED, int MODE>
-int launch_t(gq_ctx *ctx, const CUtensorMap &map, const PrefillArgs &a, dim3 grid, size_t smem) {
+int launch_t(gq_ctx *ctx, const CUtensorMap &map, const CUtensorMap &mw, const CUtensorMap &mw2,
+             const PrefillArgs &a, dim3 grid, size_t smem) {
   auto kern = prefill_tc_kernel<BITS, SIGNED, MODE>;
   static bool attr_set[64] = {};
   const int dev = ctx->device & 63;
@@ -399,29 +406,44 @@ int launch_t(gq_ctx *ctx, const CUtensorMap &map, const PrefillArgs &a, dim3 gri
     GQ_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     attr_set[dev] = true;
   }
-  GQ_CUDA_TRY(ctx, gq_launch(ctx, kern, grid, dim3(kThreads), smem, map, a));
+  GQ_CUDA_TRY(ctx, gq_launch(ctx, kern, grid, dim3(kThreads), smem, map, mw, mw2, a));
   return GQ_OK;
 }
 
 template <int BITS, bool SIGNED>
-int launch_mode(gq_ctx *ctx, int mode, const CUtensorMap &map, const PrefillArgs &a, dim3 grid, size_t smem) {
+int launch_mode(gq_ctx *ctx, int mode, const CUtensorMap &map, const CUtensorMap &mw, const CUtensorMap &mw2,
+                const PrefillArgs &a, dim3 grid, size_t smem) {
   switch (mode) {
-    case 0: return launch_t<BITS, SIGNED, 0>(ctx, map, a, grid, smem);
-    case 1: return launch_t<BITS, SIGNED, 1>(ctx, map, a, grid, smem);
-    case 2: return launch_t<BITS, SIGNED, 2>(ctx, map, a, grid, smem);
-    default: return launch_t<BITS, SIGNED, 3>(ctx, map, a, grid, smem);
+    case 0: return launch_t<BITS, SIGNED, 0>(ctx, map, mw, mw2, a, grid, smem);
+    case 1: return launch_t<BITS, SIGNED, 1>(ctx, map, mw, mw2, a, grid, smem);
+    case 2: return launch_t<BITS, SIGNED, 2>(ctx, map, mw, mw2, a, grid, smem);
+    default: return launch_t<BITS, SIGNED, 3>(ctx, map, mw, mw2, a, grid, smem);
   }
 }
 
-constexpr size_t kSmemBytes = 1024 + STAGES * (A_STAGE + B_STAGE) + (3 * STAGES + 1) * 8 + 16;
+// Tensor map over a packed weight [n rows, row_bytes] (uint8), box = one stage:
+// the packed bytes of BK codes for `rows` rows.
+CUresult encode_weight_map(CUtensorMap *map, const uint8_t *w, int64_t n, int64_t row_bytes, int bits, int rows) {
+  cuuint64_t dims[2] = {(cuuint64_t)row_bytes, (cuuint64_t)n};
+  cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+  cuuint32_t box[2] = {(cuuint32_t)(BK * bits / 8), (cuuint32_t)rows};
+  cuuint32_t estr[2] = {1, 1};
+  return encode_fn()(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t *>(w), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+constexpr size_t kSmemBytes = 1024 + STAGES * (A_STAGE + B_STAGE + P_STAGE) + (3 * STAGES + 1) * 8 + 16;
 
 }  // namespace
 
-// The tensor-core path applies to M >= 16 rows with K a multiple of 64, one
-// scale per row and a shape that packs whole bytes per 8 codes.
+// The tensor-core path applies to M >= 16 rows with K a multiple of 64 (so every
+// packed row is a whole number of 16-byte TMA units), one scale per row and a
+// 16-byte aligned packed weight.
 bool gq_prefill_supported(gq_ctx *ctx, const gq_qweight *w, int64_t m) {
   if (m < 16 || w->group_size != w->k || w->k % BK != 0 || w->k <= 0 || w->n <= 0) return false;
   if (m > (1ll << 30) || w->n > (1ll << 30) || w->k > (1 << 24)) return false;
+  if ((uintptr_t)w->bytes % 16 != 0) return false;  // the packed tiles come in by TMA
   return kSmemBytes <= ctx->smem_optin && encode_fn() != nullptr;
 }
 
@@ -481,11 +503,15 @@ int gq_prefill_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq
   a.y_col0 = y_col0;
   a.err = ctx->dev_err;
   const int ow = (mode == 1) ? BN / 2 : BN;
+  CUtensorMap mw, mw2;
+  if (encode_weight_map(&mw, w->bytes, w->n, w->row_bytes, w->bits, ow) != CUDA_SUCCESS ||
+      encode_weight_map(&mw2, w2 ? w2->bytes : w->bytes, w->n, w->row_bytes, w->bits, ow) != CUDA_SUCCESS)
+    return gq_fail(ctx, GQ_ERR_CUDA, "prefill: weight tensor map");
   dim3 grid((unsigned)((m + BM - 1) / BM), (unsigned)((w->n + ow - 1) / ow));
-  if (w->bits == 4) return launch_mode<4, false>(ctx, mode, map, a, grid, kSmemBytes);
-  if (w->bits == 2) return launch_mode<2, false>(ctx, mode, map, a, grid, kSmemBytes);
-  if (w->signed_i8) return launch_mode<8, true>(ctx, mode, map, a, grid, kSmemBytes);
-  return launch_mode<8, false>(ctx, mode, map, a, grid, kSmemBytes);
+  if (w->bits == 4) return launch_mode<4, false>(ctx, mode, map, mw, mw2, a, grid, kSmemBytes);
+  if (w->bits == 2) return launch_mode<2, false>(ctx, mode, map, mw, mw2, a, grid, kSmemBytes);
+  if (w->signed_i8) return launch_mode<8, true>(ctx, mode, map, mw, mw2, a, grid, kSmemBytes);
+  return launch_mode<8, false>(ctx, mode, map, mw, mw2, a, grid, kSmemBytes);
 }
 
 // ---- allocation-free variant ---------------------------------------------------
@@ -524,7 +550,8 @@ cudaError_t static_setup(int dev, StaticSetup **out) {
 }
 
 template <int BITS, bool SIGNED>
-cudaError_t static_launch(cudaStream_t stream, const CUtensorMap &map, const PrefillArgs &a, dim3 grid) {
+cudaError_t static_launch(cudaStream_t stream, const CUtensorMap &map, const CUtensorMap &mw, const PrefillArgs &a,
+                          dim3 grid) {
   auto kern = prefill_tc_kernel<BITS, SIGNED, 0>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
   if (e != cudaSuccess) return e;
@@ -533,7 +560,7 @@ cudaError_t static_launch(cudaStream_t stream, const CUtensorMap &map, const Pre
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = kSmemBytes;
   cfg.stream = stream;
-  return cudaLaunchKernelEx(&cfg, kern, map, a);
+  return cudaLaunchKernelEx(&cfg, kern, map, mw, mw, a);
 }
 }  // namespace
 
@@ -583,10 +610,12 @@ extern "C" int gq_linear_prefill_static(void *cuda_stream, const float *x, int64
   a.y_col0 = 0;
   a.err = nullptr;  // no context: a timed-out wait is still bounded, but not reported
   const dim3 grid((unsigned)((m + BM - 1) / BM), (unsigned)((n + BN - 1) / BN));
+  CUtensorMap mw;
+  if (encode_weight_map(&mw, qbytes, n, a.row_bytes, bits, BN) != CUDA_SUCCESS) return GQ_ERR_CUDA;
   cudaError_t e;
-  if (bits == 4) e = static_launch<4, false>(stream, map, a, grid);
-  else if (bits == 2) e = static_launch<2, false>(stream, map, a, grid);
-  else if (signed_i8) e = static_launch<8, true>(stream, map, a, grid);
-  else e = static_launch<8, false>(stream, map, a, grid);
+  if (bits == 4) e = static_launch<4, false>(stream, map, mw, a, grid);
+  else if (bits == 2) e = static_launch<2, false>(stream, map, mw, a, grid);
+  else if (signed_i8) e = static_launch<8, true>(stream, map, mw, a, grid);
+  else e = static_launch<8, false>(stream, map, mw, a, grid);
   return e == cudaSuccess ? GQ_OK : GQ_ERR_CUDA;
 }
