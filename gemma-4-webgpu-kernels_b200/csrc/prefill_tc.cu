@@ -13,9 +13,9 @@
 //  * one elected thread issues tcgen05.mma (M=128 tokens, N=256 weight rows,
 //    K=16) into a 128x256 fp32 accumulator in TMEM; tcgen05.commit releases
 //    each shared-memory stage and finally signals the epilogue;
-//  * 4 warps read the accumulator back with tcgen05.ld, apply the scale and the
-//    MODE epilogue (0 plain, 1 GeGLU, 2 gelu * column slice, 3 soft-cap) and
-//    store f32.
+//  * the 8 producer warps then read the accumulator back with tcgen05.ld, apply
+//    the scale and the MODE epilogue (0 plain, 1 GeGLU, 2 gelu * column slice,
+//    3 soft-cap) and store f32 rows through a shared-memory transpose.
 // For MODE 1 the 256 MMA columns hold 128 gate rows followed by the same 128 up
 // rows, so one MMA computes both projections of a 128-wide output tile.
 //
@@ -321,35 +321,58 @@ __global__ void __launch_bounds__(kThreads, 1)
       fence_proxy_async();  // make the generic-proxy stores visible to the tensor core
       mbar_arrive(&full_b[s]);
     }
-    // ---- epilogue: warps 2..5 read the accumulator back ----
-    if (warp < 6) {
-      const int q = warp & 3;  // TMEM lane quarter this warp may access
-      const int m = m0 + q * 32 + lane;
+    // ---- epilogue: warps 2..9 read the accumulator back ----
+    // Warp w may only touch TMEM lanes 32*(w%4)..+31 (its row quarter); warps
+    // 2-5 take the first half of the output columns and warps 6-9 the second.
+    // Each 32x32 block goes through a padded shared-memory tile so that the
+    // global stores are whole 128-byte row segments, not one row per lane.
+    {
+      const int q = warp & 3;
+      const int half = (warp - 2) >> 2;
+      constexpr int HALF_W = OW / 2;  // 128 (MODE 0/2/3) or 64 (MODE 1)
       const bool ok = gqd::mbar_wait_bounded(acc_full, 0);
       if (!ok) *abort_flag = 1;
       tc_fence_after();
       if (ok) {
-        for (int c0 = 0; c0 < OW; c0 += 16) {
-          float v[16], u[16];
-          tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + c0, v);
-          if (MODE == 1) tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + BN / 2 + c0, u);
-          if (m < a.M) {
-            float *yr = a.y + (size_t)m * a.ldy + a.y_col0;
+        // every MMA has completed, so the pipeline buffers are free for staging
+        float *stg = reinterpret_cast<float *>(sB) + (warp - 2) * (32 * 33);
+        const int row0 = m0 + q * 32;
+        for (int c0 = half * HALF_W; c0 < (half + 1) * HALF_W; c0 += 32) {
+          float v[32], u[32];
+          const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + c0;
+          tmem_ld16(taddr, *reinterpret_cast<float(*)[16]>(v));
+          tmem_ld16(taddr + 16, *reinterpret_cast<float(*)[16]>(v + 16));
+          if (MODE == 1) {
+            tmem_ld16(taddr + BN / 2, *reinterpret_cast<float(*)[16]>(u));
+            tmem_ld16(taddr + BN / 2 + 16, *reinterpret_cast<float(*)[16]>(u + 16));
+          }
+          // lane = row: scale and the row-independent part of the MODE epilogue
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              const int n = n0 + c0 + j;
-              if (n >= a.N) break;
-              float o = __fmul_rn(v[j], a.s[n]);
-              if (MODE == 1) {
-                o = __fmul_rn(gqd::gelu_tanh(o), __fmul_rn(u[j], a.s2[n]));
-              } else if (MODE == 2) {
-                o = __fmul_rn(gqd::gelu_tanh(o), a.bs[(size_t)m * a.b_stride + a.b_off + n]);
-              } else if (MODE == 3) {
-                if (a.cap > 0.0f) o = __fmul_rn(a.cap, tanhf(__fdiv_rn(o, a.cap)));
-              }
-              yr[n] = o;
+          for (int j = 0; j < 32; ++j) {
+            const int n = min(n0 + c0 + j, a.N - 1);  // columns past N are computed, never stored
+            float o = __fmul_rn(v[j], a.s[n]);
+            if (MODE == 1) {
+              o = __fmul_rn(gqd::gelu_tanh(o), __fmul_rn(u[j], a.s2[n]));
+            } else if (MODE == 2) {
+              o = gqd::gelu_tanh(o);
+            } else if (MODE == 3) {
+              if (a.cap > 0.0f) o = __fmul_rn(a.cap, tanhf(__fdiv_rn(o, a.cap)));
+            }
+            stg[lane * 33 + j] = o;
+          }
+          __syncwarp();
+          // lane = column: one 128-byte row segment per store instruction
+          const int n = n0 + c0 + lane;
+          if (n < a.N) {
+            for (int r = 0; r < 32; ++r) {
+              const int m = row0 + r;
+              if (m >= a.M) break;
+              float o = stg[r * 33 + lane];
+              if (MODE == 2) o = __fmul_rn(o, a.bs[(size_t)m * a.b_stride + a.b_off + n]);
+              a.y[(size_t)m * a.ldy + a.y_col0 + n] = o;
             }
           }
+          __syncwarp();
         }
       }
       tc_fence_before();
