@@ -29,7 +29,7 @@
 #include <algorithm>
 #include <type_traits>
 
-#include "gq_internal.cuh"
+#include "tc_common.cuh"
 
 namespace {
 
@@ -59,56 +59,7 @@ struct PrefillArgs {
   uint32_t *err;
 };
 
-// ---- PTX wrappers (tcgen05 / TMA) ----------------------------------------------
-__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int c0, int c1, uint64_t *bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
-          gqd::smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(gqd::smem_u32(bar))
-      : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(gqd::smem_u32(bar)) : "memory");
-}
-__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
-__device__ __forceinline__ void tc_commit(uint64_t *bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   gqd::smem_u32(bar))
-               : "memory");
-}
-__device__ __forceinline__ void tc_mma(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                       uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-// 32 lanes x 32 bits, 16 consecutive columns per thread.
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
-  uint32_t r[16];
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
-#pragma unroll
-  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
-}
-
-// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 B apart.
-__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr) {
-  uint64_t d = (uint64_t)((saddr & 0x3FFFFu) >> 4);
-  d |= (uint64_t)1 << 16;             // leading byte offset (unused for this layout)
-  d |= (uint64_t)(1024 >> 4) << 32;   // stride byte offset: next 8-row group
-  d |= (uint64_t)1 << 46;             // descriptor version for tcgen05
-  d |= (uint64_t)2 << 61;             // SWIZZLE_128B
-  return d;
-}
+using namespace gqt;
 
 // Instruction descriptor: bf16 x bf16 -> f32, both K-major, M=128, N=256.
 constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
@@ -289,7 +240,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint64_t bd = sw128_desc(gqd::smem_u32(sB + s * B_STAGE));
 #pragma unroll
         for (int j = 0; j < BK / 16; ++j)  // 16 bf16 = 32 bytes per MMA along K
-          tc_mma(tmem, ad + (uint64_t)(2 * j), bd + (uint64_t)(2 * j), kIdesc, (kt | j) != 0);
+          tc_mma_f16(tmem, ad + (uint64_t)(2 * j), bd + (uint64_t)(2 * j), kIdesc, (kt | j) != 0);
         tc_commit(&empty[s]);
       }
       tc_commit(acc_full);  // fires once every MMA issued above has completed
@@ -406,18 +357,7 @@ __global__ void cast_bf16_kernel(const float *x, __nv_bfloat16 *xb, int64_t n4) 
   }
 }
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (!fn) {
-    cudaDriverEntryPointQueryResult q;
-    void *p = nullptr;
-    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
-  return fn;
-}
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() { return gq_encode_fn(); }
 
 template <int BITS, bool SIGNED, int MODE>
 int launch_t(gq_ctx *ctx, const CUtensorMap &map, const CUtensorMap &mw, const CUtensorMap &mw2,

@@ -1,0 +1,106 @@
+"""Both decode GEMVs against the CPU oracle (needs a B200).
+
+Decode rows (M <= 2) have two CUDA implementations: the CUDA-core GEMV and the
+tensor-core one (exact integer dot products on tcgen05.mma.kind::i8). The
+library picks one per shape; GQ_DECODE_TC forces the choice (0 = CUDA cores,
+2 = tensor cores wherever they apply), so every shape family here runs through
+both, at the FFMA-path bound (relative L2 <= 1e-5 against the oracle).
+"""
+import numpy as np
+import pytest
+
+from oracle import oracle
+from gq import CudaBackend
+from gq import synth
+
+pytestmark = pytest.mark.gpu
+
+REL_L2 = 1e-5
+
+
+def rel_l2(a, b):
+    a = np.asarray(a, np.float64).ravel()
+    b = np.asarray(b, np.float64).ravel()
+    nb = np.linalg.norm(b)
+    return np.linalg.norm(a - b) / (nb if nb > 0 else 1.0)
+
+
+@pytest.fixture(scope="module")
+def g():
+    be = CudaBackend(0)
+    yield be
+    be.close()
+
+
+PATHS = ["0", "2"]
+
+# (rows, K, bits, signed): E2B projections and odd sizes
+SHAPES = [(2048, 1536, 8, True), (256, 1536, 8, True), (1536, 2048, 8, True), (6144, 1536, 4, False),
+          (1536, 6144, 2, False), (300, 640, 8, False), (77, 256, 4, False), (5000, 512, 2, False),
+          (40000, 1536, 8, True)]
+
+
+@pytest.mark.parametrize("path", PATHS)
+@pytest.mark.parametrize("n,k,bits,signed", SHAPES)
+@pytest.mark.parametrize("m", [1, 2])
+def test_linear_both_paths(g, monkeypatch, path, n, k, bits, signed, m):
+    monkeypatch.setenv("GQ_DECODE_TC", path)
+    w = synth.random_qweight(3000 + n + k + bits, n, k, bits, signed)
+    x = synth.normal(3001 + m, m * k).reshape(m, k)
+    got = g.readback(g.linear(g.tensor(x, x.shape), g.quant_tensor(w)))
+    assert rel_l2(got, oracle.linear(x, w)) <= REL_L2
+
+
+@pytest.mark.parametrize("path", PATHS)
+@pytest.mark.parametrize("m", [1, 2])
+def test_geglu_both_paths(g, monkeypatch, path, m):
+    monkeypatch.setenv("GQ_DECODE_TC", path)
+    n, k = 6144, 1536
+    wg = synth.random_qweight(3101, n, k, 4, False)
+    wu = synth.random_qweight(3102, n, k, 4, False)
+    x = synth.normal(3103, m * k).reshape(m, k)
+    got = g.readback(g.linear_geglu(g.tensor(x, x.shape), g.quant_tensor(wg), g.quant_tensor(wu)))
+    assert rel_l2(got, oracle.linear_geglu(x, wg, wu)) <= REL_L2
+
+
+@pytest.mark.parametrize("path", PATHS)
+def test_gelu_mul_cols_both_paths(g, monkeypatch, path):
+    monkeypatch.setenv("GQ_DECODE_TC", path)
+    n, k, m, off = 256, 1536, 2, 512
+    w = synth.random_qweight(3201, n, k, 8, True)
+    x = synth.normal(3202, m * k).reshape(m, k)
+    b = synth.normal(3203, m * 8960).reshape(m, 8960)
+    got = g.readback(g.linear_gelu_mul_cols(g.tensor(x, x.shape), g.quant_tensor(w), g.tensor(b, b.shape), off))
+    assert rel_l2(got, oracle.linear_gelu_mul_cols(x, w, b, off)) <= REL_L2
+
+
+@pytest.mark.parametrize("path", PATHS)
+def test_softcap_slice_both_paths(g, monkeypatch, path):
+    """A vocab shard written into its column range of a wider logits row."""
+    monkeypatch.setenv("GQ_DECODE_TC", path)
+    n, k, cap = 32768, 1536, 30.0
+    w = synth.random_qweight(3301, n, k, 8, True)
+    x = synth.normal(3302, k).reshape(1, k) * 4.0
+    out = g.zeros((1, 3 * n))
+    g.linear_softcap(g.tensor(x, x.shape), g.quant_tensor(w), cap, out=out, col0=n)
+    got = g.readback(out).reshape(1, 3 * n)
+    ref = oracle.softcap(oracle.linear(x, w), cap)
+    assert rel_l2(got[:, n:2 * n], ref) <= REL_L2
+    assert not np.any(got[:, :n]) and not np.any(got[:, 2 * n:])
+
+
+@pytest.mark.parametrize("path", PATHS)
+def test_extreme_activations_both_paths(g, monkeypatch, path):
+    """Fixed-point scaling across the f32 range: tiny, huge, large mean, outlier."""
+    monkeypatch.setenv("GQ_DECODE_TC", path)
+    n, k = 1024, 1536
+    w = synth.make_qweight(3401, n, k, 4)
+    base = synth.normal(3402, 2 * k).reshape(2, k)
+    for label, x in [("tiny", base * 1e-30), ("huge", base * 1e25), ("mean", base + 5.0)]:
+        x = x.astype(np.float32)
+        got = g.readback(g.linear(g.tensor(x, x.shape), g.quant_tensor(w)))
+        assert rel_l2(got, oracle.linear(x, w)) <= REL_L2, label
+    x = base.copy()
+    x[:, 7] = 300.0
+    got = g.readback(g.linear(g.tensor(x, x.shape), g.quant_tensor(w)))
+    assert rel_l2(got, oracle.linear(x, w)) <= REL_L2, "outlier"
