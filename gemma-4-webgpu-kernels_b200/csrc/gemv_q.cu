@@ -616,9 +616,9 @@ int gq_gemv_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq_qw
   while (C % max_lanes != 0) max_lanes >>= 1;
 
   // Two variants: narrow (256 threads, one row per lane group, sized so the next
-  // kernel's CTA co-resides and prefetches under PDL) for CTAs that own few rows;
-  // wide (512 threads, two rows per lane group, the SM to itself) when a CTA owns
-  // hundreds of rows (vocab-sized projections), where latency hiding matters more.
+  // kernel's CTA co-resides and prefetches under PDL) for CTAs that own a handful
+  // of rows; wide (512 threads, two rows per lane group, the SM to itself)
+  // otherwise, where latency hiding matters more.
   auto plan = [&](bool wide, int &lanes, int &tile_rows, int &stages, size_t &smem) -> bool {
     const int warps = (wide ? kWideThreads : kThreads) / 32;
     const int R = wide ? 2 : 1;
@@ -662,7 +662,10 @@ int gq_gemv_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq_qw
   };
   int lanes = 0, tile_rows = 0, stages = 0;
   size_t smem = 0;
-  bool wide = (mt == 1) && rows_per_cta >= 256 && max_lanes >= 4;  // wide holds 2 rows per >= 2-lane group
+  // Wide whenever a CTA owns a few row pairs: its 16 warps hide the dependent
+  // LDS/FFMA chains far better than the co-resident narrow CTA gains from
+  // prefetching under the previous kernel (measured on the E2B projections).
+  bool wide = (mt == 1) && rows_per_cta >= 16 && max_lanes >= 4;  // wide holds 2 rows per >= 2-lane group
   if (wide && !plan(true, lanes, tile_rows, stages, smem)) wide = false;
   if (!wide && !plan(false, lanes, tile_rows, stages, smem))
     return gq_fail(ctx, GQ_ERR_UNSUPPORTED, "gemv: no stage configuration fits shared memory");
