@@ -531,9 +531,7 @@ int launch_t(gq_ctx *ctx, const GemvArgs &a, dim3 grid, size_t smem) {
 
 template <int BITS, bool SIGNED, int MT, int MODE>
 int launch_v(gq_ctx *ctx, bool wide, const GemvArgs &a, dim3 grid, size_t smem) {
-  if constexpr (MT == 1) {
-    if (wide) return launch_t<BITS, SIGNED, MT, MODE, kWideThreads, 2>(ctx, a, grid, smem);
-  }
+  if (wide) return launch_t<BITS, SIGNED, MT, MODE, kWideThreads, MT == 1 ? 2 : 1>(ctx, a, grid, smem);
   return launch_t<BITS, SIGNED, MT, MODE, kThreads, 1>(ctx, a, grid, smem);
 }
 
@@ -571,8 +569,9 @@ bool gq_gemv_supported(gq_ctx *ctx, const gq_qweight *w, int64_t m, int nw) {
   if (w->k % 4 != 0) return false;
   int lanes = 32;
   while ((w->row_bytes / 16) % lanes != 0) lanes >>= 1;
+  // the wide variant has the SM's shared memory to itself
   return gemv_smem_bytes(w->bits, mt, nw, (int)w->row_bytes, (kThreads / 32) * (32 / lanes), 2) <=
-         ctx->smem_optin / kResident - 1024;
+         ctx->smem_optin - 1024;
 }
 
 // mode: 0 plain, 1 geglu (w2 = up), 2 gelu * bs slice, 3 soft-cap.
@@ -621,7 +620,7 @@ int gq_gemv_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq_qw
   // otherwise, where latency hiding matters more.
   auto plan = [&](bool wide, int &lanes, int &tile_rows, int &stages, size_t &smem) -> bool {
     const int warps = (wide ? kWideThreads : kThreads) / 32;
-    const int R = wide ? 2 : 1;
+    const int R = (wide && mt == 1) ? 2 : 1;
     const size_t cap = wide ? ctx->smem_optin - 1024 : ctx->smem_optin / kResident - 1024;
     // Lanes per row: a power of two dividing the chunk count. Fewer lanes per
     // row amortise the row's shuffle reduction and epilogue over more chunks per
@@ -665,10 +664,15 @@ int gq_gemv_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq_qw
   // Wide whenever a CTA owns a few row pairs: its 16 warps hide the dependent
   // LDS/FFMA chains far better than the co-resident narrow CTA gains from
   // prefetching under the previous kernel (measured on the E2B projections).
-  bool wide = (mt == 1) && rows_per_cta >= 16 && max_lanes >= 4;  // wide holds 2 rows per >= 2-lane group
+  // (for one activation row the wide variant holds 2 rows per >= 2-lane group)
+  bool wide = rows_per_cta >= 16 && (mt > 1 || max_lanes >= 4);
   if (wide && !plan(true, lanes, tile_rows, stages, smem)) wide = false;
-  if (!wide && !plan(false, lanes, tile_rows, stages, smem))
-    return gq_fail(ctx, GQ_ERR_UNSUPPORTED, "gemv: no stage configuration fits shared memory");
+  if (!wide && !plan(false, lanes, tile_rows, stages, smem)) {
+    // x rows too long for the narrow variant's half of the SM: the wide one
+    wide = mt > 1 || max_lanes >= 4;
+    if (!wide || !plan(true, lanes, tile_rows, stages, smem))
+      return gq_fail(ctx, GQ_ERR_UNSUPPORTED, "gemv: no stage configuration fits shared memory");
+  }
   a.rows_per_cta = rows_per_cta;
   a.tile_rows = tile_rows;
   a.stages = stages;
