@@ -1,0 +1,98 @@
+"""Named single-kernel workloads for profilers (one kernel family per case).
+
+    python -m gq.cases <case> [--iters N]
+
+Each case uploads synthetic weights at a BASELINE shape, runs a few warm-up calls
+and then N calls of the one hot-path entry point, synchronised, so a profiler
+can select launches of that kernel by name and skip the warm-up:
+
+  config1   4-bit GEMV [6144, 1536], M = 1 (CUDA-core gemv_q_kernel); 64
+            rotating weight copies so every call streams from HBM
+  lm_head   I8 [262144, 1536] soft-capped GEMV, M = 1 (tensor-core gemv_tc_kernel)
+  prefill   4-bit [6144, 1536] at M = 512 (cast_bf16_kernel + prefill_tc_kernel)
+  embed     config 4: 4096 ids into the 4-bit token table and the I8 PLE table
+
+Run from the package directory (or with it on PYTHONPATH).
+"""
+from __future__ import annotations
+
+import argparse
+import sys
+from ctypes import c_float, c_void_p
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("case", choices=["config1", "lm_head", "prefill", "embed"])
+    ap.add_argument("--iters", type=int, default=8)
+    ap.add_argument("--warmup", type=int, default=3)
+    args = ap.parse_args(argv)
+
+    import numpy as np
+    import torch
+
+    from . import CudaBackend, synth
+
+    g = CudaBackend(0)
+    dev = g.torch_device
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(7)
+    lib, ctx = g.lib, g.ctx
+
+    def upload(n, k, bits, signed, seed):
+        rb = k if signed else k * bits // 8
+        payload = torch.randint(0, 256, (n * rb,), generator=gen, device=dev, dtype=torch.uint8)
+        torch.cuda.synchronize()
+        return g.quant_tensor_from_device(payload, synth.uniform(seed, n, 0.005, 0.02), (n, k), bits, signed, k)
+
+    if args.case == "config1":
+        ws = [upload(6144, 1536, 4, False, 100 + i) for i in range(64)]
+        x = torch.randn(1, 1536, generator=gen, device=dev)
+        y = torch.empty(1, 6144, device=dev)
+        calls = [lambda w=w: lib.gq_linear(ctx, c_void_p(x.data_ptr()), 1, 1536, c_void_p(w.qw),
+                                           c_void_p(y.data_ptr())) for w in ws]
+    elif args.case == "lm_head":
+        w = upload(synth.VOCAB, synth.HIDDEN, 8, True, 200)
+        x = torch.randn(1, synth.HIDDEN, generator=gen, device=dev)
+        y = torch.empty(1, synth.VOCAB, device=dev)
+        calls = [lambda: lib.gq_linear_softcap(ctx, c_void_p(x.data_ptr()), 1, synth.HIDDEN, c_void_p(w.qw),
+                                               c_float(30.0), c_void_p(y.data_ptr()), synth.VOCAB, 0)]
+    elif args.case == "prefill":
+        w = upload(6144, 1536, 4, False, 300)
+        x = torch.randn(512, 1536, generator=gen, device=dev)
+        y = torch.empty(512, 6144, device=dev)
+        calls = [lambda: lib.gq_linear(ctx, c_void_p(x.data_ptr()), 512, 1536, c_void_p(w.qw),
+                                       c_void_p(y.data_ptr()))]
+    else:
+        tok = upload(synth.VOCAB, synth.HIDDEN, 4, False, 400)
+        rb = synth.LAYERS * synth.PLE_DIM
+        payload = torch.randint(0, 256, (synth.VOCAB * rb,), generator=gen, device=dev, dtype=torch.uint8)
+        torch.cuda.synchronize()
+        ple = g.quant_tensor_from_device(payload, synth.uniform(401, synth.VOCAB * synth.LAYERS, 0.005, 0.02),
+                                         (synth.VOCAB, rb), 8, True, synth.PLE_DIM)
+        ids = torch.from_numpy(np.random.default_rng(4).integers(0, synth.VOCAB, 4096).astype(np.uint32)).to(dev)
+        o1 = torch.empty(4096, synth.HIDDEN, device=dev)
+        o2 = torch.empty(4096, rb, device=dev)
+        calls = [lambda: (lib.gq_embed_rows(ctx, c_void_p(tok.qw), c_void_p(ids.data_ptr()), 4096,
+                                            c_float(float(np.sqrt(synth.HIDDEN))), c_void_p(o1.data_ptr())),
+                          lib.gq_embed_rows(ctx, c_void_p(ple.qw), c_void_p(ids.data_ptr()), 4096, c_float(16.0),
+                                            c_void_p(o2.data_ptr())))]
+
+    def run(n):
+        for i in range(n):
+            rc = calls[i % len(calls)]()
+            for r in (rc if isinstance(rc, tuple) else (rc,)):
+                if r != 0:
+                    raise RuntimeError(f"{args.case}: status {r}")
+
+    run(args.warmup)
+    g.flush()
+    run(args.iters)
+    g.flush()
+    g.close()
+    print(f"{args.case}: {args.warmup} warm-up + {args.iters} calls ok")
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
