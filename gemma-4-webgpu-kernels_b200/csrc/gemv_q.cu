@@ -615,8 +615,8 @@ int gq_gemv_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq_qw
   while (C % max_lanes != 0) max_lanes >>= 1;
 
   // Two variants: narrow (256 threads, one row per lane group, sized so the next
-  // kernel's CTA co-resides and prefetches under PDL) for CTAs that own a handful
-  // of rows; wide (512 threads, two rows per lane group, the SM to itself)
+  // kernel's CTA co-resides and prefetches under PDL) for CTAs that own < 8 rows;
+  // wide (512 threads, two rows per lane group, the SM to itself)
   // otherwise, where latency hiding matters more.
   auto plan = [&](bool wide, int &lanes, int &tile_rows, int &stages, size_t &smem) -> bool {
     const int warps = (wide ? kWideThreads : kThreads) / 32;
@@ -665,7 +665,7 @@ int gq_gemv_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq_qw
   // LDS/FFMA chains far better than the co-resident narrow CTA gains from
   // prefetching under the previous kernel (measured on the E2B projections).
   // (for one activation row the wide variant holds 2 rows per >= 2-lane group)
-  bool wide = rows_per_cta >= 16 && (mt > 1 || max_lanes >= 4);
+  bool wide = rows_per_cta >= 8 && (mt > 1 || max_lanes >= 4);
   if (wide && !plan(true, lanes, tile_rows, stages, smem)) wide = false;
   if (!wide && !plan(false, lanes, tile_rows, stages, smem)) {
     // x rows too long for the narrow variant's half of the SM: the wide one
