@@ -22,7 +22,7 @@ struct gq_ctx {
   // temporaries of the composed fallbacks (generic kernel + elementwise epilogue)
   float *scratch[2] = {nullptr, nullptr};
   size_t scratch_cap[2] = {0, 0};
-  // workspace of the tensor-core prefill path (bf16 copy of the activations)
+  // workspace of the tensor-core prefill path (f16 copy of the activations, row exponents)
   void *ws = nullptr;
   size_t ws_cap = 0;
 };

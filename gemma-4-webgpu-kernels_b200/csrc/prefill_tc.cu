@@ -3,26 +3,40 @@
 // Replaces the reference's MATMUL_Q_TILED shader (rust/src/kernels/matmul_q_tiled.wgsl:
 // 39-126, chosen for M >= 16 at rust/src/backend_wgpu.rs:663-673), whose W tile is
 // dequantized to f32 in workgroup memory and multiplied with f32 FMAs. Here:
-//   C[m, n] = epilogue( s[n] * sum_k bf16(x[m, k]) * q[n, k] )
-// with bf16 operands and fp32 accumulation in tensor memory (TMEM):
-//  * x is cast to bf16 once per call (a [M, K] workspace) and loaded tile by tile
-//    with TMA (cp.async.bulk.tensor, 128-byte swizzle);
-//  * 8 producer warps dequantize the packed weight rows straight into shared
-//    memory in the K-major 128-byte-swizzled layout tcgen05.mma reads (codes are
-//    exact in bf16; the per-row scale is applied in the epilogue);
-//  * one elected thread issues tcgen05.mma (M=128 tokens, N=256 weight rows,
-//    K=16) into a 128x256 fp32 accumulator in TMEM; tcgen05.commit releases
-//    each shared-memory stage and finally signals the epilogue;
-//  * the 8 producer warps then read the accumulator back with tcgen05.ld, apply
-//    the scale and the MODE epilogue (0 plain, 1 GeGLU, 2 gelu * column slice,
-//    3 soft-cap) and store f32 rows through a shared-memory transpose.
-// For MODE 1 the 256 MMA columns hold 128 gate rows followed by the same 128 up
-// rows, so one MMA computes both projections of a 128-wide output tile.
+//   C[m, n] = epilogue( s[n] * 2^-e[m] * sum_k f16(x[m, k] * 2^e[m]) * q[n, k] )
+// with f16 operands and fp32 accumulation in tensor memory (TMEM):
+//  * a cast kernel scales each activation row by a power of two chosen from its
+//    max|x| (so |x * 2^e| < 2^14, far inside the f16 range; the scaling is exact
+//    and undone in the epilogue) and rounds it to f16 — 11 significant bits, 3
+//    more than bf16. It also permutes K inside every 8 / 16-code group into the
+//    order the weight widening below produces, so no instruction reorders codes;
+//  * the MMA is D[weight rows, tokens] = W[128 rows, K] x X[NT tokens, K]^T: the
+//    weights are the A operand and live in TMEM, x is the B operand in shared
+//    memory. One thread issues TMA copies of the f16 x tile (NT x 64, 128-byte
+//    swizzle) and of the packed weight tile (128 rows x 64 codes) into a load
+//    ring;
+//  * 8 producer warps (two groups of four, alternate stages) widen the packed
+//    codes of their lane's weight row to f16 and write them into a TMEM A ring
+//    with tcgen05.st: a code masked into the mantissa of f16 1024 (0x6400 | n) is
+//    exactly 1024 + n, so one LOP3 per code pair and one HSUB2/HFMA2 give the
+//    signed codes (9 instructions per 8 nibbles, 17 per 16 crumbs, 5 per 4
+//    bytes). The widened weights never touch shared memory: per stage the
+//    shared-memory traffic is the x tile (TMA write + MMA read) and the packed
+//    codes, which keeps the tensor pipe, not shared-memory bandwidth, the limit;
+//  * one elected thread issues tcgen05.mma.cta_group::1.kind::f16 (M=128, N=NT,
+//    K=16, A from TMEM) into an fp32 TMEM accumulator and commits each consumed
+//    stage back to both rings, then the accumulator to the epilogue;
+//  * the 8 producer warps read the accumulator back with tcgen05.ld (lane = weight
+//    row, so every store instruction writes 32 consecutive outputs of one token
+//    row), apply the row and weight scales and the MODE epilogue (0 plain, 1
+//    GeGLU, 2 gelu * column slice, 3 soft-cap).
+// For MODE 1 the 128 weight rows of a tile are 64 gate rows followed by the same
+// 64 up rows; the up halves go through shared memory to the gate warps.
 //
 // Every wait is bounded (2 s); a timeout sets GQ_DEVERR_WAIT_TIMEOUT, drains,
 // frees TMEM and returns.
 #include <cuda.h>
-#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
@@ -33,24 +47,32 @@
 
 namespace {
 
-constexpr int BM = 128;        // tokens per tile (MMA M)
-constexpr int BN = 256;        // MMA N (weight rows, or gate+up halves)
-constexpr int BK = 64;         // K per stage: one 128-byte swizzle row of bf16
-constexpr int STAGES = 3;
-constexpr int kThreads = 320;  // warp 0: TMA(A), warp 1: MMA + TMEM, warps 2-9: B producers
-constexpr int kProducers = 256;
-constexpr uint32_t A_STAGE = BM * BK * 2;  // 16 KB
-constexpr uint32_t B_STAGE = BN * BK * 2;  // 32 KB
-constexpr uint32_t P_STAGE = BN * BK;      // packed weight tile, <= 16 KB (8-bit)
-constexpr uint32_t TMEM_COLS = 256;
+constexpr int MW = 128;        // weight rows per tile (MMA M)
+constexpr int NT_MAX = 256;    // tokens per tile (MMA N): 256, or 128 for short prefills
+constexpr int BK = 64;         // K per stage: one 128-byte swizzle row of f16
+constexpr int kThreads = 320;  // warp 0: TMA, warp 1: MMA + TMEM, warps 2-9: producers, then epilogue
+constexpr int kProdWarps = 8;
+constexpr int AS = 4;                         // TMEM A ring stages
+constexpr uint32_t A_COLS = BK / 2;           // 64 f16 per row = 32 TMEM columns per stage
+constexpr uint32_t TMEM_COLS = 512;           // accumulator (NT columns) + A ring
+constexpr uint32_t A_COL0 = NT_MAX;           // the A ring sits after the accumulator
+constexpr uint32_t X_STAGE = NT_MAX * BK * 2;  // 32 KB
+
+// Load-ring depth per code width (x tile + packed weight tile per stage).
+template <int BITS>
+struct Ring {
+  static constexpr uint32_t PW = MW * BK * BITS / 8;  // packed bytes per stage
+  static constexpr int LS = BITS == 8 ? 5 : 6;
+  static constexpr size_t kSmem =
+      1024 + (size_t)LS * (X_STAGE + PW) + (2 * LS + 2 * AS + 1) * 8 + 16 + 2 * NT_MAX * sizeof(float);
+};
 
 struct PrefillArgs {
   int M, N, K;
-  const uint8_t *w;
+  int nt;           // tokens per tile (MMA N): 128 or 256
   const float *s;
-  const uint8_t *w2;
   const float *s2;
-  int row_bytes;
+  const int *xexp;  // per activation row: the power of two e[m] applied by the cast
   const float *bs;
   int64_t b_stride, b_off;
   float cap;
@@ -61,125 +83,131 @@ struct PrefillArgs {
 
 using namespace gqt;
 
-// Instruction descriptor: bf16 x bf16 -> f32, both K-major, M=128, N=256.
-constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
-                            ((uint32_t)(BM >> 4) << 24);
+// Instruction descriptor: f16 x f16 -> f32, K-major, M=128, N=nt.
+__device__ __forceinline__ uint32_t idesc_f16(int nt) {
+  return (1u << 4) | ((uint32_t)(nt >> 3) << 17) | ((uint32_t)(MW >> 4) << 24);
+}
+__device__ __forceinline__ void tc_mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t bdesc, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// 32 lanes x 32 bits, 32 consecutive columns per thread.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]),
+      "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]),
+      "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
 
-// ---- dequantization of 8 consecutive codes to 8 bf16 (natural K order) -------
-// Sub-byte codes use the bf16 pattern 0x4300|n (= 128 + n, exact), then subtract
-// 128 + zero point. Two codes at bit offsets a (low half) and a+16 (high half)
-// come out of one masked word; PRMT then pairs neighbours into natural order.
+// ---- widening of packed codes to f16 (signed code values, exact) ----------------
+__device__ __forceinline__ uint32_t hsub2(uint32_t a, uint32_t b) {
+  uint32_t r;
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+  return r;
+}
+__device__ __forceinline__ uint32_t hfma2(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t r;
+  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+  return r;
+}
 __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
   uint32_t r;
   asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
   return r;
 }
-__device__ __forceinline__ uint32_t bsub(uint32_t v, uint32_t c2) {  // bf16x2 v - c2 (exact here)
-  __nv_bfloat162 a = *reinterpret_cast<__nv_bfloat162 *>(&v);
-  __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162 *>(&c2);
-  __nv_bfloat162 r = __hsub2(a, b);
-  return *reinterpret_cast<uint32_t *>(&r);
-}
+constexpr uint32_t kMag = 0x64006400u;  // f16 1024 in both halves
 
-// 4-bit: one 32-bit word = codes 0..7 (nibble j at bits 4j, offset binary).
-__device__ __forceinline__ uint4 deq8_b4(uint32_t w) {
-  const uint32_t A = (w & 0x000F000Fu) | 0x43004300u;          // (c0, c4)
-  const uint32_t B = ((w >> 4) & 0x000F000Fu) | 0x43004300u;   // (c1, c5)
-  const uint32_t C = ((w >> 8) & 0x000F000Fu) | 0x43004300u;   // (c2, c6)
-  const uint32_t D = ((w >> 12) & 0x000F000Fu) | 0x43004300u;  // (c3, c7)
-  const uint32_t zp = 0x43084308u;                              // 136 = 128 + 8
+// 4-bit: one word = codes 0..7 (nibble j at bits 4j, offset binary, zp 8) ->
+// f16 pairs (n0,n4) (n1,n5) (n2,n6) (n3,n7).
+__device__ __forceinline__ uint4 widen4(uint32_t w) {
+  const uint32_t w8 = w >> 8;
   uint4 r;
-  r.x = bsub(prmt(A, B, 0x5410), zp);  // (c0, c1)
-  r.y = bsub(prmt(C, D, 0x5410), zp);  // (c2, c3)
-  r.z = bsub(prmt(A, B, 0x7632), zp);  // (c4, c5)
-  r.w = bsub(prmt(C, D, 0x7632), zp);  // (c6, c7)
+  r.x = hsub2((w & 0x000F000Fu) | kMag, 0x64086408u);                // 1024+n - 1032
+  r.y = hfma2((w & 0x00F000F0u) | kMag, 0x2C002C00u, 0xD480D480u);   // (1024+16n)/16 - 72
+  r.z = hsub2((w8 & 0x000F000Fu) | kMag, 0x64086408u);
+  r.w = hfma2((w8 & 0x00F000F0u) | kMag, 0x2C002C00u, 0xD480D480u);
   return r;
 }
-// 2-bit: 16 bits = codes 0..7 (crumb j at bits 2j).
-__device__ __forceinline__ uint4 deq8_b2(uint32_t h) {
-  // E_j holds code j (low half) and code j+4 (high half)
-  const uint32_t v = (h & 0xFFu) | ((h & 0xFF00u) << 8);  // codes 0-3 at bits 0-7, codes 4-7 at bits 16-23
-  const uint32_t E0 = (v & 0x00030003u) | 0x43004300u;
-  const uint32_t E1 = ((v >> 2) & 0x00030003u) | 0x43004300u;
-  const uint32_t E2 = ((v >> 4) & 0x00030003u) | 0x43004300u;
-  const uint32_t E3 = ((v >> 6) & 0x00030003u) | 0x43004300u;
-  const uint32_t zp = 0x43024302u;  // 130 = 128 + 2
+// 2-bit: one word = codes 0..15 (crumb j at bits 2j, zp 2); the low byte of each
+// half gives f16 pairs (c0,c8) (c1,c9) (c2,c10) (c3,c11), the word shifted by 8
+// gives (c4,c12) (c5,c13) (c6,c14) (c7,c15).
+__device__ __forceinline__ uint4 widen2_half(uint32_t w) {
   uint4 r;
-  r.x = bsub(prmt(E0, E1, 0x5410), zp);  // (c0, c1)
-  r.y = bsub(prmt(E2, E3, 0x5410), zp);  // (c2, c3)
-  r.z = bsub(prmt(E0, E1, 0x7632), zp);  // (c4, c5)
-  r.w = bsub(prmt(E2, E3, 0x7632), zp);  // (c6, c7)
+  r.x = hsub2((w & 0x00030003u) | kMag, 0x64026402u);               // 1024+c - 1026
+  r.y = hfma2((w & 0x000C000Cu) | kMag, 0x34003400u, 0xDC08DC08u);  // (1024+4c)/4 - 258
+  r.z = hfma2((w & 0x00300030u) | kMag, 0x2C002C00u, 0xD420D420u);  // (1024+16c)/16 - 66
+  r.w = hfma2((w & 0x00C000C0u) | kMag, 0x24002400u, 0xCC80CC80u);  // (1024+64c)/64 - 18
   return r;
 }
-// 8-bit: two words = codes 0..7. u = byte ^ XOR is offset binary (zp 128); the f32
-// 2^23 + u minus 2^23 + 128 is the exact code, and its upper half is its bf16.
+// 8-bit: two words = codes 0..7 in natural order. u = byte (U8) or byte ^ 0x80
+// (I8) is offset binary with zp 128: 1024 + u - 1152 is the code.
 template <bool SIGNED>
-__device__ __forceinline__ uint32_t deq2_b8(uint32_t u, int j0) {
-  const uint32_t magic = 0x4B000000u;
-  const float f0 = __uint_as_float(prmt(u, magic, 0x7440u + j0)) - 8388736.0f;
-  const float f1 = __uint_as_float(prmt(u, magic, 0x7440u + j0 + 1)) - 8388736.0f;
-  return prmt(__float_as_uint(f0), __float_as_uint(f1), 0x7632);
-}
-template <bool SIGNED>
-__device__ __forceinline__ uint4 deq8_b8(uint2 q) {
-  const uint32_t x = SIGNED ? 0x80808080u : 0u;
-  const uint32_t u0 = q.x ^ x, u1 = q.y ^ x;
+__device__ __forceinline__ uint4 widen8(uint32_t w0, uint32_t w1) {
+  const uint32_t f = SIGNED ? 0x80808080u : 0u;
+  const uint32_t u0 = w0 ^ f, u1 = w1 ^ f;
   uint4 r;
-  r.x = deq2_b8<SIGNED>(u0, 0);
-  r.y = deq2_b8<SIGNED>(u0, 2);
-  r.z = deq2_b8<SIGNED>(u1, 0);
-  r.w = deq2_b8<SIGNED>(u1, 2);
+  r.x = hsub2(prmt(u0, 0x64646464u, 0x5140), 0x64806480u);
+  r.y = hsub2(prmt(u0, 0x64646464u, 0x7362), 0x64806480u);
+  r.z = hsub2(prmt(u1, 0x64646464u, 0x5140), 0x64806480u);
+  r.w = hsub2(prmt(u1, 0x64646464u, 0x7362), 0x64806480u);
   return r;
 }
 
-// Packed bytes of 8 consecutive codes.
+// Position p of a K group holds code kperm(p) (the activations follow it).
 template <int BITS>
-struct Pack8 {
-  using T = typename std::conditional<BITS == 8, uint2, typename std::conditional<BITS == 4, uint32_t, uint16_t>::type>::type;
-};
-
-template <int BITS, bool SIGNED>
-__device__ __forceinline__ uint4 deq8(typename Pack8<BITS>::T p) {
-  if constexpr (BITS == 4) return deq8_b4(p);
-  else if constexpr (BITS == 2) return deq8_b2(p);
-  else return deq8_b8<SIGNED>(p);
-}
-
-template <int BITS>
-__device__ __forceinline__ typename Pack8<BITS>::T load8(const uint8_t *row, int k) {
-  using T = typename Pack8<BITS>::T;
-  return *reinterpret_cast<const T *>(row + (size_t)k * BITS / 8);
+__host__ __device__ constexpr int kperm(int p) {
+  return BITS == 4 ? ((p & 8) | ((p & 1) << 2) | ((p >> 1) & 3))  // 0,4,1,5,2,6,3,7 per 8
+         : BITS == 2 ? (((p & 1) << 3) | (p >> 1))                // 0,8,1,9,...,7,15
+                     : p;
 }
 
 // ---- the kernel -----------------------------------------------------------------
 template <int BITS, bool SIGNED, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
-    prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_w,
+    prefill_tc_kernel(const __grid_constant__ CUtensorMap tmap_x, const __grid_constant__ CUtensorMap tmap_w,
                       const __grid_constant__ CUtensorMap tmap_w2, const PrefillArgs a) {
-  using P8 = typename Pack8<BITS>::T;
-  constexpr int OW = (MODE == 1) ? BN / 2 : BN;  // output columns per tile
+  using R = Ring<BITS>;
+  constexpr int LS = R::LS;
+  constexpr int OW = (MODE == 1) ? MW / 2 : MW;  // output columns (weight rows) per tile
+  constexpr int PK = BK * BITS / 8;              // packed bytes per weight row per stage
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t *sA = smem;                                       // [STAGES][BM x BK bf16], swizzled
-  uint8_t *sB = smem + STAGES * A_STAGE;                    // [STAGES][BN x BK bf16], swizzled
-  uint8_t *sP = sB + STAGES * B_STAGE;                      // [STAGES][BN rows x BK codes packed]
-  uint64_t *full_a = reinterpret_cast<uint64_t *>(sP + STAGES * P_STAGE);
-  uint64_t *full_b = full_a + STAGES;
-  uint64_t *empty = full_b + STAGES;
-  uint64_t *acc_full = empty + STAGES;
+  uint8_t *sX = smem;                 // [LS][NT x BK f16], swizzled (TMA)
+  uint8_t *sP = sX + LS * X_STAGE;    // [LS][MW rows x PK packed bytes] (TMA)
+  uint64_t *l_full = reinterpret_cast<uint64_t *>(sP + LS * R::PW);
+  uint64_t *l_empty = l_full + LS;
+  uint64_t *a_full = l_empty + LS;
+  uint64_t *a_empty = a_full + AS;
+  uint64_t *acc_full = a_empty + AS;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_full + 1);
   volatile uint32_t *abort_flag = tmem_slot + 1;
+  float *rs_tab = reinterpret_cast<float *>(tmem_slot + 4);  // [2][NT_MAX]: 2^-e of each token row, two factors
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.x * BM;
-  const int n0 = blockIdx.y * OW;
+  const int nt = a.nt;
+  const int m0 = blockIdx.x * nt;   // first token of the tile
+  const int n0 = blockIdx.y * OW;   // first output column (weight row) of the tile
   const int KT = a.K / BK;
+  const uint32_t x_bytes = (uint32_t)nt * BK * 2;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < STAGES; ++i) {
-      gqd::mbar_init(&full_a[i], 1);
-      gqd::mbar_init(&full_b[i], kProducers);
-      gqd::mbar_init(&empty[i], 1);
+    for (int i = 0; i < LS; ++i) {
+      gqd::mbar_init(&l_full[i], 1);
+      gqd::mbar_init(&l_empty[i], 1 + kProdWarps / 2);  // the MMA's commit (x) + the stage's 4 producer warps
+    }
+    for (int i = 0; i < AS; ++i) {
+      gqd::mbar_init(&a_full[i], kProdWarps / 2);
+      gqd::mbar_init(&a_empty[i], 1);
     }
     gqd::mbar_init(acc_full, 1);
     *abort_flag = 0;
@@ -196,134 +224,202 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  gqd::griddep_wait();  // x (the bf16 workspace) comes from the preceding cast kernel
+  gqd::griddep_wait();  // x (the f16 workspace) comes from the preceding cast kernel
 
   if (warp == 0) {
-    // ---- A: TMA loads of the bf16 activation tile ----
+    // ---- TMA: x tile + packed weight tile per stage ----
     if (lane == 0) {
       int issued = 0;
       for (int kt = 0; kt < KT && !*abort_flag; ++kt) {
-        const int s = kt % STAGES;
-        if (kt >= STAGES && !gqd::mbar_wait_bounded(&empty[s], ((kt / STAGES) - 1) & 1)) {
+        const int s = kt % LS;
+        if (kt >= LS && !gqd::mbar_wait_bounded(&l_empty[s], ((kt / LS) - 1) & 1)) {
           *abort_flag = 1;
           break;
         }
-        constexpr uint32_t pk = BK * BITS / 8;  // packed bytes of one row per stage
-        gqd::mbar_arrive_expect_tx(&full_a[s], A_STAGE + BN * pk);
-        tma_load_2d(sA + s * A_STAGE, &tmap_a, kt * BK, m0, &full_a[s]);
+        gqd::mbar_arrive_expect_tx(&l_full[s], x_bytes + MW * PK);
+        tma_load_2d(sX + s * X_STAGE, &tmap_x, kt * BK, m0, &l_full[s]);
         if (MODE == 1) {  // gate rows then the same up rows
-          tma_load_2d(sP + s * P_STAGE, &tmap_w, kt * (int)pk, n0, &full_a[s]);
-          tma_load_2d(sP + s * P_STAGE + (BN / 2) * pk, &tmap_w2, kt * (int)pk, n0, &full_a[s]);
+          tma_load_2d(sP + s * R::PW, &tmap_w, kt * PK, n0, &l_full[s]);
+          tma_load_2d(sP + s * R::PW + (MW / 2) * PK, &tmap_w2, kt * PK, n0, &l_full[s]);
         } else {
-          tma_load_2d(sP + s * P_STAGE, &tmap_w, kt * (int)pk, n0, &full_a[s]);
+          tma_load_2d(sP + s * R::PW, &tmap_w, kt * PK, n0, &l_full[s]);
         }
         issued = kt + 1;
       }
       if (*abort_flag) {
         // bounded drain of the loads still in flight before shared memory is released
-        for (int kt = issued > STAGES ? issued - STAGES : 0; kt < issued; ++kt)
-          (void)gqd::mbar_wait_bounded(&full_a[kt % STAGES], (kt / STAGES) & 1, 100000000ull);
+        for (int kt = issued > LS ? issued - LS : 0; kt < issued; ++kt)
+          (void)gqd::mbar_wait_bounded(&l_full[kt % LS], (kt / LS) & 1, 100000000ull);
       }
     }
   } else if (warp == 1) {
     // ---- MMA issue (one thread) ----
     if (lane == 0) {
+      const uint32_t idesc = idesc_f16(nt);
       for (int kt = 0; kt < KT; ++kt) {
-        const int s = kt % STAGES;
-        const uint32_t ph = (kt / STAGES) & 1;
-        if (*abort_flag || !gqd::mbar_wait_bounded(&full_a[s], ph) || !gqd::mbar_wait_bounded(&full_b[s], ph)) {
+        const int s = kt % LS, q = kt % AS;
+        if (*abort_flag || !gqd::mbar_wait_bounded(&l_full[s], (kt / LS) & 1) ||
+            !gqd::mbar_wait_bounded(&a_full[q], (kt / AS) & 1)) {
           *abort_flag = 1;
           break;
         }
         tc_fence_after();
-        const uint64_t ad = sw128_desc(gqd::smem_u32(sA + s * A_STAGE));
-        const uint64_t bd = sw128_desc(gqd::smem_u32(sB + s * B_STAGE));
-#pragma unroll
-        for (int j = 0; j < BK / 16; ++j)  // 16 bf16 = 32 bytes per MMA along K
-          tc_mma_f16(tmem, ad + (uint64_t)(2 * j), bd + (uint64_t)(2 * j), kIdesc, (kt | j) != 0);
-        tc_commit(&empty[s]);
+        const uint64_t bd = sw128_desc(gqd::smem_u32(sX + s * X_STAGE));
+        const uint32_t at = tmem + A_COL0 + (uint32_t)q * A_COLS;
+        tc_mma_f16_ts(tmem, at, bd, idesc, kt != 0);
+        tc_mma_f16_ts(tmem, at + 8, bd + 2, idesc, 1u);  // 16 f16: 8 TMEM columns, 32 bytes of x
+        tc_mma_f16_ts(tmem, at + 16, bd + 4, idesc, 1u);
+        tc_mma_f16_ts(tmem, at + 24, bd + 6, idesc, 1u);
+        tc_commit(&l_empty[s]);
+        tc_commit(&a_empty[q]);
       }
       tc_commit(acc_full);  // fires once every MMA issued above has completed
     }
   } else {
-    // ---- B: dequantize the TMA-staged packed rows into the swizzled K-major tile ----
-    const int pt = threadIdx.x - 64;  // 0..255
-    constexpr int pk = BK * BITS / 8;  // packed bytes per row per stage
-    for (int kt = 0; kt < KT; ++kt) {
-      const int s = kt % STAGES;
-      if (kt >= STAGES && (*abort_flag || !gqd::mbar_wait_bounded(&empty[s], ((kt / STAGES) - 1) & 1))) {
+    // ---- producers: widen this lane's weight row into the TMEM A ring ----
+    // Warps 2-5 take the even stages, 6-9 the odd ones; warp w writes TMEM lane
+    // quarter w % 4, i.e. weight rows 32 * (w % 4) .. + 31.
+    const int grp = (warp - 2) >> 2;
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    for (int kt = grp; kt < KT; kt += 2) {
+      const int s = kt % LS, q = kt % AS;
+      bool ok = !*abort_flag && gqd::mbar_wait_bounded(&l_full[s], (kt / LS) & 1);
+      ok = ok && (kt < AS || gqd::mbar_wait_bounded(&a_empty[q], ((kt / AS) - 1) & 1));
+      if (!__all_sync(0xffffffffu, ok)) {  // warp-uniform: tcgen05.st and the syncs below
         *abort_flag = 1;
         break;
       }
-      if (*abort_flag || !gqd::mbar_wait_bounded(&full_a[s], (kt / STAGES) & 1)) {
-        *abort_flag = 1;
-        break;
-      }
-      uint8_t *dst = sB + s * B_STAGE;
-      const uint8_t *src = sP + s * P_STAGE;
+      const uint8_t *src = sP + s * R::PW + row * PK;
+      uint32_t r[32];
+      if constexpr (BITS == 4) {
 #pragma unroll
-      for (int it = 0; it < (BN * 8) / kProducers; ++it) {
-        const int item = pt + it * kProducers;
-        const int r = item >> 3;  // tile row 0..255 (rows past N arrive zero-filled; discarded later)
-        const int c = item & 7;   // 16-byte chunk (8 codes) within the 128-byte row
-        const uint4 v = deq8<BITS, SIGNED>(*reinterpret_cast<const P8 *>(src + r * pk + c * (8 * BITS / 8)));
-        *reinterpret_cast<uint4 *>(dst + r * 128 + ((c ^ (r & 7)) << 4)) = v;
+        for (int h = 0; h < 2; ++h) {
+          const uint4 in = *reinterpret_cast<const uint4 *>(src + 16 * h);
+          const uint32_t w4[4] = {in.x, in.y, in.z, in.w};
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const uint4 o = widen4(w4[t]);
+            r[16 * h + 4 * t] = o.x;
+            r[16 * h + 4 * t + 1] = o.y;
+            r[16 * h + 4 * t + 2] = o.z;
+            r[16 * h + 4 * t + 3] = o.w;
+          }
+        }
+      } else if constexpr (BITS == 2) {
+        const uint4 in = *reinterpret_cast<const uint4 *>(src);
+        const uint32_t w4[4] = {in.x, in.y, in.z, in.w};
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const uint4 o0 = widen2_half(w4[t]), o1 = widen2_half(w4[t] >> 8);
+          r[8 * t] = o0.x;
+          r[8 * t + 1] = o0.y;
+          r[8 * t + 2] = o0.z;
+          r[8 * t + 3] = o0.w;
+          r[8 * t + 4] = o1.x;
+          r[8 * t + 5] = o1.y;
+          r[8 * t + 6] = o1.z;
+          r[8 * t + 7] = o1.w;
+        }
+      } else {
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const uint4 in = *reinterpret_cast<const uint4 *>(src + 16 * h);
+          const uint4 o0 = widen8<SIGNED>(in.x, in.y), o1 = widen8<SIGNED>(in.z, in.w);
+          r[8 * h] = o0.x;
+          r[8 * h + 1] = o0.y;
+          r[8 * h + 2] = o0.z;
+          r[8 * h + 3] = o0.w;
+          r[8 * h + 4] = o1.x;
+          r[8 * h + 5] = o1.y;
+          r[8 * h + 6] = o1.z;
+          r[8 * h + 7] = o1.w;
+        }
       }
-      fence_proxy_async();  // make the generic-proxy stores visible to the tensor core
-      mbar_arrive(&full_b[s]);
+      tmem_st32(tmem + ((uint32_t)(quarter * 32) << 16) + A_COL0 + (uint32_t)q * A_COLS, r);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive(&a_full[q]);
+        mbar_arrive(&l_empty[s]);  // the packed codes of this stage are consumed
+      }
     }
     // ---- epilogue: warps 2..9 read the accumulator back ----
-    // Warp w may only touch TMEM lanes 32*(w%4)..+31 (its row quarter); warps
-    // 2-5 take the first half of the output columns and warps 6-9 the second.
-    // Each 32x32 block goes through a padded shared-memory tile so that the
-    // global stores are whole 128-byte row segments, not one row per lane.
+    // Warp w reads TMEM lane quarter w % 4 (weight rows 32*(w%4) .. +31), warps
+    // 2-5 the first half of the tile's tokens and warps 6-9 the second. Lane =
+    // weight row, so each store writes 32 consecutive outputs of one token row.
     {
-      const int q = warp & 3;
-      const int half = (warp - 2) >> 2;
-      constexpr int HALF_W = OW / 2;  // 128 (MODE 0/2/3) or 64 (MODE 1)
-      const bool ok = gqd::mbar_wait_bounded(acc_full, 0);
+      // the tile's token-row scales 2^-e (two exact factors each), staged once
+      {
+        const int t = threadIdx.x - 64;  // 0..255
+        const int m = m0 + t;
+        const int ex = (t < nt && m < a.M) ? a.xexp[m] : 0;
+        rs_tab[t] = __int_as_float((127 - ex / 2) << 23);
+        rs_tab[NT_MAX + t] = __int_as_float((127 - (ex - ex / 2)) << 23);
+      }
+      // uniform over the 8 epilogue warps (also publishes rs_tab; MODE 1 pairs
+      // them on named barrier 1 below)
+      const bool mine = !*abort_flag && gqd::mbar_wait_bounded(acc_full, 0);
+      uint32_t all_ok;
+      asm volatile("{\n\t.reg .pred p, q;\n\tsetp.ne.u32 q, %1, 0;\n\tbar.red.and.pred p, 1, %2, q;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+                   : "=r"(all_ok)
+                   : "r"((uint32_t)mine), "r"(kProdWarps * 32)
+                   : "memory");
+      const bool ok = all_ok != 0;
       if (!ok) *abort_flag = 1;
       tc_fence_after();
+      const int half = grp;
+      const int tcount = nt / 2;
+      // weight row of this lane -> output column n
+      const int n = n0 + (MODE == 1 ? (row & (OW - 1)) : row);
+      const bool col_ok = n < a.N;
+      const float sn = col_ok ? (MODE == 1 && quarter >= 2 ? a.s2[n] : a.s[n]) : 0.0f;
+      // MODE 1: the up rows (quarters 2, 3) hand their values to the gate rows
+      float *up = reinterpret_cast<float *>(sX);  // [nt tokens][OW] (the load ring is idle now)
+      float *yc = a.y + a.y_col0 + n;
       if (ok) {
-        // every MMA has completed, so the pipeline buffers are free for staging
-        float *stg = reinterpret_cast<float *>(sB) + (warp - 2) * (32 * 33);
-        const int row0 = m0 + q * 32;
-        for (int c0 = half * HALF_W; c0 < (half + 1) * HALF_W; c0 += 32) {
-          float v[32], u[32];
-          const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + c0;
-          tmem_ld16(taddr, *reinterpret_cast<float(*)[16]>(v));
-          tmem_ld16(taddr + 16, *reinterpret_cast<float(*)[16]>(v + 16));
-          if (MODE == 1) {
-            tmem_ld16(taddr + BN / 2, *reinterpret_cast<float(*)[16]>(u));
-            tmem_ld16(taddr + BN / 2 + 16, *reinterpret_cast<float(*)[16]>(u + 16));
-          }
-          // lane = row: scale and the row-independent part of the MODE epilogue
+        for (int c0 = half * tcount; c0 < (half + 1) * tcount; c0 += 32) {
+          uint32_t d0[16], d1[16];
+          const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c0;
+          tmem_ld16_nowait(taddr, d0);
+          tmem_ld16_nowait(taddr + 16, d1);
+          tmem_wait_ld16(d0);
+          tmem_wait_ld16(d1);
+          float o[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
-            const int n = min(n0 + c0 + j, a.N - 1);  // columns past N are computed, never stored
-            float o = __fmul_rn(v[j], a.s[n]);
-            if (MODE == 1) {
-              o = __fmul_rn(gqd::gelu_tanh(o), __fmul_rn(u[j], a.s2[n]));
-            } else if (MODE == 2) {
-              o = gqd::gelu_tanh(o);
-            } else if (MODE == 3) {
-              if (a.cap > 0.0f) o = __fmul_rn(a.cap, tanhf(__fdiv_rn(o, a.cap)));
-            }
-            stg[lane * 33 + j] = o;
+            const float v = __uint_as_float(j < 16 ? d0[j] : d1[j - 16]);
+            o[j] = __fmul_rn(__fmul_rn(__fmul_rn(v, rs_tab[c0 + j]), rs_tab[NT_MAX + c0 + j]), sn);
           }
-          __syncwarp();
-          // lane = column: one 128-byte row segment per store instruction
-          const int n = n0 + c0 + lane;
-          if (n < a.N) {
-            for (int r = 0; r < 32; ++r) {
-              const int m = row0 + r;
-              if (m >= a.M) break;
-              float o = stg[r * 33 + lane];
-              if (MODE == 2) o = __fmul_rn(o, a.bs[(size_t)m * a.b_stride + a.b_off + n]);
-              a.y[(size_t)m * a.ldy + a.y_col0 + n] = o;
+          if (MODE == 1) {
+            if (quarter >= 2) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) up[(c0 + j) * OW + (row & (OW - 1))] = o[j];
+            }
+            asm volatile("bar.sync 1, %0;" ::"r"(kProdWarps * 32) : "memory");
+            if (quarter < 2 && col_ok) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                const int m = m0 + c0 + j;
+                if (m < a.M)
+                  yc[(size_t)m * a.ldy] = __fmul_rn(gqd::gelu_tanh(o[j]), up[(c0 + j) * OW + (row & (OW - 1))]);
+              }
+            }
+            asm volatile("bar.sync 1, %0;" ::"r"(kProdWarps * 32) : "memory");
+          } else if (col_ok) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int m = m0 + c0 + j;
+              if (m >= a.M) continue;
+              float r = o[j];
+              if (MODE == 2) {
+                r = __fmul_rn(gqd::gelu_tanh(r), a.bs[(size_t)m * a.b_stride + a.b_off + n]);
+              } else if (MODE == 3) {
+                if (a.cap > 0.0f) r = __fmul_rn(a.cap, tanhf(__fdiv_rn(r, a.cap)));
+              }
+              yc[(size_t)m * a.ldy] = r;
             }
           }
-          __syncwarp();
         }
       }
       tc_fence_before();
@@ -342,18 +438,56 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// f32 -> bf16 (round to nearest even), [M, K] row-major, K % 4 == 0.
-__global__ void cast_bf16_kernel(const float *x, __nv_bfloat16 *xb, int64_t n4) {
+// f32 -> f16 with a power of two per row: e[m] = 14 - ceil-exponent of max|x[m]|
+// (so |x * 2^e| < 2^14), K permuted inside each group of G codes as kperm<BITS>.
+// One block per row; the row is read twice (the second time from L1/L2).
+template <int BITS>
+__global__ void cast_f16_kernel(const float *x, __half *xh, int *xexp, int K) {
   gqd::griddep_wait();
   gqd::griddep_launch_dependents();
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
-    const float4 v = reinterpret_cast<const float4 *>(x)[i];
-    __nv_bfloat162 lo = __floats2bfloat162_rn(v.x, v.y);
-    __nv_bfloat162 hi = __floats2bfloat162_rn(v.z, v.w);
-    uint2 o;
-    o.x = *reinterpret_cast<uint32_t *>(&lo);
-    o.y = *reinterpret_cast<uint32_t *>(&hi);
-    reinterpret_cast<uint2 *>(xb)[i] = o;
+  constexpr int G = BITS == 2 ? 16 : 8;
+  const int m = blockIdx.x;
+  const float *xr = x + (size_t)m * K;
+  __shared__ float red[32];
+  float mx = 0.0f;
+  for (int k4 = threadIdx.x; k4 < K / 4; k4 += blockDim.x) {
+    const float4 v = reinterpret_cast<const float4 *>(xr)[k4];
+    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  mx = 0.0f;
+  for (int i = 0; i < (int)(blockDim.x >> 5); ++i) mx = fmaxf(mx, red[i]);
+  int e = 0;
+  if (mx > 0.0f && isfinite(mx)) frexpf(mx, &e);  // max|x| < 2^e
+  const int s = 14 - e;
+  const float f1 = __int_as_float((s / 2 + 127) << 23), f2 = __int_as_float((s - s / 2 + 127) << 23);
+  if (threadIdx.x == 0) xexp[m] = s;
+  __half *hr = xh + (size_t)m * K;
+  for (int gi = threadIdx.x; gi < K / G; gi += blockDim.x) {
+    float v[G];
+#pragma unroll
+    for (int q = 0; q < G / 4; ++q) {
+      const float4 t = reinterpret_cast<const float4 *>(xr + gi * G)[q];
+      v[4 * q] = t.x;
+      v[4 * q + 1] = t.y;
+      v[4 * q + 2] = t.z;
+      v[4 * q + 3] = t.w;
+    }
+#pragma unroll
+    for (int c = 0; c < G / 8; ++c) {
+      uint32_t o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float a0 = __fmul_rn(__fmul_rn(v[kperm<BITS>(8 * c + 2 * j)], f1), f2);
+        const float a1 = __fmul_rn(__fmul_rn(v[kperm<BITS>(8 * c + 2 * j + 1)], f1), f2);
+        const __half2 h = __floats2half2_rn(a0, a1);
+        o[j] = *reinterpret_cast<const uint32_t *>(&h);
+      }
+      reinterpret_cast<uint4 *>(hr + gi * G)[c] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
   }
 }
 
@@ -361,26 +495,26 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() { return gq_encode_fn(); }
 
 template <int BITS, bool SIGNED, int MODE>
 int launch_t(gq_ctx *ctx, const CUtensorMap &map, const CUtensorMap &mw, const CUtensorMap &mw2,
-             const PrefillArgs &a, dim3 grid, size_t smem) {
+             const PrefillArgs &a, dim3 grid) {
   auto kern = prefill_tc_kernel<BITS, SIGNED, MODE>;
   static bool attr_set[64] = {};
   const int dev = ctx->device & 63;
   if (!attr_set[dev]) {
-    GQ_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    GQ_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Ring<BITS>::kSmem));
     attr_set[dev] = true;
   }
-  GQ_CUDA_TRY(ctx, gq_launch(ctx, kern, grid, dim3(kThreads), smem, map, mw, mw2, a));
+  GQ_CUDA_TRY(ctx, gq_launch(ctx, kern, grid, dim3(kThreads), Ring<BITS>::kSmem, map, mw, mw2, a));
   return GQ_OK;
 }
 
 template <int BITS, bool SIGNED>
 int launch_mode(gq_ctx *ctx, int mode, const CUtensorMap &map, const CUtensorMap &mw, const CUtensorMap &mw2,
-                const PrefillArgs &a, dim3 grid, size_t smem) {
+                const PrefillArgs &a, dim3 grid) {
   switch (mode) {
-    case 0: return launch_t<BITS, SIGNED, 0>(ctx, map, mw, mw2, a, grid, smem);
-    case 1: return launch_t<BITS, SIGNED, 1>(ctx, map, mw, mw2, a, grid, smem);
-    case 2: return launch_t<BITS, SIGNED, 2>(ctx, map, mw, mw2, a, grid, smem);
-    default: return launch_t<BITS, SIGNED, 3>(ctx, map, mw, mw2, a, grid, smem);
+    case 0: return launch_t<BITS, SIGNED, 0>(ctx, map, mw, mw2, a, grid);
+    case 1: return launch_t<BITS, SIGNED, 1>(ctx, map, mw, mw2, a, grid);
+    case 2: return launch_t<BITS, SIGNED, 2>(ctx, map, mw, mw2, a, grid);
+    default: return launch_t<BITS, SIGNED, 3>(ctx, map, mw, mw2, a, grid);
   }
 }
 
@@ -396,7 +530,43 @@ CUresult encode_weight_map(CUtensorMap *map, const uint8_t *w, int64_t n, int64_
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
 
-constexpr size_t kSmemBytes = 1024 + STAGES * (A_STAGE + B_STAGE + P_STAGE) + (3 * STAGES + 1) * 8 + 16;
+// Tensor map over the f16 activations [m, k], box nt rows x 64 halves, 128-byte swizzle.
+CUresult encode_x_map(CUtensorMap *map, const __half *xh, int64_t m, int64_t k, int nt) {
+  cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)m};
+  cuuint64_t strides[1] = {(cuuint64_t)k * 2};
+  cuuint32_t box[2] = {BK, (cuuint32_t)nt};
+  cuuint32_t estr[2] = {1, 1};
+  return encode_fn()(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half *>(xh), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+template <int BITS>
+cudaError_t launch_cast(cudaStream_t stream, bool pdl, const float *x, __half *xh, int *xexp, int64_t m, int64_t k) {
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  cfg.gridDim = dim3((unsigned)m);
+  cfg.blockDim = dim3(256);
+  cfg.stream = stream;
+  if (pdl) {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  return cudaLaunchKernelEx(&cfg, cast_f16_kernel<BITS>, x, xh, xexp, (int)k);
+}
+
+cudaError_t cast_any(int bits, cudaStream_t stream, bool pdl, const float *x, __half *xh, int *xexp, int64_t m,
+                     int64_t k) {
+  if (bits == 4) return launch_cast<4>(stream, pdl, x, xh, xexp, m, k);
+  if (bits == 2) return launch_cast<2>(stream, pdl, x, xh, xexp, m, k);
+  return launch_cast<8>(stream, pdl, x, xh, xexp, m, k);
+}
+
+size_t smem_for(int bits) {
+  return bits == 4 ? Ring<4>::kSmem : (bits == 2 ? Ring<2>::kSmem : Ring<8>::kSmem);
+}
 
 }  // namespace
 
@@ -407,10 +577,11 @@ bool gq_prefill_supported(gq_ctx *ctx, const gq_qweight *w, int64_t m) {
   if (m < 16 || w->group_size != w->k || w->k % BK != 0 || w->k <= 0 || w->n <= 0) return false;
   if (m > (1ll << 30) || w->n > (1ll << 30) || w->k > (1 << 24)) return false;
   if ((uintptr_t)w->bytes % 16 != 0) return false;  // the packed tiles come in by TMA
-  return kSmemBytes <= ctx->smem_optin && encode_fn() != nullptr;
+  return smem_for(w->bits) <= ctx->smem_optin && encode_fn() != nullptr;
 }
 
-// Workspace for the bf16 copy of x (grown on demand, stream-ordered).
+// Workspace for the f16 copy of x and the per-row exponents (grown on demand,
+// stream-ordered).
 static int ws_get(gq_ctx *ctx, size_t bytes, void **out) {
   if (ctx->ws_cap < bytes) {
     if (ctx->ws) cudaFreeAsync(ctx->ws, ctx->stream);
@@ -427,36 +598,25 @@ int gq_prefill_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq
                       const float *bs, int64_t b_stride, int64_t b_off, float cap, float *y, int64_t ldy,
                       int64_t y_col0) {
   const int64_t K = w->k;
+  const size_t xh_bytes = ((size_t)(m * K) * 2 + 255) & ~size_t(255);
   void *wsp = nullptr;
-  int rc = ws_get(ctx, (size_t)(m * K) * 2, &wsp);
+  int rc = ws_get(ctx, xh_bytes + (size_t)m * sizeof(int), &wsp);
   if (rc != GQ_OK) return rc;
-  __nv_bfloat16 *xb = static_cast<__nv_bfloat16 *>(wsp);
-  {
-    const int64_t n4 = m * K / 4;
-    int64_t g = (n4 + 255) / 256;
-    if (g > (int64_t)ctx->num_sms * 8) g = (int64_t)ctx->num_sms * 8;
-    GQ_CUDA_TRY(ctx, gq_launch(ctx, cast_bf16_kernel, dim3((unsigned)g), dim3(256), 0, x, xb, n4));
-  }
+  __half *xh = static_cast<__half *>(wsp);
+  int *xexp = reinterpret_cast<int *>(static_cast<uint8_t *>(wsp) + xh_bytes);
+  GQ_CUDA_TRY(ctx, cast_any(w->bits, ctx->stream, ctx->pdl, x, xh, xexp, m, K));
+  const int nt = m > 128 ? NT_MAX : 128;
   CUtensorMap map;
-  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)m};
-  cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-  cuuint32_t box[2] = {BK, BM};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult cr = encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, xb, dims, strides, box, estr,
-                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (cr != CUDA_SUCCESS) return gq_fail(ctx, GQ_ERR_CUDA, "prefill: cuTensorMapEncodeTiled failed");
+  if (encode_x_map(&map, xh, m, K, nt) != CUDA_SUCCESS)
+    return gq_fail(ctx, GQ_ERR_CUDA, "prefill: activation tensor map");
   PrefillArgs a = {};
+  a.nt = nt;
   a.M = (int)m;
   a.N = (int)w->n;
   a.K = (int)K;
-  a.w = w->bytes;
   a.s = w->scales;
-  if (w2) {
-    a.w2 = w2->bytes;
-    a.s2 = w2->scales;
-  }
-  a.row_bytes = (int)w->row_bytes;
+  a.s2 = w2 ? w2->scales : nullptr;
+  a.xexp = xexp;
   a.bs = bs;
   a.b_stride = b_stride;
   a.b_off = b_off;
@@ -465,34 +625,37 @@ int gq_prefill_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq
   a.ldy = ldy;
   a.y_col0 = y_col0;
   a.err = ctx->dev_err;
-  const int ow = (mode == 1) ? BN / 2 : BN;
+  const int ow = (mode == 1) ? MW / 2 : MW;
   CUtensorMap mw, mw2;
   if (encode_weight_map(&mw, w->bytes, w->n, w->row_bytes, w->bits, ow) != CUDA_SUCCESS ||
       encode_weight_map(&mw2, w2 ? w2->bytes : w->bytes, w->n, w->row_bytes, w->bits, ow) != CUDA_SUCCESS)
     return gq_fail(ctx, GQ_ERR_CUDA, "prefill: weight tensor map");
-  dim3 grid((unsigned)((m + BM - 1) / BM), (unsigned)((w->n + ow - 1) / ow));
-  if (w->bits == 4) return launch_mode<4, false>(ctx, mode, map, mw, mw2, a, grid, kSmemBytes);
-  if (w->bits == 2) return launch_mode<2, false>(ctx, mode, map, mw, mw2, a, grid, kSmemBytes);
-  if (w->signed_i8) return launch_mode<8, true>(ctx, mode, map, mw, mw2, a, grid, kSmemBytes);
-  return launch_mode<8, false>(ctx, mode, map, mw, mw2, a, grid, kSmemBytes);
+  dim3 grid((unsigned)((m + nt - 1) / nt), (unsigned)((w->n + ow - 1) / ow));
+  if (w->bits == 4) return launch_mode<4, false>(ctx, mode, map, mw, mw2, a, grid);
+  if (w->bits == 2) return launch_mode<2, false>(ctx, mode, map, mw, mw2, a, grid);
+  if (w->signed_i8) return launch_mode<8, true>(ctx, mode, map, mw, mw2, a, grid);
+  return launch_mode<8, false>(ctx, mode, map, mw, mw2, a, grid);
 }
 
 // ---- allocation-free variant ---------------------------------------------------
 // For callers that cannot allocate device memory at call time: a serving process
 // that reserves its whole HBM budget at start-up and treats any later cudaMalloc
 // as an error, or an embedder whose buffers all come from its own arena. The
-// scratch this path needs (the bf16 copy of the activations) lives in this
-// file-scope array instead of a context workspace; every GPU that loads the
-// library holds it until the process exits.
+// scratch this path needs (the f16 copy of the activations and one exponent per
+// row) lives in these file-scope arrays instead of a context workspace; every
+// GPU that loads the library holds them until the process exits.
 namespace {
-constexpr int64_t kStaticScratchElems = int64_t(4) << 20;  // 4 Mi bf16 (8 MiB): M*K <= 4,194,304
-static __device__ __align__(256) __nv_bfloat16 g_prefill_scratch[kStaticScratchElems];
+constexpr int64_t kStaticScratchElems = int64_t(4) << 20;  // 4 Mi f16 (8 MiB): M*K <= 4,194,304
+constexpr int64_t kStaticRows = kStaticScratchElems / BK;   // K >= 64, so M <= 65,536
+static __device__ __align__(256) __half g_prefill_scratch[kStaticScratchElems];
+static __device__ __align__(256) int g_prefill_xexp[kStaticRows];
 
-// Host-side device addresses of the array, one per device. Host code must not
-// pass the symbol itself to a kernel: in host code it names a host-side
-// stand-in, not device memory.
+// Host-side device addresses of the arrays, one per device. Host code must not
+// pass the symbols themselves to a kernel: in host code they name host-side
+// stand-ins, not device memory.
 struct StaticSetup {
   void *scratch = nullptr;
+  void *xexp = nullptr;
   int smem_optin = 0;
   bool ready = false;
 };
@@ -503,7 +666,9 @@ cudaError_t static_setup(int dev, StaticSetup **out) {
   if (!st.ready) {
     cudaError_t e = cudaGetSymbolAddress(&st.scratch, g_prefill_scratch);
     if (e != cudaSuccess) return e;
-    if (st.scratch == nullptr) return cudaErrorInvalidSymbol;
+    e = cudaGetSymbolAddress(&st.xexp, g_prefill_xexp);
+    if (e != cudaSuccess) return e;
+    if (st.scratch == nullptr || st.xexp == nullptr) return cudaErrorInvalidSymbol;
     e = cudaDeviceGetAttribute(&st.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     if (e != cudaSuccess) return e;
     st.ready = true;
@@ -516,12 +681,12 @@ template <int BITS, bool SIGNED>
 cudaError_t static_launch(cudaStream_t stream, const CUtensorMap &map, const CUtensorMap &mw, const PrefillArgs &a,
                           dim3 grid) {
   auto kern = prefill_tc_kernel<BITS, SIGNED, 0>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemBytes);
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Ring<BITS>::kSmem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = kSmemBytes;
+  cfg.dynamicSmemBytes = Ring<BITS>::kSmem;
   cfg.stream = stream;
   return cudaLaunchKernelEx(&cfg, kern, map, mw, mw, a);
 }
@@ -543,38 +708,28 @@ extern "C" int gq_linear_prefill_static(void *cuda_stream, const float *x, int64
   if (cudaGetDevice(&dev) != cudaSuccess) return GQ_ERR_CUDA;
   StaticSetup *st = nullptr;
   if (static_setup(dev, &st) != cudaSuccess) return GQ_ERR_CUDA;
-  if ((size_t)st->smem_optin < kSmemBytes || encode_fn() == nullptr) return GQ_ERR_UNSUPPORTED;
+  if ((size_t)st->smem_optin < smem_for(bits) || encode_fn() == nullptr) return GQ_ERR_UNSUPPORTED;
   cudaStream_t stream = static_cast<cudaStream_t>(cuda_stream);
-  __nv_bfloat16 *xb = static_cast<__nv_bfloat16 *>(st->scratch);
-  {
-    const int64_t n4 = m * k / 4;
-    const unsigned g = (unsigned)std::min<int64_t>((n4 + 255) / 256, 148 * 8);
-    cast_bf16_kernel<<<g, 256, 0, stream>>>(x, xb, n4);
-    if (cudaGetLastError() != cudaSuccess) return GQ_ERR_CUDA;
-  }
+  __half *xh = static_cast<__half *>(st->scratch);
+  int *xexp = static_cast<int *>(st->xexp);
+  if (cast_any(bits, stream, false, x, xh, xexp, m, k) != cudaSuccess) return GQ_ERR_CUDA;
+  const int nt = m > 128 ? NT_MAX : 128;
   CUtensorMap map;
-  cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)m};
-  cuuint64_t strides[1] = {(cuuint64_t)k * 2};
-  cuuint32_t box[2] = {BK, BM};
-  cuuint32_t estr[2] = {1, 1};
-  if (encode_fn()(&map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, xb, dims, strides, box, estr,
-                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
-    return GQ_ERR_CUDA;
+  if (encode_x_map(&map, xh, m, k, nt) != CUDA_SUCCESS) return GQ_ERR_CUDA;
   PrefillArgs a = {};
+  a.nt = nt;
   a.M = (int)m;
   a.N = (int)n;
   a.K = (int)k;
-  a.w = qbytes;
   a.s = scales;
-  a.row_bytes = (int)(signed_i8 ? k : k * bits / 8);
+  a.xexp = xexp;
   a.y = y;
   a.ldy = n;
   a.y_col0 = 0;
   a.err = nullptr;  // no context: a timed-out wait is still bounded, but not reported
-  const dim3 grid((unsigned)((m + BM - 1) / BM), (unsigned)((n + BN - 1) / BN));
+  const dim3 grid((unsigned)((m + nt - 1) / nt), (unsigned)((n + MW - 1) / MW));
   CUtensorMap mw;
-  if (encode_weight_map(&mw, qbytes, n, a.row_bytes, bits, BN) != CUDA_SUCCESS) return GQ_ERR_CUDA;
+  if (encode_weight_map(&mw, qbytes, n, signed_i8 ? k : k * bits / 8, bits, MW) != CUDA_SUCCESS) return GQ_ERR_CUDA;
   cudaError_t e;
   if (bits == 4) e = static_launch<4, false>(stream, map, mw, a, grid);
   else if (bits == 2) e = static_launch<2, false>(stream, map, mw, a, grid);

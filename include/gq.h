@@ -152,12 +152,14 @@ int gq_embed_rows(gq_ctx *ctx, const gq_qweight *table, const uint32_t *ids, int
  * callers that cannot allocate device memory when they call (a serving process
  * that reserves all of its HBM at start-up and must not cudaMalloc afterwards,
  * or an embedder whose buffers all come from its own arena), and who therefore
- * cannot create a gq_ctx either. y[m, n] = bf16(x) · deq(W)ᵀ with the same
+ * cannot create a gq_ctx either. y[m, n] = x' · deq(W)ᵀ, x' = x rounded to f16
+ * after a power-of-two scaling per row (undone exactly), with the same
  * tensor-core kernel as gq_linear uses for m >= 128 (any m >= 1 is accepted).
  * Weights are caller device pointers in the upload layout: qbytes [n, row_bytes]
  * (16-byte aligned), one f32 scale per row. Requires k % 64 == 0 and
- * m * k <= 4,194,304: the bf16 copy of x goes to a file-scope 8 MiB device array
- * that every GPU loading the library holds until exit; larger sizes return
+ * m * k <= 4,194,304: the f16 copy of x goes to a file-scope 8 MiB device array
+ * (plus 256 KB of row exponents) that every GPU loading the library holds until
+ * exit; larger sizes return
  * GQ_ERR_INVALID_ARGUMENT. Nothing is allocated. The first call on a device
  * looks up that array's device address (cudaGetSymbolAddress) and should come
  * before any stream capture. All calls share the array: calls that overlap on

@@ -3,7 +3,7 @@ regular one (gq_linear), through the C ABI (needs a B200).
 
 gq_linear_prefill_static serves callers that cannot allocate device memory at
 call time (a serving process that reserved its HBM at start-up, an embedder
-whose buffers all come from its own arena): its scratch, the bf16 copy of the
+whose buffers all come from its own arena): its scratch, the f16 copy of the
 activations, is a fixed 8 MiB device array inside the library instead of a
 context workspace. These checks call it twice in a row (the second call reuses
 the array the first one left behind) and compare each result with gq_linear on
