@@ -112,6 +112,61 @@ __global__ void embed_quad_kernel(QView q, const uint32_t *ids, int64_t t, float
   }
 }
 
+// EMBED_Q, one warp per output row (the row's id, packed row and scale row are
+// looked up once): each lane turns 16 consecutive codes into 16 outputs per step
+// (one 4/8/16-byte load, four 16-byte stores), the warp covering 512 contiguous
+// output values. Same operation order as embed_quad_kernel (bit-identical).
+// Requires D % 16 == 0, group % 16 == 0 (a 16-code step never crosses a scale
+// group), 16-byte aligned output rows and packed rows aligned to one step.
+template <int BITS, bool SIGNED>
+__global__ void embed_row_kernel(QView q, const uint32_t *ids, int64_t t, float emb, float *out, uint32_t *err) {
+  gqd::griddep_wait();
+  gqd::griddep_launch_dependents();
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= t) return;
+  const uint32_t id = __ldg(ids + row);
+  float4 *orow = reinterpret_cast<float4 *>(out + row * q.k);
+  const int steps = (int)(q.k >> 4);
+  if ((int64_t)id >= q.n) {
+    for (int j = lane; j < steps; j += 32)
+#pragma unroll
+      for (int u = 0; u < 4; ++u) orow[4 * j + u] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (lane == 0) gqd::report(err, GQ_DEVERR_BAD_ID);
+    return;
+  }
+  const uint8_t *rp = q.bytes + (int64_t)id * q.row_bytes;
+  const float *sr = q.scales + (int64_t)id * q.scale_stride;
+  const int gshift = (q.group == q.k) ? 31 : (31 - __clz((int)q.group));  // group is a power of two here
+  for (int j = lane; j < steps; j += 32) {
+    int32_t c[16];
+    if constexpr (BITS == 8) {
+      const uint4 w = __ldg(reinterpret_cast<const uint4 *>(rp) + j);
+      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const uint32_t b = (ws[i >> 2] >> (8 * (i & 3))) & 0xffu;
+        c[i] = SIGNED ? (int32_t)(int8_t)b : (int32_t)b - 128;
+      }
+    } else if constexpr (BITS == 4) {
+      const uint2 w = __ldg(reinterpret_cast<const uint2 *>(rp) + j);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) c[i] = (int32_t)(((i < 8 ? w.x : w.y) >> (4 * (i & 7))) & 0xfu) - 8;
+    } else {
+      const uint32_t w = __ldg(reinterpret_cast<const uint32_t *>(rp) + j);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) c[i] = (int32_t)((w >> (2 * i)) & 0x3u) - 2;
+    }
+    const float sc = __ldg(sr + (gshift == 31 ? 0 : ((16 * j) >> gshift)));
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      orow[4 * j + u] = make_float4(__fmul_rn(__fmul_rn((float)c[4 * u], sc), emb),
+                                    __fmul_rn(__fmul_rn((float)c[4 * u + 1], sc), emb),
+                                    __fmul_rn(__fmul_rn((float)c[4 * u + 2], sc), emb),
+                                    __fmul_rn(__fmul_rn((float)c[4 * u + 3], sc), emb));
+  }
+}
+
 // EMBED_Q for any D: one thread per output element.
 __global__ void embed_scalar_kernel(QView q, const uint32_t *ids, int64_t t, float emb,
                                     float *out, uint32_t *err) {
@@ -202,6 +257,22 @@ int gq_embed_launch(gq_ctx *ctx, const gq_qweight *w, const uint32_t *ids, int64
                     float *out) {
   if (t == 0 || w->k == 0) return GQ_OK;
   const QView q = view_of(w);
+  const int64_t g = w->group_size;
+  const bool row_path = w->k % 16 == 0 && ((uintptr_t)out % 16 == 0) && (g == w->k || (g % 16 == 0 && (g & (g - 1)) == 0)) &&
+                        (uintptr_t)w->bytes % 16 == 0 && w->row_bytes % (w->signed_i8 || w->bits == 8 ? 16 : (w->bits == 4 ? 8 : 4)) == 0 &&
+                        t <= (int64_t)0x7fffffff * 8;
+  if (row_path) {
+    const unsigned blocks = (unsigned)((t + 7) / 8);
+    if (w->signed_i8)
+      GQ_CUDA_TRY(ctx, gq_launch(ctx, embed_row_kernel<8, true>, dim3(blocks), dim3(256), 0, q, ids, t, emb, out, ctx->dev_err));
+    else if (w->bits == 8)
+      GQ_CUDA_TRY(ctx, gq_launch(ctx, embed_row_kernel<8, false>, dim3(blocks), dim3(256), 0, q, ids, t, emb, out, ctx->dev_err));
+    else if (w->bits == 4)
+      GQ_CUDA_TRY(ctx, gq_launch(ctx, embed_row_kernel<4, false>, dim3(blocks), dim3(256), 0, q, ids, t, emb, out, ctx->dev_err));
+    else
+      GQ_CUDA_TRY(ctx, gq_launch(ctx, embed_row_kernel<2, false>, dim3(blocks), dim3(256), 0, q, ids, t, emb, out, ctx->dev_err));
+    return GQ_OK;
+  }
   const bool quad = (w->k % 4 == 0) && ((uintptr_t)out % 16 == 0) &&
                     (w->signed_i8 || w->bits == 8 ? w->row_bytes % 4 == 0
                                                   : (w->bits == 4 ? w->row_bytes % 2 == 0 : true));
