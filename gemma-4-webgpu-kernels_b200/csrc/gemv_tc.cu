@@ -700,6 +700,17 @@ bool tc_plan(const gq_ctx *ctx, const gq_qweight *w, int nw, TcPlan &p) {
   if (ntc == 1) {
     const int units = direct ? total_raw : p.kblocks;
     p.issuers = std::max(1, std::min(std::min(kMaxIss, units), 512 / (nw * p.tile_rows)));
+    // Slots of a ring that wraps must return to the same issuer (units are dealt
+    // round-robin; an mbarrier parity wait cannot tell a phase two completions
+    // ahead from a completed one): the depth is then a multiple of the issuers.
+    if (direct && p.raw_stages < total_raw) {
+      while (p.issuers > 1 && p.raw_stages < p.issuers) --p.issuers;
+      p.raw_stages -= p.raw_stages % p.issuers;
+    }
+    if (!direct && p.mma_stages < p.kblocks) {
+      while (p.issuers > 1 && p.mma_stages < p.issuers) --p.issuers;
+      p.mma_stages -= p.mma_stages % p.issuers;
+    }
   } else {
     p.issuers = 1;
   }

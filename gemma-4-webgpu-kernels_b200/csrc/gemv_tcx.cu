@@ -1,0 +1,739 @@
+// gemv_tcx.cu — short-M GEMV (3 <= M <= 16 activation rows) on the tensor cores.
+//
+// The same exact integer dot products as gemv_tc.cu (tcgen05.mma.kind::i8 on
+// four signed byte limbs of x in 30-bit fixed point), for the M = 3..16 rows of
+// a short decode batch or a speculative chunk (rust/src/backend_wgpu.rs:646-695
+// sends M <= 15 to MATMUL_Q, rust/src/kernels/matmul_q.wgsl:96-169):
+//  * a pre-pass kernel (one block per activation row) writes the limbs of all M
+//    rows once, as a [4*M, Kp] s8 matrix in global memory (row = token*4 + limb,
+//    K permuted inside each 16-code group like the widened weights), plus each
+//    row's exponent, sum of fixed-point values and a non-finite flag;
+//  * the GEMV streams that matrix by TMA, one 64-row x 128-byte swizzled tile per
+//    K-block (rows past 4*M arrive zero-filled), as the A operand of an M = 64
+//    MMA: accumulator row r sits in TMEM lane 32*(r/16) + r%16, so lane quarter q
+//    holds the four limbs of tokens 4q .. 4q+3 in its lanes 0-15;
+//  * weights are the B operand exactly as in gemv_tc.cu (I8 rows straight from
+//    TMA into the swizzled layout, sub-byte and U8 codes widened by 4 warps), one
+//    tile of up to 256 rows per CTA, K-blocks dealt round-robin to three issuing
+//    threads with separate accumulators;
+//  * epilogue warp q recombines the limbs of its four tokens in int64, removes
+//    the zero point exactly and converts once: y = f32(T * 2^-s_m) * scale[n].
+// The limb matrix is tiny and shared by every CTA, so after the first CTAs it
+// streams from L2; the weights stream from HBM once for all M rows.
+// Every wait is bounded (GQ_DEVERR_WAIT_TIMEOUT); TMA copies in flight are
+// drained, outstanding MMAs committed and TMEM freed before the CTA exits.
+#include <cuda_runtime.h>
+#include <math.h>
+
+#include <algorithm>
+
+#include "tc_common.cuh"
+
+namespace {
+using namespace gqt;
+
+constexpr int kThreads = 256;  // warp 0 TMA, warps 1-3 MMA issue, warps 4-7 expanders + epilogue
+constexpr int kKB = 128;       // codes per K-block
+constexpr int kMaxRaw = 8;
+constexpr int kMaxMma = 48;    // widened ring: up to every K-block of K = 6144
+constexpr int kMaxXa = 8;      // A (limb) tile ring
+constexpr int kMaxIss = 3;
+constexpr int kExpWarps = 4;
+constexpr int kMaxTok = 16;
+constexpr int kMaxK = 8192;
+constexpr uint32_t XA_TILE = 64 * 128;  // 64 limb rows x one K-block
+
+struct TcxArgs {
+  int M, K, N;
+  const float *s;
+  const float *s2;
+  const float *bs;
+  int64_t b_stride, b_off;
+  float cap;
+  float *y;
+  int64_t ldy, y_col0;
+  const int *xexp;        // [M] per-row exponent s_m (X = rint(x * 2^s_m))
+  const long long *sumx;  // [M] sum_k X
+  const uint32_t *bad;    // [M] non-finite x row
+  int tile_rows;          // MMA N: multiple of 16, <= 256 / NW
+  int kblocks, kbr;
+  int raw_stages, mma_stages, xa_stages;
+  int raw_bytes, mma_bytes;
+  int issuers;
+  int tmem_cols;
+  uint32_t *err;
+};
+
+struct TcxSmem {
+  uint32_t xa_off, raw_off, mma_off, bar_off, misc_off, total;
+};
+__host__ __device__ inline TcxSmem tcx_layout(int xa_stages, int raw_stages, int raw_bytes, int mma_stages,
+                                              int mma_bytes) {
+  TcxSmem L;
+  uint32_t o = 0;
+  L.xa_off = o;   o += (uint32_t)xa_stages * XA_TILE;
+  L.raw_off = o;  o += (uint32_t)raw_stages * (uint32_t)raw_bytes;
+  L.mma_off = o;  o += (uint32_t)mma_stages * (uint32_t)mma_bytes;
+  L.bar_off = o;  o += (2 * kMaxRaw + 2 * kMaxMma + 2 * kMaxXa + 2 * kMaxIss) * 8;
+  L.misc_off = o; o += 64;
+  L.total = o + 1024;
+  return L;
+}
+
+template <int BITS>
+__host__ __device__ constexpr int perm16(int p) {
+  return BITS == 4 ? ((p & 8) | ((p & 3) << 1) | ((p >> 2) & 1))  // 0,2,4,6,1,3,5,7 per 8
+         : BITS == 2 ? (((p & 3) << 2) | (p >> 2))               // 0,4,8,12,1,5,...
+                     : p;
+}
+
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
+  return r;
+}
+__device__ __forceinline__ bool wait_phase(uint64_t *bar, uint32_t parity) {
+  return gqd::mbar_try_wait(bar, parity) || gqd::mbar_wait_bounded(bar, parity);
+}
+
+// ---- pre-pass: x row m -> 30-bit fixed point -> four s8 limb rows ------------
+// Same arithmetic as the in-CTA staging of gemv_tc.cu: s = 30 - e with
+// max|x| < 2^e, X = rint(x * 2^s), balanced base-256 digits from X + 0x808080.
+template <int BITS>
+__global__ void xlimbs_kernel(const float *x, int K, int Kp, uint8_t *limbs, int *xexp, long long *sumx,
+                              uint32_t *bad) {
+  gqd::griddep_wait();
+  gqd::griddep_launch_dependents();
+  const int m = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const float4 *xr = reinterpret_cast<const float4 *>(x + (size_t)m * K);
+  __shared__ float wmax[8];
+  __shared__ uint32_t wbad[8];
+  __shared__ long long wsum[8];
+  float mx = 0.0f;
+  uint32_t b = 0;
+  for (int k4 = tid; k4 < K / 4; k4 += kThreads) {
+    const float4 v = __ldg(xr + k4);
+    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    b |= !(isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w));
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    b |= __shfl_xor_sync(0xffffffffu, b, o);
+  }
+  if (lane == 0) {
+    wmax[warp] = mx;
+    wbad[warp] = b;
+  }
+  __syncthreads();
+  mx = 0.0f;
+  b = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    mx = fmaxf(mx, wmax[i]);
+    b |= wbad[i];
+  }
+  int e = 0;
+  if (mx > 0.0f && isfinite(mx)) frexpf(mx, &e);
+  const int s = 30 - e;
+  const float f1 = __int_as_float((s / 2 + 127) << 23), f2 = __int_as_float((s - s / 2 + 127) << 23);
+  long long part = 0;
+  for (int gi = tid; gi < Kp / 16; gi += kThreads) {
+    int X[16];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (gi * 16 < K) v = __ldg(xr + gi * 4 + q);
+      X[4 * q + 0] = __float2int_rn(__fmul_rn(__fmul_rn(v.x, f1), f2));
+      X[4 * q + 1] = __float2int_rn(__fmul_rn(__fmul_rn(v.y, f1), f2));
+      X[4 * q + 2] = __float2int_rn(__fmul_rn(__fmul_rn(v.z, f1), f2));
+      X[4 * q + 3] = __float2int_rn(__fmul_rn(__fmul_rn(v.w, f1), f2));
+    }
+    uint32_t wv[16];
+#pragma unroll
+    for (int p = 0; p < 16; ++p) {
+      const int v = X[perm16<BITS>(p)];
+      part += v;
+      wv[p] = ((uint32_t)v + 0x00808080u) ^ 0x00808080u;
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const uint32_t t01a = prmt(wv[4 * q], wv[4 * q + 1], 0x5140), t23a = prmt(wv[4 * q + 2], wv[4 * q + 3], 0x5140);
+      const uint32_t t01b = prmt(wv[4 * q], wv[4 * q + 1], 0x7362), t23b = prmt(wv[4 * q + 2], wv[4 * q + 3], 0x7362);
+      wv[4 * q] = prmt(t01a, t23a, 0x5410);
+      wv[4 * q + 1] = prmt(t01a, t23a, 0x7632);
+      wv[4 * q + 2] = prmt(t01b, t23b, 0x5410);
+      wv[4 * q + 3] = prmt(t01b, t23b, 0x7632);
+    }
+#pragma unroll
+    for (int l = 0; l < 4; ++l)
+      *reinterpret_cast<uint4 *>(limbs + (size_t)(4 * m + l) * Kp + 16 * gi) =
+          make_uint4(wv[l], wv[4 + l], wv[8 + l], wv[12 + l]);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+  if (lane == 0) wsum[warp] = part;
+  __syncthreads();
+  if (tid == 0) {
+    long long t = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) t += wsum[i];
+    sumx[m] = t;
+    xexp[m] = s;
+    bad[m] = b;
+  }
+}
+
+// ---- the GEMV -------------------------------------------------------------------
+template <int BITS, bool SIGNED, int MODE>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemv_tcx_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_w2,
+                    const __grid_constant__ CUtensorMap map_x, const TcxArgs a) {
+  constexpr int NW = (MODE == 1) ? 2 : 1;
+  constexpr bool DIRECT = (BITS == 8 && SIGNED);
+  constexpr int KB_BYTES = kKB * BITS / 8;
+  constexpr int CPR = KB_BYTES / 16;
+  constexpr long long ZP = (BITS == 8) ? 0 : (1 << (BITS - 1));
+  // D = A * B^T: A = 64 limb rows (s8, M = 64), B = weight rows (s8, N = tile_rows), D s32.
+  const uint32_t idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(a.tile_rows >> 3) << 17) |
+                         ((uint32_t)(64 >> 4) << 24);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const TcxSmem L = tcx_layout(a.xa_stages, a.raw_stages, a.raw_bytes, a.mma_stages, a.mma_bytes);
+  uint8_t *xa = smem + L.xa_off;    // [xa_stages][64 x 128 B], swizzled (TMA)
+  uint8_t *raw = smem + L.raw_off;  // [raw_stages][raw_bytes]
+  uint8_t *wid = smem + L.mma_off;  // [mma_stages][NW][tile_rows x 128 B], swizzled
+  uint64_t *raw_full = reinterpret_cast<uint64_t *>(smem + L.bar_off);
+  uint64_t *raw_empty = raw_full + kMaxRaw;
+  uint64_t *mma_full = raw_empty + kMaxRaw;
+  uint64_t *mma_empty = mma_full + kMaxMma;
+  uint64_t *xa_full = mma_empty + kMaxMma;
+  uint64_t *xa_empty = xa_full + kMaxXa;
+  uint64_t *acc_full = xa_empty + kMaxXa;  // [kMaxIss]
+  uint64_t *done_bar = acc_full + kMaxIss;  // [kMaxIss]
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L.misc_off);
+  volatile uint32_t *abort_flag = tmem_slot + 1;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n_begin = blockIdx.x * a.tile_rows;
+  const int n_end = min(a.N, n_begin + a.tile_rows);
+  const int kblocks = a.kblocks, kbr = a.kbr, RS = a.raw_stages, MS = a.mma_stages, XS = a.xa_stages;
+  const int NI = a.issuers;
+  const int total_raw = (kblocks + kbr - 1) / kbr;
+  const int tile_bytes = a.tile_rows * 128;
+
+  if (tid == 0) {
+    for (int i = 0; i < kMaxRaw; ++i) {
+      gqd::mbar_init(&raw_full[i], 1);
+      gqd::mbar_init(&raw_empty[i], DIRECT ? 1 : kExpWarps);
+    }
+    for (int i = 0; i < kMaxMma; ++i) {
+      gqd::mbar_init(&mma_full[i], kExpWarps);
+      gqd::mbar_init(&mma_empty[i], 1);
+    }
+    for (int i = 0; i < kMaxXa; ++i) {
+      gqd::mbar_init(&xa_full[i], 1);
+      gqd::mbar_init(&xa_empty[i], 1);
+    }
+    for (int i = 0; i < kMaxIss; ++i) {
+      gqd::mbar_init(&acc_full[i], 1);
+      gqd::mbar_init(&done_bar[i], 1);
+    }
+    *abort_flag = 0;
+    gqd::fence_mbar_init();
+  }
+  __syncthreads();
+
+  auto issue = [&](int r) {  // raw stage r: K-blocks r*kbr .. +kbr-1
+    const int slot = r % RS, kb0 = r * kbr;
+    uint8_t *dst = raw + slot * a.raw_bytes;
+    if (DIRECT) {
+      const int nkb = min(kbr, kblocks - kb0);
+      gqd::mbar_arrive_expect_tx(&raw_full[slot], (uint32_t)(nkb * NW * tile_bytes));
+      for (int j = 0; j < nkb; ++j)
+        for (int h = 0; h < NW; ++h)
+          tma_load_2d(dst + (j * NW + h) * tile_bytes, h ? &map_w2 : &map_w, (kb0 + j) * kKB, n_begin,
+                      &raw_full[slot]);
+    } else {
+      gqd::mbar_arrive_expect_tx(&raw_full[slot], (uint32_t)(NW * a.tile_rows * kbr * KB_BYTES));
+      for (int h = 0; h < NW; ++h)
+        tma_load_2d(dst + h * a.tile_rows * kbr * KB_BYTES, h ? &map_w2 : &map_w, kb0 * KB_BYTES, n_begin,
+                    &raw_full[slot]);
+    }
+  };
+  // The limb ring is split per issuer (XI slots each) so every slot is filled
+  // and consumed in order by one producer and one consumer: a waiter then never
+  // asks for a phase two completions ahead of the barrier (which an mbarrier
+  // parity wait would report as already complete).
+  const int XI = XS / NI;
+  auto x_owner = [&](int g, int &ord) {  // issuer of K-block g and its ordinal there
+    if (DIRECT) {
+      const int u = g / kbr;
+      ord = (u / NI) * kbr + g % kbr;
+      return u % NI;
+    }
+    ord = g / NI;
+    return g % NI;
+  };
+  auto issue_x = [&](int slot, int g) {  // limb tile of K-block g
+    gqd::mbar_arrive_expect_tx(&xa_full[slot], XA_TILE);
+    tma_load_2d(xa + slot * XA_TILE, &map_x, g * kKB, 0, &xa_full[slot]);
+  };
+
+  // Widen K-block g into slot g % MS (warp-uniform; false on a timed-out wait).
+  auto expand = [&](int g) -> bool {
+    const int et = tid - (kThreads - kExpWarps * 32);
+    const int r = g / kbr, rslot = r % RS, j = g % kbr, mslot = g % MS;
+    bool ok = !*abort_flag && wait_phase(&raw_full[rslot], (uint32_t)(r / RS) & 1u);
+    ok = ok && (g < MS || wait_phase(&mma_empty[mslot], (uint32_t)((g / MS) - 1) & 1u));
+    if (!__all_sync(0xffffffffu, ok)) return false;
+    const int rstride = kbr * KB_BYTES;
+    const int items = NW * a.tile_rows * CPR;
+    for (int it = et; it < items; it += kExpWarps * 32) {
+      const int h = it / (a.tile_rows * CPR);
+      const int rem = it - h * (a.tile_rows * CPR);
+      const int row = rem / CPR, ic = rem - row * CPR;
+      const uint4 in = *reinterpret_cast<const uint4 *>(raw + rslot * a.raw_bytes + h * a.tile_rows * rstride +
+                                                         row * rstride + j * KB_BYTES + ic * 16);
+      uint8_t *dst = wid + mslot * a.mma_bytes + h * tile_bytes;
+      if constexpr (BITS == 4) {
+        const uint32_t m = 0x0F0F0F0Fu;
+        *reinterpret_cast<uint4 *>(dst + sw128_off(row, 2 * ic)) =
+            make_uint4(in.x & m, (in.x >> 4) & m, in.y & m, (in.y >> 4) & m);
+        *reinterpret_cast<uint4 *>(dst + sw128_off(row, 2 * ic + 1)) =
+            make_uint4(in.z & m, (in.z >> 4) & m, in.w & m, (in.w >> 4) & m);
+      } else if constexpr (BITS == 2) {
+        const uint32_t m = 0x03030303u;
+        const uint32_t w4[4] = {in.x, in.y, in.z, in.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          *reinterpret_cast<uint4 *>(dst + sw128_off(row, 4 * ic + q)) =
+              make_uint4(w4[q] & m, (w4[q] >> 2) & m, (w4[q] >> 4) & m, (w4[q] >> 6) & m);
+      } else {
+        const uint32_t f = 0x80808080u;
+        *reinterpret_cast<uint4 *>(dst + sw128_off(row, ic)) = make_uint4(in.x ^ f, in.y ^ f, in.z ^ f, in.w ^ f);
+      }
+    }
+    fence_proxy_async();
+    __syncwarp();
+    if (lane == 0) {
+      mbar_arrive(&mma_full[mslot]);
+      if (j == kbr - 1 || g == kblocks - 1) mbar_arrive(&raw_empty[rslot]);
+    }
+    return true;
+  };
+
+  // ---- before the dependency wait: weights only ----
+  const int G_pre = DIRECT ? 0 : min(MS, kblocks);
+  int issued = 0;
+  if (warp == 0 && lane == 0) {
+    for (int r = 0; r < total_raw; ++r) {
+      if (r >= RS) {
+        const int last = min((r - RS + 1) * kbr, kblocks) - 1;
+        if (DIRECT || last >= G_pre) break;
+        if (!wait_phase(&raw_empty[r % RS], (uint32_t)((r / RS) - 1) & 1u)) {
+          *abort_flag = 1;
+          break;
+        }
+      }
+      issue(r);
+      issued = r + 1;
+    }
+  }
+  int g_exp = 0;
+  bool exp_ok = true;
+  if (!DIRECT && warp >= kThreads / 32 - kExpWarps) {
+    while (exp_ok && g_exp < G_pre) exp_ok = expand(g_exp++);
+    if (!exp_ok) *abort_flag = 1;
+  }
+  gqd::griddep_launch_dependents();
+  gqd::griddep_wait();  // the limbs come from the pre-pass
+
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(gqd::smem_u32(tmem_slot)),
+                 "r"(a.tmem_cols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---- TMA producer: limb tiles and weight refills, in K-block order ----
+    if (lane == 0) {
+      int xi = 0;
+      for (int g = 0; g < kblocks && !*abort_flag; ++g) {
+        if (g % kbr == 0 && g / kbr >= issued) {
+          const int r = g / kbr;
+          if (!wait_phase(&raw_empty[r % RS], (uint32_t)((r / RS) - 1) & 1u)) {
+            *abort_flag = 1;
+            break;
+          }
+          issue(r);
+          issued = r + 1;
+        }
+        int ord;
+        const int own = x_owner(g, ord);
+        const int xslot = own * XI + ord % XI;
+        if (ord >= XI && !wait_phase(&xa_empty[xslot], (uint32_t)((ord / XI) - 1) & 1u)) {
+          *abort_flag = 1;
+          break;
+        }
+        issue_x(xslot, g);
+        xi = g + 1;
+      }
+      if (*abort_flag) {
+        // bounded drain of the copies still in flight before shared memory is released
+        for (int r = issued > RS ? issued - RS : 0; r < issued; ++r)
+          (void)gqd::mbar_wait_bounded(&raw_full[r % RS], (uint32_t)(r / RS) & 1u, 100000000ull);
+        for (int g = 0; g < xi; ++g) {
+          int ord;
+          const int own = x_owner(g, ord);
+          (void)gqd::mbar_wait_bounded(&xa_full[own * XI + ord % XI], (uint32_t)(ord / XI) & 1u, 100000000ull);
+        }
+      }
+    }
+  } else if (warp <= kMaxIss) {
+    // ---- MMA issue: K-blocks dealt round-robin to the issuers ----
+    const int iss = warp - 1;
+    if (lane == 0 && iss < NI) {
+      const uint32_t dcol = tmem + (uint32_t)(iss * NW * a.tile_rows);
+      bool ok = true, first = true;
+      int ord = 0;  // K-blocks this issuer has consumed (its limb-ring position)
+      // Work units dealt round-robin: whole raw stages for I8 (each stage is then
+      // consumed, and released, by one issuer), single K-blocks otherwise.
+      const int units = DIRECT ? total_raw : kblocks;
+      for (int u = iss; u < units && ok; u += NI) {
+        const int g0 = DIRECT ? u * kbr : u;
+        const int ng = DIRECT ? min(kbr, kblocks - g0) : 1;
+        int slot;
+        if (DIRECT) {
+          slot = u % RS;
+          ok = !*abort_flag && wait_phase(&raw_full[slot], (uint32_t)(u / RS) & 1u);
+        } else {
+          slot = u % MS;
+          ok = !*abort_flag && wait_phase(&mma_full[slot], (uint32_t)(u / MS) & 1u);
+        }
+        for (int j = 0; j < ng && ok; ++j) {
+          const int xslot = iss * XI + ord % XI;
+          ok = wait_phase(&xa_full[xslot], (uint32_t)(ord / XI) & 1u);
+          ++ord;
+          if (!ok) break;
+          tc_fence_after();
+          const uint32_t bbase = DIRECT ? gqd::smem_u32(raw + slot * a.raw_bytes + j * NW * tile_bytes)
+                                        : gqd::smem_u32(wid + slot * a.mma_bytes);
+          const uint64_t ad = sw128_desc(gqd::smem_u32(xa + xslot * XA_TILE), 1024);
+#pragma unroll
+          for (int h = 0; h < NW; ++h) {
+            const uint64_t bd = sw128_desc(bbase + h * tile_bytes, 1024);
+            const uint32_t d = dcol + h * a.tile_rows;
+            tc_mma_i8(d, ad, bd, idesc, first ? 0u : 1u);
+            tc_mma_i8(d, ad + 2, bd + 2, idesc, 1u);
+            tc_mma_i8(d, ad + 4, bd + 4, idesc, 1u);
+            tc_mma_i8(d, ad + 6, bd + 6, idesc, 1u);
+          }
+          first = false;
+          tc_commit(&xa_empty[xslot]);
+        }
+        if (!ok) break;
+        tc_commit(DIRECT ? &raw_empty[slot] : &mma_empty[slot]);
+      }
+      if (ok) tc_commit(&acc_full[iss]);
+      if (!ok) *abort_flag = 1;
+      tc_commit(&done_bar[iss]);
+      if (!gqd::mbar_wait_bounded(&done_bar[iss], 0)) *abort_flag = 1;
+    }
+  } else {
+    // ---- warps 4-7: the rest of the widening, then the epilogue ----
+    if (!DIRECT) {
+      bool ok = exp_ok && !*abort_flag;
+      for (int g = g_exp; ok && g < kblocks; ++g) ok = expand(g);
+      if (!ok) *abort_flag = 1;
+    }
+    // Warp q reads lane quarter q: lanes 0-15 hold the limb rows 16q .. 16q+15,
+    // i.e. tokens 4q .. 4q+3 (lane = 4 * (token - 4q) + limb).
+    const int quarter = warp & 3;
+    const int tok = 4 * quarter + ((lane >> 2) & 3), limb = lane & 3;
+    const bool lane_ok = lane < 16 && tok < a.M;
+    const int tk = min(tok, a.M - 1);
+    const double pwt = __longlong_as_double((long long)(1023 - a.xexp[tk]) << 52);  // 2^-s
+    const long long zct = ZP * a.sumx[tk];
+    const bool badt = a.bad[tk] != 0;
+    bool ok = !*abort_flag;
+    for (int i = 0; i < NI; ++i) ok = ok && wait_phase(&acc_full[i], 0u);
+    if (__all_sync(0xffffffffu, ok)) {
+      tc_fence_after();
+      for (int c0 = 0; c0 < a.tile_rows; c0 += 8) {
+        long long T[NW][2];
+#pragma unroll
+        for (int h = 0; h < NW; ++h) {
+          uint32_t d[kMaxIss][8];
+          const uint32_t col = (uint32_t)(h * a.tile_rows + c0) + ((uint32_t)(quarter * 32) << 16);
+#pragma unroll
+          for (int i = 0; i < kMaxIss; ++i)
+            if (i < NI) tmem_ld8_nowait(tmem + col + (uint32_t)(i * NW * a.tile_rows), d[i]);
+          int32_t dsum[8];
+#pragma unroll
+          for (int c = 0; c < 8; ++c) dsum[c] = 0;
+#pragma unroll
+          for (int i = 0; i < kMaxIss; ++i)
+            if (i < NI) {
+              tmem_wait_ld8(d[i]);
+#pragma unroll
+              for (int c = 0; c < 8; ++c) dsum[c] += (int32_t)d[i][c];
+            }
+          T[h][0] = T[h][1] = 0;
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            long long v = (long long)dsum[c] << (8 * limb);
+            v += __shfl_xor_sync(0xffffffffu, v, 1);
+            v += __shfl_xor_sync(0xffffffffu, v, 2);
+            if (c == limb) T[h][0] = v;
+            if (c == 4 + limb) T[h][1] = v;
+          }
+        }
+#pragma unroll
+        for (int hr = 0; hr < 2; ++hr) {
+          const int n = n_begin + c0 + 4 * hr + limb;
+          if (!lane_ok || n >= n_end) continue;
+          float o;
+          if (badt) {
+            o = __int_as_float(0x7fc00000);
+          } else {
+            const float v0 = __fmul_rn((float)((double)(T[0][hr] - zct) * pwt), __ldg(a.s + n));
+            if (MODE == 1) {
+              const float v1 = __fmul_rn((float)((double)(T[NW - 1][hr] - zct) * pwt), __ldg(a.s2 + n));
+              o = __fmul_rn(gqd::gelu_tanh(v0), v1);
+            } else if (MODE == 2) {
+              o = __fmul_rn(gqd::gelu_tanh(v0), a.bs[(size_t)tok * a.b_stride + a.b_off + n]);
+            } else if (MODE == 3) {
+              o = a.cap > 0.0f ? __fmul_rn(a.cap, tanhf(__fdiv_rn(v0, a.cap))) : v0;
+            } else {
+              o = v0;
+            }
+          }
+          a.y[(size_t)tok * a.ldy + a.y_col0 + n] = o;
+        }
+      }
+    } else {
+      *abort_flag = 1;
+    }
+    tc_fence_before();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (*abort_flag) {
+    if (tid == 0) gqd::report(a.err, GQ_DEVERR_WAIT_TIMEOUT);
+    __syncthreads();
+  }
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(a.tmem_cols) : "memory");
+  }
+}
+
+}  // namespace
+
+namespace {
+
+template <int BITS, bool SIGNED, int MODE>
+int launch_x(gq_ctx *ctx, const CUtensorMap &m1, const CUtensorMap &m2, const CUtensorMap &mx, const TcxArgs &a,
+             dim3 grid, size_t smem) {
+  auto kern = gemv_tcx_kernel<BITS, SIGNED, MODE>;
+  static bool attr_set[64] = {};
+  const int dev = ctx->device & 63;
+  if (!attr_set[dev]) {
+    GQ_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ctx->smem_optin));
+    attr_set[dev] = true;
+  }
+  GQ_CUDA_TRY(ctx, gq_launch(ctx, kern, grid, dim3(kThreads), smem, m1, m2, mx, a));
+  return GQ_OK;
+}
+
+template <int BITS, bool SIGNED>
+int launch_xm(gq_ctx *ctx, int mode, const CUtensorMap &m1, const CUtensorMap &m2, const CUtensorMap &mx,
+              const TcxArgs &a, dim3 grid, size_t smem) {
+  switch (mode) {
+    case 0: return launch_x<BITS, SIGNED, 0>(ctx, m1, m2, mx, a, grid, smem);
+    case 1: return launch_x<BITS, SIGNED, 1>(ctx, m1, m2, mx, a, grid, smem);
+    case 2: return launch_x<BITS, SIGNED, 2>(ctx, m1, m2, mx, a, grid, smem);
+    default: return launch_x<BITS, SIGNED, 3>(ctx, m1, m2, mx, a, grid, smem);
+  }
+}
+
+struct TcxPlan {
+  int tile_rows, gx, kblocks, kbr, raw_stages, mma_stages, xa_stages, raw_bytes, mma_bytes, issuers, tmem_cols;
+  size_t smem;
+};
+
+// One tile of weight rows per CTA (N / tile_rows CTAs), rings sized to the
+// whole SM's shared memory.
+bool tcx_plan(const gq_ctx *ctx, const gq_qweight *w, int nw, TcxPlan &p) {
+  const bool direct = (w->bits == 8 && w->signed_i8);
+  const int kb_bytes = kKB * w->bits / 8;
+  const int max_tile = 256 / nw;
+  const int64_t rows0 = (w->n + ctx->num_sms - 1) / ctx->num_sms;
+  if (rows0 > max_tile) return false;
+  p.tile_rows = (int)std::max<int64_t>(16, (rows0 + 15) / 16 * 16);
+  p.gx = (int)((w->n + p.tile_rows - 1) / p.tile_rows);
+  p.kblocks = (int)((w->k + kKB - 1) / kKB);
+  const int tile_bytes = p.tile_rows * 128;
+  const size_t budget = ctx->smem_optin - 1024;
+  p.xa_stages = kMaxXa;
+  if (direct) {
+    p.kbr = std::max(1, std::min(p.kblocks, (8192 + nw * tile_bytes - 1) / (nw * tile_bytes)));
+    p.raw_bytes = p.kbr * nw * tile_bytes;
+    p.mma_bytes = 0;
+    p.mma_stages = 0;
+  } else {
+    p.kbr = std::max(1, std::min(p.kblocks, 256 / kb_bytes));
+    p.raw_bytes = (nw * p.tile_rows * p.kbr * kb_bytes + 1023) / 1024 * 1024;
+    p.mma_bytes = nw * tile_bytes;
+    const TcxSmem L0 = tcx_layout(p.xa_stages, 2, p.raw_bytes, 0, p.mma_bytes);
+    const int fit = L0.total <= budget ? (int)((budget - L0.total) / p.mma_bytes) : 0;
+    p.mma_stages = std::min(std::min(kMaxMma, p.kblocks), fit);
+    if (p.mma_stages < 2) return false;
+  }
+  const int total_raw = (p.kblocks + p.kbr - 1) / p.kbr;
+  const TcxSmem L1 = tcx_layout(p.xa_stages, 0, p.raw_bytes, p.mma_stages, p.mma_bytes);
+  const int fit = L1.total <= budget ? (int)((budget - L1.total) / p.raw_bytes) : 0;
+  p.raw_stages = std::min(std::min(kMaxRaw, total_raw), fit);
+  if (p.raw_stages < std::min(2, total_raw)) return false;
+  const int units = direct ? total_raw : p.kblocks;
+  p.issuers = std::max(1, std::min(std::min(kMaxIss, units), 512 / (nw * p.tile_rows)));
+  // A ring that wraps must hand each slot back to the same issuer (slots are
+  // consumed round-robin): its depth is then a multiple of the issuer count.
+  if (direct && p.raw_stages < total_raw) {
+    while (p.issuers > 1 && p.raw_stages < p.issuers) --p.issuers;
+    p.raw_stages -= p.raw_stages % p.issuers;
+  }
+  if (!direct && p.mma_stages < p.kblocks) {
+    while (p.issuers > 1 && p.mma_stages < p.issuers) --p.issuers;
+    p.mma_stages -= p.mma_stages % p.issuers;
+  }
+  if (p.xa_stages / p.issuers < 2) return false;
+  const int cols = p.issuers * nw * p.tile_rows;
+  p.tmem_cols = 32;
+  while (p.tmem_cols < cols) p.tmem_cols <<= 1;
+  p.smem = tcx_layout(p.xa_stages, p.raw_stages, p.raw_bytes, p.mma_stages, p.mma_bytes).total;
+  return p.tmem_cols <= 512 && p.smem <= budget;
+}
+
+CUresult encode_w(CUtensorMap *map, const gq_qweight *w, const TcxPlan &p) {
+  const bool direct = (w->bits == 8 && w->signed_i8);
+  cuuint64_t dims[2] = {(cuuint64_t)w->row_bytes, (cuuint64_t)w->n};
+  cuuint64_t strides[1] = {(cuuint64_t)w->row_bytes};
+  cuuint32_t box[2] = {direct ? 128u : (cuuint32_t)(p.kbr * kKB * w->bits / 8), (cuuint32_t)p.tile_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return gq_encode_fn()(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, w->bytes, dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, direct ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+// The limb matrix [4*m, kp] s8; box = 64 rows x one 128-byte K-block, swizzled.
+CUresult encode_limbs(CUtensorMap *map, const uint8_t *limbs, int64_t m, int64_t kp) {
+  cuuint64_t dims[2] = {(cuuint64_t)kp, (cuuint64_t)(4 * m)};
+  cuuint64_t strides[1] = {(cuuint64_t)kp};
+  cuuint32_t box[2] = {128u, 64u};
+  cuuint32_t estr[2] = {1, 1};
+  return gq_encode_fn()(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t *>(limbs), dims, strides, box,
+                        estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+template <int BITS>
+cudaError_t launch_limbs(gq_ctx *ctx, const float *x, int64_t m, int64_t k, int64_t kp, uint8_t *limbs, int *xexp,
+                         long long *sumx, uint32_t *bad) {
+  return gq_launch(ctx, xlimbs_kernel<BITS>, dim3((unsigned)m), dim3(kThreads), 0, x, (int)k, (int)kp, limbs, xexp,
+                   sumx, bad);
+}
+
+// Context workspace shared with the prefill path (stream-ordered growth).
+int xws_get(gq_ctx *ctx, size_t bytes, void **out) {
+  if (ctx->ws_cap < bytes) {
+    if (ctx->ws) cudaFreeAsync(ctx->ws, ctx->stream);
+    ctx->ws = nullptr;
+    ctx->ws_cap = 0;
+    GQ_CUDA_TRY(ctx, cudaMallocAsync(&ctx->ws, bytes, ctx->stream));
+    ctx->ws_cap = bytes;
+  }
+  *out = ctx->ws;
+  return GQ_OK;
+}
+
+}  // namespace
+
+// 3 <= M <= 16 activation rows, one scale per weight row, K a multiple of 16 up
+// to 8192, at most 256 / nw rows per CTA, 16-byte aligned x and packed rows.
+bool gq_gemv_tcx_supported(gq_ctx *ctx, const gq_qweight *w, const float *x, int64_t m, int nw) {
+  if (m < 3 || m > kMaxTok || w->group_size != w->k || w->k <= 0 || w->n <= 0) return false;
+  if (w->k % 16 != 0 || w->k > kMaxK || w->n > (1ll << 30)) return false;
+  if (w->row_bytes % 16 != 0 || (uintptr_t)w->bytes % 16 != 0 || (uintptr_t)x % 16 != 0) return false;
+  if (gq_encode_fn() == nullptr) return false;
+  TcxPlan p;
+  return tcx_plan(ctx, w, nw, p);
+}
+
+int gq_gemv_tcx_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq_qweight *w, const gq_qweight *w2,
+                       const float *bs, int64_t b_stride, int64_t b_off, float cap, float *y, int64_t ldy,
+                       int64_t y_col0) {
+  const int nw = (mode == 1) ? 2 : 1;
+  TcxPlan p;
+  if (!tcx_plan(ctx, w, nw, p)) return gq_fail(ctx, GQ_ERR_UNSUPPORTED, "gemv_tcx: no stage configuration fits");
+  const int64_t kp = (int64_t)p.kblocks * kKB;
+  const size_t limb_bytes = ((size_t)(4 * m * kp) + 255) & ~size_t(255);
+  void *wsp = nullptr;
+  int rc = xws_get(ctx, limb_bytes + (size_t)m * 16 + 256, &wsp);
+  if (rc != GQ_OK) return rc;
+  uint8_t *limbs = static_cast<uint8_t *>(wsp);
+  long long *sumx = reinterpret_cast<long long *>(limbs + limb_bytes);
+  int *xexp = reinterpret_cast<int *>(sumx + m);
+  uint32_t *bad = reinterpret_cast<uint32_t *>(xexp + m);
+  if (w->bits == 4) {
+    GQ_CUDA_TRY(ctx, launch_limbs<4>(ctx, x, m, w->k, kp, limbs, xexp, sumx, bad));
+  } else if (w->bits == 2) {
+    GQ_CUDA_TRY(ctx, launch_limbs<2>(ctx, x, m, w->k, kp, limbs, xexp, sumx, bad));
+  } else {
+    GQ_CUDA_TRY(ctx, launch_limbs<8>(ctx, x, m, w->k, kp, limbs, xexp, sumx, bad));
+  }
+  CUtensorMap m1, m2, mx;
+  if (encode_w(&m1, w, p) != CUDA_SUCCESS || encode_w(&m2, w2 ? w2 : w, p) != CUDA_SUCCESS ||
+      encode_limbs(&mx, limbs, m, kp) != CUDA_SUCCESS)
+    return gq_fail(ctx, GQ_ERR_CUDA, "gemv_tcx: tensor map");
+  TcxArgs a = {};
+  a.M = (int)m;
+  a.K = (int)w->k;
+  a.N = (int)w->n;
+  a.s = w->scales;
+  a.s2 = w2 ? w2->scales : nullptr;
+  a.bs = bs;
+  a.b_stride = b_stride;
+  a.b_off = b_off;
+  a.cap = cap;
+  a.y = y;
+  a.ldy = ldy;
+  a.y_col0 = y_col0;
+  a.xexp = xexp;
+  a.sumx = sumx;
+  a.bad = bad;
+  a.tile_rows = p.tile_rows;
+  a.kblocks = p.kblocks;
+  a.kbr = p.kbr;
+  a.raw_stages = p.raw_stages;
+  a.mma_stages = p.mma_stages;
+  a.xa_stages = p.xa_stages;
+  a.raw_bytes = p.raw_bytes;
+  a.mma_bytes = p.mma_bytes;
+  a.issuers = p.issuers;
+  a.tmem_cols = p.tmem_cols;
+  a.err = ctx->dev_err;
+  const dim3 grid((unsigned)p.gx);
+  if (w->bits == 4) return launch_xm<4, false>(ctx, mode, m1, m2, mx, a, grid, p.smem);
+  if (w->bits == 2) return launch_xm<2, false>(ctx, mode, m1, m2, mx, a, grid, p.smem);
+  if (w->signed_i8) return launch_xm<8, true>(ctx, mode, m1, m2, mx, a, grid, p.smem);
+  return launch_xm<8, false>(ctx, mode, m1, m2, mx, a, grid, p.smem);
+}

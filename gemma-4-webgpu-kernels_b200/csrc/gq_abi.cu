@@ -20,6 +20,11 @@ int gq_gemv_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq_qw
                    const gq_qweight *w2, const float *bs, int64_t b_stride, int64_t b_off,
                    float cap, float *y, int64_t ldy, int64_t y_col0);
 int gq_scalar_linear_launch(gq_ctx *ctx, const float *x, int64_t m, const gq_qweight *w, float *y);
+// gemv_tcx.cu
+bool gq_gemv_tcx_supported(gq_ctx *ctx, const gq_qweight *w, const float *x, int64_t m, int nw);
+int gq_gemv_tcx_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq_qweight *w, const gq_qweight *w2,
+                       const float *bs, int64_t b_stride, int64_t b_off, float cap, float *y, int64_t ldy,
+                       int64_t y_col0);
 // gemv_tc.cu
 bool gq_gemv_tc_supported(gq_ctx *ctx, const gq_qweight *w, const float *x, int64_t m, int nw);
 int gq_gemv_tc_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq_qweight *w, const gq_qweight *w2,
@@ -381,9 +386,17 @@ bool use_prefill(gq_ctx *ctx, const float *x, int64_t m, const gq_qweight *w) {
 bool use_gemv_tc(gq_ctx *ctx, const float *x, int64_t m, const gq_qweight *w, int nw) {
   const char *e = getenv("GQ_DECODE_TC");
   const int mode = (e && *e) ? (*e - '0') : 1;
-  if (mode <= 0) return false;
+  if (mode <= 0 || m > 2) return false;
   if (mode == 1 && (w->n + ctx->num_sms - 1) / ctx->num_sms < 128) return false;
   return gq_gemv_tc_supported(ctx, w, x, m, nw);
+}
+
+// 3 <= M <= 16: the tensor-core GEMV with streamed limbs (weights read once for
+// all rows) unless GQ_DECODE_TC=0.
+bool use_gemv_tcx(gq_ctx *ctx, const float *x, int64_t m, const gq_qweight *w, int nw) {
+  const char *e = getenv("GQ_DECODE_TC");
+  const int mode = (e && *e) ? (*e - '0') : 1;
+  return mode > 0 && gq_gemv_tcx_supported(ctx, w, x, m, nw);
 }
 
 }  // namespace
@@ -396,6 +409,7 @@ int gq_linear(gq_ctx *ctx, const float *x, int64_t m, int64_t k, const gq_qweigh
   if (rc != GQ_OK || m == 0 || w->n == 0) return rc;
   if (use_prefill(ctx, x, m, w)) return gq_prefill_launch(ctx, 0, x, m, w, nullptr, nullptr, 0, 0, 0.0f, y, w->n, 0);
   if (use_gemv_tc(ctx, x, m, w, 1)) return gq_gemv_tc_launch(ctx, 0, x, m, w, nullptr, nullptr, 0, 0, 0.0f, y, w->n, 0);
+  if (use_gemv_tcx(ctx, x, m, w, 1)) return gq_gemv_tcx_launch(ctx, 0, x, m, w, nullptr, nullptr, 0, 0, 0.0f, y, w->n, 0);
   if (gq_gemv_supported(ctx, w, m, 1))
     return gq_gemv_launch(ctx, 0, x, m, w, nullptr, nullptr, 0, 0, 0.0f, y, w->n, 0);
   return gq_scalar_linear_launch(ctx, x, m, w, y);
@@ -415,6 +429,8 @@ int gq_linear_geglu(gq_ctx *ctx, const float *x, int64_t m, int64_t k, const gq_
     return gq_prefill_launch(ctx, 1, x, m, wg, wu, nullptr, 0, 0, 0.0f, y, wg->n, 0);
   if (same && use_gemv_tc(ctx, x, m, wg, 2))
     return gq_gemv_tc_launch(ctx, 1, x, m, wg, wu, nullptr, 0, 0, 0.0f, y, wg->n, 0);
+  if (same && use_gemv_tcx(ctx, x, m, wg, 2))
+    return gq_gemv_tcx_launch(ctx, 1, x, m, wg, wu, nullptr, 0, 0, 0.0f, y, wg->n, 0);
   if (same && gq_gemv_supported(ctx, wg, m, 2))
     return gq_gemv_launch(ctx, 1, x, m, wg, wu, nullptr, 0, 0, 0.0f, y, wg->n, 0);
   // composition of rust/src/backend.rs:156-160
@@ -440,6 +456,8 @@ int gq_linear_gelu_mul_cols(gq_ctx *ctx, const float *x, int64_t m, int64_t k, c
     return gq_prefill_launch(ctx, 2, x, m, w, nullptr, b, b_stride, b_offset, 0.0f, y, w->n, 0);
   if (use_gemv_tc(ctx, x, m, w, 1))
     return gq_gemv_tc_launch(ctx, 2, x, m, w, nullptr, b, b_stride, b_offset, 0.0f, y, w->n, 0);
+  if (use_gemv_tcx(ctx, x, m, w, 1))
+    return gq_gemv_tcx_launch(ctx, 2, x, m, w, nullptr, b, b_stride, b_offset, 0.0f, y, w->n, 0);
   if (gq_gemv_supported(ctx, w, m, 1))
     return gq_gemv_launch(ctx, 2, x, m, w, nullptr, b, b_stride, b_offset, 0.0f, y, w->n, 0);
   // composition of rust/src/backend.rs:163-167
@@ -460,6 +478,8 @@ int gq_linear_softcap(gq_ctx *ctx, const float *x, int64_t m, int64_t k, const g
   if (m == 0 || w->n == 0) return GQ_OK;
   if (use_prefill(ctx, x, m, w)) return gq_prefill_launch(ctx, 3, x, m, w, nullptr, nullptr, 0, 0, cap, y, ldy, y_col0);
   if (use_gemv_tc(ctx, x, m, w, 1)) return gq_gemv_tc_launch(ctx, 3, x, m, w, nullptr, nullptr, 0, 0, cap, y, ldy, y_col0);
+  if (use_gemv_tcx(ctx, x, m, w, 1))
+    return gq_gemv_tcx_launch(ctx, 3, x, m, w, nullptr, nullptr, 0, 0, cap, y, ldy, y_col0);
   if (gq_gemv_supported(ctx, w, m, 1))
     return gq_gemv_launch(ctx, 3, x, m, w, nullptr, nullptr, 0, 0, cap, y, ldy, y_col0);
   // composition: generic linear into scratch, then soft-cap into the strided output

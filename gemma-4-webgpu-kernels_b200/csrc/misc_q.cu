@@ -3,6 +3,8 @@
 #include <cuda_runtime.h>
 #include <math.h>
 
+#include <type_traits>
+
 #include "gq_internal.cuh"
 
 namespace {
@@ -138,32 +140,43 @@ __global__ void embed_row_kernel(QView q, const uint32_t *ids, int64_t t, float 
   const uint8_t *rp = q.bytes + (int64_t)id * q.row_bytes;
   const float *sr = q.scales + (int64_t)id * q.scale_stride;
   const int gshift = (q.group == q.k) ? 31 : (31 - __clz((int)q.group));  // group is a power of two here
-  for (int j = lane; j < steps; j += 32) {
-    int32_t c[16];
-    if constexpr (BITS == 8) {
-      const uint4 w = __ldg(reinterpret_cast<const uint4 *>(rp) + j);
-      const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+  using L = typename std::conditional<BITS == 8, uint4, typename std::conditional<BITS == 4, uint2, uint32_t>::type>::type;
+  const L *src = reinterpret_cast<const L *>(rp);
+  constexpr int U = 4;  // steps per lane in flight: all loads first, then the stores
+  for (int j0 = lane; j0 < steps; j0 += 32 * U) {
+    L w[U];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const uint32_t b = (ws[i >> 2] >> (8 * (i & 3))) & 0xffu;
-        c[i] = SIGNED ? (int32_t)(int8_t)b : (int32_t)b - 128;
-      }
-    } else if constexpr (BITS == 4) {
-      const uint2 w = __ldg(reinterpret_cast<const uint2 *>(rp) + j);
-#pragma unroll
-      for (int i = 0; i < 16; ++i) c[i] = (int32_t)(((i < 8 ? w.x : w.y) >> (4 * (i & 7))) & 0xfu) - 8;
-    } else {
-      const uint32_t w = __ldg(reinterpret_cast<const uint32_t *>(rp) + j);
-#pragma unroll
-      for (int i = 0; i < 16; ++i) c[i] = (int32_t)((w >> (2 * i)) & 0x3u) - 2;
+    for (int u = 0; u < U; ++u) {
+      const int j = j0 + 32 * u;
+      if (j < steps) w[u] = __ldg(src + j);
     }
-    const float sc = __ldg(sr + (gshift == 31 ? 0 : ((16 * j) >> gshift)));
 #pragma unroll
-    for (int u = 0; u < 4; ++u)
-      orow[4 * j + u] = make_float4(__fmul_rn(__fmul_rn((float)c[4 * u], sc), emb),
-                                    __fmul_rn(__fmul_rn((float)c[4 * u + 1], sc), emb),
-                                    __fmul_rn(__fmul_rn((float)c[4 * u + 2], sc), emb),
-                                    __fmul_rn(__fmul_rn((float)c[4 * u + 3], sc), emb));
+    for (int u = 0; u < U; ++u) {
+      const int j = j0 + 32 * u;
+      if (j >= steps) break;
+      int32_t c[16];
+      if constexpr (BITS == 8) {
+        const uint32_t ws[4] = {w[u].x, w[u].y, w[u].z, w[u].w};
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const uint32_t b = (ws[i >> 2] >> (8 * (i & 3))) & 0xffu;
+          c[i] = SIGNED ? (int32_t)(int8_t)b : (int32_t)b - 128;
+        }
+      } else if constexpr (BITS == 4) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) c[i] = (int32_t)(((i < 8 ? w[u].x : w[u].y) >> (4 * (i & 7))) & 0xfu) - 8;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) c[i] = (int32_t)((w[u] >> (2 * i)) & 0x3u) - 2;
+      }
+      const float sc = __ldg(sr + (gshift == 31 ? 0 : ((16 * j) >> gshift)));
+#pragma unroll
+      for (int v = 0; v < 4; ++v)
+        orow[4 * j + v] = make_float4(__fmul_rn(__fmul_rn((float)c[4 * v], sc), emb),
+                                      __fmul_rn(__fmul_rn((float)c[4 * v + 1], sc), emb),
+                                      __fmul_rn(__fmul_rn((float)c[4 * v + 2], sc), emb),
+                                      __fmul_rn(__fmul_rn((float)c[4 * v + 3], sc), emb));
+    }
   }
 }
 

@@ -1,7 +1,8 @@
 """Both decode GEMVs against the CPU oracle (needs a B200).
 
-Decode rows (M <= 2) have two CUDA implementations: the CUDA-core GEMV and the
-tensor-core one (exact integer dot products on tcgen05.mma.kind::i8). The
+Decode rows (M <= 16) have two CUDA implementations: the CUDA-core GEMV and the
+tensor-core ones (exact integer dot products on tcgen05.mma.kind::i8; x staged
+in the CTA for M <= 2, streamed as a limb matrix for 3 <= M <= 16). The
 library picks one per shape; GQ_DECODE_TC forces the choice (0 = CUDA cores,
 2 = tensor cores wherever they apply), so every shape family here runs through
 both, at the FFMA-path bound (relative L2 <= 1e-5 against the oracle).
@@ -42,7 +43,7 @@ SHAPES = [(2048, 1536, 8, True), (256, 1536, 8, True), (1536, 2048, 8, True), (6
 
 @pytest.mark.parametrize("path", PATHS)
 @pytest.mark.parametrize("n,k,bits,signed", SHAPES)
-@pytest.mark.parametrize("m", [1, 2])
+@pytest.mark.parametrize("m", [1, 2, 3, 8, 16])
 def test_linear_both_paths(g, monkeypatch, path, n, k, bits, signed, m):
     monkeypatch.setenv("GQ_DECODE_TC", path)
     w = synth.random_qweight(3000 + n + k + bits, n, k, bits, signed)
@@ -52,7 +53,7 @@ def test_linear_both_paths(g, monkeypatch, path, n, k, bits, signed, m):
 
 
 @pytest.mark.parametrize("path", PATHS)
-@pytest.mark.parametrize("m", [1, 2])
+@pytest.mark.parametrize("m", [1, 2, 8])
 def test_geglu_both_paths(g, monkeypatch, path, m):
     monkeypatch.setenv("GQ_DECODE_TC", path)
     n, k = 6144, 1536
@@ -64,9 +65,10 @@ def test_geglu_both_paths(g, monkeypatch, path, m):
 
 
 @pytest.mark.parametrize("path", PATHS)
-def test_gelu_mul_cols_both_paths(g, monkeypatch, path):
+@pytest.mark.parametrize("m", [2, 5])
+def test_gelu_mul_cols_both_paths(g, monkeypatch, path, m):
     monkeypatch.setenv("GQ_DECODE_TC", path)
-    n, k, m, off = 256, 1536, 2, 512
+    n, k, off = 256, 1536, 512
     w = synth.random_qweight(3201, n, k, 8, True)
     x = synth.normal(3202, m * k).reshape(m, k)
     b = synth.normal(3203, m * 8960).reshape(m, 8960)
@@ -80,10 +82,10 @@ def test_softcap_slice_both_paths(g, monkeypatch, path):
     monkeypatch.setenv("GQ_DECODE_TC", path)
     n, k, cap = 32768, 1536, 30.0
     w = synth.random_qweight(3301, n, k, 8, True)
-    x = synth.normal(3302, k).reshape(1, k) * 4.0
-    out = g.zeros((1, 3 * n))
+    x = synth.normal(3302, 4 * k).reshape(4, k) * 4.0
+    out = g.zeros((4, 3 * n))
     g.linear_softcap(g.tensor(x, x.shape), g.quant_tensor(w), cap, out=out, col0=n)
-    got = g.readback(out).reshape(1, 3 * n)
+    got = g.readback(out).reshape(4, 3 * n)
     ref = oracle.softcap(oracle.linear(x, w), cap)
     assert rel_l2(got[:, n:2 * n], ref) <= REL_L2
     assert not np.any(got[:, :n]) and not np.any(got[:, 2 * n:])
@@ -95,7 +97,7 @@ def test_extreme_activations_both_paths(g, monkeypatch, path):
     monkeypatch.setenv("GQ_DECODE_TC", path)
     n, k = 1024, 1536
     w = synth.make_qweight(3401, n, k, 4)
-    base = synth.normal(3402, 2 * k).reshape(2, k)
+    base = synth.normal(3402, 6 * k).reshape(6, k)
     for label, x in [("tiny", base * 1e-30), ("huge", base * 1e25), ("mean", base + 5.0)]:
         x = x.astype(np.float32)
         got = g.readback(g.linear(g.tensor(x, x.shape), g.quant_tensor(w)))
