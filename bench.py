@@ -413,6 +413,7 @@ def run_gq(args):
         line["lm_head_sharded"] = sharded_lm_head(torch, dist, rank, world, local, args)
     if rank == 0 and world == 1 and not args.no_extras:
         line["extras"] = extras(g, torch, stream, hbm_peak, bf16_peak)
+        line["config5_decode"] = config5(g, torch, stream, hbm_peak)
     if rank == 0 and world == 1:
         line["cpu_baseline"] = cpu_sample(step, min_seconds=10.0)
     g.destroy_graph(graph)
@@ -590,6 +591,40 @@ def extras(g, torch, stream, hbm_peak, bf16_peak):
     g.free_quant(t_tok)
     g.free_quant(t_ple)
     g.flush()
+    return out
+
+
+def config5(g, torch, stream, hbm_peak, batches=(1, 64), steps=50):
+    """the full synthetic E2B decode step (35 layers, MQA
+    attention over a 2048-token KV cache, PLE, lm_head + soft-cap) at the given
+    batches, one CUDA graph per step, weights and caches random-initialised on the
+    device. Bytes counted: packed weights + scales once, the KV rows attention
+    reads, the gathered embedding rows."""
+    from gq import e2b
+
+    cfg = e2b.e2b_config()
+    out = {}
+    for b in batches:
+        dec = e2b.Decoder(g, cfg, None, batch=b, cache_len=2047, capacity=2048, device_init_seed=77 + b)
+        dec.set_ids(np.arange(b) * 4099 % cfg.vocab)
+        dec.run()
+        g.flush()
+        graph = dec.record()
+        for _ in range(5):
+            g.replay(graph)
+        g.flush()
+        ms = cuda_events_time(torch, stream, lambda: g.replay(graph), steps) / steps
+        nbytes = dec.weight_bytes() + dec.kv_bytes() + dec.gather_bytes()
+        out[f"batch{b}"] = {"ms_per_step": round(ms, 4), "tokens_per_s": round(b / (ms / 1e3), 1),
+                            "GB/s": round(nbytes / (ms / 1e3) / 1e9, 1),
+                            "frac_of_measured_hbm": round(nbytes / (ms / 1e3) / 1e9 / hbm_peak, 4),
+                            "bytes_per_step": nbytes, "launches_per_step": dec.launches}
+        g.destroy_graph(graph)
+        dec.close()
+        del dec
+        torch.cuda.empty_cache()
+    out["config"] = "E2B shapes, KV length 2048 (new token at position 2047), f32 KV cache, I8 attention/PLE/lm_head, " \
+                    "4-bit gate/up, 2-bit down, bf16 per-layer model projection; graph-replayed"
     return out
 
 

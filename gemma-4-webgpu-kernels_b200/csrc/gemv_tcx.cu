@@ -652,18 +652,6 @@ cudaError_t launch_limbs(gq_ctx *ctx, const float *x, int64_t m, int64_t k, int6
                    sumx, bad);
 }
 
-// Context workspace shared with the prefill path (stream-ordered growth).
-int xws_get(gq_ctx *ctx, size_t bytes, void **out) {
-  if (ctx->ws_cap < bytes) {
-    if (ctx->ws) cudaFreeAsync(ctx->ws, ctx->stream);
-    ctx->ws = nullptr;
-    ctx->ws_cap = 0;
-    GQ_CUDA_TRY(ctx, cudaMallocAsync(&ctx->ws, bytes, ctx->stream));
-    ctx->ws_cap = bytes;
-  }
-  *out = ctx->ws;
-  return GQ_OK;
-}
 
 }  // namespace
 
@@ -687,7 +675,7 @@ int gq_gemv_tcx_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const g
   const int64_t kp = (int64_t)p.kblocks * kKB;
   const size_t limb_bytes = ((size_t)(4 * m * kp) + 255) & ~size_t(255);
   void *wsp = nullptr;
-  int rc = xws_get(ctx, limb_bytes + (size_t)m * 16 + 256, &wsp);
+  int rc = gq_workspace(ctx, limb_bytes + (size_t)m * 16 + 256, &wsp);
   if (rc != GQ_OK) return rc;
   uint8_t *limbs = static_cast<uint8_t *>(wsp);
   long long *sumx = reinterpret_cast<long long *>(limbs + limb_bytes);

@@ -51,16 +51,34 @@ int gq_cuda_fail(gq_ctx *ctx, cudaError_t e, const char *what) {
   return gq_fail(ctx, e == cudaErrorMemoryAllocation ? GQ_ERR_OUT_OF_MEMORY : GQ_ERR_CUDA, msg);
 }
 
-namespace {
-
-// Make the context's device current for this host thread.
-int enter(gq_ctx *ctx) {
+int gq_enter_ctx(gq_ctx *ctx) {
   int cur = -1;
   if (cudaGetDevice(&cur) != cudaSuccess || cur != ctx->device) {
     GQ_CUDA_TRY(ctx, cudaSetDevice(ctx->device));
   }
   return GQ_OK;
 }
+
+int gq_workspace(gq_ctx *ctx, size_t bytes, void **out) {
+  if (ctx->ws_cap < bytes) {
+    cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+    GQ_CUDA_TRY(ctx, cudaStreamIsCapturing(ctx->stream, &st));
+    if (st != cudaStreamCaptureStatusNone)
+      return gq_fail(ctx, GQ_ERR_INVALID_ARGUMENT,
+                     "workspace must grow while the stream is being captured: run the call once before recording");
+    if (ctx->ws) cudaFreeAsync(ctx->ws, ctx->stream);
+    ctx->ws = nullptr;
+    ctx->ws_cap = 0;
+    GQ_CUDA_TRY(ctx, cudaMallocAsync(&ctx->ws, bytes, ctx->stream));
+    ctx->ws_cap = bytes;
+  }
+  *out = ctx->ws;
+  return GQ_OK;
+}
+
+namespace {
+
+int enter(gq_ctx *ctx) { return gq_enter_ctx(ctx); }
 
 #define GQ_ENTER(ctx)                                                            \
   do {                                                                           \

@@ -44,6 +44,12 @@ struct gq_qweight {
 
 // ---- status helpers (host) ------------------------------------------------
 int gq_fail(gq_ctx *ctx, int status, const std::string &msg);
+// Make the context's device current for the calling host thread.
+int gq_enter_ctx(gq_ctx *ctx);
+// The context workspace, grown on demand with stream-ordered allocation. Growth
+// is refused while the stream is being captured (the allocation would belong to
+// the graph): run a call once eagerly before recording it.
+int gq_workspace(gq_ctx *ctx, size_t bytes, void **out);
 int gq_cuda_fail(gq_ctx *ctx, cudaError_t e, const char *what);
 #define GQ_CUDA_TRY(ctx, expr)                                   \
   do {                                                           \

@@ -580,19 +580,6 @@ bool gq_prefill_supported(gq_ctx *ctx, const gq_qweight *w, int64_t m) {
   return smem_for(w->bits) <= ctx->smem_optin && encode_fn() != nullptr;
 }
 
-// Workspace for the f16 copy of x and the per-row exponents (grown on demand,
-// stream-ordered).
-static int ws_get(gq_ctx *ctx, size_t bytes, void **out) {
-  if (ctx->ws_cap < bytes) {
-    if (ctx->ws) cudaFreeAsync(ctx->ws, ctx->stream);
-    ctx->ws = nullptr;
-    ctx->ws_cap = 0;
-    GQ_CUDA_TRY(ctx, cudaMallocAsync(&ctx->ws, bytes, ctx->stream));
-    ctx->ws_cap = bytes;
-  }
-  *out = ctx->ws;
-  return GQ_OK;
-}
 
 int gq_prefill_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq_qweight *w, const gq_qweight *w2,
                       const float *bs, int64_t b_stride, int64_t b_off, float cap, float *y, int64_t ldy,
@@ -600,7 +587,7 @@ int gq_prefill_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq
   const int64_t K = w->k;
   const size_t xh_bytes = ((size_t)(m * K) * 2 + 255) & ~size_t(255);
   void *wsp = nullptr;
-  int rc = ws_get(ctx, xh_bytes + (size_t)m * sizeof(int), &wsp);
+  int rc = gq_workspace(ctx, xh_bytes + (size_t)m * sizeof(int), &wsp);
   if (rc != GQ_OK) return rc;
   __half *xh = static_cast<__half *>(wsp);
   int *xexp = reinterpret_cast<int *>(static_cast<uint8_t *>(wsp) + xh_bytes);

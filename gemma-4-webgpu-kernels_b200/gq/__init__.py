@@ -12,6 +12,10 @@ names, argument meaning and error behaviour follow the trait:
 * ``softcap(a, cap)`` / ``geglu(gate, up)``            rust/src/backend.rs:113-116
 * ``tensor`` / ``zeros`` / ``reshape`` / ``readback`` / ``flush`` /
   ``begin_frame`` / ``end_frame`` / ``free_tensor``    rust/src/backend.rs:94-98, 169-179
+* support ops of a decode step: ``rms_norm``, ``add``, ``mul``, ``scale``,
+  ``scale_by_tensor``, ``rope``, ``attention``, ``slice_rows``, ``slice_cols``,
+  ``concat_rows``, ``kv_append`` (rust/src/backend.rs:103-130), ``add_rms_norm``,
+  ``head_norm_rope`` (:137-154), and ``linear`` with a bf16-stored plain weight
 
 Ops enqueue on the backend's stream (torch's current stream of the device) and
 return immediately; ``readback`` blocks, like the reference. Failures raise
@@ -30,7 +34,7 @@ import numpy as np
 from . import _abi
 from ._abi import GqError
 
-__all__ = ["QuantWeight", "GqTensor", "CudaBackend", "GqError"]
+__all__ = ["QuantWeight", "GqTensor", "CudaBackend", "GqError", "AttnOpts", "KvAppend"]
 
 
 @dataclass
@@ -72,18 +76,41 @@ class QuantWeight:
 
 @dataclass
 class GqTensor:
-    """A backend tensor: dense row-major f32 on the device, or a quantized weight."""
+    """A backend tensor: dense row-major f32 on the device, a quantized weight, or a
+    plain weight stored as bf16 (``bf16=True``: ``data`` is a cuda int16 tensor of
+    the bf16 bit patterns)."""
 
     shape: tuple
     data: object = None          # torch.Tensor (cuda, float32, contiguous) for f32 tensors
     qw: Optional[int] = None     # gq_qweight* for quantized tensors
     quant: Optional[QuantWeight] = field(default=None, repr=False)
+    bf16: bool = False
 
     def size(self) -> int:
         return int(np.prod(self.shape)) if self.shape else 1
 
     def ptr(self) -> int:
         return self.data.data_ptr()
+
+
+@dataclass
+class AttnOpts:
+    """rust/src/backend.rs:59-69: query / key positions, score scale, sliding
+    window (0 = none) and attention soft-cap (0 = none)."""
+
+    q_pos: Sequence[int]
+    k_pos: Sequence[int]
+    scale: float = 1.0
+    sliding_window: int = 0
+    attn_softcap: float = 0.0
+
+
+@dataclass
+class KvAppend:
+    """rust/src/backend.rs:71-77: the grown tensor and the one it superseded."""
+
+    tensor: GqTensor
+    dead: Optional[GqTensor] = None
 
 
 class CudaBackend:
@@ -301,6 +328,146 @@ class CudaBackend:
         self._check(self.lib.gq_geglu(self.ctx, c_void_p(gate.ptr()), c_void_p(up.ptr()), gate.size(),
                                       c_void_p(y.ptr())), "geglu")
         return y
+
+    # ---- support ops of a decode step (rust/src/backend.rs:103-154) ------------
+    def _u32_dev(self, vals):
+        if isinstance(vals, self._torch.Tensor) and vals.is_cuda:
+            t = vals.to(self._torch.int32).contiguous()
+        else:
+            arr = np.ascontiguousarray(np.asarray(vals, dtype=np.uint32))
+            t = self._torch.from_numpy(arr.view(np.int32)).to(self.torch_device)
+        self._frame.append(GqTensor(shape=(t.numel(),), data=t))  # alive until the frame ends
+        return t
+
+    def tensor_bf16(self, data, shape: Sequence[int]) -> GqTensor:
+        """A plain weight stored as bf16 (round to nearest even; exact for values that
+        are bf16 on disk, like the reference's BF16 checkpoint tensors)."""
+        arr = np.ascontiguousarray(np.asarray(data, dtype=np.float32).reshape(tuple(shape)))
+        u = arr.view(np.uint32)
+        rounded = ((u + np.uint32(0x7FFF) + ((u >> np.uint32(16)) & np.uint32(1))) >> np.uint32(16)).astype(np.uint16)
+        t = self._torch.from_numpy(rounded.view(np.int16)).to(self.torch_device)
+        return GqTensor(shape=tuple(shape), data=t, bf16=True)
+
+    def rms_norm(self, x: GqTensor, w: Optional[GqTensor], eps: float) -> GqTensor:
+        """y = x / sqrt(mean(x²) + eps) * w per row (rust/src/backend.rs:103-104)."""
+        d = x.shape[-1]
+        y = self._alloc(x.shape)
+        self._check(self.lib.gq_rms_norm(self.ctx, c_void_p(x.ptr()), x.size() // d, d,
+                                         c_void_p(w.ptr()) if w is not None else None, float(eps),
+                                         c_void_p(y.ptr()), d), "rms_norm")
+        return y
+
+    def add_rms_norm(self, residual: GqTensor, x: GqTensor, w: GqTensor, eps: float,
+                     scale_by: Optional[GqTensor] = None) -> GqTensor:
+        """(residual + rms_norm(x, w)) * scale_by[0] (rust/src/backend.rs:137-144)."""
+        d = x.shape[-1]
+        y = self._alloc(x.shape)
+        self._check(self.lib.gq_add_rms_norm(self.ctx, c_void_p(residual.ptr()), c_void_p(x.ptr()), x.size() // d,
+                                             d, c_void_p(w.ptr()), float(eps),
+                                             c_void_p(scale_by.ptr()) if scale_by is not None else None,
+                                             c_void_p(y.ptr())), "add_rms_norm")
+        return y
+
+    def head_norm_rope(self, x: GqTensor, w: GqTensor, eps: float, positions, theta: float, head_dim: int,
+                       heads: int, rotary_dim: int) -> GqTensor:
+        """Per-head weighted RMSNorm then partial RoPE (rust/src/backend.rs:148-154)."""
+        pos = self._u32_dev(positions)
+        t = x.size() // (heads * head_dim)
+        y = self._alloc(x.shape)
+        self._check(self.lib.gq_head_norm_rope(self.ctx, c_void_p(x.ptr()), t, heads, head_dim, c_void_p(w.ptr()),
+                                               float(eps), c_void_p(pos.data_ptr()), float(theta), rotary_dim,
+                                               c_void_p(y.ptr()), 0), "head_norm_rope")
+        return y
+
+    def rope(self, x: GqTensor, positions, theta: float, head_dim: int, heads: int, rotary_dim: int) -> GqTensor:
+        """Half-split partial RoPE on [T, heads, head_dim] (rust/src/backend.rs:118-119)."""
+        pos = self._u32_dev(positions)
+        t = x.size() // (heads * head_dim)
+        y = self._alloc(x.shape)
+        self._check(self.lib.gq_rope(self.ctx, c_void_p(x.ptr()), t, heads, head_dim, c_void_p(pos.data_ptr()),
+                                     float(theta), rotary_dim, c_void_p(y.ptr()), 0), "rope")
+        return y
+
+    def attention(self, q: GqTensor, k: GqTensor, v: GqTensor, opts: AttnOpts) -> GqTensor:
+        """q [T, Hq, Dh], k/v [S, Hkv, Dh] -> [T, Hq*Dh] (rust/src/backend.rs:120-121)."""
+        t, hq, dh = q.shape
+        s, hkv = k.shape[0], k.shape[1]
+        if v.shape[-1] != dh or k.shape[-1] != dh:
+            raise GqError(_abi.GQ_ERR_UNSUPPORTED, "attention: value head_dim must equal key head_dim")
+        qp, kp = self._u32_dev(opts.q_pos), self._u32_dev(opts.k_pos)
+        kpos = np.asarray(opts.k_pos, dtype=np.int64)
+        flags = _abi.GQ_ATTN_KPOS_ASCENDING if (kpos.size < 2 or bool(np.all(np.diff(kpos) > 0))) else 0
+        y = self._alloc((t, hq * dh))
+        self._check(self.lib.gq_attention(self.ctx, c_void_p(q.ptr()), 1, t, hq, dh, c_void_p(k.ptr()),
+                                          c_void_p(v.ptr()), s, hkv, 0, c_void_p(qp.data_ptr()),
+                                          c_void_p(kp.data_ptr()), 0, float(opts.scale), int(opts.sliding_window),
+                                          float(opts.attn_softcap), flags, c_void_p(y.ptr())), "attention")
+        return y
+
+    def linear_plain(self, x: GqTensor, w: GqTensor) -> GqTensor:
+        """linear with a plain (bf16-stored) weight [N, K] (rust/src/backend_cpu.rs:174-222)."""
+        if not w.bf16:
+            raise GqError(_abi.GQ_ERR_INVALID_ARGUMENT, "linear_plain: weight must come from tensor_bf16")
+        m, k = self._xm(x)
+        n = w.shape[0]
+        y = self._alloc((m, n))
+        self._check(self.lib.gq_linear_bf16(self.ctx, c_void_p(x.ptr()), m, k, c_void_p(w.ptr()), n,
+                                            c_void_p(y.ptr())), "linear_bf16")
+        return y
+
+    def _ew(self, fn, *args, shape, what):
+        y = self._alloc(shape)
+        self._check(fn(self.ctx, *args, c_void_p(y.ptr())), what)
+        return y
+
+    def add(self, a: GqTensor, b: GqTensor) -> GqTensor:
+        return self._ew(self.lib.gq_add, c_void_p(a.ptr()), c_void_p(b.ptr()), a.size(), shape=a.shape, what="add")
+
+    def mul(self, a: GqTensor, b: GqTensor) -> GqTensor:
+        return self._ew(self.lib.gq_mul, c_void_p(a.ptr()), c_void_p(b.ptr()), a.size(), shape=a.shape, what="mul")
+
+    def scale(self, a: GqTensor, s: float) -> GqTensor:
+        return self._ew(self.lib.gq_scale, c_void_p(a.ptr()), a.size(), float(s), shape=a.shape, what="scale")
+
+    def scale_by_tensor(self, a: GqTensor, s: GqTensor) -> GqTensor:
+        return self._ew(self.lib.gq_scale_by_tensor, c_void_p(a.ptr()), a.size(), c_void_p(s.ptr()), shape=a.shape,
+                        what="scale_by_tensor")
+
+    def _copy_rows(self, src: GqTensor, rows: int, cols: int, src_stride: int, src_off: int, dst: GqTensor,
+                   dst_stride: int, dst_off: int) -> None:
+        self._check(self.lib.gq_copy_rows(self.ctx, c_void_p(src.ptr() + 4 * src_off), rows, cols, src_stride,
+                                          c_void_p(dst.ptr() + 4 * dst_off), dst_stride), "copy_rows")
+
+    def slice_rows(self, x: GqTensor, start: int, count: int) -> GqTensor:
+        """Rows [start, start+count) of [rows, dim] (rust/src/backend.rs:122-123)."""
+        dim = x.shape[1]
+        y = self._alloc((count, dim))
+        self._copy_rows(x, count, dim, dim, start * dim, y, dim, 0)
+        return y
+
+    def slice_cols(self, x: GqTensor, offset: int, width: int) -> GqTensor:
+        """[:, offset:offset+width] of [rows, stride] (rust/src/backend.rs:124-125)."""
+        rows, stride = x.shape
+        y = self._alloc((rows, width))
+        self._copy_rows(x, rows, width, stride, offset, y, width, 0)
+        return y
+
+    def concat_rows(self, a: Optional[GqTensor], b: GqTensor) -> GqTensor:
+        """Concatenate along dim 0 (rust/src/backend.rs:126-127)."""
+        if a is None:
+            y = self._alloc(b.shape)
+            self._copy_rows(b, 1, b.size(), b.size(), 0, y, b.size(), 0)
+            return y
+        shape = (a.shape[0] + b.shape[0],) + tuple(a.shape[1:])
+        y = self._alloc(shape)
+        self._copy_rows(a, 1, a.size(), a.size(), 0, y, a.size(), 0)
+        self._copy_rows(b, 1, b.size(), b.size(), 0, y, b.size(), a.size())
+        return y
+
+    def kv_append(self, existing: Optional[GqTensor], add: GqTensor) -> KvAppend:
+        """Append rows (rust/src/backend.rs:128-130): a new tensor holding old ++ new;
+        the old one is reported dead, as on the CPU backend."""
+        return KvAppend(tensor=self.concat_rows(existing, add), dead=existing)
 
     # ---- sync / lifecycle (rust/src/backend.rs:169-179) ------------------------
     def readback(self, t: GqTensor) -> np.ndarray:

@@ -77,7 +77,25 @@ SIGNATURES = {
         c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int32, c_int32, c_void_p]),
     "gq_softcap": (c_int, [c_void_p, c_void_p, c_int64, c_float, c_void_p]),
     "gq_geglu": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
+    "gq_rms_norm": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_float, c_void_p, c_int64]),
+    "gq_add_rms_norm": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_float, c_void_p,
+                                c_void_p]),
+    "gq_head_norm_rope": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_float, c_void_p,
+                                  c_float, c_int64, c_void_p, c_int64]),
+    "gq_rope": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_float, c_int64, c_void_p,
+                        c_int64]),
+    "gq_attention": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int64,
+                             c_int64, c_int64, c_void_p, c_void_p, c_int64, c_float, c_uint32, c_float, c_uint32,
+                             c_void_p]),
+    "gq_linear_bf16": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_int64, c_void_p]),
+    "gq_add": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
+    "gq_mul": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
+    "gq_scale": (c_int, [c_void_p, c_void_p, c_int64, c_float, c_void_p]),
+    "gq_scale_by_tensor": (c_int, [c_void_p, c_void_p, c_int64, c_void_p, c_void_p]),
+    "gq_copy_rows": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int64]),
 }
+
+GQ_ATTN_KPOS_ASCENDING = 0x1
 
 _lib = None
 

@@ -174,6 +174,73 @@ int gq_linear_prefill_static(void *cuda_stream, const float *x, int64_t m, int64
 int gq_softcap(gq_ctx *ctx, const float *x, int64_t n, float cap, float *y);
 int gq_geglu(gq_ctx *ctx, const float *gate, const float *up, int64_t n, float *y);
 
+/* ---- support ops of a decode step ----------------------------------------------
+ * The non-quantized methods of the Backend trait that a Gemma-4 decode step runs
+ * between the MATMUL_Q calls (rust/src/backend.rs:103-154; CPU semantics in
+ * rust/src/backend_cpu.rs:149-336). All pointers are device pointers; f32
+ * tensors are dense row-major unless a stride says otherwise. */
+
+/* Backend::rms_norm (rust/src/backend.rs:103-104; CPU rust/src/backend_cpu.rs:149-172):
+ * y = x / sqrt(mean(x^2) + eps) * w per row of d values; w NULL is the unweighted
+ * variant. Output row r starts at y + r * y_stride (0 = d), which lets a value row
+ * land directly in its KV-cache slot. */
+int gq_rms_norm(gq_ctx *ctx, const float *x, int64_t rows, int64_t d, const float *w, float eps, float *y,
+                int64_t y_stride);
+
+/* Backend::add_rms_norm (rust/src/backend.rs:137-144): y = (residual + rms_norm(x, w))
+ * * scale_by[0]; scale_by is a device scalar or NULL. */
+int gq_add_rms_norm(gq_ctx *ctx, const float *residual, const float *x, int64_t rows, int64_t d, const float *w,
+                    float eps, const float *scale_by, float *y);
+
+/* Backend::head_norm_rope (rust/src/backend.rs:148-154) and Backend::rope
+ * (rust/src/backend.rs:118-119; CPU rust/src/backend_cpu.rs:248-268) on x [t, heads,
+ * head_dim]: per-head weighted RMSNorm (head_norm_rope only), then the half-split
+ * rotation of the first rotary_dim values at positions[t] (device u32). Token i's
+ * heads are written at y + i * y_tok_stride (0 = heads * head_dim), so a key row can
+ * be written straight into a KV cache. rotary_dim must be even and <= 512. */
+int gq_head_norm_rope(gq_ctx *ctx, const float *x, int64_t t, int64_t heads, int64_t head_dim, const float *w,
+                      float eps, const uint32_t *positions, float theta, int64_t rotary_dim, float *y,
+                      int64_t y_tok_stride);
+int gq_rope(gq_ctx *ctx, const float *x, int64_t t, int64_t heads, int64_t head_dim, const uint32_t *positions,
+            float theta, int64_t rotary_dim, float *y, int64_t y_tok_stride);
+
+/* Key positions are strictly ascending (a KV cache's are): the causal and sliding-window
+ * bounds are then found by binary search and masked keys are never read. */
+#define GQ_ATTN_KPOS_ASCENDING 0x1u
+
+/* Backend::attention (rust/src/backend.rs:120-121; CPU rust/src/backend_cpu.rs:270-336),
+ * over `batch` independent sequences: q [batch, t, hq, head_dim], k and v of sequence b
+ * at k + b * kv_batch_stride as [s, hkv, head_dim], q_pos [batch * t], k_pos of
+ * sequence b at k_pos + b * kpos_batch_stride ([s]). Causal + optional sliding window
+ * (a key is visible when kpos <= qpos and qpos - kpos < window), scores * scale,
+ * optional tanh soft-cap, softmax, weighted sum of v -> out [batch * t, hq * head_dim].
+ * A query with no visible key gets zeros. batch = 1, kv_batch_stride = 0 is the
+ * trait's call. Requires hq / hkv <= 8, head_dim % 4 == 0 and <= 1024, 16-byte
+ * aligned q/k/v/out and kv_batch_stride % 4 == 0. Long key ranges are split over
+ * several CTAs whose partial results live in the context workspace. */
+int gq_attention(gq_ctx *ctx, const float *q, int64_t batch, int64_t t, int64_t hq, int64_t head_dim, const float *k,
+                 const float *v, int64_t s, int64_t hkv, int64_t kv_batch_stride, const uint32_t *q_pos,
+                 const uint32_t *k_pos, int64_t kpos_batch_stride, float scale, uint32_t sliding_window,
+                 float attn_softcap, uint32_t flags, float *out);
+
+/* Backend::linear with a plain weight (the CpuBackend non-quant branch of
+ * rust/src/backend_cpu.rs:174-222), weight stored as bf16 [n, k]: exact for weights
+ * that are bf16 on disk (Gemma-4's per_layer_model_projection, rust/src/weights.rs:11-14).
+ * y [m, n] = x [m, k] . w^T in f32. */
+int gq_linear_bf16(gq_ctx *ctx, const float *x, int64_t m, int64_t k, const uint16_t *w, int64_t n, float *y);
+
+/* Backend::add / mul / scale / scale_by_tensor (rust/src/backend.rs:107-111; CPU
+ * rust/src/backend_cpu.rs:224-235) on n elements; s of scale_by_tensor is a device scalar. */
+int gq_add(gq_ctx *ctx, const float *a, const float *b, int64_t n, float *y);
+int gq_mul(gq_ctx *ctx, const float *a, const float *b, int64_t n, float *y);
+int gq_scale(gq_ctx *ctx, const float *a, int64_t n, float s, float *y);
+int gq_scale_by_tensor(gq_ctx *ctx, const float *a, int64_t n, const float *s, float *y);
+
+/* Strided row copy dst[r * dst_stride + c] = src[r * src_stride + c]: slice_rows,
+ * slice_cols, concat_rows and kv_append of rust/src/backend.rs:122-130. */
+int gq_copy_rows(gq_ctx *ctx, const float *src, int64_t rows, int64_t cols, int64_t src_stride, float *dst,
+                 int64_t dst_stride);
+
 #ifdef __cplusplus
 }
 #endif

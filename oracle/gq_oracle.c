@@ -281,3 +281,149 @@ int32_t gqo_linear_gelu_mul_cols(const float *x, int64_t t, int64_t k, const gqo
   free(s);
   return rc;
 }
+
+/* ---- support ops of the decode step (SURVEY (a')) ----------------------- */
+
+/* rust/src/backend_cpu.rs:149-172: y = x / sqrt(mean(x^2) + eps) * w per row of
+ * d values (w NULL: unweighted). Sequential f32 sum of squares. */
+void gqo_rms_norm(const float *x, int64_t rows, int64_t d, const float *w, float eps, float *out) {
+  for (int64_t i = 0; i < rows; i++) {
+    const float *xr = x + i * d;
+    float *o = out + i * d;
+    float ss = 0.0f;
+    for (int64_t dd = 0; dd < d; dd++) ss += xr[dd] * xr[dd];
+    const float inv = 1.0f / sqrtf(ss / (float)d + eps);
+    if (w) {
+      for (int64_t dd = 0; dd < d; dd++) o[dd] = xr[dd] * inv * w[dd];
+    } else {
+      for (int64_t dd = 0; dd < d; dd++) o[dd] = xr[dd] * inv;
+    }
+  }
+}
+
+/* rust/src/backend_cpu.rs:224-235 */
+void gqo_add(const float *a, const float *b, size_t n, float *out) {
+  for (size_t i = 0; i < n; i++) out[i] = a[i] + b[i];
+}
+void gqo_mul(const float *a, const float *b, size_t n, float *out) {
+  for (size_t i = 0; i < n; i++) out[i] = a[i] * b[i];
+}
+void gqo_scale(const float *a, size_t n, float s, float *out) {
+  for (size_t i = 0; i < n; i++) out[i] = a[i] * s;
+}
+
+/* rust/src/backend.rs:137-144: (residual + rms_norm(x, w)) * scale_by[0]. */
+void gqo_add_rms_norm(const float *residual, const float *x, int64_t rows, int64_t d, const float *w,
+                      float eps, const float *scale_by, float *out) {
+  const size_t n = (size_t)(rows * d);
+  float *t = (float *)malloc((n ? n : 1) * sizeof(float));
+  gqo_rms_norm(x, rows, d, w, eps, t);
+  gqo_add(residual, t, n, out);
+  if (scale_by) gqo_scale(out, n, scale_by[0], out);
+  free(t);
+}
+
+/* rust/src/backend_cpu.rs:248-268: half-split partial RoPE on [t, heads, head_dim];
+ * the first rotary_dim values of every head rotate, the rest pass through. */
+void gqo_rope(const float *x, int64_t t, int64_t heads, int64_t head_dim, const uint32_t *positions,
+              float theta, int64_t rotary_dim, float *out) {
+  const size_t n = (size_t)(t * heads * head_dim);
+  if (out != x) memcpy(out, x, n * sizeof(float));
+  const int64_t half = rotary_dim / 2;
+  for (int64_t i = 0; i < t; i++) {
+    const float pos = (float)positions[i];
+    for (int64_t h = 0; h < heads; h++) {
+      const int64_t base = (i * heads + h) * head_dim;
+      for (int64_t j = 0; j < half; j++) {
+        const float freq = powf(theta, -(2.0f * (float)j) / (float)rotary_dim);
+        const float ang = pos * freq;
+        const float s = sinf(ang), c = cosf(ang);
+        const float a = x[base + j], b = x[base + j + half];
+        out[base + j] = a * c - b * s;
+        out[base + j + half] = b * c + a * s;
+      }
+    }
+  }
+}
+
+/* rust/src/backend.rs:148-154: per-head weighted RMSNorm, then rope. */
+void gqo_head_norm_rope(const float *x, int64_t t, int64_t heads, int64_t head_dim, const float *w,
+                        float eps, const uint32_t *positions, float theta, int64_t rotary_dim,
+                        float *out) {
+  const size_t n = (size_t)(t * heads * head_dim);
+  float *normed = (float *)malloc((n ? n : 1) * sizeof(float));
+  gqo_rms_norm(x, t * heads, head_dim, w, eps, normed);
+  gqo_rope(normed, t, heads, head_dim, positions, theta, rotary_dim, out);
+  free(normed);
+}
+
+/* ---- attention: rust/src/backend_cpu.rs:270-336 -------------------------- */
+
+typedef struct {
+  const float *q, *k, *v;
+  int64_t tt, hq, dh, s, hkv, dv;
+  const uint32_t *q_pos, *k_pos;
+  float scale;
+  uint32_t window;
+  float softcap;
+  float *out;
+} attn_ctx;
+
+static void attn_rows(void *p, int64_t start, int64_t end) {
+  attn_ctx *c = (attn_ctx *)p;
+  const int64_t s = c->s, hq = c->hq, dh = c->dh, dv = c->dv, hkv = c->hkv, group = hq / hkv;
+  float *scores = (float *)malloc((size_t)(s > 0 ? s : 1) * sizeof(float));
+  for (int64_t r = start; r < end; r++) {
+    const int64_t i = r / hq, h = r % hq;
+    const uint32_t qpos = c->q_pos[i];
+    const int64_t kvh = h / group;
+    const int64_t qb = (i * hq + h) * dh;
+    float maxv = -INFINITY;
+    for (int64_t j = 0; j < s; j++) {
+      const uint32_t kpos = c->k_pos[j];
+      /* causal + optional sliding-window mask */
+      if (kpos > qpos || (c->window > 0 && qpos - kpos >= c->window)) {
+        scores[j] = -INFINITY;
+        continue;
+      }
+      const int64_t kb = (j * hkv + kvh) * dh;
+      float dot = 0.0f;
+      for (int64_t d = 0; d < dh; d++) dot += c->q[qb + d] * c->k[kb + d];
+      dot *= c->scale;
+      if (c->softcap > 0.0f) dot = c->softcap * tanhf(dot / c->softcap);
+      scores[j] = dot;
+      if (dot > maxv) maxv = dot;
+    }
+    float sum = 0.0f;
+    for (int64_t j = 0; j < s; j++) {
+      if (scores[j] == -INFINITY) {
+        scores[j] = 0.0f;
+      } else {
+        const float e = expf(scores[j] - maxv);
+        scores[j] = e;
+        sum += e;
+      }
+    }
+    const float inv = sum > 0.0f ? 1.0f / sum : 0.0f;
+    float *o = c->out + r * dv;
+    for (int64_t d = 0; d < dv; d++) o[d] = 0.0f;
+    for (int64_t j = 0; j < s; j++) {
+      const float wgt = scores[j] * inv;
+      if (wgt == 0.0f) continue;
+      const int64_t vb = (j * hkv + kvh) * dv;
+      for (int64_t d = 0; d < dv; d++) o[d] += wgt * c->v[vb + d];
+    }
+  }
+  free(scores);
+}
+
+int32_t gqo_attention(const float *q, int64_t t, int64_t hq, int64_t dh, const float *k, const float *v,
+                      int64_t s, int64_t hkv, int64_t dv, const uint32_t *q_pos, const uint32_t *k_pos,
+                      float scale, uint32_t sliding_window, float attn_softcap, float *out,
+                      int32_t threads) {
+  if (t < 0 || s < 0 || hq <= 0 || hkv <= 0 || hq % hkv != 0) return -1;
+  attn_ctx c = {q, k, v, t, hq, dh, s, hkv, dv, q_pos, k_pos, scale, sliding_window, attn_softcap, out};
+  if (t == 0) return 0;
+  par_ranges(t * hq, (uint64_t)(t * hq) * (uint64_t)s * (uint64_t)(dh + dv), threads, attn_rows, &c);
+  return 0;
+}

@@ -17,6 +17,9 @@
  *                                   sequential f32 dot, k ascending)
  *   rust/src/backend_cpu.rs:239-244 geglu / softcap
  *   rust/src/backend.rs:155-167   linear_geglu / linear_gelu_mul_cols compositions
+ *   rust/src/backend_cpu.rs:149-172, 224-235, 248-336 rms_norm, add/mul/scale, rope,
+ *                                 attention; rust/src/backend.rs:137-154 add_rms_norm,
+ *                                 head_norm_rope (the support ops of a decode step)
  *
  * Arithmetic order follows the Rust code exactly (no FMA contraction: the build
  * uses -ffp-contract=off), so results are bit-identical to the reference CPU
@@ -99,6 +102,31 @@ int32_t gqo_linear_geglu(const float *x, int64_t t, int64_t k, const gqo_qweight
 int32_t gqo_linear_gelu_mul_cols(const float *x, int64_t t, int64_t k, const gqo_qweight *w,
                                  const float *b, int64_t b_stride, int64_t offset, float *y,
                                  int32_t threads);
+
+
+/* ---- support ops of the decode step ---------------------------------------
+ * rust/src/backend_cpu.rs:149-172 rms_norm (w NULL: unweighted) */
+void gqo_rms_norm(const float *x, int64_t rows, int64_t d, const float *w, float eps, float *out);
+/* rust/src/backend_cpu.rs:224-235 add / mul / scale */
+void gqo_add(const float *a, const float *b, size_t n, float *out);
+void gqo_mul(const float *a, const float *b, size_t n, float *out);
+void gqo_scale(const float *a, size_t n, float s, float *out);
+/* rust/src/backend.rs:137-144: (residual + rms_norm(x, w)) * scale_by[0] (scale_by may be NULL) */
+void gqo_add_rms_norm(const float *residual, const float *x, int64_t rows, int64_t d, const float *w,
+                      float eps, const float *scale_by, float *out);
+/* rust/src/backend_cpu.rs:248-268: half-split partial RoPE on [t, heads, head_dim] */
+void gqo_rope(const float *x, int64_t t, int64_t heads, int64_t head_dim, const uint32_t *positions,
+              float theta, int64_t rotary_dim, float *out);
+/* rust/src/backend.rs:148-154: per-head weighted RMSNorm then rope */
+void gqo_head_norm_rope(const float *x, int64_t t, int64_t heads, int64_t head_dim, const float *w,
+                        float eps, const uint32_t *positions, float theta, int64_t rotary_dim,
+                        float *out);
+/* rust/src/backend_cpu.rs:270-336: causal (+ sliding window) grouped-query
+ * attention. q [t, hq, dh], k [s, hkv, dh], v [s, hkv, dv] -> out [t, hq*dv]. */
+int32_t gqo_attention(const float *q, int64_t t, int64_t hq, int64_t dh, const float *k, const float *v,
+                      int64_t s, int64_t hkv, int64_t dv, const uint32_t *q_pos, const uint32_t *k_pos,
+                      float scale, uint32_t sliding_window, float attn_softcap, float *out,
+                      int32_t threads);
 
 #ifdef __cplusplus
 }

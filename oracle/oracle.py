@@ -58,6 +58,16 @@ def load() -> ctypes.CDLL:
         "gqo_linear_geglu": (c_int32, [c_void_p, c_int64, c_int64, P, P, c_void_p, c_int32]),
         "gqo_linear_gelu_mul_cols": (c_int32, [c_void_p, c_int64, c_int64, P, c_void_p, c_int64, c_int64,
                                                c_void_p, c_int32]),
+        "gqo_rms_norm": (None, [c_void_p, c_int64, c_int64, c_void_p, c_float, c_void_p]),
+        "gqo_add": (None, [c_void_p, c_void_p, c_size_t, c_void_p]),
+        "gqo_mul": (None, [c_void_p, c_void_p, c_size_t, c_void_p]),
+        "gqo_scale": (None, [c_void_p, c_size_t, c_float, c_void_p]),
+        "gqo_add_rms_norm": (None, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_float, c_void_p, c_void_p]),
+        "gqo_rope": (None, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_float, c_int64, c_void_p]),
+        "gqo_head_norm_rope": (None, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_float, c_void_p, c_float,
+                                      c_int64, c_void_p]),
+        "gqo_attention": (c_int32, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int64,
+                                    c_int64, c_void_p, c_void_p, c_float, c_uint32, c_float, c_void_p, c_int32]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -198,4 +208,83 @@ def softcap(x, cap: float) -> np.ndarray:
     x = _f32(x)
     out = np.empty_like(x)
     load().gqo_softcap(_p(x), x.size, cap, _p(out))
+    return out
+
+
+# ---- support ops of the decode step (rust/src/backend_cpu.rs, rust/src/backend.rs) ----
+
+def _u32(a) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a, dtype=np.uint32))
+
+
+def rms_norm(x, w, eps: float) -> np.ndarray:
+    """rust/src/backend_cpu.rs:149-172, per row of the last axis (w None: unweighted)."""
+    x = _f32(x)
+    d = x.shape[-1]
+    out = np.empty_like(x)
+    wp = None if w is None else _f32(w)
+    load().gqo_rms_norm(_p(x), x.size // d, d, None if wp is None else _p(wp), eps, _p(out))
+    return out
+
+
+def add(a, b) -> np.ndarray:
+    a, b = _f32(a), _f32(b)
+    out = np.empty_like(a)
+    load().gqo_add(_p(a), _p(b), a.size, _p(out))
+    return out
+
+
+def mul(a, b) -> np.ndarray:
+    a, b = _f32(a), _f32(b)
+    out = np.empty_like(a)
+    load().gqo_mul(_p(a), _p(b), a.size, _p(out))
+    return out
+
+
+def scale(a, s: float) -> np.ndarray:
+    a = _f32(a)
+    out = np.empty_like(a)
+    load().gqo_scale(_p(a), a.size, s, _p(out))
+    return out
+
+
+def add_rms_norm(residual, x, w, eps: float, scale_by=None) -> np.ndarray:
+    """rust/src/backend.rs:137-144: (residual + rms_norm(x, w)) * scale_by[0]."""
+    r, x, w = _f32(residual), _f32(x), _f32(w)
+    d = x.shape[-1]
+    out = np.empty_like(x)
+    sb = None if scale_by is None else _f32(np.atleast_1d(scale_by))
+    load().gqo_add_rms_norm(_p(r), _p(x), x.size // d, d, _p(w), eps, None if sb is None else _p(sb), _p(out))
+    return out
+
+
+def rope(x, positions, theta: float, head_dim: int, heads: int, rotary_dim: int) -> np.ndarray:
+    """rust/src/backend_cpu.rs:248-268 on [t, heads, head_dim]."""
+    x, pos = _f32(x), _u32(positions)
+    out = np.empty_like(x)
+    load().gqo_rope(_p(x), pos.size, heads, head_dim, _p(pos), theta, rotary_dim, _p(out))
+    return out
+
+
+def head_norm_rope(x, w, eps: float, positions, theta: float, head_dim: int, heads: int,
+                   rotary_dim: int) -> np.ndarray:
+    """rust/src/backend.rs:148-154."""
+    x, w, pos = _f32(x), _f32(w), _u32(positions)
+    out = np.empty_like(x)
+    load().gqo_head_norm_rope(_p(x), pos.size, heads, head_dim, _p(w), eps, _p(pos), theta, rotary_dim, _p(out))
+    return out
+
+
+def attention(q, k, v, q_pos, k_pos, scale: float = 1.0, sliding_window: int = 0, attn_softcap: float = 0.0,
+              threads: int = 0) -> np.ndarray:
+    """rust/src/backend_cpu.rs:270-336: q [t, hq, dh], k [s, hkv, dh], v [s, hkv, dv] -> [t, hq*dv]."""
+    q, k, v = _f32(q), _f32(k), _f32(v)
+    qp, kp = _u32(q_pos), _u32(k_pos)
+    t, hq, dh = q.shape
+    s, hkv, dv = v.shape
+    out = np.empty((t, hq * dv), dtype=np.float32)
+    rc = load().gqo_attention(_p(q), t, hq, dh, _p(k), _p(v), s, hkv, dv, _p(qp), _p(kp), scale,
+                              int(sliding_window), attn_softcap, _p(out), threads)
+    if rc != 0:
+        raise ValueError("oracle attention: bad shape")
     return out

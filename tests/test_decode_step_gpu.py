@@ -1,0 +1,243 @@
+"""The support ops and the whole decode step on the GPU against the CPU oracle
+(needs a B200).
+
+Op cases follow the reference's own parity tests (rust/tests/gpu.rs:38-143 for
+rms_norm / rope / attention / slices, :257-296 grouped attention, :299-333 fused
+ops) with the tolerances written below: relative L2 against the oracle, which
+restates the Rust CPU backend. The decode step (rust/src/model.rs at the E2B
+shapes) is compared on its logits: relative L2 <= 1e-4 and
+max |diff| < 5e-3 (the reference's full-model bound, rust/tests/gpu.rs:200).
+"""
+import ctypes
+from ctypes import c_float, c_void_p
+
+import numpy as np
+import pytest
+
+from gq import AttnOpts, CudaBackend, e2b, synth
+from gq._abi import GQ_ATTN_KPOS_ASCENDING
+from oracle import e2b_ref
+from oracle import oracle as o
+
+pytestmark = pytest.mark.gpu
+
+OP_REL = 2e-6        # norms / rope / elementwise: one tree-ordered row sum apart
+ATTN_REL = 1e-5      # attention: split softmax and tree-ordered dots
+STEP_REL = 1e-4      # whole decode step, logits
+STEP_MAX_ABS = 5e-3  # rust/tests/gpu.rs:200
+
+
+def rel(a, b):
+    a, b = np.asarray(a, np.float64).ravel(), np.asarray(b, np.float64).ravel()
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+@pytest.fixture(scope="module")
+def g():
+    b = CudaBackend(0)
+    yield b
+    b.close()
+
+
+@pytest.mark.parametrize("rows,d", [(5, 48), (1, 1536), (64, 1536), (280, 256), (3, 7)])
+def test_rms_norm(g, rows, d):
+    x = synth.normal(100 + d, rows * d).reshape(rows, d) * 3.0
+    w = synth.uniform(101 + d, d, -0.1, 0.1)
+    got = g.readback(g.rms_norm(g.tensor(x, x.shape), g.tensor(w, (d,)), 1e-6))
+    assert rel(got, o.rms_norm(x, w, 1e-6)) <= OP_REL
+    got = g.readback(g.rms_norm(g.tensor(x, x.shape), None, 1e-6))
+    assert rel(got, o.rms_norm(x, None, 1e-6)) <= OP_REL
+
+
+@pytest.mark.parametrize("with_scalar", [False, True])
+def test_add_rms_norm(g, with_scalar):
+    t, d = 5, 48
+    x, r = synth.normal(110, t * d).reshape(t, d), synth.normal(111, t * d).reshape(t, d)
+    w = synth.uniform(112, d, -0.1, 0.1)
+    s = np.array([1.37], np.float32)
+    gs = g.tensor(s, (1,)) if with_scalar else None
+    got = g.readback(g.add_rms_norm(g.tensor(r, r.shape), g.tensor(x, x.shape), g.tensor(w, (d,)), 1e-6, gs))
+    assert rel(got, o.add_rms_norm(r, x, w, 1e-6, s if with_scalar else None)) <= OP_REL
+
+
+@pytest.mark.parametrize("t,heads,dh,rot", [(3, 4, 16, 8), (2, 8, 256, 256), (2, 1, 512, 128), (4, 2, 16, 8)])
+def test_head_norm_rope_and_rope(g, t, heads, dh, rot):
+    x = synth.normal(120 + dh, t * heads * dh).reshape(t, heads, dh)
+    w = synth.uniform(121 + dh, dh, -0.1, 0.1)
+    pos = [i * 7 + 3 for i in range(t)]
+    got = g.readback(g.head_norm_rope(g.tensor(x, x.shape), g.tensor(w, (dh,)), 1e-6, pos, 1e4, dh, heads, rot))
+    assert rel(got, o.head_norm_rope(x, w, 1e-6, pos, 1e4, dh, heads, rot)) <= OP_REL
+    got = g.readback(g.rope(g.tensor(x, x.shape), pos, 1e4, dh, heads, rot))
+    assert rel(got, o.rope(x, pos, 1e4, dh, heads, rot)) <= OP_REL
+
+
+def test_rope_large_positions(g):
+    """Decode positions up to 2047 at both E2B rope settings (theta 1e4 full, 1e6 partial)."""
+    for dh, rot, theta in [(256, 256, 1e4), (512, 128, 1e6)]:
+        x = synth.normal(130 + dh, 4 * 8 * dh).reshape(4, 8, dh)
+        pos = [0, 511, 1024, 2047]
+        got = g.readback(g.rope(g.tensor(x, x.shape), pos, theta, dh, 8, rot))
+        assert rel(got, o.rope(x, pos, theta, dh, 8, rot)) <= OP_REL
+
+
+ATTN_CASES = [  # (t, s, hq, hkv, dh, window, scale) — rust/tests/gpu.rs:122-141, 263-296
+    (6, 6, 4, 1, 16, 3, 0.25), (3, 300, 2, 1, 32, 0, 1.0), (3, 300, 2, 1, 32, 150, 1.0),
+    (3, 300, 8, 1, 256, 0, 1 / 16), (3, 300, 8, 1, 256, 150, 1 / 16), (1, 700, 8, 1, 512, 0, 1 / np.sqrt(512)),
+    (1, 900, 8, 1, 256, 512, 1 / 16), (5, 5, 8, 1, 256, 0, 1 / 16), (6, 70, 8, 1, 256, 3, 1 / 16),
+    (2, 200, 4, 1, 256, 0, 1 / 16), (1, 64, 8, 2, 512, 0, 1 / np.sqrt(512)), (1, 2048, 8, 1, 512, 0, 1.0),
+    (1, 2048, 8, 1, 256, 512, 1.0),
+]
+
+
+@pytest.mark.parametrize("t,s,hq,hkv,dh,window,scale", ATTN_CASES)
+def test_attention(g, t, s, hq, hkv, dh, window, scale):
+    q = synth.normal(140 + s + dh, t * hq * dh).reshape(t, hq, dh) * 0.5
+    k = synth.normal(141 + s + dh, s * hkv * dh).reshape(s, hkv, dh) * 0.5
+    v = synth.normal(142 + s + dh, s * hkv * dh).reshape(s, hkv, dh) * 0.5
+    kp = list(range(s))
+    qp = list(range(s - t, s))
+    opts = AttnOpts(q_pos=qp, k_pos=kp, scale=float(scale), sliding_window=window)
+    got = g.readback(g.attention(g.tensor(q, q.shape), g.tensor(k, k.shape), g.tensor(v, v.shape), opts))
+    assert rel(got, o.attention(q, k, v, qp, kp, float(scale), window)) <= ATTN_REL
+
+
+def test_attention_unsorted_positions_and_softcap(g):
+    """Key positions in no order (no range trimming) and an attention soft-cap."""
+    t, s, hq, dh = 2, 40, 4, 16
+    q = synth.normal(150, t * hq * dh).reshape(t, hq, dh)
+    k = synth.normal(151, s * dh).reshape(s, 1, dh)
+    v = synth.normal(152, s * dh).reshape(s, 1, dh)
+    kp = list(np.random.RandomState(3).permutation(s))
+    qp = [20, 39]
+    opts = AttnOpts(q_pos=qp, k_pos=kp, scale=0.5, sliding_window=10, attn_softcap=5.0)
+    got = g.readback(g.attention(g.tensor(q, q.shape), g.tensor(k, k.shape), g.tensor(v, v.shape), opts))
+    assert rel(got, o.attention(q, k, v, qp, kp, 0.5, 10, 5.0)) <= ATTN_REL
+
+
+@pytest.mark.parametrize("batch,s,dh,window", [(4, 2048, 512, 0), (4, 2048, 256, 512), (64, 300, 256, 0)])
+def test_attention_batched_kv_cache(g, batch, s, dh, window):
+    """The decode layout: `batch` sequences, each a [capacity, dh] cache, one query each."""
+    import torch
+
+    cap = s + 8
+    hq = 8
+    q = synth.normal(160 + dh, batch * hq * dh).reshape(batch, hq, dh)
+    kc = synth.normal(161 + dh, batch * cap * dh).reshape(batch, cap, dh)
+    vc = synth.normal(162 + dh, batch * cap * dh).reshape(batch, cap, dh)
+    dev = g.torch_device
+    tq, tk, tv = (torch.from_numpy(a).to(dev) for a in (q, kc, vc))
+    qpos = torch.full((batch,), s - 1, dtype=torch.int32, device=dev)
+    kpos = torch.arange(cap, dtype=torch.int32, device=dev)
+    out = torch.empty(batch, hq * dh, device=dev)
+    lib = g.lib
+    rc = lib.gq_attention(g.ctx, c_void_p(tq.data_ptr()), batch, 1, hq, dh, c_void_p(tk.data_ptr()),
+                          c_void_p(tv.data_ptr()), s, 1, cap * dh, c_void_p(qpos.data_ptr()),
+                          c_void_p(kpos.data_ptr()), 0, c_float(1.0), window, c_float(0.0), GQ_ATTN_KPOS_ASCENDING,
+                          c_void_p(out.data_ptr()))
+    g._check(rc, "attention")
+    g.flush()
+    got = out.cpu().numpy()
+    for b in (0, batch // 2, batch - 1):
+        want = o.attention(q[b:b + 1], kc[b, :s].reshape(s, 1, dh), vc[b, :s].reshape(s, 1, dh), [s - 1],
+                           list(range(s)), 1.0, window)
+        assert rel(got[b], want) <= ATTN_REL, b
+
+
+@pytest.mark.parametrize("m,k,n", [(1, 1536, 8960), (64, 1536, 8960), (3, 40, 23), (2, 4096, 100)])
+def test_linear_bf16(g, m, k, n):
+    x = synth.normal(170 + k, m * k).reshape(m, k)
+    w = e2b._bf16_round(synth.uniform(171 + k, n * k, -0.04, 0.04)).reshape(n, k)
+    got = g.readback(g.linear_plain(g.tensor(x, x.shape), g.tensor_bf16(w, w.shape)))
+    assert rel(got, o.linear_f32(x, w)) <= 1e-5
+
+
+def test_elementwise_and_rows(g):
+    n = 100
+    a, b = synth.normal(180, n), synth.normal(181, n)
+    ga, gb = g.tensor(a, (n,)), g.tensor(b, (n,))
+    assert np.array_equal(g.readback(g.add(ga, gb)), o.add(a, b))
+    assert np.array_equal(g.readback(g.mul(ga, gb)), o.mul(a, b))
+    assert np.array_equal(g.readback(g.scale(ga, 3.5)), o.scale(a, 3.5))
+    assert np.array_equal(g.readback(g.scale_by_tensor(ga, g.tensor([0.37], (1,)))), o.scale(a, np.float32(0.37)))
+    x = synth.normal(182, 4 * 20).reshape(4, 20)
+    gx = g.tensor(x, x.shape)
+    assert np.array_equal(g.readback(g.slice_cols(gx, 5, 7)).reshape(4, 7), x[:, 5:12])
+    assert np.array_equal(g.readback(g.slice_rows(gx, 2, 2)).reshape(2, 20), x[2:4])
+    y = synth.normal(183, 3 * 20).reshape(3, 20)
+    cat = g.readback(g.concat_rows(gx, g.tensor(y, y.shape))).reshape(7, 20)
+    assert np.array_equal(cat, np.concatenate([x, y]))
+    grown = None
+    for i in range(3):  # three appends of 200 rows (rust/tests/gpu.rs:109-121)
+        chunk = synth.normal(190 + i, 200 * 8).reshape(200, 8)
+        grown = g.kv_append(grown, g.tensor(chunk, chunk.shape)).tensor
+    assert grown.shape == (600, 8)
+
+
+# ---- the decode step -------------------------------------------------------------
+
+def run_step(g, cfg, w, batch, cache_len, ids, capacity=None):
+    cap = capacity or cache_len + 1
+    dec = e2b.Decoder(g, cfg, w, batch=batch, cache_len=cache_len, capacity=cap)
+    dec.set_ids(ids)
+    dec.run()
+    logits = dec.read(dec.logits)
+    kv = e2b_ref.kv_from_weights(cfg, w, batch, cache_len, cap)
+    want = e2b_ref.decode_step(cfg, w, ids, cache_len, kv)
+    return dec, logits, want, kv
+
+
+def check_logits(got, want):
+    assert np.isfinite(got).all()
+    r = rel(got, want)
+    d = float(np.max(np.abs(got - want)))
+    assert r <= STEP_REL and d < STEP_MAX_ABS, (r, d)
+
+
+@pytest.mark.parametrize("batch,cache_len", [(1, 0), (1, 4), (3, 6)])
+def test_decode_step_tiny(g, batch, cache_len):
+    cfg = e2b.tiny_config(48)
+    w = e2b.Weights(cfg, 123)
+    ids = [2, 5, 47][:batch]
+    _, got, want, _ = run_step(g, cfg, w, batch, cache_len, ids, capacity=cache_len + 3)
+    check_logits(got, want)
+
+
+def test_decode_step_small_batched(g):
+    cfg = e2b.small_config(4096)
+    w = e2b.Weights(cfg, 7)
+    dec, got, want, kv = run_step(g, cfg, w, 5, 40, [1, 17, 300, 4095, 17], capacity=48)
+    check_logits(got, want)
+    # the step's key/value rows landed in slot 40 of every source cache
+    for i, (K, V) in kv.items():
+        kg = dec.kcache[i].cpu().numpy()
+        vg = dec.vcache[i].cpu().numpy()
+        assert rel(kg[:, 40], K[:, 40]) <= 1e-4 and rel(vg[:, 40], V[:, 40]) <= 1e-4
+        assert np.array_equal(kg[:, :40], K[:, :40])
+
+
+def test_decode_step_graph_replay_matches_eager():
+    g = CudaBackend(0, own_stream=True)
+    try:
+        cfg = e2b.small_config(2048)
+        w = e2b.Weights(cfg, 9)
+        dec = e2b.Decoder(g, cfg, w, batch=2, cache_len=20, capacity=24)
+        dec.set_ids([7, 9])
+        dec.run()
+        eager = dec.read(dec.logits)
+        graph = dec.record()
+        dec.logits.zero_()
+        g.flush()
+        g.replay(graph)
+        assert np.array_equal(dec.read(dec.logits), eager)
+        g.destroy_graph(graph)
+    finally:
+        g.close()
+
+
+def test_decode_step_e2b_batch1(g):
+    """The full E2B shapes at KV length 2048 (the new token at position 2047)."""
+    cfg = e2b.e2b_config()
+    w = e2b.Weights(cfg, 123)
+    dec, got, want, _ = run_step(g, cfg, w, 1, 2047, [1234])
+    check_logits(got, want)
+    del dec
