@@ -15,13 +15,15 @@
 //    the CPU and passed by value in the kernel parameters (no table in memory,
 //    nothing to allocate, graph-capturable);
 //  * attention: a CTA owns one (query token, KV head) pair and a contiguous
-//    chunk of the active key range (causal and window bounds found by binary
-//    search when key positions are ascending, as a KV cache's are); every
-//    thread owns 4 of the head_dim columns for all the query heads of the group
-//    (MQA: 8 heads read each K/V element once), so K and V stream from HBM with
-//    coalesced 16-byte loads and no shared-memory staging; score partials are
-//    reduced by a transposing warp butterfly; chunk results (max, sum, output)
-//    are merged by a second kernel when the range is split.
+//    chunk of the active key range (causal and window bounds computed directly
+//    when key j sits at position j, as in a KV cache, or found by binary search
+//    when positions only ascend); every thread owns 4 of the head_dim columns
+//    for all the query heads of the group (MQA: 8 heads read each K/V element
+//    once); score partials are reduced by a transposing warp butterfly; chunk
+//    results (max, sum, output) are merged by a second kernel when the range is
+//    split. With one KV head (rows contiguous) the chunk streams through a ring
+//    of shared-memory stages filled by bulk copies (TMA engine), softmax online;
+//    otherwise K and V are read with coalesced 16-byte loads straight from HBM.
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdint.h>
@@ -123,6 +125,61 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const float *x, c
   }
 }
 
+// Register-resident variant of rmsnorm_kernel for rows of d <= 128 * VPL values
+// (d % 4 == 0, 16-byte aligned rows): every lane issues all of its x, w and
+// residual loads before the first use, so a row costs one memory round trip
+// instead of one per strided loop iteration.
+template <int KIND, int VPL>
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_reg_kernel(const float *x, const float *r, const float *w,
+                                                                   const float *s, int64_t rows, int64_t d,
+                                                                   float eps, float *y, RowMap ymap) {
+  gqd::griddep_wait();
+  gqd::griddep_launch_dependents();
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (kNormThreads / 32) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int n4 = (int)(d / 4);
+  const float4 *x4 = reinterpret_cast<const float4 *>(x + row * d);
+  const float4 *w4 = reinterpret_cast<const float4 *>(w);
+  const float4 *r4 = reinterpret_cast<const float4 *>(KIND == 1 ? r + row * d : nullptr);
+  const float sc = (KIND == 1 && s) ? __ldg(s) : 1.0f;
+  float4 xv[VPL], wv[VPL], rv[VPL];
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int c = lane + 32 * i;
+    const bool in = c < n4;
+    xv[i] = in ? x4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+    wv[i] = (in && w) ? __ldg(w4 + c) : make_float4(1.f, 1.f, 1.f, 1.f);
+    rv[i] = (KIND == 1 && in) ? r4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  float ss = 0.0f;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    ss = __fadd_rn(ss, __fmul_rn(xv[i].x, xv[i].x));
+    ss = __fadd_rn(ss, __fmul_rn(xv[i].y, xv[i].y));
+    ss = __fadd_rn(ss, __fmul_rn(xv[i].z, xv[i].z));
+    ss = __fadd_rn(ss, __fmul_rn(xv[i].w, xv[i].w));
+  }
+  const float inv = rms_inv(warp_sum(ss), d, eps);
+  auto one = [&](float xx, float ww, float rr) {
+    float n = __fmul_rn(xx, inv);
+    if (w) n = __fmul_rn(n, ww);
+    if (KIND == 1) {
+      n = __fadd_rn(rr, n);
+      if (s) n = __fmul_rn(n, sc);
+    }
+    return n;
+  };
+  float4 *y4 = reinterpret_cast<float4 *>(y + ymap.at(row));
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int c = lane + 32 * i;
+    if (c < n4)
+      y4[c] = make_float4(one(xv[i].x, wv[i].x, rv[i].x), one(xv[i].y, wv[i].y, rv[i].y),
+                          one(xv[i].z, wv[i].z, rv[i].z), one(xv[i].w, wv[i].w, rv[i].w));
+  }
+}
+
 struct RopeFreq {
   float f[kMaxHalfRot];
 };
@@ -162,6 +219,71 @@ __global__ void __launch_bounds__(kNormThreads) head_rope_kernel(const float *x,
   for (int64_t i = 2 * half + lane; i < dh; i += 32) yr[i] = nrm(i);
 }
 
+// Register-resident head_rope_kernel for head_dim <= 128 * VPL (head_dim % 4 == 0,
+// 16-byte aligned rows): the row and its weights are loaded up front, the
+// normalised row goes through a per-warp shared-memory buffer so each lane can
+// read the pair (j, j + half) it rotates.
+template <bool NORM, int VPL>
+__global__ void __launch_bounds__(kNormThreads) head_rope_reg_kernel(const float *x, const float *w, int64_t rows,
+                                                                     int64_t heads, int64_t dh, float eps,
+                                                                     const uint32_t *positions, int half,
+                                                                     const __grid_constant__ RopeFreq fr, float *y,
+                                                                     RowMap ymap) {
+  __shared__ __align__(16) float buf[kNormThreads / 32][128 * VPL];
+  gqd::griddep_wait();
+  gqd::griddep_launch_dependents();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t row = (int64_t)blockIdx.x * (kNormThreads / 32) + warp;
+  if (row >= rows) return;
+  const int n4 = (int)(dh / 4);
+  const float4 *x4 = reinterpret_cast<const float4 *>(x + row * dh);
+  const float4 *w4 = reinterpret_cast<const float4 *>(w);
+  const float pos = (float)__ldg(positions + row / heads);
+  float4 xv[VPL], wv[VPL];
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int c = lane + 32 * i;
+    const bool in = c < n4;
+    xv[i] = in ? x4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+    wv[i] = (NORM && in) ? __ldg(w4 + c) : make_float4(1.f, 1.f, 1.f, 1.f);
+  }
+  float inv = 1.0f;
+  if (NORM) {
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < VPL; ++i) {
+      ss = __fadd_rn(ss, __fmul_rn(xv[i].x, xv[i].x));
+      ss = __fadd_rn(ss, __fmul_rn(xv[i].y, xv[i].y));
+      ss = __fadd_rn(ss, __fmul_rn(xv[i].z, xv[i].z));
+      ss = __fadd_rn(ss, __fmul_rn(xv[i].w, xv[i].w));
+    }
+    inv = rms_inv(warp_sum(ss), dh, eps);
+  }
+  float *b = buf[warp];
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int c = lane + 32 * i;
+    if (c < n4) {
+      float4 n = xv[i];
+      if (NORM)
+        n = make_float4(__fmul_rn(__fmul_rn(n.x, inv), wv[i].x), __fmul_rn(__fmul_rn(n.y, inv), wv[i].y),
+                        __fmul_rn(__fmul_rn(n.z, inv), wv[i].z), __fmul_rn(__fmul_rn(n.w, inv), wv[i].w));
+      reinterpret_cast<float4 *>(b)[c] = n;
+    }
+  }
+  __syncwarp();
+  float *yr = y + ymap.at(row);
+  for (int j = lane; j < half; j += 32) {
+    const float ang = __fmul_rn(pos, fr.f[j]);
+    float sn, cs;
+    sincosf(ang, &sn, &cs);
+    const float a = b[j], bb = b[j + half];
+    yr[j] = __fsub_rn(__fmul_rn(a, cs), __fmul_rn(bb, sn));
+    yr[j + half] = __fadd_rn(__fmul_rn(bb, cs), __fmul_rn(a, sn));
+  }
+  for (int64_t i = 2 * half + lane; i < dh; i += 32) yr[i] = b[i];
+}
+
 // ---- attention --------------------------------------------------------------
 
 struct AttnArgs {
@@ -175,7 +297,8 @@ struct AttnArgs {
   int64_t kpos_batch_stride;
   float scale, softcap;
   uint32_t window;
-  int sorted, chunk, splits;
+  int sorted, identity, chunk, splits;
+  uint32_t *err;
 };
 
 // First index in [0, n) whose key position exceeds `bound` (ascending positions).
@@ -212,18 +335,28 @@ __global__ void __launch_bounds__(NT) attn_chunk_kernel(const AttnArgs a) {
   const float *vb = a.v + b * a.kv_batch_stride + kvh * a.dh;
   const int64_t kv_row = a.Hkv * a.dh;
 
-  if (tid == 0) {
-    int64_t lo = 0, hi = a.S;
-    if (a.sorted) {
-      hi = upper_bound_pos(kp, a.S, qpos);
-      if (a.window > 0 && qpos >= a.window) lo = upper_bound_pos(kp, hi, qpos - a.window);
+  int64_t j0, j1;
+  if (a.identity) {
+    // key j sits at position j: the visible range is arithmetic
+    const int64_t hi = min(a.S, (int64_t)qpos + 1);
+    const int64_t lo = (a.window > 0 && qpos >= a.window) ? (int64_t)(qpos - a.window) + 1 : 0;
+    j0 = lo + (int64_t)blockIdx.x * a.chunk;
+    j1 = min(hi, j0 + (int64_t)a.chunk);
+  } else {
+    if (tid == 0) {
+      int64_t lo = 0, hi = a.S;
+      if (a.sorted) {
+        hi = upper_bound_pos(kp, a.S, qpos);
+        if (a.window > 0 && qpos >= a.window) lo = upper_bound_pos(kp, hi, qpos - a.window);
+      }
+      const int64_t jj0 = lo + (int64_t)blockIdx.x * a.chunk;
+      range[0] = jj0;
+      range[1] = min(hi, jj0 + (int64_t)a.chunk);
     }
-    const int64_t j0 = lo + (int64_t)blockIdx.x * a.chunk;
-    range[0] = j0;
-    range[1] = min(hi, j0 + (int64_t)a.chunk);
+    __syncthreads();
+    j0 = range[0];
+    j1 = range[1];
   }
-  __syncthreads();
-  const int64_t j0 = range[0], j1 = range[1];
   const int nkeys = j1 > j0 ? (int)(j1 - j0) : 0;
 
   const int col = 4 * tid;
@@ -283,7 +416,7 @@ __global__ void __launch_bounds__(NT) attn_chunk_kernel(const AttnArgs a) {
         const int g = idx / kKeyBatch, kk = idx % kKeyBatch;
         const int jj = jb + kk;
         if (g < G && jj < nkeys) {
-          const uint32_t kpos = kp[j0 + jj];
+          const uint32_t kpos = a.identity ? (uint32_t)(j0 + jj) : kp[j0 + jj];
           float s = __fmul_rn(sum, a.scale);
           if (a.softcap > 0.0f) s = __fmul_rn(a.softcap, tanhf(__fdiv_rn(s, a.softcap)));
           if (kpos > qpos || (a.window > 0 && qpos - kpos >= a.window)) s = -INFINITY;
@@ -359,31 +492,256 @@ __global__ void __launch_bounds__(NT) attn_chunk_kernel(const AttnArgs a) {
   }
 }
 
+// Single-KV-head attention over contiguous cache rows (the decode layout): the
+// CTA streams its key chunk through a ring of kRingStages shared-memory stages,
+// each holding kSubKeys key rows and the matching value rows, filled by two 1-D
+// bulk copies (TMA engine) that complete on the stage's mbarrier; softmax is
+// online across sub-tiles (running max, sum and output rescaled per head).
+// Thread t owns head_dim columns 4t .. 4t+3 for all G query heads, as above.
+constexpr int kSubKeys = 8;
+constexpr int kRingStages = 4;
+
+template <int NT>
+__global__ void __launch_bounds__(NT) attn_ring_kernel(const AttnArgs a) {
+  static_assert(NT >= kMaxGroup * kKeyBatch, "one thread per (head, key) entry of a sub-tile");
+  constexpr int NWARP = NT / 32;
+  extern __shared__ __align__(128) uint8_t smem_dyn[];
+  float *ring = reinterpret_cast<float *>(smem_dyn);  // [stage][K|V][kSubKeys][dh]
+  __shared__ __align__(8) uint64_t full[kRingStages];
+  __shared__ float sc[kSubKeys][kMaxGroup];
+  __shared__ float red[NWARP][kKeyBatch * kMaxGroup];
+  __shared__ float m_run[kMaxGroup], l_run[kMaxGroup], corr[kMaxGroup];
+  __shared__ int abort_flag;
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int G = (int)a.Hq;  // one KV head
+  const int64_t bt = blockIdx.y;
+  const int64_t b = bt / a.T;
+  const int dh = (int)a.dh;
+  const uint32_t stage_floats = (uint32_t)(2 * kSubKeys * dh);
+  if (tid == 0) {
+    for (int i = 0; i < kRingStages; ++i) gqd::mbar_init(&full[i], 1);
+    gqd::fence_mbar_init();
+    abort_flag = 0;
+  }
+  if (tid < kMaxGroup) {
+    m_run[tid] = -INFINITY;
+    l_run[tid] = 0.0f;
+  }
+  gqd::griddep_wait();
+  gqd::griddep_launch_dependents();
+  const uint32_t qpos = a.q_pos[bt];
+  int64_t lo = 0, hi = a.S;
+  if (a.identity) {
+    hi = min(a.S, (int64_t)qpos + 1);
+    lo = (a.window > 0 && qpos >= a.window) ? (int64_t)(qpos - a.window) + 1 : 0;
+  } else {
+    const uint32_t *kpb = a.k_pos + b * a.kpos_batch_stride;
+    hi = upper_bound_pos(kpb, a.S, qpos);
+    if (a.window > 0 && qpos >= a.window) lo = upper_bound_pos(kpb, hi, qpos - a.window);
+  }
+  const int64_t j0 = lo + (int64_t)blockIdx.x * a.chunk;
+  const int64_t j1 = min(hi, j0 + (int64_t)a.chunk);
+  const int nkeys = j1 > j0 ? (int)(j1 - j0) : 0;
+  const int ntiles = (nkeys + kSubKeys - 1) / kSubKeys;
+  const float *kb = a.k + b * a.kv_batch_stride;
+  const float *vb = a.v + b * a.kv_batch_stride;
+  const uint32_t *kp = a.identity ? nullptr : a.k_pos + b * a.kpos_batch_stride;
+  __syncthreads();
+
+  auto issue = [&](int t) {  // sub-tile t into stage t % kRingStages
+    const int st = t % kRingStages;
+    const int rows = min(kSubKeys, nkeys - t * kSubKeys);
+    const uint32_t bytes = (uint32_t)rows * (uint32_t)dh * 4u;
+    float *dst = ring + (size_t)st * stage_floats;
+    gqd::mbar_arrive_expect_tx(&full[st], 2u * bytes);
+    gqd::bulk_g2s(dst, kb + (j0 + (int64_t)t * kSubKeys) * dh, bytes, &full[st]);
+    gqd::bulk_g2s(dst + kSubKeys * dh, vb + (j0 + (int64_t)t * kSubKeys) * dh, bytes, &full[st]);
+  };
+  if (tid == 0)
+    for (int t = 0; t < min(ntiles, kRingStages); ++t) issue(t);
+
+  const int col = 4 * tid;
+  const bool colv = col < dh;
+  float4 q[kMaxGroup], o[kMaxGroup];
+#pragma unroll
+  for (int g = 0; g < kMaxGroup; ++g) {
+    q[g] = (g < G && colv) ? *reinterpret_cast<const float4 *>(a.q + bt * a.Hq * a.dh + g * a.dh + col)
+                           : make_float4(0.f, 0.f, 0.f, 0.f);
+    o[g] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+
+  int issued = min(ntiles, kRingStages);
+  for (int t = 0; t < ntiles; ++t) {
+    const int st = t % kRingStages;
+    const bool ok = gqd::mbar_wait_bounded(&full[st], (uint32_t)(t / kRingStages) & 1u);
+    if (!ok) abort_flag = 1;
+    __syncthreads();
+    if (abort_flag) break;
+    const float *kt = ring + (size_t)st * stage_floats;
+    const float *vt = kt + kSubKeys * dh;
+    const int rows = min(kSubKeys, nkeys - t * kSubKeys);
+    // scores of the sub-tile
+    float p[kMaxGroup * kKeyBatch];
+    {
+      float4 kv[kKeyBatch];
+#pragma unroll
+      for (int kk = 0; kk < kKeyBatch; ++kk)
+        kv[kk] = (colv && kk < rows) ? *reinterpret_cast<const float4 *>(kt + kk * dh + col) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int g = 0; g < kMaxGroup; ++g)
+#pragma unroll
+        for (int kk = 0; kk < kKeyBatch; ++kk) {
+          float v = __fmul_rn(q[g].x, kv[kk].x);
+          v = __fmaf_rn(q[g].y, kv[kk].y, v);
+          v = __fmaf_rn(q[g].z, kv[kk].z, v);
+          v = __fmaf_rn(q[g].w, kv[kk].w, v);
+          p[g * kKeyBatch + kk] = v;
+        }
+    }
+#pragma unroll
+    for (int off = 16, n = kMaxGroup * kKeyBatch; off >= 1; off >>= 1, n >>= 1) {
+      const bool up = (lane & off) != 0;
+#pragma unroll
+      for (int i = 0; i < n / 2; ++i) {
+        const float send = up ? p[i] : p[i + n / 2];
+        const float keep = up ? p[i + n / 2] : p[i];
+        p[i] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+      }
+    }
+    red[warp][2 * lane] = p[0];
+    red[warp][2 * lane + 1] = p[1];
+    __syncthreads();
+    // online softmax: thread e < 64 owns entry (head g, key kk); 8 lanes per head
+    if (tid < kMaxGroup * kKeyBatch) {
+      const int g = tid / kKeyBatch, kk = tid % kKeyBatch;
+      float sum = 0.0f;
+#pragma unroll
+      for (int w2 = 0; w2 < NWARP; ++w2) sum += red[w2][tid];
+      float sv = -INFINITY;
+      if (g < G && kk < rows) {
+        const int64_t j = j0 + (int64_t)t * kSubKeys + kk;
+        const uint32_t kpos = a.identity ? (uint32_t)j : kp[j];
+        sv = __fmul_rn(sum, a.scale);
+        if (a.softcap > 0.0f) sv = __fmul_rn(a.softcap, tanhf(__fdiv_rn(sv, a.softcap)));
+        if (kpos > qpos || (a.window > 0 && qpos - kpos >= a.window)) sv = -INFINITY;
+      }
+      float mt = sv;
+#pragma unroll
+      for (int off = 4; off >= 1; off >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, off));
+      const float mo = m_run[g];
+      const float mn = fmaxf(mo, mt);
+      const float e = (sv == -INFINITY) ? 0.0f : expf(__fsub_rn(sv, mn));
+      float lt = e;
+#pragma unroll
+      for (int off = 4; off >= 1; off >>= 1) lt += __shfl_xor_sync(0xffffffffu, lt, off);
+      sc[kk][g] = e;
+      if (kk == 0) {
+        const float cf = (mo == -INFINITY) ? 0.0f : expf(__fsub_rn(mo, mn));
+        corr[g] = cf;
+        l_run[g] = __fmaf_rn(l_run[g], cf, lt);
+        m_run[g] = mn;
+      }
+    }
+    __syncthreads();
+    // P.V of the sub-tile, after rescaling the running output
+#pragma unroll
+    for (int g = 0; g < kMaxGroup; ++g) {
+      const float cf = corr[g];
+      o[g] = make_float4(__fmul_rn(o[g].x, cf), __fmul_rn(o[g].y, cf), __fmul_rn(o[g].z, cf), __fmul_rn(o[g].w, cf));
+    }
+#pragma unroll
+    for (int kk = 0; kk < kKeyBatch; ++kk) {
+      if (kk >= rows) break;
+      const float4 vv = colv ? *reinterpret_cast<const float4 *>(vt + kk * dh + col) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+      for (int g = 0; g < kMaxGroup; ++g) {
+        const float pr = sc[kk][g];
+        o[g].x = __fmaf_rn(pr, vv.x, o[g].x);
+        o[g].y = __fmaf_rn(pr, vv.y, o[g].y);
+        o[g].z = __fmaf_rn(pr, vv.z, o[g].z);
+        o[g].w = __fmaf_rn(pr, vv.w, o[g].w);
+      }
+    }
+    __syncthreads();  // stage t and sc are free
+    if (tid == 0 && issued < ntiles) {
+      gqd::fence_proxy_async_smem();
+      issue(issued);
+      ++issued;
+    }
+  }
+
+  if (abort_flag) {
+    // drain the copies still in flight (bounded) before the CTA's shared memory goes away
+    if (tid == 0) {
+      for (int t = max(0, issued - kRingStages); t < issued; ++t)
+        (void)gqd::mbar_wait_bounded(&full[t % kRingStages], (uint32_t)(t / kRingStages) & 1u, 100000000ull);
+      gqd::report(a.err, GQ_DEVERR_WAIT_TIMEOUT);
+    }
+    return;
+  }
+  if (!colv) return;
+#pragma unroll
+  for (int g = 0; g < kMaxGroup; ++g) {
+    if (g >= G) break;
+    if (a.splits == 1) {
+      const float inv = l_run[g] > 0.0f ? __fdiv_rn(1.0f, l_run[g]) : 0.0f;
+      *reinterpret_cast<float4 *>(a.out + bt * a.Hq * a.dh + g * a.dh + col) =
+          make_float4(__fmul_rn(o[g].x, inv), __fmul_rn(o[g].y, inv), __fmul_rn(o[g].z, inv), __fmul_rn(o[g].w, inv));
+    } else {
+      const int64_t prow = (bt * a.Hq + g) * a.splits + blockIdx.x;
+      *reinterpret_cast<float4 *>(a.part_o + prow * a.dh + col) = o[g];
+      if (tid == 0) {
+        a.part_ml[2 * prow] = m_run[g];
+        a.part_ml[2 * prow + 1] = l_run[g];
+      }
+    }
+  }
+}
+
 // Merge the chunks of one (token, head) row: out = sum_s e^(m_s - M) o_s / sum_s e^(m_s - M) l_s.
+// The chunk statistics are read in parallel (one per thread) into shared memory.
+constexpr int kMaxSplits = 256;
 __global__ void attn_combine_kernel(const float *part_o, const float *part_ml, int64_t rows, int64_t Hq, int64_t dh,
                                     int splits, float *out) {
+  __shared__ float wgt[kMaxSplits];
+  __shared__ float wred[8], lred[8];
   gqd::griddep_wait();
   gqd::griddep_launch_dependents();
   const int64_t row = blockIdx.x;  // (token, head)
-  if (row >= rows) return;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
   const float *ml = part_ml + row * splits * 2;
+  float m = -INFINITY, l = 0.0f;
+  for (int s2 = tid; s2 < splits; s2 += blockDim.x) m = fmaxf(m, ml[2 * s2]);
+  m = warp_max(m);
+  if (lane == 0) wred[warp] = m;
+  __syncthreads();
   float M = -INFINITY;
-  for (int s = 0; s < splits; ++s) M = fmaxf(M, ml[2 * s]);
+  for (int i = 0; i < nw; ++i) M = fmaxf(M, wred[i]);
+  for (int s2 = tid; s2 < splits; s2 += blockDim.x) {
+    const float ms = ml[2 * s2];
+    const float w = (ms == -INFINITY) ? 0.0f : expf(__fsub_rn(ms, M));
+    wgt[s2] = w;
+    l += __fmul_rn(w, ml[2 * s2 + 1]);
+  }
+  l = warp_sum(l);
+  if (lane == 0) lred[warp] = l;
+  __syncthreads();
   float L = 0.0f;
-  for (int s = 0; s < splits; ++s)
-    if (ml[2 * s] != -INFINITY) L += __fmul_rn(expf(__fsub_rn(ml[2 * s], M)), ml[2 * s + 1]);
+  for (int i = 0; i < nw; ++i) L += lred[i];
   const float inv = L > 0.0f ? __fdiv_rn(1.0f, L) : 0.0f;
   const int64_t bt = row / Hq, h = row % Hq;
-  for (int64_t c = 4 * threadIdx.x; c < dh; c += 4 * blockDim.x) {
+  for (int64_t c = 4 * tid; c < dh; c += 4 * blockDim.x) {
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int s = 0; s < splits; ++s) {
-      if (ml[2 * s] == -INFINITY) continue;
-      const float wgt = expf(__fsub_rn(ml[2 * s], M));
-      const float4 v = *reinterpret_cast<const float4 *>(part_o + (row * splits + s) * dh + c);
-      acc.x = __fmaf_rn(wgt, v.x, acc.x);
-      acc.y = __fmaf_rn(wgt, v.y, acc.y);
-      acc.z = __fmaf_rn(wgt, v.z, acc.z);
-      acc.w = __fmaf_rn(wgt, v.w, acc.w);
+    const float *po = part_o + row * splits * dh + c;
+#pragma unroll 4
+    for (int s2 = 0; s2 < splits; ++s2) {
+      const float w = wgt[s2];
+      const float4 v = *reinterpret_cast<const float4 *>(po + (int64_t)s2 * dh);
+      acc.x = __fmaf_rn(w, v.x, acc.x);
+      acc.y = __fmaf_rn(w, v.y, acc.y);
+      acc.z = __fmaf_rn(w, v.z, acc.z);
+      acc.w = __fmaf_rn(w, v.w, acc.w);
     }
     *reinterpret_cast<float4 *>(out + bt * Hq * dh + h * dh + c) =
         make_float4(__fmul_rn(acc.x, inv), __fmul_rn(acc.y, inv), __fmul_rn(acc.z, inv), __fmul_rn(acc.w, inv));
@@ -491,9 +849,41 @@ unsigned blocks_for(gq_ctx *ctx, int64_t work, int threads) {
     if (_rc != GQ_OK) return _rc;            \
   } while (0)
 
+template <int KIND>
+cudaError_t norm_reg_launch(gq_ctx *ctx, int vpl, dim3 grid, const float *x, const float *r, const float *w,
+                            const float *s, int64_t rows, int64_t d, float eps, float *y, RowMap ym) {
+  const dim3 blk(kNormThreads);
+  switch (vpl) {
+    case 1: return gq_launch(ctx, rmsnorm_reg_kernel<KIND, 1>, grid, blk, 0, x, r, w, s, rows, d, eps, y, ym);
+    case 2: return gq_launch(ctx, rmsnorm_reg_kernel<KIND, 2>, grid, blk, 0, x, r, w, s, rows, d, eps, y, ym);
+    case 4: return gq_launch(ctx, rmsnorm_reg_kernel<KIND, 4>, grid, blk, 0, x, r, w, s, rows, d, eps, y, ym);
+    case 8: return gq_launch(ctx, rmsnorm_reg_kernel<KIND, 8>, grid, blk, 0, x, r, w, s, rows, d, eps, y, ym);
+    case 12: return gq_launch(ctx, rmsnorm_reg_kernel<KIND, 12>, grid, blk, 0, x, r, w, s, rows, d, eps, y, ym);
+    default: return gq_launch(ctx, rmsnorm_reg_kernel<KIND, 16>, grid, blk, 0, x, r, w, s, rows, d, eps, y, ym);
+  }
+}
+
+// float4 per lane for a register-resident row of d values (0: use the strided kernel)
+int reg_vpl(int64_t d) {
+  const int64_t need = (d + 127) / 128;
+  for (int v : {1, 2, 4, 8, 12, 16})
+    if (need <= v) return v;
+  return 0;
+}
+
 int norm_launch(gq_ctx *ctx, int kind, const float *x, const float *r, const float *w, const float *s, int64_t rows,
                 int64_t d, float eps, float *y, RowMap ym) {
   const dim3 grid((unsigned)((rows + kNormThreads / 32 - 1) / (kNormThreads / 32)));
+  const int vpl = reg_vpl(d);
+  const bool aligned = d % 4 == 0 && ((uintptr_t)x | (uintptr_t)y | (uintptr_t)w | (uintptr_t)r) % 16 == 0 &&
+                       (ym.group_stride % 4 == 0) && (ym.inner_stride % 4 == 0);
+  if (vpl && aligned) {
+    if (kind == 0)
+      GQ_CUDA_TRY(ctx, norm_reg_launch<0>(ctx, vpl, grid, x, r, w, s, rows, d, eps, y, ym));
+    else
+      GQ_CUDA_TRY(ctx, norm_reg_launch<1>(ctx, vpl, grid, x, r, w, s, rows, d, eps, y, ym));
+    return GQ_OK;
+  }
   if (kind == 0)
     GQ_CUDA_TRY(ctx, gq_launch(ctx, rmsnorm_kernel<0>, grid, dim3(kNormThreads), 0, x, r, w, s, rows, d, eps, y, ym));
   else
@@ -516,6 +906,23 @@ int rope_launch(gq_ctx *ctx, bool norm, const float *x, const float *w, int64_t 
   const int64_t rows = t * heads;
   const RowMap ym{heads, y_tok_stride, dh};
   const dim3 grid((unsigned)((rows + kNormThreads / 32 - 1) / (kNormThreads / 32)));
+  const int vpl = reg_vpl(dh);
+  const bool aligned = dh % 4 == 0 && ((uintptr_t)x % 16 == 0) && (!norm || (uintptr_t)w % 16 == 0);
+  if (aligned && vpl && vpl <= 4) {
+    cudaError_t e;
+    const dim3 blk(kNormThreads);
+    if (norm) {
+      e = vpl == 1 ? gq_launch(ctx, head_rope_reg_kernel<true, 1>, grid, blk, 0, x, w, rows, heads, dh, eps, positions, half, fr, y, ym)
+        : vpl == 2 ? gq_launch(ctx, head_rope_reg_kernel<true, 2>, grid, blk, 0, x, w, rows, heads, dh, eps, positions, half, fr, y, ym)
+                   : gq_launch(ctx, head_rope_reg_kernel<true, 4>, grid, blk, 0, x, w, rows, heads, dh, eps, positions, half, fr, y, ym);
+    } else {
+      e = vpl == 1 ? gq_launch(ctx, head_rope_reg_kernel<false, 1>, grid, blk, 0, x, w, rows, heads, dh, eps, positions, half, fr, y, ym)
+        : vpl == 2 ? gq_launch(ctx, head_rope_reg_kernel<false, 2>, grid, blk, 0, x, w, rows, heads, dh, eps, positions, half, fr, y, ym)
+                   : gq_launch(ctx, head_rope_reg_kernel<false, 4>, grid, blk, 0, x, w, rows, heads, dh, eps, positions, half, fr, y, ym);
+    }
+    GQ_CUDA_TRY(ctx, e);
+    return GQ_OK;
+  }
   if (norm)
     GQ_CUDA_TRY(ctx, gq_launch(ctx, head_rope_kernel<true>, grid, dim3(kNormThreads), 0, x, w, rows, heads, dh, eps,
                                positions, half, fr, y, ym));
@@ -528,6 +935,19 @@ int rope_launch(gq_ctx *ctx, bool norm, const float *x, const float *w, int64_t 
 template <int NT>
 cudaError_t attn_launch_nt(gq_ctx *ctx, dim3 grid, const AttnArgs &a) {
   return gq_launch(ctx, attn_chunk_kernel<NT>, grid, dim3(NT), 0, a);
+}
+
+template <int NT>
+cudaError_t attn_ring_launch_nt(gq_ctx *ctx, dim3 grid, const AttnArgs &a, size_t smem) {
+  static bool attr_set[64] = {};
+  const int dev = ctx->device & 63;
+  if (!attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(attn_ring_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)(2 * kRingStages * kSubKeys * 4 * NT * 4));
+    if (e != cudaSuccess) return e;
+    attr_set[dev] = true;
+  }
+  return gq_launch(ctx, attn_ring_kernel<NT>, grid, dim3(NT), smem, a);
 }
 
 }  // namespace
@@ -579,7 +999,7 @@ int gq_attention(gq_ctx *ctx, const float *q, int64_t batch, int64_t t, int64_t 
   if (head_dim % 4 != 0 || head_dim > 4 * 256)
     return gq_fail(ctx, GQ_ERR_UNSUPPORTED, "attention: head_dim must be a multiple of 4, at most 1024");
   if (batch * t == 0) return GQ_OK;
-  if (!q || !out || !q_pos || (s > 0 && (!k || !v || !k_pos)))
+  if (!q || !out || !q_pos || (s > 0 && (!k || !v || (!k_pos && !(flags & GQ_ATTN_KPOS_IDENTITY)))))
     return gq_fail(ctx, GQ_ERR_INVALID_ARGUMENT, "attention: null pointer");
   if (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)out) % 16 != 0 || kv_batch_stride % 4 != 0)
     return gq_fail(ctx, GQ_ERR_INVALID_ARGUMENT,
@@ -601,15 +1021,31 @@ int gq_attention(gq_ctx *ctx, const float *q, int64_t batch, int64_t t, int64_t 
   a.scale = scale;
   a.softcap = attn_softcap;
   a.window = sliding_window;
-  a.sorted = (flags & GQ_ATTN_KPOS_ASCENDING) ? 1 : 0;
+  a.identity = (flags & GQ_ATTN_KPOS_IDENTITY) ? 1 : 0;
+  a.sorted = (a.identity || (flags & GQ_ATTN_KPOS_ASCENDING)) ? 1 : 0;
   // keys a query can reach: the window bounds the range when positions ascend
+  a.err = ctx->dev_err;
   const int64_t active = (a.sorted && sliding_window > 0) ? std::min<int64_t>(s, sliding_window) : s;
   const int64_t rows = batch * t * hkv;
-  int chunk = 32;
-  while (chunk < kMaxChunk && rows * ((active + chunk - 1) / chunk) > 4 * (int64_t)ctx->num_sms * 4) chunk *= 2;
+  if (rows > 65535) return gq_fail(ctx, GQ_ERR_UNSUPPORTED, "attention: more than 65535 (token, kv head) rows");
+  // One KV head with its rows contiguous (kv row stride == head_dim): stream key
+  // chunks through the shared-memory ring; chunks sized for ~4 CTAs per SM.
+  const bool ring = hkv == 1 && a.sorted && head_dim <= 512;
+  int chunk;
+  if (ring) {
+    const int64_t target = 4 * (int64_t)ctx->num_sms;
+    int64_t per = (rows * active + target - 1) / target;  // keys per CTA for `target` CTAs
+    per = std::max<int64_t>(16, (per + kSubKeys - 1) / kSubKeys * kSubKeys);
+    per = std::max<int64_t>(per, (active + kMaxSplits - 1) / kMaxSplits);
+    chunk = (int)std::min<int64_t>(per, 1 << 30);
+  } else {
+    chunk = 32;
+    while (chunk < kMaxChunk && rows * ((active + chunk - 1) / chunk) > 4 * (int64_t)ctx->num_sms * 4) chunk *= 2;
+    if ((active + chunk - 1) / chunk > kMaxSplits)
+      return gq_fail(ctx, GQ_ERR_UNSUPPORTED, "attention: key range too long for the generic kernel");
+  }
   a.chunk = chunk;
   a.splits = (int)std::max<int64_t>(1, (active + chunk - 1) / chunk);
-  if (rows > 65535) return gq_fail(ctx, GQ_ERR_UNSUPPORTED, "attention: more than 65535 (token, kv head) rows");
   if (a.splits > 1) {
     const size_t orow = (size_t)(batch * t * hq) * a.splits;
     void *ws = nullptr;
@@ -621,7 +1057,14 @@ int gq_attention(gq_ctx *ctx, const float *q, int64_t batch, int64_t t, int64_t 
   const dim3 grid((unsigned)a.splits, (unsigned)rows);
   const int nt = head_dim <= 128 ? 32 : head_dim <= 256 ? 64 : head_dim <= 512 ? 128 : 256;
   cudaError_t e;
-  switch (nt) {
+  if (ring) {
+    const size_t smem = (size_t)2 * kRingStages * kSubKeys * head_dim * 4;
+    // at least two warps: the softmax step gives one thread to each of the 64 (head, key) entries
+    if (head_dim <= 256)
+      e = attn_ring_launch_nt<64>(ctx, grid, a, smem);
+    else
+      e = attn_ring_launch_nt<128>(ctx, grid, a, smem);
+  } else switch (nt) {
     case 32: e = attn_launch_nt<32>(ctx, grid, a); break;
     case 64: e = attn_launch_nt<64>(ctx, grid, a); break;
     case 128: e = attn_launch_nt<128>(ctx, grid, a); break;

@@ -141,6 +141,12 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
       : "memory");
 }
 
+// Order this thread's earlier shared-memory accesses before later async-proxy
+// (bulk copy) writes to the same shared memory.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 __device__ __forceinline__ void report(uint32_t *err, uint32_t bits) {
   if (err) atomicOr(err, bits);
 }

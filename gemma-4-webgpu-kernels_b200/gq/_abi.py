@@ -96,6 +96,7 @@ SIGNATURES = {
 }
 
 GQ_ATTN_KPOS_ASCENDING = 0x1
+GQ_ATTN_KPOS_IDENTITY = 0x2
 
 _lib = None
 

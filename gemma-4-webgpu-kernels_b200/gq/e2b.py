@@ -32,7 +32,7 @@ from typing import Dict, List, Optional, Tuple
 import numpy as np
 
 from . import QuantWeight, synth
-from ._abi import GQ_ATTN_KPOS_ASCENDING, GqError
+from ._abi import GQ_ATTN_KPOS_IDENTITY, GqError
 
 
 @dataclass
@@ -353,8 +353,8 @@ class Decoder:
                 add(pre + "v_norm", lib.gq_rms_norm, ctx, V(self.vn), B, dh, None, eps,
                     c_void_p(vc.data_ptr() + 4 * p * kvd), cstride)
             add(pre + "attention", lib.gq_attention, ctx, V(self.qr), B, 1, c.heads_q, dh, V(kc), V(vc), S,
-                c.heads_kv, cstride, V(self.pos), V(self.kpos), 0, c_float(1.0), c.window_of(i), c_float(0.0),
-                GQ_ATTN_KPOS_ASCENDING, V(self.attn))
+                c.heads_kv, cstride, V(self.pos), None, 0, c_float(1.0), c.window_of(i), c_float(0.0),
+                GQ_ATTN_KPOS_IDENTITY, V(self.attn))
             add(pre + "o_proj", lib.gq_linear, ctx, V(self.attn), B, c.heads_q * dh, Q(pre + "o_proj"), V(self.o))
             add(pre + "post_attn", lib.gq_add_rms_norm, ctx, V(self.h), V(self.o), B, H, F(pre + "post_attn_ln"), eps,
                 None, V(self.h))

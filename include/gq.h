@@ -207,6 +207,9 @@ int gq_rope(gq_ctx *ctx, const float *x, int64_t t, int64_t heads, int64_t head_
 /* Key positions are strictly ascending (a KV cache's are): the causal and sliding-window
  * bounds are then found by binary search and masked keys are never read. */
 #define GQ_ATTN_KPOS_ASCENDING 0x1u
+/* Key j is at position j (k_pos may be NULL): a KV cache indexed by position. The
+ * visible range is then computed without reading k_pos. Implies ascending. */
+#define GQ_ATTN_KPOS_IDENTITY 0x2u
 
 /* Backend::attention (rust/src/backend.rs:120-121; CPU rust/src/backend_cpu.rs:270-336),
  * over `batch` independent sequences: q [batch, t, hq, head_dim], k and v of sequence b

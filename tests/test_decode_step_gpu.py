@@ -15,7 +15,7 @@ import numpy as np
 import pytest
 
 from gq import AttnOpts, CudaBackend, e2b, synth
-from gq._abi import GQ_ATTN_KPOS_ASCENDING
+from gq._abi import GQ_ATTN_KPOS_ASCENDING, GQ_ATTN_KPOS_IDENTITY
 from oracle import e2b_ref
 from oracle import oracle as o
 
@@ -114,8 +114,10 @@ def test_attention_unsorted_positions_and_softcap(g):
     assert rel(got, o.attention(q, k, v, qp, kp, 0.5, 10, 5.0)) <= ATTN_REL
 
 
-@pytest.mark.parametrize("batch,s,dh,window", [(4, 2048, 512, 0), (4, 2048, 256, 512), (64, 300, 256, 0)])
-def test_attention_batched_kv_cache(g, batch, s, dh, window):
+@pytest.mark.parametrize("flags", [GQ_ATTN_KPOS_ASCENDING, GQ_ATTN_KPOS_IDENTITY])
+@pytest.mark.parametrize("batch,s,dh,window", [(4, 2048, 512, 0), (4, 2048, 256, 512), (64, 300, 256, 0),
+                                               (2, 100, 256, 512), (3, 40, 64, 16)])
+def test_attention_batched_kv_cache(g, batch, s, dh, window, flags):
     """The decode layout: `batch` sequences, each a [capacity, dh] cache, one query each."""
     import torch
 
@@ -132,7 +134,8 @@ def test_attention_batched_kv_cache(g, batch, s, dh, window):
     lib = g.lib
     rc = lib.gq_attention(g.ctx, c_void_p(tq.data_ptr()), batch, 1, hq, dh, c_void_p(tk.data_ptr()),
                           c_void_p(tv.data_ptr()), s, 1, cap * dh, c_void_p(qpos.data_ptr()),
-                          c_void_p(kpos.data_ptr()), 0, c_float(1.0), window, c_float(0.0), GQ_ATTN_KPOS_ASCENDING,
+                          c_void_p(kpos.data_ptr()) if flags == GQ_ATTN_KPOS_ASCENDING else None, 0, c_float(1.0),
+                          window, c_float(0.0), flags,
                           c_void_p(out.data_ptr()))
     g._check(rc, "attention")
     g.flush()
