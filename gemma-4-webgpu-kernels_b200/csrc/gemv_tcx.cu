@@ -1,24 +1,28 @@
-// gemv_tcx.cu — short-M GEMV (3 <= M <= 16 activation rows) on the tensor cores.
+// gemv_tcx.cu — short-M GEMV (3 <= M <= 64 activation rows) on the tensor cores.
 //
 // The same exact integer dot products as gemv_tc.cu (tcgen05.mma.kind::i8 on
-// four signed byte limbs of x in 30-bit fixed point), for the M = 3..16 rows of
-// a short decode batch or a speculative chunk (rust/src/backend_wgpu.rs:646-695
-// sends M <= 15 to MATMUL_Q, rust/src/kernels/matmul_q.wgsl:96-169):
+// four signed byte limbs of x in 30-bit fixed point), for the M = 3..64 rows of
+// a decode batch (rust/src/backend_wgpu.rs:646-695 sends M <= 15 to MATMUL_Q,
+// rust/src/kernels/matmul_q.wgsl:96-169; BASELINE config 5 decodes 64 sequences):
 //  * a pre-pass kernel (one block per activation row) writes the limbs of all M
 //    rows once, as a [4*M, Kp] s8 matrix in global memory (row = token*4 + limb,
 //    K permuted inside each 16-code group like the widened weights), plus each
 //    row's exponent, sum of fixed-point values and a non-finite flag;
-//  * the GEMV streams that matrix by TMA, one 64-row x 128-byte swizzled tile per
-//    K-block (rows past 4*M arrive zero-filled), as the A operand of an M = 64
-//    MMA: accumulator row r sits in TMEM lane 32*(r/16) + r%16, so lane quarter q
-//    holds the four limbs of tokens 4q .. 4q+3 in its lanes 0-15;
+//  * the GEMV streams that matrix by TMA, one swizzled tile of 64 / 128 / 256 limb
+//    rows x 128 bytes per K-block, as the A operand: one M = 64 MMA for up to 16
+//    tokens (accumulator row r in TMEM lane 32*(r/16) + r%16), else one or two
+//    M = 128 MMAs (row r of half h in lane r of that half's accumulator);
 //  * weights are the B operand exactly as in gemv_tc.cu (I8 rows straight from
 //    TMA into the swizzled layout, sub-byte and U8 codes widened by 4 warps), one
-//    tile of up to 256 rows per CTA, K-blocks dealt round-robin to three issuing
-//    threads with separate accumulators;
-//  * epilogue warp q recombines the limbs of its four tokens in int64, removes
-//    the zero point exactly and converts once: y = f32(T * 2^-s_m) * scale[n].
-// The limb matrix is tiny and shared by every CTA, so after the first CTAs it
+//    tile of up to 256 rows per CTA, K-blocks dealt round-robin to up to three
+//    issuing threads with separate accumulators; weights taller than one tile
+//    per SM are processed as row slices, one launch each, sharing the limbs;
+//  * the tile's scales come into shared memory by one bulk copy issued before
+//    the grid dependency wait;
+//  * epilogue warp q drains lane quarter q, recombines the limbs of each token in
+//    int64, removes the zero point exactly and converts once:
+//    y = f32(T * 2^-s_m) * scale[n].
+// The limb matrix is small and shared by every CTA, so after the first CTAs it
 // streams from L2; the weights stream from HBM once for all M rows.
 // Every wait is bounded (GQ_DEVERR_WAIT_TIMEOUT); TMA copies in flight are
 // drained, outstanding MMAs committed and TMEM freed before the CTA exits.
@@ -36,12 +40,11 @@ constexpr int kThreads = 256;  // warp 0 TMA, warps 1-3 MMA issue, warps 4-7 exp
 constexpr int kKB = 128;       // codes per K-block
 constexpr int kMaxRaw = 8;
 constexpr int kMaxMma = 48;    // widened ring: up to every K-block of K = 6144
-constexpr int kMaxXa = 8;      // A (limb) tile ring
+constexpr int kMaxXa = 24;     // A (limb) tile ring, all issuers together
 constexpr int kMaxIss = 3;
 constexpr int kExpWarps = 4;
-constexpr int kMaxTok = 16;
+constexpr int kMaxTok = 64;
 constexpr int kMaxK = 8192;
-constexpr uint32_t XA_TILE = 64 * 128;  // 64 limb rows x one K-block
 
 struct TcxArgs {
   int M, K, N;
@@ -55,27 +58,29 @@ struct TcxArgs {
   const int *xexp;        // [M] per-row exponent s_m (X = rint(x * 2^s_m))
   const long long *sumx;  // [M] sum_k X
   const uint32_t *bad;    // [M] non-finite x row
-  int tile_rows;          // MMA N: multiple of 16, <= 256 / NW
+  int tile_rows;          // MMA N: multiple of 16
+  int mh;                 // 0: one M=64 MMA (<= 16 tokens); 1 or 2: M=128 halves
   int kblocks, kbr;
-  int raw_stages, mma_stages, xa_stages;
-  int raw_bytes, mma_bytes;
+  int raw_stages, mma_stages, xa_stages, xi, xi_log2;
+  int raw_bytes, mma_bytes, xa_tile;
   int issuers;
   int tmem_cols;
   uint32_t *err;
 };
 
 struct TcxSmem {
-  uint32_t xa_off, raw_off, mma_off, bar_off, misc_off, total;
+  uint32_t xa_off, raw_off, mma_off, sc_off, bar_off, misc_off, total;
 };
-__host__ __device__ inline TcxSmem tcx_layout(int xa_stages, int raw_stages, int raw_bytes, int mma_stages,
-                                              int mma_bytes) {
+__host__ __device__ inline TcxSmem tcx_layout(int xa_stages, int xa_tile, int raw_stages, int raw_bytes,
+                                              int mma_stages, int mma_bytes, int sc_bytes) {
   TcxSmem L;
   uint32_t o = 0;
-  L.xa_off = o;   o += (uint32_t)xa_stages * XA_TILE;
+  L.xa_off = o;   o += (uint32_t)xa_stages * (uint32_t)xa_tile;
   L.raw_off = o;  o += (uint32_t)raw_stages * (uint32_t)raw_bytes;
   L.mma_off = o;  o += (uint32_t)mma_stages * (uint32_t)mma_bytes;
-  L.bar_off = o;  o += (2 * kMaxRaw + 2 * kMaxMma + 2 * kMaxXa + 2 * kMaxIss) * 8;
-  L.misc_off = o; o += 64;
+  L.sc_off = o;   o += (uint32_t)((sc_bytes + 127) & ~127);
+  L.bar_off = o;  o += (2 * kMaxRaw + 2 * kMaxMma + 2 * kMaxXa + 2 * kMaxIss + 2) * 8;
+  L.misc_off = o; o += 64 + kMaxTok * 24;
   L.total = o + 1024;
   return L;
 }
@@ -95,6 +100,8 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
 __device__ __forceinline__ bool wait_phase(uint64_t *bar, uint32_t parity) {
   return gqd::mbar_try_wait(bar, parity) || gqd::mbar_wait_bounded(bar, parity);
 }
+// barrier among the 4 expander/epilogue warps only
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, %0;" ::"r"(kExpWarps * 32) : "memory"); }
 
 // ---- pre-pass: x row m -> 30-bit fixed point -> four s8 limb rows ------------
 // Same arithmetic as the in-CTA staging of gemv_tc.cu: s = 30 - e with
@@ -185,6 +192,9 @@ __global__ void xlimbs_kernel(const float *x, int K, int Kp, uint8_t *limbs, int
 }
 
 // ---- the GEMV -------------------------------------------------------------------
+// Control flow is division-free in the steady state (ring slots and phases are
+// stepped incrementally): the producer and issuer threads run one K-block every
+// few tens of cycles, so they never pace the pipeline.
 template <int BITS, bool SIGNED, int MODE>
 __global__ void __launch_bounds__(kThreads, 1)
     gemv_tcx_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_w2,
@@ -194,16 +204,20 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int KB_BYTES = kKB * BITS / 8;
   constexpr int CPR = KB_BYTES / 16;
   constexpr long long ZP = (BITS == 8) ? 0 : (1 << (BITS - 1));
-  // D = A * B^T: A = 64 limb rows (s8, M = 64), B = weight rows (s8, N = tile_rows), D s32.
+  constexpr int kBars = 2 * kMaxRaw + 2 * kMaxMma + 2 * kMaxXa + 2 * kMaxIss + 1;
+  const int MH = a.mh > 0 ? a.mh : 1;  // accumulator halves
+  // D = A * B^T: A = limb rows (s8, M = 64 or 128), B = weight rows (s8, N = tile_rows), D s32.
   const uint32_t idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(a.tile_rows >> 3) << 17) |
-                         ((uint32_t)(64 >> 4) << 24);
+                         ((uint32_t)((a.mh == 0 ? 64 : 128) >> 4) << 24);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const TcxSmem L = tcx_layout(a.xa_stages, a.raw_stages, a.raw_bytes, a.mma_stages, a.mma_bytes);
-  uint8_t *xa = smem + L.xa_off;    // [xa_stages][64 x 128 B], swizzled (TMA)
+  const TcxSmem L = tcx_layout(a.xa_stages, a.xa_tile, a.raw_stages, a.raw_bytes, a.mma_stages, a.mma_bytes,
+                               NW * a.tile_rows * 4);
+  uint8_t *xa = smem + L.xa_off;    // [xa_stages][xa_rows x 128 B], swizzled (TMA)
   uint8_t *raw = smem + L.raw_off;  // [raw_stages][raw_bytes]
   uint8_t *wid = smem + L.mma_off;  // [mma_stages][NW][tile_rows x 128 B], swizzled
+  float *scb = reinterpret_cast<float *>(smem + L.sc_off);  // [NW][tile_rows]
   uint64_t *raw_full = reinterpret_cast<uint64_t *>(smem + L.bar_off);
   uint64_t *raw_empty = raw_full + kMaxRaw;
   uint64_t *mma_full = raw_empty + kMaxRaw;
@@ -212,41 +226,35 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t *xa_empty = xa_full + kMaxXa;
   uint64_t *acc_full = xa_empty + kMaxXa;  // [kMaxIss]
   uint64_t *done_bar = acc_full + kMaxIss;  // [kMaxIss]
+  uint64_t *sc_bar = done_bar + kMaxIss;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + L.misc_off);
   volatile uint32_t *abort_flag = tmem_slot + 1;
+  double *tok_pw = reinterpret_cast<double *>(smem + L.misc_off + 64);  // [kMaxTok] 2^-s
+  long long *tok_zc = reinterpret_cast<long long *>(tok_pw + kMaxTok);  // [kMaxTok] ZP * sum X
+  uint32_t *tok_bad = reinterpret_cast<uint32_t *>(tok_zc + kMaxTok);   // [kMaxTok]
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n_begin = blockIdx.x * a.tile_rows;
   const int n_end = min(a.N, n_begin + a.tile_rows);
-  const int kblocks = a.kblocks, kbr = a.kbr, RS = a.raw_stages, MS = a.mma_stages, XS = a.xa_stages;
-  const int NI = a.issuers;
+  const int kblocks = a.kblocks, kbr = a.kbr, RS = a.raw_stages, MS = a.mma_stages;
+  const int NI = a.issuers, XI = a.xi, XL = a.xi_log2;
   const int total_raw = (kblocks + kbr - 1) / kbr;
   const int tile_bytes = a.tile_rows * 128;
+  const uint32_t xa_tile = (uint32_t)a.xa_tile;
 
-  if (tid == 0) {
-    for (int i = 0; i < kMaxRaw; ++i) {
-      gqd::mbar_init(&raw_full[i], 1);
-      gqd::mbar_init(&raw_empty[i], DIRECT ? 1 : kExpWarps);
-    }
-    for (int i = 0; i < kMaxMma; ++i) {
-      gqd::mbar_init(&mma_full[i], kExpWarps);
-      gqd::mbar_init(&mma_empty[i], 1);
-    }
-    for (int i = 0; i < kMaxXa; ++i) {
-      gqd::mbar_init(&xa_full[i], 1);
-      gqd::mbar_init(&xa_empty[i], 1);
-    }
-    for (int i = 0; i < kMaxIss; ++i) {
-      gqd::mbar_init(&acc_full[i], 1);
-      gqd::mbar_init(&done_bar[i], 1);
-    }
-    *abort_flag = 0;
+  // one barrier per thread (all the arrays are contiguous from raw_full)
+  if (tid < kBars) {
+    uint32_t cnt = 1;
+    if (!DIRECT && tid >= kMaxRaw && tid < 2 * kMaxRaw) cnt = kExpWarps;  // raw_empty: each widening warp
+    if (!DIRECT && tid >= 2 * kMaxRaw && tid < 2 * kMaxRaw + kMaxMma) cnt = kExpWarps;  // mma_full: likewise
+    gqd::mbar_init(raw_full + tid, cnt);
     gqd::fence_mbar_init();
   }
+  if (tid == 0) *abort_flag = 0;
   __syncthreads();
 
-  auto issue = [&](int r) {  // raw stage r: K-blocks r*kbr .. +kbr-1
-    const int slot = r % RS, kb0 = r * kbr;
+  auto issue = [&](int r, int slot) {  // raw stage r (K-blocks r*kbr .. +kbr-1) into `slot`
+    const int kb0 = r * kbr;
     uint8_t *dst = raw + slot * a.raw_bytes;
     if (DIRECT) {
       const int nkb = min(kbr, kblocks - kb0);
@@ -262,12 +270,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                     &raw_full[slot]);
     }
   };
-  // The limb ring is split per issuer (XI slots each) so every slot is filled
-  // and consumed in order by one producer and one consumer: a waiter then never
-  // asks for a phase two completions ahead of the barrier (which an mbarrier
-  // parity wait would report as already complete).
-  const int XI = XS / NI;
-  auto x_owner = [&](int g, int &ord) {  // issuer of K-block g and its ordinal there
+  // The limb ring is split per issuer (XI slots each, a power of two) so every
+  // slot is filled and consumed in order by one producer and one consumer: a
+  // waiter then never asks for a phase two completions ahead of the barrier
+  // (which an mbarrier parity wait would report as already complete).
+  // K-block g belongs to issuer own(g) as its ord(g)-th K-block: whole raw
+  // stages round-robin for I8 (stage u -> issuer u % NI), single K-blocks otherwise.
+  auto x_owner = [&](int g, int &ord) {  // (abort path only; the loops step these incrementally)
     if (DIRECT) {
       const int u = g / kbr;
       ord = (u / NI) * kbr + g % kbr;
@@ -277,74 +286,91 @@ __global__ void __launch_bounds__(kThreads, 1)
     return g % NI;
   };
   auto issue_x = [&](int slot, int g) {  // limb tile of K-block g
-    gqd::mbar_arrive_expect_tx(&xa_full[slot], XA_TILE);
-    tma_load_2d(xa + slot * XA_TILE, &map_x, g * kKB, 0, &xa_full[slot]);
+    gqd::mbar_arrive_expect_tx(&xa_full[slot], xa_tile);
+    tma_load_2d(xa + (size_t)slot * xa_tile, &map_x, g * kKB, 0, &xa_full[slot]);
   };
 
-  // Widen K-block g into slot g % MS (warp-uniform; false on a timed-out wait).
-  auto expand = [&](int g) -> bool {
-    const int et = tid - (kThreads - kExpWarps * 32);
-    const int r = g / kbr, rslot = r % RS, j = g % kbr, mslot = g % MS;
-    bool ok = !*abort_flag && wait_phase(&raw_full[rslot], (uint32_t)(r / RS) & 1u);
-    ok = ok && (g < MS || wait_phase(&mma_empty[mslot], (uint32_t)((g / MS) - 1) & 1u));
-    if (!__all_sync(0xffffffffu, ok)) return false;
+  // ---- widening of sub-byte / U8 codes: the 4 warps widen one raw stage at a time ----
+  // Stages are widened in order by all four warps together, so every wait is for
+  // the next phase of its barrier (never two phases ahead).
+  const int ew = warp - (kThreads / 32 - kExpWarps);  // expander warp index (valid for warps 4-7)
+  const int et = tid - (kThreads - kExpWarps * 32);   // expander thread index
+  int er = 0, erslot = 0, erk = 0;   // next raw stage to widen
+  int emslot = 0, emk = 0;           // widened-ring slot of its first K-block and its use count
+  // Widen raw stage er (warp-uniform; false on a timed-out wait).
+  auto expand_stage = [&]() -> bool {
+    const int g0 = er * kbr, nkb = min(kbr, kblocks - g0);
+    if (!__all_sync(0xffffffffu, wait_phase(&raw_full[erslot], (uint32_t)erk & 1u))) return false;
     const int rstride = kbr * KB_BYTES;
-    const int items = NW * a.tile_rows * CPR;
-    for (int it = et; it < items; it += kExpWarps * 32) {
-      const int h = it / (a.tile_rows * CPR);
-      const int rem = it - h * (a.tile_rows * CPR);
-      const int row = rem / CPR, ic = rem - row * CPR;
-      const uint4 in = *reinterpret_cast<const uint4 *>(raw + rslot * a.raw_bytes + h * a.tile_rows * rstride +
-                                                         row * rstride + j * KB_BYTES + ic * 16);
-      uint8_t *dst = wid + mslot * a.mma_bytes + h * tile_bytes;
-      if constexpr (BITS == 4) {
-        const uint32_t m = 0x0F0F0F0Fu;
-        *reinterpret_cast<uint4 *>(dst + sw128_off(row, 2 * ic)) =
-            make_uint4(in.x & m, (in.x >> 4) & m, in.y & m, (in.y >> 4) & m);
-        *reinterpret_cast<uint4 *>(dst + sw128_off(row, 2 * ic + 1)) =
-            make_uint4(in.z & m, (in.z >> 4) & m, in.w & m, (in.w >> 4) & m);
-      } else if constexpr (BITS == 2) {
-        const uint32_t m = 0x03030303u;
-        const uint32_t w4[4] = {in.x, in.y, in.z, in.w};
+    const uint8_t *src0 = raw + erslot * a.raw_bytes;
+    for (int j = 0; j < nkb; ++j) {
+      // the slot's previous K-block must have been consumed by its MMAs
+      if (!__all_sync(0xffffffffu, emk == 0 || wait_phase(&mma_empty[emslot], (uint32_t)(emk - 1) & 1u)))
+        return false;
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
-          *reinterpret_cast<uint4 *>(dst + sw128_off(row, 4 * ic + q)) =
-              make_uint4(w4[q] & m, (w4[q] >> 2) & m, (w4[q] >> 4) & m, (w4[q] >> 6) & m);
-      } else {
-        const uint32_t f = 0x80808080u;
-        *reinterpret_cast<uint4 *>(dst + sw128_off(row, ic)) = make_uint4(in.x ^ f, in.y ^ f, in.z ^ f, in.w ^ f);
+      for (int h = 0; h < NW; ++h) {
+        const uint8_t *src = src0 + h * a.tile_rows * rstride + j * KB_BYTES;
+        uint8_t *dst = wid + emslot * a.mma_bytes + h * tile_bytes;
+        for (int it = et; it < a.tile_rows * CPR; it += kExpWarps * 32) {
+          const int row = it / CPR, ic = it % CPR;  // CPR is a compile-time power of two
+          const uint4 in = *reinterpret_cast<const uint4 *>(src + row * rstride + ic * 16);
+          if constexpr (BITS == 4) {
+            const uint32_t m = 0x0F0F0F0Fu;
+            *reinterpret_cast<uint4 *>(dst + sw128_off(row, 2 * ic)) =
+                make_uint4(in.x & m, (in.x >> 4) & m, in.y & m, (in.y >> 4) & m);
+            *reinterpret_cast<uint4 *>(dst + sw128_off(row, 2 * ic + 1)) =
+                make_uint4(in.z & m, (in.z >> 4) & m, in.w & m, (in.w >> 4) & m);
+          } else if constexpr (BITS == 2) {
+            const uint32_t m = 0x03030303u;
+            const uint32_t w4[4] = {in.x, in.y, in.z, in.w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              *reinterpret_cast<uint4 *>(dst + sw128_off(row, 4 * ic + q)) =
+                  make_uint4(w4[q] & m, (w4[q] >> 2) & m, (w4[q] >> 4) & m, (w4[q] >> 6) & m);
+          } else {
+            const uint32_t f = 0x80808080u;
+            *reinterpret_cast<uint4 *>(dst + sw128_off(row, ic)) = make_uint4(in.x ^ f, in.y ^ f, in.z ^ f, in.w ^ f);
+          }
+        }
       }
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&mma_full[emslot]);
+      if (++emslot == MS) { emslot = 0; ++emk; }
     }
-    fence_proxy_async();
-    __syncwarp();
-    if (lane == 0) {
-      mbar_arrive(&mma_full[mslot]);
-      if (j == kbr - 1 || g == kblocks - 1) mbar_arrive(&raw_empty[rslot]);
-    }
+    if (lane == 0) mbar_arrive(&raw_empty[erslot]);
+    ++er;
+    if (++erslot == RS) { erslot = 0; ++erk; }
     return true;
   };
 
-  // ---- before the dependency wait: weights only ----
+  // ---- before the dependency wait: weights and scales only ----
   const int G_pre = DIRECT ? 0 : min(MS, kblocks);
   int issued = 0;
   if (warp == 0 && lane == 0) {
+    // the tile's scales (rows rounded up to 16 bytes: the allocation extends past them)
+    const uint32_t sbytes = (uint32_t)(((n_end - n_begin) * 4 + 15) & ~15);
+    gqd::mbar_arrive_expect_tx(sc_bar, NW * sbytes);
+    gqd::bulk_g2s(scb, a.s + n_begin, sbytes, sc_bar);
+    if (NW == 2) gqd::bulk_g2s(scb + a.tile_rows, a.s2 + n_begin, sbytes, sc_bar);
+    int rslot = 0, rk = 0;
     for (int r = 0; r < total_raw; ++r) {
       if (r >= RS) {
         const int last = min((r - RS + 1) * kbr, kblocks) - 1;
         if (DIRECT || last >= G_pre) break;
-        if (!wait_phase(&raw_empty[r % RS], (uint32_t)((r / RS) - 1) & 1u)) {
+        if (!wait_phase(&raw_empty[rslot], (uint32_t)(rk - 1) & 1u)) {
           *abort_flag = 1;
           break;
         }
       }
-      issue(r);
+      issue(r, rslot);
       issued = r + 1;
+      if (++rslot == RS) { rslot = 0; ++rk; }
     }
   }
-  int g_exp = 0;
   bool exp_ok = true;
-  if (!DIRECT && warp >= kThreads / 32 - kExpWarps) {
-    while (exp_ok && g_exp < G_pre) exp_ok = expand(g_exp++);
+  if (!DIRECT && ew >= 0) {
+    while (exp_ok && er < total_raw && min((er + 1) * kbr, kblocks) <= G_pre) exp_ok = expand_stage();
     if (!exp_ok) *abort_flag = 1;
   }
   gqd::griddep_launch_dependents();
@@ -363,83 +389,93 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ---- TMA producer: limb tiles and weight refills, in K-block order ----
-    if (lane == 0) {
+    if (lane == 0 && !*abort_flag) {
       int xi = 0;
-      for (int g = 0; g < kblocks && !*abort_flag; ++g) {
-        if (g % kbr == 0 && g / kbr >= issued) {
-          const int r = g / kbr;
-          if (!wait_phase(&raw_empty[r % RS], (uint32_t)((r / RS) - 1) & 1u)) {
-            *abort_flag = 1;
+      bool ok = true;
+      int jj = 0, r = 0, rslot = 0, rk = 0;  // position of K-block g in the raw stages
+      int own = 0, ord = 0, base_ord = 0;    // limb-ring owner of K-block g
+      for (int g = 0; g < kblocks; ++g) {
+        if (jj == 0 && r >= issued) {
+          if (!wait_phase(&raw_empty[rslot], (uint32_t)(rk - 1) & 1u)) {
+            ok = false;
             break;
           }
-          issue(r);
+          issue(r, rslot);
           issued = r + 1;
         }
-        int ord;
-        const int own = x_owner(g, ord);
-        const int xslot = own * XI + ord % XI;
-        if (ord >= XI && !wait_phase(&xa_empty[xslot], (uint32_t)((ord / XI) - 1) & 1u)) {
-          *abort_flag = 1;
+        if (DIRECT) ord = base_ord + jj;
+        const int xslot = own * XI + (ord & (XI - 1));
+        if (ord >= XI && !wait_phase(&xa_empty[xslot], (uint32_t)((ord >> XL) - 1) & 1u)) {
+          ok = false;
           break;
         }
         issue_x(xslot, g);
         xi = g + 1;
+        if (++jj == kbr) {
+          jj = 0;
+          ++r;
+          if (++rslot == RS) { rslot = 0; ++rk; }
+          if (DIRECT && ++own == NI) { own = 0; base_ord += kbr; }
+        }
+        if (!DIRECT && ++own == NI) { own = 0; ++ord; }
       }
+      if (!ok) *abort_flag = 1;
       if (*abort_flag) {
         // bounded drain of the copies still in flight before shared memory is released
-        for (int r = issued > RS ? issued - RS : 0; r < issued; ++r)
-          (void)gqd::mbar_wait_bounded(&raw_full[r % RS], (uint32_t)(r / RS) & 1u, 100000000ull);
-        for (int g = 0; g < xi; ++g) {
-          int ord;
-          const int own = x_owner(g, ord);
-          (void)gqd::mbar_wait_bounded(&xa_full[own * XI + ord % XI], (uint32_t)(ord / XI) & 1u, 100000000ull);
+        for (int rr = issued > RS ? issued - RS : 0; rr < issued; ++rr)
+          (void)gqd::mbar_wait_bounded(&raw_full[rr % RS], (uint32_t)(rr / RS) & 1u, 100000000ull);
+        for (int gg = 0; gg < xi; ++gg) {
+          int o2;
+          const int ow = x_owner(gg, o2);
+          (void)gqd::mbar_wait_bounded(&xa_full[ow * XI + (o2 & (XI - 1))], (uint32_t)(o2 >> XL) & 1u, 100000000ull);
         }
+        (void)gqd::mbar_wait_bounded(sc_bar, 0u, 100000000ull);
       }
     }
   } else if (warp <= kMaxIss) {
     // ---- MMA issue: K-blocks dealt round-robin to the issuers ----
     const int iss = warp - 1;
     if (lane == 0 && iss < NI) {
-      const uint32_t dcol = tmem + (uint32_t)(iss * NW * a.tile_rows);
-      bool ok = true, first = true;
+      const uint32_t dcol = tmem + (uint32_t)(iss * MH * NW * a.tile_rows);
+      bool ok = !*abort_flag, first = true;
       int ord = 0;  // K-blocks this issuer has consumed (its limb-ring position)
-      // Work units dealt round-robin: whole raw stages for I8 (each stage is then
-      // consumed, and released, by one issuer), single K-blocks otherwise.
+      const int S = DIRECT ? RS : MS;
       const int units = DIRECT ? total_raw : kblocks;
+      int slot = iss, par = 0;
+      while (slot >= S) { slot -= S; par ^= 1; }
+      const uint64_t xa_desc0 = sw128_desc(gqd::smem_u32(xa), 1024);
+      const uint64_t w_desc0 = sw128_desc(gqd::smem_u32(DIRECT ? raw : wid), 1024);
+      const uint32_t w_stride = (uint32_t)(DIRECT ? a.raw_bytes : a.mma_bytes);
       for (int u = iss; u < units && ok; u += NI) {
-        const int g0 = DIRECT ? u * kbr : u;
-        const int ng = DIRECT ? min(kbr, kblocks - g0) : 1;
-        int slot;
-        if (DIRECT) {
-          slot = u % RS;
-          ok = !*abort_flag && wait_phase(&raw_full[slot], (uint32_t)(u / RS) & 1u);
-        } else {
-          slot = u % MS;
-          ok = !*abort_flag && wait_phase(&mma_full[slot], (uint32_t)(u / MS) & 1u);
-        }
+        const int ng = DIRECT ? min(kbr, kblocks - u * kbr) : 1;
+        ok = wait_phase(DIRECT ? &raw_full[slot] : &mma_full[slot], (uint32_t)par);
         for (int j = 0; j < ng && ok; ++j) {
-          const int xslot = iss * XI + ord % XI;
-          ok = wait_phase(&xa_full[xslot], (uint32_t)(ord / XI) & 1u);
+          const int xslot = iss * XI + (ord & (XI - 1));
+          ok = wait_phase(&xa_full[xslot], (uint32_t)(ord >> XL) & 1u);
           ++ord;
           if (!ok) break;
           tc_fence_after();
-          const uint32_t bbase = DIRECT ? gqd::smem_u32(raw + slot * a.raw_bytes + j * NW * tile_bytes)
-                                        : gqd::smem_u32(wid + slot * a.mma_bytes);
-          const uint64_t ad = sw128_desc(gqd::smem_u32(xa + xslot * XA_TILE), 1024);
+          const uint64_t ad = xa_desc0 + (uint64_t)(((uint32_t)xslot * xa_tile) >> 4);
+          const uint64_t bd0 = w_desc0 + (uint64_t)((slot * w_stride + (DIRECT ? j * NW * tile_bytes : 0)) >> 4);
 #pragma unroll
           for (int h = 0; h < NW; ++h) {
-            const uint64_t bd = sw128_desc(bbase + h * tile_bytes, 1024);
-            const uint32_t d = dcol + h * a.tile_rows;
-            tc_mma_i8(d, ad, bd, idesc, first ? 0u : 1u);
-            tc_mma_i8(d, ad + 2, bd + 2, idesc, 1u);
-            tc_mma_i8(d, ad + 4, bd + 4, idesc, 1u);
-            tc_mma_i8(d, ad + 6, bd + 6, idesc, 1u);
+            const uint64_t bd = bd0 + (uint64_t)((h * tile_bytes) >> 4);
+            for (int hh = 0; hh < MH; ++hh) {
+              const uint32_t d = dcol + (uint32_t)((hh * NW + h) * a.tile_rows);
+              const uint64_t ah = ad + (uint64_t)(hh * (16384 >> 4));  // rows 128*hh.. of the limb tile
+              tc_mma_i8(d, ah, bd, idesc, first ? 0u : 1u);
+              tc_mma_i8(d, ah + 2, bd + 2, idesc, 1u);
+              tc_mma_i8(d, ah + 4, bd + 4, idesc, 1u);
+              tc_mma_i8(d, ah + 6, bd + 6, idesc, 1u);
+            }
           }
           first = false;
           tc_commit(&xa_empty[xslot]);
         }
         if (!ok) break;
         tc_commit(DIRECT ? &raw_empty[slot] : &mma_empty[slot]);
+        slot += NI;
+        while (slot >= S) { slot -= S; par ^= 1; }
       }
       if (ok) tc_commit(&acc_full[iss]);
       if (!ok) *abort_flag = 1;
@@ -450,72 +486,81 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---- warps 4-7: the rest of the widening, then the epilogue ----
     if (!DIRECT) {
       bool ok = exp_ok && !*abort_flag;
-      for (int g = g_exp; ok && g < kblocks; ++g) ok = expand(g);
+      while (ok && er < total_raw) ok = expand_stage();
       if (!ok) *abort_flag = 1;
     }
-    // Warp q reads lane quarter q: lanes 0-15 hold the limb rows 16q .. 16q+15,
-    // i.e. tokens 4q .. 4q+3 (lane = 4 * (token - 4q) + limb).
-    const int quarter = warp & 3;
-    const int tok = 4 * quarter + ((lane >> 2) & 3), limb = lane & 3;
-    const bool lane_ok = lane < 16 && tok < a.M;
-    const int tk = min(tok, a.M - 1);
-    const double pwt = __longlong_as_double((long long)(1023 - a.xexp[tk]) << 52);  // 2^-s
-    const long long zct = ZP * a.sumx[tk];
-    const bool badt = a.bad[tk] != 0;
-    bool ok = !*abort_flag;
+    if (et < a.M) {
+      tok_pw[et] = __longlong_as_double((long long)(1023 - a.xexp[et]) << 52);  // 2^-s
+      tok_zc[et] = ZP * a.sumx[et];
+      tok_bad[et] = a.bad[et];
+    }
+    epi_sync();
+    const int quarter = warp & 3, limb = lane & 3;
+    bool ok = !*abort_flag && wait_phase(sc_bar, 0u);
     for (int i = 0; i < NI; ++i) ok = ok && wait_phase(&acc_full[i], 0u);
     if (__all_sync(0xffffffffu, ok)) {
       tc_fence_after();
-      for (int c0 = 0; c0 < a.tile_rows; c0 += 8) {
-        long long T[NW][2];
+      for (int hh = 0; hh < MH; ++hh) {
+        // M=64: lane quarter q holds limb rows 16q.. in lanes 0-15 (tokens 4q..4q+3);
+        // M=128: lane quarter q of half hh holds limb rows 128hh + 32q + lane.
+        const int tok = a.mh == 0 ? 4 * quarter + ((lane >> 2) & 3) : 32 * hh + 8 * quarter + (lane >> 2);
+        const bool lane_ok = (a.mh != 0 || lane < 16) && tok < a.M;
+        const int tk = min(tok, a.M - 1);
+        const double pwt = tok_pw[tk];
+        const long long zct = tok_zc[tk];
+        const bool badt = tok_bad[tk] != 0;
+        for (int c0 = 0; c0 < a.tile_rows; c0 += 8) {
+          long long T[NW][2];
 #pragma unroll
-        for (int h = 0; h < NW; ++h) {
-          uint32_t d[kMaxIss][8];
-          const uint32_t col = (uint32_t)(h * a.tile_rows + c0) + ((uint32_t)(quarter * 32) << 16);
+          for (int h = 0; h < NW; ++h) {
+            uint32_t d[kMaxIss][8];
+            const uint32_t col = (uint32_t)((hh * NW + h) * a.tile_rows + c0) + ((uint32_t)(quarter * 32) << 16);
 #pragma unroll
-          for (int i = 0; i < kMaxIss; ++i)
-            if (i < NI) tmem_ld8_nowait(tmem + col + (uint32_t)(i * NW * a.tile_rows), d[i]);
-          int32_t dsum[8];
+            for (int i = 0; i < kMaxIss; ++i)
+              if (i < NI) tmem_ld8_nowait(tmem + col + (uint32_t)(i * MH * NW * a.tile_rows), d[i]);
+            int32_t dsum[8];
 #pragma unroll
-          for (int c = 0; c < 8; ++c) dsum[c] = 0;
+            for (int c = 0; c < 8; ++c) dsum[c] = 0;
 #pragma unroll
-          for (int i = 0; i < kMaxIss; ++i)
-            if (i < NI) {
-              tmem_wait_ld8(d[i]);
+            for (int i = 0; i < kMaxIss; ++i)
+              if (i < NI) {
+                tmem_wait_ld8(d[i]);
 #pragma unroll
-              for (int c = 0; c < 8; ++c) dsum[c] += (int32_t)d[i][c];
+                for (int c = 0; c < 8; ++c) dsum[c] += (int32_t)d[i][c];
+              }
+            T[h][0] = T[h][1] = 0;
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              long long v = (long long)dsum[c] << (8 * limb);
+              v += __shfl_xor_sync(0xffffffffu, v, 1);
+              v += __shfl_xor_sync(0xffffffffu, v, 2);
+              if (c == limb) T[h][0] = v;
+              if (c == 4 + limb) T[h][1] = v;
             }
-          T[h][0] = T[h][1] = 0;
-#pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            long long v = (long long)dsum[c] << (8 * limb);
-            v += __shfl_xor_sync(0xffffffffu, v, 1);
-            v += __shfl_xor_sync(0xffffffffu, v, 2);
-            if (c == limb) T[h][0] = v;
-            if (c == 4 + limb) T[h][1] = v;
           }
-        }
 #pragma unroll
-        for (int hr = 0; hr < 2; ++hr) {
-          const int n = n_begin + c0 + 4 * hr + limb;
-          if (!lane_ok || n >= n_end) continue;
-          float o;
-          if (badt) {
-            o = __int_as_float(0x7fc00000);
-          } else {
-            const float v0 = __fmul_rn((float)((double)(T[0][hr] - zct) * pwt), __ldg(a.s + n));
-            if (MODE == 1) {
-              const float v1 = __fmul_rn((float)((double)(T[NW - 1][hr] - zct) * pwt), __ldg(a.s2 + n));
-              o = __fmul_rn(gqd::gelu_tanh(v0), v1);
-            } else if (MODE == 2) {
-              o = __fmul_rn(gqd::gelu_tanh(v0), a.bs[(size_t)tok * a.b_stride + a.b_off + n]);
-            } else if (MODE == 3) {
-              o = a.cap > 0.0f ? __fmul_rn(a.cap, tanhf(__fdiv_rn(v0, a.cap))) : v0;
+          for (int hr = 0; hr < 2; ++hr) {
+            const int nl = c0 + 4 * hr + limb;
+            const int n = n_begin + nl;
+            if (!lane_ok || n >= n_end) continue;
+            float o;
+            if (badt) {
+              o = __int_as_float(0x7fc00000);
             } else {
-              o = v0;
+              const float v0 = __fmul_rn((float)((double)(T[0][hr] - zct) * pwt), scb[nl]);
+              if (MODE == 1) {
+                const float v1 = __fmul_rn((float)((double)(T[NW - 1][hr] - zct) * pwt), scb[a.tile_rows + nl]);
+                o = __fmul_rn(gqd::gelu_tanh(v0), v1);
+              } else if (MODE == 2) {
+                o = __fmul_rn(gqd::gelu_tanh(v0), a.bs[(size_t)tok * a.b_stride + a.b_off + n]);
+              } else if (MODE == 3) {
+                o = a.cap > 0.0f ? __fmul_rn(a.cap, tanhf(__fdiv_rn(v0, a.cap))) : v0;
+              } else {
+                o = v0;
+              }
             }
+            a.y[(size_t)tok * a.ldy + a.y_col0 + n] = o;
           }
-          a.y[(size_t)tok * a.ldy + a.y_col0 + n] = o;
         }
       }
     } else {
@@ -566,24 +611,39 @@ int launch_xm(gq_ctx *ctx, int mode, const CUtensorMap &m1, const CUtensorMap &m
 }
 
 struct TcxPlan {
-  int tile_rows, gx, kblocks, kbr, raw_stages, mma_stages, xa_stages, raw_bytes, mma_bytes, issuers, tmem_cols;
+  int tile_rows, mh, gx, slice_rows, kblocks, kbr, raw_stages, mma_stages, xa_stages, xi, raw_bytes, mma_bytes,
+      xa_tile, issuers, tmem_cols;
   size_t smem;
 };
 
-// One tile of weight rows per CTA (N / tile_rows CTAs), rings sized to the
-// whole SM's shared memory.
-bool tcx_plan(const gq_ctx *ctx, const gq_qweight *w, int nw, TcxPlan &p) {
+int mh_of(int64_t m) { return m <= 16 ? 0 : (m <= 32 ? 1 : 2); }
+
+// One tile of weight rows per CTA. Weights taller than num_sms tiles run as
+// row slices of num_sms * tile_rows rows. Rings sized to the SM's shared memory:
+// the limb ring gets up to ~half of it, the weight rings the rest.
+bool tcx_plan(const gq_ctx *ctx, const gq_qweight *w, int64_t m, int nw, TcxPlan &p) {
   const bool direct = (w->bits == 8 && w->signed_i8);
   const int kb_bytes = kKB * w->bits / 8;
-  const int max_tile = 256 / nw;
+  p.mh = mh_of(m);
+  const int MH = p.mh > 0 ? p.mh : 1;
+  const int xa_rows = p.mh == 0 ? 64 : 128 * p.mh;
+  p.xa_tile = xa_rows * 128;
+  const int max_tile = std::min(256 / nw, 512 / (MH * nw)) / 16 * 16;
   const int64_t rows0 = (w->n + ctx->num_sms - 1) / ctx->num_sms;
-  if (rows0 > max_tile) return false;
-  p.tile_rows = (int)std::max<int64_t>(16, (rows0 + 15) / 16 * 16);
-  p.gx = (int)((w->n + p.tile_rows - 1) / p.tile_rows);
+  p.tile_rows = (int)std::min<int64_t>(max_tile, std::max<int64_t>(16, (rows0 + 15) / 16 * 16));
+  p.slice_rows = (int)std::min<int64_t>(w->n, (int64_t)ctx->num_sms * p.tile_rows);
+  p.gx = (int)((p.slice_rows + p.tile_rows - 1) / p.tile_rows);
   p.kblocks = (int)((w->k + kKB - 1) / kKB);
   const int tile_bytes = p.tile_rows * 128;
+  const int sc_bytes = nw * p.tile_rows * 4;
   const size_t budget = ctx->smem_optin - 1024;
-  p.xa_stages = kMaxXa;
+  // issuers: TMEM columns, work units; then the limb ring: XI >= 2 slots each
+  const int units_hint = direct ? p.kblocks : p.kblocks;
+  p.issuers = std::max(1, std::min(std::min(kMaxIss, units_hint), 512 / (MH * nw * p.tile_rows)));
+  const size_t xa_budget = std::min<size_t>(budget / 2 + 16384, 131072);
+  while (p.issuers > 1 && (size_t)p.issuers * 2 * p.xa_tile > xa_budget) --p.issuers;
+  p.xi = (int)std::max<size_t>(2, std::min<size_t>(kMaxXa / p.issuers, xa_budget / ((size_t)p.issuers * p.xa_tile)));
+  p.xi = std::min(p.xi, std::max(2, (p.kblocks + p.issuers - 1) / p.issuers));
   if (direct) {
     p.kbr = std::max(1, std::min(p.kblocks, (8192 + nw * tile_bytes - 1) / (nw * tile_bytes)));
     p.raw_bytes = p.kbr * nw * tile_bytes;
@@ -593,18 +653,31 @@ bool tcx_plan(const gq_ctx *ctx, const gq_qweight *w, int nw, TcxPlan &p) {
     p.kbr = std::max(1, std::min(p.kblocks, 256 / kb_bytes));
     p.raw_bytes = (nw * p.tile_rows * p.kbr * kb_bytes + 1023) / 1024 * 1024;
     p.mma_bytes = nw * tile_bytes;
-    const TcxSmem L0 = tcx_layout(p.xa_stages, 2, p.raw_bytes, 0, p.mma_bytes);
-    const int fit = L0.total <= budget ? (int)((budget - L0.total) / p.mma_bytes) : 0;
-    p.mma_stages = std::min(std::min(kMaxMma, p.kblocks), fit);
-    if (p.mma_stages < 2) return false;
   }
   const int total_raw = (p.kblocks + p.kbr - 1) / p.kbr;
-  const TcxSmem L1 = tcx_layout(p.xa_stages, 0, p.raw_bytes, p.mma_stages, p.mma_bytes);
-  const int fit = L1.total <= budget ? (int)((budget - L1.total) / p.raw_bytes) : 0;
-  p.raw_stages = std::min(std::min(kMaxRaw, total_raw), fit);
-  if (p.raw_stages < std::min(2, total_raw)) return false;
+  for (;;) {
+    p.xa_stages = p.issuers * p.xi;
+    if (!direct) {
+      const TcxSmem L0 = tcx_layout(p.xa_stages, p.xa_tile, 2, p.raw_bytes, 0, p.mma_bytes, sc_bytes);
+      const int fit = L0.total <= budget ? (int)((budget - L0.total) / p.mma_bytes) : 0;
+      p.mma_stages = std::min(std::min(kMaxMma, p.kblocks), fit);
+    }
+    const TcxSmem L1 = tcx_layout(p.xa_stages, p.xa_tile, 0, p.raw_bytes, p.mma_stages, p.mma_bytes, sc_bytes);
+    const int fit = L1.total <= budget ? (int)((budget - L1.total) / p.raw_bytes) : 0;
+    p.raw_stages = std::min(std::min(kMaxRaw, total_raw), fit);
+    const bool ok = p.raw_stages >= std::min(2, total_raw) && (direct || p.mma_stages >= 2);
+    if (ok) break;
+    if (p.xi > 2) {
+      --p.xi;
+    } else if (p.issuers > 1) {
+      --p.issuers;
+      p.xi = 2;
+    } else {
+      return false;
+    }
+  }
   const int units = direct ? total_raw : p.kblocks;
-  p.issuers = std::max(1, std::min(std::min(kMaxIss, units), 512 / (nw * p.tile_rows)));
+  p.issuers = std::min(p.issuers, std::max(1, units));
   // A ring that wraps must hand each slot back to the same issuer (slots are
   // consumed round-robin): its depth is then a multiple of the issuer count.
   if (direct && p.raw_stages < total_raw) {
@@ -615,11 +688,13 @@ bool tcx_plan(const gq_ctx *ctx, const gq_qweight *w, int nw, TcxPlan &p) {
     while (p.issuers > 1 && p.mma_stages < p.issuers) --p.issuers;
     p.mma_stages -= p.mma_stages % p.issuers;
   }
-  if (p.xa_stages / p.issuers < 2) return false;
-  const int cols = p.issuers * nw * p.tile_rows;
+  while (p.xi & (p.xi - 1)) --p.xi;  // a power of two (slots and phases by mask and shift)
+  p.xa_stages = p.issuers * p.xi;
+  if (p.xa_stages > kMaxXa || p.xi < 2) return false;
+  const int cols = p.issuers * MH * nw * p.tile_rows;
   p.tmem_cols = 32;
   while (p.tmem_cols < cols) p.tmem_cols <<= 1;
-  p.smem = tcx_layout(p.xa_stages, p.raw_stages, p.raw_bytes, p.mma_stages, p.mma_bytes).total;
+  p.smem = tcx_layout(p.xa_stages, p.xa_tile, p.raw_stages, p.raw_bytes, p.mma_stages, p.mma_bytes, sc_bytes).total;
   return p.tmem_cols <= 512 && p.smem <= budget;
 }
 
@@ -634,11 +709,11 @@ CUresult encode_w(CUtensorMap *map, const gq_qweight *w, const TcxPlan &p) {
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
 
-// The limb matrix [4*m, kp] s8; box = 64 rows x one 128-byte K-block, swizzled.
-CUresult encode_limbs(CUtensorMap *map, const uint8_t *limbs, int64_t m, int64_t kp) {
+// The limb matrix [4*m, kp] s8; box = xa_rows rows x one 128-byte K-block, swizzled.
+CUresult encode_limbs(CUtensorMap *map, const uint8_t *limbs, int64_t m, int64_t kp, int xa_rows) {
   cuuint64_t dims[2] = {(cuuint64_t)kp, (cuuint64_t)(4 * m)};
   cuuint64_t strides[1] = {(cuuint64_t)kp};
-  cuuint32_t box[2] = {128u, 64u};
+  cuuint32_t box[2] = {128u, (cuuint32_t)xa_rows};
   cuuint32_t estr[2] = {1, 1};
   return gq_encode_fn()(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t *>(limbs), dims, strides, box,
                         estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -652,18 +727,26 @@ cudaError_t launch_limbs(gq_ctx *ctx, const float *x, int64_t m, int64_t k, int6
                    sumx, bad);
 }
 
+// Rows [r0, r0 + n) of a weight as a weight of its own (same layout).
+gq_qweight row_slice(const gq_qweight *w, int64_t r0, int64_t n) {
+  gq_qweight v = *w;
+  v.bytes = w->bytes + r0 * w->row_bytes;
+  v.scales = w->scales + r0 * w->scale_stride;
+  v.n = n;
+  return v;
+}
 
 }  // namespace
 
-// 3 <= M <= 16 activation rows, one scale per weight row, K a multiple of 16 up
-// to 8192, at most 256 / nw rows per CTA, 16-byte aligned x and packed rows.
+// 3 <= M <= 64 activation rows, one scale per weight row, K a multiple of 16 up
+// to 8192, 16-byte aligned x and packed rows.
 bool gq_gemv_tcx_supported(gq_ctx *ctx, const gq_qweight *w, const float *x, int64_t m, int nw) {
   if (m < 3 || m > kMaxTok || w->group_size != w->k || w->k <= 0 || w->n <= 0) return false;
   if (w->k % 16 != 0 || w->k > kMaxK || w->n > (1ll << 30)) return false;
   if (w->row_bytes % 16 != 0 || (uintptr_t)w->bytes % 16 != 0 || (uintptr_t)x % 16 != 0) return false;
   if (gq_encode_fn() == nullptr) return false;
   TcxPlan p;
-  return tcx_plan(ctx, w, nw, p);
+  return tcx_plan(ctx, w, m, nw, p);
 }
 
 int gq_gemv_tcx_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq_qweight *w, const gq_qweight *w2,
@@ -671,7 +754,7 @@ int gq_gemv_tcx_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const g
                        int64_t y_col0) {
   const int nw = (mode == 1) ? 2 : 1;
   TcxPlan p;
-  if (!tcx_plan(ctx, w, nw, p)) return gq_fail(ctx, GQ_ERR_UNSUPPORTED, "gemv_tcx: no stage configuration fits");
+  if (!tcx_plan(ctx, w, m, nw, p)) return gq_fail(ctx, GQ_ERR_UNSUPPORTED, "gemv_tcx: no stage configuration fits");
   const int64_t kp = (int64_t)p.kblocks * kKB;
   const size_t limb_bytes = ((size_t)(4 * m * kp) + 255) & ~size_t(255);
   void *wsp = nullptr;
@@ -688,40 +771,53 @@ int gq_gemv_tcx_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const g
   } else {
     GQ_CUDA_TRY(ctx, launch_limbs<8>(ctx, x, m, w->k, kp, limbs, xexp, sumx, bad));
   }
-  CUtensorMap m1, m2, mx;
-  if (encode_w(&m1, w, p) != CUDA_SUCCESS || encode_w(&m2, w2 ? w2 : w, p) != CUDA_SUCCESS ||
-      encode_limbs(&mx, limbs, m, kp) != CUDA_SUCCESS)
-    return gq_fail(ctx, GQ_ERR_CUDA, "gemv_tcx: tensor map");
-  TcxArgs a = {};
-  a.M = (int)m;
-  a.K = (int)w->k;
-  a.N = (int)w->n;
-  a.s = w->scales;
-  a.s2 = w2 ? w2->scales : nullptr;
-  a.bs = bs;
-  a.b_stride = b_stride;
-  a.b_off = b_off;
-  a.cap = cap;
-  a.y = y;
-  a.ldy = ldy;
-  a.y_col0 = y_col0;
-  a.xexp = xexp;
-  a.sumx = sumx;
-  a.bad = bad;
-  a.tile_rows = p.tile_rows;
-  a.kblocks = p.kblocks;
-  a.kbr = p.kbr;
-  a.raw_stages = p.raw_stages;
-  a.mma_stages = p.mma_stages;
-  a.xa_stages = p.xa_stages;
-  a.raw_bytes = p.raw_bytes;
-  a.mma_bytes = p.mma_bytes;
-  a.issuers = p.issuers;
-  a.tmem_cols = p.tmem_cols;
-  a.err = ctx->dev_err;
-  const dim3 grid((unsigned)p.gx);
-  if (w->bits == 4) return launch_xm<4, false>(ctx, mode, m1, m2, mx, a, grid, p.smem);
-  if (w->bits == 2) return launch_xm<2, false>(ctx, mode, m1, m2, mx, a, grid, p.smem);
-  if (w->signed_i8) return launch_xm<8, true>(ctx, mode, m1, m2, mx, a, grid, p.smem);
-  return launch_xm<8, false>(ctx, mode, m1, m2, mx, a, grid, p.smem);
+  CUtensorMap mx;
+  if (encode_limbs(&mx, limbs, m, kp, p.mh == 0 ? 64 : 128 * p.mh) != CUDA_SUCCESS)
+    return gq_fail(ctx, GQ_ERR_CUDA, "gemv_tcx: limb tensor map");
+  for (int64_t r0 = 0; r0 < w->n; r0 += p.slice_rows) {
+    const int64_t rows = std::min<int64_t>(p.slice_rows, w->n - r0);
+    const gq_qweight ws = row_slice(w, r0, rows);
+    const gq_qweight ws2 = row_slice(w2 ? w2 : w, r0, rows);
+    CUtensorMap m1, m2;
+    if (encode_w(&m1, &ws, p) != CUDA_SUCCESS || encode_w(&m2, &ws2, p) != CUDA_SUCCESS)
+      return gq_fail(ctx, GQ_ERR_CUDA, "gemv_tcx: weight tensor map");
+    TcxArgs a = {};
+    a.M = (int)m;
+    a.K = (int)w->k;
+    a.N = (int)rows;
+    a.s = ws.scales;
+    a.s2 = w2 ? ws2.scales : nullptr;
+    a.bs = bs;
+    a.b_stride = b_stride;
+    a.b_off = b_off + r0;
+    a.cap = cap;
+    a.y = y;
+    a.ldy = ldy;
+    a.y_col0 = y_col0 + r0;
+    a.xexp = xexp;
+    a.sumx = sumx;
+    a.bad = bad;
+    a.tile_rows = p.tile_rows;
+    a.mh = p.mh;
+    a.kblocks = p.kblocks;
+    a.kbr = p.kbr;
+    a.raw_stages = p.raw_stages;
+    a.mma_stages = p.mma_stages;
+    a.xa_stages = p.xa_stages;
+    a.xi = p.xi;
+    a.xi_log2 = __builtin_ctz((unsigned)p.xi);
+    a.raw_bytes = p.raw_bytes;
+    a.mma_bytes = p.mma_bytes;
+    a.xa_tile = p.xa_tile;
+    a.issuers = p.issuers;
+    a.tmem_cols = p.tmem_cols;
+    a.err = ctx->dev_err;
+    const dim3 grid((unsigned)((rows + p.tile_rows - 1) / p.tile_rows));
+    if (w->bits == 4) rc = launch_xm<4, false>(ctx, mode, m1, m2, mx, a, grid, p.smem);
+    else if (w->bits == 2) rc = launch_xm<2, false>(ctx, mode, m1, m2, mx, a, grid, p.smem);
+    else if (w->signed_i8) rc = launch_xm<8, true>(ctx, mode, m1, m2, mx, a, grid, p.smem);
+    else rc = launch_xm<8, false>(ctx, mode, m1, m2, mx, a, grid, p.smem);
+    if (rc != GQ_OK) return rc;
+  }
+  return GQ_OK;
 }

@@ -409,12 +409,14 @@ bool use_gemv_tc(gq_ctx *ctx, const float *x, int64_t m, const gq_qweight *w, in
   return gq_gemv_tc_supported(ctx, w, x, m, nw);
 }
 
-// 3 <= M <= 16: the tensor-core GEMV with streamed limbs (weights read once for
-// all rows) unless GQ_DECODE_TC=0.
+// 5 <= M <= 64 (3 <= M with GQ_DECODE_TC=2): the tensor-core GEMV with streamed
+// limbs (weights read once for all rows); up to 4 rows the CUDA-core GEMV covers
+// them in one pass and is faster (measured on the E2B layer sweep).
 bool use_gemv_tcx(gq_ctx *ctx, const float *x, int64_t m, const gq_qweight *w, int nw) {
   const char *e = getenv("GQ_DECODE_TC");
   const int mode = (e && *e) ? (*e - '0') : 1;
-  return mode > 0 && gq_gemv_tcx_supported(ctx, w, x, m, nw);
+  if (mode <= 0 || (mode == 1 && m < 5)) return false;
+  return gq_gemv_tcx_supported(ctx, w, x, m, nw);
 }
 
 }  // namespace

@@ -1,8 +1,10 @@
 """Both decode GEMVs against the CPU oracle (needs a B200).
 
-Decode rows (M <= 16) have two CUDA implementations: the CUDA-core GEMV and the
+Decode rows (M <= 64) have two CUDA implementations: the CUDA-core GEMV and the
 tensor-core ones (exact integer dot products on tcgen05.mma.kind::i8; x staged
-in the CTA for M <= 2, streamed as a limb matrix for 3 <= M <= 16). The
+in the CTA for M <= 2, streamed as a limb matrix for 3 <= M <= 64: one M=64 MMA
+up to 16 rows, one or two M=128 MMAs up to 32 / 64 rows; weights taller than one
+tile per SM run as row slices, e.g. the 40000-row case below). The
 library picks one per shape; GQ_DECODE_TC forces the choice (0 = CUDA cores,
 2 = tensor cores wherever they apply), so every shape family here runs through
 both, at the FFMA-path bound (relative L2 <= 1e-5 against the oracle).
@@ -43,7 +45,7 @@ SHAPES = [(2048, 1536, 8, True), (256, 1536, 8, True), (1536, 2048, 8, True), (6
 
 @pytest.mark.parametrize("path", PATHS)
 @pytest.mark.parametrize("n,k,bits,signed", SHAPES)
-@pytest.mark.parametrize("m", [1, 2, 3, 8, 16])
+@pytest.mark.parametrize("m", [1, 2, 3, 8, 16, 24, 40, 64])
 def test_linear_both_paths(g, monkeypatch, path, n, k, bits, signed, m):
     monkeypatch.setenv("GQ_DECODE_TC", path)
     w = synth.random_qweight(3000 + n + k + bits, n, k, bits, signed)
@@ -53,7 +55,7 @@ def test_linear_both_paths(g, monkeypatch, path, n, k, bits, signed, m):
 
 
 @pytest.mark.parametrize("path", PATHS)
-@pytest.mark.parametrize("m", [1, 2, 8])
+@pytest.mark.parametrize("m", [1, 2, 8, 33, 64])
 def test_geglu_both_paths(g, monkeypatch, path, m):
     monkeypatch.setenv("GQ_DECODE_TC", path)
     n, k = 6144, 1536
@@ -65,7 +67,7 @@ def test_geglu_both_paths(g, monkeypatch, path, m):
 
 
 @pytest.mark.parametrize("path", PATHS)
-@pytest.mark.parametrize("m", [2, 5])
+@pytest.mark.parametrize("m", [2, 5, 40])
 def test_gelu_mul_cols_both_paths(g, monkeypatch, path, m):
     monkeypatch.setenv("GQ_DECODE_TC", path)
     n, k, off = 256, 1536, 512
@@ -77,27 +79,29 @@ def test_gelu_mul_cols_both_paths(g, monkeypatch, path, m):
 
 
 @pytest.mark.parametrize("path", PATHS)
-def test_softcap_slice_both_paths(g, monkeypatch, path):
+@pytest.mark.parametrize("m,n", [(4, 32768), (48, 32768), (6, 65536)])
+def test_softcap_slice_both_paths(g, monkeypatch, path, m, n):
     """A vocab shard written into its column range of a wider logits row."""
     monkeypatch.setenv("GQ_DECODE_TC", path)
-    n, k, cap = 32768, 1536, 30.0
+    k, cap = 1536, 30.0
     w = synth.random_qweight(3301, n, k, 8, True)
-    x = synth.normal(3302, 4 * k).reshape(4, k) * 4.0
-    out = g.zeros((4, 3 * n))
+    x = synth.normal(3302, m * k).reshape(m, k) * 4.0
+    out = g.zeros((m, 3 * n))
     g.linear_softcap(g.tensor(x, x.shape), g.quant_tensor(w), cap, out=out, col0=n)
-    got = g.readback(out).reshape(4, 3 * n)
+    got = g.readback(out).reshape(m, 3 * n)
     ref = oracle.softcap(oracle.linear(x, w), cap)
     assert rel_l2(got[:, n:2 * n], ref) <= REL_L2
     assert not np.any(got[:, :n]) and not np.any(got[:, 2 * n:])
 
 
 @pytest.mark.parametrize("path", PATHS)
-def test_extreme_activations_both_paths(g, monkeypatch, path):
+@pytest.mark.parametrize("m", [6, 36])
+def test_extreme_activations_both_paths(g, monkeypatch, path, m):
     """Fixed-point scaling across the f32 range: tiny, huge, large mean, outlier."""
     monkeypatch.setenv("GQ_DECODE_TC", path)
     n, k = 1024, 1536
     w = synth.make_qweight(3401, n, k, 4)
-    base = synth.normal(3402, 6 * k).reshape(6, k)
+    base = synth.normal(3402, m * k).reshape(m, k)
     for label, x in [("tiny", base * 1e-30), ("huge", base * 1e25), ("mean", base + 5.0)]:
         x = x.astype(np.float32)
         got = g.readback(g.linear(g.tensor(x, x.shape), g.quant_tensor(w)))
