@@ -180,6 +180,74 @@ __global__ void __launch_bounds__(kNormThreads) rmsnorm_reg_kernel(const float *
   }
 }
 
+// add_rms_norm followed by rms_norm of its result, in one pass over the row:
+// h = (r + rms_norm(x, w1)) * s, xn = rms_norm(h, w2). Every element and row sum
+// is computed exactly as rmsnorm_reg_kernel computes it, so both outputs equal
+// the two separate calls bit for bit. h may alias r.
+template <int VPL>
+__global__ void __launch_bounds__(kNormThreads) add_norm_norm_kernel(const float *x, const float *r, const float *w1,
+                                                                     const float *s, const float *w2, int64_t rows,
+                                                                     int64_t d, float eps, float *h, float *xn) {
+  gqd::griddep_wait();
+  gqd::griddep_launch_dependents();
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (kNormThreads / 32) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int n4 = (int)(d / 4);
+  const float4 *x4 = reinterpret_cast<const float4 *>(x + row * d);
+  const float4 *r4 = reinterpret_cast<const float4 *>(r + row * d);
+  const float4 *w14 = reinterpret_cast<const float4 *>(w1);
+  const float4 *w24 = reinterpret_cast<const float4 *>(w2);
+  const float sc = s ? __ldg(s) : 1.0f;
+  float4 xv[VPL], rv[VPL], wv[VPL], w2v[VPL];
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int c = lane + 32 * i;
+    const bool in = c < n4;
+    xv[i] = in ? x4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+    rv[i] = in ? r4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+    wv[i] = in ? __ldg(w14 + c) : make_float4(1.f, 1.f, 1.f, 1.f);
+    w2v[i] = in ? __ldg(w24 + c) : make_float4(1.f, 1.f, 1.f, 1.f);
+  }
+  float ss = 0.0f;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    ss = __fadd_rn(ss, __fmul_rn(xv[i].x, xv[i].x));
+    ss = __fadd_rn(ss, __fmul_rn(xv[i].y, xv[i].y));
+    ss = __fadd_rn(ss, __fmul_rn(xv[i].z, xv[i].z));
+    ss = __fadd_rn(ss, __fmul_rn(xv[i].w, xv[i].w));
+  }
+  const float inv = rms_inv(warp_sum(ss), d, eps);
+  auto one = [&](float xx, float ww, float rr) {
+    float n = __fadd_rn(rr, __fmul_rn(__fmul_rn(xx, inv), ww));
+    if (s) n = __fmul_rn(n, sc);
+    return n;
+  };
+  float ss2 = 0.0f;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    xv[i] = make_float4(one(xv[i].x, wv[i].x, rv[i].x), one(xv[i].y, wv[i].y, rv[i].y),
+                        one(xv[i].z, wv[i].z, rv[i].z), one(xv[i].w, wv[i].w, rv[i].w));
+    if (lane + 32 * i >= n4) xv[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    ss2 = __fadd_rn(ss2, __fmul_rn(xv[i].x, xv[i].x));
+    ss2 = __fadd_rn(ss2, __fmul_rn(xv[i].y, xv[i].y));
+    ss2 = __fadd_rn(ss2, __fmul_rn(xv[i].z, xv[i].z));
+    ss2 = __fadd_rn(ss2, __fmul_rn(xv[i].w, xv[i].w));
+  }
+  const float inv2 = rms_inv(warp_sum(ss2), d, eps);
+  float4 *h4 = reinterpret_cast<float4 *>(h + row * d);
+  float4 *y4 = reinterpret_cast<float4 *>(xn + row * d);
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int c = lane + 32 * i;
+    if (c < n4) {
+      h4[c] = xv[i];
+      y4[c] = make_float4(__fmul_rn(__fmul_rn(xv[i].x, inv2), w2v[i].x), __fmul_rn(__fmul_rn(xv[i].y, inv2), w2v[i].y),
+                          __fmul_rn(__fmul_rn(xv[i].z, inv2), w2v[i].z), __fmul_rn(__fmul_rn(xv[i].w, inv2), w2v[i].w));
+    }
+  }
+}
+
 struct RopeFreq {
   float f[kMaxHalfRot];
 };
@@ -499,7 +567,7 @@ __global__ void __launch_bounds__(NT) attn_chunk_kernel(const AttnArgs a) {
 // online across sub-tiles (running max, sum and output rescaled per head).
 // Thread t owns head_dim columns 4t .. 4t+3 for all G query heads, as above.
 constexpr int kSubKeys = 8;
-constexpr int kRingStages = 4;
+constexpr int kRingStages = 3;  // 96 KB at head_dim 512: two CTAs per SM
 
 template <int NT>
 __global__ void __launch_bounds__(NT) attn_ring_kernel(const AttnArgs a) {
@@ -700,16 +768,20 @@ __global__ void __launch_bounds__(NT) attn_ring_kernel(const AttnArgs a) {
 }
 
 // Merge the chunks of one (token, head) row: out = sum_s e^(m_s - M) o_s / sum_s e^(m_s - M) l_s.
-// The chunk statistics are read in parallel (one per thread) into shared memory.
+// Grid: x = (token, head) row, y = slice of 128 output columns. Block: 32 column
+// threads (4 columns each) x 8 groups that split the chunks; the chunk weights are
+// computed once in shared memory, the 8 group sums are added through shared memory.
 constexpr int kMaxSplits = 256;
-__global__ void attn_combine_kernel(const float *part_o, const float *part_ml, int64_t rows, int64_t Hq, int64_t dh,
-                                    int splits, float *out) {
+constexpr int kCombGroups = 8;
+__global__ void __launch_bounds__(256) attn_combine_kernel(const float *part_o, const float *part_ml, int64_t rows,
+                                                           int64_t Hq, int64_t dh, int splits, float *out) {
   __shared__ float wgt[kMaxSplits];
   __shared__ float wred[8], lred[8];
+  __shared__ float4 acc_s[kCombGroups][32];
   gqd::griddep_wait();
   gqd::griddep_launch_dependents();
   const int64_t row = blockIdx.x;  // (token, head)
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = blockDim.x >> 5;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const float *ml = part_ml + row * splits * 2;
   float m = -INFINITY, l = 0.0f;
   for (int s2 = tid; s2 < splits; s2 += blockDim.x) m = fmaxf(m, ml[2 * s2]);
@@ -717,7 +789,8 @@ __global__ void attn_combine_kernel(const float *part_o, const float *part_ml, i
   if (lane == 0) wred[warp] = m;
   __syncthreads();
   float M = -INFINITY;
-  for (int i = 0; i < nw; ++i) M = fmaxf(M, wred[i]);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) M = fmaxf(M, wred[i]);
   for (int s2 = tid; s2 < splits; s2 += blockDim.x) {
     const float ms = ml[2 * s2];
     const float w = (ms == -INFINITY) ? 0.0f : expf(__fsub_rn(ms, M));
@@ -728,14 +801,16 @@ __global__ void attn_combine_kernel(const float *part_o, const float *part_ml, i
   if (lane == 0) lred[warp] = l;
   __syncthreads();
   float L = 0.0f;
-  for (int i = 0; i < nw; ++i) L += lred[i];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) L += lred[i];
   const float inv = L > 0.0f ? __fdiv_rn(1.0f, L) : 0.0f;
-  const int64_t bt = row / Hq, h = row % Hq;
-  for (int64_t c = 4 * tid; c < dh; c += 4 * blockDim.x) {
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  const int64_t c = (int64_t)blockIdx.y * 128 + 4 * lane;  // this thread's 4 columns
+  const int grp = warp;                                    // chunks grp, grp + 8, ...
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (c < dh) {
     const float *po = part_o + row * splits * dh + c;
 #pragma unroll 4
-    for (int s2 = 0; s2 < splits; ++s2) {
+    for (int s2 = grp; s2 < splits; s2 += kCombGroups) {
       const float w = wgt[s2];
       const float4 v = *reinterpret_cast<const float4 *>(po + (int64_t)s2 * dh);
       acc.x = __fmaf_rn(w, v.x, acc.x);
@@ -743,8 +818,22 @@ __global__ void attn_combine_kernel(const float *part_o, const float *part_ml, i
       acc.z = __fmaf_rn(w, v.z, acc.z);
       acc.w = __fmaf_rn(w, v.w, acc.w);
     }
+  }
+  acc_s[grp][lane] = acc;
+  __syncthreads();
+  if (warp == 0 && c < dh) {
+    float4 t = acc_s[0][lane];
+#pragma unroll
+    for (int g2 = 1; g2 < kCombGroups; ++g2) {
+      const float4 u = acc_s[g2][lane];
+      t.x = __fadd_rn(t.x, u.x);
+      t.y = __fadd_rn(t.y, u.y);
+      t.z = __fadd_rn(t.z, u.z);
+      t.w = __fadd_rn(t.w, u.w);
+    }
+    const int64_t bt = row / Hq, h = row % Hq;
     *reinterpret_cast<float4 *>(out + bt * Hq * dh + h * dh + c) =
-        make_float4(__fmul_rn(acc.x, inv), __fmul_rn(acc.y, inv), __fmul_rn(acc.z, inv), __fmul_rn(acc.w, inv));
+        make_float4(__fmul_rn(t.x, inv), __fmul_rn(t.y, inv), __fmul_rn(t.z, inv), __fmul_rn(t.w, inv));
   }
 }
 
@@ -973,6 +1062,34 @@ int gq_add_rms_norm(gq_ctx *ctx, const float *residual, const float *x, int64_t 
   return norm_launch(ctx, 1, x, residual, w, scale_by, rows, d, eps, y, RowMap{1, d, 0});
 }
 
+int gq_add_rms_norm_norm(gq_ctx *ctx, const float *residual, const float *x, int64_t rows, int64_t d, const float *w1,
+                         float eps, const float *scale_by, const float *w2, float *h, float *xn) {
+  ENTER(ctx);
+  if (rows < 0 || d <= 0 || !x || !residual || !w1 || !w2 || !h || !xn)
+    return gq_fail(ctx, GQ_ERR_INVALID_ARGUMENT, "add_rms_norm_norm: bad shape or null pointer");
+  if (rows == 0) return GQ_OK;
+  const int vpl = reg_vpl(d);
+  const bool aligned = d % 4 == 0 && ((uintptr_t)x | (uintptr_t)residual | (uintptr_t)w1 | (uintptr_t)w2 |
+                                      (uintptr_t)h | (uintptr_t)xn) % 16 == 0;
+  if (!vpl || vpl > 12 || !aligned) {  // the two calls it fuses
+    int rc = norm_launch(ctx, 1, x, residual, w1, scale_by, rows, d, eps, h, RowMap{1, d, 0});
+    if (rc != GQ_OK) return rc;
+    return norm_launch(ctx, 0, h, nullptr, w2, nullptr, rows, d, eps, xn, RowMap{1, d, 0});
+  }
+  const dim3 grid((unsigned)((rows + kNormThreads / 32 - 1) / (kNormThreads / 32))), blk(kNormThreads);
+  cudaError_t e;
+  switch (vpl) {
+    case 1: e = gq_launch(ctx, add_norm_norm_kernel<1>, grid, blk, 0, x, residual, w1, scale_by, w2, rows, d, eps, h, xn); break;
+    case 2: e = gq_launch(ctx, add_norm_norm_kernel<2>, grid, blk, 0, x, residual, w1, scale_by, w2, rows, d, eps, h, xn); break;
+    case 4: e = gq_launch(ctx, add_norm_norm_kernel<4>, grid, blk, 0, x, residual, w1, scale_by, w2, rows, d, eps, h, xn); break;
+    case 8: e = gq_launch(ctx, add_norm_norm_kernel<8>, grid, blk, 0, x, residual, w1, scale_by, w2, rows, d, eps, h, xn); break;
+    case 12: e = gq_launch(ctx, add_norm_norm_kernel<12>, grid, blk, 0, x, residual, w1, scale_by, w2, rows, d, eps, h, xn); break;
+    default: e = gq_launch(ctx, add_norm_norm_kernel<12>, grid, blk, 0, x, residual, w1, scale_by, w2, rows, d, eps, h, xn); break;
+  }
+  GQ_CUDA_TRY(ctx, e);
+  return GQ_OK;
+}
+
 int gq_head_norm_rope(gq_ctx *ctx, const float *x, int64_t t, int64_t heads, int64_t head_dim, const float *w,
                       float eps, const uint32_t *positions, float theta, int64_t rotary_dim, float *y,
                       int64_t y_tok_stride) {
@@ -1035,7 +1152,7 @@ int gq_attention(gq_ctx *ctx, const float *q, int64_t batch, int64_t t, int64_t 
   if (ring) {
     const int64_t target = 4 * (int64_t)ctx->num_sms;
     int64_t per = (rows * active + target - 1) / target;  // keys per CTA for `target` CTAs
-    per = std::max<int64_t>(16, (per + kSubKeys - 1) / kSubKeys * kSubKeys);
+    per = std::max<int64_t>(32, (per + kSubKeys - 1) / kSubKeys * kSubKeys);
     per = std::max<int64_t>(per, (active + kMaxSplits - 1) / kMaxSplits);
     chunk = (int)std::min<int64_t>(per, 1 << 30);
   } else {
@@ -1072,9 +1189,9 @@ int gq_attention(gq_ctx *ctx, const float *q, int64_t batch, int64_t t, int64_t 
   }
   GQ_CUDA_TRY(ctx, e);
   if (a.splits > 1) {
-    const int ct = (int)std::min<int64_t>(256, std::max<int64_t>(32, (head_dim / 4 + 31) / 32 * 32));
-    GQ_CUDA_TRY(ctx, gq_launch(ctx, attn_combine_kernel, dim3((unsigned)(batch * t * hq)), dim3(ct), 0, a.part_o,
-                               a.part_ml, batch * t * hq, hq, head_dim, a.splits, out));
+    const dim3 cgrid((unsigned)(batch * t * hq), (unsigned)((head_dim + 127) / 128));
+    GQ_CUDA_TRY(ctx, gq_launch(ctx, attn_combine_kernel, cgrid, dim3(256), 0, a.part_o, a.part_ml, batch * t * hq, hq,
+                               head_dim, a.splits, out));
   }
   return GQ_OK;
 }

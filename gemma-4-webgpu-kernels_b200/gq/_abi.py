@@ -80,6 +80,8 @@ SIGNATURES = {
     "gq_rms_norm": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_float, c_void_p, c_int64]),
     "gq_add_rms_norm": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_float, c_void_p,
                                 c_void_p]),
+    "gq_add_rms_norm_norm": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_float, c_void_p,
+                                     c_void_p, c_void_p, c_void_p]),
     "gq_head_norm_rope": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_float, c_void_p,
                                   c_float, c_int64, c_void_p, c_int64]),
     "gq_rope": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_float, c_int64, c_void_p,

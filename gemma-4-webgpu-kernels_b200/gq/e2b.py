@@ -327,6 +327,8 @@ class Decoder:
         add("ple_combine", lib.gq_add_rms_norm, ctx, V(self.emb), V(self.proj), B * L, P, F("ple_proj_norm"), eps,
             V(self.rsqrt2), V(self.ple))
         S = p + 1
+        # input norm of layer 0; later layers get theirs fused into the previous layer's last norm
+        add("l0.input_norm", lib.gq_rms_norm, ctx, V(self.h), B, H, F("l0.input_ln"), eps, V(self.x), H)
         for i in range(L):
             pre = f"l{i}."
             dh = c.dh(i)
@@ -336,7 +338,6 @@ class Decoder:
             kvd = c.heads_kv * dh
             cstride = self.capacity * kvd
             # attention block (rust/src/model.rs:214-219, 233-300)
-            add(pre + "input_norm", lib.gq_rms_norm, ctx, V(self.h), B, H, F(pre + "input_ln"), eps, V(self.x), H)
             add(pre + "q_proj", lib.gq_linear, ctx, V(self.x), B, H, Q(pre + "q_proj"), V(self.q))
             add(pre + "q_norm_rope", lib.gq_head_norm_rope, ctx, V(self.q), B, c.heads_q, dh, F(pre + "q_norm"), eps,
                 V(self.pos), c_float(theta), rot, V(self.qr), c.heads_q * dh)
@@ -356,10 +357,10 @@ class Decoder:
                 c.heads_kv, cstride, V(self.pos), None, 0, c_float(1.0), c.window_of(i), c_float(0.0),
                 GQ_ATTN_KPOS_IDENTITY, V(self.attn))
             add(pre + "o_proj", lib.gq_linear, ctx, V(self.attn), B, c.heads_q * dh, Q(pre + "o_proj"), V(self.o))
-            add(pre + "post_attn", lib.gq_add_rms_norm, ctx, V(self.h), V(self.o), B, H, F(pre + "post_attn_ln"), eps,
-                None, V(self.h))
+            # h = h + post_attn_norm(o), then x = pre_ffn_norm(h): one pass (rust/src/model.rs:219, 223)
+            add(pre + "post_attn", lib.gq_add_rms_norm_norm, ctx, V(self.h), V(self.o), B, H, F(pre + "post_attn_ln"),
+                eps, None, F(pre + "pre_ffn_ln"), V(self.h), V(self.x))
             # GeGLU MLP (rust/src/model.rs:221-227)
-            add(pre + "pre_ffn_norm", lib.gq_rms_norm, ctx, V(self.h), B, H, F(pre + "pre_ffn_ln"), eps, V(self.x), H)
             add(pre + "gate_up", lib.gq_linear_geglu, ctx, V(self.x), B, H, Q(pre + "gate"), Q(pre + "up"),
                 V(self.ff))
             add(pre + "down", lib.gq_linear, ctx, V(self.ff), B, c.inter, Q(pre + "down"), V(self.o))
@@ -369,10 +370,12 @@ class Decoder:
             add(pre + "ple_gate", lib.gq_linear_gelu_mul_cols, ctx, V(self.h), B, H, Q(pre + "ple_gate"),
                 V(self.ple), L * P, i * P, V(self.inj))
             add(pre + "ple_proj", lib.gq_linear, ctx, V(self.inj), B, P, Q(pre + "ple_proj"), V(self.o))
-            add(pre + "ple_norm", lib.gq_add_rms_norm, ctx, V(self.h), V(self.o), B, H, F(pre + "ple_norm"), eps,
-                F(pre + "layer_scalar"), V(self.h))
-        # final norm + lm_head with the soft-cap (rust/src/model.rs:183-192)
-        add("final_norm", lib.gq_rms_norm, ctx, V(self.h), B, H, F("final_norm"), eps, V(self.x), H)
+            # h = (h + ple_norm(inj)) * layer_scalar, then the next layer's input norm (or the
+            # final norm, rust/src/model.rs:183) of h: one pass
+            nxt = f"l{i + 1}.input_ln" if i + 1 < L else "final_norm"
+            add(pre + "ple_norm", lib.gq_add_rms_norm_norm, ctx, V(self.h), V(self.o), B, H, F(pre + "ple_norm"), eps,
+                F(pre + "layer_scalar"), F(nxt), V(self.h), V(self.x))
+        # lm_head with the soft-cap on the final-normed h (rust/src/model.rs:183-192)
         add("lm_head", lib.gq_linear_softcap, ctx, V(self.x), B, H, Q("lm_head"), c_float(c.lm_softcap),
             V(self.logits), c.vocab, 0)
         return calls

@@ -192,6 +192,13 @@ int gq_rms_norm(gq_ctx *ctx, const float *x, int64_t rows, int64_t d, const floa
 int gq_add_rms_norm(gq_ctx *ctx, const float *residual, const float *x, int64_t rows, int64_t d, const float *w,
                     float eps, const float *scale_by, float *y);
 
+/* add_rms_norm followed by rms_norm of its result (the post-norm + residual of one
+ * block and the input norm of the next: rust/src/model.rs:219 then :223, and :236
+ * then the next layer's :214), in one pass: h = (residual + rms_norm(x, w1)) * scale_by[0],
+ * xn = rms_norm(h, w2). Results equal the two calls exactly. h may alias residual. */
+int gq_add_rms_norm_norm(gq_ctx *ctx, const float *residual, const float *x, int64_t rows, int64_t d, const float *w1,
+                         float eps, const float *scale_by, const float *w2, float *h, float *xn);
+
 /* Backend::head_norm_rope (rust/src/backend.rs:148-154) and Backend::rope
  * (rust/src/backend.rs:118-119; CPU rust/src/backend_cpu.rs:248-268) on x [t, heads,
  * head_dim]: per-head weighted RMSNorm (head_norm_rope only), then the half-split

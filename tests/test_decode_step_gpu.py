@@ -60,6 +60,31 @@ def test_add_rms_norm(g, with_scalar):
     assert rel(got, o.add_rms_norm(r, x, w, 1e-6, s if with_scalar else None)) <= OP_REL
 
 
+@pytest.mark.parametrize("rows,d,with_scalar", [(1, 1536, False), (64, 1536, True), (5, 48, True), (3, 7, False)])
+def test_add_rms_norm_norm_equals_the_two_calls(g, rows, d, with_scalar):
+    """The fused post-norm + next input norm gives exactly the two separate ops."""
+    import torch
+
+    x = g.tensor(synth.normal(115 + d, rows * d).reshape(rows, d), (rows, d))
+    r = g.tensor(synth.normal(116 + d, rows * d).reshape(rows, d), (rows, d))
+    w1 = g.tensor(synth.uniform(117, d, 0.9, 1.1), (d,))
+    w2 = g.tensor(synth.uniform(118, d, 0.9, 1.1), (d,))
+    s = g.tensor([1.05], (1,)) if with_scalar else None
+    h_ref = g.add_rms_norm(r, x, w1, 1e-6, s)
+    x_ref = g.rms_norm(h_ref, w2, 1e-6)
+    h = g.zeros((rows, d))
+    xn = g.zeros((rows, d))
+    g._check(g.lib.gq_add_rms_norm_norm(g.ctx, c_void_p(r.ptr()), c_void_p(x.ptr()), rows, d, c_void_p(w1.ptr()),
+                                        c_float(1e-6), c_void_p(s.ptr()) if s is not None else None,
+                                        c_void_p(w2.ptr()), c_void_p(h.ptr()), c_void_p(xn.ptr())), "fused")
+    assert np.array_equal(g.readback(h), g.readback(h_ref))
+    assert np.array_equal(g.readback(xn), g.readback(x_ref))
+    want = o.add_rms_norm(g.readback(r).reshape(rows, d), g.readback(x).reshape(rows, d),
+                          g.readback(w1), 1e-6, [1.05] if with_scalar else None)
+    assert rel(g.readback(h), want) <= OP_REL
+    del torch
+
+
 @pytest.mark.parametrize("t,heads,dh,rot", [(3, 4, 16, 8), (2, 8, 256, 256), (2, 1, 512, 128), (4, 2, 16, 8)])
 def test_head_norm_rope_and_rope(g, t, heads, dh, rot):
     x = synth.normal(120 + dh, t * heads * dh).reshape(t, heads, dh)
