@@ -11,6 +11,10 @@ can select launches of that kernel by name and skip the warm-up:
   lm_head   I8 [262144, 1536] soft-capped GEMV, M = 1 (tensor-core gemv_tc_kernel)
   prefill   4-bit [6144, 1536] at M = 512 (cast_bf16_kernel + prefill_tc_kernel)
   embed     config 4: 4096 ids into the 4-bit token table and the I8 PLE table
+  decode    config 5: whole E2B decode steps (gq.e2b.Decoder, --batch sequences,
+            2047-token cache); each "call" is one step (451 launches)
+  attn      batch-64 attention over 2048 cached keys at head_dim 512 (ring kernel)
+  tcx       8-row I8 GEMV [2048, 1536] (short-M tensor-core gemv_tcx_kernel)
 
 Run from the package directory (or with it on PYTHONPATH).
 """
@@ -23,8 +27,9 @@ from ctypes import c_float, c_void_p
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["config1", "lm_head", "prefill", "embed"])
+    ap.add_argument("case", choices=["config1", "lm_head", "prefill", "embed", "decode", "attn", "tcx"])
     ap.add_argument("--iters", type=int, default=8)
+    ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--warmup", type=int, default=3)
     args = ap.parse_args(argv)
 
@@ -62,6 +67,36 @@ def main(argv=None) -> int:
         x = torch.randn(512, 1536, generator=gen, device=dev)
         y = torch.empty(512, 6144, device=dev)
         calls = [lambda: lib.gq_linear(ctx, c_void_p(x.data_ptr()), 512, 1536, c_void_p(w.qw),
+                                       c_void_p(y.data_ptr()))]
+    elif args.case == "decode":
+        from . import e2b
+
+        dec = e2b.Decoder(g, e2b.e2b_config(), None, batch=args.batch, cache_len=2047, capacity=2048,
+                          device_init_seed=5)
+        dec.set_ids(np.arange(args.batch) * 4099 % synth.VOCAB)
+
+        def step():
+            dec.run()
+            return 0
+        calls = [step]
+    elif args.case == "attn":
+        from ._abi import GQ_ATTN_KPOS_IDENTITY
+
+        b, s, dh = 64, 2048, 512
+        q = torch.randn(b, 8, dh, generator=gen, device=dev)
+        kc = torch.randn(b, s, dh, generator=gen, device=dev)
+        vc = torch.randn(b, s, dh, generator=gen, device=dev)
+        pos = torch.full((b,), s - 1, dtype=torch.int32, device=dev)
+        out = torch.empty(b, 8 * dh, device=dev)
+        calls = [lambda: lib.gq_attention(ctx, c_void_p(q.data_ptr()), b, 1, 8, dh, c_void_p(kc.data_ptr()),
+                                          c_void_p(vc.data_ptr()), s, 1, s * dh, c_void_p(pos.data_ptr()), None, 0,
+                                          c_float(1.0), 0, c_float(0.0), GQ_ATTN_KPOS_IDENTITY,
+                                          c_void_p(out.data_ptr()))]
+    elif args.case == "tcx":
+        w = upload(2048, 1536, 8, True, 500)
+        x = torch.randn(8, 1536, generator=gen, device=dev)
+        y = torch.empty(8, 2048, device=dev)
+        calls = [lambda: lib.gq_linear(ctx, c_void_p(x.data_ptr()), 8, 1536, c_void_p(w.qw),
                                        c_void_p(y.data_ptr()))]
     else:
         tok = upload(synth.VOCAB, synth.HIDDEN, 4, False, 400)
