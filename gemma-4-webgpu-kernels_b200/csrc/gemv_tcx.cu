@@ -29,6 +29,8 @@
 #include <cuda_runtime.h>
 #include <math.h>
 
+#include <stdlib.h>
+
 #include <algorithm>
 
 #include "tc_common.cuh"
@@ -60,6 +62,8 @@ struct TcxArgs {
   const uint32_t *bad;    // [M] non-finite x row
   int tile_rows;          // MMA N: multiple of 16
   int mh;                 // 0: one M=64 MMA (<= 16 tokens); 1 or 2: M=128 halves
+  int wa;                 // 1: weights are the A operand (M = 128 rows), limb rows the B operand (N = lrows)
+  int lrows;              // limb rows per tile when wa (4*M rounded up to 16, <= 256)
   int kblocks, kbr;
   int raw_stages, mma_stages, xa_stages, xi, xi_log2;
   int raw_bytes, mma_bytes, xa_tile;
@@ -207,8 +211,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int kBars = 2 * kMaxRaw + 2 * kMaxMma + 2 * kMaxXa + 2 * kMaxIss + 1;
   const int MH = a.mh > 0 ? a.mh : 1;  // accumulator halves
   // D = A * B^T: A = limb rows (s8, M = 64 or 128), B = weight rows (s8, N = tile_rows), D s32.
-  const uint32_t idesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(a.tile_rows >> 3) << 17) |
-                         ((uint32_t)((a.mh == 0 ? 64 : 128) >> 4) << 24);
+  const uint32_t idesc = a.wa ? ((2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(a.lrows >> 3) << 17) |
+                                 ((uint32_t)(128 >> 4) << 24))
+                              : ((2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(a.tile_rows >> 3) << 17) |
+                                 ((uint32_t)((a.mh == 0 ? 64 : 128) >> 4) << 24));
+  // accumulator columns per (issuer, weight): [NW][LR] when wa, [MH][NW][tile_rows] otherwise
+  const int acc_cols = a.wa ? NW * a.lrows : MH * NW * a.tile_rows;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -436,7 +444,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---- MMA issue: K-blocks dealt round-robin to the issuers ----
     const int iss = warp - 1;
     if (lane == 0 && iss < NI) {
-      const uint32_t dcol = tmem + (uint32_t)(iss * MH * NW * a.tile_rows);
+      const uint32_t dcol = tmem + (uint32_t)(iss * acc_cols);
       bool ok = !*abort_flag, first = true;
       int ord = 0;  // K-blocks this issuer has consumed (its limb-ring position)
       const int S = DIRECT ? RS : MS;
@@ -460,6 +468,14 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int h = 0; h < NW; ++h) {
             const uint64_t bd = bd0 + (uint64_t)((h * tile_bytes) >> 4);
+            if (a.wa) {  // D[weight row][limb row] = W . L^T
+              const uint32_t d = dcol + (uint32_t)(h * a.lrows);
+              tc_mma_i8(d, bd, ad, idesc, first ? 0u : 1u);
+              tc_mma_i8(d, bd + 2, ad + 2, idesc, 1u);
+              tc_mma_i8(d, bd + 4, ad + 4, idesc, 1u);
+              tc_mma_i8(d, bd + 6, ad + 6, idesc, 1u);
+              continue;
+            }
             for (int hh = 0; hh < MH; ++hh) {
               const uint32_t d = dcol + (uint32_t)((hh * NW + h) * a.tile_rows);
               const uint64_t ah = ad + (uint64_t)(hh * (16384 >> 4));  // rows 128*hh.. of the limb tile
@@ -498,7 +514,60 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3, limb = lane & 3;
     bool ok = !*abort_flag && wait_phase(sc_bar, 0u);
     for (int i = 0; i < NI; ++i) ok = ok && wait_phase(&acc_full[i], 0u);
-    if (__all_sync(0xffffffffu, ok)) {
+    if (__all_sync(0xffffffffu, ok) && a.wa) {
+      // Thread et owns weight row et (TMEM lane et); columns 4*tok + limb hold the
+      // limb dot products of token tok, recombined here in int64.
+      tc_fence_after();
+      const int nl = et, n = n_begin + nl;
+      const bool nok = n < n_end;
+      const float sc0 = scb[nl], sc1 = NW == 2 ? scb[a.tile_rows + nl] : 0.0f;
+      for (int t0 = 0; t0 < a.M; t0 += 4) {
+        long long T[NW][4];
+#pragma unroll
+        for (int h = 0; h < NW; ++h) {
+          uint32_t d[kMaxIss][16];
+          const uint32_t col = (uint32_t)(h * a.lrows + 4 * t0) + ((uint32_t)(quarter * 32) << 16);
+#pragma unroll
+          for (int i = 0; i < kMaxIss; ++i)
+            if (i < NI) tmem_ld16_nowait(tmem + col + (uint32_t)(i * acc_cols), d[i]);
+#pragma unroll
+          for (int t = 0; t < 4; ++t) T[h][t] = 0;
+#pragma unroll
+          for (int i = 0; i < kMaxIss; ++i)
+            if (i < NI) {
+              tmem_wait_ld16(d[i]);
+#pragma unroll
+              for (int t = 0; t < 4; ++t)
+#pragma unroll
+                for (int l = 0; l < 4; ++l) T[h][t] += (long long)(int32_t)d[i][4 * t + l] << (8 * l);
+            }
+        }
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+          const int tok = t0 + t;
+          if (!nok || tok >= a.M) continue;
+          float o;
+          if (tok_bad[tok]) {
+            o = __int_as_float(0x7fc00000);
+          } else {
+            const double pwt = tok_pw[tok];
+            const long long zct = tok_zc[tok];
+            const float v0 = __fmul_rn((float)((double)(T[0][t] - zct) * pwt), sc0);
+            if (MODE == 1) {
+              const float v1 = __fmul_rn((float)((double)(T[NW - 1][t] - zct) * pwt), sc1);
+              o = __fmul_rn(gqd::gelu_tanh(v0), v1);
+            } else if (MODE == 2) {
+              o = __fmul_rn(gqd::gelu_tanh(v0), a.bs[(size_t)tok * a.b_stride + a.b_off + n]);
+            } else if (MODE == 3) {
+              o = a.cap > 0.0f ? __fmul_rn(a.cap, tanhf(__fdiv_rn(v0, a.cap))) : v0;
+            } else {
+              o = v0;
+            }
+          }
+          a.y[(size_t)tok * a.ldy + a.y_col0 + n] = o;
+        }
+      }
+    } else if (__all_sync(0xffffffffu, ok)) {
       tc_fence_after();
       for (int hh = 0; hh < MH; ++hh) {
         // M=64: lane quarter q holds limb rows 16q.. in lanes 0-15 (tokens 4q..4q+3);
@@ -611,6 +680,7 @@ int launch_xm(gq_ctx *ctx, int mode, const CUtensorMap &m1, const CUtensorMap &m
 }
 
 struct TcxPlan {
+  int wa, lrows;
   int tile_rows, mh, gx, slice_rows, kblocks, kbr, raw_stages, mma_stages, xa_stages, xi, raw_bytes, mma_bytes,
       xa_tile, issuers, tmem_cols;
   size_t smem;
@@ -621,16 +691,19 @@ int mh_of(int64_t m) { return m <= 16 ? 0 : (m <= 32 ? 1 : 2); }
 // One tile of weight rows per CTA. Weights taller than num_sms tiles run as
 // row slices of num_sms * tile_rows rows. Rings sized to the SM's shared memory:
 // the limb ring gets up to ~half of it, the weight rings the rest.
-bool tcx_plan(const gq_ctx *ctx, const gq_qweight *w, int64_t m, int nw, TcxPlan &p) {
+bool tcx_plan(const gq_ctx *ctx, const gq_qweight *w, int64_t m, int nw, bool wa, TcxPlan &p) {
   const bool direct = (w->bits == 8 && w->signed_i8);
   const int kb_bytes = kKB * w->bits / 8;
-  p.mh = mh_of(m);
-  const int MH = p.mh > 0 ? p.mh : 1;
-  const int xa_rows = p.mh == 0 ? 64 : 128 * p.mh;
+  p.wa = wa;
+  p.mh = wa ? 0 : mh_of(m);
+  p.lrows = (int)((4 * m + 15) / 16 * 16);
+  const int MH = (wa || p.mh == 0) ? 1 : p.mh;
+  const int xa_rows = wa ? p.lrows : (p.mh == 0 ? 64 : 128 * p.mh);
   p.xa_tile = xa_rows * 128;
-  const int max_tile = std::min(256 / nw, 512 / (MH * nw)) / 16 * 16;
+  const int max_tile = wa ? 128 : std::min(256 / nw, 512 / (MH * nw)) / 16 * 16;
   const int64_t rows0 = (w->n + ctx->num_sms - 1) / ctx->num_sms;
-  p.tile_rows = (int)std::min<int64_t>(max_tile, std::max<int64_t>(16, (rows0 + 15) / 16 * 16));
+  p.tile_rows = wa ? 128 : (int)std::min<int64_t>(max_tile, std::max<int64_t>(16, (rows0 + 15) / 16 * 16));
+  const int acc_cols = wa ? nw * p.lrows : MH * nw * p.tile_rows;
   p.slice_rows = (int)std::min<int64_t>(w->n, (int64_t)ctx->num_sms * p.tile_rows);
   p.gx = (int)((p.slice_rows + p.tile_rows - 1) / p.tile_rows);
   p.kblocks = (int)((w->k + kKB - 1) / kKB);
@@ -639,7 +712,7 @@ bool tcx_plan(const gq_ctx *ctx, const gq_qweight *w, int64_t m, int nw, TcxPlan
   const size_t budget = ctx->smem_optin - 1024;
   // issuers: TMEM columns, work units; then the limb ring: XI >= 2 slots each
   const int units_hint = direct ? p.kblocks : p.kblocks;
-  p.issuers = std::max(1, std::min(std::min(kMaxIss, units_hint), 512 / (MH * nw * p.tile_rows)));
+  p.issuers = std::max(1, std::min(std::min(kMaxIss, units_hint), 512 / acc_cols));
   const size_t xa_budget = std::min<size_t>(budget / 2 + 16384, 131072);
   while (p.issuers > 1 && (size_t)p.issuers * 2 * p.xa_tile > xa_budget) --p.issuers;
   p.xi = (int)std::max<size_t>(2, std::min<size_t>(kMaxXa / p.issuers, xa_budget / ((size_t)p.issuers * p.xa_tile)));
@@ -650,7 +723,8 @@ bool tcx_plan(const gq_ctx *ctx, const gq_qweight *w, int64_t m, int nw, TcxPlan
     p.mma_bytes = 0;
     p.mma_stages = 0;
   } else {
-    p.kbr = std::max(1, std::min(p.kblocks, 256 / kb_bytes));
+    // K-blocks per packed stage: up to 256-byte TMA rows, stages of at most ~32 KB
+    p.kbr = std::max(1, std::min(std::min(p.kblocks, 256 / kb_bytes), 32768 / (nw * p.tile_rows * kb_bytes)));
     p.raw_bytes = (nw * p.tile_rows * p.kbr * kb_bytes + 1023) / 1024 * 1024;
     p.mma_bytes = nw * tile_bytes;
   }
@@ -691,7 +765,7 @@ bool tcx_plan(const gq_ctx *ctx, const gq_qweight *w, int64_t m, int nw, TcxPlan
   while (p.xi & (p.xi - 1)) --p.xi;  // a power of two (slots and phases by mask and shift)
   p.xa_stages = p.issuers * p.xi;
   if (p.xa_stages > kMaxXa || p.xi < 2) return false;
-  const int cols = p.issuers * MH * nw * p.tile_rows;
+  const int cols = p.issuers * acc_cols;
   p.tmem_cols = 32;
   while (p.tmem_cols < cols) p.tmem_cols <<= 1;
   p.smem = tcx_layout(p.xa_stages, p.xa_tile, p.raw_stages, p.raw_bytes, p.mma_stages, p.mma_bytes, sc_bytes).total;
@@ -727,6 +801,16 @@ cudaError_t launch_limbs(gq_ctx *ctx, const float *x, int64_t m, int64_t k, int6
                    sumx, bad);
 }
 
+// Operand layout. Default: limb rows as A (M = 64 / 128) and weight tiles of
+// 16..256 rows as N, one tile per SM. GQ_TCX_WA=1 selects weights as A (128-row
+// tiles, limb rows as N up to 256): full-size MMAs but 8-12x fewer CTAs; measured
+// slower on the E2B sweep (M = 32: 4.87 vs 3.35 ms, M = 64: 6.92 vs 4.13 ms).
+bool tcx_weights_as_a(int64_t m) {
+  const char *e = getenv("GQ_TCX_WA");
+  (void)m;
+  return e && *e == '1';
+}
+
 // Rows [r0, r0 + n) of a weight as a weight of its own (same layout).
 gq_qweight row_slice(const gq_qweight *w, int64_t r0, int64_t n) {
   gq_qweight v = *w;
@@ -746,7 +830,7 @@ bool gq_gemv_tcx_supported(gq_ctx *ctx, const gq_qweight *w, const float *x, int
   if (w->row_bytes % 16 != 0 || (uintptr_t)w->bytes % 16 != 0 || (uintptr_t)x % 16 != 0) return false;
   if (gq_encode_fn() == nullptr) return false;
   TcxPlan p;
-  return tcx_plan(ctx, w, m, nw, p);
+  return tcx_plan(ctx, w, m, nw, tcx_weights_as_a(m), p);
 }
 
 int gq_gemv_tcx_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq_qweight *w, const gq_qweight *w2,
@@ -754,7 +838,8 @@ int gq_gemv_tcx_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const g
                        int64_t y_col0) {
   const int nw = (mode == 1) ? 2 : 1;
   TcxPlan p;
-  if (!tcx_plan(ctx, w, m, nw, p)) return gq_fail(ctx, GQ_ERR_UNSUPPORTED, "gemv_tcx: no stage configuration fits");
+  if (!tcx_plan(ctx, w, m, nw, tcx_weights_as_a(m), p))
+    return gq_fail(ctx, GQ_ERR_UNSUPPORTED, "gemv_tcx: no stage configuration fits");
   const int64_t kp = (int64_t)p.kblocks * kKB;
   const size_t limb_bytes = ((size_t)(4 * m * kp) + 255) & ~size_t(255);
   void *wsp = nullptr;
@@ -772,7 +857,7 @@ int gq_gemv_tcx_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const g
     GQ_CUDA_TRY(ctx, launch_limbs<8>(ctx, x, m, w->k, kp, limbs, xexp, sumx, bad));
   }
   CUtensorMap mx;
-  if (encode_limbs(&mx, limbs, m, kp, p.mh == 0 ? 64 : 128 * p.mh) != CUDA_SUCCESS)
+  if (encode_limbs(&mx, limbs, m, kp, p.wa ? p.lrows : (p.mh == 0 ? 64 : 128 * p.mh)) != CUDA_SUCCESS)
     return gq_fail(ctx, GQ_ERR_CUDA, "gemv_tcx: limb tensor map");
   for (int64_t r0 = 0; r0 < w->n; r0 += p.slice_rows) {
     const int64_t rows = std::min<int64_t>(p.slice_rows, w->n - r0);
@@ -799,6 +884,8 @@ int gq_gemv_tcx_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const g
     a.bad = bad;
     a.tile_rows = p.tile_rows;
     a.mh = p.mh;
+    a.wa = p.wa;
+    a.lrows = p.lrows;
     a.kblocks = p.kblocks;
     a.kbr = p.kbr;
     a.raw_stages = p.raw_stages;

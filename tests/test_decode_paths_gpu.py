@@ -110,3 +110,35 @@ def test_extreme_activations_both_paths(g, monkeypatch, path, m):
     x[:, 7] = 300.0
     got = g.readback(g.linear(g.tensor(x, x.shape), g.quant_tensor(w)))
     assert rel_l2(got, oracle.linear(x, w)) <= REL_L2, "outlier"
+
+
+@pytest.mark.parametrize("wa", ["0", "1"])
+@pytest.mark.parametrize("n,k,bits,signed", [(2048, 1536, 8, True), (6144, 1536, 4, False), (1536, 6144, 2, False),
+                                             (300, 640, 8, False), (40000, 1536, 8, True)])
+@pytest.mark.parametrize("m", [5, 16, 24, 64])
+def test_short_m_tensor_core_layouts(g, monkeypatch, wa, n, k, bits, signed, m):
+    """Both operand layouts of the short-M tensor-core GEMV (limb rows as A with
+    weight tiles as N, or weight tiles as A with limb rows as N) at every size."""
+    monkeypatch.setenv("GQ_DECODE_TC", "2")
+    monkeypatch.setenv("GQ_TCX_WA", wa)
+    w = synth.random_qweight(3500 + n + k + bits, n, k, bits, signed)
+    x = synth.normal(3501 + m, m * k).reshape(m, k)
+    got = g.readback(g.linear(g.tensor(x, x.shape), g.quant_tensor(w)))
+    assert rel_l2(got, oracle.linear(x, w)) <= REL_L2
+
+
+@pytest.mark.parametrize("wa", ["0", "1"])
+@pytest.mark.parametrize("m", [7, 40])
+def test_short_m_tensor_core_layouts_fused(g, monkeypatch, wa, m):
+    monkeypatch.setenv("GQ_DECODE_TC", "2")
+    monkeypatch.setenv("GQ_TCX_WA", wa)
+    n, k = 6144, 1536
+    wg = synth.random_qweight(3601, n, k, 4, False)
+    wu = synth.random_qweight(3602, n, k, 4, False)
+    x = synth.normal(3603, m * k).reshape(m, k)
+    got = g.readback(g.linear_geglu(g.tensor(x, x.shape), g.quant_tensor(wg), g.quant_tensor(wu)))
+    assert rel_l2(got, oracle.linear_geglu(x, wg, wu)) <= REL_L2
+    w = synth.random_qweight(3604, 256, k, 8, True)
+    b = synth.normal(3605, m * 8960).reshape(m, 8960)
+    got = g.readback(g.linear_gelu_mul_cols(g.tensor(x, x.shape), g.quant_tensor(w), g.tensor(b, b.shape), 768))
+    assert rel_l2(got, oracle.linear_gelu_mul_cols(x, w, b, 768)) <= REL_L2
