@@ -8,8 +8,9 @@
 //    rows once, as a [4*M, Kp] s8 matrix in global memory (row = token*4 + limb,
 //    K permuted inside each 16-code group like the widened weights), plus each
 //    row's exponent, sum of fixed-point values and a non-finite flag;
-//  * the GEMV streams that matrix by TMA, one swizzled tile of 64 / 128 / 256 limb
-//    rows x 128 bytes per K-block, as the A operand: one M = 64 MMA for up to 16
+//  * the pre-pass lays the matrix out as the GEMV's swizzled shared-memory tiles
+//    (64 / 128 / 256 limb rows x 128 bytes per K-block, zero rows past 4M), so the
+//    GEMV fetches each K-block's A operand with one 1-D bulk copy: one M = 64 MMA for up to 16
 //    tokens (accumulator row r in TMEM lane 32*(r/16) + r%16), else one or two
 //    M = 128 MMAs (row r of half h in lane r of that half's accumulator);
 //  * weights are the B operand exactly as in gemv_tc.cu (I8 rows straight from
@@ -60,6 +61,7 @@ struct TcxArgs {
   const int *xexp;        // [M] per-row exponent s_m (X = rint(x * 2^s_m))
   const long long *sumx;  // [M] sum_k X
   const uint32_t *bad;    // [M] non-finite x row
+  const uint8_t *limbs;   // [kblocks][xa_rows][128 B] pre-swizzled A tiles
   int tile_rows;          // MMA N: multiple of 16
   int mh;                 // 0: one M=64 MMA (<= 16 tokens); 1 or 2: M=128 halves
   int wa;                 // 1: weights are the A operand (M = 128 rows), limb rows the B operand (N = lrows)
@@ -110,12 +112,26 @@ __device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, %0;" ::"r
 // ---- pre-pass: x row m -> 30-bit fixed point -> four s8 limb rows ------------
 // Same arithmetic as the in-CTA staging of gemv_tc.cu: s = 30 - e with
 // max|x| < 2^e, X = rint(x * 2^s), balanced base-256 digits from X + 0x808080.
+// The limbs are written as the GEMV's shared-memory A tiles: K-block kb of limb
+// row r at limbs + kb*xa_rows*128 + r*128, 16-byte chunk c stored at chunk
+// c ^ (r % 8) (the 128-byte swizzle), so one K-block tile is one contiguous
+// xa_rows*128-byte block that a 1-D bulk copy moves as is. Block M zero-fills
+// the tile rows past 4*M.
 template <int BITS>
-__global__ void xlimbs_kernel(const float *x, int K, int Kp, uint8_t *limbs, int *xexp, long long *sumx,
-                              uint32_t *bad) {
+__global__ void xlimbs_kernel(const float *x, int K, int Kp, int M, int xa_rows, uint8_t *limbs, int *xexp,
+                              long long *sumx, uint32_t *bad) {
   gqd::griddep_wait();
   gqd::griddep_launch_dependents();
   const int m = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (m == M) {  // zero rows 4M .. xa_rows-1 of every K-block tile
+    const int pad = xa_rows - 4 * M, kbs = Kp / kKB;
+    for (int i = tid; i < kbs * pad * 8; i += kThreads) {
+      const int kb = i / (pad * 8), rem = i - kb * pad * 8;
+      *reinterpret_cast<uint4 *>(limbs + ((size_t)kb * xa_rows + 4 * M) * 128 + (size_t)rem * 16) =
+          make_uint4(0u, 0u, 0u, 0u);
+    }
+    return;
+  }
   const float4 *xr = reinterpret_cast<const float4 *>(x + (size_t)m * K);
   __shared__ float wmax[8];
   __shared__ uint32_t wbad[8];
@@ -176,10 +192,13 @@ __global__ void xlimbs_kernel(const float *x, int K, int Kp, uint8_t *limbs, int
       wv[4 * q + 2] = prmt(t01b, t23b, 0x5410);
       wv[4 * q + 3] = prmt(t01b, t23b, 0x7632);
     }
+    const int kb = gi >> 3, c = gi & 7;
 #pragma unroll
-    for (int l = 0; l < 4; ++l)
-      *reinterpret_cast<uint4 *>(limbs + (size_t)(4 * m + l) * Kp + 16 * gi) =
+    for (int l = 0; l < 4; ++l) {
+      const int r = 4 * m + l;
+      *reinterpret_cast<uint4 *>(limbs + ((size_t)kb * xa_rows + r) * 128 + ((c ^ (r & 7)) << 4)) =
           make_uint4(wv[l], wv[4 + l], wv[8 + l], wv[12 + l]);
+    }
   }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
@@ -199,10 +218,10 @@ __global__ void xlimbs_kernel(const float *x, int K, int Kp, uint8_t *limbs, int
 // Control flow is division-free in the steady state (ring slots and phases are
 // stepped incrementally): the producer and issuer threads run one K-block every
 // few tens of cycles, so they never pace the pipeline.
-template <int BITS, bool SIGNED, int MODE>
+template <int BITS, bool SIGNED, int MODE, bool WA>
 __global__ void __launch_bounds__(kThreads, 1)
     gemv_tcx_kernel(const __grid_constant__ CUtensorMap map_w, const __grid_constant__ CUtensorMap map_w2,
-                    const __grid_constant__ CUtensorMap map_x, const TcxArgs a) {
+                    const TcxArgs a) {
   constexpr int NW = (MODE == 1) ? 2 : 1;
   constexpr bool DIRECT = (BITS == 8 && SIGNED);
   constexpr int KB_BYTES = kKB * BITS / 8;
@@ -211,12 +230,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int kBars = 2 * kMaxRaw + 2 * kMaxMma + 2 * kMaxXa + 2 * kMaxIss + 1;
   const int MH = a.mh > 0 ? a.mh : 1;  // accumulator halves
   // D = A * B^T: A = limb rows (s8, M = 64 or 128), B = weight rows (s8, N = tile_rows), D s32.
-  const uint32_t idesc = a.wa ? ((2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(a.lrows >> 3) << 17) |
+  const uint32_t idesc = WA ? ((2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(a.lrows >> 3) << 17) |
                                  ((uint32_t)(128 >> 4) << 24))
                               : ((2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(a.tile_rows >> 3) << 17) |
                                  ((uint32_t)((a.mh == 0 ? 64 : 128) >> 4) << 24));
   // accumulator columns per (issuer, weight): [NW][LR] when wa, [MH][NW][tile_rows] otherwise
-  const int acc_cols = a.wa ? NW * a.lrows : MH * NW * a.tile_rows;
+  const int acc_cols = WA ? NW * a.lrows : MH * NW * a.tile_rows;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -295,7 +314,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   };
   auto issue_x = [&](int slot, int g) {  // limb tile of K-block g
     gqd::mbar_arrive_expect_tx(&xa_full[slot], xa_tile);
-    tma_load_2d(xa + (size_t)slot * xa_tile, &map_x, g * kKB, 0, &xa_full[slot]);
+    gqd::bulk_g2s(xa + (size_t)slot * xa_tile, a.limbs + (size_t)g * xa_tile, xa_tile, &xa_full[slot]);
   };
 
   // ---- widening of sub-byte / U8 codes: the 4 warps widen one raw stage at a time ----
@@ -468,21 +487,21 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int h = 0; h < NW; ++h) {
             const uint64_t bd = bd0 + (uint64_t)((h * tile_bytes) >> 4);
-            if (a.wa) {  // D[weight row][limb row] = W . L^T
+            if constexpr (WA) {  // D[weight row][limb row] = W . L^T
               const uint32_t d = dcol + (uint32_t)(h * a.lrows);
               tc_mma_i8(d, bd, ad, idesc, first ? 0u : 1u);
               tc_mma_i8(d, bd + 2, ad + 2, idesc, 1u);
               tc_mma_i8(d, bd + 4, ad + 4, idesc, 1u);
               tc_mma_i8(d, bd + 6, ad + 6, idesc, 1u);
-              continue;
-            }
-            for (int hh = 0; hh < MH; ++hh) {
-              const uint32_t d = dcol + (uint32_t)((hh * NW + h) * a.tile_rows);
-              const uint64_t ah = ad + (uint64_t)(hh * (16384 >> 4));  // rows 128*hh.. of the limb tile
-              tc_mma_i8(d, ah, bd, idesc, first ? 0u : 1u);
-              tc_mma_i8(d, ah + 2, bd + 2, idesc, 1u);
-              tc_mma_i8(d, ah + 4, bd + 4, idesc, 1u);
-              tc_mma_i8(d, ah + 6, bd + 6, idesc, 1u);
+            } else {
+              for (int hh = 0; hh < MH; ++hh) {
+                const uint32_t d = dcol + (uint32_t)((hh * NW + h) * a.tile_rows);
+                const uint64_t ah = ad + (uint64_t)(hh * (16384 >> 4));  // rows 128*hh.. of the limb tile
+                tc_mma_i8(d, ah, bd, idesc, first ? 0u : 1u);
+                tc_mma_i8(d, ah + 2, bd + 2, idesc, 1u);
+                tc_mma_i8(d, ah + 4, bd + 4, idesc, 1u);
+                tc_mma_i8(d, ah + 6, bd + 6, idesc, 1u);
+              }
             }
           }
           first = false;
@@ -514,7 +533,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3, limb = lane & 3;
     bool ok = !*abort_flag && wait_phase(sc_bar, 0u);
     for (int i = 0; i < NI; ++i) ok = ok && wait_phase(&acc_full[i], 0u);
-    if (__all_sync(0xffffffffu, ok) && a.wa) {
+    if (WA && __all_sync(0xffffffffu, ok)) {
       // Thread et owns weight row et (TMEM lane et); columns 4*tok + limb hold the
       // limb dot products of token tok, recombined here in int64.
       tc_fence_after();
@@ -567,7 +586,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           a.y[(size_t)tok * a.ldy + a.y_col0 + n] = o;
         }
       }
-    } else if (__all_sync(0xffffffffu, ok)) {
+    } else if (!WA && __all_sync(0xffffffffu, ok)) {
       tc_fence_after();
       for (int hh = 0; hh < MH; ++hh) {
         // M=64: lane quarter q holds limb rows 16q.. in lanes 0-15 (tokens 4q..4q+3);
@@ -655,27 +674,26 @@ __global__ void __launch_bounds__(kThreads, 1)
 namespace {
 
 template <int BITS, bool SIGNED, int MODE>
-int launch_x(gq_ctx *ctx, const CUtensorMap &m1, const CUtensorMap &m2, const CUtensorMap &mx, const TcxArgs &a,
-             dim3 grid, size_t smem) {
-  auto kern = gemv_tcx_kernel<BITS, SIGNED, MODE>;
-  static bool attr_set[64] = {};
+int launch_x(gq_ctx *ctx, const CUtensorMap &m1, const CUtensorMap &m2, const TcxArgs &a, dim3 grid, size_t smem) {
+  auto kern = a.wa ? gemv_tcx_kernel<BITS, SIGNED, MODE, true> : gemv_tcx_kernel<BITS, SIGNED, MODE, false>;
+  static bool attr_set[64][2] = {};
   const int dev = ctx->device & 63;
-  if (!attr_set[dev]) {
+  if (!attr_set[dev][a.wa]) {
     GQ_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ctx->smem_optin));
-    attr_set[dev] = true;
+    attr_set[dev][a.wa] = true;
   }
-  GQ_CUDA_TRY(ctx, gq_launch(ctx, kern, grid, dim3(kThreads), smem, m1, m2, mx, a));
+  GQ_CUDA_TRY(ctx, gq_launch(ctx, kern, grid, dim3(kThreads), smem, m1, m2, a));
   return GQ_OK;
 }
 
 template <int BITS, bool SIGNED>
-int launch_xm(gq_ctx *ctx, int mode, const CUtensorMap &m1, const CUtensorMap &m2, const CUtensorMap &mx,
-              const TcxArgs &a, dim3 grid, size_t smem) {
+int launch_xm(gq_ctx *ctx, int mode, const CUtensorMap &m1, const CUtensorMap &m2, const TcxArgs &a, dim3 grid,
+              size_t smem) {
   switch (mode) {
-    case 0: return launch_x<BITS, SIGNED, 0>(ctx, m1, m2, mx, a, grid, smem);
-    case 1: return launch_x<BITS, SIGNED, 1>(ctx, m1, m2, mx, a, grid, smem);
-    case 2: return launch_x<BITS, SIGNED, 2>(ctx, m1, m2, mx, a, grid, smem);
-    default: return launch_x<BITS, SIGNED, 3>(ctx, m1, m2, mx, a, grid, smem);
+    case 0: return launch_x<BITS, SIGNED, 0>(ctx, m1, m2, a, grid, smem);
+    case 1: return launch_x<BITS, SIGNED, 1>(ctx, m1, m2, a, grid, smem);
+    case 2: return launch_x<BITS, SIGNED, 2>(ctx, m1, m2, a, grid, smem);
+    default: return launch_x<BITS, SIGNED, 3>(ctx, m1, m2, a, grid, smem);
   }
 }
 
@@ -783,22 +801,12 @@ CUresult encode_w(CUtensorMap *map, const gq_qweight *w, const TcxPlan &p) {
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
 
-// The limb matrix [4*m, kp] s8; box = xa_rows rows x one 128-byte K-block, swizzled.
-CUresult encode_limbs(CUtensorMap *map, const uint8_t *limbs, int64_t m, int64_t kp, int xa_rows) {
-  cuuint64_t dims[2] = {(cuuint64_t)kp, (cuuint64_t)(4 * m)};
-  cuuint64_t strides[1] = {(cuuint64_t)kp};
-  cuuint32_t box[2] = {128u, (cuuint32_t)xa_rows};
-  cuuint32_t estr[2] = {1, 1};
-  return gq_encode_fn()(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<uint8_t *>(limbs), dims, strides, box,
-                        estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-}
-
 template <int BITS>
-cudaError_t launch_limbs(gq_ctx *ctx, const float *x, int64_t m, int64_t k, int64_t kp, uint8_t *limbs, int *xexp,
-                         long long *sumx, uint32_t *bad) {
-  return gq_launch(ctx, xlimbs_kernel<BITS>, dim3((unsigned)m), dim3(kThreads), 0, x, (int)k, (int)kp, limbs, xexp,
-                   sumx, bad);
+cudaError_t launch_limbs(gq_ctx *ctx, const float *x, int64_t m, int64_t k, int64_t kp, int xa_rows, uint8_t *limbs,
+                         int *xexp, long long *sumx, uint32_t *bad) {
+  // m blocks write the token rows, one more zero-fills the tile rows past 4*m
+  return gq_launch(ctx, xlimbs_kernel<BITS>, dim3((unsigned)(m + (4 * m < xa_rows ? 1 : 0))), dim3(kThreads), 0, x,
+                   (int)k, (int)kp, (int)m, xa_rows, limbs, xexp, sumx, bad);
 }
 
 // Operand layout. Default: limb rows as A (M = 64 / 128) and weight tiles of
@@ -841,7 +849,8 @@ int gq_gemv_tcx_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const g
   if (!tcx_plan(ctx, w, m, nw, tcx_weights_as_a(m), p))
     return gq_fail(ctx, GQ_ERR_UNSUPPORTED, "gemv_tcx: no stage configuration fits");
   const int64_t kp = (int64_t)p.kblocks * kKB;
-  const size_t limb_bytes = ((size_t)(4 * m * kp) + 255) & ~size_t(255);
+  const int xa_rows = p.xa_tile / 128;
+  const size_t limb_bytes = ((size_t)p.kblocks * p.xa_tile + 255) & ~size_t(255);
   void *wsp = nullptr;
   int rc = gq_workspace(ctx, limb_bytes + (size_t)m * 16 + 256, &wsp);
   if (rc != GQ_OK) return rc;
@@ -850,15 +859,12 @@ int gq_gemv_tcx_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const g
   int *xexp = reinterpret_cast<int *>(sumx + m);
   uint32_t *bad = reinterpret_cast<uint32_t *>(xexp + m);
   if (w->bits == 4) {
-    GQ_CUDA_TRY(ctx, launch_limbs<4>(ctx, x, m, w->k, kp, limbs, xexp, sumx, bad));
+    GQ_CUDA_TRY(ctx, launch_limbs<4>(ctx, x, m, w->k, kp, xa_rows, limbs, xexp, sumx, bad));
   } else if (w->bits == 2) {
-    GQ_CUDA_TRY(ctx, launch_limbs<2>(ctx, x, m, w->k, kp, limbs, xexp, sumx, bad));
+    GQ_CUDA_TRY(ctx, launch_limbs<2>(ctx, x, m, w->k, kp, xa_rows, limbs, xexp, sumx, bad));
   } else {
-    GQ_CUDA_TRY(ctx, launch_limbs<8>(ctx, x, m, w->k, kp, limbs, xexp, sumx, bad));
+    GQ_CUDA_TRY(ctx, launch_limbs<8>(ctx, x, m, w->k, kp, xa_rows, limbs, xexp, sumx, bad));
   }
-  CUtensorMap mx;
-  if (encode_limbs(&mx, limbs, m, kp, p.wa ? p.lrows : (p.mh == 0 ? 64 : 128 * p.mh)) != CUDA_SUCCESS)
-    return gq_fail(ctx, GQ_ERR_CUDA, "gemv_tcx: limb tensor map");
   for (int64_t r0 = 0; r0 < w->n; r0 += p.slice_rows) {
     const int64_t rows = std::min<int64_t>(p.slice_rows, w->n - r0);
     const gq_qweight ws = row_slice(w, r0, rows);
@@ -882,6 +888,7 @@ int gq_gemv_tcx_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const g
     a.xexp = xexp;
     a.sumx = sumx;
     a.bad = bad;
+    a.limbs = limbs;
     a.tile_rows = p.tile_rows;
     a.mh = p.mh;
     a.wa = p.wa;
@@ -900,10 +907,10 @@ int gq_gemv_tcx_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const g
     a.tmem_cols = p.tmem_cols;
     a.err = ctx->dev_err;
     const dim3 grid((unsigned)((rows + p.tile_rows - 1) / p.tile_rows));
-    if (w->bits == 4) rc = launch_xm<4, false>(ctx, mode, m1, m2, mx, a, grid, p.smem);
-    else if (w->bits == 2) rc = launch_xm<2, false>(ctx, mode, m1, m2, mx, a, grid, p.smem);
-    else if (w->signed_i8) rc = launch_xm<8, true>(ctx, mode, m1, m2, mx, a, grid, p.smem);
-    else rc = launch_xm<8, false>(ctx, mode, m1, m2, mx, a, grid, p.smem);
+    if (w->bits == 4) rc = launch_xm<4, false>(ctx, mode, m1, m2, a, grid, p.smem);
+    else if (w->bits == 2) rc = launch_xm<2, false>(ctx, mode, m1, m2, a, grid, p.smem);
+    else if (w->signed_i8) rc = launch_xm<8, true>(ctx, mode, m1, m2, a, grid, p.smem);
+    else rc = launch_xm<8, false>(ctx, mode, m1, m2, a, grid, p.smem);
     if (rc != GQ_OK) return rc;
   }
   return GQ_OK;
