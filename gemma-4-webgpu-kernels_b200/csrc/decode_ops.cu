@@ -567,9 +567,8 @@ __global__ void __launch_bounds__(NT) attn_chunk_kernel(const AttnArgs a) {
 // online across sub-tiles (running max, sum and output rescaled per head).
 // Thread t owns head_dim columns 4t .. 4t+3 for all G query heads, as above.
 constexpr int kSubKeys = 8;
-constexpr int kRingStages = 3;  // 96 KB at head_dim 512: two CTAs per SM
 
-template <int NT>
+template <int NT, int kRingStages>
 __global__ void __launch_bounds__(NT) attn_ring_kernel(const AttnArgs a) {
   static_assert(NT >= kMaxGroup * kKeyBatch, "one thread per (head, key) entry of a sub-tile");
   constexpr int NWARP = NT / 32;
@@ -888,6 +887,82 @@ __global__ void __launch_bounds__(kLinWarps * 32) linear_bf16_kernel(const float
   }
 }
 
+// M > 4 rows: a 64 (weight rows) x 64 (activation rows) output tile per CTA,
+// K in chunks of 32 staged through shared memory (weights widened from bf16
+// once per chunk and shared by all 64 activation rows), 4 x 4 outputs per thread.
+constexpr int kLbT = 64, kLbK = 32;
+__global__ void __launch_bounds__(256) linear_bf16_tiled_kernel(const float *x, int64_t m, int64_t k,
+                                                                const uint16_t *w, int64_t n, float *y) {
+  __shared__ float ws[kLbK][kLbT + 4];
+  __shared__ float xs[kLbK][kLbT + 4];
+  gqd::griddep_wait();
+  gqd::griddep_launch_dependents();
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int64_t n0 = (int64_t)blockIdx.x * kLbT, m0 = (int64_t)blockIdx.y * kLbT;
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+  const int lr = tid >> 2, lk = (tid & 3) * 8;  // loader: row lr, 8 columns from lk
+  for (int64_t k0 = 0; k0 < k; k0 += kLbK) {
+    {
+      const int64_t nn = n0 + lr, kk = k0 + lk;
+      float wv[8];
+      if (nn < n && kk + 8 <= k) {
+        const uint4 u = __ldg(reinterpret_cast<const uint4 *>(w + nn * k + kk));
+        const uint32_t q[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          wv[2 * i] = bf16lo(q[i]);
+          wv[2 * i + 1] = bf16hi(q[i]);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          wv[i] = (nn < n && kk + i < k) ? __uint_as_float((uint32_t)w[nn * k + kk + i] << 16) : 0.0f;
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ws[lk + i][lr] = wv[i];
+      const int64_t mm = m0 + lr;
+      float xv[8];
+      if (mm < m && kk + 8 <= k) {
+        const float4 a0 = __ldg(reinterpret_cast<const float4 *>(x + mm * k + kk));
+        const float4 a1 = __ldg(reinterpret_cast<const float4 *>(x + mm * k + kk + 4));
+        xv[0] = a0.x; xv[1] = a0.y; xv[2] = a0.z; xv[3] = a0.w;
+        xv[4] = a1.x; xv[5] = a1.y; xv[6] = a1.z; xv[7] = a1.w;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) xv[i] = (mm < m && kk + i < k) ? x[mm * k + kk + i] : 0.0f;
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) xs[lk + i][lr] = xv[i];
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int kk = 0; kk < kLbK; ++kk) {
+      const float4 a = *reinterpret_cast<const float4 *>(&ws[kk][4 * tx]);
+      const float4 b = *reinterpret_cast<const float4 *>(&xs[kk][4 * ty]);
+      const float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = __fmaf_rn(bv[j], av[i], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const int64_t mm = m0 + 4 * ty + j;
+    if (mm >= m) continue;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int64_t nn = n0 + 4 * tx + i;
+      if (nn < n) y[mm * n + nn] = acc[i][j];
+    }
+  }
+}
+
 // Any shape: one thread per output, sequential k (the CPU's order).
 __global__ void linear_bf16_scalar_kernel(const float *x, int64_t m, int64_t k, const uint16_t *w, int64_t n,
                                           float *y) {
@@ -1026,17 +1101,25 @@ cudaError_t attn_launch_nt(gq_ctx *ctx, dim3 grid, const AttnArgs &a) {
   return gq_launch(ctx, attn_chunk_kernel<NT>, grid, dim3(NT), 0, a);
 }
 
+// Ring depth: three stages (96 KB at head_dim 512, two CTAs per SM). Measured on
+// batch 64: two stages (three CTAs per SM) gave the same at head_dim 512, four
+// stages lost 25 % at head_dim 256.
 template <int NT>
-cudaError_t attn_ring_launch_nt(gq_ctx *ctx, dim3 grid, const AttnArgs &a, size_t smem) {
+constexpr int ring_stages() { return 3; }
+
+template <int NT>
+cudaError_t attn_ring_launch_nt(gq_ctx *ctx, dim3 grid, const AttnArgs &a) {
+  constexpr int ST = ring_stages<NT>();
+  const size_t smem = (size_t)2 * ST * kSubKeys * a.dh * 4;
   static bool attr_set[64] = {};
   const int dev = ctx->device & 63;
   if (!attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(attn_ring_kernel<NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)(2 * kRingStages * kSubKeys * 4 * NT * 4));
+    cudaError_t e = cudaFuncSetAttribute(attn_ring_kernel<NT, ST>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)(2 * ST * kSubKeys * 4 * NT * 4));
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
-  return gq_launch(ctx, attn_ring_kernel<NT>, grid, dim3(NT), smem, a);
+  return gq_launch(ctx, attn_ring_kernel<NT, ST>, grid, dim3(NT), smem, a);
 }
 
 }  // namespace
@@ -1175,12 +1258,11 @@ int gq_attention(gq_ctx *ctx, const float *q, int64_t batch, int64_t t, int64_t 
   const int nt = head_dim <= 128 ? 32 : head_dim <= 256 ? 64 : head_dim <= 512 ? 128 : 256;
   cudaError_t e;
   if (ring) {
-    const size_t smem = (size_t)2 * kRingStages * kSubKeys * head_dim * 4;
     // at least two warps: the softmax step gives one thread to each of the 64 (head, key) entries
     if (head_dim <= 256)
-      e = attn_ring_launch_nt<64>(ctx, grid, a, smem);
+      e = attn_ring_launch_nt<64>(ctx, grid, a);
     else
-      e = attn_ring_launch_nt<128>(ctx, grid, a, smem);
+      e = attn_ring_launch_nt<128>(ctx, grid, a);
   } else switch (nt) {
     case 32: e = attn_launch_nt<32>(ctx, grid, a); break;
     case 64: e = attn_launch_nt<64>(ctx, grid, a); break;
@@ -1202,7 +1284,10 @@ int gq_linear_bf16(gq_ctx *ctx, const float *x, int64_t m, int64_t k, const uint
   if (m == 0 || n == 0) return GQ_OK;
   if (!x || !w || !y) return gq_fail(ctx, GQ_ERR_INVALID_ARGUMENT, "linear_bf16: null pointer");
   const bool vec = k % 8 == 0 && k > 0 && (uintptr_t)x % 16 == 0 && (uintptr_t)w % 16 == 0;
-  if (vec) {
+  if (vec && m > 4) {
+    const dim3 grid((unsigned)((n + kLbT - 1) / kLbT), (unsigned)((m + kLbT - 1) / kLbT));
+    GQ_CUDA_TRY(ctx, gq_launch(ctx, linear_bf16_tiled_kernel, grid, dim3(256), 0, x, m, k, w, n, y));
+  } else if (vec) {
     GQ_CUDA_TRY(ctx, gq_launch(ctx, linear_bf16_kernel, dim3((unsigned)((n + kLinWarps - 1) / kLinWarps)),
                                dim3(kLinWarps * 32), 0, x, m, k, w, n, y));
   } else {

@@ -171,7 +171,8 @@ def test_attention_batched_kv_cache(g, batch, s, dh, window, flags):
         assert rel(got[b], want) <= ATTN_REL, b
 
 
-@pytest.mark.parametrize("m,k,n", [(1, 1536, 8960), (64, 1536, 8960), (3, 40, 23), (2, 4096, 100)])
+@pytest.mark.parametrize("m,k,n", [(1, 1536, 8960), (64, 1536, 8960), (3, 40, 23), (2, 4096, 100), (7, 40, 70),
+                                   (65, 1536, 200), (9, 100, 33)])
 def test_linear_bf16(g, m, k, n):
     x = synth.normal(170 + k, m * k).reshape(m, k)
     w = e2b._bf16_round(synth.uniform(171 + k, n * k, -0.04, 0.04)).reshape(n, k)
