@@ -484,6 +484,28 @@ def sharded_lm_head(torch, dist, rank, world, local, args):
     out = {"world": world, "ms": round(ms, 4), "GB/s_whole_head": round(nbytes / (ms / 1e3) / 1e9, 1),
            "logits_shape": list(logits.shape), "collective": "NCCL all_gather_into_tensor",
            "note": "strong scaling of one matrix: shard GEMV + all-gather, max over ranks"}
+
+    # the same with the exchange fused into the GEMV epilogue (peer stores over NVLink)
+    from gq.parallel import PeerLmHead
+    peer = PeerLmHead(g2, wt, V, rank, world, max_m=1, cap=30.0)
+    for _ in range(max(3, args.warmup)):
+        peer.forward(x)
+    torch.cuda.synchronize()
+    dist.barrier()
+    s.record()
+    for _ in range(reps):
+        peer.forward(x)
+    e.record()
+    e.synchronize()
+    ms2 = torch.tensor([s.elapsed_time(e) / reps], device=g2.torch_device)
+    dist.all_reduce(ms2, op=dist.ReduceOp.MAX)
+    ms2 = float(ms2.item())
+    same = bool(torch.equal(peer.forward(x), head.forward(x)))
+    peer.close()
+    out["fused_peer_stores"] = {"ms": round(ms2, 4), "GB/s_whole_head": round(nbytes / (ms2 / 1e3) / 1e9, 1),
+                                "equals_nccl_result": same,
+                                "exchange": "shard GEMV epilogue stores each logit into every rank's buffer over "
+                                            "NVLink (CUDA IPC); 1-element NCCL all-reduce as the completion barrier"}
     g2.free_quant(wt)
     g2.close()
     return out

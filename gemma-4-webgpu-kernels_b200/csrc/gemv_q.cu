@@ -60,6 +60,7 @@ struct GemvArgs {
   int64_t b_stride, b_off;
   float cap;
   float *y;
+  PeerDst peers;  // extra output destinations (peer buffers); n = 0: none
   int64_t ldy, y_col0;
   int row_bytes;    // bytes per packed row, multiple of 16
   int rows_per_cta; // contiguous rows per CTA
@@ -505,6 +506,9 @@ __global__ void __launch_bounds__(THREADS, THREADS == kThreads ? kResident : 1) 
   // A timed-out wait leaves this warp; report it and drain (bounded) the copies
   // this CTA may still have in flight before its shared memory is released.
   const bool any_failed = __syncthreads_or(failed);
+  if (!any_failed && a.peers.n > 0)
+    gqd::push_to_peers(a.y + (size_t)m0 * a.ldy, a.peers, min(MT, a.M - m0), a.ldy, a.y_col0 + n_begin,
+                       a.y_col0 + n_end);
   if (any_failed) {
     if (tid == 0) {
       gqd::report(a.err, GQ_DEVERR_WAIT_TIMEOUT);
@@ -605,6 +609,7 @@ int gq_gemv_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq_qw
   a.y_col0 = y_col0;
   a.row_bytes = rb;
   a.err = ctx->dev_err;
+  a.peers = ctx->peers;
 
   // Grid: one CTA per SM over contiguous row ranges.
   // (a multiple of 4 rows, so each tile's scale copy starts 16-byte aligned)

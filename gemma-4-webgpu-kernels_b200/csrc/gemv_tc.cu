@@ -65,6 +65,7 @@ struct TcArgs {
   int64_t b_stride, b_off;
   float cap;
   float *y;
+  PeerDst peers;  // extra output destinations (peer buffers); n = 0: none
   int64_t ldy, y_col0;
   int rows_per_cta;  // whole tiles
   int tile_rows;     // MMA N: multiple of 16, <= 256
@@ -604,6 +605,8 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   tc_fence_before();
   __syncthreads();
+  if (!*abort_flag && a.peers.n > 0)
+    gqd::push_to_peers(a.y, a.peers, a.M, a.ldy, a.y_col0 + n_begin, a.y_col0 + n_end);
   if (*abort_flag) {
     if (tid == 0) gqd::report(a.err, GQ_DEVERR_WAIT_TIMEOUT);
     if (warp == 0 && lane == 0) {
@@ -783,6 +786,7 @@ int gq_gemv_tc_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq
   a.issuers = p.issuers;
   a.tmem_cols = p.tmem_cols;
   a.err = ctx->dev_err;
+  a.peers = ctx->peers;
   const int mt = m <= 1 ? 1 : 2;
   const dim3 grid((unsigned)p.gx);
   if (w->bits == 4) return launch_mt<4, false>(ctx, mt, mode, m1, m2, a, grid, p.smem);

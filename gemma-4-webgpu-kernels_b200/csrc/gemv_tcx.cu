@@ -57,6 +57,7 @@ struct TcxArgs {
   int64_t b_stride, b_off;
   float cap;
   float *y;
+  PeerDst peers;  // extra output destinations (peer buffers); n = 0: none
   int64_t ldy, y_col0;
   const int *xexp;        // [M] per-row exponent s_m (X = rint(x * 2^s_m))
   const long long *sumx;  // [M] sum_k X
@@ -659,6 +660,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  if (!*abort_flag && a.peers.n > 0) gqd::push_to_peers(a.y, a.peers, a.M, a.ldy, a.y_col0 + n_begin, a.y_col0 + n_end);
   if (*abort_flag) {
     if (tid == 0) gqd::report(a.err, GQ_DEVERR_WAIT_TIMEOUT);
     __syncthreads();
@@ -906,6 +908,7 @@ int gq_gemv_tcx_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const g
     a.issuers = p.issuers;
     a.tmem_cols = p.tmem_cols;
     a.err = ctx->dev_err;
+    a.peers = ctx->peers;
     const dim3 grid((unsigned)((rows + p.tile_rows - 1) / p.tile_rows));
     if (w->bits == 4) rc = launch_xm<4, false>(ctx, mode, m1, m2, a, grid, p.smem);
     else if (w->bits == 2) rc = launch_xm<2, false>(ctx, mode, m1, m2, a, grid, p.smem);

@@ -488,6 +488,53 @@ int gq_linear_gelu_mul_cols(gq_ctx *ctx, const float *x, int64_t m, int64_t k, c
   return gq_elementwise_launch(ctx, 2, g, b, (int64_t)cnt, w->n, b_stride, b_offset, 0.0f, y);
 }
 
+int gq_linear_softcap_peers(gq_ctx *ctx, const float *x, int64_t m, int64_t k, const gq_qweight *w, float cap,
+                            float *y, int64_t ldy, int64_t y_col0, float *const *peer_y, int32_t npeers) {
+  GQ_ENTER(ctx);
+  if (npeers < 0 || npeers > kMaxPeerDst || (npeers > 0 && !peer_y))
+    return gq_fail(ctx, GQ_ERR_INVALID_ARGUMENT, "linear_softcap_peers: 0..8 peer buffers");
+  int rc = check_linear_args(ctx, "linear_softcap_peers", x, m, k, w, y);
+  if (rc != GQ_OK) return rc;
+  for (int i = 0; i < npeers; ++i)
+    if (!peer_y[i]) return gq_fail(ctx, GQ_ERR_INVALID_ARGUMENT, "linear_softcap_peers: null peer buffer");
+  // only the GEMV kernels carry the peer stores in their epilogue
+  const bool gemv = !use_prefill(ctx, x, m, w) &&
+                    (use_gemv_tc(ctx, x, m, w, 1) || use_gemv_tcx(ctx, x, m, w, 1) || gq_gemv_supported(ctx, w, m, 1));
+  if (!gemv)
+    return gq_fail(ctx, GQ_ERR_UNSUPPORTED, "linear_softcap_peers: shape not served by a GEMV kernel (M < 128, whole rows)");
+  ctx->peers.n = npeers;
+  for (int i = 0; i < npeers; ++i) ctx->peers.p[i] = peer_y[i];
+  rc = gq_linear_softcap(ctx, x, m, k, w, cap, y, ldy, y_col0);
+  ctx->peers = PeerDst{};
+  return rc;
+}
+
+int gq_ipc_get_handle(gq_ctx *ctx, void *dptr, uint8_t *handle64) {
+  GQ_ENTER(ctx);
+  if (!dptr || !handle64) return gq_fail(ctx, GQ_ERR_INVALID_ARGUMENT, "ipc_get_handle: null pointer");
+  cudaIpcMemHandle_t h;
+  GQ_CUDA_TRY(ctx, cudaIpcGetMemHandle(&h, dptr));
+  static_assert(sizeof(h) == 64, "CUDA IPC handles are 64 bytes");
+  memcpy(handle64, &h, 64);
+  return GQ_OK;
+}
+
+int gq_ipc_open(gq_ctx *ctx, const uint8_t *handle64, void **dptr) {
+  GQ_ENTER(ctx);
+  if (!dptr || !handle64) return gq_fail(ctx, GQ_ERR_INVALID_ARGUMENT, "ipc_open: null pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle64, 64);
+  GQ_CUDA_TRY(ctx, cudaIpcOpenMemHandle(dptr, h, cudaIpcMemLazyEnablePeerAccess));
+  return GQ_OK;
+}
+
+int gq_ipc_close(gq_ctx *ctx, void *dptr) {
+  GQ_ENTER(ctx);
+  if (!dptr) return GQ_OK;
+  GQ_CUDA_TRY(ctx, cudaIpcCloseMemHandle(dptr));
+  return GQ_OK;
+}
+
 int gq_linear_softcap(gq_ctx *ctx, const float *x, int64_t m, int64_t k, const gq_qweight *w,
                       float cap, float *y, int64_t ldy, int64_t y_col0) {
   GQ_ENTER(ctx);

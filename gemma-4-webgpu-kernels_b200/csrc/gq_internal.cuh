@@ -10,6 +10,15 @@
 
 #include "../../include/gq.h"
 
+// Extra destinations of a GEMV's output: peer GPUs' buffers mapped into this
+// device's address space (CUDA IPC). Every output element is also stored at
+// p[i] + (its offset in y). n = 0 is the plain single output.
+constexpr int kMaxPeerDst = 8;
+struct PeerDst {
+  float *p[kMaxPeerDst];
+  int n;
+};
+
 struct gq_ctx {
   int device = 0;
   int num_sms = 0;
@@ -25,6 +34,8 @@ struct gq_ctx {
   // workspace of the tensor-core prefill path (f16 copy of the activations, row exponents)
   void *ws = nullptr;
   size_t ws_cap = 0;
+  // set by gq_linear_softcap_peers for the duration of one call
+  PeerDst peers = {};
 };
 
 struct gq_qweight {
@@ -145,6 +156,41 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
 // (bulk copy) writes to the same shared memory.
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Push this CTA's finished outputs (token rows 0..m-1, columns [c0, c1) of the
+// [m, ldy] output) from its local buffer to every peer destination with
+// coalesced 16-byte NVLink stores, then fence: call after a block barrier that
+// follows the CTA's local output stores (bar.sync makes them visible to the
+// block), by all threads of the block. One thread's system-scope fence after a
+// second barrier orders every store of the CTA (fences are cumulative).
+__device__ __forceinline__ void push_to_peers(const float *y, const PeerDst &pd, int m, int64_t ldy, int64_t c0,
+                                              int64_t c1) {
+  if (pd.n == 0 || c1 <= c0) return;
+  const int tid = threadIdx.x, nt = blockDim.x;
+  for (int r = 0; r < m; ++r) {
+    const int64_t base = (int64_t)r * ldy;
+    int64_t a = c0, b = c1;
+    // ragged head and tail element by element, the aligned middle as float4
+    while (a < b && ((base + a) & 3)) {
+      if (tid == 0)
+        for (int i = 0; i < pd.n; ++i) pd.p[i][base + a] = y[base + a];
+      ++a;
+    }
+    while (b > a && ((base + b) & 3)) {
+      --b;
+      if (tid == 0)
+        for (int i = 0; i < pd.n; ++i) pd.p[i][base + b] = y[base + b];
+    }
+    const int64_t n4 = (b - a) / 4;
+    const float4 *src = reinterpret_cast<const float4 *>(y + base + a);
+    for (int64_t j = tid; j < n4; j += nt) {
+      const float4 v = src[j];
+      for (int i = 0; i < pd.n; ++i) reinterpret_cast<float4 *>(pd.p[i] + base + a)[j] = v;
+    }
+  }
+  __syncthreads();
+  if (tid == 0) __threadfence_system();
 }
 
 __device__ __forceinline__ void report(uint32_t *err, uint32_t bits) {

@@ -72,6 +72,12 @@ SIGNATURES = {
         c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int64, c_void_p]),
     "gq_linear_softcap": (
         c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_float, c_void_p, c_int64, c_int64]),
+    "gq_linear_softcap_peers": (
+        c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_float, c_void_p, c_int64, c_int64, c_void_p,
+                c_int32]),
+    "gq_ipc_get_handle": (c_int, [c_void_p, c_void_p, c_void_p]),
+    "gq_ipc_open": (c_int, [c_void_p, c_void_p, POINTER(c_void_p)]),
+    "gq_ipc_close": (c_int, [c_void_p, c_void_p]),
     "gq_embed_rows": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_float, c_void_p]),
     "gq_linear_prefill_static": (
         c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int32, c_int32, c_void_p]),

@@ -11,6 +11,10 @@ logits equal that single-device result row for row.
 The host logic here (row split, slicing a packed weight, reassembling the
 gathered [G, M, V/G] blocks into [M, V]) is backend-agnostic so it is tested on
 CPU with gloo ranks and the oracle as the per-shard compute.
+
+Two exchanges: ShardedLmHead gathers the shards with NCCL's all-gather;
+PeerLmHead fuses the exchange into the shard GEMV (its epilogue stores every
+logit into all ranks' buffers over NVLink through CUDA IPC mappings).
 """
 from __future__ import annotations
 
@@ -89,3 +93,90 @@ class ShardedLmHead:
             self.g.linear_softcap(x, self.w, self.cap, out=self.g.from_torch(local), col0=0)
         self.dist.all_gather_into_tensor(gathered, local, group=self.group)
         return assemble(gathered, m, self.world, self.per, self.vocab)
+
+
+class _DeviceArray:
+    """A raw device float32 buffer exposed to torch (__cuda_array_interface__)."""
+
+    def __init__(self, ptr: int, shape):
+        self.__cuda_array_interface__ = {"data": (int(ptr), False), "shape": tuple(shape), "typestr": "<f4",
+                                         "version": 3}
+
+
+class PeerLmHead:
+    """One rank's share of the lm_head with the all-gather fused into the GEMV.
+
+    Every rank owns a full logits buffer [max_m, V] (gq_alloc, so it is an
+    allocation base CUDA IPC can export) and maps every peer's buffer into its own
+    device (gq_ipc_open). forward(x) runs gq_linear_softcap_peers: the shard GEMV's
+    epilogue stores each logit of this rank's vocab columns into its own buffer
+    and, over NVLink, into every peer's buffer at the same offset. A 1-element
+    NCCL all-reduce issued on the same stream afterwards is the completion
+    barrier: when it finishes on a rank, every rank's GEMV (and its
+    system-fenced peer stores) finished before it. The data never goes through
+    NCCL. forward returns a torch view [M, V] of this rank's buffer."""
+
+    def __init__(self, backend, shard, vocab: int, rank: int, world: int, max_m: int, cap: float = 30.0, group=None):
+        import ctypes
+        from ctypes import c_uint8, c_void_p
+
+        import torch
+        import torch.distributed as dist
+
+        from . import _abi
+
+        self.torch, self.dist, self.g = torch, dist, backend
+        self.rank, self.world, self.vocab, self.cap, self.group, self.max_m = rank, world, vocab, cap, group, max_m
+        self.r0, self.r1 = shard_rows(vocab, world, rank)
+        assert shard.shape[0] == self.r1 - self.r0
+        self.w = shard if getattr(shard, "qw", None) is not None else backend.quant_tensor(shard)
+        lib, ctx = backend.lib, backend.ctx
+        ptr = c_void_p()
+        _abi.check(lib.gq_alloc(ctx, max_m * vocab * 4, ctypes.byref(ptr)), ctx, "alloc logits")
+        self.buf = ptr.value
+        handle = (c_uint8 * 64)()
+        _abi.check(lib.gq_ipc_get_handle(ctx, c_void_p(self.buf), handle), ctx, "ipc handle")
+        handles = [None] * world
+        dist.all_gather_object(handles, bytes(handle), group=group)
+        self.peers = []
+        for r, h in enumerate(handles):
+            if r == rank:
+                continue
+            p = c_void_p()
+            _abi.check(lib.gq_ipc_open(ctx, (c_uint8 * 64).from_buffer_copy(h), ctypes.byref(p)), ctx, "ipc open")
+            self.peers.append(p.value)
+        self.peer_arr = (c_void_p * max(1, len(self.peers)))(*self.peers)
+        self.logits = torch.as_tensor(_DeviceArray(self.buf, (max_m, vocab)), device=backend.torch_device)
+        self.flag = torch.zeros(1, device=backend.torch_device)
+        self.stream = torch.cuda.ExternalStream(backend.stream_ptr(), device=backend.torch_device) \
+            if backend.own_stream else torch.cuda.current_stream(backend.torch_device)
+
+    def forward(self, x):
+        """x: GqTensor [M, K] (M <= max_m) -> torch view [M, V], complete on this rank's stream."""
+        from ctypes import c_float, c_void_p
+
+        from . import _abi
+
+        m, k = x.shape
+        assert m <= self.max_m
+        lib, ctx = self.g.lib, self.g.ctx
+        _abi.check(lib.gq_linear_softcap_peers(ctx, c_void_p(x.ptr()), m, k, c_void_p(self.w.qw), c_float(self.cap),
+                                               c_void_p(self.buf), self.vocab, self.r0, self.peer_arr,
+                                               len(self.peers)), ctx, "linear_softcap_peers")
+        with self.torch.cuda.stream(self.stream):
+            self.dist.all_reduce(self.flag, group=self.group)
+        return self.logits[:m]
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's (after every rank stopped writing)."""
+        from ctypes import c_void_p
+
+        self.torch.cuda.synchronize(self.g.torch_device)
+        self.dist.barrier(group=self.group)
+        for p in self.peers:
+            self.g.lib.gq_ipc_close(self.g.ctx, c_void_p(p))
+        self.peers = []
+        self.dist.barrier(group=self.group)
+        if self.buf:
+            self.g.lib.gq_free(self.g.ctx, c_void_p(self.buf))
+            self.buf = 0

@@ -140,6 +140,26 @@ int gq_linear_gelu_mul_cols(gq_ctx *ctx, const float *x, int64_t m, int64_t k,
 int gq_linear_softcap(gq_ctx *ctx, const float *x, int64_t m, int64_t k, const gq_qweight *w,
                       float cap, float *y, int64_t ldy, int64_t y_col0);
 
+/* The lm_head of a vocab-sharded model with its all-gather fused in: the same
+ * output as gq_linear_softcap (rows of w = this rank's vocab shard, written at
+ * columns y_col0 .. y_col0 + N of the [m, ldy] logits), and every element is also
+ * stored at the same offset of each peer_y[i] — other GPUs' logits buffers mapped
+ * into this device (gq_ipc_open) — by the GEMV epilogue itself, over NVLink.
+ * After the call, a stream-ordered collective on every rank (any NCCL op) makes
+ * the full logits complete on all of them. 0 <= npeers <= 8; M < 128 and shapes
+ * served by the GEMV kernels only (GQ_ERR_UNSUPPORTED otherwise). No counterpart
+ * in the reference (its lm_head runs on one device); replaces the NCCL all-gather
+ * of vocab sharding (rust/src/model.rs:192 is the op itself). */
+int gq_linear_softcap_peers(gq_ctx *ctx, const float *x, int64_t m, int64_t k, const gq_qweight *w, float cap,
+                            float *y, int64_t ldy, int64_t y_col0, float *const *peer_y, int32_t npeers);
+
+/* CUDA IPC for the peer buffers above: the 64-byte handle of a gq_alloc'd device
+ * buffer, the mapping of a peer's handle into this context's device (peer access
+ * enabled), and its release. */
+int gq_ipc_get_handle(gq_ctx *ctx, void *dptr, uint8_t *handle64);
+int gq_ipc_open(gq_ctx *ctx, const uint8_t *handle64, void **dptr);
+int gq_ipc_close(gq_ctx *ctx, void *dptr);
+
 /* Backend::embed_rows for a quantized table (rust/src/backend.rs:101-102;
  * CPU rust/src/backend_cpu.rs:127-137, wgpu EMBED_Q at
  * rust/src/backend_wgpu.rs:734-754): out[i, d] = deq(table, ids[i], d) * scale.

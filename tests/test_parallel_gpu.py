@@ -1,0 +1,90 @@
+"""The vocab-sharded lm_head on 2 GPUs (needs two B200s; skipped with fewer).
+
+Both exchanges against the single-device oracle and against each other: the
+NCCL all-gather (ShardedLmHead) and the fused GEMV + peer stores over NVLink
+(PeerLmHead, gq_linear_softcap_peers). Each rank computes the same kernels on the
+same shard bytes, so the two full logits tensors must be identical; against the
+oracle the FFMA bound applies (relative L2 <= 1e-5)."""
+import os
+import socket
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+V, K, CAP = 20000, 1536, 30.0
+
+
+def _gpus() -> int:
+    try:
+        import torch
+
+        return torch.cuda.device_count()
+    except Exception:
+        return 0
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, q):
+    from datetime import timedelta
+
+    import torch
+    import torch.distributed as dist
+
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        torch.cuda.set_device(rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                                device_id=torch.device("cuda", rank))
+        from gq import CudaBackend, synth
+        from gq.parallel import PeerLmHead, ShardedLmHead, shard_rows, slice_rows
+        from oracle import oracle
+
+        full = synth.random_qweight(4100, V, K, 8, True)
+        r0, r1 = shard_rows(V, world, rank)
+        shard = slice_rows(full, r0, r1)
+        g = CudaBackend(rank)
+        res = {}
+        for m in (1, 5, 40):
+            x = synth.normal(4101 + m, m * K).reshape(m, K).astype(np.float32)
+            gx = g.tensor(x, x.shape)
+            nccl = ShardedLmHead(g, shard, V, rank, world, CAP).forward(gx).cpu().numpy()
+            peer = PeerLmHead(g, shard, V, rank, world, max_m=m, cap=CAP)
+            got = peer.forward(gx).cpu().numpy().copy()
+            got2 = peer.forward(gx).cpu().numpy().copy()  # second call into the same buffers
+            peer.close()
+            ref = oracle.softcap(oracle.linear(x, full), CAP)
+            rel = float(np.linalg.norm(got.astype(np.float64) - ref) / np.linalg.norm(ref))
+            res[m] = (rel, bool(np.array_equal(got, nccl)), bool(np.array_equal(got, got2)))
+        g.close()
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, res))
+    except Exception as e:  # report instead of hanging the parent
+        q.put((rank, repr(e)))
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="needs two GPUs")
+def test_sharded_lm_head_two_gpus_both_exchanges():
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    out = dict(q.get(timeout=600) for _ in ps)
+    for p in ps:
+        p.join(timeout=120)
+    for rank, res in out.items():
+        assert isinstance(res, dict), f"rank {rank}: {res}"
+        for m, (rel, same_as_nccl, repeatable) in res.items():
+            assert rel <= 1e-5, (rank, m, rel)
+            assert same_as_nccl and repeatable, (rank, m)
