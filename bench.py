@@ -485,27 +485,81 @@ def sharded_lm_head(torch, dist, rank, world, local, args):
            "logits_shape": list(logits.shape), "collective": "NCCL all_gather_into_tensor",
            "note": "strong scaling of one matrix: shard GEMV + all-gather, max over ranks"}
 
-    # the same with the exchange fused into the GEMV epilogue (peer stores over NVLink)
+    # the same with the exchange fused into the GEMV epilogue (peer stores over NVLink),
+    # with the completion barrier a 1-element NCCL all-reduce or the GEMV's own flags
     from gq.parallel import PeerLmHead
-    peer = PeerLmHead(g2, wt, V, rank, world, max_m=1, cap=30.0)
-    for _ in range(max(3, args.warmup)):
-        peer.forward(x)
+    for barrier, key, how in (("nccl", "fused_peer_stores", "1-element NCCL all-reduce as the completion barrier"),
+                              ("device", "fused_peer_stores_device_barrier",
+                               "the GEMV's last CTA stores an epoch flag into every rank (release, system scope), "
+                               "a one-thread kernel waits for all flags (acquire); no NCCL call")):
+        peer = PeerLmHead(g2, wt, V, rank, world, max_m=1, cap=30.0, barrier=barrier)
+        for _ in range(max(3, args.warmup)):
+            peer.forward(x)
+        torch.cuda.synchronize()
+        dist.barrier()
+        s.record()
+        for _ in range(reps):
+            peer.forward(x)
+        e.record()
+        e.synchronize()
+        ms2 = torch.tensor([s.elapsed_time(e) / reps], device=g2.torch_device)
+        dist.all_reduce(ms2, op=dist.ReduceOp.MAX)
+        ms2 = float(ms2.item())
+        same = bool(torch.equal(peer.forward(x), head.forward(x)))
+        g2.flush()
+        peer.close()
+        out[key] = {"ms": round(ms2, 4), "GB/s_whole_head": round(nbytes / (ms2 / 1e3) / 1e9, 1),
+                    "equals_nccl_result": same,
+                    "exchange": "shard GEMV epilogue stores each logit into every rank's buffer over NVLink "
+                                "(CUDA IPC); " + how}
+
+    # graph-replayed (no host launch cost in the loop): the shard GEMV alone, and
+    # the fused GEMV + device barrier (its epoch is device-resident)
+    g3 = CudaBackend(local, own_stream=True)
+    st3 = torch.cuda.ExternalStream(g3.stream_ptr(), device=g3.torch_device)
+    wt3 = g3.quant_tensor_from_device(payload, synth.uniform(56 + rank, r1 - r0, 0.005, 0.02), (r1 - r0, K), 8,
+                                      True, K)
+    x3 = g3.tensor(synth.normal(57, K).reshape(1, K), (1, K))
+    y3 = torch.empty(1, V, device=g3.torch_device)
     torch.cuda.synchronize()
-    dist.barrier()
-    s.record()
-    for _ in range(reps):
-        peer.forward(x)
-    e.record()
-    e.synchronize()
-    ms2 = torch.tensor([s.elapsed_time(e) / reps], device=g2.torch_device)
-    dist.all_reduce(ms2, op=dist.ReduceOp.MAX)
-    ms2 = float(ms2.item())
-    same = bool(torch.equal(peer.forward(x), head.forward(x)))
-    peer.close()
-    out["fused_peer_stores"] = {"ms": round(ms2, 4), "GB/s_whole_head": round(nbytes / (ms2 / 1e3) / 1e9, 1),
-                                "equals_nccl_result": same,
-                                "exchange": "shard GEMV epilogue stores each logit into every rank's buffer over "
-                                            "NVLink (CUDA IPC); 1-element NCCL all-reduce as the completion barrier"}
+    from ctypes import c_float, c_void_p
+    per_graph = 20
+
+    def shard_only():
+        for _ in range(per_graph):
+            g3._check(g3.lib.gq_linear_softcap(g3.ctx, c_void_p(x3.ptr()), 1, K, c_void_p(wt3.qw), c_float(30.0),
+                                               c_void_p(y3.data_ptr()), V, r0), "shard gemv")
+
+    peer3 = PeerLmHead(g3, wt3, V, rank, world, max_m=1, cap=30.0, barrier="device")
+
+    def fused():
+        for _ in range(per_graph):
+            peer3.forward(x3)
+
+    graphed = {}
+    for key, fn in (("shard_gemv_only", shard_only), ("fused_peer_stores_device_barrier", fused)):
+        gr = g3.record(fn)
+        for _ in range(3):
+            g3.replay(gr)
+        g3.flush()
+        dist.barrier()
+        reps_g = max(5, min(args.steps, 50))
+        msg = cuda_events_time(torch, st3, lambda: g3.replay(gr), reps_g) / (reps_g * per_graph)
+        g3.flush()
+        g3.destroy_graph(gr)
+        t = torch.tensor([msg], device=g3.torch_device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        graphed[key] = {"ms": round(float(t.item()), 4),
+                        "GB/s_whole_head": round(nbytes / (float(t.item()) / 1e3) / 1e9, 1)}
+    same = bool(torch.equal(peer3.forward(x3), head.forward(x)))
+    g3.flush()
+    peer3.close()
+    graphed["fused_peer_stores_device_barrier"]["equals_nccl_result"] = same
+    graphed["note"] = (f"CUDA graph of {per_graph} calls replayed back to back, max over ranks; shard_gemv_only "
+                       "writes this rank's columns only (no exchange)")
+    out["graph_replayed"] = graphed
+    g3.free_quant(wt3)
+    g3.close()
     g2.free_quant(wt)
     g2.close()
     return out

@@ -506,7 +506,7 @@ __global__ void __launch_bounds__(THREADS, THREADS == kThreads ? kResident : 1) 
   // A timed-out wait leaves this warp; report it and drain (bounded) the copies
   // this CTA may still have in flight before its shared memory is released.
   const bool any_failed = __syncthreads_or(failed);
-  if (!any_failed && a.peers.n > 0)
+  if (!any_failed && (a.peers.n > 0 || a.peers.signal))
     gqd::push_to_peers(a.y + (size_t)m0 * a.ldy, a.peers, min(MT, a.M - m0), a.ldy, a.y_col0 + n_begin,
                        a.y_col0 + n_end);
   if (any_failed) {

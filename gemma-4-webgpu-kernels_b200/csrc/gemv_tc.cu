@@ -605,7 +605,7 @@ __global__ void __launch_bounds__(kThreads, 2)
 
   tc_fence_before();
   __syncthreads();
-  if (!*abort_flag && a.peers.n > 0)
+  if (!*abort_flag && (a.peers.n > 0 || a.peers.signal))
     gqd::push_to_peers(a.y, a.peers, a.M, a.ldy, a.y_col0 + n_begin, a.y_col0 + n_end);
   if (*abort_flag) {
     if (tid == 0) gqd::report(a.err, GQ_DEVERR_WAIT_TIMEOUT);

@@ -660,7 +660,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (!*abort_flag && a.peers.n > 0) gqd::push_to_peers(a.y, a.peers, a.M, a.ldy, a.y_col0 + n_begin, a.y_col0 + n_end);
+  if (!*abort_flag && (a.peers.n > 0 || a.peers.signal)) gqd::push_to_peers(a.y, a.peers, a.M, a.ldy, a.y_col0 + n_begin, a.y_col0 + n_end);
   if (*abort_flag) {
     if (tid == 0) gqd::report(a.err, GQ_DEVERR_WAIT_TIMEOUT);
     __syncthreads();
@@ -909,6 +909,7 @@ int gq_gemv_tcx_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const g
     a.tmem_cols = p.tmem_cols;
     a.err = ctx->dev_err;
     a.peers = ctx->peers;
+    a.peers.signal = ctx->peers.signal && (r0 + p.slice_rows >= w->n);  // the launch that completes y
     const dim3 grid((unsigned)((rows + p.tile_rows - 1) / p.tile_rows));
     if (w->bits == 4) rc = launch_xm<4, false>(ctx, mode, m1, m2, a, grid, p.smem);
     else if (w->bits == 2) rc = launch_xm<2, false>(ctx, mode, m1, m2, a, grid, p.smem);

@@ -488,6 +488,56 @@ int gq_linear_gelu_mul_cols(gq_ctx *ctx, const float *x, int64_t m, int64_t k, c
   return gq_elementwise_launch(ctx, 2, g, b, (int64_t)cnt, w->n, b_stride, b_offset, 0.0f, y);
 }
 
+namespace {
+// One thread waits (bounded) until every rank's flag has reached this rank's
+// epoch sync[1] (written by the signalling GEMV before this kernel in stream
+// order); acquire, system scope. A peer one call ahead holds epoch + 1, so the
+// test is a wrap-safe >=. On timeout it reports GQ_DEVERR_WAIT_TIMEOUT and returns.
+__global__ void peer_wait_kernel(const uint32_t *flags, int world, const uint32_t *sync, uint32_t *err) {
+  gqd::griddep_wait();
+  if (threadIdx.x != 0) return;
+  const uint32_t epoch = *reinterpret_cast<const volatile uint32_t *>(sync + 1);
+  const uint64_t t0 = gqd::globaltimer_ns();
+  for (int r = 0; r < world; ++r) {
+    for (uint32_t it = 0;; ++it) {
+      uint32_t v;
+      asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + r) : "memory");
+      if ((int32_t)(v - epoch) >= 0) break;
+      if ((it & 255u) == 255u && gqd::globaltimer_ns() - t0 > 2000000000ull) {
+        gqd::report(err, GQ_DEVERR_WAIT_TIMEOUT);
+        return;
+      }
+      __nanosleep(64);
+    }
+  }
+  gqd::griddep_launch_dependents();
+}
+}  // namespace
+
+int gq_peer_wait(gq_ctx *ctx, const uint32_t *flags, int32_t world, const uint32_t *sync) {
+  GQ_ENTER(ctx);
+  if (!flags || !sync || world < 1 || world > kMaxPeerDst + 1)
+    return gq_fail(ctx, GQ_ERR_INVALID_ARGUMENT, "peer_wait: flags, sync word, 1..9 ranks");
+  GQ_CUDA_TRY(ctx, gq_launch(ctx, peer_wait_kernel, dim3(1), dim3(32), 0, flags, (int)world, sync, ctx->dev_err));
+  return GQ_OK;
+}
+
+int gq_linear_softcap_peers_signal(gq_ctx *ctx, const float *x, int64_t m, int64_t k, const gq_qweight *w, float cap,
+                                   float *y, int64_t ldy, int64_t y_col0, float *const *peer_y, int32_t npeers,
+                                   uint32_t *const *flags, uint32_t *sync, int32_t rank) {
+  GQ_ENTER(ctx);
+  if (!flags || !sync || rank < 0 || rank > npeers) return gq_fail(ctx, GQ_ERR_INVALID_ARGUMENT, "peers_signal: flags, sync word, rank");
+  for (int i = 0; i <= npeers && i <= kMaxPeerDst; ++i)
+    if (!flags[i]) return gq_fail(ctx, GQ_ERR_INVALID_ARGUMENT, "peers_signal: null flag array");
+  ctx->peer_signal.sync = sync;
+  ctx->peer_signal.rank = rank;
+  for (int i = 0; i <= npeers && i <= kMaxPeerDst; ++i) ctx->peer_signal.flag[i] = flags[i];
+  ctx->peer_signal.signal = 1;
+  const int rc = gq_linear_softcap_peers(ctx, x, m, k, w, cap, y, ldy, y_col0, peer_y, npeers);
+  ctx->peer_signal = PeerDst{};
+  return rc;
+}
+
 int gq_linear_softcap_peers(gq_ctx *ctx, const float *x, int64_t m, int64_t k, const gq_qweight *w, float cap,
                             float *y, int64_t ldy, int64_t y_col0, float *const *peer_y, int32_t npeers) {
   GQ_ENTER(ctx);
@@ -502,6 +552,7 @@ int gq_linear_softcap_peers(gq_ctx *ctx, const float *x, int64_t m, int64_t k, c
                     (use_gemv_tc(ctx, x, m, w, 1) || use_gemv_tcx(ctx, x, m, w, 1) || gq_gemv_supported(ctx, w, m, 1));
   if (!gemv)
     return gq_fail(ctx, GQ_ERR_UNSUPPORTED, "linear_softcap_peers: shape not served by a GEMV kernel (M < 128, whole rows)");
+  ctx->peers = ctx->peer_signal;  // completion signal, when a caller set one
   ctx->peers.n = npeers;
   for (int i = 0; i < npeers; ++i) ctx->peers.p[i] = peer_y[i];
   rc = gq_linear_softcap(ctx, x, m, k, w, cap, y, ldy, y_col0);

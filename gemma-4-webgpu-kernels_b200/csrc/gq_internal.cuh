@@ -17,6 +17,15 @@ constexpr int kMaxPeerDst = 8;
 struct PeerDst {
   float *p[kMaxPeerDst];
   int n;
+  // completion signal (optional): sync = {CTA counter, epoch}, zeroed at set-up,
+  // on this device. The last CTA of the grid (after every CTA's pushes) resets
+  // the counter, increments the epoch and stores it at flag[i] + rank for every
+  // rank i (own flags first, then the peers'). The epoch lives in device memory
+  // so a captured graph replays with fresh epochs.
+  uint32_t *flag[kMaxPeerDst + 1];
+  uint32_t *sync;
+  int rank;
+  int signal;  // 1 on the launch that completes the output (the last row slice)
 };
 
 struct gq_ctx {
@@ -34,8 +43,9 @@ struct gq_ctx {
   // workspace of the tensor-core prefill path (f16 copy of the activations, row exponents)
   void *ws = nullptr;
   size_t ws_cap = 0;
-  // set by gq_linear_softcap_peers for the duration of one call
+  // set by gq_linear_softcap_peers(_signal) for the duration of one call
   PeerDst peers = {};
+  PeerDst peer_signal = {};
 };
 
 struct gq_qweight {
@@ -166,9 +176,10 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 // second barrier orders every store of the CTA (fences are cumulative).
 __device__ __forceinline__ void push_to_peers(const float *y, const PeerDst &pd, int m, int64_t ldy, int64_t c0,
                                               int64_t c1) {
-  if (pd.n == 0 || c1 <= c0) return;
   const int tid = threadIdx.x, nt = blockDim.x;
-  for (int r = 0; r < m; ++r) {
+  if (pd.n == 0 && !pd.signal) return;
+  // a CTA with no columns still counts towards the completion signal
+  for (int r = 0; r < m && c1 > c0 && pd.n > 0; ++r) {
     const int64_t base = (int64_t)r * ldy;
     int64_t a = c0, b = c1;
     // ragged head and tail element by element, the aligned middle as float4
@@ -190,7 +201,22 @@ __device__ __forceinline__ void push_to_peers(const float *y, const PeerDst &pd,
     }
   }
   __syncthreads();
-  if (tid == 0) __threadfence_system();
+  if (tid == 0) {
+    __threadfence_system();
+    if (pd.signal && pd.sync) {
+      // the last CTA to finish publishes the next epoch to every rank (release, system scope)
+      const uint32_t total = gridDim.x * gridDim.y * gridDim.z;
+      if (atomicAdd(pd.sync, 1u) == total - 1) {
+        __threadfence_system();
+        volatile uint32_t *sy = pd.sync;
+        sy[0] = 0u;
+        const uint32_t e = sy[1] + 1u;
+        sy[1] = e;
+        for (int i = 0; i <= pd.n; ++i)
+          asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(pd.flag[i] + pd.rank), "r"(e) : "memory");
+      }
+    }
+  }
 }
 
 __device__ __forceinline__ void report(uint32_t *err, uint32_t bits) {

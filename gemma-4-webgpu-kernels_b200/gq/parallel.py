@@ -106,17 +106,29 @@ class _DeviceArray:
 class PeerLmHead:
     """One rank's share of the lm_head with the all-gather fused into the GEMV.
 
-    Every rank owns a full logits buffer [max_m, V] (gq_alloc, so it is an
-    allocation base CUDA IPC can export) and maps every peer's buffer into its own
-    device (gq_ipc_open). forward(x) runs gq_linear_softcap_peers: the shard GEMV's
-    epilogue stores each logit of this rank's vocab columns into its own buffer
-    and, over NVLink, into every peer's buffer at the same offset. A 1-element
-    NCCL all-reduce issued on the same stream afterwards is the completion
-    barrier: when it finishes on a rank, every rank's GEMV (and its
-    system-fenced peer stores) finished before it. The data never goes through
-    NCCL. forward returns a torch view [M, V] of this rank's buffer."""
+    Every rank owns two logits buffers [max_m, V] (one gq_alloc, an allocation
+    base CUDA IPC can export) and maps every peer's into its own device
+    (gq_ipc_open). forward(x) runs the shard GEMV whose epilogue stores each logit
+    of this rank's vocab columns into its own buffer and, over NVLink, into every
+    peer's buffer at the same offset. Calls alternate between the two buffers, so
+    a rank that runs ahead writes the buffer its peers finished reading a call
+    earlier (a rank can be at most one call ahead: each call waits for all ranks).
+    The buffer is chosen on the host, so a CUDA graph should capture calls in
+    pairs.
 
-    def __init__(self, backend, shard, vocab: int, rank: int, world: int, max_m: int, cap: float = 30.0, group=None):
+    Completion barrier, `barrier=`:
+      "device" (default): gq_linear_softcap_peers_signal — the GEMV's last CTA
+        increments a device-resident epoch and stores it into a flag slot of
+        every rank (release, system scope) — then gq_peer_wait on this rank's
+        flags. No NCCL call per step, and the pair replays inside a graph.
+      "nccl": gq_linear_softcap_peers then a 1-element NCCL all-reduce on the same
+        stream: when it finishes on a rank, every rank's GEMV (and its
+        system-fenced peer stores) finished before it.
+    The data never goes through NCCL. forward returns a torch view [M, V] of this
+    rank's buffer, valid until the call after the next one."""
+
+    def __init__(self, backend, shard, vocab: int, rank: int, world: int, max_m: int, cap: float = 30.0, group=None,
+                 barrier: str = "device"):
         import ctypes
         from ctypes import c_uint8, c_void_p
 
@@ -125,15 +137,26 @@ class PeerLmHead:
 
         from . import _abi
 
-        self.torch, self.dist, self.g = torch, dist, backend
+        if barrier not in ("device", "nccl"):
+            raise ValueError(f"barrier must be 'device' or 'nccl', not {barrier!r}")
+        self.torch, self.dist, self.g, self.barrier = torch, dist, backend, barrier
         self.rank, self.world, self.vocab, self.cap, self.group, self.max_m = rank, world, vocab, cap, group, max_m
         self.r0, self.r1 = shard_rows(vocab, world, rank)
         assert shard.shape[0] == self.r1 - self.r0
         self.w = shard if getattr(shard, "qw", None) is not None else backend.quant_tensor(shard)
         lib, ctx = backend.lib, backend.ctx
-        ptr = c_void_p()
-        _abi.check(lib.gq_alloc(ctx, max_m * vocab * 4, ctypes.byref(ptr)), ctx, "alloc logits")
+        self.buf_floats = max_m * vocab
+        # [2 logits buffers][flags: world u32, padded to 256 B]; the {CTA counter, epoch} pair is local
+        self.flag_off = 2 * self.buf_floats * 4
+        nbytes = self.flag_off + 256
+        ptr, sync = c_void_p(), c_void_p()
+        _abi.check(lib.gq_alloc(ctx, nbytes, ctypes.byref(ptr)), ctx, "alloc logits")
         self.buf = ptr.value
+        _abi.check(lib.gq_alloc(ctx, 256, ctypes.byref(sync)), ctx, "alloc sync words")
+        self.sync = sync.value
+        _abi.check(lib.gq_memset(ctx, c_void_p(self.buf + self.flag_off), 0, 256), ctx, "zero flags")
+        _abi.check(lib.gq_memset(ctx, c_void_p(self.sync), 0, 256), ctx, "zero sync words")
+        _abi.check(lib.gq_sync(ctx), ctx, "sync")
         handle = (c_uint8 * 64)()
         _abi.check(lib.gq_ipc_get_handle(ctx, c_void_p(self.buf), handle), ctx, "ipc handle")
         handles = [None] * world
@@ -145,11 +168,17 @@ class PeerLmHead:
             p = c_void_p()
             _abi.check(lib.gq_ipc_open(ctx, (c_uint8 * 64).from_buffer_copy(h), ctypes.byref(p)), ctx, "ipc open")
             self.peers.append(p.value)
-        self.peer_arr = (c_void_p * max(1, len(self.peers)))(*self.peers)
-        self.logits = torch.as_tensor(_DeviceArray(self.buf, (max_m, vocab)), device=backend.torch_device)
+        n = max(1, len(self.peers))
+        self.peer_arr = [(c_void_p * n)(*[p + k * self.buf_floats * 4 for p in self.peers]) for k in (0, 1)]
+        self.flag_arr = (c_void_p * (1 + len(self.peers)))(
+            *[b + self.flag_off for b in [self.buf] + self.peers])
+        self.logits = [torch.as_tensor(_DeviceArray(self.buf + k * self.buf_floats * 4, (max_m, vocab)),
+                                       device=backend.torch_device) for k in (0, 1)]
+        self.calls = 0
         self.flag = torch.zeros(1, device=backend.torch_device)
         self.stream = torch.cuda.ExternalStream(backend.stream_ptr(), device=backend.torch_device) \
             if backend.own_stream else torch.cuda.current_stream(backend.torch_device)
+        dist.barrier(group=group)  # every rank's flags are zero before any rank signals
 
     def forward(self, x):
         """x: GqTensor [M, K] (M <= max_m) -> torch view [M, V], complete on this rank's stream."""
@@ -160,23 +189,36 @@ class PeerLmHead:
         m, k = x.shape
         assert m <= self.max_m
         lib, ctx = self.g.lib, self.g.ctx
-        _abi.check(lib.gq_linear_softcap_peers(ctx, c_void_p(x.ptr()), m, k, c_void_p(self.w.qw), c_float(self.cap),
-                                               c_void_p(self.buf), self.vocab, self.r0, self.peer_arr,
-                                               len(self.peers)), ctx, "linear_softcap_peers")
-        with self.torch.cuda.stream(self.stream):
-            self.dist.all_reduce(self.flag, group=self.group)
-        return self.logits[:m]
+        self.calls += 1
+        par = self.calls & 1
+        y = self.buf + par * self.buf_floats * 4
+        if self.barrier == "device":
+            _abi.check(lib.gq_linear_softcap_peers_signal(
+                ctx, c_void_p(x.ptr()), m, k, c_void_p(self.w.qw), c_float(self.cap), c_void_p(y), self.vocab,
+                self.r0, self.peer_arr[par], len(self.peers), self.flag_arr, c_void_p(self.sync), self.rank),
+                ctx, "linear_softcap_peers_signal")
+            _abi.check(lib.gq_peer_wait(ctx, c_void_p(self.buf + self.flag_off), self.world, c_void_p(self.sync)),
+                       ctx, "peer_wait")
+        else:
+            _abi.check(lib.gq_linear_softcap_peers(ctx, c_void_p(x.ptr()), m, k, c_void_p(self.w.qw),
+                                                   c_float(self.cap), c_void_p(y), self.vocab, self.r0,
+                                                   self.peer_arr[par], len(self.peers)), ctx, "linear_softcap_peers")
+            with self.torch.cuda.stream(self.stream):
+                self.dist.all_reduce(self.flag, group=self.group)
+        return self.logits[par][:m]
 
     def close(self) -> None:
         """Unmap the peers' buffers and free this rank's (after every rank stopped writing)."""
         from ctypes import c_void_p
 
         self.torch.cuda.synchronize(self.g.torch_device)
+        self.g.lib.gq_sync(self.g.ctx)
         self.dist.barrier(group=self.group)
         for p in self.peers:
             self.g.lib.gq_ipc_close(self.g.ctx, c_void_p(p))
         self.peers = []
         self.dist.barrier(group=self.group)
-        if self.buf:
-            self.g.lib.gq_free(self.g.ctx, c_void_p(self.buf))
-            self.buf = 0
+        for attr in ("buf", "sync"):
+            if getattr(self, attr):
+                self.g.lib.gq_free(self.g.ctx, c_void_p(getattr(self, attr)))
+                setattr(self, attr, 0)

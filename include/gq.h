@@ -153,6 +153,27 @@ int gq_linear_softcap(gq_ctx *ctx, const float *x, int64_t m, int64_t k, const g
 int gq_linear_softcap_peers(gq_ctx *ctx, const float *x, int64_t m, int64_t k, const gq_qweight *w, float cap,
                             float *y, int64_t ldy, int64_t y_col0, float *const *peer_y, int32_t npeers);
 
+/* The same call with the completion barrier fused in as well: flags[0] is this
+ * rank's array of `world` uint32 flags and flags[1 + i] the array of the rank
+ * that owns peer_y[i] (gq_ipc_open'd); sync is a zeroed pair of uint32 on this
+ * device {CTA counter, epoch}. The last CTA of the GEMV (after every CTA's peer
+ * stores and a system fence) increments the epoch and stores it at element
+ * `rank` of every rank's flag array; gq_peer_wait then holds the stream
+ * (bounded) until all of this rank's flags have reached the epoch, so no NCCL
+ * call is needed. The epoch is device-resident: the pair of calls can be
+ * captured in a graph and replayed. After a device error the flags and sync
+ * words must be re-zeroed on every rank. No counterpart in the reference (see
+ * gq_linear_softcap_peers). */
+int gq_linear_softcap_peers_signal(gq_ctx *ctx, const float *x, int64_t m, int64_t k, const gq_qweight *w,
+                                   float cap, float *y, int64_t ldy, int64_t y_col0, float *const *peer_y,
+                                   int32_t npeers, uint32_t *const *flags, uint32_t *sync, int32_t rank);
+
+/* Stream-ordered wait until flags[0 .. world) have all reached the epoch in
+ * sync[1] (acquire, system scope). A wait that runs past 2 s sets
+ * GQ_DEVERR_WAIT_TIMEOUT in the context's device error word (read by the next
+ * gq_sync) and returns. */
+int gq_peer_wait(gq_ctx *ctx, const uint32_t *flags, int32_t world, const uint32_t *sync);
+
 /* CUDA IPC for the peer buffers above: the 64-byte handle of a gq_alloc'd device
  * buffer, the mapping of a peer's handle into this context's device (peer access
  * enabled), and its release. */

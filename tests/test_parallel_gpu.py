@@ -2,7 +2,8 @@
 
 Both exchanges against the single-device oracle and against each other: the
 NCCL all-gather (ShardedLmHead) and the fused GEMV + peer stores over NVLink
-(PeerLmHead, gq_linear_softcap_peers). Each rank computes the same kernels on the
+(PeerLmHead, gq_linear_softcap_peers), the latter with either completion barrier
+(NCCL all-reduce, or the GEMV's own epoch flags and gq_peer_wait). Each rank computes the same kernels on the
 same shard bytes, so the two full logits tensors must be identical; against the
 oracle the FFMA bound applies (relative L2 <= 1e-5)."""
 import os
@@ -55,13 +56,35 @@ def _worker(rank, world, port, q):
             x = synth.normal(4101 + m, m * K).reshape(m, K).astype(np.float32)
             gx = g.tensor(x, x.shape)
             nccl = ShardedLmHead(g, shard, V, rank, world, CAP).forward(gx).cpu().numpy()
-            peer = PeerLmHead(g, shard, V, rank, world, max_m=m, cap=CAP)
-            got = peer.forward(gx).cpu().numpy().copy()
-            got2 = peer.forward(gx).cpu().numpy().copy()  # second call into the same buffers
-            peer.close()
             ref = oracle.softcap(oracle.linear(x, full), CAP)
-            rel = float(np.linalg.norm(got.astype(np.float64) - ref) / np.linalg.norm(ref))
-            res[m] = (rel, bool(np.array_equal(got, nccl)), bool(np.array_equal(got, got2)))
+            for barrier in ("nccl", "device"):
+                peer = PeerLmHead(g, shard, V, rank, world, max_m=m, cap=CAP, barrier=barrier)
+                got = peer.forward(gx).cpu().numpy().copy()
+                # later calls alternate buffers and epochs
+                again = [peer.forward(gx).cpu().numpy().copy() for _ in range(3)]
+                g.flush()
+                peer.close()
+                rel = float(np.linalg.norm(got.astype(np.float64) - ref) / np.linalg.norm(ref))
+                res[(m, barrier)] = (rel, bool(np.array_equal(got, nccl)),
+                                     all(np.array_equal(got, a) for a in again))
+        # the device barrier replayed from a CUDA graph (device-resident epochs)
+        gg = CudaBackend(rank, own_stream=True)
+        x = synth.normal(4199, 3 * K).reshape(3, K).astype(np.float32)
+        gx = gg.tensor(x, x.shape)
+        peer = PeerLmHead(gg, shard, V, rank, world, max_m=3, cap=CAP, barrier="device")
+        outs = []
+        graph = gg.record(lambda: outs.extend([peer.forward(gx), peer.forward(gx)]))
+        reps = []
+        for _ in range(3):
+            gg.replay(graph)
+            gg.flush()
+            reps.append([o.cpu().numpy().copy() for o in outs])
+        gg.destroy_graph(graph)
+        peer.close()
+        gg.close()
+        ref = oracle.softcap(oracle.linear(x, full), CAP)
+        rel = float(np.linalg.norm(reps[0][0].astype(np.float64) - ref) / np.linalg.norm(ref))
+        res["graph"] = (rel, True, all(np.array_equal(reps[0][0], o) for r in reps for o in r))
         g.close()
         dist.barrier()
         dist.destroy_process_group()
