@@ -64,9 +64,11 @@ def peaks():
 # ---- the decode-step workload -------------------------------------------------
 
 class DecodeStep:
-    """All MATMUL_Q calls of one E2B decode step, with pre-bound C-ABI arguments."""
+    """All MATMUL_Q calls of one E2B decode step, with pre-bound C-ABI arguments.
+    stack_qkv: a KV layer's q, k and v projections as one stacked GEMV, as the
+    decoder runs them (False: the separate config-2 sweep shapes)."""
 
-    def __init__(self, g, m: int, seed: int, with_lm_head: bool = True):
+    def __init__(self, g, m: int, seed: int, with_lm_head: bool = True, stack_qkv: bool = True):
         import torch
         from gq import synth
 
@@ -102,7 +104,7 @@ class DecodeStep:
 
         from ctypes import c_float, c_void_p
         for i in range(synth.LAYERS):
-            for p in synth.layer_projections(i):
+            for p in synth.layer_projections(i, stack_qkv):
                 t, payload, scales = qweight(p.n, p.k, p.bits, p.signed)
                 if i in (0, 4):  # host copies of one local + one global layer (CPU sample)
                     self.host_weights[(i, p.name, 0)] = (payload.cpu().numpy(), scales, p)
@@ -605,7 +607,7 @@ def extras(g, torch, stream, hbm_peak, bf16_peak):
         g.free_quant(t)
 
     # config 2 at M=8 (whole step, graph-replayed)
-    step8 = DecodeStep(g, 8, seed=4321, with_lm_head=False)
+    step8 = DecodeStep(g, 8, seed=4321, with_lm_head=False, stack_qkv=False)
     step8.run()
     g.flush()
     graph = g.record(step8.run)
@@ -743,7 +745,7 @@ def run_reference(args):
     ple = synth.normal(20, m * synth.LAYERS * synth.PLE_DIM).reshape(m, -1)
     work, nbytes, seed = [], 0, 7000
     for i in layers:
-        for p in synth.layer_projections(i):
+        for p in synth.layer_projections(i, stack_qkv=True):
             seed += 1
             q = synth.random_qweight(seed, p.n, p.k, p.bits, p.signed)
             x = rng_x[p.k]

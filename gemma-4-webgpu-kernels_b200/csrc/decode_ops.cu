@@ -352,6 +352,90 @@ __global__ void __launch_bounds__(kNormThreads) head_rope_reg_kernel(const float
   for (int64_t i = 2 * half + lane; i < dh; i += 32) yr[i] = b[i];
 }
 
+// The attention inputs of a KV layer in one launch (rust/src/model.rs:254-273):
+// rows of the stacked projection output [t, (hq + 2 hkv) * dh] are, per token,
+// hq query heads (weighted norm + RoPE), hkv key heads (weighted norm + RoPE) and
+// hkv value heads (unweighted norm). One warp per (token, head) row with the
+// arithmetic of head_rope_reg_kernel (the value norm is that kernel's with unit
+// weights, the same products as rms_norm with no weight).
+struct QkvArgs {
+  const float *qkv;
+  int64_t t, qkv_stride;
+  int hq, hkv;
+  int64_t dh;
+  const float *qw, *kw;
+  float eps;
+  const uint32_t *positions;
+  int half;
+  float *q_out, *k_out, *v_out;
+  int64_t q_stride, k_stride, v_stride;
+};
+
+template <int VPL>
+__global__ void __launch_bounds__(kNormThreads) qkv_norm_rope_kernel(const QkvArgs a,
+                                                                     const __grid_constant__ RopeFreq fr) {
+  __shared__ __align__(16) float buf[kNormThreads / 32][128 * VPL];
+  gqd::griddep_wait();
+  gqd::griddep_launch_dependents();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int per_tok = a.hq + 2 * a.hkv;
+  const int64_t row = (int64_t)blockIdx.x * (kNormThreads / 32) + warp;
+  if (row >= a.t * per_tok) return;
+  const int64_t tok = row / per_tok;
+  const int r = (int)(row - tok * per_tok);
+  const int kind = r < a.hq ? 0 : (r < a.hq + a.hkv ? 1 : 2);  // q, k, v
+  const float *w = kind == 0 ? a.qw : (kind == 1 ? a.kw : nullptr);
+  float *yr = kind == 0 ? a.q_out + tok * a.q_stride + (int64_t)r * a.dh
+            : kind == 1 ? a.k_out + tok * a.k_stride + (int64_t)(r - a.hq) * a.dh
+                        : a.v_out + tok * a.v_stride + (int64_t)(r - a.hq - a.hkv) * a.dh;
+  const int n4 = (int)(a.dh / 4);
+  const float4 *x4 = reinterpret_cast<const float4 *>(a.qkv + tok * a.qkv_stride + (int64_t)r * a.dh);
+  const float4 *w4 = reinterpret_cast<const float4 *>(w);
+  float4 xv[VPL], wv[VPL];
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int c = lane + 32 * i;
+    const bool in = c < n4;
+    xv[i] = in ? x4[c] : make_float4(0.f, 0.f, 0.f, 0.f);
+    wv[i] = (w && in) ? __ldg(w4 + c) : make_float4(1.f, 1.f, 1.f, 1.f);
+  }
+  float ss = 0.0f;
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    ss = __fadd_rn(ss, __fmul_rn(xv[i].x, xv[i].x));
+    ss = __fadd_rn(ss, __fmul_rn(xv[i].y, xv[i].y));
+    ss = __fadd_rn(ss, __fmul_rn(xv[i].z, xv[i].z));
+    ss = __fadd_rn(ss, __fmul_rn(xv[i].w, xv[i].w));
+  }
+  const float inv = rms_inv(warp_sum(ss), a.dh, a.eps);
+  float *b = buf[warp];
+#pragma unroll
+  for (int i = 0; i < VPL; ++i) {
+    const int c = lane + 32 * i;
+    if (c < n4) {
+      const float4 n = xv[i];
+      reinterpret_cast<float4 *>(b)[c] =
+          make_float4(__fmul_rn(__fmul_rn(n.x, inv), wv[i].x), __fmul_rn(__fmul_rn(n.y, inv), wv[i].y),
+                      __fmul_rn(__fmul_rn(n.z, inv), wv[i].z), __fmul_rn(__fmul_rn(n.w, inv), wv[i].w));
+    }
+  }
+  __syncwarp();
+  if (kind == 2) {
+    for (int64_t i = lane; i < a.dh; i += 32) yr[i] = b[i];
+    return;
+  }
+  const float pos = (float)__ldg(a.positions + tok);
+  for (int j = lane; j < a.half; j += 32) {
+    const float ang = __fmul_rn(pos, fr.f[j]);
+    float sn, cs;
+    sincosf(ang, &sn, &cs);
+    const float x0 = b[j], x1 = b[j + a.half];
+    yr[j] = __fsub_rn(__fmul_rn(x0, cs), __fmul_rn(x1, sn));
+    yr[j + a.half] = __fadd_rn(__fmul_rn(x1, cs), __fmul_rn(x0, sn));
+  }
+  for (int64_t i = 2 * a.half + lane; i < a.dh; i += 32) yr[i] = b[i];
+}
+
 // ---- attention --------------------------------------------------------------
 
 struct AttnArgs {
@@ -1179,6 +1263,45 @@ int gq_head_norm_rope(gq_ctx *ctx, const float *x, int64_t t, int64_t heads, int
   ENTER(ctx);
   if (y_tok_stride == 0) y_tok_stride = heads * head_dim;
   return rope_launch(ctx, true, x, w, t, heads, head_dim, eps, positions, theta, rotary_dim, y, y_tok_stride);
+}
+
+int gq_qkv_norm_rope(gq_ctx *ctx, const float *qkv, int64_t t, int64_t qkv_tok_stride, int64_t hq, int64_t hkv,
+                     int64_t head_dim, const float *q_w, const float *k_w, float eps, const uint32_t *positions,
+                     float theta, int64_t rotary_dim, float *q_out, int64_t q_tok_stride, float *k_out,
+                     int64_t k_tok_stride, float *v_out, int64_t v_tok_stride) {
+  ENTER(ctx);
+  const int64_t dh = head_dim, rot = rotary_dim;
+  if (t < 0 || hq <= 0 || hkv <= 0 || dh <= 0 || rot < 0 || rot > dh || rot % 2 != 0)
+    return gq_fail(ctx, GQ_ERR_INVALID_ARGUMENT, "qkv_norm_rope: bad shape (rotary_dim even, <= head_dim)");
+  if (!qkv || !q_w || !k_w || !q_out || !k_out || !v_out || (t > 0 && !positions))
+    return gq_fail(ctx, GQ_ERR_INVALID_ARGUMENT, "qkv_norm_rope: null pointer");
+  if (qkv_tok_stride == 0) qkv_tok_stride = (hq + 2 * hkv) * dh;
+  if (q_tok_stride == 0) q_tok_stride = hq * dh;
+  if (k_tok_stride == 0) k_tok_stride = hkv * dh;
+  if (v_tok_stride == 0) v_tok_stride = hkv * dh;
+  if (qkv_tok_stride < (hq + 2 * hkv) * dh || q_tok_stride < hq * dh || k_tok_stride < hkv * dh ||
+      v_tok_stride < hkv * dh)
+    return gq_fail(ctx, GQ_ERR_INVALID_ARGUMENT, "qkv_norm_rope: token stride too small");
+  const int vpl = reg_vpl(dh);
+  if (dh % 4 != 0 || qkv_tok_stride % 4 != 0 || (uintptr_t)qkv % 16 || (uintptr_t)q_w % 16 || (uintptr_t)k_w % 16 ||
+      !vpl || vpl > 4)
+    return gq_fail(ctx, GQ_ERR_UNSUPPORTED,
+                   "qkv_norm_rope: head_dim a multiple of 4 up to 512, 16-byte aligned rows and weights");
+  if (rot / 2 > kMaxHalfRot) return gq_fail(ctx, GQ_ERR_UNSUPPORTED, "qkv_norm_rope: rotary_dim > 512");
+  if (t == 0) return GQ_OK;
+  RopeFreq fr;
+  const int half = (int)(rot / 2);
+  // the reference's frequency, same f32 expression as rope_launch (rust/src/backend_cpu.rs:258)
+  for (int j = 0; j < half; ++j) fr.f[j] = powf(theta, -(2.0f * (float)j) / (float)rot);
+  QkvArgs a{qkv, t, qkv_tok_stride, (int)hq, (int)hkv, dh, q_w, k_w, eps, positions, half,
+            q_out, k_out, v_out, q_tok_stride, k_tok_stride, v_tok_stride};
+  const int64_t rows = t * (hq + 2 * hkv);
+  const dim3 grid((unsigned)((rows + kNormThreads / 32 - 1) / (kNormThreads / 32))), blk(kNormThreads);
+  cudaError_t e = vpl == 1 ? gq_launch(ctx, qkv_norm_rope_kernel<1>, grid, blk, 0, a, fr)
+                : vpl == 2 ? gq_launch(ctx, qkv_norm_rope_kernel<2>, grid, blk, 0, a, fr)
+                           : gq_launch(ctx, qkv_norm_rope_kernel<4>, grid, blk, 0, a, fr);
+  GQ_CUDA_TRY(ctx, e);
+  return GQ_OK;
 }
 
 int gq_rope(gq_ctx *ctx, const float *x, int64_t t, int64_t heads, int64_t head_dim, const uint32_t *positions,

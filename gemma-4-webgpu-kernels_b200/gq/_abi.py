@@ -94,6 +94,9 @@ SIGNATURES = {
                                      c_void_p, c_void_p, c_void_p]),
     "gq_head_norm_rope": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_float, c_void_p,
                                   c_float, c_int64, c_void_p, c_int64]),
+    "gq_qkv_norm_rope": (
+        c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_float, c_void_p,
+                c_float, c_int64, c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int64]),
     "gq_rope": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_float, c_int64, c_void_p,
                         c_int64]),
     "gq_attention": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int64,

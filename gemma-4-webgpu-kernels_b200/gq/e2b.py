@@ -223,6 +223,30 @@ class Decoder:
             del payload
             return t
 
+        def qt_stack(pre, parts, k, bits):
+            """One device weight holding the rows of several projections of the same
+            input, stacked in order (packed rows are independent, so one GEMV over
+            the stack gives each projection's outputs side by side)."""
+            for nm, rows in parts:
+                self.meta[pre + nm] = (rows, k, bits, k)
+            n = sum(rows for _, rows in parts)
+            if weights is not None:
+                qs = [weights.q[pre + nm] for nm, _ in parts]
+                from . import QuantWeight
+                return g.quant_tensor(QuantWeight(
+                    qbytes=np.concatenate([np.asarray(q.qbytes, dtype=np.uint8) for q in qs]),
+                    scales=np.concatenate([np.asarray(q.scales, dtype=np.float32) for q in qs]),
+                    shape=(n, k), bits=qs[0].bits, signed_i8=qs[0].signed_i8, group_size=qs[0].group_size))
+            rb = k if bits == 8 else k * bits // 8
+            payload = torch.cat([torch.randint(0, 256, (rows * rb,), generator=gen, device=dev, dtype=torch.uint8)
+                                 for _, rows in parts])
+            sc = np.concatenate([synth.uniform(zlib.crc32((pre + nm).encode()), rows, 0.005, 0.02)
+                                 for nm, rows in parts])
+            torch.cuda.synchronize(dev)
+            t = g.quant_tensor_from_device(payload, sc, (n, k), bits, bits == 8, k)
+            del payload
+            return t
+
         def ft(name, n):
             if weights is not None:
                 a = weights.f[name].reshape(-1)
@@ -250,11 +274,13 @@ class Decoder:
                 self.w[p + nm] = ft(p + nm, H)
             self.w[p + "q_norm"] = ft(p + "q_norm", dh)
             self.w[p + "layer_scalar"] = ft(p + "layer_scalar", 1)
-            self.w[p + "q_proj"] = qt(p + "q_proj", c.heads_q * dh, H, c.attn_bits)
             if c.kv_source(i) == i:
-                self.w[p + "k_proj"] = qt(p + "k_proj", c.heads_kv * dh, H, c.attn_bits)
-                self.w[p + "v_proj"] = qt(p + "v_proj", c.heads_kv * dh, H, c.attn_bits)
+                # q, k and v read the same normed input: one stacked weight, one GEMV
+                self.w[p + "qkv_proj"] = qt_stack(p, [("q_proj", c.heads_q * dh), ("k_proj", c.heads_kv * dh),
+                                                      ("v_proj", c.heads_kv * dh)], H, c.attn_bits)
                 self.w[p + "k_norm"] = ft(p + "k_norm", dh)
+            else:
+                self.w[p + "q_proj"] = qt(p + "q_proj", c.heads_q * dh, H, c.attn_bits)
             self.w[p + "o_proj"] = qt(p + "o_proj", H, c.heads_q * dh, c.attn_bits)
             self.w[p + "gate"] = qt(p + "gate", c.inter, H, c.mlp_bits)
             self.w[p + "up"] = qt(p + "up", c.inter, H, c.mlp_bits)
@@ -291,7 +317,7 @@ class Decoder:
         self.h, self.x = z(B, H), z(B, H)
         self.emb, self.proj, self.ple = z(B, L * P), z(B, L * P), z(B, L * P)
         self.q, self.qr, self.attn = z(B, dq), z(B, dq), z(B, dq)
-        self.kn, self.vn = z(B, c.heads_kv * c.global_head_dim), z(B, c.heads_kv * c.global_head_dim)
+        self.qkv = z(B, (c.heads_q + 2 * c.heads_kv) * c.global_head_dim)
         self.o, self.ff, self.inj = z(B, H), z(B, c.inter), z(B, P)
         self.logits = z(B, c.vocab)
         self.position = -1
@@ -338,21 +364,19 @@ class Decoder:
             kvd = c.heads_kv * dh
             cstride = self.capacity * kvd
             # attention block (rust/src/model.rs:214-219, 233-300)
-            add(pre + "q_proj", lib.gq_linear, ctx, V(self.x), B, H, Q(pre + "q_proj"), V(self.q))
-            add(pre + "q_norm_rope", lib.gq_head_norm_rope, ctx, V(self.q), B, c.heads_q, dh, F(pre + "q_norm"), eps,
-                V(self.pos), c_float(theta), rot, V(self.qr), c.heads_q * dh)
             if src == i:
-                add(pre + "k_proj", lib.gq_linear, ctx, V(self.x), B, H, Q(pre + "k_proj"), V(self.kn))
-                add(pre + "v_proj", lib.gq_linear, ctx, V(self.x), B, H, Q(pre + "v_proj"), V(self.vn))
-                # k: norm + rope, written into slot p of every sequence's cache
-                add(pre + "k_norm_rope", lib.gq_head_norm_rope, ctx, V(self.kn), B, c.heads_kv, dh,
-                    F(pre + "k_norm"), eps, V(self.pos), c_float(theta), rot,
-                    c_void_p(kc.data_ptr() + 4 * p * kvd), cstride)
-                # v: unweighted per-head norm into slot p (rust/src/model.rs:272-273)
-                if c.heads_kv != 1:
-                    raise GqError(2, "Decoder: value rows are written per sequence (heads_kv must be 1)")
-                add(pre + "v_norm", lib.gq_rms_norm, ctx, V(self.vn), B, dh, None, eps,
+                # q|k|v in one GEMV, then the q and k norms + RoPE and the unweighted
+                # value norm (rust/src/model.rs:258-273) in one launch, k and v written
+                # straight into slot p of every sequence's cache
+                add(pre + "qkv_proj", lib.gq_linear, ctx, V(self.x), B, H, Q(pre + "qkv_proj"), V(self.qkv))
+                add(pre + "qkv_norm_rope", lib.gq_qkv_norm_rope, ctx, V(self.qkv), B, (c.heads_q + 2 * c.heads_kv) * dh,
+                    c.heads_q, c.heads_kv, dh, F(pre + "q_norm"), F(pre + "k_norm"), eps, V(self.pos),
+                    c_float(theta), rot, V(self.qr), c.heads_q * dh, c_void_p(kc.data_ptr() + 4 * p * kvd), cstride,
                     c_void_p(vc.data_ptr() + 4 * p * kvd), cstride)
+            else:
+                add(pre + "q_proj", lib.gq_linear, ctx, V(self.x), B, H, Q(pre + "q_proj"), V(self.q))
+                add(pre + "q_norm_rope", lib.gq_head_norm_rope, ctx, V(self.q), B, c.heads_q, dh, F(pre + "q_norm"),
+                    eps, V(self.pos), c_float(theta), rot, V(self.qr), c.heads_q * dh)
             add(pre + "attention", lib.gq_attention, ctx, V(self.qr), B, 1, c.heads_q, dh, V(kc), V(vc), S,
                 c.heads_kv, cstride, V(self.pos), None, 0, c_float(1.0), c.window_of(i), c_float(0.0),
                 GQ_ATTN_KPOS_IDENTITY, V(self.attn))

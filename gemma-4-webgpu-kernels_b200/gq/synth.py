@@ -165,12 +165,17 @@ class Proj:
     mode: int = 0  # 0 linear, 1 geglu (gate+up pair), 2 gelu * PLE slice
 
 
-def layer_projections(i: int) -> list:
+def layer_projections(i: int, stack_qkv: bool = False) -> list:
     """The quantized projections of decoder layer i at the BASELINE config-2 bit
-    widths: I8 attention and PLE, 4-bit gate/up (fused GeGLU), 2-bit down."""
+    widths: I8 attention and PLE, 4-bit gate/up (fused GeGLU), 2-bit down.
+    stack_qkv: the q, k and v projections of a KV layer as one stacked weight
+    (they read the same input; the decode step runs them as one GEMV)."""
     dh = HEAD_DIM_GLOBAL if is_global(i) else HEAD_DIM_LOCAL
-    out = [Proj(f"l{i}.q_proj", HEADS_Q * dh, HIDDEN, 8, True)]
-    if i < KV_LAYERS:
+    if stack_qkv and i < KV_LAYERS:
+        out = [Proj(f"l{i}.qkv_proj", (HEADS_Q + 2) * dh, HIDDEN, 8, True)]
+    else:
+        out = [Proj(f"l{i}.q_proj", HEADS_Q * dh, HIDDEN, 8, True)]
+    if i < KV_LAYERS and not stack_qkv:
         out += [Proj(f"l{i}.k_proj", dh, HIDDEN, 8, True), Proj(f"l{i}.v_proj", dh, HIDDEN, 8, True)]
     out += [
         Proj(f"l{i}.o_proj", HIDDEN, HEADS_Q * dh, 8, True),

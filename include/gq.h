@@ -249,6 +249,18 @@ int gq_add_rms_norm_norm(gq_ctx *ctx, const float *residual, const float *x, int
 int gq_head_norm_rope(gq_ctx *ctx, const float *x, int64_t t, int64_t heads, int64_t head_dim, const float *w,
                       float eps, const uint32_t *positions, float theta, int64_t rotary_dim, float *y,
                       int64_t y_tok_stride);
+/* The attention inputs of a KV layer in one launch, on the stacked q|k|v
+ * projection output qkv [t, (hq + 2 hkv) * head_dim] (token stride qkv_tok_stride,
+ * 0 = packed): q = head_norm_rope(q rows, q_w), k = head_norm_rope(k rows, k_w) and
+ * v = rms_norm(v rows, no weight) per head, the composition of
+ * rust/src/model.rs:258-273 (the three Backend::head_norm_rope / rms_norm calls).
+ * Each output token i is written at out + i * out_tok_stride (0 = packed), so the
+ * key and value rows can go straight into a KV cache. Same arithmetic as the
+ * separate calls (bit-identical). head_dim a multiple of 4 up to 512. */
+int gq_qkv_norm_rope(gq_ctx *ctx, const float *qkv, int64_t t, int64_t qkv_tok_stride, int64_t hq, int64_t hkv,
+                     int64_t head_dim, const float *q_w, const float *k_w, float eps, const uint32_t *positions,
+                     float theta, int64_t rotary_dim, float *q_out, int64_t q_tok_stride, float *k_out,
+                     int64_t k_tok_stride, float *v_out, int64_t v_tok_stride);
 int gq_rope(gq_ctx *ctx, const float *x, int64_t t, int64_t heads, int64_t head_dim, const uint32_t *positions,
             float theta, int64_t rotary_dim, float *y, int64_t y_tok_stride);
 

@@ -96,6 +96,46 @@ def test_head_norm_rope_and_rope(g, t, heads, dh, rot):
     assert rel(got, o.rope(x, pos, 1e4, dh, heads, rot)) <= OP_REL
 
 
+@pytest.mark.parametrize("t,hq,hkv,dh,rot,theta", [(1, 8, 1, 256, 256, 1e4), (3, 8, 1, 512, 128, 1e6),
+                                                     (64, 8, 1, 256, 256, 1e4), (5, 4, 2, 16, 8, 1e4)])
+def test_qkv_norm_rope_equals_the_three_calls(g, t, hq, hkv, dh, rot, theta):
+    """gq_qkv_norm_rope on the stacked q|k|v rows gives exactly q/k head_norm_rope and
+    the unweighted value rms_norm, with k and v written into strided cache rows."""
+    import torch
+
+    width = (hq + 2 * hkv) * dh
+    qkv_h = synth.normal(130 + dh + t, t * width).reshape(t, width) * 2.0
+    qw_h, kw_h = synth.uniform(131 + dh, dh, 0.8, 1.2), synth.uniform(132 + dh, dh, 0.8, 1.2)
+    pos_h = [2047 - 5 * i for i in range(t)]
+    qkv = g.tensor(qkv_h, qkv_h.shape)
+    qw, kw = g.tensor(qw_h, (dh,)), g.tensor(kw_h, (dh,))
+    pos = g._u32_dev(pos_h)
+    cap = 7  # cache rows per sequence; the step writes row 2 of each
+    kc = torch.zeros(t, cap, hkv * dh, device=g.torch_device)
+    vc = torch.zeros(t, cap, hkv * dh, device=g.torch_device)
+    q = g.zeros((t, hq * dh))
+    g._check(g.lib.gq_qkv_norm_rope(g.ctx, c_void_p(qkv.ptr()), t, 0, hq, hkv, dh, c_void_p(qw.ptr()),
+                                    c_void_p(kw.ptr()), c_float(1e-6), c_void_p(pos.data_ptr()), c_float(theta), rot,
+                                    c_void_p(q.ptr()), 0, c_void_p(kc.data_ptr() + 4 * 2 * hkv * dh), cap * hkv * dh,
+                                    c_void_p(vc.data_ptr() + 4 * 2 * hkv * dh), cap * hkv * dh), "qkv_norm_rope")
+    qs = qkv_h[:, : hq * dh].reshape(t, hq, dh)
+    ks = qkv_h[:, hq * dh: (hq + hkv) * dh].reshape(t, hkv, dh)
+    vs = qkv_h[:, (hq + hkv) * dh:].reshape(t * hkv, dh)
+    q_ref = g.readback(g.head_norm_rope(g.tensor(qs, qs.shape), qw, 1e-6, pos_h, theta, dh, hq, rot))
+    k_ref = g.readback(g.head_norm_rope(g.tensor(ks, ks.shape), kw, 1e-6, pos_h, theta, dh, hkv, rot))
+    v_ref = g.readback(g.rms_norm(g.tensor(vs, vs.shape), None, 1e-6))
+    g.flush()
+    k_got, v_got = kc[:, 2].cpu().numpy(), vc[:, 2].cpu().numpy()
+    assert np.array_equal(g.readback(q).reshape(q_ref.shape), q_ref)
+    assert np.array_equal(k_got.reshape(k_ref.shape), k_ref)
+    assert np.array_equal(v_got.reshape(v_ref.shape), v_ref)
+    # untouched cache rows
+    assert not kc[:, [0, 1, 3]].any() and not vc[:, [0, 1, 3]].any()
+    assert rel(g.readback(q), o.head_norm_rope(qs, qw_h, 1e-6, pos_h, theta, dh, hq, rot)) <= OP_REL
+    assert rel(k_got, o.head_norm_rope(ks, kw_h, 1e-6, pos_h, theta, dh, hkv, rot)) <= OP_REL
+    assert rel(v_got, o.rms_norm(vs, None, 1e-6)) <= OP_REL
+
+
 def test_rope_large_positions(g):
     """Decode positions up to 2047 at both E2B rope settings (theta 1e4 full, 1e6 partial)."""
     for dh, rot, theta in [(256, 256, 1e4), (512, 128, 1e6)]:
