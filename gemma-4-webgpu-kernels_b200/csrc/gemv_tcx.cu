@@ -31,6 +31,7 @@
 #include <math.h>
 
 #include <stdlib.h>
+#include <string.h>
 
 #include <algorithm>
 
@@ -72,6 +73,8 @@ struct TcxArgs {
   int raw_bytes, mma_bytes, xa_tile;
   int issuers;
   int tmem_cols;
+  int ksplit;             // K splits: the CTAs of one cluster (cluster rank = blockIdx.y)
+  int kb_per;             // K-blocks per split (the last split may have fewer)
   uint32_t *err;
 };
 
@@ -109,6 +112,20 @@ __device__ __forceinline__ bool wait_phase(uint64_t *bar, uint32_t parity) {
 }
 // barrier among the 4 expander/epilogue warps only
 __device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, %0;" ::"r"(kExpWarps * 32) : "memory"); }
+// all threads of every CTA of the cluster (release / acquire at cluster scope)
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+// the shared::cluster address of this CTA's shared-memory location p in cluster CTA `rank`
+__device__ __forceinline__ uint32_t cluster_addr(const void *p, uint32_t rank) {
+  uint32_t ra;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(gqd::smem_u32(p)), "r"(rank));
+  return ra;
+}
+// two 64-bit values at a shared::cluster address (16-byte aligned)
+__device__ __forceinline__ void ld_cluster_v2s64(uint32_t addr, long long &v0, long long &v1) {
+  asm volatile("ld.shared::cluster.v2.s64 {%0, %1}, [%2];" : "=l"(v0), "=l"(v1) : "r"(addr) : "memory");
+}
 
 // ---- pre-pass: x row m -> 30-bit fixed point -> four s8 limb rows ------------
 // Same arithmetic as the in-CTA staging of gemv_tc.cu: s = 30 - e with
@@ -260,13 +277,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   double *tok_pw = reinterpret_cast<double *>(smem + L.misc_off + 64);  // [kMaxTok] 2^-s
   long long *tok_zc = reinterpret_cast<long long *>(tok_pw + kMaxTok);  // [kMaxTok] ZP * sum X
   uint32_t *tok_bad = reinterpret_cast<uint32_t *>(tok_zc + kMaxTok);   // [kMaxTok]
+  // split-K partials [NW][M][tile_rows] (int64), over the rings once every MMA has completed
+  long long *part = reinterpret_cast<long long *>(smem);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int n_begin = blockIdx.x * a.tile_rows;
   const int n_end = min(a.N, n_begin + a.tile_rows);
-  const int kblocks = a.kblocks, kbr = a.kbr, RS = a.raw_stages, MS = a.mma_stages;
-  const int NI = a.issuers, XI = a.xi, XL = a.xi_log2;
+  // split-K: this CTA (cluster rank sidx) owns K-blocks kbase .. kbase + kblocks - 1
+  const int KS = a.ksplit, sidx = KS > 1 ? (int)blockIdx.y : 0;
+  const int kbase = sidx * a.kb_per;
+  const int kblocks = KS > 1 ? min(a.kb_per, a.kblocks - kbase) : a.kblocks;
+  const int kbr = a.kbr, RS = a.raw_stages, MS = a.mma_stages;
   const int total_raw = (kblocks + kbr - 1) / kbr;
+  // issuers with work: the last K split may own fewer work units than the plan's
+  // issuer count (its rings then never wrap, so the slot ownership still holds)
+  const int NI = max(1, min(a.issuers, DIRECT ? total_raw : kblocks)), XI = a.xi, XL = a.xi_log2;
   const int tile_bytes = a.tile_rows * 128;
   const uint32_t xa_tile = (uint32_t)a.xa_tile;
 
@@ -289,12 +314,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       gqd::mbar_arrive_expect_tx(&raw_full[slot], (uint32_t)(nkb * NW * tile_bytes));
       for (int j = 0; j < nkb; ++j)
         for (int h = 0; h < NW; ++h)
-          tma_load_2d(dst + (j * NW + h) * tile_bytes, h ? &map_w2 : &map_w, (kb0 + j) * kKB, n_begin,
+          tma_load_2d(dst + (j * NW + h) * tile_bytes, h ? &map_w2 : &map_w, (kbase + kb0 + j) * kKB, n_begin,
                       &raw_full[slot]);
     } else {
       gqd::mbar_arrive_expect_tx(&raw_full[slot], (uint32_t)(NW * a.tile_rows * kbr * KB_BYTES));
       for (int h = 0; h < NW; ++h)
-        tma_load_2d(dst + h * a.tile_rows * kbr * KB_BYTES, h ? &map_w2 : &map_w, kb0 * KB_BYTES, n_begin,
+        tma_load_2d(dst + h * a.tile_rows * kbr * KB_BYTES, h ? &map_w2 : &map_w, (kbase + kb0) * KB_BYTES, n_begin,
                     &raw_full[slot]);
     }
   };
@@ -315,7 +340,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   };
   auto issue_x = [&](int slot, int g) {  // limb tile of K-block g
     gqd::mbar_arrive_expect_tx(&xa_full[slot], xa_tile);
-    gqd::bulk_g2s(xa + (size_t)slot * xa_tile, a.limbs + (size_t)g * xa_tile, xa_tile, &xa_full[slot]);
+    gqd::bulk_g2s(xa + (size_t)slot * xa_tile, a.limbs + (size_t)(kbase + g) * xa_tile, xa_tile, &xa_full[slot]);
   };
 
   // ---- widening of sub-byte / U8 codes: the 4 warps widen one raw stage at a time ----
@@ -632,6 +657,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int nl = c0 + 4 * hr + limb;
             const int n = n_begin + nl;
             if (!lane_ok || n >= n_end) continue;
+            if (KS > 1) {  // this split's exact partial sums, finalised after the cluster barrier
+#pragma unroll
+              for (int h = 0; h < NW; ++h) part[((size_t)h * a.M + tok) * a.tile_rows + nl] = T[h][hr];
+              continue;
+            }
             float o;
             if (badt) {
               o = __int_as_float(0x7fc00000);
@@ -660,7 +690,71 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (!*abort_flag && (a.peers.n > 0 || a.peers.signal)) gqd::push_to_peers(a.y, a.peers, a.M, a.ldy, a.y_col0 + n_begin, a.y_col0 + n_end);
+  int c_lo = n_begin, c_hi = n_end;  // output columns this CTA completes
+  if (KS > 1) {
+    // Every CTA of the cluster holds its split's partials; CTA sidx finalises
+    // rows [r_lo, r_hi) of the tile for every token: the partials are summed in
+    // int64 (exact, fixed order) over the cluster's shared memory.
+    cluster_sync_all();
+    const int per = ((a.tile_rows + KS - 1) / KS + 3) & ~3;
+    const int r_lo = min(n_end - n_begin, sidx * per), r_hi = min(n_end - n_begin, r_lo + per);
+    c_lo = n_begin + r_lo;
+    c_hi = n_begin + r_hi;
+    const int nr = r_hi - r_lo;
+    if (!*abort_flag && nr > 0) {
+      uint32_t rbase[8];  // the partials' base in every cluster CTA
+#pragma unroll
+      for (int q = 0; q < 8; ++q) rbase[q] = cluster_addr(part, (uint32_t)(q < KS ? q : 0));
+      const int np = (nr + 1) >> 1;  // pairs of adjacent rows (r_lo is even, partial rows are 16-byte pairs)
+      for (int idx = tid; idx < a.M * np; idx += kThreads) {
+        const int tok = idx / np, nl = r_lo + 2 * (idx - tok * np);
+        long long T[NW][2];
+#pragma unroll
+        for (int h = 0; h < NW; ++h) {
+          const uint32_t off = (uint32_t)((((size_t)h * a.M + tok) * a.tile_rows + nl) * 8);
+          long long v[8][2];
+#pragma unroll
+          for (int q = 0; q < 8; ++q)  // all loads issued before the sums
+            if (q < KS) ld_cluster_v2s64(rbase[q] + off, v[q][0], v[q][1]);
+          T[h][0] = T[h][1] = 0;
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            if (q < KS) {
+              T[h][0] += v[q][0];
+              T[h][1] += v[q][1];
+            }
+        }
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int nle = nl + e, n = n_begin + nle;
+          if (nle >= r_hi) break;
+          float o;
+          if (tok_bad[tok]) {
+            o = __int_as_float(0x7fc00000);
+          } else {
+            const double pwt = tok_pw[tok];
+            const long long zct = tok_zc[tok];
+            const float v0 = __fmul_rn((float)((double)(T[0][e] - zct) * pwt), scb[nle]);
+            if (MODE == 1) {
+              const float v1 = __fmul_rn((float)((double)(T[NW - 1][e] - zct) * pwt), scb[a.tile_rows + nle]);
+              o = __fmul_rn(gqd::gelu_tanh(v0), v1);
+            } else if (MODE == 2) {
+              o = __fmul_rn(gqd::gelu_tanh(v0), a.bs[(size_t)tok * a.b_stride + a.b_off + n]);
+            } else if (MODE == 3) {
+              o = a.cap > 0.0f ? __fmul_rn(a.cap, tanhf(__fdiv_rn(v0, a.cap))) : v0;
+            } else {
+              o = v0;
+            }
+          }
+          a.y[(size_t)tok * a.ldy + a.y_col0 + n] = o;
+        }
+      }
+    }
+    __syncthreads();
+  }
+  if (!*abort_flag && (a.peers.n > 0 || a.peers.signal)) gqd::push_to_peers(a.y, a.peers, a.M, a.ldy, a.y_col0 + c_lo, a.y_col0 + c_hi);
+  // no CTA leaves (releasing its shared memory) while a cluster peer may still read it
+  if (KS > 1) cluster_sync_all();
   if (*abort_flag) {
     if (tid == 0) gqd::report(a.err, GQ_DEVERR_WAIT_TIMEOUT);
     __syncthreads();
@@ -684,7 +778,28 @@ int launch_x(gq_ctx *ctx, const CUtensorMap &m1, const CUtensorMap &m2, const Tc
     GQ_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ctx->smem_optin));
     attr_set[dev][a.wa] = true;
   }
-  GQ_CUDA_TRY(ctx, gq_launch(ctx, kern, grid, dim3(kThreads), smem, m1, m2, a));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = ctx->stream;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (ctx->pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (a.ksplit > 1) {  // the split CTAs of one tile form a cluster (grid y = split index)
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 1;
+    attr[na].val.clusterDim.y = (unsigned)a.ksplit;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  GQ_CUDA_TRY(ctx, cudaLaunchKernelEx(&cfg, kern, m1, m2, a));
   return GQ_OK;
 }
 
@@ -703,15 +818,25 @@ struct TcxPlan {
   int wa, lrows;
   int tile_rows, mh, gx, slice_rows, kblocks, kbr, raw_stages, mma_stages, xa_stages, xi, raw_bytes, mma_bytes,
       xa_tile, issuers, tmem_cols;
+  int ksplit, kb_per;
   size_t smem;
 };
 
 int mh_of(int64_t m) { return m <= 16 ? 0 : (m <= 32 ? 1 : 2); }
 
-// One tile of weight rows per CTA. Weights taller than num_sms tiles run as
-// row slices of num_sms * tile_rows rows. Rings sized to the SM's shared memory:
-// the limb ring gets up to ~half of it, the weight rings the rest.
-bool tcx_plan(const gq_ctx *ctx, const gq_qweight *w, int64_t m, int nw, bool wa, TcxPlan &p) {
+int tcx_max_tile(int64_t m, int nw, bool wa) {
+  const int MH = (wa || mh_of(m) == 0) ? 1 : mh_of(m);
+  return wa ? 128 : std::min(256 / nw, 512 / (MH * nw)) / 16 * 16;
+}
+
+// One tile of weight rows per CTA (tile_rows <= 0: the default, N / num_sms
+// rounded up to 16). Weights taller than num_sms tiles run as row slices of
+// num_sms * tile_rows rows. ks > 1 splits the K-blocks over a cluster of ks
+// CTAs per tile (one slice only, limb rows as A). Rings sized to the SM's
+// shared memory for the CTA's own K-blocks: the limb ring gets up to ~half of
+// it, the weight rings the rest.
+bool tcx_plan_with(const gq_ctx *ctx, const gq_qweight *w, int64_t m, int nw, bool wa, int tile_rows, int ks,
+                   TcxPlan &p) {
   const bool direct = (w->bits == 8 && w->signed_i8);
   const int kb_bytes = kKB * w->bits / 8;
   p.wa = wa;
@@ -720,41 +845,50 @@ bool tcx_plan(const gq_ctx *ctx, const gq_qweight *w, int64_t m, int nw, bool wa
   const int MH = (wa || p.mh == 0) ? 1 : p.mh;
   const int xa_rows = wa ? p.lrows : (p.mh == 0 ? 64 : 128 * p.mh);
   p.xa_tile = xa_rows * 128;
-  const int max_tile = wa ? 128 : std::min(256 / nw, 512 / (MH * nw)) / 16 * 16;
+  const int max_tile = tcx_max_tile(m, nw, wa);
   const int64_t rows0 = (w->n + ctx->num_sms - 1) / ctx->num_sms;
-  p.tile_rows = wa ? 128 : (int)std::min<int64_t>(max_tile, std::max<int64_t>(16, (rows0 + 15) / 16 * 16));
+  if (tile_rows <= 0) tile_rows = (int)std::min<int64_t>(max_tile, std::max<int64_t>(16, (rows0 + 15) / 16 * 16));
+  if (wa) tile_rows = 128;
+  if (tile_rows % 16 != 0 || tile_rows < 16 || tile_rows > max_tile) return false;
+  p.tile_rows = tile_rows;
   const int acc_cols = wa ? nw * p.lrows : MH * nw * p.tile_rows;
   p.slice_rows = (int)std::min<int64_t>(w->n, (int64_t)ctx->num_sms * p.tile_rows);
   p.gx = (int)((p.slice_rows + p.tile_rows - 1) / p.tile_rows);
   p.kblocks = (int)((w->k + kKB - 1) / kKB);
+  // split-K: a cluster of ks CTAs per tile, every split non-empty, one slice
+  if (ks < 1 || ks > 8 || (ks > 1 && (wa || p.slice_rows < w->n || (int64_t)p.gx * ks > ctx->num_sms))) return false;
+  p.ksplit = ks;
+  p.kb_per = (p.kblocks + ks - 1) / ks;
+  if (ks > 1 && (int64_t)(ks - 1) * p.kb_per >= p.kblocks) return false;
+  const int kbl = p.kb_per;  // K-blocks of one CTA (rings are sized for these)
   const int tile_bytes = p.tile_rows * 128;
   const int sc_bytes = nw * p.tile_rows * 4;
   const size_t budget = ctx->smem_optin - 1024;
   // issuers: TMEM columns, work units; then the limb ring: XI >= 2 slots each
-  const int units_hint = direct ? p.kblocks : p.kblocks;
+  const int units_hint = direct ? kbl : kbl;
   p.issuers = std::max(1, std::min(std::min(kMaxIss, units_hint), 512 / acc_cols));
   const size_t xa_budget = std::min<size_t>(budget / 2 + 16384, 131072);
   while (p.issuers > 1 && (size_t)p.issuers * 2 * p.xa_tile > xa_budget) --p.issuers;
   p.xi = (int)std::max<size_t>(2, std::min<size_t>(kMaxXa / p.issuers, xa_budget / ((size_t)p.issuers * p.xa_tile)));
-  p.xi = std::min(p.xi, std::max(2, (p.kblocks + p.issuers - 1) / p.issuers));
+  p.xi = std::min(p.xi, std::max(2, (kbl + p.issuers - 1) / p.issuers));
   if (direct) {
-    p.kbr = std::max(1, std::min(p.kblocks, (8192 + nw * tile_bytes - 1) / (nw * tile_bytes)));
+    p.kbr = std::max(1, std::min(kbl, (8192 + nw * tile_bytes - 1) / (nw * tile_bytes)));
     p.raw_bytes = p.kbr * nw * tile_bytes;
     p.mma_bytes = 0;
     p.mma_stages = 0;
   } else {
     // K-blocks per packed stage: up to 256-byte TMA rows, stages of at most ~32 KB
-    p.kbr = std::max(1, std::min(std::min(p.kblocks, 256 / kb_bytes), 32768 / (nw * p.tile_rows * kb_bytes)));
+    p.kbr = std::max(1, std::min(std::min(kbl, 256 / kb_bytes), 32768 / (nw * p.tile_rows * kb_bytes)));
     p.raw_bytes = (nw * p.tile_rows * p.kbr * kb_bytes + 1023) / 1024 * 1024;
     p.mma_bytes = nw * tile_bytes;
   }
-  const int total_raw = (p.kblocks + p.kbr - 1) / p.kbr;
+  const int total_raw = (kbl + p.kbr - 1) / p.kbr;
   for (;;) {
     p.xa_stages = p.issuers * p.xi;
     if (!direct) {
       const TcxSmem L0 = tcx_layout(p.xa_stages, p.xa_tile, 2, p.raw_bytes, 0, p.mma_bytes, sc_bytes);
       const int fit = L0.total <= budget ? (int)((budget - L0.total) / p.mma_bytes) : 0;
-      p.mma_stages = std::min(std::min(kMaxMma, p.kblocks), fit);
+      p.mma_stages = std::min(std::min(kMaxMma, kbl), fit);
     }
     const TcxSmem L1 = tcx_layout(p.xa_stages, p.xa_tile, 0, p.raw_bytes, p.mma_stages, p.mma_bytes, sc_bytes);
     const int fit = L1.total <= budget ? (int)((budget - L1.total) / p.raw_bytes) : 0;
@@ -770,7 +904,7 @@ bool tcx_plan(const gq_ctx *ctx, const gq_qweight *w, int64_t m, int nw, bool wa
       return false;
     }
   }
-  const int units = direct ? total_raw : p.kblocks;
+  const int units = direct ? total_raw : kbl;
   p.issuers = std::min(p.issuers, std::max(1, units));
   // A ring that wraps must hand each slot back to the same issuer (slots are
   // consumed round-robin): its depth is then a multiple of the issuer count.
@@ -778,7 +912,7 @@ bool tcx_plan(const gq_ctx *ctx, const gq_qweight *w, int64_t m, int nw, bool wa
     while (p.issuers > 1 && p.raw_stages < p.issuers) --p.issuers;
     p.raw_stages -= p.raw_stages % p.issuers;
   }
-  if (!direct && p.mma_stages < p.kblocks) {
+  if (!direct && p.mma_stages < kbl) {
     while (p.issuers > 1 && p.mma_stages < p.issuers) --p.issuers;
     p.mma_stages -= p.mma_stages % p.issuers;
   }
@@ -789,7 +923,42 @@ bool tcx_plan(const gq_ctx *ctx, const gq_qweight *w, int64_t m, int nw, bool wa
   p.tmem_cols = 32;
   while (p.tmem_cols < cols) p.tmem_cols <<= 1;
   p.smem = tcx_layout(p.xa_stages, p.xa_tile, p.raw_stages, p.raw_bytes, p.mma_stages, p.mma_bytes, sc_bytes).total;
+  if (ks > 1) {  // the partials [nw][m][tile_rows] int64 overlay the rings
+    const TcxSmem L = tcx_layout(p.xa_stages, p.xa_tile, p.raw_stages, p.raw_bytes, p.mma_stages, p.mma_bytes,
+                                 sc_bytes);
+    if ((size_t)nw * (size_t)m * (size_t)p.tile_rows * 8 > L.sc_off) return false;
+  }
   return p.tmem_cols <= 512 && p.smem <= budget;
+}
+
+// Plan choice. The per-CTA cost grows with its K-block count (each K-block is
+// a limb tile fetch and a few small MMAs), so long rows split K over a cluster:
+// measured on the E2B projections (graph-replayed, M = 8 / 64, one B200):
+//   K = 6144 (2-bit down)      25.6 -> 12.4 / 29.2 -> 15.9 us with 4 splits, 64-row tiles
+//   K = 4096 (global o_proj)   14.0 -> 10.9 / 20.3 -> 13.9 us with 4 splits, 64-row tiles
+//   K = 2048 (local o_proj)     9.2 ->  8.9 / 13.3 -> 11.5 us with 2 splits, 32-row tiles
+//   N = 256, K = 1536 (PLE gate) 8.5 -> 7.6 / 12.1 ->  9.3 us with 4 splits, 32-row tiles
+// and no gain for K = 1536 with N >= 2048 (q|k|v, gate|up) or K = 256. The first
+// candidate that fits is taken. GQ_TCX_SPLIT="S" or "S:tile" forces a split
+// count (and tile) when that plan fits.
+bool tcx_plan(const gq_ctx *ctx, const gq_qweight *w, int64_t m, int nw, bool wa, TcxPlan &p) {
+  const char *e = getenv("GQ_TCX_SPLIT");
+  if (e && *e && !wa) {
+    int ks = atoi(e), tile = 0;
+    const char *c = strchr(e, ':');
+    if (c) tile = atoi(c + 1);
+    if (ks >= 1 && tcx_plan_with(ctx, w, m, nw, wa, tile, ks, p)) return true;
+  } else if (!wa) {
+    const int kb = (int)((w->k + kKB - 1) / kKB);
+    if (kb >= 24) {
+      if (tcx_plan_with(ctx, w, m, nw, wa, 64, 4, p) || tcx_plan_with(ctx, w, m, nw, wa, 32, 2, p)) return true;
+    } else if (kb >= 16) {
+      if (tcx_plan_with(ctx, w, m, nw, wa, 32, 2, p)) return true;
+    } else if (kb >= 8 && w->n <= 1024) {
+      if (tcx_plan_with(ctx, w, m, nw, wa, 32, 4, p)) return true;
+    }
+  }
+  return tcx_plan_with(ctx, w, m, nw, wa, 0, 1, p);
 }
 
 CUresult encode_w(CUtensorMap *map, const gq_qweight *w, const TcxPlan &p) {
@@ -907,10 +1076,12 @@ int gq_gemv_tcx_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const g
     a.xa_tile = p.xa_tile;
     a.issuers = p.issuers;
     a.tmem_cols = p.tmem_cols;
+    a.ksplit = p.ksplit;
+    a.kb_per = p.kb_per;
     a.err = ctx->dev_err;
     a.peers = ctx->peers;
     a.peers.signal = ctx->peers.signal && (r0 + p.slice_rows >= w->n);  // the launch that completes y
-    const dim3 grid((unsigned)((rows + p.tile_rows - 1) / p.tile_rows));
+    const dim3 grid((unsigned)((rows + p.tile_rows - 1) / p.tile_rows), (unsigned)p.ksplit);
     if (w->bits == 4) rc = launch_xm<4, false>(ctx, mode, m1, m2, a, grid, p.smem);
     else if (w->bits == 2) rc = launch_xm<2, false>(ctx, mode, m1, m2, a, grid, p.smem);
     else if (w->signed_i8) rc = launch_xm<8, true>(ctx, mode, m1, m2, a, grid, p.smem);

@@ -142,3 +142,54 @@ def test_short_m_tensor_core_layouts_fused(g, monkeypatch, wa, m):
     b = synth.normal(3605, m * 8960).reshape(m, 8960)
     got = g.readback(g.linear_gelu_mul_cols(g.tensor(x, x.shape), g.quant_tensor(w), g.tensor(b, b.shape), 768))
     assert rel_l2(got, oracle.linear_gelu_mul_cols(x, w, b, 768)) <= REL_L2
+
+
+# (rows, K, bits, signed, M, "splits:tile"): split-K plans that fit (one CTA
+# cluster of `splits` CTAs per weight tile, at most one CTA per SM)
+SPLITS = [(1536, 6144, 2, False, 64, "8:128"), (1536, 6144, 2, False, 8, "8:128"), (1536, 6144, 2, False, 24, "4:64"),
+          (2048, 1536, 8, True, 64, "8:128"), (2048, 1536, 8, True, 5, "4:128"), (6144, 1536, 4, False, 40, "2:128"),
+          (300, 640, 8, False, 16, "2:64"), (1536, 2048, 8, True, 33, "8:128"), (77, 256, 4, False, 7, "2:16")]
+
+
+@pytest.mark.parametrize("n,k,bits,signed,m,split", SPLITS)
+def test_short_m_split_k_is_exact(g, monkeypatch, n, k, bits, signed, m, split):
+    """Split-K over a CTA cluster: every split's exact int64 partial sums are
+    added over distributed shared memory before the one conversion, so the
+    output is bit-identical to the unsplit kernel's (and within the FFMA bound
+    of the oracle)."""
+    monkeypatch.setenv("GQ_DECODE_TC", "2")
+    w = synth.random_qweight(3700 + n + k + bits, n, k, bits, signed)
+    x = synth.normal(3701 + m, m * k).reshape(m, k)
+    gw, gx = g.quant_tensor(w), g.tensor(x, x.shape)
+    monkeypatch.setenv("GQ_TCX_SPLIT", "1")  # one CTA per tile, all K-blocks
+    base = g.readback(g.linear(gx, gw))
+    monkeypatch.setenv("GQ_TCX_SPLIT", split)
+    got = g.readback(g.linear(gx, gw))
+    again = g.readback(g.linear(gx, gw))
+    assert np.array_equal(got, base) and np.array_equal(again, base)
+    assert rel_l2(got, oracle.linear(x, w)) <= REL_L2
+
+
+def test_short_m_split_k_fused_modes(g, monkeypatch):
+    monkeypatch.setenv("GQ_DECODE_TC", "2")
+    k = 1536
+    x = synth.normal(3801, 40 * k).reshape(40, k)
+    gx = g.tensor(x, x.shape)
+    wg = g.quant_tensor(synth.random_qweight(3802, 6144, k, 4, False))
+    wu = g.quant_tensor(synth.random_qweight(3803, 6144, k, 4, False))
+    wp = synth.random_qweight(3804, 256, k, 8, True)
+    gwp = g.quant_tensor(wp)
+    b = synth.normal(3805, 40 * 8960).reshape(40, 8960)
+    gb = g.tensor(b, b.shape)
+    wl = synth.random_qweight(3806, 2000, k, 8, True)
+    gwl = g.quant_tensor(wl)
+    outs = []
+    for split in ("1", "", "2:128", "4:32", "8:128"):
+        monkeypatch.setenv("GQ_TCX_SPLIT", split)
+        outs.append((g.readback(g.linear_geglu(gx, wg, wu)),
+                     g.readback(g.linear_gelu_mul_cols(gx, gwp, gb, 768)),
+                     g.readback(g.linear_softcap(gx, gwl, 30.0))))
+    for o in outs[1:]:
+        for a, b0 in zip(o, outs[0]):
+            assert np.array_equal(a, b0)
+    assert rel_l2(outs[0][2], oracle.softcap(oracle.linear(x, wl), 30.0)) <= REL_L2
