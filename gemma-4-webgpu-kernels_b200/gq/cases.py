@@ -15,6 +15,8 @@ can select launches of that kernel by name and skip the warm-up:
             2047-token cache); each "call" is one step (451 launches)
   attn      batch-64 attention over 2048 cached keys at head_dim 512 (ring kernel)
   tcx       8-row I8 GEMV [2048, 1536] (short-M tensor-core gemv_tcx_kernel)
+  tcx_down  64-row 2-bit GEMV [1536, 6144], the batch-64 down projection (split-K
+            over 4-CTA clusters)
 
 Run from the package directory (or with it on PYTHONPATH).
 """
@@ -27,7 +29,7 @@ from ctypes import c_float, c_void_p
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["config1", "lm_head", "prefill", "embed", "decode", "attn", "tcx"])
+    ap.add_argument("case", choices=["config1", "lm_head", "prefill", "embed", "decode", "attn", "tcx", "tcx_down"])
     ap.add_argument("--iters", type=int, default=8)
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--warmup", type=int, default=3)
@@ -97,6 +99,12 @@ def main(argv=None) -> int:
         x = torch.randn(8, 1536, generator=gen, device=dev)
         y = torch.empty(8, 2048, device=dev)
         calls = [lambda: lib.gq_linear(ctx, c_void_p(x.data_ptr()), 8, 1536, c_void_p(w.qw),
+                                       c_void_p(y.data_ptr()))]
+    elif args.case == "tcx_down":
+        w = upload(1536, 6144, 2, False, 600)
+        x = torch.randn(64, 6144, generator=gen, device=dev)
+        y = torch.empty(64, 1536, device=dev)
+        calls = [lambda: lib.gq_linear(ctx, c_void_p(x.data_ptr()), 64, 6144, c_void_p(w.qw),
                                        c_void_p(y.data_ptr()))]
     else:
         tok = upload(synth.VOCAB, synth.HIDDEN, 4, False, 400)
