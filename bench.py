@@ -433,6 +433,7 @@ def run_gq(args):
 
     if world > 1:
         line["lm_head_sharded"] = sharded_lm_head(torch, dist, rank, world, local, args)
+        line["decode_sharded_lm_head"] = decode_sharded(torch, dist, rank, world, local, args)
     if rank == 0 and world == 1 and not args.no_extras:
         line["extras"] = extras(g, torch, stream, hbm_peak, bf16_peak)
         line["config5_decode"] = config5(g, torch, stream, hbm_peak)
@@ -726,6 +727,50 @@ def config5(g, torch, stream, hbm_peak, batches=(1, 64), steps=50):
         torch.cuda.empty_cache()
     out["config"] = "E2B shapes, KV length 2048 (new token at position 2047), f32 KV cache, I8 attention/PLE/lm_head, " \
                     "4-bit gate/up, 2-bit down, bf16 per-layer model projection; graph-replayed"
+    return out
+
+
+def decode_sharded(torch, dist, rank, world, local, args, batches=(1, 64)):
+    """BASELINE config 5 end to end at N GPUs: the E2B decode step with the trunk
+    replicated and the lm_head split by vocab rows over the ranks (fused sharded
+    lm_head, device barrier), beside the same step with the whole lm_head on each
+    GPU; graph-replayed (two steps per graph, one per logits buffer), max over
+    ranks. Strong scaling of one step's latency (every rank decodes the same batch)."""
+    from gq import CudaBackend, e2b
+
+    cfg = e2b.e2b_config()
+    g = CudaBackend(local, own_stream=True)
+    st = torch.cuda.ExternalStream(g.stream_ptr(), device=g.torch_device)
+    reps = max(10, min(args.steps, 50))
+    out = {}
+    for b in batches:
+        res = {}
+        for key, shard in (("replicated_lm_head", None), ("sharded_lm_head", (rank, world, None))):
+            dec = e2b.Decoder(g, cfg, None, batch=b, cache_len=2047, capacity=2048, device_init_seed=77 + b,
+                              lm_shard=shard)
+            dec.set_ids(np.arange(b) * 4099 % cfg.vocab)
+            dec.run()
+            g.flush()
+            graph = dec.record()
+            for _ in range(3):
+                g.replay(graph)
+            g.flush()
+            dist.barrier()
+            ms = cuda_events_time(torch, st, lambda: g.replay(graph), reps) / (reps * dec.steps_per_graph)
+            g.flush()
+            t = torch.tensor([ms], device=g.torch_device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            ms = float(t.item())
+            res[key] = {"ms_per_step": round(ms, 4), "tokens_per_s": round(b / (ms / 1e3), 1),
+                        "launches_per_step": dec.launches}
+            g.destroy_graph(graph)
+            dec.close()
+            del dec
+            torch.cuda.empty_cache()
+        res["speedup"] = round(res["replicated_lm_head"]["ms_per_step"] / res["sharded_lm_head"]["ms_per_step"], 4)
+        out[f"batch{b}"] = res
+    out["config"] = f"E2B decode step (config 5) at KV length 2048, lm_head [262144, 1536] I8 split {world} ways"
+    g.close()
     return out
 
 

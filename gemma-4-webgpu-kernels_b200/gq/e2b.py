@@ -185,10 +185,18 @@ class Decoder:
     """One decode step of `batch` sequences through the C ABI, with device-resident
     weights, KV caches and activations (all buffers fixed, so a step records into a
     graph). The cache holds `cache_len` seeded tokens (positions 0..cache_len-1);
-    ``set_position(p)`` selects the slot a step writes and attends up to."""
+    ``set_position(p)`` selects the slot a step writes and attends up to.
+
+    lm_shard=(rank, world, group): the lm_head is split by vocab rows over `world`
+    ranks (one process per GPU, torch.distributed initialised). This rank holds
+    rows [r0, r1) and runs the fused sharded lm_head (gq.parallel.PeerLmHead,
+    device barrier): its GEMV stores its logits into every rank's buffer over
+    NVLink, so every rank ends the step with the full logits. The trunk is
+    replicated. Steps alternate between two logits buffers, so ``record`` then
+    captures two steps (one per buffer) and a replay runs both."""
 
     def __init__(self, g, cfg: Config, weights: Optional[Weights], batch: int, cache_len: int,
-                 capacity: Optional[int] = None, device_init_seed: Optional[int] = None):
+                 capacity: Optional[int] = None, device_init_seed: Optional[int] = None, lm_shard=None):
         import torch
 
         self.g, self.cfg, self.batch = g, cfg, batch
@@ -266,7 +274,27 @@ class Decoder:
             self.w["ple_model_proj"] = GqTensor(shape=(L * P, H), data=v.view(torch.int16), bf16=True)
         self.w["ple_proj_norm"] = ft("ple_proj_norm", P)
         self.w["final_norm"] = ft("final_norm", H)
-        self.w["lm_head"] = qt("lm_head", c.vocab, H, c.lm_bits)
+        self.peer = None
+        if lm_shard is None:
+            self.w["lm_head"] = qt("lm_head", c.vocab, H, c.lm_bits)
+        else:
+            from .parallel import PeerLmHead, shard_rows, slice_rows
+            rank, world, group = lm_shard
+            r0, r1 = shard_rows(c.vocab, world, rank)
+            self.meta["lm_head"] = (c.vocab, H, c.lm_bits, H)
+            if weights is not None:
+                shard = g.quant_tensor(slice_rows(weights.q["lm_head"], r0, r1))
+            else:  # the same random stream as the full table, then this rank's rows
+                rb = H if c.lm_bits == 8 else H * c.lm_bits // 8
+                payload = torch.randint(0, 256, (c.vocab * rb,), generator=gen, device=dev, dtype=torch.uint8)
+                sc = synth.uniform(zlib.crc32(b"lm_head"), c.vocab, 0.005, 0.02)
+                torch.cuda.synchronize(dev)
+                shard = g.quant_tensor_from_device(payload[r0 * rb: r1 * rb].contiguous(), sc[r0:r1], (r1 - r0, H),
+                                                   c.lm_bits, c.lm_bits == 8, H)
+                del payload
+            self.w["lm_head"] = shard
+            self.peer = PeerLmHead(g, shard, c.vocab, rank, world, max_m=batch, cap=c.lm_softcap, group=group,
+                                   barrier="device")
         for i in range(L):
             dh = c.dh(i)
             p = f"l{i}."
@@ -320,6 +348,7 @@ class Decoder:
         self.qkv = z(B, (c.heads_q + 2 * c.heads_kv) * c.global_head_dim)
         self.o, self.ff, self.inj = z(B, H), z(B, c.inter), z(B, P)
         self.logits = z(B, c.vocab)
+        self._par = 0
         self.position = -1
         self.set_position(cache_len)
 
@@ -400,13 +429,21 @@ class Decoder:
             add(pre + "ple_norm", lib.gq_add_rms_norm_norm, ctx, V(self.h), V(self.o), B, H, F(pre + "ple_norm"), eps,
                 F(pre + "layer_scalar"), F(nxt), V(self.h), V(self.x))
         # lm_head with the soft-cap on the final-normed h (rust/src/model.rs:183-192)
-        add("lm_head", lib.gq_linear_softcap, ctx, V(self.x), B, H, Q("lm_head"), c_float(c.lm_softcap),
-            V(self.logits), c.vocab, 0)
+        if self.peer is None:
+            add("lm_head", lib.gq_linear_softcap, ctx, V(self.x), B, H, Q("lm_head"), c_float(c.lm_softcap),
+                V(self.logits), c.vocab, 0)
+        else:  # this rank's vocab rows, stored into every rank's logits buffer `par` (set per step)
+            self._lm_calls = [self.peer.device_calls(self.x.data_ptr(), B, H, par) for par in (0, 1)]
         return calls
 
     def run(self) -> None:
         """Enqueue one step (no host synchronisation)."""
-        for label, fn, args in self._calls:
+        calls = self._calls
+        if self.peer is not None:
+            calls = calls + self._lm_calls[self._par]
+            self.logits = self.peer.logits[self._par][: self.batch]
+            self._par ^= 1
+        for label, fn, args in calls:
             rc = fn(*args)
             if rc != 0:
                 self.g._check(rc, label)
@@ -419,11 +456,27 @@ class Decoder:
         return out
 
     def record(self):
-        """Capture one step into a graph (the backend must own its stream; run once first)."""
-        return self.g.record(self.run)
+        """Capture one step into a graph (the backend must own its stream; run once
+        first). With a sharded lm_head the graph holds two steps, one per logits
+        buffer, and ``logits`` is the second one's."""
+        if self.peer is None:
+            return self.g.record(self.run)
+        self._par = 0
+
+        def two():
+            self.run()
+            self.run()
+        return self.g.record(two)
+
+    @property
+    def steps_per_graph(self) -> int:
+        return 1 if self.peer is None else 2
 
     def close(self) -> None:
         """Free the decoder's quantized weights (device memory of the rest is torch's)."""
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
         for t in self.w.values():
             if getattr(t, "qw", None) is not None:
                 self.g.free_quant(t)
@@ -433,7 +486,7 @@ class Decoder:
 
     @property
     def launches(self) -> int:
-        return len(self._calls)
+        return len(self._calls) + (2 if self.peer is not None else 0)
 
     def labels(self) -> List[str]:
         return [c[0] for c in self._calls]

@@ -207,6 +207,21 @@ class PeerLmHead:
                 self.dist.all_reduce(self.flag, group=self.group)
         return self.logits[par][:m]
 
+    def device_calls(self, x_ptr: int, m: int, k: int, par: int):
+        """The two C-ABI calls of one device-barrier forward into buffer `par` (0 or 1),
+        with their arguments bound, as (label, fn, args) for a caller's launch list
+        (a captured graph replays them with fresh epochs); the logits are then
+        ``self.logits[par][:m]``."""
+        from ctypes import c_float, c_void_p
+
+        lib, ctx = self.g.lib, self.g.ctx
+        y = self.buf + par * self.buf_floats * 4
+        return [("lm_head_shard", lib.gq_linear_softcap_peers_signal,
+                 (ctx, c_void_p(x_ptr), m, k, c_void_p(self.w.qw), c_float(self.cap), c_void_p(y), self.vocab,
+                  self.r0, self.peer_arr[par], len(self.peers), self.flag_arr, c_void_p(self.sync), self.rank)),
+                ("lm_head_wait", lib.gq_peer_wait,
+                 (ctx, c_void_p(self.buf + self.flag_off), self.world, c_void_p(self.sync)))]
+
     def close(self) -> None:
         """Unmap the peers' buffers and free this rank's (after every rank stopped writing)."""
         from ctypes import c_void_p

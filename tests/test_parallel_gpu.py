@@ -111,3 +111,71 @@ def test_sharded_lm_head_two_gpus_both_exchanges():
         for m, (rel, same_as_nccl, repeatable) in res.items():
             assert rel <= 1e-5, (rank, m, rel)
             assert same_as_nccl and repeatable, (rank, m)
+
+
+def _decoder_worker(rank, world, port, q):
+    """The decode step with its lm_head sharded over the ranks (fused exchange,
+    device barrier) against the same step with the whole lm_head on one GPU."""
+    from datetime import timedelta
+
+    import torch
+    import torch.distributed as dist
+
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        torch.cuda.set_device(rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                                device_id=torch.device("cuda", rank))
+        from gq import CudaBackend, e2b
+
+        c = e2b.small_config(2000)
+        w = e2b.Weights(c, 21)
+        ids = [5, 1999, 777]
+        g = CudaBackend(rank, own_stream=True)
+        full = e2b.Decoder(g, c, w, batch=3, cache_len=20, capacity=24)
+        full.set_ids(ids)
+        full.run()
+        g.flush()
+        want = full.read(full.logits)
+        full.close()
+        dec = e2b.Decoder(g, c, w, batch=3, cache_len=20, capacity=24, lm_shard=(rank, world, None))
+        dec.set_ids(ids)
+        dec.run()
+        g.flush()
+        eager = dec.read(dec.logits)
+        graph = dec.record()  # two steps, one per logits buffer
+        outs = []
+        for _ in range(2):
+            g.replay(graph)
+            g.flush()
+            outs.append(dec.read(dec.logits))
+        g.destroy_graph(graph)
+        dec.close()
+        g.close()
+        rel = float(np.linalg.norm(eager.astype(np.float64) - want) / np.linalg.norm(want))
+        same = all(np.array_equal(o, eager) for o in outs)
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, (rel, same, dec.steps_per_graph)))
+    except Exception as e:  # report instead of hanging the parent
+        q.put((rank, repr(e)))
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="needs two GPUs")
+def test_decode_step_with_sharded_lm_head_two_gpus():
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_decoder_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    out = dict(q.get(timeout=600) for _ in ps)
+    for p in ps:
+        p.join(timeout=120)
+    for rank, res in out.items():
+        assert isinstance(res, tuple), f"rank {rank}: {res}"
+        rel, same, spg = res
+        assert rel <= 1e-5, (rank, rel)
+        assert same and spg == 2, rank
