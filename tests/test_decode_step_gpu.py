@@ -284,6 +284,20 @@ def test_decode_step_small_batched(g):
         assert np.array_equal(kg[:, :40], K[:, :40])
 
 
+@pytest.mark.parametrize("batch", [1, 6])
+def test_decode_step_4bit_attention_projections(g, batch):
+    """The real checkpoint stores the attention projections at 4 bits (the BASELINE
+    configs use I8): the same step with 4-bit q|k|v / o projections, CUDA-core
+    (M = 1) and short-M tensor-core (M = 6) GEMVs, against the oracle."""
+    import dataclasses
+
+    cfg = dataclasses.replace(e2b.small_config(4096), attn_bits=4)
+    w = e2b.Weights(cfg, 9)
+    ids = [3, 4000, 77, 1024, 9, 2048][:batch]
+    _, got, want, _ = run_step(g, cfg, w, batch, 30, ids, capacity=40)
+    check_logits(got, want)
+
+
 def test_decode_step_graph_replay_matches_eager():
     g = CudaBackend(0, own_stream=True)
     try:

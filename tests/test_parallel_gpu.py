@@ -150,13 +150,14 @@ def _decoder_worker(rank, world, port, q):
             g.flush()
             outs.append(dec.read(dec.logits))
         g.destroy_graph(graph)
+        spg = dec.steps_per_graph
         dec.close()
         g.close()
         rel = float(np.linalg.norm(eager.astype(np.float64) - want) / np.linalg.norm(want))
         same = all(np.array_equal(o, eager) for o in outs)
         dist.barrier()
         dist.destroy_process_group()
-        q.put((rank, (rel, same, dec.steps_per_graph)))
+        q.put((rank, (rel, same, spg)))
     except Exception as e:  # report instead of hanging the parent
         q.put((rank, repr(e)))
 
