@@ -546,6 +546,8 @@ def sharded_lm_head(torch, dist, rank, world, local, args):
             g3.replay(gr)
         g3.flush()
         dist.barrier()
+        with torch.cuda.stream(st3):  # the GPUs start the timed replays together
+            dist.all_reduce(torch.zeros(1, device=g3.torch_device))
         reps_g = max(5, min(args.steps, 50))
         msg = cuda_events_time(torch, st3, lambda: g3.replay(gr), reps_g) / (reps_g * per_graph)
         g3.flush()
@@ -741,7 +743,7 @@ def decode_sharded(torch, dist, rank, world, local, args, batches=(1, 64)):
     cfg = e2b.e2b_config()
     g = CudaBackend(local, own_stream=True)
     st = torch.cuda.ExternalStream(g.stream_ptr(), device=g.torch_device)
-    reps = max(10, min(args.steps, 50))
+    reps = max(20, min(args.steps, 50))
     out = {}
     for b in batches:
         res = {}
@@ -756,6 +758,11 @@ def decode_sharded(torch, dist, rank, world, local, args, batches=(1, 64)):
                 g.replay(graph)
             g.flush()
             dist.barrier()
+            # line the GPUs up on the timed stream itself: the host-side barrier leaves
+            # the ranks' first replays up to ~1 ms apart, which the per-step exchange
+            # would charge to every step
+            with torch.cuda.stream(st):
+                dist.all_reduce(torch.zeros(1, device=g.torch_device))
             ms = cuda_events_time(torch, st, lambda: g.replay(graph), reps) / (reps * dec.steps_per_graph)
             g.flush()
             t = torch.tensor([ms], device=g.torch_device)
