@@ -751,6 +751,8 @@ def decode_sharded(torch, dist, rank, world, local, args, batches=(1, 64)):
             dec = e2b.Decoder(g, cfg, None, batch=b, cache_len=2047, capacity=2048, device_init_seed=77 + b,
                               lm_shard=shard)
             dec.set_ids(np.arange(b) * 4099 % cfg.vocab)
+            g.flush()
+            dist.barrier()  # weight set-up time differs per rank; the step's exchange waits are bounded (2 s)
             dec.run()
             g.flush()
             graph = dec.record()

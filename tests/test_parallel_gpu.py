@@ -140,6 +140,8 @@ def _decoder_worker(rank, world, port, q):
         full.close()
         dec = e2b.Decoder(g, c, w, batch=3, cache_len=20, capacity=24, lm_shard=(rank, world, None))
         dec.set_ids(ids)
+        g.flush()
+        dist.barrier()  # the step's exchange waits are bounded: start the ranks together
         dec.run()
         g.flush()
         eager = dec.read(dec.logits)
