@@ -353,7 +353,7 @@ def run_gq(args):
     ms_e2e = float(t.item())
 
     # Roofline of the dominant kernel family: the per-layer MATMUL_Q launches
-    # (CUDA-core gemv_q_kernel, ~90% of the step's device time), recorded as a
+    # (CUDA-core gemv_q_kernel, ~95% of the step's device time), recorded as a
     # graph of their own and replayed back to back exactly as inside the step;
     # CUDA events on the context stream bracket the replays.
     graph_l = g.record(step.run_layers)
