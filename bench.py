@@ -433,7 +433,10 @@ def run_gq(args):
 
     if world > 1:
         line["lm_head_sharded"] = sharded_lm_head(torch, dist, rank, world, local, args)
-        line["decode_sharded_lm_head"] = decode_sharded(torch, dist, rank, world, local, args)
+        try:  # a failure of this leg (on every rank alike) keeps the rest of the line
+            line["decode_sharded_lm_head"] = decode_sharded(torch, dist, rank, world, local, args)
+        except Exception as e:  # noqa: BLE001
+            line["decode_sharded_lm_head"] = {"error": repr(e)[:300]}
     if rank == 0 and world == 1 and not args.no_extras:
         line["extras"] = extras(g, torch, stream, hbm_peak, bf16_peak)
         line["config5_decode"] = config5(g, torch, stream, hbm_peak)
