@@ -436,6 +436,58 @@ __global__ void __launch_bounds__(kNormThreads) qkv_norm_rope_kernel(const QkvAr
   for (int64_t i = 2 * a.half + lane; i < a.dh; i += 32) yr[i] = b[i];
 }
 
+// ---- row argmax (greedy decoding over a vocab shard) ----------------------------
+// Per row: the largest value and the first column holding it, with NaN above
+// every number (numpy.argmax semantics) and -0 equal to +0. Each block folds a
+// column range to one 64-bit key, (order-preserving value bits << 32) | ~column,
+// so the atomic max over keys keeps the largest value and, among equal values,
+// the smallest column.
+__device__ __forceinline__ uint32_t argmax_order(float v) {
+  if (v != v) return 0xFFFFFFFFu;  // NaN
+  uint32_t u = __float_as_uint(v == 0.0f ? 0.0f : v);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+constexpr int kArgThreads = 256;
+
+__global__ void __launch_bounds__(kArgThreads) argmax_rows_kernel(const float *x, int64_t n, int64_t ldx, int cols_per_block,
+                                                                  unsigned long long *keys) {
+  gqd::griddep_wait();
+  gqd::griddep_launch_dependents();
+  const int64_t row = blockIdx.y;
+  const int64_t c0 = (int64_t)blockIdx.x * cols_per_block;
+  const int64_t c1 = min(n, c0 + cols_per_block);
+  const float *xr = x + row * ldx;
+  unsigned long long best = 0ull;
+  for (int64_t c = c0 + threadIdx.x; c < c1; c += kArgThreads) {  // ascending per thread
+    const unsigned long long k = ((unsigned long long)argmax_order(xr[c]) << 32) | (uint32_t)(0xFFFFFFFFu - (uint32_t)c);
+    best = k > best ? k : best;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+    best = other > best ? other : best;
+  }
+  __shared__ unsigned long long wbest[kArgThreads / 32];
+  if ((threadIdx.x & 31) == 0) wbest[threadIdx.x >> 5] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < kArgThreads / 32; ++w) best = wbest[w] > best ? wbest[w] : best;
+    atomicMax(keys + row, best);
+  }
+}
+
+__global__ void argmax_finish_kernel(const float *x, int64_t m, int64_t ldx, int64_t idx_base,
+                                     const unsigned long long *keys, float *val, int64_t *idx) {
+  gqd::griddep_wait();
+  gqd::griddep_launch_dependents();
+  const int64_t row = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (row >= m) return;
+  const int64_t c = (int64_t)(0xFFFFFFFFu - (uint32_t)(keys[row] & 0xFFFFFFFFull));
+  val[row] = x[row * ldx + c];
+  idx[row] = idx_base + c;
+}
+
 // ---- attention --------------------------------------------------------------
 
 struct AttnArgs {
@@ -1301,6 +1353,30 @@ int gq_qkv_norm_rope(gq_ctx *ctx, const float *qkv, int64_t t, int64_t qkv_tok_s
                 : vpl == 2 ? gq_launch(ctx, qkv_norm_rope_kernel<2>, grid, blk, 0, a, fr)
                            : gq_launch(ctx, qkv_norm_rope_kernel<4>, grid, blk, 0, a, fr);
   GQ_CUDA_TRY(ctx, e);
+  return GQ_OK;
+}
+
+int gq_argmax_rows(gq_ctx *ctx, const float *x, int64_t m, int64_t n, int64_t ldx, int64_t idx_base, float *val,
+                   int64_t *idx) {
+  ENTER(ctx);
+  if (m < 0 || n <= 0 || n > 0xFFFFFFFFll || (m > 0 && (!x || !val || !idx)))
+    return gq_fail(ctx, GQ_ERR_INVALID_ARGUMENT, "argmax_rows: bad shape or null pointer");
+  if (ldx == 0) ldx = n;
+  if (ldx < n) return gq_fail(ctx, GQ_ERR_INVALID_ARGUMENT, "argmax_rows: ldx < n");
+  if (m == 0) return GQ_OK;
+  void *ws = nullptr;
+  int rc = gq_workspace(ctx, (size_t)m * 8, &ws);
+  if (rc != GQ_OK) return rc;
+  unsigned long long *keys = static_cast<unsigned long long *>(ws);
+  GQ_CUDA_TRY(ctx, cudaMemsetAsync(keys, 0, (size_t)m * 8, ctx->stream));
+  // about two blocks per SM in all, at least 4096 columns per block
+  int64_t blocks = std::max<int64_t>(1, (2 * (int64_t)ctx->num_sms + m - 1) / m);
+  int64_t per = std::max<int64_t>(4096, (n + blocks - 1) / blocks);
+  blocks = (n + per - 1) / per;
+  GQ_CUDA_TRY(ctx, gq_launch(ctx, argmax_rows_kernel, dim3((unsigned)blocks, (unsigned)m), dim3(kArgThreads), 0, x, n,
+                             ldx, (int)per, keys));
+  GQ_CUDA_TRY(ctx, gq_launch(ctx, argmax_finish_kernel, dim3((unsigned)((m + 127) / 128)), dim3(128), 0, x, m, ldx,
+                             idx_base, (const unsigned long long *)keys, val, idx));
   return GQ_OK;
 }
 

@@ -79,6 +79,7 @@ SIGNATURES = {
         c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_float, c_void_p, c_int64, c_int64, c_void_p,
                 c_int32, c_void_p, c_void_p, c_int32]),
     "gq_peer_wait": (c_int, [c_void_p, c_void_p, c_int32, c_void_p]),
+    "gq_argmax_rows": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p]),
     "gq_ipc_get_handle": (c_int, [c_void_p, c_void_p, c_void_p]),
     "gq_ipc_open": (c_int, [c_void_p, c_void_p, POINTER(c_void_p)]),
     "gq_ipc_close": (c_int, [c_void_p, c_void_p]),

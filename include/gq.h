@@ -174,6 +174,18 @@ int gq_linear_softcap_peers_signal(gq_ctx *ctx, const float *x, int64_t m, int64
  * gq_sync) and returns. */
 int gq_peer_wait(gq_ctx *ctx, const uint32_t *flags, int32_t world, const uint32_t *sync);
 
+/* Greedy decoding over a vocab shard: for each of the m rows of x (row stride
+ * ldx floats, 0 = n) the largest of its n values and the first column holding it
+ * (NaN ranks above every number, -0 equals +0: numpy.argmax), written as val[row]
+ * and idx[row] = idx_base + column. With idx_base = the shard's first vocab row,
+ * the best of the ranks' (val, idx) pairs (ties to the smaller index) is the
+ * argmax of the full logits, so a vocab-sharded lm_head exchanges m pairs per
+ * rank instead of its logits. Uses the context workspace (m * 8 bytes). No
+ * counterpart in the reference (its sampler reads the whole logits row,
+ * rust/src/sampler.rs). */
+int gq_argmax_rows(gq_ctx *ctx, const float *x, int64_t m, int64_t n, int64_t ldx, int64_t idx_base, float *val,
+                   int64_t *idx);
+
 /* CUDA IPC for the peer buffers above: the 64-byte handle of a gq_alloc'd device
  * buffer, the mapping of a peer's handle into this context's device (peer access
  * enabled), and its release. */

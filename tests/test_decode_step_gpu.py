@@ -298,6 +298,32 @@ def test_decode_step_4bit_attention_projections(g, batch):
     check_logits(got, want)
 
 
+@pytest.mark.parametrize("m,n,ldx,base", [(1, 131072, 0, 131072), (5, 7, 9, 0), (64, 32768, 32768, 229376),
+                                           (3, 1, 0, 5), (2, 262144, 0, 0)])
+def test_argmax_rows_is_numpy_argmax(g, m, n, ldx, base):
+    """gq_argmax_rows against numpy.argmax, bit-exact in value and index, with
+    planted ties (first index wins), a NaN row and a row of signed zeros."""
+    import torch
+
+    rng = np.random.default_rng(n + m)
+    ld = ldx or n
+    x = (rng.integers(-50, 50, (m, ld)) / 8.0).astype(np.float32)  # many exact ties
+    if m >= 3:
+        x[1, [n // 3, n - 1]] = np.nan
+        x[2, :n] = -0.0
+        x[2, (2 * n) // 3] = 0.0
+    gx = g.tensor(x, x.shape)
+    val = torch.empty(m, device=g.torch_device)
+    idx = torch.empty(m, dtype=torch.int64, device=g.torch_device)
+    g._check(g.lib.gq_argmax_rows(g.ctx, c_void_p(gx.ptr()), m, n, ldx, base, c_void_p(val.data_ptr()),
+                                  c_void_p(idx.data_ptr())), "argmax_rows")
+    g.flush()
+    want = np.argmax(x[:, :n], axis=1)
+    assert np.array_equal(idx.cpu().numpy(), want + base)
+    got_v, want_v = val.cpu().numpy(), x[np.arange(m), want]
+    assert np.array_equal(got_v, want_v, equal_nan=True)
+
+
 def test_decode_step_graph_replay_matches_eager():
     g = CudaBackend(0, own_stream=True)
     try:

@@ -182,3 +182,55 @@ def test_decode_step_with_sharded_lm_head_two_gpus():
         rel, same, spg = res
         assert rel <= 1e-5, (rank, rel)
         assert same and spg == 2, rank
+
+
+def _greedy_worker(rank, world, port, q):
+    from datetime import timedelta
+
+    import torch
+    import torch.distributed as dist
+
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        torch.cuda.set_device(rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                                device_id=torch.device("cuda", rank))
+        from gq import CudaBackend, synth
+        from gq.parallel import ShardedGreedy, shard_rows, slice_rows
+        from oracle import oracle
+
+        full = synth.random_qweight(4200, V, K, 8, True)
+        r0, r1 = shard_rows(V, world, rank)
+        g = CudaBackend(rank)
+        sg = ShardedGreedy(g, slice_rows(full, r0, r1), V, rank, world, max_m=5, cap=CAP)
+        x = synth.normal(4201, 5 * K).reshape(5, K).astype(np.float32)
+        _, idx = sg.forward(g.tensor(x, x.shape))
+        ref = oracle.softcap(oracle.linear(x, full), CAP).reshape(5, V)
+        g.close()
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, (idx.tolist(), np.argmax(ref, axis=1).tolist())))
+    except Exception as e:  # report instead of hanging the parent
+        q.put((rank, repr(e)))
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="needs two GPUs")
+def test_sharded_greedy_two_gpus():
+    """Greedy decoding with the vocab split over 2 GPUs: each shard's (max, first
+    index) on the GPU, pairs all-gathered, merged: the token ids of the oracle's
+    argmax over the full logits (the GEMV is within 1e-5 of the oracle, so this
+    holds unless a row's two largest logits lie within that rounding)."""
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_greedy_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    out = dict(q.get(timeout=600) for _ in ps)
+    for p in ps:
+        p.join(timeout=120)
+    for rank, res in out.items():
+        assert isinstance(res, tuple), f"rank {rank}: {res}"
+        assert res[0] == res[1], rank
