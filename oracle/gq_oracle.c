@@ -282,7 +282,7 @@ int32_t gqo_linear_gelu_mul_cols(const float *x, int64_t t, int64_t k, const gqo
   return rc;
 }
 
-/* ---- support ops of the decode step (SURVEY (a')) ----------------------- */
+/* ---- support ops of the decode step (norms, rope, attention, elementwise) --- */
 
 /* rust/src/backend_cpu.rs:149-172: y = x / sqrt(mean(x^2) + eps) * w per row of
  * d values (w NULL: unweighted). Sequential f32 sum of squares. */
