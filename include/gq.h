@@ -4,9 +4,10 @@
  * This is the drop-in boundary for the quantized-weight hot path of the Gemma-4
  * engine in Dhruba531/gemma-4-webgpu-kernels. Each entry point replaces one
  * method of the Rust `Backend` trait (rust/src/backend.rs:88-180) for quantized
- * tensors; a Rust `CudaBackend` binds these symbols through `extern "C"` (see
- * INTEGRATION.md) and maps a non-zero status to `panic!`, which is what the
- * trait's infallible signatures do today.
+ * tensors; a Rust `CudaBackend` binds these symbols through `extern "C"` (an
+ * `extern "C"` block mirroring the declarations below, built by build.rs) and
+ * maps a non-zero status to `panic!`, which is what the trait's infallible
+ * signatures do today.
  *
  * Conventions
  *  - Every function returns an int status (GQ_OK == 0). Nothing aborts or traps.
