@@ -77,3 +77,11 @@ def test_no_gpu_context_create_fails_cleanly():
     ctx = ctypes.c_void_p()
     assert lib.gq_ctx_create(0, ctypes.byref(ctx)) != _abi.GQ_OK
     assert not ctx.value
+
+
+def test_integration_binding_declares_every_entry_point():
+    """The Rust extern block a maintainer copies into the engine (the integration
+    notes) names every entry point of the header."""
+    text = open(os.path.join(ROOT, "INTEGRATION.md")).read()
+    ffi = set(re.findall(r"pub fn (gq_\w+)\(", text))
+    assert set(declared(HEADER, "gq_")) <= ffi, sorted(set(declared(HEADER, "gq_")) - ffi)
