@@ -191,6 +191,12 @@ void *gq_ctx_get_stream(gq_ctx *ctx) { return ctx ? static_cast<void *>(ctx->str
 
 int gq_ctx_num_sms(gq_ctx *ctx) { return ctx ? ctx->num_sms : 0; }
 
+int gq_ctx_set_wait_limit(gq_ctx *ctx, uint64_t limit_ns) {
+  if (!ctx || limit_ns < 1000000ull || limit_ns > 60000000000ull) return GQ_ERR_INVALID_ARGUMENT;
+  ctx->wait_limit_ns = limit_ns;
+  return GQ_OK;
+}
+
 const char *gq_last_error(gq_ctx *ctx) { return ctx ? ctx->last_error.c_str() : "null context"; }
 
 int gq_sync(gq_ctx *ctx) {
@@ -493,7 +499,8 @@ namespace {
 // epoch sync[1] (written by the signalling GEMV before this kernel in stream
 // order); acquire, system scope. A peer one call ahead holds epoch + 1, so the
 // test is a wrap-safe >=. On timeout it reports GQ_DEVERR_WAIT_TIMEOUT and returns.
-__global__ void peer_wait_kernel(const uint32_t *flags, int world, const uint32_t *sync, uint32_t *err) {
+__global__ void peer_wait_kernel(const uint32_t *flags, int world, const uint32_t *sync, uint64_t limit_ns,
+                                 uint32_t *err) {
   gqd::griddep_wait();
   if (threadIdx.x != 0) return;
   const uint32_t epoch = *reinterpret_cast<const volatile uint32_t *>(sync + 1);
@@ -503,7 +510,7 @@ __global__ void peer_wait_kernel(const uint32_t *flags, int world, const uint32_
       uint32_t v;
       asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flags + r) : "memory");
       if ((int32_t)(v - epoch) >= 0) break;
-      if ((it & 255u) == 255u && gqd::globaltimer_ns() - t0 > 2000000000ull) {
+      if ((it & 255u) == 255u && gqd::globaltimer_ns() - t0 > limit_ns) {
         gqd::report(err, GQ_DEVERR_WAIT_TIMEOUT);
         return;
       }
@@ -518,7 +525,8 @@ int gq_peer_wait(gq_ctx *ctx, const uint32_t *flags, int32_t world, const uint32
   GQ_ENTER(ctx);
   if (!flags || !sync || world < 1 || world > kMaxPeerDst + 1)
     return gq_fail(ctx, GQ_ERR_INVALID_ARGUMENT, "peer_wait: flags, sync word, 1..9 ranks");
-  GQ_CUDA_TRY(ctx, gq_launch(ctx, peer_wait_kernel, dim3(1), dim3(32), 0, flags, (int)world, sync, ctx->dev_err));
+  GQ_CUDA_TRY(ctx, gq_launch(ctx, peer_wait_kernel, dim3(1), dim3(32), 0, flags, (int)world, sync, ctx->wait_limit_ns,
+                             ctx->dev_err));
   return GQ_OK;
 }
 

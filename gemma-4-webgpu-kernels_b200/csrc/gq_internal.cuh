@@ -36,6 +36,7 @@ struct gq_ctx {
   cudaStream_t stream = nullptr;
   uint32_t *dev_err = nullptr; // device status word (GQ_DEVERR_*)
   bool pdl = true;             // launch with programmatic stream serialization
+  uint64_t wait_limit_ns = 2000000000ull;  // bound of the cross-GPU waits (gq_peer_wait)
   std::string last_error;
   // temporaries of the composed fallbacks (generic kernel + elementwise epilogue)
   float *scratch[2] = {nullptr, nullptr};

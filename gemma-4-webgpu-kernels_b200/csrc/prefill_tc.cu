@@ -41,6 +41,8 @@
 #include <cudaTypedefs.h>
 
 #include <algorithm>
+#include <atomic>
+#include <mutex>
 #include <type_traits>
 
 #include "tc_common.cuh"
@@ -576,6 +578,7 @@ size_t smem_for(int bits) {
 bool gq_prefill_supported(gq_ctx *ctx, const gq_qweight *w, int64_t m) {
   if (m < 16 || w->group_size != w->k || w->k % BK != 0 || w->k <= 0 || w->n <= 0) return false;
   if (m > (1ll << 30) || w->n > (1ll << 30) || w->k > (1 << 24)) return false;
+  if ((w->n + MW / 2 - 1) / (MW / 2) > 65535) return false;  // grid.y = weight tiles (GeGLU: MW/2 rows)
   if ((uintptr_t)w->bytes % 16 != 0) return false;  // the packed tiles come in by TMA
   return smem_for(w->bits) <= ctx->smem_optin && encode_fn() != nullptr;
 }
@@ -634,31 +637,51 @@ int gq_prefill_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq
 namespace {
 constexpr int64_t kStaticScratchElems = int64_t(4) << 20;  // 4 Mi f16 (8 MiB): M*K <= 4,194,304
 constexpr int64_t kStaticRows = kStaticScratchElems / BK;   // K >= 64, so M <= 65,536
+constexpr int64_t kStaticMaxN = int64_t(65535) * MW;        // grid.y = N / 128 weight tiles
 static __device__ __align__(256) __half g_prefill_scratch[kStaticScratchElems];
 static __device__ __align__(256) int g_prefill_xexp[kStaticRows];
+// GQ_DEVERR_* bits of the calls on this device (a bounded wait that gave up),
+// read and cleared by gq_linear_prefill_static_status.
+static __device__ __align__(16) uint32_t g_prefill_status;
 
 // Host-side device addresses of the arrays, one per device. Host code must not
 // pass the symbols themselves to a kernel: in host code they name host-side
-// stand-ins, not device memory.
+// stand-ins, not device memory. The look-up runs once per device under a lock
+// (two host threads making their first call on one device do not race on it);
+// `ready` is published with release order and read with acquire order.
 struct StaticSetup {
   void *scratch = nullptr;
   void *xexp = nullptr;
+  uint32_t *status = nullptr;
   int smem_optin = 0;
-  bool ready = false;
+  std::atomic<bool> ready{false};
 };
 StaticSetup g_static_setup[64];
+std::mutex g_static_mu;
 
 cudaError_t static_setup(int dev, StaticSetup **out) {
-  StaticSetup &st = g_static_setup[dev & 63];
-  if (!st.ready) {
-    cudaError_t e = cudaGetSymbolAddress(&st.scratch, g_prefill_scratch);
-    if (e != cudaSuccess) return e;
-    e = cudaGetSymbolAddress(&st.xexp, g_prefill_xexp);
-    if (e != cudaSuccess) return e;
-    if (st.scratch == nullptr || st.xexp == nullptr) return cudaErrorInvalidSymbol;
-    e = cudaDeviceGetAttribute(&st.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-    if (e != cudaSuccess) return e;
-    st.ready = true;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  StaticSetup &st = g_static_setup[dev];
+  if (!st.ready.load(std::memory_order_acquire)) {
+    std::lock_guard<std::mutex> lock(g_static_mu);
+    if (!st.ready.load(std::memory_order_relaxed)) {
+      void *scratch = nullptr, *xexp = nullptr, *status = nullptr;
+      cudaError_t e = cudaGetSymbolAddress(&scratch, g_prefill_scratch);
+      if (e != cudaSuccess) return e;
+      e = cudaGetSymbolAddress(&xexp, g_prefill_xexp);
+      if (e != cudaSuccess) return e;
+      e = cudaGetSymbolAddress(&status, g_prefill_status);
+      if (e != cudaSuccess) return e;
+      if (scratch == nullptr || xexp == nullptr || status == nullptr) return cudaErrorInvalidSymbol;
+      int optin = 0;
+      e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+      if (e != cudaSuccess) return e;
+      st.scratch = scratch;
+      st.xexp = xexp;
+      st.status = static_cast<uint32_t *>(status);
+      st.smem_optin = optin;
+      st.ready.store(true, std::memory_order_release);
+    }
   }
   *out = &st;
   return cudaSuccess;
@@ -688,7 +711,7 @@ extern "C" int gq_linear_prefill_static(void *cuda_stream, const float *x, int64
   if (signed_i8 ? bits != 8 : (bits != 2 && bits != 4 && bits != 8)) return GQ_ERR_UNSUPPORTED;
   if (k % BK != 0) return GQ_ERR_UNSUPPORTED;
   if (m > kStaticScratchElems / k) return GQ_ERR_INVALID_ARGUMENT;  // M*K beyond the static scratch
-  if (n > (int64_t(1) << 30)) return GQ_ERR_UNSUPPORTED;
+  if (n > kStaticMaxN) return GQ_ERR_UNSUPPORTED;  // more weight tiles than a grid dimension holds
   if ((uintptr_t)x % 16 != 0 || (uintptr_t)qbytes % 16 != 0 || (uintptr_t)scales % 4 != 0)
     return GQ_ERR_INVALID_ARGUMENT;
   int dev = 0;
@@ -713,7 +736,7 @@ extern "C" int gq_linear_prefill_static(void *cuda_stream, const float *x, int64
   a.y = y;
   a.ldy = n;
   a.y_col0 = 0;
-  a.err = nullptr;  // no context: a timed-out wait is still bounded, but not reported
+  a.err = st->status;  // a timed-out wait: gq_linear_prefill_static_status reports it
   const dim3 grid((unsigned)((m + nt - 1) / nt), (unsigned)((n + MW - 1) / MW));
   CUtensorMap mw;
   if (encode_weight_map(&mw, qbytes, n, signed_i8 ? k : k * bits / 8, bits, MW) != CUDA_SUCCESS) return GQ_ERR_CUDA;
@@ -723,4 +746,20 @@ extern "C" int gq_linear_prefill_static(void *cuda_stream, const float *x, int64
   else if (signed_i8) e = static_launch<8, true>(stream, map, mw, a, grid);
   else e = static_launch<8, false>(stream, map, mw, a, grid);
   return e == cudaSuccess ? GQ_OK : GQ_ERR_CUDA;
+}
+
+extern "C" int gq_linear_prefill_static_status(void *cuda_stream, uint32_t *status_bits) {
+  if (!status_bits) return GQ_ERR_INVALID_ARGUMENT;
+  *status_bits = 0;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return GQ_ERR_CUDA;
+  StaticSetup *st = nullptr;
+  if (static_setup(dev, &st) != cudaSuccess) return GQ_ERR_CUDA;
+  cudaStream_t stream = static_cast<cudaStream_t>(cuda_stream);
+  if (cudaStreamSynchronize(stream) != cudaSuccess) return GQ_ERR_CUDA;
+  uint32_t bits = 0;
+  if (cudaMemcpy(&bits, st->status, sizeof(bits), cudaMemcpyDeviceToHost) != cudaSuccess) return GQ_ERR_CUDA;
+  if (bits != 0 && cudaMemset(st->status, 0, sizeof(uint32_t)) != cudaSuccess) return GQ_ERR_CUDA;
+  *status_bits = bits;
+  return bits ? GQ_ERR_DEVICE : GQ_OK;
 }

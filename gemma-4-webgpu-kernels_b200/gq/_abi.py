@@ -7,7 +7,7 @@ from __future__ import annotations
 
 import ctypes
 import os
-from ctypes import POINTER, c_char_p, c_float, c_int, c_int32, c_int64, c_size_t, c_uint8, c_uint32, c_void_p
+from ctypes import POINTER, c_char_p, c_float, c_int, c_int32, c_int64, c_size_t, c_uint8, c_uint32, c_uint64, c_void_p
 
 LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libgq.so")
 
@@ -79,6 +79,7 @@ SIGNATURES = {
         c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_float, c_void_p, c_int64, c_int64, c_void_p,
                 c_int32, c_void_p, c_void_p, c_int32]),
     "gq_peer_wait": (c_int, [c_void_p, c_void_p, c_int32, c_void_p]),
+    "gq_ctx_set_wait_limit": (c_int, [c_void_p, c_uint64]),
     "gq_argmax_rows": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p]),
     "gq_ipc_get_handle": (c_int, [c_void_p, c_void_p, c_void_p]),
     "gq_ipc_open": (c_int, [c_void_p, c_void_p, POINTER(c_void_p)]),
@@ -86,6 +87,7 @@ SIGNATURES = {
     "gq_embed_rows": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_float, c_void_p]),
     "gq_linear_prefill_static": (
         c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int32, c_int32, c_void_p]),
+    "gq_linear_prefill_static_status": (c_int, [c_void_p, POINTER(c_uint32)]),
     "gq_softcap": (c_int, [c_void_p, c_void_p, c_int64, c_float, c_void_p]),
     "gq_geglu": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
     "gq_rms_norm": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_float, c_void_p, c_int64]),

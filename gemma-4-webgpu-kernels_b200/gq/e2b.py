@@ -193,10 +193,16 @@ class Decoder:
     device barrier): its GEMV stores its logits into every rank's buffer over
     NVLink, so every rank ends the step with the full logits. The trunk is
     replicated. Steps alternate between two logits buffers, so ``record`` then
-    captures two steps (one per buffer) and a replay runs both."""
+    captures two steps (one per buffer) and a replay runs both.
+
+    kv_device_seed: draw the cache prefix ~N(0,1) on the device from this seed even
+    when host weights are given (large batches: the host draw of a 64-sequence,
+    2047-token cache takes minutes); a checker reads it back from ``kcache`` /
+    ``vcache``."""
 
     def __init__(self, g, cfg: Config, weights: Optional[Weights], batch: int, cache_len: int,
-                 capacity: Optional[int] = None, device_init_seed: Optional[int] = None, lm_shard=None):
+                 capacity: Optional[int] = None, device_init_seed: Optional[int] = None, lm_shard=None,
+                 kv_device_seed: Optional[int] = None):
         import torch
 
         self.g, self.cfg, self.batch = g, cfg, batch
@@ -214,6 +220,10 @@ class Decoder:
         if weights is None:
             gen = torch.Generator(device=dev)
             gen.manual_seed(device_init_seed or 1)
+        kv_gen = gen
+        if kv_device_seed is not None:  # cache prefix drawn on the device even with host weights
+            kv_gen = torch.Generator(device=dev)
+            kv_gen.manual_seed(kv_device_seed)
 
         # ---- weights -------------------------------------------------------------
         self.meta: Dict[str, Tuple[int, int, int, int]] = {}  # name -> (n, k, bits, group)
@@ -325,13 +335,13 @@ class Decoder:
             kc = torch.zeros(batch, self.capacity, d, dtype=f32, device=dev)
             vc = torch.zeros(batch, self.capacity, d, dtype=f32, device=dev)
             if cache_len:
-                if weights is not None:
+                if weights is not None and kv_device_seed is None:
                     kk, vv = weights.kv_prefix(i, batch, cache_len)
                     kc[:, :cache_len] = torch.from_numpy(kk).to(dev)
                     vc[:, :cache_len] = torch.from_numpy(vv).to(dev)
                 else:
-                    kc[:, :cache_len].normal_(generator=gen)
-                    vc[:, :cache_len].normal_(generator=gen)
+                    kc[:, :cache_len].normal_(generator=kv_gen)
+                    vc[:, :cache_len].normal_(generator=kv_gen)
             self.kcache[i], self.vcache[i] = kc, vc
 
         # ---- activations and step inputs ------------------------------------------

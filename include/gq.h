@@ -170,10 +170,19 @@ int gq_linear_softcap_peers_signal(gq_ctx *ctx, const float *x, int64_t m, int64
                                    int32_t npeers, uint32_t *const *flags, uint32_t *sync, int32_t rank);
 
 /* Stream-ordered wait until flags[0 .. world) have all reached the epoch in
- * sync[1] (acquire, system scope). A wait that runs past 2 s sets
+ * sync[1] (acquire, system scope). A wait that runs past the context's wait
+ * limit (2 s unless gq_ctx_set_wait_limit changed it) sets
  * GQ_DEVERR_WAIT_TIMEOUT in the context's device error word (read by the next
- * gq_sync) and returns. */
+ * gq_sync) and returns; the context stays usable. */
 int gq_peer_wait(gq_ctx *ctx, const uint32_t *flags, int32_t world, const uint32_t *sync);
+
+/* Bound of the cross-GPU waits of this context (gq_peer_wait), in nanoseconds,
+ * 1 ms .. 60 s; applies to waits enqueued afterwards (a captured graph keeps the
+ * bound it was recorded with). The failure detector of a multi-GPU caller: a
+ * rank that dies or stalls makes its peers' waits end with
+ * GQ_DEVERR_WAIT_TIMEOUT after this long instead of hanging their GPUs. No
+ * counterpart in the reference (single device). */
+int gq_ctx_set_wait_limit(gq_ctx *ctx, uint64_t limit_ns);
 
 /* Greedy decoding over a vocab shard: for each of the m rows of x (row stride
  * ldx floats, 0 = n) the largest of its n values and the first column holding it
@@ -210,18 +219,31 @@ int gq_embed_rows(gq_ctx *ctx, const gq_qweight *table, const uint32_t *ids, int
  * after a power-of-two scaling per row (undone exactly), with the same
  * tensor-core kernel as gq_linear uses for m >= 128 (any m >= 1 is accepted).
  * Weights are caller device pointers in the upload layout: qbytes [n, row_bytes]
- * (16-byte aligned), one f32 scale per row. Requires k % 64 == 0 and
- * m * k <= 4,194,304: the f16 copy of x goes to a file-scope 8 MiB device array
- * (plus 256 KB of row exponents) that every GPU loading the library holds until
- * exit; larger sizes return
- * GQ_ERR_INVALID_ARGUMENT. Nothing is allocated. The first call on a device
- * looks up that array's device address (cudaGetSymbolAddress) and should come
- * before any stream capture. All calls share the array: calls that overlap on
- * the GPU (different streams, concurrent) race on it. Work is enqueued on
- * cuda_stream (NULL = legacy default stream) of the current device. */
+ * (16-byte aligned), one f32 scale per row. Requires k % 64 == 0,
+ * m * k <= 4,194,304 (GQ_ERR_INVALID_ARGUMENT beyond) and n <= 8,388,480
+ * (GQ_ERR_UNSUPPORTED beyond): the f16 copy of x goes to a file-scope 8 MiB device
+ * array (plus 256 KB of row exponents) that every GPU loading the library holds
+ * until exit. Nothing is allocated by the call.
+ * Set-up: the first call on a device looks up the arrays' device addresses
+ * (cudaGetSymbolAddress, once per device, thread-safe). Under CUDA's lazy module
+ * loading (the default) that first call is also when the arrays and the kernels
+ * are placed in device memory, so make it at start-up — a small valid call, e.g.
+ * m = 1 — before reserving the rest of HBM and before any stream capture, or run
+ * with CUDA_MODULE_LOADING=EAGER.
+ * All calls share the arrays and each leaves its scratch behind: calls that
+ * overlap on the GPU (different streams, concurrent) race on them. Work is
+ * enqueued on cuda_stream (NULL = legacy default stream) of the current device.
+ * A pipeline wait that gave up (bounded at 2 s) leaves y incomplete and sets
+ * GQ_DEVERR_WAIT_TIMEOUT in a device status word that
+ * gq_linear_prefill_static_status reports. */
 int gq_linear_prefill_static(void *cuda_stream, const float *x, int64_t m, int64_t k,
                              const uint8_t *qbytes, const float *scales, int64_t n, int32_t bits,
                              int32_t signed_i8, float *y);
+/* Status of the allocation-free calls on the current device: synchronises
+ * cuda_stream, stores the GQ_DEVERR_* bits raised since the last read in
+ * *status_bits, clears them, and returns GQ_ERR_DEVICE when any was set
+ * (GQ_OK otherwise). Allocates nothing. No counterpart in the reference. */
+int gq_linear_prefill_static_status(void *cuda_stream, uint32_t *status_bits);
 
 /* Backend::softcap / geglu / gelu_tanh (rust/src/backend.rs:112-116) on n
  * f32 elements. */

@@ -79,9 +79,54 @@ def test_no_gpu_context_create_fails_cleanly():
     assert not ctx.value
 
 
-def test_integration_binding_declares_every_entry_point():
-    """The Rust extern block a maintainer copies into the engine (the integration
-    notes) names every entry point of the header."""
-    text = open(os.path.join(ROOT, "INTEGRATION.md")).read()
-    ffi = set(re.findall(r"pub fn (gq_\w+)\(", text))
-    assert set(declared(HEADER, "gq_")) <= ffi, sorted(set(declared(HEADER, "gq_")) - ffi)
+RUST = os.path.join(ROOT, "gemma-4-webgpu-kernels_b200", "rust")
+
+
+def header_params(header: str, prefix: str = "gq_"):
+    """name -> number of parameters of every function the header declares."""
+    text = re.sub(r"/\*.*?\*/", "", open(header).read(), flags=re.S)
+    out = {}
+    for name, args in re.findall(r"\b(%s\w+)\s*\(([^)]*)\)\s*;" % prefix, text):
+        args = " ".join(args.split())
+        out[name] = 0 if args in ("", "void") else args.count(",") + 1
+    return out
+
+
+def rust_params(path: str):
+    """name -> number of parameters of every `pub fn gq_*` in a Rust extern block."""
+    text = re.sub(r"//[^\n]*", "", open(path).read())
+    out = {}
+    for name, args in re.findall(r"pub fn (gq_\w+)\(([^)]*)\)", text):
+        parts = [a for a in (x.strip() for x in args.split(",")) if a]
+        out[name] = len(parts)
+    return out
+
+
+def test_rust_binding_declares_every_entry_point():
+    """The Rust extern block a maintainer drops into the engine
+    (rust/src/backend_cuda/ffi.rs) declares every entry point of the header with
+    the same number of parameters."""
+    want = header_params(HEADER)
+    assert set(want) == set(declared(HEADER, "gq_"))
+    got = rust_params(os.path.join(RUST, "src", "backend_cuda", "ffi.rs"))
+    assert set(want) <= set(got), sorted(set(want) - set(got))
+    wrong = {n: (want[n], got[n]) for n in want if want[n] != got[n]}
+    assert not wrong, wrong
+
+
+def test_rust_backend_implements_the_trait_surface():
+    """rust/src/backend_cuda.rs implements every method of the reference's `trait
+    Backend` (rust/src/backend.rs:88-180, listed here) and calls only symbols
+    that ffi.rs declares; build.rs builds and links libgq."""
+    src = open(os.path.join(RUST, "src", "backend_cuda.rs")).read()
+    trait = ["name", "tensor", "quant_tensor", "zeros", "reshape", "embed_rows", "rms_norm", "linear", "add", "mul",
+             "scale", "scale_by_tensor", "gelu_tanh", "geglu", "softcap", "rope", "attention", "slice_rows",
+             "slice_cols", "concat_rows", "kv_append", "add_rms_norm", "head_norm_rope", "linear_geglu",
+             "linear_gelu_mul_cols", "readback", "flush", "end_frame", "free_tensor"]
+    impl = src[src.index("impl Backend for CudaBackend"):]
+    have = set(re.findall(r"\bfn (\w+)\(", impl))
+    assert set(trait) <= have, sorted(set(trait) - have)
+    called = set(re.findall(r"ffi::(gq_\w+)", src))
+    assert called <= set(rust_params(os.path.join(RUST, "src", "backend_cuda", "ffi.rs"))), called
+    build = open(os.path.join(RUST, "build.rs")).read()
+    assert "rustc-link-lib=dylib=gq" in build and '"make"' in build

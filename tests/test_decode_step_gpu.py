@@ -343,10 +343,62 @@ def test_decode_step_graph_replay_matches_eager():
         g.close()
 
 
+_E2B_WEIGHTS = {}
+
+
+def e2b_weights(seed: int = 123):
+    """The host E2B weight set (about 3 GB), drawn once per test session."""
+    if seed not in _E2B_WEIGHTS:
+        _E2B_WEIGHTS.clear()
+        _E2B_WEIGHTS[seed] = e2b.Weights(e2b.e2b_config(), seed)
+    return _E2B_WEIGHTS[seed]
+
+
 def test_decode_step_e2b_batch1(g):
     """The full E2B shapes at KV length 2048 (the new token at position 2047)."""
     cfg = e2b.e2b_config()
-    w = e2b.Weights(cfg, 123)
+    w = e2b_weights()
     dec, got, want, _ = run_step(g, cfg, w, 1, 2047, [1234])
     check_logits(got, want)
     del dec
+
+
+def test_decode_step_e2b_batch64(g):
+    """BASELINE config 5 at batch 64: the full E2B shapes, 64 sequences each with a
+    2047-token cache, the new token at position 2047. This is the configuration in
+    which the short-M tensor-core GEMV (with its split-K cluster reduction) and the
+    batched attention ring run together at E2B shapes. The reference runs one
+    sequence per forward (rust/src/model.rs:142-205), so the oracle for a batch is
+    each sequence's own forward; the oracle computes every row of a batch with the
+    same arithmetic whatever the row count, so checking a seeded subset of 8
+    sequences (the first and the last among them) through one batched oracle call
+    is the same as 8 batch-1 forwards. Bars: the batch-1 ones (logits rel-L2 and
+    max |diff|) plus the step's new key/value rows."""
+    cfg = e2b.e2b_config()
+    w = e2b_weights()
+    B, pos = 64, 2047
+    ids = [int(v) for v in synth.int_codes(640, B, 0, cfg.vocab - 1)]
+    ids[5] = ids[6]  # two sequences with the same token (different caches)
+    dec = e2b.Decoder(g, cfg, w, batch=B, cache_len=pos, capacity=pos + 1, kv_device_seed=6400)
+    dec.set_ids(ids)
+    dec.run()
+    logits = dec.read(dec.logits).reshape(B, cfg.vocab)
+    sub = [0, 5, 6, 17, 31, 42, 58, 63]
+    kv = {}
+    got_rows = {}
+    for i in dec.kcache:
+        K = dec.kcache[i][sub].cpu().numpy()
+        V = dec.vcache[i][sub].cpu().numpy()
+        got_rows[i] = (K[:, pos].copy(), V[:, pos].copy())
+        K[:, pos] = 0.0
+        V[:, pos] = 0.0
+        kv[i] = (K, V)
+    del dec
+    want = e2b_ref.decode_step(cfg, w, [ids[b] for b in sub], pos, kv)
+    check_logits(logits[sub], want)
+    for i, (K, V) in kv.items():
+        assert rel(got_rows[i][0], K[:, pos]) <= 1e-4 and rel(got_rows[i][1], V[:, pos]) <= 1e-4, i
+
+
+def test_zz_release_e2b_weights():
+    _E2B_WEIGHTS.clear()

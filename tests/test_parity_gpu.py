@@ -246,6 +246,28 @@ def test_embed_config4_shapes_bit_exact(g):
         assert np.array_equal(got.reshape(ref.shape), ref)
 
 
+def test_embed_config4_full_size_bit_exact(g):
+    """BASELINE config 4 at its own size: the 262,144-row 4-bit token table and the
+    I8 per-layer table [262,144, 35 x 256 = 8960] with one scale per 256-column
+    block, 4096 ids including row 0, the last row (262,143, whose byte offset in the
+    I8 table passes 2^31) and duplicates; bit-exact against the oracle
+    (rust/src/backend_cpu.rs:127-137)."""
+    v = 262144
+    tok = synth.random_qweight(7401, v, 1536, 4)
+    ple = synth.random_qweight(7402, v, 35 * 256, 8, True, group_size=256)
+    ids = synth.int_codes(7403, 4096, 0, v - 1).astype(np.uint32)
+    ids[:4] = [0, v - 1, v - 1, 0]
+    ids[100:110] = ids[200:210]
+    ids[-1] = v - 1
+    assert int(v - 1) * 8960 > 2 ** 31
+    for table, emb in ((tok, float(np.sqrt(np.float32(1536)))), (ple, 16.0)):
+        qt = g.quant_tensor(table)
+        got = g.readback(g.embed_rows(qt, ids, emb))
+        g.free_quant(qt)
+        ref = oracle.embed_rows(table, ids, emb)
+        assert np.array_equal(got.reshape(ref.shape), ref)
+
+
 def test_embed_odd_width_and_duplicates(g):
     t = synth.make_qweight(81, 20, 18, 4)  # D % 4 != 0 -> per-element kernel
     ids = [0, 19, 19, 5, 0]
