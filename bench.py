@@ -68,7 +68,10 @@ class DecodeStep:
     stack_qkv: a KV layer's q, k and v projections as one stacked GEMV, as the
     decoder runs them (False: the separate config-2 sweep shapes)."""
 
-    def __init__(self, g, m: int, seed: int, with_lm_head: bool = True, stack_qkv: bool = True):
+    def __init__(self, g, m: int, seed: int, with_lm_head: bool = True, stack_qkv: bool = True, lm_shard=None):
+        """lm_shard=(rank, world): the lm_head split by vocab rows over the ranks through
+        the fused sharded lm_head (gq.parallel.PeerLmHead, device barrier); a graph of
+        the step then holds two steps, one per logits buffer."""
         import torch
         from gq import synth
 
@@ -134,7 +137,27 @@ class DecodeStep:
                                        (ctx, c_void_p(x.data_ptr()), m, p.k, c_void_p(t.qw), c_void_p(y.data_ptr())),
                                        b, p))
                 self.last_out = y
-        if with_lm_head:
+        self.peer = None
+        self.lm_pair = []
+        if with_lm_head and lm_shard is not None:
+            from gq.parallel import PeerLmHead, shard_rows
+            rank, world = lm_shard
+            p = synth.Proj("lm_head", synth.VOCAB, synth.HIDDEN, 8, True)
+            r0, r1 = shard_rows(p.n, world, rank)
+            payload = torch.randint(0, 256, ((r1 - r0) * p.k,), generator=gen, device=dev, dtype=torch.uint8)
+            torch.cuda.synchronize(dev)
+            t = g.quant_tensor_from_device(payload, synth.uniform(wseed + 1, r1 - r0, 0.005, 0.02), (r1 - r0, p.k),
+                                           8, True, p.k)
+            self.keep.append(t)
+            self.bytes += synth.proj_bytes(p, m)  # the whole head: the step's work across the ranks
+            self.peer = PeerLmHead(g, t, p.n, rank, world, max_m=m, cap=30.0, barrier="device")
+            # one (GEMV with peer stores + completion signal, bounded wait) pair per logits buffer
+            self.lm_pair = [[(lab, fn, a, 0, p) for lab, fn, a in
+                             self.peer.device_calls(self.x_hidden.data_ptr(), m, p.k, par)] for par in (0, 1)]
+            self.calls += self.lm_pair[0]
+            self.logits = self.peer.logits[1][:m]
+            self.last_out = self.logits
+        elif with_lm_head:
             p = synth.Proj("lm_head", synth.VOCAB, synth.HIDDEN, 8, True)
             t, payload, scales = qweight(p.n, p.k, 8, True)
             self.logits = torch.empty(m, p.n, device=dev, dtype=torch.float32)
@@ -145,18 +168,36 @@ class DecodeStep:
                                (ctx, c_void_p(self.x_hidden.data_ptr()), m, p.k, c_void_p(t.qw), c_float(30.0),
                                 c_void_p(self.logits.data_ptr()), p.n, 0), b, p))
             self.last_out = self.logits
-        self.launches = len(self.calls)
+        self.steps_per_graph = 2 if self.peer is not None else 1
+        self.launches = len(self.calls)  # per step
 
-    def run(self):
-        for label, fn, args, _, _ in self.calls:
+    def _exec(self, calls):
+        for label, fn, args, _, _ in calls:
             rc = fn(*args)
             if rc != 0:
                 self.g._check(rc, label)
 
+    def run(self):
+        """One step (with a sharded lm_head: two steps, one per logits buffer)."""
+        if self.peer is None:
+            self._exec(self.calls)
+            return
+        layers = [c for c in self.calls if not c[0].startswith("lm_head")]
+        for par in (0, 1):
+            self._exec(layers)
+            self._exec(self.lm_pair[par])
+
+    run_graph_body = run
+
+    def close(self):
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
+
     def run_layers(self):
         """The per-layer projections only (everything but the lm_head)."""
         for label, fn, args, _, _ in self.calls:
-            if label == "lm_head":
+            if label.startswith("lm_head"):
                 continue
             rc = fn(*args)
             if rc != 0:
@@ -307,11 +348,16 @@ def run_gq(args):
     hbm_peak, bf16_peak, peak_kind = peaks()
     g = CudaBackend(local, own_stream=True)
     stream = torch.cuda.ExternalStream(g.stream_ptr(), device=g.torch_device)
-    step = DecodeStep(g, args.m, seed=1234 + rank)
+    # N = 1: the whole step on one GPU. N > 1: the same step (same metric, same bytes)
+    # with the lm_head split by vocab rows over the ranks (the one component that
+    # shards) and the trunk replicated: strong scaling of one decode stream.
+    step = DecodeStep(g, args.m, seed=1234, lm_shard=(rank, world) if world > 1 else None)
     g.flush()
     step.run()  # eager once (also sets kernel attributes before recording)
     g.flush()
-    graph = g.record(step.run)
+    if world > 1:
+        dist.barrier()
+    graph = g.record(step.run_graph_body)
 
     for _ in range(args.warmup):
         g.replay(graph)
@@ -322,12 +368,12 @@ def run_gq(args):
     with ClockSampler(local) as clk:
         ms_total = cuda_events_time(torch, stream, lambda: g.replay(graph), args.steps)
     g.flush()
-    ms = ms_total / args.steps
+    ms = ms_total / (args.steps * step.steps_per_graph)
     t = torch.tensor([ms], device=g.torch_device)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
-    value = step.bytes * world / (ms_max / 1e3) / 1e9
+    value = step.bytes / (ms_max / 1e3) / 1e9
 
     # e2e: pinned host activation in, logits out, through the C ABI, each step.
     from ctypes import c_void_p
@@ -346,7 +392,7 @@ def run_gq(args):
     for _ in range(max(3, args.warmup // 4)):
         e2e_step()
     e2e_steps = max(10, min(args.steps, 500))
-    ms_e2e = cuda_events_time(torch, stream, e2e_step, e2e_steps) / e2e_steps
+    ms_e2e = cuda_events_time(torch, stream, e2e_step, e2e_steps) / (e2e_steps * step.steps_per_graph)
     t = torch.tensor([ms_e2e], device=g.torch_device)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -363,7 +409,7 @@ def run_gq(args):
     reps_l = max(20, min(args.steps, 200))
     ms_l = cuda_events_time(torch, stream, lambda: g.replay(graph_l), reps_l) / reps_l
     g.destroy_graph(graph_l)
-    layer_calls = [c for c in step.calls if c[0] != "lm_head"]
+    layer_calls = [c for c in step.calls if not c[0].startswith("lm_head")]
     layer_bytes = sum(c[3] for c in layer_calls)
     achieved = layer_bytes / (ms_l / 1e3) / 1e9
 
@@ -386,6 +432,8 @@ def run_gq(args):
     lm = [(c, mm) for c, mm in zip(step.calls, med) if c[0] == "lm_head"]
     by_kind = {}
     for c, mm in zip(step.calls, med):
+        if c[0].startswith("lm_head"):
+            continue
         key = f"{c[4].bits}b{'s' if c[4].signed else ''}_mode{c[4].mode}"
         d = by_kind.setdefault(key, [0, 0.0, 0])
         d[0] += c[3]
@@ -402,19 +450,20 @@ def run_gq(args):
 
     line = {
         "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": round(ms_max, 5), "higher_is_better": True, "scaling": "weak",
+        "warmup": args.warmup, "ms_per_step": round(ms_max, 5), "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "u8/i8 weights, f32 activations+accumulate", "data": "synthetic",
         "config": {"workload": f"e2b_quantized_decode_step_m{args.m}", "layers": synth.LAYERS,
                    "tokens_per_step": args.m, "lm_head": "i8 262144x1536 softcap 30",
                    "bits": "q/k/v/o/ple i8, gate+up 4-bit (geglu fused), down 2-bit",
                    "bytes_per_step": step.bytes, "l2": "weights 1.12 GB per step >> 126 MB L2; no flush",
-                   "parallelism": f"replicas x{world}" if world > 1 else "single"},
-        "matmul_q_only_tokens_per_s": round(args.m * world / (ms_max / 1e3), 1),
+                   "parallelism": (f"lm_head vocab-sharded x{world} (fused NVLink all-gather, device barrier), "
+                                   "trunk replicated") if world > 1 else "single"},
+        "matmul_q_only_tokens_per_s": round(args.m / (ms_max / 1e3), 1),
         "frac_of_measured_hbm": round(value / world / hbm_peak, 4),
         "frac_of_8tbs_nominal": round(value / world / 8000.0, 4),
-        "e2e": {"value": round(step.bytes * world / (ms_e2e / 1e3) / 1e9, 2), "unit": UNIT,
+        "e2e": {"value": round(step.bytes / (ms_e2e / 1e3) / 1e9, 2), "unit": UNIT,
                 "ms_per_step": round(ms_e2e, 5), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-        "gpu_launches": step.launches * args.steps,
+        "gpu_launches": step.launches * step.steps_per_graph * args.steps,
         "roofline": {"bound": "hbm",
                      "kernel": f"gemv_q_kernel: the {len(layer_calls)} per-layer MATMUL_Q launches of the step, "
                                f"graph-replayed back to back ({layer_bytes} algorithmic B per replay)",
@@ -432,6 +481,7 @@ def run_gq(args):
     line["clocks"] = clk.summary()
 
     if world > 1:
+        line["replicas"] = replicas(torch, dist, g, stream, rank, world, args)
         line["lm_head_sharded"] = sharded_lm_head(torch, dist, rank, world, local, args)
         try:  # a failure of this leg (on every rank alike) keeps the rest of the line
             line["decode_sharded_lm_head"] = decode_sharded(torch, dist, rank, world, local, args)
@@ -446,12 +496,41 @@ def run_gq(args):
     if rank == 0 and world == 1:
         line["cpu_baseline"] = cpu_sample(step, min_seconds=10.0)
     g.destroy_graph(graph)
+    step.close()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(line), flush=True)
     g.close()
+
+
+def replicas(torch, dist, g, stream, rank, world, args):
+    """Weak scaling beside the headline: every rank decodes its own stream with the
+    whole step (its own weights, no collective on the data path), max over ranks;
+    value = all ranks' bytes / time."""
+    step = DecodeStep(g, args.m, seed=4321 + rank)
+    g.flush()
+    step.run()
+    g.flush()
+    graph = g.record(step.run)
+    for _ in range(3):
+        g.replay(graph)
+    g.flush()
+    dist.barrier()
+    with torch.cuda.stream(stream):
+        dist.all_reduce(torch.zeros(1, device=g.torch_device))
+    reps = max(20, min(args.steps, 500))
+    ms = cuda_events_time(torch, stream, lambda: g.replay(graph), reps) / reps
+    g.flush()
+    t = torch.tensor([ms], device=g.torch_device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    g.destroy_graph(graph)
+    out = {"ms_per_step": round(ms, 5), "GB/s_all_ranks": round(step.bytes * world / (ms / 1e3) / 1e9, 2),
+           "scaling": "weak", "note": "independent decode streams, one per GPU, whole lm_head on each"}
+    step.close()
+    return out
 
 
 def sharded_lm_head(torch, dist, rank, world, local, args):

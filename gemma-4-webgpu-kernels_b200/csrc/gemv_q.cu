@@ -578,11 +578,18 @@ bool gq_gemv_supported(gq_ctx *ctx, const gq_qweight *w, int64_t m, int nw) {
          ctx->smem_optin - 1024;
 }
 
+bool gq_gemv_r1_supported(gq_ctx *ctx, const gq_qweight *w, int64_t m, int nw);
+int gq_gemv_r1_launch(gq_ctx *ctx, int mode, const float *x, const gq_qweight *w, const gq_qweight *w2,
+                      const float *bs, int64_t b_off, float cap, float *y, int64_t y_col0);
+
 // mode: 0 plain, 1 geglu (w2 = up), 2 gelu * bs slice, 3 soft-cap.
 int gq_gemv_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq_qweight *w,
                    const gq_qweight *w2, const float *bs, int64_t b_stride, int64_t b_off,
                    float cap, float *y, int64_t ldy, int64_t y_col0) {
   const int nw = (mode == 1) ? 2 : 1;
+  // one activation row: the register-x kernel (gemv_r1.cu) where its shape rules hold
+  if (m == 1 && (uintptr_t)x % 16 == 0 && gq_gemv_r1_supported(ctx, w, m, nw))
+    return gq_gemv_r1_launch(ctx, mode, x, w, w2, bs, b_off, cap, y, y_col0);
   const int mt = m <= 1 ? 1 : (m == 2 ? 2 : 4);
   const int rb = (int)w->row_bytes;
   const int C = rb / 16;

@@ -10,8 +10,10 @@
 
 #include <cstdio>
 #include <cstring>
+#include <algorithm>
 #include <string>
 
+#include "gq_host.h"
 #include "gq_internal.cuh"
 
 // kernels (gemv_q.cu, misc_q.cu)
@@ -108,6 +110,8 @@ int scratch_get(gq_ctx *ctx, int slot, size_t floats, float **out) {
 }
 
 }  // namespace
+
+int gq_set_error(gq_ctx *ctx, int status, const std::string &msg) { return gq_fail(ctx, status, msg); }
 
 extern "C" {
 
@@ -209,6 +213,7 @@ int gq_sync(gq_ctx *ctx) {
     std::string msg = "device error:";
     if (flags & GQ_DEVERR_BAD_ID) msg += " embedding id out of range;";
     if (flags & GQ_DEVERR_WAIT_TIMEOUT) msg += " pipeline wait timed out;";
+    if (flags & GQ_DEVERR_SAMPLE_CAP) msg += " top-p nucleus larger than the device sampler's 256 candidates;";
     return gq_fail(ctx, GQ_ERR_DEVICE, msg);
   }
   return GQ_OK;
@@ -425,6 +430,35 @@ bool use_gemv_tcx(gq_ctx *ctx, const float *x, int64_t m, const gq_qweight *w, i
   return gq_gemv_tcx_supported(ctx, w, x, m, nw);
 }
 
+// More than 64 rows that the tensor-core prefill GEMM does not take (below its
+// threshold, or a shape it does not support): the short-M GEMV in row blocks of
+// at most 64 (equal blocks, so none falls under the GEMV's minimum), each block a
+// launch over the same weights (L2 serves the later blocks of weights that fit).
+// Exact integer dot products, so these rows keep the FFMA-path bound.
+int64_t tcx_block_rows(int64_t m) {
+  const int64_t nb = (m + 63) / 64;
+  return (m + nb - 1) / nb;
+}
+
+bool use_gemv_tcx_blocked(gq_ctx *ctx, const float *x, int64_t m, const gq_qweight *w, int nw) {
+  if (m <= 64 || w->k % 4 != 0) return false;  // row offsets of x stay 16-byte aligned
+  if (ctx->peers.n > 0 || ctx->peers.signal) return false;  // one launch per call carries the peer stores
+  return use_gemv_tcx(ctx, x, tcx_block_rows(m), w, nw);
+}
+
+int tcx_blocked_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq_qweight *w, const gq_qweight *w2,
+                       const float *bs, int64_t b_stride, int64_t b_off, float cap, float *y, int64_t ldy,
+                       int64_t y_col0) {
+  const int64_t rb = tcx_block_rows(m);
+  for (int64_t r0 = 0; r0 < m; r0 += rb) {
+    const int64_t mb = std::min(rb, m - r0);
+    const int rc = gq_gemv_tcx_launch(ctx, mode, x + r0 * w->k, mb, w, w2, bs ? bs + r0 * b_stride : nullptr, b_stride,
+                                      b_off, cap, y + r0 * ldy, ldy, y_col0);
+    if (rc != GQ_OK) return rc;
+  }
+  return GQ_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -436,6 +470,8 @@ int gq_linear(gq_ctx *ctx, const float *x, int64_t m, int64_t k, const gq_qweigh
   if (use_prefill(ctx, x, m, w)) return gq_prefill_launch(ctx, 0, x, m, w, nullptr, nullptr, 0, 0, 0.0f, y, w->n, 0);
   if (use_gemv_tc(ctx, x, m, w, 1)) return gq_gemv_tc_launch(ctx, 0, x, m, w, nullptr, nullptr, 0, 0, 0.0f, y, w->n, 0);
   if (use_gemv_tcx(ctx, x, m, w, 1)) return gq_gemv_tcx_launch(ctx, 0, x, m, w, nullptr, nullptr, 0, 0, 0.0f, y, w->n, 0);
+  if (use_gemv_tcx_blocked(ctx, x, m, w, 1))
+    return tcx_blocked_launch(ctx, 0, x, m, w, nullptr, nullptr, 0, 0, 0.0f, y, w->n, 0);
   if (gq_gemv_supported(ctx, w, m, 1))
     return gq_gemv_launch(ctx, 0, x, m, w, nullptr, nullptr, 0, 0, 0.0f, y, w->n, 0);
   return gq_scalar_linear_launch(ctx, x, m, w, y);
@@ -457,6 +493,8 @@ int gq_linear_geglu(gq_ctx *ctx, const float *x, int64_t m, int64_t k, const gq_
     return gq_gemv_tc_launch(ctx, 1, x, m, wg, wu, nullptr, 0, 0, 0.0f, y, wg->n, 0);
   if (same && use_gemv_tcx(ctx, x, m, wg, 2))
     return gq_gemv_tcx_launch(ctx, 1, x, m, wg, wu, nullptr, 0, 0, 0.0f, y, wg->n, 0);
+  if (same && use_gemv_tcx_blocked(ctx, x, m, wg, 2))
+    return tcx_blocked_launch(ctx, 1, x, m, wg, wu, nullptr, 0, 0, 0.0f, y, wg->n, 0);
   if (same && gq_gemv_supported(ctx, wg, m, 2))
     return gq_gemv_launch(ctx, 1, x, m, wg, wu, nullptr, 0, 0, 0.0f, y, wg->n, 0);
   // composition of rust/src/backend.rs:156-160
@@ -484,6 +522,8 @@ int gq_linear_gelu_mul_cols(gq_ctx *ctx, const float *x, int64_t m, int64_t k, c
     return gq_gemv_tc_launch(ctx, 2, x, m, w, nullptr, b, b_stride, b_offset, 0.0f, y, w->n, 0);
   if (use_gemv_tcx(ctx, x, m, w, 1))
     return gq_gemv_tcx_launch(ctx, 2, x, m, w, nullptr, b, b_stride, b_offset, 0.0f, y, w->n, 0);
+  if (use_gemv_tcx_blocked(ctx, x, m, w, 1))
+    return tcx_blocked_launch(ctx, 2, x, m, w, nullptr, b, b_stride, b_offset, 0.0f, y, w->n, 0);
   if (gq_gemv_supported(ctx, w, m, 1))
     return gq_gemv_launch(ctx, 2, x, m, w, nullptr, b, b_stride, b_offset, 0.0f, y, w->n, 0);
   // composition of rust/src/backend.rs:163-167
@@ -606,6 +646,8 @@ int gq_linear_softcap(gq_ctx *ctx, const float *x, int64_t m, int64_t k, const g
   if (use_gemv_tc(ctx, x, m, w, 1)) return gq_gemv_tc_launch(ctx, 3, x, m, w, nullptr, nullptr, 0, 0, cap, y, ldy, y_col0);
   if (use_gemv_tcx(ctx, x, m, w, 1))
     return gq_gemv_tcx_launch(ctx, 3, x, m, w, nullptr, nullptr, 0, 0, cap, y, ldy, y_col0);
+  if (use_gemv_tcx_blocked(ctx, x, m, w, 1))
+    return tcx_blocked_launch(ctx, 3, x, m, w, nullptr, nullptr, 0, 0, cap, y, ldy, y_col0);
   if (gq_gemv_supported(ctx, w, m, 1))
     return gq_gemv_launch(ctx, 3, x, m, w, nullptr, nullptr, 0, 0, cap, y, ldy, y_col0);
   // composition: generic linear into scratch, then soft-cap into the strided output

@@ -115,67 +115,63 @@ __global__ void embed_quad_kernel(QView q, const uint32_t *ids, int64_t t, float
 }
 
 // EMBED_Q, one warp per output row (the row's id, packed row and scale row are
-// looked up once): each lane turns 16 consecutive codes into 16 outputs per step
-// (one 4/8/16-byte load, four 16-byte stores), the warp covering 512 contiguous
-// output values. Same operation order as embed_quad_kernel (bit-identical).
-// Requires D % 16 == 0, group % 16 == 0 (a 16-code step never crosses a scale
-// group), 16-byte aligned output rows and packed rows aligned to one step.
+// looked up once). Lane l owns the four outputs 4l..4l+3 of every 128-column step,
+// so each warp store writes 512 contiguous bytes (the output is 80 % of the bytes
+// moved: a 16-byte store per lane at a 64-byte lane stride, as an earlier version
+// did, spreads one store instruction over 32 sectors of 16 lines). The four codes
+// of a lane are one 4-, 2- or 1-byte load (I8 / 4-bit / 2-bit), all U steps' loads
+// are issued before the first store, and the stores stream past L2 (st.global.cs:
+// an embedding row is not read again by this kernel). Arithmetic order
+// (q * s) * emb as embed_quad_kernel and the CPU (bit-identical).
+// Requires D % 4 == 0, group == D or a power of two >= 4, 16-byte aligned output
+// rows, and packed rows aligned to one lane's load.
 template <int BITS, bool SIGNED>
-__global__ void embed_row_kernel(QView q, const uint32_t *ids, int64_t t, float emb, float *out, uint32_t *err) {
+__global__ void __launch_bounds__(256) embed_row_kernel(QView q, const uint32_t *ids, int64_t t, float emb,
+                                                        float *out, uint32_t *err) {
   gqd::griddep_wait();
   gqd::griddep_launch_dependents();
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= t) return;
   const uint32_t id = __ldg(ids + row);
-  float4 *orow = reinterpret_cast<float4 *>(out + row * q.k);
-  const int steps = (int)(q.k >> 4);
+  float *orow = out + row * q.k;
+  const int64_t D = q.k;
   if ((int64_t)id >= q.n) {
-    for (int j = lane; j < steps; j += 32)
-#pragma unroll
-      for (int u = 0; u < 4; ++u) orow[4 * j + u] = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int64_t c = 4 * lane; c < D; c += 128) __stcs(reinterpret_cast<float4 *>(orow + c), make_float4(0.f, 0.f, 0.f, 0.f));
     if (lane == 0) gqd::report(err, GQ_DEVERR_BAD_ID);
     return;
   }
   const uint8_t *rp = q.bytes + (int64_t)id * q.row_bytes;
   const float *sr = q.scales + (int64_t)id * q.scale_stride;
-  const int gshift = (q.group == q.k) ? 31 : (31 - __clz((int)q.group));  // group is a power of two here
-  using L = typename std::conditional<BITS == 8, uint4, typename std::conditional<BITS == 4, uint2, uint32_t>::type>::type;
-  const L *src = reinterpret_cast<const L *>(rp);
-  constexpr int U = 4;  // steps per lane in flight: all loads first, then the stores
-  for (int j0 = lane; j0 < steps; j0 += 32 * U) {
-    L w[U];
+  const int gshift = (q.group == q.k) ? 63 : (31 - __clz((int)q.group));  // group is a power of two here
+  constexpr int U = 8;  // 128-column steps per lane in flight: all loads first, then the stores
+  for (int64_t c0 = 4 * lane; c0 < D; c0 += 128 * U) {
+    uint32_t w[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const int j = j0 + 32 * u;
-      if (j < steps) w[u] = __ldg(src + j);
+      const int64_t c = c0 + 128 * u;
+      w[u] = 0;
+      if (c < D) {
+        if constexpr (BITS == 8) w[u] = __ldg(reinterpret_cast<const uint32_t *>(rp + c));
+        else if constexpr (BITS == 4) w[u] = __ldg(reinterpret_cast<const uint16_t *>(rp + (c >> 1)));
+        else w[u] = __ldg(rp + (c >> 2));
+      }
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const int j = j0 + 32 * u;
-      if (j >= steps) break;
-      int32_t c[16];
-      if constexpr (BITS == 8) {
-        const uint32_t ws[4] = {w[u].x, w[u].y, w[u].z, w[u].w};
+      const int64_t c = c0 + 128 * u;
+      if (c >= D) break;
+      int32_t cd[4];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const uint32_t b = (ws[i >> 2] >> (8 * (i & 3))) & 0xffu;
-          c[i] = SIGNED ? (int32_t)(int8_t)b : (int32_t)b - 128;
-        }
-      } else if constexpr (BITS == 4) {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) c[i] = (int32_t)(((i < 8 ? w[u].x : w[u].y) >> (4 * (i & 7))) & 0xfu) - 8;
-      } else {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) c[i] = (int32_t)((w[u] >> (2 * i)) & 0x3u) - 2;
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t b = (w[u] >> (BITS * i)) & ((1u << BITS) - 1u);
+        if constexpr (BITS == 8) cd[i] = SIGNED ? (int32_t)(int8_t)b : (int32_t)b - 128;
+        else cd[i] = (int32_t)b - (1 << (BITS - 1));
       }
-      const float sc = __ldg(sr + (gshift == 31 ? 0 : ((16 * j) >> gshift)));
-#pragma unroll
-      for (int v = 0; v < 4; ++v)
-        orow[4 * j + v] = make_float4(__fmul_rn(__fmul_rn((float)c[4 * v], sc), emb),
-                                      __fmul_rn(__fmul_rn((float)c[4 * v + 1], sc), emb),
-                                      __fmul_rn(__fmul_rn((float)c[4 * v + 2], sc), emb),
-                                      __fmul_rn(__fmul_rn((float)c[4 * v + 3], sc), emb));
+      const float sc = __ldg(sr + (gshift == 63 ? 0 : (c >> gshift)));
+      __stcs(reinterpret_cast<float4 *>(orow + c),
+             make_float4(__fmul_rn(__fmul_rn((float)cd[0], sc), emb), __fmul_rn(__fmul_rn((float)cd[1], sc), emb),
+                         __fmul_rn(__fmul_rn((float)cd[2], sc), emb), __fmul_rn(__fmul_rn((float)cd[3], sc), emb)));
     }
   }
 }
@@ -271,8 +267,8 @@ int gq_embed_launch(gq_ctx *ctx, const gq_qweight *w, const uint32_t *ids, int64
   if (t == 0 || w->k == 0) return GQ_OK;
   const QView q = view_of(w);
   const int64_t g = w->group_size;
-  const bool row_path = w->k % 16 == 0 && ((uintptr_t)out % 16 == 0) && (g == w->k || (g % 16 == 0 && (g & (g - 1)) == 0)) &&
-                        (uintptr_t)w->bytes % 16 == 0 && w->row_bytes % (w->signed_i8 || w->bits == 8 ? 16 : (w->bits == 4 ? 8 : 4)) == 0 &&
+  const bool row_path = w->k % 4 == 0 && ((uintptr_t)out % 16 == 0) && (g == w->k || (g >= 4 && (g & (g - 1)) == 0)) &&
+                        (uintptr_t)w->bytes % 4 == 0 && w->row_bytes % (w->signed_i8 || w->bits == 8 ? 4 : (w->bits == 4 ? 2 : 1)) == 0 &&
                         t <= (int64_t)0x7fffffff * 8;
   if (row_path) {
     const unsigned blocks = (unsigned)((t + 7) / 8);

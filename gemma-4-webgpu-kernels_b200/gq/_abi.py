@@ -20,6 +20,12 @@ GQ_ERR_DEVICE = 5
 
 GQ_DEVERR_BAD_ID = 0x1
 GQ_DEVERR_WAIT_TIMEOUT = 0x2
+GQ_DEVERR_SAMPLE_CAP = 0x4
+
+
+class SampleOpts(ctypes.Structure):
+    """gq_sample_opts (include/gq.h): the reference's SampleOpts (rust/src/sampler.rs:29-39)."""
+    _fields_ = [("temperature", c_float), ("top_k", c_int32), ("top_p", c_float), ("repetition_penalty", c_float)]
 
 
 class GqError(RuntimeError):
@@ -81,10 +87,26 @@ SIGNATURES = {
     "gq_peer_wait": (c_int, [c_void_p, c_void_p, c_int32, c_void_p]),
     "gq_ctx_set_wait_limit": (c_int, [c_void_p, c_uint64]),
     "gq_argmax_rows": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p]),
+    "gq_sample_rows": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int64,
+                               c_void_p, c_void_p]),
+    "gq_topk_rows": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_int32, c_float, c_void_p,
+                             c_int64, c_int64, c_void_p, c_void_p]),
+    "gq_sample_candidates": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p,
+                                     c_void_p]),
     "gq_ipc_get_handle": (c_int, [c_void_p, c_void_p, c_void_p]),
     "gq_ipc_open": (c_int, [c_void_p, c_void_p, POINTER(c_void_p)]),
     "gq_ipc_close": (c_int, [c_void_p, c_void_p]),
     "gq_embed_rows": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_float, c_void_p]),
+    "gq_st_open": (c_int, [c_char_p, POINTER(c_void_p)]),
+    "gq_st_open_memory": (c_int, [c_void_p, c_size_t, POINTER(c_void_p)]),
+    "gq_st_close": (c_int, [c_void_p]),
+    "gq_st_count": (c_int64, [c_void_p]),
+    "gq_st_name": (c_char_p, [c_void_p, c_int64]),
+    "gq_st_info": (c_int, [c_void_p, c_char_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "gq_st_read_f32": (c_int, [c_void_p, c_char_p, c_void_p, c_size_t]),
+    "gq_bits_for": (c_int32, [c_char_p, c_void_p, c_void_p, c_int32]),
+    "gq_st_resolve": (c_int, [c_char_p, c_void_p, c_void_p, c_void_p]),
+    "gq_st_upload_quant": (c_int, [c_void_p, c_void_p, c_char_p, c_int32, POINTER(c_void_p)]),
     "gq_linear_prefill_static": (
         c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int32, c_int32, c_void_p]),
     "gq_linear_prefill_static_status": (c_int, [c_void_p, POINTER(c_uint32)]),

@@ -19,6 +19,19 @@ pub struct GqQWeight {
 pub struct GqGraph {
     _p: [u8; 0],
 }
+#[repr(C)]
+pub struct GqStFile {
+    _p: [u8; 0],
+}
+/// gq_sample_opts: the fields of the reference's SampleOpts (src/sampler.rs:29-39).
+#[repr(C)]
+#[derive(Clone, Copy, Debug)]
+pub struct GqSampleOpts {
+    pub temperature: f32,
+    pub top_k: i32,
+    pub top_p: f32,
+    pub repetition_penalty: f32,
+}
 
 pub const GQ_OK: c_int = 0;
 pub const GQ_ERR_INVALID_ARGUMENT: c_int = 1;
@@ -28,6 +41,7 @@ pub const GQ_ERR_OUT_OF_MEMORY: c_int = 4;
 pub const GQ_ERR_DEVICE: c_int = 5;
 pub const GQ_DEVERR_BAD_ID: u32 = 0x1;
 pub const GQ_DEVERR_WAIT_TIMEOUT: u32 = 0x2;
+pub const GQ_DEVERR_SAMPLE_CAP: u32 = 0x4;
 pub const GQ_ATTN_KPOS_ASCENDING: u32 = 0x1;
 pub const GQ_ATTN_KPOS_IDENTITY: u32 = 0x2;
 
@@ -82,9 +96,32 @@ extern "C" {
     pub fn gq_peer_wait(ctx: *mut GqCtx, flags: *const u32, world: i32, sync: *const u32) -> c_int;
     pub fn gq_argmax_rows(ctx: *mut GqCtx, x: *const f32, m: i64, n: i64, ldx: i64, idx_base: i64,
         val: *mut f32, idx: *mut i64) -> c_int;
+    // sampling on the device (src/sampler.rs:116-190) and the sharded candidate exchange
+    pub fn gq_sample_rows(ctx: *mut GqCtx, logits: *const f32, m: i64, vocab: i64, ld: i64,
+        opts: *const GqSampleOpts, recent: *const u32, n_recent: i64, recent_stride: i64,
+        rng_state: *mut u64, tokens: *mut i32) -> c_int;
+    pub fn gq_topk_rows(ctx: *mut GqCtx, logits: *const f32, m: i64, n: i64, ld: i64, idx_base: i64, k: i32,
+        repetition_penalty: f32, recent: *const u32, n_recent: i64, recent_stride: i64, val: *mut f32,
+        idx: *mut i64) -> c_int;
+    pub fn gq_sample_candidates(ctx: *mut GqCtx, val: *const f32, idx: *const i64, m: i64, ncand: i64,
+        opts: *const GqSampleOpts, rng_state: *mut u64, tokens: *mut i32) -> c_int;
     pub fn gq_ipc_get_handle(ctx: *mut GqCtx, dptr: *mut c_void, handle64: *mut u8) -> c_int;
     pub fn gq_ipc_open(ctx: *mut GqCtx, handle64: *const u8, dptr: *mut *mut c_void) -> c_int;
     pub fn gq_ipc_close(ctx: *mut GqCtx, dptr: *mut c_void) -> c_int;
+    // checkpoint loading (src/safetensors.rs, src/weights.rs:37-118 restated in libgq)
+    pub fn gq_st_open(path: *const c_char, out: *mut *mut GqStFile) -> c_int;
+    pub fn gq_st_open_memory(bytes: *const u8, nbytes: usize, out: *mut *mut GqStFile) -> c_int;
+    pub fn gq_st_close(f: *mut GqStFile) -> c_int;
+    pub fn gq_st_count(f: *const GqStFile) -> i64;
+    pub fn gq_st_name(f: *const GqStFile, i: i64) -> *const c_char;
+    pub fn gq_st_info(f: *const GqStFile, name: *const c_char, dtype16: *mut c_char, shape8: *mut i64,
+        ndim: *mut i32, data: *mut *const u8, nbytes: *mut usize) -> c_int;
+    pub fn gq_st_read_f32(f: *const GqStFile, name: *const c_char, dst_host: *mut f32, count: usize) -> c_int;
+    pub fn gq_bits_for(name: *const c_char, patterns: *const *const c_char, bits: *const i32, nrules: i32) -> i32;
+    pub fn gq_st_resolve(logical: *const c_char, weight256: *mut c_char, scale256: *mut c_char,
+        bare256: *mut c_char) -> c_int;
+    pub fn gq_st_upload_quant(ctx: *mut GqCtx, f: *const GqStFile, logical: *const c_char, bits_u8: i32,
+        out: *mut *mut GqQWeight) -> c_int;
     // EMBED_Q (Backend::embed_rows on a quantized table)
     pub fn gq_embed_rows(ctx: *mut GqCtx, table: *const GqQWeight, ids: *const u32, t: i64, scale: f32,
         out: *mut f32) -> c_int;

@@ -48,6 +48,7 @@ typedef enum gq_status {
 /* Device status bits reported through GQ_ERR_DEVICE. */
 #define GQ_DEVERR_BAD_ID 0x1u       /* embed id >= table rows (output row zeroed) */
 #define GQ_DEVERR_WAIT_TIMEOUT 0x2u /* a bounded pipeline wait gave up */
+#define GQ_DEVERR_SAMPLE_CAP 0x4u   /* a top-p nucleus exceeded the device sampler's candidates */
 
 typedef struct gq_ctx gq_ctx;         /* device + stream + error word + workspace */
 typedef struct gq_qweight gq_qweight; /* packed weight resident on the device */
@@ -196,12 +197,102 @@ int gq_ctx_set_wait_limit(gq_ctx *ctx, uint64_t limit_ns);
 int gq_argmax_rows(gq_ctx *ctx, const float *x, int64_t m, int64_t n, int64_t ldx, int64_t idx_base, float *val,
                    int64_t *idx);
 
+/* ---- sampling: the reference's sampler (rust/src/sampler.rs:116-190) on the
+ *      device, so a decode step reads back token ids, not logits rows. */
+/* SampleOpts (rust/src/sampler.rs:29-39): temperature <= 0 is greedy; top_k = 0
+ * disables top-k (1..256 on the device); top_p >= 1 disables top-p;
+ * repetition_penalty = 1 disables the penalty. */
+typedef struct gq_sample_opts {
+  float temperature;
+  int32_t top_k;
+  float top_p;
+  float repetition_penalty;
+} gq_sample_opts;
+
+/* sample() for each of the m rows of logits [m, vocab] (row stride ld floats, 0 =
+ * vocab): the repetition penalty over recent[row * recent_stride .. + n_recent)
+ * (device u32 ids; 0 <= n_recent <= 4096; ids >= vocab ignored; each distinct id
+ * once; the logits are not modified), then greedy, sample_all, or top-k / top-p
+ * over the sorted candidates (ties to the smaller id), the draw being
+ * Rng::next_f64 of rng_state[row] (device u64 splitmix64 states, advanced in place
+ * by every non-greedy row, as the reference's Rng). tokens[row] (device int32)
+ * receives the id. top_k = 0 with top_p < 1 keeps the 256 largest as candidates
+ * (with the whole row's softmax denominator): a row whose nucleus needs more gets
+ * -1 and raises GQ_DEVERR_SAMPLE_CAP at the next gq_sync. Sums over a whole row are
+ * chunked (a draw within f32 rounding of a token boundary may pick its
+ * neighbour); the candidate arithmetic is the reference's sequential f32 order.
+ * Uses the context workspace. No counterpart in the reference's backend (its
+ * sampler reads the logits back, rust/src/engine.rs:207-215). */
+int gq_sample_rows(gq_ctx *ctx, const float *logits, int64_t m, int64_t vocab, int64_t ld,
+                   const gq_sample_opts *opts, const uint32_t *recent, int64_t n_recent,
+                   int64_t recent_stride, uint64_t *rng_state, int32_t *tokens);
+
+/* The k largest (1 <= k <= 256) of each row of a vocab shard's logits [m, n] (row
+ * stride ld, 0 = n), after the repetition penalty (ids relative to the whole
+ * vocabulary: column c is id idx_base + c), sorted by value, ties to the smaller id:
+ * val [m, k] f32 and idx [m, k] int64 (device; -inf / -1 past the row's end). The
+ * union of every shard's top k holds the whole vocabulary's top k, so a
+ * vocab-sharded lm_head exchanges G * k pairs per row (any all-gather) and samples
+ * them with gq_sample_candidates. Uses the context workspace. No counterpart in the
+ * reference. */
+int gq_topk_rows(gq_ctx *ctx, const float *logits, int64_t m, int64_t n, int64_t ld, int64_t idx_base,
+                 int32_t k, float repetition_penalty, const uint32_t *recent, int64_t n_recent,
+                 int64_t recent_stride, float *val, int64_t *idx);
+
+/* Greedy or top-k (+ top-p) sampling of rows given as candidate pairs val/idx
+ * [m, ncand] (device; idx -1 = none; 1 <= ncand <= 4096), e.g. every rank's
+ * gq_topk_rows output gathered: the candidates are sorted (value, then smaller
+ * id) and sampled as gq_sample_rows does with the same options (penalty already
+ * applied by gq_topk_rows). Modes that need the whole row's softmax (top_k = 0
+ * with temperature > 0) return GQ_ERR_UNSUPPORTED. No counterpart in the
+ * reference. */
+int gq_sample_candidates(gq_ctx *ctx, const float *val, const int64_t *idx, int64_t m, int64_t ncand,
+                         const gq_sample_opts *opts, uint64_t *rng_state, int32_t *tokens);
+
 /* CUDA IPC for the peer buffers above: the 64-byte handle of a gq_alloc'd device
  * buffer, the mapping of a peer's handle into this context's device (peer access
  * enabled), and its release. */
 int gq_ipc_get_handle(gq_ctx *ctx, void *dptr, uint8_t *handle64);
 int gq_ipc_open(gq_ctx *ctx, const uint8_t *handle64, void **dptr);
 int gq_ipc_close(gq_ctx *ctx, void *dptr);
+
+/* ---- checkpoint loading: the reference's safetensors reader and quantized-weight
+ *      construction (rust/src/safetensors.rs, rust/src/weights.rs:37-118), on the
+ *      host side of this library, so a caller without the Rust loader (C, Python)
+ *      reads the real QAT checkpoint layout straight into gq_qweight objects. */
+typedef struct gq_st_file gq_st_file; /* a parsed safetensors file */
+
+/* Memory-map a safetensors file read-only and parse its header (parse_header,
+ * rust/src/safetensors.rs:52-72: [u64 LE header length][JSON header][payload];
+ * __metadata__ skipped). Tensor bytes are read only when used. */
+int gq_st_open(const char *path, gq_st_file **out);
+/* Same over a caller-owned blob in host memory (kept referenced until gq_st_close). */
+int gq_st_open_memory(const uint8_t *bytes, size_t nbytes, gq_st_file **out);
+int gq_st_close(gq_st_file *f);
+/* Tensor count and the i-th name (names sorted; the pointer lives as long as f). */
+int64_t gq_st_count(const gq_st_file *f);
+const char *gq_st_name(const gq_st_file *f, int64_t i);
+/* dtype (NUL-terminated, 16 bytes), shape (up to 8 dims), the payload slice inside the
+ * mapping and its size (offsets checked against the file: raw_bytes,
+ * rust/src/safetensors.rs:154-163). Any out pointer may be NULL. */
+int gq_st_info(const gq_st_file *f, const char *name, char *dtype16, int64_t *shape8, int32_t *ndim,
+               const uint8_t **data, size_t *nbytes);
+/* decode_to_f32 (rust/src/safetensors.rs:98-105) of an F32 / F16 / BF16 tensor of
+ * exactly `count` elements into host memory. */
+int gq_st_read_f32(const gq_st_file *f, const char *name, float *dst_host, size_t count);
+/* Gemma4Config::bits_for (rust/src/config.rs:161-169): the bits of the first pattern
+ * (ECMAScript regex, searched anywhere in name) that matches, 16 when none does, -1
+ * for a bad pattern or argument. */
+int32_t gq_bits_for(const char *name, const char *const *patterns, const int32_t *bits, int32_t nrules);
+/* resolve_tensor_names (rust/src/weights.rs:37-48): the on-disk weight, scale and bare
+ * names (256-byte buffers; bare is "" when there is none) of a logical weight name. */
+int gq_st_resolve(const char *logical, char *weight256, char *scale256, char *bare256);
+/* ModelWeights::load for a quantized tensor (rust/src/weights.rs:86-110): the U8 / I8
+ * payload of `logical` (resolved as above, falling back to the bare name) and its F32
+ * / F16 / BF16 scale become a weight with bits = 8 for I8 else bits_u8 (the caller's
+ * gq_bits_for of the logical name without ".weight"), K = stored columns x values per
+ * byte and group_size = K / scale columns, uploaded with gq_qweight_upload. */
+int gq_st_upload_quant(gq_ctx *ctx, const gq_st_file *f, const char *logical, int32_t bits_u8, gq_qweight **out);
 
 /* Backend::embed_rows for a quantized table (rust/src/backend.rs:101-102;
  * CPU rust/src/backend_cpu.rs:127-137, wgpu EMBED_Q at

@@ -427,3 +427,177 @@ int32_t gqo_attention(const float *q, int64_t t, int64_t hq, int64_t dh, const f
   par_ranges(t * hq, (uint64_t)(t * hq) * (uint64_t)s * (uint64_t)(dh + dv), threads, attn_rows, &c);
   return 0;
 }
+
+/* ---- sampling (rust/src/sampler.rs) --------------------------------------------- */
+
+/* Rng::next_u64 / next_f64 (sampler.rs:13-26) */
+uint64_t gqo_rng_next_u64(uint64_t *state) {
+  *state += 0x9e3779b97f4a7c15ull;
+  uint64_t z = *state;
+  z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+  z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+  return z ^ (z >> 31);
+}
+
+double gqo_rng_next_f64(uint64_t *state) {
+  return (double)(gqo_rng_next_u64(state) >> 11) / (double)(1ull << 53);
+}
+
+/* softmax_over (sampler.rs:46-54): max by f32::max (NaN ignored), exp((l - max) * inv_t),
+ * sequential f32 sum, then each divided by the sum. */
+static void softmax_over(const float *l, const int64_t *idx, int64_t n, float inv_t, float *probs) {
+  float mx = -INFINITY;
+  for (int64_t i = 0; i < n; i++) mx = fmaxf(mx, l[idx[i]]);
+  float sum = 0.0f;
+  for (int64_t i = 0; i < n; i++) {
+    probs[i] = expf((l[idx[i]] - mx) * inv_t);
+    sum += probs[i];
+  }
+  for (int64_t i = 0; i < n; i++) probs[i] /= sum;
+}
+
+/* sample_all (sampler.rs:58-69) */
+static int32_t sample_all(const float *l, int64_t vocab, float inv_t, double u) {
+  float mx = -INFINITY;
+  for (int64_t i = 0; i < vocab; i++) mx = fmaxf(mx, l[i]);
+  float sum = 0.0f;
+  for (int64_t i = 0; i < vocab; i++) sum += expf((l[i] - mx) * inv_t);
+  float r = (float)u * sum;
+  for (int64_t i = 0; i < vocab; i++) {
+    r -= expf((l[i] - mx) * inv_t);
+    if (r <= 0.0f) return (int32_t)i;
+  }
+  return (int32_t)(vocab - 1);
+}
+
+/* values[b].partial_cmp(&values[a]) of the descending sorts: Greater / Less / Equal
+ * (unordered counts as Equal), as -1 when a goes first. */
+static int desc_cmp(const float *v, int64_t a, int64_t b) {
+  if (v[a] > v[b]) return -1;
+  if (v[a] < v[b]) return 1;
+  return 0;
+}
+
+/* stable merge sort of idx[0..n) by desc_cmp (Rust's sort_by is stable) */
+static void stable_sort_desc(const float *v, int64_t *idx, int64_t n, int64_t *tmp) {
+  for (int64_t width = 1; width < n; width *= 2) {
+    for (int64_t lo = 0; lo < n; lo += 2 * width) {
+      int64_t mid = lo + width < n ? lo + width : n;
+      int64_t hi = lo + 2 * width < n ? lo + 2 * width : n;
+      int64_t i = lo, j = mid, o = lo;
+      while (i < mid && j < hi) tmp[o++] = desc_cmp(v, idx[j], idx[i]) < 0 ? idx[j++] : idx[i++];
+      while (i < mid) tmp[o++] = idx[i++];
+      while (j < hi) tmp[o++] = idx[j++];
+    }
+    memcpy(idx, tmp, (size_t)n * sizeof(int64_t));
+  }
+}
+
+/* top_k_desc (sampler.rs:73-113): a bounded min-heap (heap[0] the smallest), then the
+ * stable descending sort of the heap's contents in heap order. Returns k. */
+static int64_t top_k_desc(const float *v, int64_t vocab, int64_t k, int64_t *heap, int64_t *tmp) {
+  int64_t len = 0;
+  for (int64_t i = 0; i < vocab; i++) {
+    if (len < k) {
+      heap[len++] = i;
+      int64_t c = len - 1;
+      while (c > 0) { /* sift_up */
+        const int64_t parent = (c - 1) / 2;
+        if (v[heap[c]] >= v[heap[parent]]) break;
+        const int64_t t = heap[c]; heap[c] = heap[parent]; heap[parent] = t;
+        c = parent;
+      }
+    } else if (v[i] > v[heap[0]]) {
+      heap[0] = i;
+      int64_t c = 0;
+      for (;;) { /* sift_down */
+        const int64_t l = 2 * c + 1, r = 2 * c + 2;
+        int64_t m = c;
+        if (l < len && v[heap[l]] < v[heap[m]]) m = l;
+        if (r < len && v[heap[r]] < v[heap[m]]) m = r;
+        if (m == c) break;
+        const int64_t t = heap[c]; heap[c] = heap[m]; heap[m] = t;
+        c = m;
+      }
+    }
+  }
+  stable_sort_desc(v, heap, len, tmp);
+  return len;
+}
+
+int32_t gqo_sample(const float *logits, int64_t vocab, float temperature, int64_t top_k, float top_p,
+                   float repetition_penalty, const uint32_t *recent, int64_t n_recent, double u) {
+  if (!logits || vocab <= 0 || top_k < 0 || n_recent < 0 || (n_recent > 0 && !recent)) return -1;
+  float *l = (float *)malloc((size_t)vocab * sizeof(float));
+  int64_t *idx = (int64_t *)malloc((size_t)vocab * sizeof(int64_t));
+  int64_t *tmp = (int64_t *)malloc((size_t)vocab * sizeof(int64_t));
+  float *probs = (float *)malloc((size_t)vocab * sizeof(float));
+  int32_t out = -1;
+  if (!l || !idx || !tmp || !probs) goto done;
+  memcpy(l, logits, (size_t)vocab * sizeof(float));
+  /* repetition penalty on the copy, each vocabulary item once (sampler.rs:120-133) */
+  if (repetition_penalty != 1.0f && n_recent > 0) {
+    for (int64_t j = 0; j < n_recent; j++) {
+      const uint32_t tok = recent[j];
+      if ((int64_t)tok >= vocab) continue;
+      int seen = 0;
+      for (int64_t i = 0; i < j && !seen; i++) seen = recent[i] == tok;
+      if (seen) continue;
+      const float x = l[tok];
+      l[tok] = x > 0.0f ? x / repetition_penalty : x * repetition_penalty;
+    }
+  }
+  if (temperature <= 0.0f) { /* greedy (sampler.rs:135-145) */
+    int64_t best = 0;
+    float bv = -INFINITY;
+    for (int64_t i = 0; i < vocab; i++)
+      if (l[i] > bv) {
+        bv = l[i];
+        best = i;
+      }
+    out = (int32_t)best;
+    goto done;
+  }
+  {
+    const float inv_t = 1.0f / temperature;
+    if (top_k == 0 && top_p >= 1.0f) {
+      out = sample_all(l, vocab, inv_t, u);
+      goto done;
+    }
+    int64_t n;
+    if (top_k > 0) {
+      n = top_k_desc(l, vocab, top_k < vocab ? top_k : vocab, idx, tmp);
+    } else {
+      for (int64_t i = 0; i < vocab; i++) idx[i] = i;
+      stable_sort_desc(l, idx, vocab, tmp);
+      n = vocab;
+    }
+    if (top_p < 1.0f) {
+      softmax_over(l, idx, n, inv_t, probs);
+      float cum = 0.0f;
+      int64_t keep = 0;
+      for (int64_t i = 0; i < n; i++) {
+        keep = i + 1;
+        cum += probs[i];
+        if (cum >= top_p) break;
+      }
+      n = keep;
+    }
+    softmax_over(l, idx, n, inv_t, probs);
+    float r = (float)u;
+    for (int64_t i = 0; i < n; i++) {
+      r -= probs[i];
+      if (r <= 0.0f) {
+        out = (int32_t)idx[i];
+        goto done;
+      }
+    }
+    out = (int32_t)idx[n - 1];
+  }
+done:
+  free(l);
+  free(idx);
+  free(tmp);
+  free(probs);
+  return out;
+}

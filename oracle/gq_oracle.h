@@ -20,6 +20,7 @@
  *   rust/src/backend_cpu.rs:149-172, 224-235, 248-336 rms_norm, add/mul/scale, rope,
  *                                 attention; rust/src/backend.rs:137-154 add_rms_norm,
  *                                 head_norm_rope (the support ops of a decode step)
+ *   rust/src/sampler.rs:5-190     Rng, top_k_desc, softmax_over, sample_all, sample
  *
  * Arithmetic order follows the Rust code exactly (no FMA contraction: the build
  * uses -ffp-contract=off), so results are bit-identical to the reference CPU
@@ -127,6 +128,21 @@ int32_t gqo_attention(const float *q, int64_t t, int64_t hq, int64_t dh, const f
                       int64_t s, int64_t hkv, int64_t dv, const uint32_t *q_pos, const uint32_t *k_pos,
                       float scale, uint32_t sliding_window, float attn_softcap, float *out,
                       int32_t threads);
+
+/* ---- sampling: rust/src/sampler.rs ------------------------------------------------
+ * Rng (sampler.rs:5-27): splitmix64; next_u64 advances *state, next_f64 is
+ * (next_u64 >> 11) / 2^53. */
+uint64_t gqo_rng_next_u64(uint64_t *state);
+double gqo_rng_next_f64(uint64_t *state);
+/* sample (sampler.rs:116-190) of one logits row: repetition penalty on a copy (each
+ * distinct recent token < vocab once), greedy when temperature <= 0, else one draw
+ * u in [0, 1) (the caller's rng()) through sample_all (no top-k, top-p >= 1) or the
+ * candidate path: top_k_desc (the bounded min-heap of sampler.rs:67-113, then a
+ * stable descending sort) or a stable sort of the whole row, the top-p cut over
+ * softmax_over, and the draw over the kept candidates. Returns the token id, or -1
+ * for a bad argument. */
+int32_t gqo_sample(const float *logits, int64_t vocab, float temperature, int64_t top_k, float top_p,
+                   float repetition_penalty, const uint32_t *recent, int64_t n_recent, double u);
 
 #ifdef __cplusplus
 }

@@ -68,6 +68,10 @@ def load() -> ctypes.CDLL:
                                       c_int64, c_void_p]),
         "gqo_attention": (c_int32, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int64,
                                     c_int64, c_void_p, c_void_p, c_float, c_uint32, c_float, c_void_p, c_int32]),
+        "gqo_rng_next_u64": (ctypes.c_uint64, [c_void_p]),
+        "gqo_rng_next_f64": (ctypes.c_double, [c_void_p]),
+        "gqo_sample": (c_int32, [c_void_p, c_int64, c_float, c_int64, c_float, c_float, c_void_p, c_int64,
+                                 ctypes.c_double]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(lib, name)
@@ -288,3 +292,22 @@ def attention(q, k, v, q_pos, k_pos, scale: float = 1.0, sliding_window: int = 0
     if rc != 0:
         raise ValueError("oracle attention: bad shape")
     return out
+
+
+def rng_next_f64(state: int):
+    """Rng::next_f64 (rust/src/sampler.rs:23-26): (u in [0, 1), the advanced state)."""
+    st = ctypes.c_uint64(state & 0xFFFFFFFFFFFFFFFF)
+    u = load().gqo_rng_next_f64(ctypes.byref(st))
+    return float(u), int(st.value)
+
+
+def sample(logits, temperature: float, top_k: int, top_p: float, repetition_penalty: float = 1.0,
+           recent=None, u: float = 0.0) -> int:
+    """sample (rust/src/sampler.rs:116-190) of one logits row with the draw u."""
+    lg = _f32(logits).ravel()
+    rc = _u32(recent if recent is not None else []).ravel()
+    tok = load().gqo_sample(_p(lg), lg.size, temperature, int(top_k), top_p, repetition_penalty,
+                            _p(rc) if rc.size else None, rc.size, float(u))
+    if tok < 0:
+        raise ValueError("oracle sample: bad argument")
+    return int(tok)

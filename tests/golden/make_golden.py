@@ -8,6 +8,8 @@ Sources (Dhruba531/gemma-4-webgpu-kernels):
                                scales=[0.5,2.0], group 4 -> [0.5,-1,1.5,0,4,4,-2,8]
   rust/tests/weights.rs:64-71  per-tensor bit widths of the E2B quantization table
   rust/assets/config.json:57-89 the regex table those widths come from
+  rust/tests/model.rs:77-101   sampler: greedy, top-k = 1, the once-per-token
+                               repetition penalty, top-p head, seed determinism
 
 The packed byte images are derived from the documented format (offset binary,
 LSB-first; I8 two's complement: rust/src/dequant.rs:1-12) by the independent
@@ -62,6 +64,20 @@ def main():
         "language_model.layers.0.self_attn.q_proj": 4,
         "language_model.norm": 16,
     }
+    # rust/tests/model.rs:77-101 (fn sampler): logits, options, the draw its closure
+    # returns, and the asserted token; "determinism" has no asserted token (the test
+    # checks two equal runs from Rng::new(1) and the range)
+    kat["sampler"] = [
+        {"logits": [0.1, 5.0, 0.2, -1.0], "temperature": 0.0, "top_k": 0, "top_p": 1.0, "penalty": 1.0,
+         "recent": [], "u": 0.99, "token": 1},
+        {"logits": [0.0, 10.0, 9.0, -5.0], "temperature": 1.0, "top_k": 1, "top_p": 1.0, "penalty": 1.0,
+         "recent": [], "u": 0.99, "token": 1},
+        {"logits": [10.0, 4.0], "temperature": 0.0, "top_k": 0, "top_p": 1.0, "penalty": 2.0,
+         "recent": [0, 0], "u": 0.99, "token": 0},
+        {"logits": [0.0, 10.0, 9.9, -5.0], "temperature": 1.0, "top_k": 0, "top_p": 0.5, "penalty": 1.0,
+         "recent": [], "u": 0.0, "token": 1},
+    ]
+    kat["sampler_determinism"] = {"n": 100, "step": 0.37, "seed": 1, "temperature": 1.0, "top_k": 64, "top_p": 0.95}
     path = os.path.join(os.path.dirname(os.path.abspath(__file__)), "kat.json")
     with open(path, "w") as f:
         json.dump(kat, f, indent=1)

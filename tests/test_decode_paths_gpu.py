@@ -193,3 +193,76 @@ def test_short_m_split_k_fused_modes(g, monkeypatch):
         for a, b0 in zip(o, outs[0]):
             assert np.array_equal(a, b0)
     assert rel_l2(outs[0][2], oracle.softcap(oracle.linear(x, wl), 30.0)) <= REL_L2
+
+
+# M = 1 has two CUDA-core kernels: the register-x GEMV (gemv_r1.cu, for rows of a
+# multiple of 128 bytes whose slice fits in shared memory) and the shared-memory GEMV
+# (gemv_q.cu); GQ_GEMV_R1 selects (1) or deselects (0) the former.
+R1_SHAPES = SHAPES + [(4608, 1536, 8, True), (1536, 4096, 8, True), (2560, 1536, 8, True), (96, 4096, 2, False),
+                      (130, 1024, 4, False)]
+
+
+@pytest.mark.parametrize("r1", ["0", "1"])
+@pytest.mark.parametrize("n,k,bits,signed", R1_SHAPES)
+def test_m1_kernels_linear(g, monkeypatch, r1, n, k, bits, signed):
+    monkeypatch.setenv("GQ_DECODE_TC", "0")
+    monkeypatch.setenv("GQ_GEMV_R1", r1)
+    w = synth.random_qweight(3300 + n + k + bits, n, k, bits, signed)
+    for seed, shift in ((3301, 0.0), (3302, 3.0)):  # zero-mean and shifted activations
+        x = (synth.normal(seed, k) + shift).reshape(1, k)
+        got = g.readback(g.linear(g.tensor(x, x.shape), g.quant_tensor(w)))
+        assert rel_l2(got, oracle.linear(x, w)) <= REL_L2
+
+
+@pytest.mark.parametrize("r1", ["0", "1"])
+def test_m1_kernels_fused_modes(g, monkeypatch, r1):
+    """GeGLU (two weights), gelu * PLE slice and the soft-capped lm_head slice at M = 1."""
+    monkeypatch.setenv("GQ_DECODE_TC", "0")
+    monkeypatch.setenv("GQ_GEMV_R1", r1)
+    k = 1536
+    x = synth.normal(3401, k).reshape(1, k)
+    gx = g.tensor(x, x.shape)
+    wg = synth.random_qweight(3402, 6144, k, 4, False)
+    wu = synth.random_qweight(3403, 6144, k, 4, False)
+    got = g.readback(g.linear_geglu(gx, g.quant_tensor(wg), g.quant_tensor(wu)))
+    assert rel_l2(got, oracle.linear_geglu(x, wg, wu)) <= REL_L2
+    w = synth.random_qweight(3404, 256, k, 8, True)
+    b = synth.normal(3405, 8960).reshape(1, 8960)
+    for off in (0, 17 * 256, 34 * 256):
+        got = g.readback(g.linear_gelu_mul_cols(gx, g.quant_tensor(w), g.tensor(b, b.shape), off))
+        assert rel_l2(got, oracle.linear_gelu_mul_cols(x, w, b, off)) <= REL_L2
+    wl = synth.random_qweight(3406, 4096, k, 8, True)
+    xs = (4.0 * synth.normal(3407, k)).reshape(1, k)
+    full = g.zeros((1, 3 * 4096))
+    g.linear_softcap(g.tensor(xs, xs.shape), g.quant_tensor(wl), 30.0, out=full, col0=4096)
+    got = g.readback(full).reshape(1, 3 * 4096)
+    assert rel_l2(got[:, 4096:8192], oracle.softcap(oracle.linear(xs, wl), 30.0)) <= REL_L2
+    assert not got[:, :4096].any() and not got[:, 8192:].any()
+
+
+@pytest.mark.parametrize("m", [65, 96, 127])
+@pytest.mark.parametrize("n,k,bits,signed", [(2048, 1536, 8, True), (1536, 6144, 2, False), (6144, 1536, 4, False),
+                                             (300, 640, 8, False)])
+def test_rows_65_to_127_blocked_tensor_core_gemv(g, monkeypatch, m, n, k, bits, signed):
+    """Between the short-M GEMV (<= 64 rows) and the prefill GEMM (>= 128 rows): the
+    short-M tensor-core GEMV in equal row blocks of at most 64, exact integer dot
+    products, so the FFMA-path bound holds (the reference switches to its tiled
+    kernel here, rust/src/backend_wgpu.rs:663-673)."""
+    monkeypatch.delenv("GQ_DECODE_TC", raising=False)
+    w = synth.random_qweight(3500 + n + k + bits, n, k, bits, signed)
+    x = synth.normal(3501 + m, m * k).reshape(m, k)
+    gw = g.quant_tensor(w)
+    got = g.readback(g.linear(g.tensor(x, x.shape), gw))
+    assert rel_l2(got, oracle.linear(x, w)) <= REL_L2
+    if n == 6144:
+        wu = synth.random_qweight(3502, n, k, bits, signed)
+        got = g.readback(g.linear_geglu(g.tensor(x, x.shape), gw, g.quant_tensor(wu)))
+        assert rel_l2(got, oracle.linear_geglu(x, w, wu)) <= REL_L2
+    if n == 2048:
+        full = g.zeros((m, n + 64))
+        g.linear_softcap(g.tensor(x, x.shape), gw, 30.0, out=full, col0=64)
+        got = g.readback(full).reshape(m, n + 64)
+        assert rel_l2(got[:, 64:], oracle.softcap(oracle.linear(x, w), 30.0)) <= REL_L2
+        b = synth.normal(3503, m * 4096).reshape(m, 4096)
+        got = g.readback(g.linear_gelu_mul_cols(g.tensor(x, x.shape), gw, g.tensor(b, b.shape), 1024))
+        assert rel_l2(got, oracle.linear_gelu_mul_cols(x, w, b, 1024)) <= REL_L2

@@ -145,3 +145,73 @@ def test_lcg_matches_reference_definition():
     for _ in range(5):
         s = (s * 1103515245 + 12345) & 0x7FFFFFFF
         assert r.next() == np.float32(s) / np.float32(0x7FFFFFFF)
+
+
+def _splitmix64_py(state: int):
+    """An independent restatement of Rng::next_u64 (rust/src/sampler.rs:13-20)."""
+    mask = (1 << 64) - 1
+    state = (state + 0x9E3779B97F4A7C15) & mask
+    z = state
+    z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & mask
+    z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & mask
+    return z ^ (z >> 31), state
+
+
+def test_oracle_rng_is_the_reference_splitmix64():
+    st = 1
+    for _ in range(8):
+        want, st_next = _splitmix64_py(st)
+        u, st2 = oracle.rng_next_f64(st)
+        assert st2 == st_next and u == (want >> 11) / float(1 << 53)
+        st = st2
+    # splitmix64's published first output from state 0
+    assert _splitmix64_py(0)[0] == 0xE220A8397B1DCDAF
+
+
+def test_oracle_sampler_known_answers():
+    """rust/tests/model.rs:77-101 against the sampler restatement."""
+    kat = KAT
+    for c in kat["sampler"]:
+        tok = oracle.sample(np.array(c["logits"], np.float32), c["temperature"], c["top_k"], c["top_p"],
+                            c["penalty"], c["recent"], c["u"])
+        assert tok == c["token"], c
+    d = kat["sampler_determinism"]
+    row = np.array([np.float32(np.sin(np.float32(i) * np.float32(d["step"]))) for i in range(d["n"])], np.float32)
+    toks = []
+    for _ in range(2):
+        u, _ = oracle.rng_next_f64(d["seed"])
+        toks.append(oracle.sample(row, d["temperature"], d["top_k"], d["top_p"], 1.0, None, u))
+    assert toks[0] == toks[1] and 0 <= toks[0] < d["n"]
+
+
+def test_oracle_sampler_against_float64_restatement():
+    """Candidate path (top-k then top-p) and sample_all against a float64 numpy
+    reading of rust/src/sampler.rs on tie-free rows: the token agrees wherever the
+    draw is not within 1e-4 of a boundary."""
+    rng = np.random.default_rng(8)
+    for trial in range(40):
+        n = int(rng.integers(5, 3000))
+        row = (rng.standard_normal(n) * rng.uniform(0.5, 4)).astype(np.float32)
+        t = float(rng.uniform(0.3, 2.0))
+        k = int(rng.integers(0, 80))
+        p = float(rng.choice([1.0, 0.9, 0.5]))
+        u = float(rng.uniform(0, 1))
+        x = row.astype(np.float64)
+        if k == 0 and p >= 1.0:
+            w = np.exp((x - x.max()) / t)
+            cdf = np.cumsum(w) / w.sum()
+            order = np.arange(n)
+        else:
+            order = np.argsort(-x, kind="stable")
+            if k > 0:
+                order = order[:min(k, n)]
+            w = np.exp((x[order] - x[order].max()) / t)
+            if p < 1.0:
+                cum = np.cumsum(w / w.sum())
+                keep = int(np.searchsorted(cum, p) + 1)
+                order, w = order[:keep], w[:keep]
+            cdf = np.cumsum(w) / w.sum()
+        if np.min(np.abs(cdf - u)) < 1e-4:
+            continue
+        want = int(order[min(int(np.searchsorted(cdf, u)), len(order) - 1)])
+        assert oracle.sample(row, t, k, p, 1.0, None, u) == want, trial
