@@ -38,6 +38,8 @@ sys.path.insert(0, ROOT)
 import numpy as np  # noqa: E402
 
 METRIC = "MATMUL_Q decode GB/s (E2B quantized decode step, M=1)"
+# completion barrier of the vocab-sharded lm_head in the N > 1 step (gq.parallel.PeerLmHead)
+LM_BARRIER = os.environ.get("GQ_BENCH_LM_BARRIER", "device")
 UNIT = "GB/s"
 
 
@@ -150,7 +152,7 @@ class DecodeStep:
                                            8, True, p.k)
             self.keep.append(t)
             self.bytes += synth.proj_bytes(p, m)  # the whole head: the step's work across the ranks
-            self.peer = PeerLmHead(g, t, p.n, rank, world, max_m=m, cap=30.0, barrier="device")
+            self.peer = PeerLmHead(g, t, p.n, rank, world, max_m=m, cap=30.0, barrier=LM_BARRIER)
             # one (GEMV with peer stores + completion signal, bounded wait) pair per logits buffer
             self.lm_pair = [[(lab, fn, a, 0, p) for lab, fn, a in
                              self.peer.device_calls(self.x_hidden.data_ptr(), m, p.k, par)] for par in (0, 1)]
@@ -226,12 +228,25 @@ class ClockSampler:
         self.dev = device_index
         self.proc = None
         self.lines = []
+        self.err = ""
+
+    def _gpu_id(self):
+        """nvidia-smi's id of this process's device: its UUID (a CUDA device index is
+        relative to CUDA_VISIBLE_DEVICES, nvidia-smi's -i index is not)."""
+        try:
+            import torch
+            u = str(torch.cuda.get_device_properties(self.dev).uuid)
+            return u if u.startswith("GPU-") else "GPU-" + u
+        except Exception:
+            return str(self.dev)
 
     def __enter__(self):
         try:
+            self.errf = open(os.path.join(ROOT, "gpurun_out", "clock_sampler.err"), "w") \
+                if os.path.isdir(os.path.join(ROOT, "gpurun_out")) else subprocess.DEVNULL
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100",
-                 "-i", str(self.dev)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-i", self._gpu_id()], stdout=subprocess.PIPE, stderr=self.errf, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
         except Exception:
@@ -249,6 +264,8 @@ class ClockSampler:
                 self.proc.wait(timeout=5)
             except Exception:
                 self.proc.kill()
+            if hasattr(self.errf, "close"):
+                self.errf.close()
 
     def summary(self):
         sm, mx, reasons = [], None, set()
@@ -616,13 +633,19 @@ def sharded_lm_head(torch, dist, rank, world, local, args):
                                                c_void_p(y3.data_ptr()), V, r0), "shard gemv")
 
     peer3 = PeerLmHead(g3, wt3, V, rank, world, max_m=1, cap=30.0, barrier="device")
+    peer4 = PeerLmHead(g3, wt3, V, rank, world, max_m=1, cap=30.0, barrier="fused")
 
     def fused():
         for _ in range(per_graph):
             peer3.forward(x3)
 
+    def fused_one_launch():
+        for _ in range(per_graph):
+            peer4.forward(x3)
+
     graphed = {}
-    for key, fn in (("shard_gemv_only", shard_only), ("fused_peer_stores_device_barrier", fused)):
+    for key, fn in (("shard_gemv_only", shard_only), ("fused_peer_stores_device_barrier", fused),
+                    ("fused_peer_stores_wait_in_gemv", fused_one_launch)):
         gr = g3.record(fn)
         for _ in range(3):
             g3.replay(gr)
@@ -639,9 +662,12 @@ def sharded_lm_head(torch, dist, rank, world, local, args):
         graphed[key] = {"ms": round(float(t.item()), 4),
                         "GB/s_whole_head": round(nbytes / (float(t.item()) / 1e3) / 1e9, 1)}
     same = bool(torch.equal(peer3.forward(x3), head.forward(x)))
+    same4 = bool(torch.equal(peer4.forward(x3), head.forward(x)))
     g3.flush()
     peer3.close()
+    peer4.close()
     graphed["fused_peer_stores_device_barrier"]["equals_nccl_result"] = same
+    graphed["fused_peer_stores_wait_in_gemv"]["equals_nccl_result"] = same4
     graphed["note"] = (f"CUDA graph of {per_graph} calls replayed back to back, max over ranks; shard_gemv_only "
                        "writes this rank's columns only (no exchange)")
     out["graph_replayed"] = graphed
@@ -742,7 +768,8 @@ def extras(g, torch, stream, hbm_peak, bf16_peak):
         c3[name] = {"us": round(ms * 1e3, 2), "TFLOP/s": round(tf, 1),
                     "frac_of_measured_bf16": round(tf / bf16_peak, 4)}
         g.destroy_graph(graph)
-    c3["note"] = "each call = bf16 cast of x + tcgen05 GEMM; 10 calls per graph replay"
+    c3["note"] = ("each call = the activation cast (per-row power-of-two scaling, f16 rounding) + the tcgen05 GEMM "
+                  "(weights widened to f16 into TMEM); 10 calls per graph replay")
     out["config3_prefill_m512"] = c3
     for t in (wg, wu, wd):
         g.free_quant(t)

@@ -527,6 +527,8 @@ int launch_t(gq_ctx *ctx, const GemvArgs &a, dim3 grid, size_t smem) {
   if (!attr_set[dev]) {
     GQ_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           (int)ctx->smem_optin));
+    if (const char *c = getenv("GQ_CARVEOUT"))
+      GQ_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, atoi(c)));
     attr_set[dev] = true;
   }
   GQ_CUDA_TRY(ctx, gq_launch(ctx, kern, grid, dim3(THREADS), smem, a));
@@ -565,11 +567,16 @@ static size_t gemv_smem_bytes(int bits, int mt, int nw, int row_bytes, int tile_
 
 // True when the CUDA-core GEMV handles this shape: whole 16-byte chunks per row,
 // one scale per row (group == K), and x rows that fit in shared memory.
+// Activation rows per pass (grid row): 1, 2 or 4 (more rows take several passes;
+// a single 8-row pass measured slower on the E2B projections than the short-M
+// tensor-core GEMV that takes 5 or more rows by default).
+static int gemv_mt(gq_ctx *, const gq_qweight *, int64_t m, int) { return m <= 1 ? 1 : (m == 2 ? 2 : 4); }
+
 bool gq_gemv_supported(gq_ctx *ctx, const gq_qweight *w, int64_t m, int nw) {
   if (w->group_size != w->k || w->k <= 0 || w->n <= 0 || m <= 0) return false;
   if (w->row_bytes % 16 != 0 || w->row_bytes > 65536) return false;
   if (w->n > (1ll << 30)) return false;
-  const int mt = m <= 1 ? 1 : (m == 2 ? 2 : 4);
+  const int mt = gemv_mt(ctx, w, m, nw);
   if (w->k % 4 != 0) return false;
   int lanes = 32;
   while ((w->row_bytes / 16) % lanes != 0) lanes >>= 1;
@@ -590,7 +597,7 @@ int gq_gemv_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq_qw
   // one activation row: the register-x kernel (gemv_r1.cu) where its shape rules hold
   if (m == 1 && (uintptr_t)x % 16 == 0 && gq_gemv_r1_supported(ctx, w, m, nw))
     return gq_gemv_r1_launch(ctx, mode, x, w, w2, bs, b_off, cap, y, y_col0);
-  const int mt = m <= 1 ? 1 : (m == 2 ? 2 : 4);
+  const int mt = gemv_mt(ctx, w, m, nw);
   const int rb = (int)w->row_bytes;
   const int C = rb / 16;
   GemvArgs a = {};

@@ -333,6 +333,10 @@ int r1_launch_t(gq_ctx *ctx, const R1Args &a, dim3 grid, size_t smem) {
   const int dev = ctx->device & 63;
   if (!attr_set[dev]) {
     GQ_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)ctx->smem_optin));
+    // the largest shared-memory carveout, as the other decode GEMVs get from their
+    // large dynamic shared memory, so consecutive launches need no SM reconfiguration
+    GQ_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                          (int)cudaSharedmemCarveoutMaxShared));
     attr_set[dev] = true;
   }
   GQ_CUDA_TRY(ctx, gq_launch(ctx, kern, grid, dim3(kThreads), smem, a));
@@ -419,20 +423,28 @@ bool r1_plan(const gq_ctx *ctx, const gq_qweight *w, int nw, R1Plan *p) {
   return true;
 }
 
-bool r1_enabled() {
+// GQ_GEMV_R1=1 sends every supported M = 1 shape here, =0 none; by default the
+// shapes whose CTAs have little MAC work (measured in the E2B decode chain: the
+// per-layer-input gate [256, 1536] and projection [1536, 256], 2.6 -> 2.1 and
+// 2.8 -> 2.3 us per launch), where the shared-memory GEMV's x staging dominates. With
+// more work per CTA the shared-memory GEMV's 16 warps finish sooner (e.g. the 4-bit
+// gate|up pair: 5.4 us there, 8.6 us here).
+int r1_mode() {
   const char *e = getenv("GQ_GEMV_R1");
-  return e && e[0] == '1';
+  return (e && *e) ? (e[0] == '1' ? 1 : 0) : 2;
 }
+constexpr int64_t kR1SmallWork = 8192;  // codes per CTA (rows x K x weights) below which it wins
 
 }  // namespace
 
-// True when the register-x GEMV takes this M = 1 shape. It is selected with
-// GQ_GEMV_R1=1 (read per call, so tests compare both kernels); the shared-memory
-// GEMV stays the default until this one measures faster in the decode chain.
+// True when the register-x GEMV takes this M = 1 shape (GQ_GEMV_R1 read per call,
+// so tests compare both kernels).
 bool gq_gemv_r1_supported(gq_ctx *ctx, const gq_qweight *w, int64_t m, int nw) {
-  if (m != 1 || !r1_enabled() || ctx->peers.n > 0 || ctx->peers.signal) return false;
+  const int mode = r1_mode();
+  if (m != 1 || mode == 0 || ctx->peers.n > 0 || ctx->peers.signal) return false;
   R1Plan p;
-  return r1_plan(ctx, w, nw, &p);
+  if (!r1_plan(ctx, w, nw, &p)) return false;
+  return mode == 1 || (int64_t)p.rows_per_cta * w->k * nw <= kR1SmallWork;
 }
 
 // mode: 0 plain, 1 geglu (w2 = up), 2 gelu * bs slice, 3 soft-cap. One activation row.

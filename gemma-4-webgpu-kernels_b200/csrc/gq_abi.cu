@@ -570,9 +570,9 @@ int gq_peer_wait(gq_ctx *ctx, const uint32_t *flags, int32_t world, const uint32
   return GQ_OK;
 }
 
-int gq_linear_softcap_peers_signal(gq_ctx *ctx, const float *x, int64_t m, int64_t k, const gq_qweight *w, float cap,
+static int softcap_peers_signal_impl(gq_ctx *ctx, const float *x, int64_t m, int64_t k, const gq_qweight *w, float cap,
                                    float *y, int64_t ldy, int64_t y_col0, float *const *peer_y, int32_t npeers,
-                                   uint32_t *const *flags, uint32_t *sync, int32_t rank) {
+                                   uint32_t *const *flags, uint32_t *sync, int32_t rank, int fused_wait) {
   GQ_ENTER(ctx);
   if (!flags || !sync || rank < 0 || rank > npeers) return gq_fail(ctx, GQ_ERR_INVALID_ARGUMENT, "peers_signal: flags, sync word, rank");
   for (int i = 0; i <= npeers && i <= kMaxPeerDst; ++i)
@@ -581,9 +581,24 @@ int gq_linear_softcap_peers_signal(gq_ctx *ctx, const float *x, int64_t m, int64
   ctx->peer_signal.rank = rank;
   for (int i = 0; i <= npeers && i <= kMaxPeerDst; ++i) ctx->peer_signal.flag[i] = flags[i];
   ctx->peer_signal.signal = 1;
+  ctx->peer_signal.fused_wait = fused_wait;
+  ctx->peer_signal.wait_limit_ns = ctx->wait_limit_ns;
+  ctx->peer_signal.err = ctx->dev_err;
   const int rc = gq_linear_softcap_peers(ctx, x, m, k, w, cap, y, ldy, y_col0, peer_y, npeers);
   ctx->peer_signal = PeerDst{};
   return rc;
+}
+
+int gq_linear_softcap_peers_signal(gq_ctx *ctx, const float *x, int64_t m, int64_t k, const gq_qweight *w, float cap,
+                                   float *y, int64_t ldy, int64_t y_col0, float *const *peer_y, int32_t npeers,
+                                   uint32_t *const *flags, uint32_t *sync, int32_t rank) {
+  return softcap_peers_signal_impl(ctx, x, m, k, w, cap, y, ldy, y_col0, peer_y, npeers, flags, sync, rank, 0);
+}
+
+int gq_linear_softcap_peers_sync(gq_ctx *ctx, const float *x, int64_t m, int64_t k, const gq_qweight *w, float cap,
+                                 float *y, int64_t ldy, int64_t y_col0, float *const *peer_y, int32_t npeers,
+                                 uint32_t *const *flags, uint32_t *sync, int32_t rank) {
+  return softcap_peers_signal_impl(ctx, x, m, k, w, cap, y, ldy, y_col0, peer_y, npeers, flags, sync, rank, 1);
 }
 
 int gq_linear_softcap_peers(gq_ctx *ctx, const float *x, int64_t m, int64_t k, const gq_qweight *w, float cap,

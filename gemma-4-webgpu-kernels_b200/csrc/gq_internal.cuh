@@ -26,6 +26,13 @@ struct PeerDst {
   uint32_t *sync;
   int rank;
   int signal;  // 1 on the launch that completes the output (the last row slice)
+  // fused completion wait: after publishing, the last CTA also waits (bounded by
+  // wait_limit_ns, timeout reported in *err) until every rank's flag in this rank's
+  // own array (flag[0][0 .. n]) has reached the epoch, so the grid completes only
+  // when the full logits are on this rank
+  int fused_wait;
+  uint64_t wait_limit_ns;
+  uint32_t *err;
 };
 
 struct gq_ctx {
@@ -215,6 +222,23 @@ __device__ __forceinline__ void push_to_peers(const float *y, const PeerDst &pd,
         sy[1] = e;
         for (int i = 0; i <= pd.n; ++i)
           asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(pd.flag[i] + pd.rank), "r"(e) : "memory");
+        if (pd.fused_wait) {
+          const uint64_t t0 = globaltimer_ns();
+          bool timed_out = false;
+          for (int r = 0; r <= pd.n && !timed_out; ++r) {
+            for (uint32_t it = 0;; ++it) {
+              uint32_t v;
+              asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(pd.flag[0] + r) : "memory");
+              if ((int32_t)(v - e) >= 0) break;
+              if ((it & 255u) == 255u && globaltimer_ns() - t0 > pd.wait_limit_ns) {
+                if (pd.err) atomicOr(pd.err, GQ_DEVERR_WAIT_TIMEOUT);
+                timed_out = true;
+                break;
+              }
+              __nanosleep(32);
+            }
+          }
+        }
       }
     }
   }

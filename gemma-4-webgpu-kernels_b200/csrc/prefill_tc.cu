@@ -72,6 +72,8 @@ struct Ring {
 struct PrefillArgs {
   int M, N, K;
   int nt;           // tokens per tile (MMA N): 128 or 256
+  int ksplit;       // K splits: the CTAs of one cluster (cluster rank = blockIdx.z), 1 = none
+  int kt_per;       // stages (BK each) per split
   const float *s;
   const float *s2;
   const int *xexp;  // per activation row: the power of two e[m] applied by the cast
@@ -98,6 +100,19 @@ __device__ __forceinline__ void tc_mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, 
       "r"(a_tmem), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+// all threads of every CTA of the cluster (release / acquire at cluster scope)
+__device__ __forceinline__ void pf_cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+// f32 at this CTA's shared-memory location p in cluster CTA `rank`
+__device__ __forceinline__ float pf_ld_cluster(const float *p, uint32_t rank) {
+  uint32_t ra;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(gqd::smem_u32(p)), "r"(rank));
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
+  return v;
+}
+
 // 32 lanes x 32 bits, 32 consecutive columns per thread.
 __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
@@ -199,7 +214,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nt = a.nt;
   const int m0 = blockIdx.x * nt;   // first token of the tile
   const int n0 = blockIdx.y * OW;   // first output column (weight row) of the tile
-  const int KT = a.K / BK;
+  // split-K: this CTA (cluster rank blockIdx.z) owns stages kt0 .. kt0 + KT - 1 of the K range
+  const int KS = a.ksplit, sidx = KS > 1 ? (int)blockIdx.z : 0;
+  const int kt0 = sidx * a.kt_per;
+  const int KT = KS > 1 ? min(a.kt_per, a.K / BK - kt0) : a.K / BK;
   const uint32_t x_bytes = (uint32_t)nt * BK * 2;
 
   if (threadIdx.x == 0) {
@@ -239,12 +257,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         gqd::mbar_arrive_expect_tx(&l_full[s], x_bytes + MW * PK);
-        tma_load_2d(sX + s * X_STAGE, &tmap_x, kt * BK, m0, &l_full[s]);
+        tma_load_2d(sX + s * X_STAGE, &tmap_x, (kt0 + kt) * BK, m0, &l_full[s]);
         if (MODE == 1) {  // gate rows then the same up rows
-          tma_load_2d(sP + s * R::PW, &tmap_w, kt * PK, n0, &l_full[s]);
-          tma_load_2d(sP + s * R::PW + (MW / 2) * PK, &tmap_w2, kt * PK, n0, &l_full[s]);
+          tma_load_2d(sP + s * R::PW, &tmap_w, (kt0 + kt) * PK, n0, &l_full[s]);
+          tma_load_2d(sP + s * R::PW + (MW / 2) * PK, &tmap_w2, (kt0 + kt) * PK, n0, &l_full[s]);
         } else {
-          tma_load_2d(sP + s * R::PW, &tmap_w, kt * PK, n0, &l_full[s]);
+          tma_load_2d(sP + s * R::PW, &tmap_w, (kt0 + kt) * PK, n0, &l_full[s]);
         }
         issued = kt + 1;
       }
@@ -370,6 +388,29 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool ok = all_ok != 0;
       if (!ok) *abort_flag = 1;
       tc_fence_after();
+      if (KS > 1) {
+        // Split-K: this CTA's fp32 partial tile goes to its shared memory as
+        // part[token][weight row] (the load ring is idle now); after a cluster
+        // barrier CTA sidx finalises output columns [sidx*per, (sidx+1)*per) of the
+        // tile for every token, adding the KS partials read over distributed shared
+        // memory in cluster-rank order, then applies the epilogue. The final cluster
+        // barrier (after the join below) keeps every partial alive until its peers
+        // have read it.
+        float *part = reinterpret_cast<float *>(sX);
+        if (ok) {
+          for (int c0 = grp * (nt / 2); c0 < (grp + 1) * (nt / 2); c0 += 32) {
+            uint32_t d0[16], d1[16];
+            const uint32_t taddr = tmem + ((uint32_t)(quarter * 32) << 16) + (uint32_t)c0;
+            tmem_ld16_nowait(taddr, d0);
+            tmem_ld16_nowait(taddr + 16, d1);
+            tmem_wait_ld16(d0);
+            tmem_wait_ld16(d1);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) part[(c0 + j) * MW + row] = __uint_as_float(j < 16 ? d0[j] : d1[j - 16]);
+          }
+        }
+        tc_fence_before();
+      } else {
       const int half = grp;
       const int tcount = nt / 2;
       // weight row of this lane -> output column n
@@ -425,7 +466,40 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
       tc_fence_before();
+      }  // KS == 1
     }
+  }
+
+  if (KS > 1) {
+    // every CTA of the cluster reaches both barriers (abort or not), so none waits
+    // for a peer that left; the second one keeps the partials alive for the readers
+    pf_cluster_sync();
+    if (!*abort_flag && threadIdx.x >= 64) {
+      const float *part = reinterpret_cast<const float *>(sX);
+      const int per = (OW + KS - 1) / KS;
+      const int c_lo = sidx * per, c_hi = min(OW, c_lo + per), ncol = c_hi - c_lo;
+      for (int i = threadIdx.x - 64; ncol > 0 && i < nt * ncol; i += kThreads - 64) {
+        const int t = i / ncol, col = c_lo + i % ncol;  // consecutive threads: consecutive columns
+        const int m = m0 + t, n = n0 + col;
+        if (m >= a.M || n >= a.N) continue;
+        float v0 = 0.0f, v1 = 0.0f;
+        for (int p = 0; p < KS; ++p) {
+          v0 += pf_ld_cluster(part + t * MW + col, (uint32_t)p);
+          if (MODE == 1) v1 += pf_ld_cluster(part + t * MW + col + MW / 2, (uint32_t)p);
+        }
+        const float r0 = rs_tab[t], r1 = rs_tab[NT_MAX + t];
+        float r = __fmul_rn(__fmul_rn(__fmul_rn(v0, r0), r1), a.s[n]);
+        if (MODE == 1) {
+          r = __fmul_rn(gqd::gelu_tanh(r), __fmul_rn(__fmul_rn(__fmul_rn(v1, r0), r1), a.s2[n]));
+        } else if (MODE == 2) {
+          r = __fmul_rn(gqd::gelu_tanh(r), a.bs[(size_t)m * a.b_stride + a.b_off + n]);
+        } else if (MODE == 3) {
+          if (a.cap > 0.0f) r = __fmul_rn(a.cap, tanhf(__fdiv_rn(r, a.cap)));
+        }
+        a.y[(size_t)m * a.ldy + a.y_col0 + n] = r;
+      }
+    }
+    pf_cluster_sync();
   }
 
   __syncthreads();
@@ -505,7 +579,29 @@ int launch_t(gq_ctx *ctx, const CUtensorMap &map, const CUtensorMap &mw, const C
     GQ_CUDA_TRY(ctx, cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Ring<BITS>::kSmem));
     attr_set[dev] = true;
   }
-  GQ_CUDA_TRY(ctx, gq_launch(ctx, kern, grid, dim3(kThreads), Ring<BITS>::kSmem, map, mw, mw2, a));
+  // the K splits of one output tile form a cluster along z
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = Ring<BITS>::kSmem;
+  cfg.stream = ctx->stream;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (ctx->pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (a.ksplit > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = 1;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = (unsigned)a.ksplit;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  GQ_CUDA_TRY(ctx, cudaLaunchKernelEx(&cfg, kern, map, mw, mw2, a));
   return GQ_OK;
 }
 
@@ -621,6 +717,20 @@ int gq_prefill_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq
       encode_weight_map(&mw2, w2 ? w2->bytes : w->bytes, w->n, w->row_bytes, w->bits, ow) != CUDA_SUCCESS)
     return gq_fail(ctx, GQ_ERR_CUDA, "prefill: weight tensor map");
   dim3 grid((unsigned)((m + nt - 1) / nt), (unsigned)((w->n + ow - 1) / ow));
+  // Split K over a cluster of up to 8 CTAs when the output tiles leave SMs idle (the
+  // 2-bit down projection of config 3 has 24 tiles on 148 SMs), keeping at least 8
+  // stages per split; the splits' fp32 partials are added over distributed shared
+  // memory in a fixed order (deterministic).
+  const int kt_all = (int)(K / BK);
+  const int tiles = (int)(grid.x * grid.y);
+  int ks = 1;
+  if (tiles < ctx->num_sms && grid.y <= 65535) {
+    ks = std::min(8, ctx->num_sms / tiles);
+    while (ks > 1 && kt_all / ks < 8) --ks;
+  }
+  a.kt_per = (kt_all + ks - 1) / ks;
+  a.ksplit = (kt_all + a.kt_per - 1) / a.kt_per;  // no empty split
+  grid.z = (unsigned)a.ksplit;
   if (w->bits == 4) return launch_mode<4, false>(ctx, mode, map, mw, mw2, a, grid);
   if (w->bits == 2) return launch_mode<2, false>(ctx, mode, map, mw, mw2, a, grid);
   if (w->signed_i8) return launch_mode<8, true>(ctx, mode, map, mw, mw2, a, grid);

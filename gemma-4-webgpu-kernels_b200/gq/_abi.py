@@ -84,6 +84,9 @@ SIGNATURES = {
     "gq_linear_softcap_peers_signal": (
         c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_float, c_void_p, c_int64, c_int64, c_void_p,
                 c_int32, c_void_p, c_void_p, c_int32]),
+    "gq_linear_softcap_peers_sync": (
+        c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_float, c_void_p, c_int64, c_int64, c_void_p,
+                c_int32, c_void_p, c_void_p, c_int32]),
     "gq_peer_wait": (c_int, [c_void_p, c_void_p, c_int32, c_void_p]),
     "gq_ctx_set_wait_limit": (c_int, [c_void_p, c_uint64]),
     "gq_argmax_rows": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p]),

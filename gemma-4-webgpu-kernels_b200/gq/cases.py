@@ -9,8 +9,12 @@ can select launches of that kernel by name and skip the warm-up:
   config1   4-bit GEMV [6144, 1536], M = 1 (CUDA-core gemv_q_kernel); 64
             rotating weight copies so every call streams from HBM
   lm_head   I8 [262144, 1536] soft-capped GEMV, M = 1 (tensor-core gemv_tc_kernel)
-  prefill   4-bit [6144, 1536] at M = 512 (cast_bf16_kernel + prefill_tc_kernel)
+  prefill   4-bit [6144, 1536] at M = 512 (cast_f16_kernel + prefill_tc_kernel)
+  prefill_down  2-bit [1536, 6144] at M = 512, the config-3 down projection (K split
+            over 6-CTA clusters)
   embed     config 4: 4096 ids into the 4-bit token table and the I8 PLE table
+  embed_small  the same 4096 gathers from 32768-row tables (0.3 GB on the device,
+            outputs 172 MB > L2): the case for multi-pass profiler captures
   decode    config 5: whole E2B decode steps (gq.e2b.Decoder, --batch sequences,
             2047-token cache); each "call" is one step (451 launches)
   attn      batch-64 attention over 2048 cached keys at head_dim 512 (ring kernel)
@@ -29,7 +33,8 @@ from ctypes import c_float, c_void_p
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("case", choices=["config1", "lm_head", "prefill", "embed", "decode", "attn", "tcx", "tcx_down"])
+    ap.add_argument("case", choices=["config1", "lm_head", "prefill", "prefill_down", "embed", "embed_small", "decode",
+                                     "attn", "tcx", "tcx_down"])
     ap.add_argument("--iters", type=int, default=8)
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--warmup", type=int, default=3)
@@ -70,6 +75,12 @@ def main(argv=None) -> int:
         y = torch.empty(512, 6144, device=dev)
         calls = [lambda: lib.gq_linear(ctx, c_void_p(x.data_ptr()), 512, 1536, c_void_p(w.qw),
                                        c_void_p(y.data_ptr()))]
+    elif args.case == "prefill_down":
+        w = upload(1536, 6144, 2, False, 310)
+        x = torch.randn(512, 6144, generator=gen, device=dev)
+        y = torch.empty(512, 1536, device=dev)
+        calls = [lambda: lib.gq_linear(ctx, c_void_p(x.data_ptr()), 512, 6144, c_void_p(w.qw),
+                                       c_void_p(y.data_ptr()))]
     elif args.case == "decode":
         from . import e2b
 
@@ -107,13 +118,14 @@ def main(argv=None) -> int:
         calls = [lambda: lib.gq_linear(ctx, c_void_p(x.data_ptr()), 64, 6144, c_void_p(w.qw),
                                        c_void_p(y.data_ptr()))]
     else:
-        tok = upload(synth.VOCAB, synth.HIDDEN, 4, False, 400)
+        rows = synth.VOCAB if args.case == "embed" else 32768
+        tok = upload(rows, synth.HIDDEN, 4, False, 400)
         rb = synth.LAYERS * synth.PLE_DIM
-        payload = torch.randint(0, 256, (synth.VOCAB * rb,), generator=gen, device=dev, dtype=torch.uint8)
+        payload = torch.randint(0, 256, (rows * rb,), generator=gen, device=dev, dtype=torch.uint8)
         torch.cuda.synchronize()
-        ple = g.quant_tensor_from_device(payload, synth.uniform(401, synth.VOCAB * synth.LAYERS, 0.005, 0.02),
-                                         (synth.VOCAB, rb), 8, True, synth.PLE_DIM)
-        ids = torch.from_numpy(np.random.default_rng(4).integers(0, synth.VOCAB, 4096).astype(np.uint32)).to(dev)
+        ple = g.quant_tensor_from_device(payload, synth.uniform(401, rows * synth.LAYERS, 0.005, 0.02),
+                                         (rows, rb), 8, True, synth.PLE_DIM)
+        ids = torch.from_numpy(np.random.default_rng(4).integers(0, rows, 4096).astype(np.uint32)).to(dev)
         o1 = torch.empty(4096, synth.HIDDEN, device=dev)
         o2 = torch.empty(4096, rb, device=dev)
         calls = [lambda: (lib.gq_embed_rows(ctx, c_void_p(tok.qw), c_void_p(ids.data_ptr()), 4096,

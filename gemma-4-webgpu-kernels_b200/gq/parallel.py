@@ -121,6 +121,8 @@ class PeerLmHead:
         increments a device-resident epoch and stores it into a flag slot of
         every rank (release, system scope) — then gq_peer_wait on this rank's
         flags. No NCCL call per step, and the pair replays inside a graph.
+      "fused": gq_linear_softcap_peers_sync — the same, with the wait done by the
+        GEMV's last CTA itself (one launch instead of two).
       "nccl": gq_linear_softcap_peers then a 1-element NCCL all-reduce on the same
         stream: when it finishes on a rank, every rank's GEMV (and its
         system-fenced peer stores) finished before it.
@@ -137,8 +139,8 @@ class PeerLmHead:
 
         from . import _abi
 
-        if barrier not in ("device", "nccl"):
-            raise ValueError(f"barrier must be 'device' or 'nccl', not {barrier!r}")
+        if barrier not in ("device", "fused", "nccl"):
+            raise ValueError(f"barrier must be 'device', 'fused' or 'nccl', not {barrier!r}")
         self.torch, self.dist, self.g, self.barrier = torch, dist, backend, barrier
         self.rank, self.world, self.vocab, self.cap, self.group, self.max_m = rank, world, vocab, cap, group, max_m
         self.r0, self.r1 = shard_rows(vocab, world, rank)
@@ -192,13 +194,9 @@ class PeerLmHead:
         self.calls += 1
         par = self.calls & 1
         y = self.buf + par * self.buf_floats * 4
-        if self.barrier == "device":
-            _abi.check(lib.gq_linear_softcap_peers_signal(
-                ctx, c_void_p(x.ptr()), m, k, c_void_p(self.w.qw), c_float(self.cap), c_void_p(y), self.vocab,
-                self.r0, self.peer_arr[par], len(self.peers), self.flag_arr, c_void_p(self.sync), self.rank),
-                ctx, "linear_softcap_peers_signal")
-            _abi.check(lib.gq_peer_wait(ctx, c_void_p(self.buf + self.flag_off), self.world, c_void_p(self.sync)),
-                       ctx, "peer_wait")
+        if self.barrier in ("device", "fused"):
+            for label, fn, args in self.device_calls(x.ptr(), m, k, par):
+                _abi.check(fn(*args), ctx, label)
         else:
             _abi.check(lib.gq_linear_softcap_peers(ctx, c_void_p(x.ptr()), m, k, c_void_p(self.w.qw),
                                                    c_float(self.cap), c_void_p(y), self.vocab, self.r0,
@@ -216,9 +214,11 @@ class PeerLmHead:
 
         lib, ctx = self.g.lib, self.g.ctx
         y = self.buf + par * self.buf_floats * 4
-        return [("lm_head_shard", lib.gq_linear_softcap_peers_signal,
-                 (ctx, c_void_p(x_ptr), m, k, c_void_p(self.w.qw), c_float(self.cap), c_void_p(y), self.vocab,
-                  self.r0, self.peer_arr[par], len(self.peers), self.flag_arr, c_void_p(self.sync), self.rank)),
+        args = (ctx, c_void_p(x_ptr), m, k, c_void_p(self.w.qw), c_float(self.cap), c_void_p(y), self.vocab,
+                self.r0, self.peer_arr[par], len(self.peers), self.flag_arr, c_void_p(self.sync), self.rank)
+        if self.barrier == "fused":  # one launch: the GEMV's last CTA also waits for every rank
+            return [("lm_head_shard", lib.gq_linear_softcap_peers_sync, args)]
+        return [("lm_head_shard", lib.gq_linear_softcap_peers_signal, args),
                 ("lm_head_wait", lib.gq_peer_wait,
                  (ctx, c_void_p(self.buf + self.flag_off), self.world, c_void_p(self.sync)))]
 

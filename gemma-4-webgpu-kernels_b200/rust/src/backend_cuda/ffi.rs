@@ -93,6 +93,9 @@ extern "C" {
     pub fn gq_linear_softcap_peers_signal(ctx: *mut GqCtx, x: *const f32, m: i64, k: i64, w: *const GqQWeight,
         cap: f32, y: *mut f32, ldy: i64, y_col0: i64, peer_y: *const *mut f32, npeers: i32,
         flags: *const *mut u32, sync: *mut u32, rank: i32) -> c_int;
+    pub fn gq_linear_softcap_peers_sync(ctx: *mut GqCtx, x: *const f32, m: i64, k: i64, w: *const GqQWeight,
+        cap: f32, y: *mut f32, ldy: i64, y_col0: i64, peer_y: *const *mut f32, npeers: i32,
+        flags: *const *mut u32, sync: *mut u32, rank: i32) -> c_int;
     pub fn gq_peer_wait(ctx: *mut GqCtx, flags: *const u32, world: i32, sync: *const u32) -> c_int;
     pub fn gq_argmax_rows(ctx: *mut GqCtx, x: *const f32, m: i64, n: i64, ldx: i64, idx_base: i64,
         val: *mut f32, idx: *mut i64) -> c_int;

@@ -170,6 +170,16 @@ int gq_linear_softcap_peers_signal(gq_ctx *ctx, const float *x, int64_t m, int64
                                    float cap, float *y, int64_t ldy, int64_t y_col0, float *const *peer_y,
                                    int32_t npeers, uint32_t *const *flags, uint32_t *sync, int32_t rank);
 
+/* gq_linear_softcap_peers_signal with the completion wait folded into the same
+ * launch: after publishing the epoch, the GEMV's last CTA waits (acquire, system
+ * scope, bounded by the context's wait limit -> GQ_DEVERR_WAIT_TIMEOUT) until every
+ * rank's flag in flags[0] has reached it, so the kernel completes only when the
+ * full logits are on this rank and no gq_peer_wait launch follows. Same arguments
+ * and set-up. No counterpart in the reference. */
+int gq_linear_softcap_peers_sync(gq_ctx *ctx, const float *x, int64_t m, int64_t k, const gq_qweight *w,
+                                 float cap, float *y, int64_t ldy, int64_t y_col0, float *const *peer_y,
+                                 int32_t npeers, uint32_t *const *flags, uint32_t *sync, int32_t rank);
+
 /* Stream-ordered wait until flags[0 .. world) have all reached the epoch in
  * sync[1] (acquire, system scope). A wait that runs past the context's wait
  * limit (2 s unless gq_ctx_set_wait_limit changed it) sets

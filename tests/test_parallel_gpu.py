@@ -57,7 +57,7 @@ def _worker(rank, world, port, q):
             gx = g.tensor(x, x.shape)
             nccl = ShardedLmHead(g, shard, V, rank, world, CAP).forward(gx).cpu().numpy()
             ref = oracle.softcap(oracle.linear(x, full), CAP)
-            for barrier in ("nccl", "device"):
+            for barrier in ("nccl", "device", "fused"):
                 peer = PeerLmHead(g, shard, V, rank, world, max_m=m, cap=CAP, barrier=barrier)
                 got = peer.forward(gx).cpu().numpy().copy()
                 # later calls alternate buffers and epochs
@@ -67,24 +67,25 @@ def _worker(rank, world, port, q):
                 rel = float(np.linalg.norm(got.astype(np.float64) - ref) / np.linalg.norm(ref))
                 res[(m, barrier)] = (rel, bool(np.array_equal(got, nccl)),
                                      all(np.array_equal(got, a) for a in again))
-        # the device barrier replayed from a CUDA graph (device-resident epochs)
+        # the device barriers replayed from a CUDA graph (device-resident epochs)
         gg = CudaBackend(rank, own_stream=True)
         x = synth.normal(4199, 3 * K).reshape(3, K).astype(np.float32)
         gx = gg.tensor(x, x.shape)
-        peer = PeerLmHead(gg, shard, V, rank, world, max_m=3, cap=CAP, barrier="device")
-        outs = []
-        graph = gg.record(lambda: outs.extend([peer.forward(gx), peer.forward(gx)]))
-        reps = []
-        for _ in range(3):
-            gg.replay(graph)
-            gg.flush()
-            reps.append([o.cpu().numpy().copy() for o in outs])
-        gg.destroy_graph(graph)
-        peer.close()
-        gg.close()
         ref = oracle.softcap(oracle.linear(x, full), CAP)
-        rel = float(np.linalg.norm(reps[0][0].astype(np.float64) - ref) / np.linalg.norm(ref))
-        res["graph"] = (rel, True, all(np.array_equal(reps[0][0], o) for r in reps for o in r))
+        for barrier in ("device", "fused"):
+            peer = PeerLmHead(gg, shard, V, rank, world, max_m=3, cap=CAP, barrier=barrier)
+            outs = []
+            graph = gg.record(lambda: outs.extend([peer.forward(gx), peer.forward(gx)]))
+            reps = []
+            for _ in range(3):
+                gg.replay(graph)
+                gg.flush()
+                reps.append([o.cpu().numpy().copy() for o in outs])
+            gg.destroy_graph(graph)
+            peer.close()
+            rel = float(np.linalg.norm(reps[0][0].astype(np.float64) - ref) / np.linalg.norm(ref))
+            res[("graph", barrier)] = (rel, True, all(np.array_equal(reps[0][0], o) for r in reps for o in r))
+        gg.close()
         g.close()
         dist.barrier()
         dist.destroy_process_group()

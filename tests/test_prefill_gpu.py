@@ -84,3 +84,29 @@ def test_prefill_reference_tile_sizes(g):
             x = synth.normal(600 + m, m * 128).reshape(m, 128)
             got = g.readback(g.linear(g.tensor(x, x.shape), g.quant_tensor(w))).reshape(m, 70)
             assert rel_l2(got, oracle.linear(f16_round(x), w)) <= 1e-5, (bits, m)
+
+
+@pytest.mark.parametrize("m,n,k,bits,mode", [(512, 1536, 6144, 2, 0), (256, 1024, 2048, 4, 1), (129, 640, 4096, 8, 0),
+                                             (300, 96, 2048, 4, 3)])
+def test_prefill_split_k_over_a_cluster(g, m, n, k, bits, mode):
+    """Grids with fewer output tiles than SMs split K over a cluster of up to 8 CTAs
+    (partials added over distributed shared memory): the config-3 down projection (24
+    tiles, 6 splits), GeGLU pairs, a ragged token tile and the soft-capped epilogue,
+    at the same bars as the unsplit kernel."""
+    w = synth.make_qweight(900 + n + k, n, k, bits, bits == 8)
+    x = synth.normal(901 + m, m * k).reshape(m, k)
+    gx = g.tensor(x, x.shape)
+    if mode == 1:
+        wu = synth.make_qweight(902 + n, n, k, bits)
+        got = g.readback(g.linear_geglu(gx, g.quant_tensor(w), g.quant_tensor(wu))).reshape(m, n)
+        ref = oracle.linear_geglu(f16_round(x), w, wu)
+    elif mode == 3:
+        full = g.zeros((m, n + 32))
+        g.linear_softcap(gx, g.quant_tensor(w), 30.0, out=full, col0=16)
+        got = g.readback(full).reshape(m, n + 32)[:, 16:16 + n]
+        ref = oracle.softcap(oracle.linear(f16_round(x), w), 30.0)
+    else:
+        got = g.readback(g.linear(gx, g.quant_tensor(w))).reshape(m, n)
+        ref = oracle.linear(f16_round(x), w)
+        assert rel_l2(got, oracle.linear(x, w)) <= 1e-2
+    assert rel_l2(got, ref) <= 1e-5

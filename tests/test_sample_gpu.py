@@ -60,6 +60,34 @@ def sample_rows(g, logits, o, seeds, recent=None, vocab=None):
     return tok.cpu().numpy(), st.cpu().numpy().view(np.uint64), sync
 
 
+def penalized(row, penalty, recent):
+    """The repetition penalty of rust/src/sampler.rs:120-133 on a copy (f32)."""
+    l = np.array(row, dtype=np.float32).copy()
+    if penalty != 1.0 and recent is not None:
+        seen = set()
+        for t in np.asarray(recent).ravel():
+            t = int(t)
+            if t < l.size and t not in seen:
+                seen.add(t)
+                l[t] = l[t] / np.float32(penalty) if l[t] > 0 else l[t] * np.float32(penalty)
+    return l
+
+
+def check_sample_all(row, o, seed, tok, state, recent=None, eps=2e-5):
+    """sample_all (rust/src/sampler.rs:58-69) sums the whole row: the device's chunked
+    sums round differently from the reference's sequential f32 sum, so the check is
+    that the draw falls inside the token's interval of the float64 CDF (index order),
+    widened by eps; and the state advanced by one draw."""
+    u, st = oracle.rng_next_f64(seed)
+    assert state == st
+    l = penalized(row, o.repetition_penalty, recent).astype(np.float64)
+    w = np.exp((l - l.max()) / np.float64(o.temperature))
+    cdf = np.cumsum(w) / w.sum()
+    lo = cdf[tok - 1] if tok > 0 else 0.0
+    assert lo - eps <= u <= cdf[tok] + eps, (tok, u, lo, cdf[tok])
+    return 1
+
+
 def check_row(row, o, seed, tok, state, recent=None, delta=1e-6):
     """1 when the token is decided by the draw (and must match), 0 when skipped."""
     if o.temperature <= 0:
@@ -67,6 +95,8 @@ def check_row(row, o, seed, tok, state, recent=None, delta=1e-6):
         assert tok == want
         assert state == seed  # greedy rows draw nothing
         return 1
+    if o.top_k == 0 and o.top_p >= 1.0:
+        return check_sample_all(row, o, seed, tok, state, recent)
     u, st = oracle.rng_next_f64(seed)
     assert state == st
     want = oracle.sample(row, o.temperature, o.top_k, o.top_p, o.repetition_penalty, recent, u)
