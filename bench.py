@@ -804,6 +804,30 @@ def extras(g, torch, stream, hbm_peak, bf16_peak):
     g.free_quant(t_tok)
     g.free_quant(t_ple)
     g.flush()
+
+    # on-device sampling of [m, 262144] logits (gq_sample_rows), the engine's default
+    # options (temperature 1, top-k 64, top-p 0.95) and greedy: what replaces the
+    # 1 MB-per-row logits readback and the host sampler
+    import ctypes
+    from gq import _abi
+    samp = {}
+    for m in (1, 64):
+        lg = torch.randn(m, synth.VOCAB, generator=gen, device=dev) * 3
+        st = torch.arange(1, m + 1, dtype=torch.int64, device=dev)
+        tok = torch.empty(m, dtype=torch.int32, device=dev)
+        for name, o in (("top_k64_top_p095", _abi.SampleOpts(1.0, 64, 0.95, 1.0)),
+                        ("greedy", _abi.SampleOpts(0.0, 0, 1.0, 1.0))):
+            def one(o=o):
+                g._check(lib.gq_sample_rows(ctx, c_void_p(lg.data_ptr()), m, synth.VOCAB, 0, ctypes.byref(o), None, 0,
+                                            0, c_void_p(st.data_ptr()), c_void_p(tok.data_ptr())), "sample")
+            for _ in range(3):
+                one()
+            g.flush()
+            ms = cuda_events_time(torch, stream, one, 20) / 20
+            samp[f"m{m}_{name}"] = {"us": round(ms * 1e3, 2),
+                                    "GB/s_logits": round(m * synth.VOCAB * 4 / (ms / 1e3) / 1e9, 1)}
+    samp["note"] = "one gq_sample_rows call (3 launches) on logits resident in HBM; events on the library stream"
+    out["sampling"] = samp
     return out
 
 

@@ -104,12 +104,19 @@ __device__ __forceinline__ void tc_mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, 
 __device__ __forceinline__ void pf_cluster_sync() {
   asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
 }
-// f32 at this CTA's shared-memory location p in cluster CTA `rank`
-__device__ __forceinline__ float pf_ld_cluster(const float *p, uint32_t rank) {
+// the shared::cluster address of this CTA's shared-memory location p in cluster CTA `rank`
+__device__ __forceinline__ uint32_t pf_cluster_addr(const void *p, uint32_t rank) {
   uint32_t ra;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(gqd::smem_u32(p)), "r"(rank));
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(ra) : "memory");
+  return ra;
+}
+// four f32 at a shared::cluster address (16-byte aligned)
+__device__ __forceinline__ float4 pf_ld_cluster4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
   return v;
 }
 
@@ -475,28 +482,46 @@ __global__ void __launch_bounds__(kThreads, 1)
     // for a peer that left; the second one keeps the partials alive for the readers
     pf_cluster_sync();
     if (!*abort_flag && threadIdx.x >= 64) {
+      // groups of four columns: one 16-byte distributed-shared-memory load per peer,
+      // all KS loads of a group issued before they are added (in rank order)
+      constexpr int kMaxKs = 8;
       const float *part = reinterpret_cast<const float *>(sX);
-      const int per = (OW + KS - 1) / KS;
-      const int c_lo = sidx * per, c_hi = min(OW, c_lo + per), ncol = c_hi - c_lo;
-      for (int i = threadIdx.x - 64; ncol > 0 && i < nt * ncol; i += kThreads - 64) {
-        const int t = i / ncol, col = c_lo + i % ncol;  // consecutive threads: consecutive columns
-        const int m = m0 + t, n = n0 + col;
-        if (m >= a.M || n >= a.N) continue;
-        float v0 = 0.0f, v1 = 0.0f;
-        for (int p = 0; p < KS; ++p) {
-          v0 += pf_ld_cluster(part + t * MW + col, (uint32_t)p);
-          if (MODE == 1) v1 += pf_ld_cluster(part + t * MW + col + MW / 2, (uint32_t)p);
-        }
+      const int per = ((OW + KS - 1) / KS + 3) & ~3;
+      const int c_lo = sidx * per, c_hi = min(OW, c_lo + per), ng = (c_hi - c_lo) / 4;
+      for (int i = threadIdx.x - 64; ng > 0 && i < nt * ng; i += kThreads - 64) {
+        const int t = i / ng, col = c_lo + 4 * (i % ng);  // consecutive threads: consecutive column groups
+        const int m = m0 + t;
+        if (m >= a.M) continue;
+        float4 p0[kMaxKs], p1[kMaxKs];
+#pragma unroll
+        for (int p = 0; p < kMaxKs; ++p)
+          if (p < KS) {
+            p0[p] = pf_ld_cluster4(pf_cluster_addr(part + t * MW + col, (uint32_t)p));
+            if (MODE == 1) p1[p] = pf_ld_cluster4(pf_cluster_addr(part + t * MW + col + MW / 2, (uint32_t)p));
+          }
+        float4 v0 = p0[0], v1 = MODE == 1 ? p1[0] : v0;
+#pragma unroll
+        for (int p = 1; p < kMaxKs; ++p)
+          if (p < KS) {
+            v0.x += p0[p].x; v0.y += p0[p].y; v0.z += p0[p].z; v0.w += p0[p].w;
+            if (MODE == 1) { v1.x += p1[p].x; v1.y += p1[p].y; v1.z += p1[p].z; v1.w += p1[p].w; }
+          }
+        const float a0[4] = {v0.x, v0.y, v0.z, v0.w}, a1[4] = {v1.x, v1.y, v1.z, v1.w};
         const float r0 = rs_tab[t], r1 = rs_tab[NT_MAX + t];
-        float r = __fmul_rn(__fmul_rn(__fmul_rn(v0, r0), r1), a.s[n]);
-        if (MODE == 1) {
-          r = __fmul_rn(gqd::gelu_tanh(r), __fmul_rn(__fmul_rn(__fmul_rn(v1, r0), r1), a.s2[n]));
-        } else if (MODE == 2) {
-          r = __fmul_rn(gqd::gelu_tanh(r), a.bs[(size_t)m * a.b_stride + a.b_off + n]);
-        } else if (MODE == 3) {
-          if (a.cap > 0.0f) r = __fmul_rn(a.cap, tanhf(__fdiv_rn(r, a.cap)));
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int n = n0 + col + c;
+          if (n >= a.N) break;
+          float r = __fmul_rn(__fmul_rn(__fmul_rn(a0[c], r0), r1), a.s[n]);
+          if (MODE == 1) {
+            r = __fmul_rn(gqd::gelu_tanh(r), __fmul_rn(__fmul_rn(__fmul_rn(a1[c], r0), r1), a.s2[n]));
+          } else if (MODE == 2) {
+            r = __fmul_rn(gqd::gelu_tanh(r), a.bs[(size_t)m * a.b_stride + a.b_off + n]);
+          } else if (MODE == 3) {
+            if (a.cap > 0.0f) r = __fmul_rn(a.cap, tanhf(__fdiv_rn(r, a.cap)));
+          }
+          a.y[(size_t)m * a.ldy + a.y_col0 + n] = r;
         }
-        a.y[(size_t)m * a.ldy + a.y_col0 + n] = r;
       }
     }
     pf_cluster_sync();
@@ -727,6 +752,10 @@ int gq_prefill_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq
   if (tiles < ctx->num_sms && grid.y <= 65535) {
     ks = std::min(8, ctx->num_sms / tiles);
     while (ks > 1 && kt_all / ks < 8) --ks;
+  }
+  if (const char *e = getenv("GQ_PREFILL_KSPLIT")) {  // explicit split (tuning and tests): 1..8
+    const int v = atoi(e);
+    if (v >= 1 && v <= 8) ks = std::min(v, kt_all);
   }
   a.kt_per = (kt_all + ks - 1) / ks;
   a.ksplit = (kt_all + a.kt_per - 1) / a.kt_per;  // no empty split

@@ -27,8 +27,10 @@
 // two tokens can pick the neighbour.
 //
 // Kernels: topk_chunk_kernel (one CTA per 4096-column chunk of a row: penalty,
-// 64-bit keys (order-preserving value bits above the complemented column),
-// bitonic sort in shared memory, the chunk's top K and its max), chunk_expsum_kernel
+// 64-bit keys (order-preserving value bits above the complemented column), the
+// chunk's top K by a four-pass radix select of the K-th largest key, and its max;
+// a full bitonic sort of the chunk measured 90 us for one row and 924 us for 64),
+// chunk_expsum_kernel
 // (per-chunk sum of exp((l - max) / T), only for the whole-row modes) and
 // sample_row_kernel (one CTA per row: merge of the chunks' candidates by a second
 // bitonic sort, then the reference's sequential candidate arithmetic, or the
@@ -152,18 +154,101 @@ __global__ void __launch_bounds__(kChunkThreads) topk_chunk_kernel(const SampleA
       a.ckeys[(row * a.nchunks + chunk)] = b;
     }
   } else {
-    for (int i = threadIdx.x; i < kChunk; i += blockDim.x) {
-      const int64_t c = c0 + i;
-      uint64_t kk = 0;  // padding past the row's end
+    // The chunk's k largest keys by radix select: four 8-bit passes over the value
+    // keys (histogram of the keys still matching the selected prefix, then the bin
+    // holding the k-th largest from the top) give the k-th largest value key T; the
+    // keys above T are taken, and of those equal to T the ones in the smallest
+    // columns (a block scan in column order). The k candidates go out unsorted (the
+    // row kernel sorts every chunk's candidates together). Thread t holds columns
+    // c0 + 16t .. c0 + 16t + 15; columns past the row's end are padding (key 0).
+    constexpr int PT = kChunk / kChunkThreads;  // 16 keys per thread
+    uint32_t* hist = reinterpret_cast<uint32_t *>(keys);            // [256] (keys[] is free here)
+    __shared__ uint32_t sel_prefix, sel_need, out_count, warp_ties[kChunkThreads / 32];
+    uint32_t kv[PT];
+#pragma unroll
+    for (int j = 0; j < PT; ++j) {
+      const int64_t c = c0 + (int64_t)threadIdx.x * PT + j;
+      kv[j] = 0u;
       if (c < c1) {
         const float v = logit_at(a, row, c, pen);
         mx = fmaxf(mx, v);
-        kk = ckey(v, (uint32_t)(a.idx_base + c));
+        kv[j] = vkey(v);
       }
-      keys[i] = kk;
     }
-    bitonic_desc(keys, kChunk);
-    for (int i = threadIdx.x; i < a.k; i += blockDim.x) a.ckeys[(row * a.nchunks + chunk) * a.k + i] = keys[i];
+    uint32_t prefix = 0u, mask = 0u, need = (uint32_t)a.k;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+      for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0u;
+      __syncthreads();
+#pragma unroll
+      for (int j = 0; j < PT; ++j)
+        if ((kv[j] & mask) == prefix) atomicAdd(&hist[(kv[j] >> shift) & 255u], 1u);
+      __syncthreads();
+      if (threadIdx.x < 32) {
+        // lane l owns bins 255-8l .. 248-8l; counts from the top
+        const int lane = threadIdx.x;
+        uint32_t cnt[8], tot = 0;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          cnt[q] = hist[255 - 8 * lane - q];
+          tot += cnt[q];
+        }
+        uint32_t incl = tot;  // inclusive prefix over lanes 0..l (higher bins first)
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
+          if (lane >= o) incl += t;
+        }
+        const uint32_t excl = incl - tot;
+        if (excl < need && incl >= need) {  // the bin of the need-th largest is in this lane
+          uint32_t acc = excl;
+          int q = 0;
+          for (; q < 8; ++q) {
+            if (acc + cnt[q] >= need) break;
+            acc += cnt[q];
+          }
+          const uint32_t bin = 255u - 8u * lane - (uint32_t)q;
+          sel_prefix = prefix | (bin << shift);
+          sel_need = need - acc;
+        }
+      }
+      __syncthreads();
+      prefix = sel_prefix;
+      need = sel_need;
+      mask |= 255u << shift;
+      __syncthreads();
+    }
+    // T = prefix: keys > T are taken; of the keys == T, the first `need` in column order
+    uint32_t ties = 0;
+#pragma unroll
+    for (int j = 0; j < PT; ++j) ties += kv[j] == prefix;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    uint32_t incl = ties;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += t;
+    }
+    if (lane == 31) warp_ties[warp] = incl;
+    if (threadIdx.x == 0) out_count = 0u;
+    __syncthreads();
+    uint32_t before = incl - ties;
+    for (int w = 0; w < warp; ++w) before += warp_ties[w];
+    uint64_t *out = a.ckeys + (row * a.nchunks + chunk) * a.k;
+#pragma unroll
+    for (int j = 0; j < PT; ++j) {
+      bool take = kv[j] > prefix;
+      if (kv[j] == prefix) {
+        take = before < need;
+        ++before;
+      }
+      if (take) {
+        const uint32_t slot = atomicAdd(&out_count, 1u);
+        if (slot < (uint32_t)a.k) {
+          const uint32_t col = (uint32_t)(a.idx_base + c0 + (int64_t)threadIdx.x * PT + j);
+          out[slot] = kv[j] ? (((uint64_t)kv[j] << 32) | (uint64_t)(0xffffffffu - col)) : 0ull;
+        }
+      }
+    }
   }
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;

@@ -310,3 +310,78 @@ class ShardedGreedy:
         dist.all_gather_into_tensor(vals, self.val[:m].contiguous(), group=self.group)
         dist.all_gather_into_tensor(idxs, self.idx[:m].contiguous(), group=self.group)
         return merge_argmax(vals.cpu().numpy().reshape(self.world, m), idxs.cpu().numpy().reshape(self.world, m))
+
+
+class ShardedSampler:
+    """Sampling over a vocab-sharded lm_head with the per-shard top-k exchange: each
+    rank computes its shard's soft-capped logits, keeps every row's k best (value,
+    id) pairs after the repetition penalty (gq_topk_rows, ids offset by the shard's
+    first row), all-gathers the G*k pairs per row (G*k*12 bytes instead of its M*V/G
+    logits), and samples them on the device (gq_sample_candidates) with a splitmix64
+    state per row that every rank advances identically, so every rank draws the same
+    token. Greedy (temperature <= 0) and top-k (+ top-p) options, as the reference's
+    sample() (rust/src/sampler.rs:116-190); the union of the shards' top k holds the
+    vocabulary's top k, so the result equals sampling the whole row."""
+
+    def __init__(self, backend, shard, vocab: int, rank: int, world: int, max_m: int, opts, seeds, cap: float = 30.0,
+                 group=None):
+        import torch
+        import torch.distributed as dist
+
+        from . import _abi
+
+        if opts.temperature > 0 and opts.top_k == 0:
+            raise ValueError("ShardedSampler: top_k > 0 (or greedy) is needed for the per-shard exchange")
+        self.torch, self.dist, self.g, self.opts = torch, dist, backend, opts
+        self.rank, self.world, self.vocab, self.cap, self.group = rank, world, vocab, cap, group
+        self.r0, self.r1 = shard_rows(vocab, world, rank)
+        self.per = self.r1 - self.r0
+        assert shard.shape[0] == self.per
+        self.w = shard if getattr(shard, "qw", None) is not None else backend.quant_tensor(shard)
+        self.k = max(1, int(opts.top_k)) if opts.temperature > 0 else 1
+        dev = backend.torch_device
+        self.max_m = max_m
+        self.logits = torch.empty(max_m, max(1, self.per), device=dev)
+        self.val = torch.empty(max_m, self.k, device=dev)
+        self.idx = torch.empty(max_m, self.k, dtype=torch.int64, device=dev)
+        seeds = np.asarray(seeds, dtype=np.uint64).reshape(-1)
+        assert seeds.size >= max_m
+        self.state = torch.from_numpy(seeds[:max_m].view(np.int64).copy()).to(dev)
+        self.tokens = torch.empty(max_m, dtype=torch.int32, device=dev)
+        self._abi = _abi
+
+    def forward(self, x, recent=None):
+        """x: GqTensor [M, K]; recent: optional device int32 [M, R] history (ids of the
+        whole vocabulary). Returns the token ids [M] (numpy), the same on every rank."""
+        import ctypes
+        from ctypes import c_float, c_void_p
+
+        _abi = self._abi
+        m, k = x.shape
+        assert m <= self.max_m
+        lib, ctx = self.g.lib, self.g.ctx
+        torch, dist = self.torch, self.dist
+        n_rec = 0 if recent is None else int(recent.shape[1])
+        rec_p = None if recent is None else c_void_p(recent.data_ptr())
+        if self.per > 0:
+            _abi.check(lib.gq_linear_softcap(ctx, c_void_p(x.ptr()), m, k, c_void_p(self.w.qw), c_float(self.cap),
+                                             c_void_p(self.logits.data_ptr()), self.per, 0), ctx, "shard logits")
+            _abi.check(lib.gq_topk_rows(ctx, c_void_p(self.logits.data_ptr()), m, self.per, self.per, self.r0, self.k,
+                                        c_float(self.opts.repetition_penalty), rec_p, n_rec, n_rec,
+                                        c_void_p(self.val.data_ptr()), c_void_p(self.idx.data_ptr())), ctx, "topk_rows")
+        else:  # an empty shard offers no candidate
+            self.val[:m].fill_(float("-inf"))
+            self.idx[:m].fill_(-1)
+        self.g.flush()
+        vals = torch.empty(self.world, m, self.k, device=self.val.device)
+        idxs = torch.empty(self.world, m, self.k, dtype=torch.int64, device=self.idx.device)
+        dist.all_gather_into_tensor(vals, self.val[:m].contiguous(), group=self.group)
+        dist.all_gather_into_tensor(idxs, self.idx[:m].contiguous(), group=self.group)
+        cv = vals.permute(1, 0, 2).reshape(m, self.world * self.k).contiguous()  # [M][rank][k]
+        ci = idxs.permute(1, 0, 2).reshape(m, self.world * self.k).contiguous()
+        _abi.check(lib.gq_sample_candidates(ctx, c_void_p(cv.data_ptr()), c_void_p(ci.data_ptr()), m,
+                                            self.world * self.k, ctypes.byref(self.opts),
+                                            c_void_p(self.state.data_ptr()), c_void_p(self.tokens.data_ptr())),
+                   ctx, "sample_candidates")
+        self.g.flush()
+        return self.tokens[:m].cpu().numpy().copy()

@@ -235,3 +235,78 @@ def test_sharded_greedy_two_gpus():
     for rank, res in out.items():
         assert isinstance(res, tuple), f"rank {rank}: {res}"
         assert res[0] == res[1], rank
+
+
+def _sampler_worker(rank, world, port, q):
+    from ctypes import byref, c_float, c_void_p
+    from datetime import timedelta
+
+    import torch
+    import torch.distributed as dist
+
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        torch.cuda.set_device(rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                                device_id=torch.device("cuda", rank))
+        from gq import CudaBackend, _abi, synth
+        from gq.parallel import ShardedSampler, shard_rows, slice_rows
+
+        full = synth.random_qweight(4300, V, K, 8, True)
+        r0, r1 = shard_rows(V, world, rank)
+        g = CudaBackend(rank)
+        m = 4
+        x = (3.0 * synth.normal(4301, m * K)).reshape(m, K).astype(np.float32)
+        gx = g.tensor(x, x.shape)
+        seeds = [int(s) for s in synth.splitmix64(4302, m)]
+        recent = torch.from_numpy(np.array([[1, 2, 2, V + 9]] * m, dtype=np.int32)).to(g.torch_device)
+        res = {}
+        for name, o in (("greedy", _abi.SampleOpts(0.0, 0, 1.0, 1.3)),
+                        ("top_k64_top_p", _abi.SampleOpts(1.0, 64, 0.95, 1.3)),
+                        ("top_k8", _abi.SampleOpts(0.7, 8, 1.0, 1.0))):
+            ss = ShardedSampler(g, slice_rows(full, r0, r1), V, rank, world, max_m=m, opts=o, seeds=seeds, cap=CAP)
+            got = ss.forward(gx, recent=recent)
+            # the same draws on the whole row, on this GPU
+            wq = g.quant_tensor(full)
+            logits = torch.empty(m, V, device=g.torch_device)
+            g._check(g.lib.gq_linear_softcap(g.ctx, c_void_p(gx.ptr()), m, K, c_void_p(wq.qw), c_float(CAP),
+                                             c_void_p(logits.data_ptr()), V, 0), "full logits")
+            st = torch.from_numpy(np.array(seeds, dtype=np.uint64).view(np.int64)).to(g.torch_device)
+            tok = torch.empty(m, dtype=torch.int32, device=g.torch_device)
+            g._check(g.lib.gq_sample_rows(g.ctx, c_void_p(logits.data_ptr()), m, V, 0, byref(o),
+                                          c_void_p(recent.data_ptr()), recent.shape[1], recent.shape[1],
+                                          c_void_p(st.data_ptr()), c_void_p(tok.data_ptr())), "sample_rows")
+            g.flush()
+            res[name] = (got.tolist(), tok.cpu().numpy().tolist(), ss.state.cpu().numpy().tolist(),
+                         st.cpu().numpy().tolist())
+            g.free_quant(wq)
+        g.close()
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, res))
+    except Exception as e:  # report instead of hanging the parent
+        q.put((rank, repr(e)))
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="needs two GPUs")
+def test_sharded_sampler_two_gpus():
+    """Sampling with the vocab split over 2 GPUs through the per-shard top-k exchange
+    (gq_topk_rows with the penalty, all-gather of the pairs, gq_sample_candidates):
+    every rank draws the token gq_sample_rows draws on the whole row with the same
+    seeds, and advances the states the same way, for greedy and top-k (+ top-p)."""
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_sampler_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    out = dict(q.get(timeout=600) for _ in ps)
+    for p in ps:
+        p.join(timeout=120)
+    for rank, res in out.items():
+        assert isinstance(res, dict), f"rank {rank}: {res}"
+        for name, (got, want, st, want_st) in res.items():
+            assert got == want and st == want_st, (rank, name)
+    assert out[0] == out[1]
