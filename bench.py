@@ -482,8 +482,12 @@ def run_gq(args):
                 "ms_per_step": round(ms_e2e, 5), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": step.launches * step.steps_per_graph * args.steps,
         "roofline": {"bound": "hbm",
-                     "kernel": f"gemv_q_kernel: the {len(layer_calls)} per-layer MATMUL_Q launches of the step, "
-                               f"graph-replayed back to back ({layer_bytes} algorithmic B per replay)",
+                     "kernel": f"gemv_q_kernel + gemv_r1_kernel (CUDA-core decode GEMVs): the {len(layer_calls)} "
+                               f"per-layer MATMUL_Q launches of the step, graph-replayed back to back "
+                               f"({layer_bytes} algorithmic B per replay)",
+                     "floor": "a dependent launch with no MAC work costs 2.09 us on this GPU "
+                              "(tests/native/chain_latency.cu): 210 launches >= 0.44 ms, i.e. <= 1.65 TB/s "
+                              "(25 % of measured HBM) for this family at batch 1",
                      "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(achieved / hbm_peak, 4), "peak_kind": peak_kind,
                      "us_per_launch": round(ms_l * 1e3 / len(layer_calls), 3),

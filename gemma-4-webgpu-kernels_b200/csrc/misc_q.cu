@@ -5,6 +5,8 @@
 
 #include <type_traits>
 
+#include <algorithm>
+
 #include "gq_internal.cuh"
 
 namespace {
@@ -125,33 +127,40 @@ __global__ void embed_quad_kernel(QView q, const uint32_t *ids, int64_t t, float
 // (q * s) * emb as embed_quad_kernel and the CPU (bit-identical).
 // Requires D % 4 == 0, group == D or a power of two >= 4, 16-byte aligned output
 // rows, and packed rows aligned to one lane's load.
+// A row may be split over wpr warps (contiguous ranges of spw 128-column steps), so
+// that few rows (a decode step's one token, or 4096 rows on 148 SMs) still put
+// enough warps and bytes in flight on every SM.
 template <int BITS, bool SIGNED>
 __global__ void __launch_bounds__(256) embed_row_kernel(QView q, const uint32_t *ids, int64_t t, float emb,
-                                                        float *out, uint32_t *err) {
+                                                        float *out, uint32_t *err, int wpr, int spw) {
   gqd::griddep_wait();
   gqd::griddep_launch_dependents();
   const int lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int64_t gw = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int64_t row = gw / wpr;
   if (row >= t) return;
+  const int part = (int)(gw - row * wpr);
   const uint32_t id = __ldg(ids + row);
   float *orow = out + row * q.k;
   const int64_t D = q.k;
+  const int64_t cbeg = (int64_t)part * spw * 128, cend = min(D, cbeg + (int64_t)spw * 128);
   if ((int64_t)id >= q.n) {
-    for (int64_t c = 4 * lane; c < D; c += 128) __stcs(reinterpret_cast<float4 *>(orow + c), make_float4(0.f, 0.f, 0.f, 0.f));
-    if (lane == 0) gqd::report(err, GQ_DEVERR_BAD_ID);
+    for (int64_t c = cbeg + 4 * lane; c < cend; c += 128)
+      __stcs(reinterpret_cast<float4 *>(orow + c), make_float4(0.f, 0.f, 0.f, 0.f));
+    if (lane == 0 && part == 0) gqd::report(err, GQ_DEVERR_BAD_ID);
     return;
   }
   const uint8_t *rp = q.bytes + (int64_t)id * q.row_bytes;
   const float *sr = q.scales + (int64_t)id * q.scale_stride;
   const int gshift = (q.group == q.k) ? 63 : (31 - __clz((int)q.group));  // group is a power of two here
   constexpr int U = 8;  // 128-column steps per lane in flight: all loads first, then the stores
-  for (int64_t c0 = 4 * lane; c0 < D; c0 += 128 * U) {
+  for (int64_t c0 = cbeg + 4 * lane; c0 < cend; c0 += 128 * U) {
     uint32_t w[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int64_t c = c0 + 128 * u;
       w[u] = 0;
-      if (c < D) {
+      if (c < cend) {
         if constexpr (BITS == 8) w[u] = __ldg(reinterpret_cast<const uint32_t *>(rp + c));
         else if constexpr (BITS == 4) w[u] = __ldg(reinterpret_cast<const uint16_t *>(rp + (c >> 1)));
         else w[u] = __ldg(rp + (c >> 2));
@@ -160,7 +169,7 @@ __global__ void __launch_bounds__(256) embed_row_kernel(QView q, const uint32_t 
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int64_t c = c0 + 128 * u;
-      if (c >= D) break;
+      if (c >= cend) break;
       int32_t cd[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
@@ -269,17 +278,29 @@ int gq_embed_launch(gq_ctx *ctx, const gq_qweight *w, const uint32_t *ids, int64
   const int64_t g = w->group_size;
   const bool row_path = w->k % 4 == 0 && ((uintptr_t)out % 16 == 0) && (g == w->k || (g >= 4 && (g & (g - 1)) == 0)) &&
                         (uintptr_t)w->bytes % 4 == 0 && w->row_bytes % (w->signed_i8 || w->bits == 8 ? 4 : (w->bits == 4 ? 2 : 1)) == 0 &&
-                        t <= (int64_t)0x7fffffff * 8;
+                        t <= (int64_t)0x7fffffff;
   if (row_path) {
-    const unsigned blocks = (unsigned)((t + 7) / 8);
+    // warps per row: enough warps for ~48 per SM (three quarters of the SM's warp
+    // slots), each keeping at least two 128-column steps
+    const int64_t steps = (w->k + 127) / 128;
+    int64_t wpr = ((int64_t)ctx->num_sms * 48 + t - 1) / t;
+    wpr = std::max<int64_t>(1, std::min<int64_t>(wpr, (steps + 1) / 2));
+    const int spw = (int)((steps + wpr - 1) / wpr);
+    wpr = (steps + spw - 1) / spw;  // no empty part
+    const unsigned blocks = (unsigned)((t * wpr + 7) / 8);
+    const int iw = (int)wpr;
     if (w->signed_i8)
-      GQ_CUDA_TRY(ctx, gq_launch(ctx, embed_row_kernel<8, true>, dim3(blocks), dim3(256), 0, q, ids, t, emb, out, ctx->dev_err));
+      GQ_CUDA_TRY(ctx, gq_launch(ctx, embed_row_kernel<8, true>, dim3(blocks), dim3(256), 0, q, ids, t, emb, out,
+                                 ctx->dev_err, iw, spw));
     else if (w->bits == 8)
-      GQ_CUDA_TRY(ctx, gq_launch(ctx, embed_row_kernel<8, false>, dim3(blocks), dim3(256), 0, q, ids, t, emb, out, ctx->dev_err));
+      GQ_CUDA_TRY(ctx, gq_launch(ctx, embed_row_kernel<8, false>, dim3(blocks), dim3(256), 0, q, ids, t, emb, out,
+                                 ctx->dev_err, iw, spw));
     else if (w->bits == 4)
-      GQ_CUDA_TRY(ctx, gq_launch(ctx, embed_row_kernel<4, false>, dim3(blocks), dim3(256), 0, q, ids, t, emb, out, ctx->dev_err));
+      GQ_CUDA_TRY(ctx, gq_launch(ctx, embed_row_kernel<4, false>, dim3(blocks), dim3(256), 0, q, ids, t, emb, out,
+                                 ctx->dev_err, iw, spw));
     else
-      GQ_CUDA_TRY(ctx, gq_launch(ctx, embed_row_kernel<2, false>, dim3(blocks), dim3(256), 0, q, ids, t, emb, out, ctx->dev_err));
+      GQ_CUDA_TRY(ctx, gq_launch(ctx, embed_row_kernel<2, false>, dim3(blocks), dim3(256), 0, q, ids, t, emb, out,
+                                 ctx->dev_err, iw, spw));
     return GQ_OK;
   }
   const bool quad = (w->k % 4 == 0) && ((uintptr_t)out % 16 == 0) &&
