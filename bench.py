@@ -70,10 +70,12 @@ class DecodeStep:
     stack_qkv: a KV layer's q, k and v projections as one stacked GEMV, as the
     decoder runs them (False: the separate config-2 sweep shapes)."""
 
-    def __init__(self, g, m: int, seed: int, with_lm_head: bool = True, stack_qkv: bool = True, lm_shard=None):
+    def __init__(self, g, m: int, seed: int, with_lm_head: bool = True, stack_qkv: bool = True, lm_shard=None,
+                 use_chain=None):
         """lm_shard=(rank, world): the lm_head split by vocab rows over the ranks through
         the fused sharded lm_head (gq.parallel.PeerLmHead, device barrier); a graph of
-        the step then holds two steps, one per logits buffer."""
+        the step then holds two steps, one per logits buffer. use_chain: run the
+        per-layer calls as one decode chain (default: at m = 1)."""
         import torch
         from gq import synth
 
@@ -93,6 +95,7 @@ class DecodeStep:
         self.ple = f32(m, synth.LAYERS * synth.PLE_DIM)
         self.keep = []
         self.calls = []   # (label, fn, args, bytes)
+        self.chain_ops = []  # the same per-layer calls as decode-chain ops (m = 1)
         self.bytes = 0
         self.host_weights = {}
         wseed = seed * 1000
@@ -126,15 +129,19 @@ class DecodeStep:
                     if i in (0, 4):
                         self.host_weights[(i, p.name, 1)] = (payload2.cpu().numpy(), scales2, p)
                     self.keep.append(t2)
+                    self.chain_ops.append((1, t, t2, x.data_ptr(), y.data_ptr(), None, 0, 0.0))
                     self.calls.append((p.name, lib.gq_linear_geglu,
                                        (ctx, c_void_p(x.data_ptr()), m, p.k, c_void_p(t.qw), c_void_p(t2.qw),
                                         c_void_p(y.data_ptr())), b, p))
                 elif p.mode == 2:
+                    self.chain_ops.append((2, t, None, x.data_ptr(), y.data_ptr(), self.ple.data_ptr(),
+                                           i * synth.PLE_DIM, 0.0))
                     self.calls.append((p.name, lib.gq_linear_gelu_mul_cols,
                                        (ctx, c_void_p(x.data_ptr()), m, p.k, c_void_p(t.qw),
                                         c_void_p(self.ple.data_ptr()), self.ple.shape[1], i * synth.PLE_DIM,
                                         c_void_p(y.data_ptr())), b, p))
                 else:
+                    self.chain_ops.append((0, t, None, x.data_ptr(), y.data_ptr(), None, 0, 0.0))
                     self.calls.append((p.name, lib.gq_linear,
                                        (ctx, c_void_p(x.data_ptr()), m, p.k, c_void_p(t.qw), c_void_p(y.data_ptr())),
                                        b, p))
@@ -171,7 +178,16 @@ class DecodeStep:
                                 c_void_p(self.logits.data_ptr()), p.n, 0), b, p))
             self.last_out = self.logits
         self.steps_per_graph = 2 if self.peer is not None else 1
-        self.launches = len(self.calls)  # per step
+        self.layer_calls = [c for c in self.calls if not c[0].startswith("lm_head")]
+        self.head_calls = [c for c in self.calls if c[0].startswith("lm_head")]
+        # GQ_BENCH_CHAIN=1: at one activation row, the per-layer calls run as one decode
+        # chain (gq_chain, a single persistent launch) instead of one launch per call
+        self.chain = None
+        if use_chain is None:
+            use_chain = m == 1 and os.environ.get("GQ_BENCH_CHAIN", "0") == "1"
+        if use_chain:
+            self.chain = g.chain(self.chain_ops)
+        self.launches = (1 if self.chain is not None else len(self.layer_calls)) + len(self.head_calls)  # per step
 
     def _exec(self, calls):
         for label, fn, args, _, _ in calls:
@@ -179,14 +195,21 @@ class DecodeStep:
             if rc != 0:
                 self.g._check(rc, label)
 
+    def run_layers(self):
+        """The per-layer projections only (everything but the lm_head)."""
+        if self.chain is not None:
+            self.chain.run()
+        else:
+            self._exec(self.layer_calls)
+
     def run(self):
         """One step (with a sharded lm_head: two steps, one per logits buffer)."""
         if self.peer is None:
-            self._exec(self.calls)
+            self.run_layers()
+            self._exec(self.head_calls)
             return
-        layers = [c for c in self.calls if not c[0].startswith("lm_head")]
         for par in (0, 1):
-            self._exec(layers)
+            self.run_layers()
             self._exec(self.lm_pair[par])
 
     run_graph_body = run
@@ -195,15 +218,9 @@ class DecodeStep:
         if self.peer is not None:
             self.peer.close()
             self.peer = None
-
-    def run_layers(self):
-        """The per-layer projections only (everything but the lm_head)."""
-        for label, fn, args, _, _ in self.calls:
-            if label.startswith("lm_head"):
-                continue
-            rc = fn(*args)
-            if rc != 0:
-                self.g._check(rc, label)
+        if self.chain is not None:
+            self.chain.close()
+            self.chain = None
 
 
 def cuda_events_time(torch, stream, fn, iters):
@@ -415,20 +432,27 @@ def run_gq(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_e2e = float(t.item())
 
-    # Roofline of the dominant kernel family: the per-layer MATMUL_Q launches
-    # (CUDA-core gemv_q_kernel, ~95% of the step's device time), recorded as a
-    # graph of their own and replayed back to back exactly as inside the step;
-    # CUDA events on the context stream bracket the replays.
-    graph_l = g.record(step.run_layers)
-    for _ in range(3):
-        g.replay(graph_l)
-    g.flush()
+    # Roofline of the dominant kernel: the per-layer MATMUL_Q calls (all of the
+    # step but the lm_head) -- one decode-chain launch (chain_kernel) at m = 1,
+    # else one GEMV launch per call -- recorded as a graph of their own and
+    # replayed back to back exactly as inside the step; CUDA events on the
+    # context stream bracket the replays.
+    def time_graph(body, reps):
+        gr = g.record(body)
+        for _ in range(3):
+            g.replay(gr)
+        g.flush()
+        ms_ = cuda_events_time(torch, stream, lambda: g.replay(gr), reps) / reps
+        g.destroy_graph(gr)
+        return ms_
+
     reps_l = max(20, min(args.steps, 200))
-    ms_l = cuda_events_time(torch, stream, lambda: g.replay(graph_l), reps_l) / reps_l
-    g.destroy_graph(graph_l)
-    layer_calls = [c for c in step.calls if not c[0].startswith("lm_head")]
+    ms_l = time_graph(step.run_layers, reps_l)
+    layer_calls = step.layer_calls
     layer_bytes = sum(c[3] for c in layer_calls)
     achieved = layer_bytes / (ms_l / 1e3) / 1e9
+    # the same calls as one dependent GEMV launch each (programmatic dependent launch)
+    ms_launches = time_graph(lambda: step._exec(layer_calls), reps_l) if step.chain is not None else ms_l
 
     # per-launch durations with events around each launch (no overlap between
     # launches; an upper bound on each launch's time), grouped by weight kind
@@ -482,15 +506,21 @@ def run_gq(args):
                 "ms_per_step": round(ms_e2e, 5), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": step.launches * step.steps_per_graph * args.steps,
         "roofline": {"bound": "hbm",
-                     "kernel": f"gemv_q_kernel + gemv_r1_kernel (CUDA-core decode GEMVs): the {len(layer_calls)} "
-                               f"per-layer MATMUL_Q launches of the step, graph-replayed back to back "
-                               f"({layer_bytes} algorithmic B per replay)",
-                     "floor": "a dependent launch with no MAC work costs 2.09 us on this GPU "
-                              "(tests/native/chain_latency.cu): 210 launches >= 0.44 ms, i.e. <= 1.65 TB/s "
-                              "(25 % of measured HBM) for this family at batch 1",
+                     "kernel": (f"chain_kernel (decode chain): ONE persistent launch running the "
+                                f"{len(layer_calls)} per-layer MATMUL_Q calls of the step in order, each waiting "
+                                f"for the one before it ({layer_bytes} algorithmic B per launch)")
+                     if step.chain is not None else
+                     (f"gemv_q_kernel + gemv_r1_kernel (CUDA-core decode GEMVs): the {len(layer_calls)} "
+                      f"per-layer MATMUL_Q launches of the step, graph-replayed back to back "
+                      f"({layer_bytes} algorithmic B per replay)"),
                      "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                      "frac": round(achieved / hbm_peak, 4), "peak_kind": peak_kind,
-                     "us_per_launch": round(ms_l * 1e3 / len(layer_calls), 3),
+                     "us_per_call": round(ms_l * 1e3 / len(layer_calls), 3),
+                     "one_launch_per_call": {
+                         "GB/s": round(layer_bytes / (ms_launches / 1e3) / 1e9, 1),
+                         "us_per_launch": round(ms_launches * 1e3 / len(layer_calls), 3),
+                         "floor": "a dependent launch with no MAC work costs 2.09 us on this GPU "
+                                  "(tests/native/chain_latency.cu): 210 launches >= 0.44 ms, i.e. <= 1.65 TB/s"},
                      "traffic": traffic, "traffic_case": traffic_note,
                      "per_kind_isolated": {k: {"GB/s": round(v[0] / (v[1] / 1e3) / 1e9, 1), "launches": v[2],
                                                "ms": round(v[1], 4)} for k, v in sorted(by_kind.items())}},

@@ -11,6 +11,8 @@
 
 namespace {
 
+constexpr int64_t kEmbedWarpsPerSm = 16;  // embed_row_kernel: row splitting stops above this
+
 // Integer code of element [n, k]: rust/src/backend.rs:46-54 (offset binary for
 // sub-byte and unsigned 8-bit payloads, two's complement for I8).
 __device__ __forceinline__ int32_t code_at(const uint8_t *bytes, int64_t row_bytes, int bits,
@@ -280,10 +282,12 @@ int gq_embed_launch(gq_ctx *ctx, const gq_qweight *w, const uint32_t *ids, int64
                         (uintptr_t)w->bytes % 4 == 0 && w->row_bytes % (w->signed_i8 || w->bits == 8 ? 4 : (w->bits == 4 ? 2 : 1)) == 0 &&
                         t <= (int64_t)0x7fffffff;
   if (row_path) {
-    // warps per row: enough warps for ~48 per SM (three quarters of the SM's warp
-    // slots), each keeping at least two 128-column steps
+    // warps per row: split a row only when the rows alone give fewer than ~16 warps
+    // per SM (each warp keeps U = 8 steps of loads in flight; at 4096 rows of the
+    // PLE table a second warp per row measured slower), each part keeping at
+    // least two 128-column steps
     const int64_t steps = (w->k + 127) / 128;
-    int64_t wpr = ((int64_t)ctx->num_sms * 48 + t - 1) / t;
+    int64_t wpr = ((int64_t)ctx->num_sms * kEmbedWarpsPerSm + t - 1) / t;
     wpr = std::max<int64_t>(1, std::min<int64_t>(wpr, (steps + 1) / 2));
     const int spw = (int)((steps + wpr - 1) / wpr);
     wpr = (steps + spw - 1) / spw;  // no empty part

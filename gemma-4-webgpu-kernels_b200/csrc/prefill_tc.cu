@@ -742,17 +742,17 @@ int gq_prefill_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq
       encode_weight_map(&mw2, w2 ? w2->bytes : w->bytes, w->n, w->row_bytes, w->bits, ow) != CUDA_SUCCESS)
     return gq_fail(ctx, GQ_ERR_CUDA, "prefill: weight tensor map");
   dim3 grid((unsigned)((m + nt - 1) / nt), (unsigned)((w->n + ow - 1) / ow));
-  // Split K over a cluster of up to 8 CTAs when the output tiles leave SMs idle (the
-  // 2-bit down projection of config 3 has 24 tiles on 148 SMs), keeping at least 8
-  // stages per split; the splits' fp32 partials are added over distributed shared
-  // memory in a fixed order (deterministic).
+  // Split K over a cluster of 2, 4 or 8 CTAs when the output tiles leave SMs idle
+  // (the 2-bit down projection of config 3 has 24 tiles on 148 SMs): the largest
+  // power of two that keeps the grid within one wave and >= 3 stages per split.
+  // Measured on B200 at the E2B shapes (M = 128..512): one wave beats two, and
+  // clusters of 3, 5 or 6 CTAs run slower than the power of two below them. The
+  // splits' fp32 partials are added over distributed shared memory in a fixed
+  // order (deterministic).
   const int kt_all = (int)(K / BK);
   const int tiles = (int)(grid.x * grid.y);
   int ks = 1;
-  if (tiles < ctx->num_sms && grid.y <= 65535) {
-    ks = std::min(8, ctx->num_sms / tiles);
-    while (ks > 1 && kt_all / ks < 8) --ks;
-  }
+  while (ks < 8 && (int64_t)tiles * ks * 2 <= ctx->num_sms && kt_all / (ks * 2) >= 3) ks *= 2;
   if (const char *e = getenv("GQ_PREFILL_KSPLIT")) {  // explicit split (tuning and tests): 1..8
     const int v = atoi(e);
     if (v >= 1 && v <= 8) ks = std::min(v, kt_all);

@@ -113,6 +113,27 @@ class KvAppend:
     dead: Optional[GqTensor] = None
 
 
+class Chain:
+    """A created decode chain (gq_chain): run() enqueues it on the backend's
+    stream (recordable into a graph), reset() clears its counters after a
+    timed-out run, close() frees it."""
+
+    def __init__(self, backend: "CudaBackend", handle: c_void_p):
+        self.backend = backend
+        self.handle = handle
+
+    def run(self) -> None:
+        self.backend._check(self.backend.lib.gq_chain_run(self.handle), "chain_run")
+
+    def reset(self) -> None:
+        self.backend._check(self.backend.lib.gq_chain_reset(self.handle), "chain_reset")
+
+    def close(self) -> None:
+        if self.handle is not None and self.handle.value:
+            self.backend.lib.gq_chain_destroy(self.handle)
+        self.handle = None
+
+
 class CudaBackend:
     """The Backend-trait surface of the quantized hot path, on one CUDA device."""
 
@@ -198,6 +219,21 @@ class CudaBackend:
 
     def destroy_graph(self, graph) -> None:
         self.lib.gq_graph_destroy(graph)
+
+    # ---- decode chains (include/gq.h gq_chain_*) ------------------------------------
+    def chain(self, ops) -> "Chain":
+        """A decode chain over `ops`: tuples (mode, w, w2, x, y, b, b_offset, cap)
+        with w/w2 quantized GqTensors (w2 None unless mode 1), x/y/b device
+        pointers (int) or f32 GqTensors (b None unless mode 2). One activation row
+        per op; `Chain.run()` issues them all as one launch."""
+        arr = (_abi.ChainOp * len(ops))()
+        for i, (mode, w, w2, x, y, b, b_off, cap) in enumerate(ops):
+            ptr = lambda t: None if t is None else (t if isinstance(t, int) else t.ptr())
+            arr[i] = _abi.ChainOp(int(mode), c_void_p(w.qw), c_void_p(w2.qw if w2 is not None else None),
+                                  c_void_p(ptr(x)), c_void_p(ptr(y)), c_void_p(ptr(b)), int(b_off), float(cap))
+        out = c_void_p()
+        self._check(self.lib.gq_chain_create(self.ctx, arr, len(ops), ctypes.byref(out)), "chain_create")
+        return Chain(self, out)
 
     # ---- construction (rust/src/backend.rs:94-98) ----------------------------
     def tensor(self, data, shape: Sequence[int]) -> GqTensor:

@@ -28,6 +28,12 @@ class SampleOpts(ctypes.Structure):
     _fields_ = [("temperature", c_float), ("top_k", c_int32), ("top_p", c_float), ("repetition_penalty", c_float)]
 
 
+class ChainOp(ctypes.Structure):
+    """gq_chain_op (include/gq.h): one one-row MATMUL_Q call of a decode chain."""
+    _fields_ = [("mode", c_int32), ("w", c_void_p), ("w2", c_void_p), ("x", c_void_p), ("y", c_void_p),
+                ("b", c_void_p), ("b_offset", c_int64), ("cap", c_float)]
+
+
 class GqError(RuntimeError):
     """A non-zero status from libgq (the Rust trait would panic here)."""
 
@@ -89,6 +95,10 @@ SIGNATURES = {
                 c_int32, c_void_p, c_void_p, c_int32]),
     "gq_peer_wait": (c_int, [c_void_p, c_void_p, c_int32, c_void_p]),
     "gq_ctx_set_wait_limit": (c_int, [c_void_p, c_uint64]),
+    "gq_chain_create": (c_int, [c_void_p, c_void_p, c_int32, POINTER(c_void_p)]),
+    "gq_chain_run": (c_int, [c_void_p]),
+    "gq_chain_reset": (c_int, [c_void_p]),
+    "gq_chain_destroy": (c_int, [c_void_p]),
     "gq_argmax_rows": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p, c_void_p]),
     "gq_sample_rows": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_int64, c_int64,
                                c_void_p, c_void_p]),

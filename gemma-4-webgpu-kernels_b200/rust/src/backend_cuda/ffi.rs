@@ -23,6 +23,25 @@ pub struct GqGraph {
 pub struct GqStFile {
     _p: [u8; 0],
 }
+#[repr(C)]
+pub struct GqChain {
+    _p: [u8; 0],
+}
+/// gq_chain_op: one one-row MATMUL_Q call of a decode chain (mode 0 linear,
+/// 1 linear_geglu with `w2` = up, 2 linear_gelu_mul_cols over `b[b_offset..]`,
+/// 3 soft-capped linear).
+#[repr(C)]
+#[derive(Clone, Copy, Debug)]
+pub struct GqChainOp {
+    pub mode: i32,
+    pub w: *const GqQWeight,
+    pub w2: *const GqQWeight,
+    pub x: *const f32,
+    pub y: *mut f32,
+    pub b: *const f32,
+    pub b_offset: i64,
+    pub cap: f32,
+}
 /// gq_sample_opts: the fields of the reference's SampleOpts (src/sampler.rs:29-39).
 #[repr(C)]
 #[derive(Clone, Copy, Debug)]
@@ -55,6 +74,11 @@ extern "C" {
     pub fn gq_ctx_get_stream(ctx: *mut GqCtx) -> *mut c_void;
     pub fn gq_ctx_num_sms(ctx: *mut GqCtx) -> c_int;
     pub fn gq_ctx_set_wait_limit(ctx: *mut GqCtx, limit_ns: u64) -> c_int;
+    // decode chains: consecutive one-row linear calls in one persistent launch
+    pub fn gq_chain_create(ctx: *mut GqCtx, ops: *const GqChainOp, n_ops: i32, out: *mut *mut GqChain) -> c_int;
+    pub fn gq_chain_run(chain: *mut GqChain) -> c_int;
+    pub fn gq_chain_reset(chain: *mut GqChain) -> c_int;
+    pub fn gq_chain_destroy(chain: *mut GqChain) -> c_int;
     pub fn gq_last_error(ctx: *mut GqCtx) -> *const c_char;
     // sync / memory (Backend::{tensor, zeros, readback, flush, free_tensor})
     pub fn gq_sync(ctx: *mut GqCtx) -> c_int;

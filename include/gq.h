@@ -187,13 +187,53 @@ int gq_linear_softcap_peers_sync(gq_ctx *ctx, const float *x, int64_t m, int64_t
  * gq_sync) and returns; the context stays usable. */
 int gq_peer_wait(gq_ctx *ctx, const uint32_t *flags, int32_t world, const uint32_t *sync);
 
-/* Bound of the cross-GPU waits of this context (gq_peer_wait), in nanoseconds,
- * 1 ms .. 60 s; applies to waits enqueued afterwards (a captured graph keeps the
- * bound it was recorded with). The failure detector of a multi-GPU caller: a
- * rank that dies or stalls makes its peers' waits end with
- * GQ_DEVERR_WAIT_TIMEOUT after this long instead of hanging their GPUs. No
- * counterpart in the reference (single device). */
+/* Bound of the cross-GPU waits of this context (gq_peer_wait) and of the
+ * inter-CTA waits of a decode chain (gq_chain_run), in nanoseconds, 1 ms .. 60 s;
+ * applies to waits enqueued afterwards (a captured graph keeps the bound it was
+ * recorded with). The failure detector of a multi-GPU caller: a rank that dies
+ * or stalls makes its peers' waits end with GQ_DEVERR_WAIT_TIMEOUT after this
+ * long instead of hanging their GPUs. No counterpart in the reference (single
+ * device). */
 int gq_ctx_set_wait_limit(gq_ctx *ctx, uint64_t limit_ns);
+
+/* ---- decode chains: consecutive one-row MATMUL_Q calls in one launch.
+ * The reference records each call as its own dispatch in one compute pass
+ * (rust/src/backend_wgpu.rs:311-367, :768-835); a chain gives the results of
+ * issuing its ops one after another on the context's stream (each op may read
+ * what the ops before it wrote), from a single persistent kernel that streams
+ * the weights of later ops while earlier ones wait for their inputs. Every op
+ * has ONE activation row (m = 1): x is [k] and y is [w.n], device pointers fixed
+ * when the chain is created (bind the decode step's buffers once). Modes:
+ *   0  gq_linear                       y = x · deq(W)ᵀ
+ *   1  gq_linear_geglu                 y = gelu_tanh(x·Wᵀ) * (x·W2ᵀ)   (w2 = up)
+ *   2  gq_linear_gelu_mul_cols         y = gelu_tanh(x·Wᵀ) * b[b_offset + j]
+ *   3  gq_linear_softcap               y = cap·tanh((x·Wᵀ)/cap), cap <= 0: none
+ * Requirements (GQ_ERR_UNSUPPORTED otherwise): one scale per weight row
+ * (group_size = k), rows a whole number of 16 bytes, k a multiple of 4, x 16-byte
+ * aligned, a row that fits the kernel's 24 KB ring slot. y must not overlap the
+ * op's x or b (GQ_ERR_INVALID_ARGUMENT). Results agree with the single calls to
+ * the GEMV tolerance (the same dequantising arithmetic; sums grouped per CTA).
+ * One chain runs at a time per stream; all of its CTAs are resident at once (a
+ * cooperative launch of one CTA per SM). Waits between CTAs are bounded by the
+ * context's wait limit: a timeout reports GQ_DEVERR_WAIT_TIMEOUT at the next
+ * gq_sync, and the chain then needs gq_chain_reset before it runs again. A chain
+ * may be captured by gq_graph_begin/end; destroy it only after the last graph
+ * that holds it. No counterpart in the reference. */
+typedef struct gq_chain gq_chain;
+typedef struct gq_chain_op {
+  int32_t mode;
+  const gq_qweight *w;
+  const gq_qweight *w2; /* mode 1: the up weight (same shape and format as w) */
+  const float *x;       /* [w.k] */
+  float *y;             /* [w.n] */
+  const float *b;       /* mode 2: the columns b[b_offset .. b_offset + w.n) */
+  int64_t b_offset;
+  float cap;            /* mode 3 */
+} gq_chain_op;
+int gq_chain_create(gq_ctx *ctx, const gq_chain_op *ops, int32_t n_ops, gq_chain **out);
+int gq_chain_run(gq_chain *chain);
+int gq_chain_reset(gq_chain *chain);
+int gq_chain_destroy(gq_chain *chain);
 
 /* Greedy decoding over a vocab shard: for each of the m rows of x (row stride
  * ldx floats, 0 = n) the largest of its n values and the first column holding it
