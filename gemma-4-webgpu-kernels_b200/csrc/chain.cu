@@ -25,7 +25,7 @@
 //    the op, all of its ring slots at once spread over every warp, with the
 //    one-LOP3-one-FFMA dequant of gemv_core.cuh, the lane-group shuffle
 //    reduction and the MODE epilogue. After its last row store the CTA adds one
-//    to op j's counter.
+//    to op j's counter (a release reduction).
 //  * The counters return to zero at the end of every run (the last CTA to
 //    finish the last op clears them), so a captured graph replays the chain.
 //    Every wait is bounded (wall clock); a timeout sets an abort word that every
@@ -449,13 +449,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       // the CTA's rows of op j are stored: count it finished (release at GPU scope)
       named_sync();
       if (tid == 0) {
-        __threadfence();
-        const uint32_t prev = atomicAdd(state + kCounterStride * (j + 1), 1u);
-        if (j == nops - 1 && prev == (uint32_t)G - 1u && !aborted(&sh->abort, g_abort)) {
-          // every CTA is past all of its waits: clear the counters for the next run
-          fence_acq_rel();
-          for (int i = 1; i <= nops; ++i) state[kCounterStride * i] = 0u;
+        uint32_t *cnt = state + kCounterStride * (j + 1);
+        if (j < nops - 1) {  // a release reduction: no round trip on this CTA's path
+          asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(cnt), "r"(1u) : "memory");
+        } else {
           __threadfence();
+          const uint32_t prev = atomicAdd(cnt, 1u);
+          if (prev == (uint32_t)G - 1u && !aborted(&sh->abort, g_abort)) {
+            // every CTA is past all of its waits: clear the counters for the next run
+            fence_acq_rel();
+            for (int i = 1; i <= nops; ++i) state[kCounterStride * i] = 0u;
+            __threadfence();
+          }
         }
       }
     }

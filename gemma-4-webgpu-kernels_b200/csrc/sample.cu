@@ -383,20 +383,25 @@ __global__ void __launch_bounds__(kRowThreads) sample_row_kernel(const RowArgs a
     if (lane == 0) a.tokens[row] = tok;
     return;
   }
-  if (threadIdx.x != 0) return;
   if (a.mode == 0) {
-    a.tokens[row] = keys[0] ? (int32_t)ckey_col(keys[0]) : -1;
+    if (threadIdx.x == 0) a.tokens[row] = keys[0] ? (int32_t)ckey_col(keys[0]) : -1;
     return;
   }
-  // candidates, sorted; the reference's softmax_over / top-p / draw in its order
+  // candidates, sorted; the reference's softmax_over / top-p / draw in its order.
+  // Every candidate's exp is computed once, in parallel; the sums stay sequential.
+  __shared__ float exs[kSampleCap];
   int nc = a.top_k < n2 ? a.top_k : n2;
   while (nc > 0 && keys[nc - 1] == 0ull) --nc;  // padding (rows or shards shorter than k)
   if (nc == 0) {
-    a.tokens[row] = -1;
+    if (threadIdx.x == 0) a.tokens[row] = -1;
     return;
   }
   const float mx = vkey_value((uint32_t)(keys[0] >> 32));
-  auto ex = [&](int i) { return expf(__fmul_rn(vkey_value((uint32_t)(keys[i] >> 32)) - mx, s.inv_t)); };
+  for (int i = threadIdx.x; i < nc; i += blockDim.x)
+    exs[i] = expf(__fmul_rn(vkey_value((uint32_t)(keys[i] >> 32)) - mx, s.inv_t));
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  auto ex = [&](int i) { return exs[i]; };
   int keep = nc;
   if (a.top_p < 1.0f) {
     float denom = 0.0f;

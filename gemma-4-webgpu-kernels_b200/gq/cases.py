@@ -11,7 +11,7 @@ can select launches of that kernel by name and skip the warm-up:
   lm_head   I8 [262144, 1536] soft-capped GEMV, M = 1 (tensor-core gemv_tc_kernel)
   prefill   4-bit [6144, 1536] at M = 512 (cast_f16_kernel + prefill_tc_kernel)
   prefill_down  2-bit [1536, 6144] at M = 512, the config-3 down projection (K split
-            over 6-CTA clusters)
+            over 4-CTA clusters)
   embed     config 4: 4096 ids into the 4-bit token table and the I8 PLE table
   embed_small  the same 4096 gathers from 32768-row tables (0.3 GB on the device,
             outputs 172 MB > L2): the case for multi-pass profiler captures
@@ -21,6 +21,8 @@ can select launches of that kernel by name and skip the warm-up:
   tcx       8-row I8 GEMV [2048, 1536] (short-M tensor-core gemv_tcx_kernel)
   tcx_down  64-row 2-bit GEMV [1536, 6144], the batch-64 down projection (split-K
             over 4-CTA clusters)
+  sample    gq_sample_rows on --batch rows of 262144 logits, temperature 1, top-k 64,
+            top-p 0.95 (chunk top-k, chunk exp-sum, per-row candidate draw)
 
 Run from the package directory (or with it on PYTHONPATH).
 """
@@ -34,7 +36,7 @@ from ctypes import c_float, c_void_p
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("case", choices=["config1", "lm_head", "prefill", "prefill_down", "embed", "embed_small", "decode",
-                                     "attn", "tcx", "tcx_down"])
+                                     "attn", "tcx", "tcx_down", "sample"])
     ap.add_argument("--iters", type=int, default=8)
     ap.add_argument("--batch", type=int, default=1)
     ap.add_argument("--warmup", type=int, default=3)
@@ -117,6 +119,18 @@ def main(argv=None) -> int:
         y = torch.empty(64, 1536, device=dev)
         calls = [lambda: lib.gq_linear(ctx, c_void_p(x.data_ptr()), 64, 6144, c_void_p(w.qw),
                                        c_void_p(y.data_ptr()))]
+    elif args.case == "sample":
+        import ctypes
+
+        from . import _abi
+
+        m = args.batch
+        lg = torch.randn(m, synth.VOCAB, generator=gen, device=dev) * 3
+        st = torch.arange(1, m + 1, dtype=torch.int64, device=dev)
+        tok = torch.empty(m, dtype=torch.int32, device=dev)
+        opts = _abi.SampleOpts(1.0, 64, 0.95, 1.0)
+        calls = [lambda: lib.gq_sample_rows(ctx, c_void_p(lg.data_ptr()), m, synth.VOCAB, 0, ctypes.byref(opts),
+                                            None, 0, 0, c_void_p(st.data_ptr()), c_void_p(tok.data_ptr()))]
     else:
         rows = synth.VOCAB if args.case == "embed" else 32768
         tok = upload(rows, synth.HIDDEN, 4, False, 400)
