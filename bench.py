@@ -39,7 +39,10 @@ import numpy as np  # noqa: E402
 
 METRIC = "MATMUL_Q decode GB/s (E2B quantized decode step, M=1)"
 # completion barrier of the vocab-sharded lm_head in the N > 1 step (gq.parallel.PeerLmHead)
-LM_BARRIER = os.environ.get("GQ_BENCH_LM_BARRIER", "device")
+# completion of the fused sharded lm_head at N > 1: "fused" = the shard GEMV's last CTA
+# waits for every rank's flag (one launch), "device" = a separate one-thread wait
+# kernel, "nccl" = a 1-element all-reduce (measured at 2 GPUs: 0.8726 / 0.8741 ms per step)
+LM_BARRIER = os.environ.get("GQ_BENCH_LM_BARRIER", "fused")
 UNIT = "GB/s"
 
 
@@ -497,7 +500,7 @@ def run_gq(args):
                    "tokens_per_step": args.m, "lm_head": "i8 262144x1536 softcap 30",
                    "bits": "q/k/v/o/ple i8, gate+up 4-bit (geglu fused), down 2-bit",
                    "bytes_per_step": step.bytes, "l2": "weights 1.12 GB per step >> 126 MB L2; no flush",
-                   "parallelism": (f"lm_head vocab-sharded x{world} (fused NVLink all-gather, device barrier), "
+                   "parallelism": (f"lm_head vocab-sharded x{world} (fused NVLink all-gather, {LM_BARRIER} barrier), "
                                    "trunk replicated") if world > 1 else "single"},
         "matmul_q_only_tokens_per_s": round(args.m / (ms_max / 1e3), 1),
         "frac_of_measured_hbm": round(value / world / hbm_peak, 4),

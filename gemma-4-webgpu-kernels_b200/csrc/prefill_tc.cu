@@ -654,6 +654,17 @@ CUresult encode_weight_map(CUtensorMap *map, const uint8_t *w, int64_t n, int64_
 }
 
 // Tensor map over the f16 activations [m, k], box nt rows x 64 halves, 128-byte swizzle.
+// Tokens per tile (the MMA N): 256, or 128 for short prefills. GQ_PREFILL_NT
+// (64, 128, 192 or 256: a multiple of 64, the epilogue's drain step per half)
+// overrides it for tuning and tests.
+int token_tile(int64_t m) {
+  if (const char *e = getenv("GQ_PREFILL_NT")) {
+    const int v = atoi(e);
+    if (v == 64 || v == 128 || v == 192 || v == 256) return v;
+  }
+  return m > 128 ? NT_MAX : 128;
+}
+
 CUresult encode_x_map(CUtensorMap *map, const __half *xh, int64_t m, int64_t k, int nt) {
   cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)m};
   cuuint64_t strides[1] = {(cuuint64_t)k * 2};
@@ -716,7 +727,7 @@ int gq_prefill_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq
   __half *xh = static_cast<__half *>(wsp);
   int *xexp = reinterpret_cast<int *>(static_cast<uint8_t *>(wsp) + xh_bytes);
   GQ_CUDA_TRY(ctx, cast_any(w->bits, ctx->stream, ctx->pdl, x, xh, xexp, m, K));
-  const int nt = m > 128 ? NT_MAX : 128;
+  const int nt = token_tile(m);
   CUtensorMap map;
   if (encode_x_map(&map, xh, m, K, nt) != CUDA_SUCCESS)
     return gq_fail(ctx, GQ_ERR_CUDA, "prefill: activation tensor map");
@@ -862,7 +873,7 @@ extern "C" int gq_linear_prefill_static(void *cuda_stream, const float *x, int64
   __half *xh = static_cast<__half *>(st->scratch);
   int *xexp = static_cast<int *>(st->xexp);
   if (cast_any(bits, stream, false, x, xh, xexp, m, k) != cudaSuccess) return GQ_ERR_CUDA;
-  const int nt = m > 128 ? NT_MAX : 128;
+  const int nt = token_tile(m);
   CUtensorMap map;
   if (encode_x_map(&map, xh, m, k, nt) != CUDA_SUCCESS) return GQ_ERR_CUDA;
   PrefillArgs a = {};

@@ -88,6 +88,81 @@ __device__ void bitonic_desc(uint64_t *k, int n) {
   __syncthreads();
 }
 
+// The k largest of n distinct-or-zero 64-bit keys in shared memory, all threads:
+// radix select over eight 8-bit digits from the top (a histogram of the keys
+// still matching the selected prefix, counts aggregated per warp with
+// match.any, the bin holding the k-th largest found from the top by one warp's
+// scan), then every key above the k-th and enough copies of it go to out[0..k)
+// unsorted. Zero keys (padding) are the only repeats and rank last.
+__device__ void select_top(const uint64_t *keys, int n, int k, uint64_t *out) {
+  __shared__ uint32_t hist[2][256];  // double-buffered: pass p counts into hist[p & 1]
+  __shared__ unsigned long long s_prefix;
+  __shared__ uint32_t s_need, s_count, s_ties;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  uint64_t prefix = 0ull, mask = 0ull;
+  uint32_t need = (uint32_t)k;
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[0][i] = 0u;
+  __syncthreads();
+  for (int shift = 56, p = 0; shift >= 0; shift -= 8, ++p) {
+    uint32_t *h = hist[p & 1];
+    for (int base = warp * 32; base < n; base += nw * 32) {
+      const int i = base + lane;
+      const uint64_t kk = i < n ? keys[i] : 0ull;
+      const bool live = i < n && (kk & mask) == prefix;
+      const uint32_t bin = live ? (uint32_t)(kk >> shift) & 255u : 256u;
+      const unsigned peers = __match_any_sync(0xffffffffu, bin);
+      if (live && lane == __ffs(peers) - 1) atomicAdd(&h[bin], (uint32_t)__popc(peers));
+    }
+    __syncthreads();
+    if (warp == 0) {
+      // lane l owns bins 255-8l .. 248-8l; counts from the top; the other
+      // histogram is cleared for the next pass meanwhile
+      uint32_t cnt[8], tot = 0;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        cnt[q] = h[255 - 8 * lane - q];
+        tot += cnt[q];
+        hist[(p + 1) & 1][8 * lane + q] = 0u;
+      }
+      uint32_t incl = tot;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += t;
+      }
+      const uint32_t excl = incl - tot;
+      if (excl < need && incl >= need) {
+        uint32_t acc = excl;
+        int q = 0;
+        for (; q < 8; ++q) {
+          if (acc + cnt[q] >= need) break;
+          acc += cnt[q];
+        }
+        s_prefix = prefix | ((unsigned long long)(255u - 8u * lane - (uint32_t)q) << shift);
+        s_need = need - acc;
+      }
+      if (shift == 0 && lane == 0) {
+        s_count = 0u;
+        s_ties = 0u;
+      }
+    }
+    __syncthreads();
+    prefix = s_prefix;
+    need = s_need;
+    mask |= 255ull << shift;
+  }
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const uint64_t kk = keys[i];
+    bool take = kk > prefix;
+    if (kk == prefix) take = atomicAdd(&s_ties, 1u) < need;
+    if (take) {
+      const uint32_t slot = atomicAdd(&s_count, 1u);
+      if (slot < (uint32_t)k) out[slot] = kk;
+    }
+  }
+  __syncthreads();
+}
+
 struct SampleArgs {
   const float *logits;
   int64_t m, n, ld;       // rows, columns, row stride (floats)
@@ -323,8 +398,24 @@ __global__ void __launch_bounds__(kRowThreads) sample_row_kernel(const RowArgs a
   while (n2 < total) n2 <<= 1;
   uint64_t *keys = reinterpret_cast<uint64_t *>(smem);
   uint8_t *pen = smem + (size_t)n2 * 8;
+  uint64_t *sel = reinterpret_cast<uint64_t *>(pen + kChunk);  // [kSampleCap]
   for (int i = threadIdx.x; i < n2; i += blockDim.x) keys[i] = i < total ? s.ckeys[row * total + i] : 0ull;
-  if (n2 > 1) bitonic_desc(keys, n2);
+  // candidates in descending order: sort them all when few, else select the
+  // top_k first and sort only those
+  const int want = (a.mode == 1 || (a.cand_val && a.cand_idx)) ? a.top_k : 1;
+  if (want >= 1 && want <= kSampleCap && total > 4 * want && total > 256) {
+    __syncthreads();
+    int w2 = 1;
+    while (w2 < want) w2 <<= 1;
+    for (int i = threadIdx.x; i < w2; i += blockDim.x) sel[i] = 0ull;
+    __syncthreads();
+    select_top(keys, total, want, sel);
+    bitonic_desc(sel, w2);
+    keys = sel;
+    n2 = w2;
+  } else if (n2 > 1) {
+    bitonic_desc(keys, n2);
+  }
   __syncthreads();
   if (a.cand_val && a.cand_idx) {  // merged candidates out (no sampling)
     for (int i = threadIdx.x; i < a.top_k; i += blockDim.x) {
@@ -488,7 +579,7 @@ int sample_prepare(gq_ctx *ctx, const float *logits, int64_t m, int64_t n, int64
 size_t row_smem(const SampleArgs &a) {
   size_t n2 = 1;
   while (n2 < (size_t)a.nchunks * a.k) n2 <<= 1;
-  return n2 * 8 + kChunk;
+  return n2 * 8 + kChunk + kSampleCap * 8;
 }
 
 int launch_rows(gq_ctx *ctx, const RowArgs &r) {

@@ -304,7 +304,7 @@ class Decoder:
                 del payload
             self.w["lm_head"] = shard
             self.peer = PeerLmHead(g, shard, c.vocab, rank, world, max_m=batch, cap=c.lm_softcap, group=group,
-                                   barrier="device")
+                                   barrier="fused")
         for i in range(L):
             dh = c.dh(i)
             p = f"l{i}."
@@ -496,7 +496,7 @@ class Decoder:
 
     @property
     def launches(self) -> int:
-        return len(self._calls) + (2 if self.peer is not None else 0)
+        return len(self._calls) + (len(self._lm_calls[0]) if self.peer is not None else 0)
 
     def labels(self) -> List[str]:
         return [c[0] for c in self._calls]

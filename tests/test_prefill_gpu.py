@@ -91,7 +91,7 @@ def test_prefill_reference_tile_sizes(g):
 def test_prefill_split_k_over_a_cluster(g, m, n, k, bits, mode):
     """Grids with fewer output tiles than SMs split K over a cluster of up to 8 CTAs
     (partials added over distributed shared memory): the config-3 down projection (24
-    tiles, 6 splits), GeGLU pairs, a ragged token tile and the soft-capped epilogue,
+    tiles, 4 splits), GeGLU pairs, a ragged token tile and the soft-capped epilogue,
     at the same bars as the unsplit kernel."""
     w = synth.make_qweight(900 + n + k, n, k, bits, bits == 8)
     x = synth.normal(901 + m, m * k).reshape(m, k)
@@ -109,4 +109,28 @@ def test_prefill_split_k_over_a_cluster(g, m, n, k, bits, mode):
         got = g.readback(g.linear(gx, g.quant_tensor(w))).reshape(m, n)
         ref = oracle.linear(f16_round(x), w)
         assert rel_l2(got, oracle.linear(x, w)) <= 1e-2
+    assert rel_l2(got, ref) <= 1e-5
+
+
+@pytest.mark.parametrize("nt", [64, 192])
+@pytest.mark.parametrize("m,n,k,bits,mode", [(512, 1536, 6144, 2, 0), (512, 768, 1536, 4, 1), (200, 300, 2048, 8, 2)])
+def test_prefill_token_tiles(g, monkeypatch, nt, m, n, k, bits, mode):
+    """Token tiles of 64 and 192 (GQ_PREFILL_NT; the default is 256, or 128 for
+    short prefills): ragged last tiles, K split over clusters where the grid is
+    small, GeGLU pairs and the column-slice epilogue, at the unsplit bars."""
+    monkeypatch.setenv("GQ_PREFILL_NT", str(nt))
+    w = synth.make_qweight(950 + n + k, n, k, bits, bits == 8)
+    x = synth.normal(951 + m, m * k).reshape(m, k)
+    gx = g.tensor(x, x.shape)
+    if mode == 1:
+        wu = synth.make_qweight(952 + n, n, k, bits)
+        got = g.readback(g.linear_geglu(gx, g.quant_tensor(w), g.quant_tensor(wu))).reshape(m, n)
+        ref = oracle.linear_geglu(f16_round(x), w, wu)
+    elif mode == 2:
+        b = synth.normal(953, m * (n + 40)).reshape(m, n + 40)
+        got = g.readback(g.linear_gelu_mul_cols(gx, g.quant_tensor(w), g.tensor(b, b.shape), 40)).reshape(m, n)
+        ref = oracle.linear_gelu_mul_cols(f16_round(x), w, b, 40)
+    else:
+        got = g.readback(g.linear(gx, g.quant_tensor(w))).reshape(m, n)
+        ref = oracle.linear(f16_round(x), w)
     assert rel_l2(got, ref) <= 1e-5

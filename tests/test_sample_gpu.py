@@ -200,6 +200,45 @@ def test_small_vocab_strided_rows_and_ties(g):
         assert check_row(rows[r, :n], o, seeds[r], int(tok[r]), int(st[r])) in (0, 1)
 
 
+@pytest.mark.parametrize("top_k", [1, 7, 64, 256])
+def test_top_k_over_heavy_ties(g, top_k):
+    """Logits on a few levels, so thousands of columns tie across chunks. The merged
+    candidate list (radix select of the chunks' candidates, then a sort of the
+    selected) holds the same candidates as the reference (among equal values, the
+    first columns: its size-k heap admits only larger values once full) in column
+    order; the reference lists equal candidates in its heap's internal order, so a
+    draw may land on a different one of several EQUAL-probability candidates. The
+    check: the state advanced as the oracle's, the token is one of the oracle's
+    candidates and carries the value the oracle's token has; and the sorted top-k
+    pairs of gq_topk_rows match numpy's stable order exactly."""
+    rng = np.random.default_rng(44)
+    m = 3
+    logits = (rng.integers(0, 6, (m, V)) * 0.5).astype(np.float32)
+    logits[1, 100000:100300] = 3.0  # a block of tied maxima inside one chunk
+    o = opts(temperature=0.8, top_k=top_k, top_p=0.9)
+    seeds = [11, 12, 13]
+    tok, st, _ = sample_rows(g, logits, o, seeds)
+    for r in range(m):
+        u, want_st = oracle.rng_next_f64(seeds[r])
+        assert int(st[r]) == want_st
+        want = oracle.sample(logits[r], o.temperature, o.top_k, o.top_p, 1.0, None, u)
+        cands = np.argsort(-logits[r], kind="stable")[:top_k]
+        assert int(tok[r]) in set(cands.tolist())
+        assert logits[r][int(tok[r])] == logits[r][want]
+    torch = g._torch
+    lg = dev(g, logits, np.float32)
+    val = torch.empty(m, top_k, dtype=torch.float32, device=g.torch_device)
+    idx = torch.empty(m, top_k, dtype=torch.int64, device=g.torch_device)
+    rc = g.lib.gq_topk_rows(g.ctx, c_void_p(lg.data_ptr()), m, V, V, 0, top_k, 1.0, None, 0, 0,
+                            c_void_p(val.data_ptr()), c_void_p(idx.data_ptr()))
+    assert rc == _abi.GQ_OK
+    g.flush()
+    for r in range(m):
+        want = np.argsort(-logits[r], kind="stable")[:top_k]
+        assert np.array_equal(idx[r].cpu().numpy(), want)
+        assert np.array_equal(val[r].cpu().numpy(), logits[r][want])
+
+
 @pytest.mark.parametrize("mode", ["greedy", "engine_default", "top_k_40"])
 def test_sharded_candidates_equal_whole_row(g, mode):
     """A vocab-sharded lm_head: each of 4 shards' top k (gq_topk_rows with the shard's
