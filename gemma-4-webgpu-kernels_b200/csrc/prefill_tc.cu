@@ -654,15 +654,33 @@ CUresult encode_weight_map(CUtensorMap *map, const uint8_t *w, int64_t n, int64_
 }
 
 // Tensor map over the f16 activations [m, k], box nt rows x 64 halves, 128-byte swizzle.
-// Tokens per tile (the MMA N): 256, or 128 for short prefills. GQ_PREFILL_NT
-// (64, 128, 192 or 256: a multiple of 64, the epilogue's drain step per half)
-// overrides it for tuning and tests.
-int token_tile(int64_t m) {
+// Tokens per tile (the MMA N, a multiple of 64: the epilogue drains 32 columns
+// per half). 128 for short prefills. For longer ones a tile's time is mostly
+// fixed cost, so fewer idle SMs win: where 256-token tiles fill less than half
+// the SMs (the K-split regime), a smaller tile that fills half to all of them in
+// one wave without a split, else 256 with K split over clusters; otherwise the
+// smallest of 128 / 192 / 256 that needs no more waves than 256. Measured on B200
+// (µs per call incl. the cast): 4-bit gate [6144, 1536] at M = 512 21.2 -> 20.1
+// (192), fused gate+up 51.9 -> 46.2 (192), M = 1024 40.0 -> 37.7 (192), M = 256
+// 19.6 (256, K in 2) -> 17.2 (128); the 2-bit down [1536, 6144] at M = 512 stays at
+// 256 with K in 4 (24.6; 33.9 at 128, 38.4 at 192), as does M = 2048 (three waves).
+// GQ_PREFILL_NT (64, 128, 192 or 256) overrides the choice for tuning and tests.
+int token_tile(int64_t m, int64_t wtiles, int kt_all, int num_sms) {
   if (const char *e = getenv("GQ_PREFILL_NT")) {
     const int v = atoi(e);
     if (v == 64 || v == 128 || v == 192 || v == 256) return v;
   }
-  return m > 128 ? NT_MAX : 128;
+  if (m <= 128) return 128;
+  auto tiles = [&](int nt) { return ((m + nt - 1) / nt) * wtiles; };
+  if (tiles(NT_MAX) * 2 <= num_sms && kt_all / 2 >= 3) {
+    for (int nt : {128, 192})
+      if (tiles(nt) * 2 >= num_sms && tiles(nt) <= num_sms) return nt;
+    return NT_MAX;  // K split over clusters
+  }
+  auto waves = [&](int nt) { return (tiles(nt) + num_sms - 1) / num_sms; };
+  for (int nt : {128, 192})
+    if (waves(nt) <= waves(NT_MAX)) return nt;
+  return NT_MAX;
 }
 
 CUresult encode_x_map(CUtensorMap *map, const __half *xh, int64_t m, int64_t k, int nt) {
@@ -727,7 +745,8 @@ int gq_prefill_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq
   __half *xh = static_cast<__half *>(wsp);
   int *xexp = reinterpret_cast<int *>(static_cast<uint8_t *>(wsp) + xh_bytes);
   GQ_CUDA_TRY(ctx, cast_any(w->bits, ctx->stream, ctx->pdl, x, xh, xexp, m, K));
-  const int nt = token_tile(m);
+  const int ow_sel = (mode == 1) ? MW / 2 : MW;
+  const int nt = token_tile(m, (w->n + ow_sel - 1) / ow_sel, (int)(K / BK), ctx->num_sms);
   CUtensorMap map;
   if (encode_x_map(&map, xh, m, K, nt) != CUDA_SUCCESS)
     return gq_fail(ctx, GQ_ERR_CUDA, "prefill: activation tensor map");
@@ -873,7 +892,8 @@ extern "C" int gq_linear_prefill_static(void *cuda_stream, const float *x, int64
   __half *xh = static_cast<__half *>(st->scratch);
   int *xexp = static_cast<int *>(st->xexp);
   if (cast_any(bits, stream, false, x, xh, xexp, m, k) != cudaSuccess) return GQ_ERR_CUDA;
-  const int nt = token_tile(m);
+  // no SM count here and no K split: 256 (128 for short prefills) unless overridden
+  const int nt = token_tile(m, int64_t(1) << 30, (int)(k / BK), 1);
   CUtensorMap map;
   if (encode_x_map(&map, xh, m, k, nt) != CUDA_SUCCESS) return GQ_ERR_CUDA;
   PrefillArgs a = {};
