@@ -251,7 +251,25 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  gqd::griddep_wait();  // x (the f16 workspace) comes from the preceding cast kernel
+  // The packed weights are immutable: the first ring's worth of weight tiles is
+  // requested before the dependency wait, so under programmatic dependent launch
+  // their HBM latency overlaps the cast kernel; their stages' x tiles follow the
+  // wait (x, the f16 workspace, comes from the cast).
+  const int pre = min(LS, KT);
+  auto load_w = [&](int kt, int s) {
+    if (MODE == 1) {  // gate rows then the same up rows
+      tma_load_2d(sP + s * R::PW, &tmap_w, (kt0 + kt) * PK, n0, &l_full[s]);
+      tma_load_2d(sP + s * R::PW + (MW / 2) * PK, &tmap_w2, (kt0 + kt) * PK, n0, &l_full[s]);
+    } else {
+      tma_load_2d(sP + s * R::PW, &tmap_w, (kt0 + kt) * PK, n0, &l_full[s]);
+    }
+  };
+  if (warp == 0 && lane == 0)
+    for (int kt = 0; kt < pre; ++kt) {
+      gqd::mbar_arrive_expect_tx(&l_full[kt], x_bytes + MW * PK);
+      load_w(kt, kt);
+    }
+  gqd::griddep_wait();
 
   if (warp == 0) {
     // ---- TMA: x tile + packed weight tile per stage ----
@@ -263,16 +281,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           *abort_flag = 1;
           break;
         }
-        gqd::mbar_arrive_expect_tx(&l_full[s], x_bytes + MW * PK);
+        if (kt >= pre) gqd::mbar_arrive_expect_tx(&l_full[s], x_bytes + MW * PK);
         tma_load_2d(sX + s * X_STAGE, &tmap_x, (kt0 + kt) * BK, m0, &l_full[s]);
-        if (MODE == 1) {  // gate rows then the same up rows
-          tma_load_2d(sP + s * R::PW, &tmap_w, (kt0 + kt) * PK, n0, &l_full[s]);
-          tma_load_2d(sP + s * R::PW + (MW / 2) * PK, &tmap_w2, (kt0 + kt) * PK, n0, &l_full[s]);
-        } else {
-          tma_load_2d(sP + s * R::PW, &tmap_w, (kt0 + kt) * PK, n0, &l_full[s]);
-        }
+        if (kt >= pre) load_w(kt, s);
         issued = kt + 1;
       }
+      if (issued < pre) issued = pre;  // weight tiles of stages whose x never came: drained below
       if (*abort_flag) {
         // bounded drain of the loads still in flight before shared memory is released
         for (int kt = issued > LS ? issued - LS : 0; kt < issued; ++kt)
