@@ -92,15 +92,24 @@ __device__ void bitonic_desc(uint64_t *k, int n) {
 // radix select over eight 8-bit digits from the top (a histogram of the keys
 // still matching the selected prefix, counts aggregated per warp with
 // match.any, the bin holding the k-th largest found from the top by one warp's
-// scan), then every key above the k-th and enough copies of it go to out[0..k)
-// unsorted. Zero keys (padding) are the only repeats and rank last.
-__device__ void select_top(const uint64_t *keys, int n, int k, uint64_t *out) {
+// scan; once that bin holds at most kSurv keys they are compacted and the later
+// passes scan only them), then every key above the k-th and enough copies of it
+// go to out[0..k) unsorted. Zero keys (padding) are the only repeats and rank last.
+constexpr int kSurv = 1024;  // select_top: keys still tied on the selected prefix, compacted
+
+__device__ void select_top(const uint64_t *all_keys, int all_n, int k, uint64_t *out) {
   __shared__ uint32_t hist[2][256];  // double-buffered: pass p counts into hist[p & 1]
+  __shared__ uint64_t surv[kSurv];
   __shared__ unsigned long long s_prefix;
-  __shared__ uint32_t s_need, s_count, s_ties;
+  __shared__ uint32_t s_need, s_count, s_ties, s_bin_count, s_nsurv;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
   uint64_t prefix = 0ull, mask = 0ull;
   uint32_t need = (uint32_t)k;
+  // the passes scan `keys`: all keys until the keys matching the selected prefix
+  // fit the survivor buffer, then only those (the final gather scans all keys)
+  const uint64_t *keys = all_keys;
+  int n = all_n;
+  bool compacted = false;
   for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[0][i] = 0u;
   __syncthreads();
   for (int shift = 56, p = 0; shift >= 0; shift -= 8, ++p) {
@@ -140,19 +149,33 @@ __device__ void select_top(const uint64_t *keys, int n, int k, uint64_t *out) {
         }
         s_prefix = prefix | ((unsigned long long)(255u - 8u * lane - (uint32_t)q) << shift);
         s_need = need - acc;
+        s_bin_count = cnt[q];
       }
-      if (shift == 0 && lane == 0) {
-        s_count = 0u;
-        s_ties = 0u;
+      if (lane == 0) {
+        s_nsurv = 0u;
+        if (shift == 0) {
+          s_count = 0u;
+          s_ties = 0u;
+        }
       }
     }
     __syncthreads();
     prefix = s_prefix;
     need = s_need;
     mask |= 255ull << shift;
+    if (!compacted && shift > 0 && s_bin_count <= (uint32_t)kSurv) {  // uniform: read after the barrier
+      for (int base = warp * 32; base < n; base += nw * 32) {
+        const int i = base + lane;
+        if (i < n && (keys[i] & mask) == prefix) surv[atomicAdd(&s_nsurv, 1u)] = keys[i];
+      }
+      __syncthreads();
+      keys = surv;
+      n = (int)s_nsurv;
+      compacted = true;
+    }
   }
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    const uint64_t kk = keys[i];
+  for (int i = threadIdx.x; i < all_n; i += blockDim.x) {
+    const uint64_t kk = all_keys[i];
     bool take = kk > prefix;
     if (kk == prefix) take = atomicAdd(&s_ties, 1u) < need;
     if (take) {
@@ -584,11 +607,14 @@ size_t row_smem(const SampleArgs &a) {
 
 int launch_rows(gq_ctx *ctx, const RowArgs &r) {
   const size_t smem = row_smem(r.s);
-  if (smem + 1024 > ctx->smem_optin) return gq_fail(ctx, GQ_ERR_UNSUPPORTED, "sample: too many candidates per row");
+  // (16 KB for the kernel's static shared memory: histograms, survivors, exps)
+  if (smem + 16384 > ctx->smem_optin) return gq_fail(ctx, GQ_ERR_UNSUPPORTED, "sample: too many candidates per row");
   // the dynamic shared memory the kernel may use, raised per device as larger merges come
   static size_t attr_set[64] = {};
   const int dev = ctx->device & 63;
-  if (smem > 48 * 1024 && smem > attr_set[dev]) {
+  // (set whenever the need grows: the kernel's static shared memory counts
+  // toward the 48 KB a launch may use without it)
+  if (smem > attr_set[dev]) {
     GQ_CUDA_TRY(ctx, cudaFuncSetAttribute(sample_row_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     attr_set[dev] = smem;
   }
