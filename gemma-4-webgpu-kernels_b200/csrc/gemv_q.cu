@@ -70,6 +70,13 @@ struct GemvArgs {
   int lanes;        // lanes per row (power of two dividing row_bytes/16)
   double inv_k;     // 1 / K
   uint32_t *err;
+  // Norm prologue (kernels built with PRO, one activation row): x is not read
+  // from memory but made in the CTA as the decode step's residual add + RMSNorm
+  // would make it, h = (pr + po * inv(po) * pw1) [* *ps], written to ph by CTA 0,
+  // and x = pw2 ? h * inv(h) * pw2 : h, with inv(v) = 1 / sqrt(sum(v^2) / K + peps).
+  const float *po, *pr, *pw1, *ps, *pw2;
+  float *ph;
+  float peps;
 };
 
 using gqcore::Fmt;
@@ -79,11 +86,12 @@ using gqcore::mac_chunk;
 
 // Shared-memory carve-up, identical on host (sizing) and device (addressing).
 struct GemvSmem {
-  size_t stage_off, xs_off, bar_off, cnt_off, dscr_off, fscr_off, par_off, total;
+  size_t stage_off, xs_off, bar_off, cnt_off, dscr_off, fscr_off, par_off, pro_off, total;
 };
 __host__ __device__ inline size_t align16(size_t v) { return (v + 15) & ~size_t(15); }
+// pro_k: floats per row buffer of the norm prologue (four buffers), 0 = none.
 __host__ __device__ inline GemvSmem gemv_layout(int bits, int mt, int nw, int row_bytes,
-                                                int tile_rows, int stages) {
+                                                int tile_rows, int stages, int pro_k = 0) {
   const int C = row_bytes / 16;
   const int per_chunk = 4 * (32 / bits);
   GemvSmem L;
@@ -96,6 +104,7 @@ __host__ __device__ inline GemvSmem gemv_layout(int bits, int mt, int nw, int ro
   L.dscr_off = o;  o = align16(o + (size_t)kMaxWarps * mt * sizeof(double));
   L.fscr_off = o;  o = align16(o + (size_t)kMaxWarps * mt * sizeof(float));
   L.par_off = o;   o = align16(o + (size_t)mt * (sizeof(double) + 2 * sizeof(float)));
+  L.pro_off = o;   o = align16(o + (size_t)4 * pro_k * sizeof(float) + 2 * sizeof(float));
   L.total = o;
   return L;
 }
@@ -109,8 +118,9 @@ __host__ __device__ inline GemvSmem gemv_layout(int bits, int mt, int nw, int ro
 // the stage's rows in passes of WARPS*R*32/LANES. Row sums are reduced with
 // shuffles inside the lane group; no block barrier is needed per stage: the last
 // warp to finish a stage refills it.
-template <int BITS, bool SIGNED, int MT, int MODE, int THREADS, int R>
+template <int BITS, bool SIGNED, int MT, int MODE, int THREADS, int R, bool PRO = false>
 __global__ void __launch_bounds__(THREADS, THREADS == kThreads ? kResident : 1) gemv_q_kernel(const GemvArgs a) {
+  static_assert(!PRO || MT == 1, "the norm prologue makes one activation row");
   using F = Fmt<BITS>;
   constexpr int WARPS = THREADS / 32;
   constexpr int NW = (MODE == 1) ? 2 : 1;  // weights streamed together
@@ -121,7 +131,8 @@ __global__ void __launch_bounds__(THREADS, THREADS == kThreads ? kResident : 1) 
   const int C = a.row_bytes >> 4;  // chunks per row
   const int stage_bytes = a.tile_rows * a.row_bytes;                    // one weight's tile
   const int stage_stride = NW * (stage_bytes + 2 * a.tile_rows * 4);    // weights + row operands
-  const GemvSmem L = gemv_layout(BITS, MT, NW, a.row_bytes, a.tile_rows, a.stages);
+  const int pro_k = PRO ? ((a.K + 3) & ~3) : 0;
+  const GemvSmem L = gemv_layout(BITS, MT, NW, a.row_bytes, a.tile_rows, a.stages, pro_k);
   uint8_t *stage_buf = smem + L.stage_off;                        // [stages][NW][stage_bytes]
   float *xs = reinterpret_cast<float *>(smem + L.xs_off);         // [MT][C][kPad]
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + L.bar_off);  // [kMaxStages]
@@ -189,6 +200,88 @@ __global__ void __launch_bounds__(THREADS, THREADS == kThreads ? kResident : 1) 
   gqd::griddep_launch_dependents();
   gqd::griddep_wait();
 
+  // ---- norm prologue: the activation row made here (PRO) ------------------------
+  // The arithmetic of the row-norm kernels (decode_ops.cu: add_norm_norm_kernel,
+  // rmsnorm_reg_kernel): lane l of warp 0 sums the squares of elements
+  // 4(l + 32i) .. +3 for i = 0, 1, ... in that order, then a butterfly over the
+  // warp, so x equals what those kernels write, bit for bit. The four rows come
+  // in with one round trip by every thread.
+  const float *xsrc = nullptr;
+  if constexpr (PRO) {
+    float *bo = reinterpret_cast<float *>(smem + L.pro_off), *br = bo + pro_k, *bw1 = br + pro_k, *bw2 = bw1 + pro_k;
+    float *inv_s = bw2 + pro_k;  // [2]
+    const int n4 = a.K >> 2;
+    const float4 one4 = make_float4(1.f, 1.f, 1.f, 1.f);
+    for (int c = tid; c < n4; c += THREADS) {
+      reinterpret_cast<float4 *>(bo)[c] = __ldcg(reinterpret_cast<const float4 *>(a.po) + c);
+      reinterpret_cast<float4 *>(br)[c] = __ldcg(reinterpret_cast<const float4 *>(a.pr) + c);
+      reinterpret_cast<float4 *>(bw1)[c] = __ldg(reinterpret_cast<const float4 *>(a.pw1) + c);
+      reinterpret_cast<float4 *>(bw2)[c] = a.pw2 ? __ldg(reinterpret_cast<const float4 *>(a.pw2) + c) : one4;
+    }
+    const float sc = a.ps ? __ldg(a.ps) : 1.0f;
+    __syncthreads();
+    auto row_inv = [&](const float *v) {  // warp 0
+      float ss = 0.0f;
+      for (int c = lane; c < n4; c += 32) {
+        const float4 t = reinterpret_cast<const float4 *>(v)[c];
+        ss = __fadd_rn(ss, __fmul_rn(t.x, t.x));
+        ss = __fadd_rn(ss, __fmul_rn(t.y, t.y));
+        ss = __fadd_rn(ss, __fmul_rn(t.z, t.z));
+        ss = __fadd_rn(ss, __fmul_rn(t.w, t.w));
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      return __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, (float)a.K), a.peps)));
+    };
+    if (warp == 0) {
+      const float inv = row_inv(bo);
+      if (lane == 0) inv_s[0] = inv;
+    }
+    __syncthreads();
+    {
+      const float inv = inv_s[0];
+      const bool writer = blockIdx.x == 0 && blockIdx.y == 0;
+      auto one = [&](float xx, float ww, float rr) {
+        float n = __fadd_rn(rr, __fmul_rn(__fmul_rn(xx, inv), ww));
+        if (a.ps) n = __fmul_rn(n, sc);
+        return n;
+      };
+      for (int c = tid; c < n4; c += THREADS) {
+        const float4 o4 = reinterpret_cast<const float4 *>(bo)[c];
+        const float4 w4 = reinterpret_cast<const float4 *>(bw1)[c];
+        const float4 r4 = reinterpret_cast<const float4 *>(br)[c];
+        const float4 h4 = make_float4(one(o4.x, w4.x, r4.x), one(o4.y, w4.y, r4.y), one(o4.z, w4.z, r4.z),
+                                      one(o4.w, w4.w, r4.w));
+        reinterpret_cast<float4 *>(br)[c] = h4;
+        if (writer) reinterpret_cast<float4 *>(a.ph)[c] = h4;
+      }
+    }
+    __syncthreads();
+    if (a.pw2) {
+      if (warp == 0) {
+        const float inv2 = row_inv(br);
+        if (lane == 0) inv_s[1] = inv2;
+      }
+      __syncthreads();
+      const float inv2 = inv_s[1];
+      for (int c = tid; c < n4; c += THREADS) {
+        const float4 h4 = reinterpret_cast<const float4 *>(br)[c];
+        const float4 w4 = reinterpret_cast<const float4 *>(bw2)[c];
+        reinterpret_cast<float4 *>(bo)[c] =
+            make_float4(__fmul_rn(__fmul_rn(h4.x, inv2), w4.x), __fmul_rn(__fmul_rn(h4.y, inv2), w4.y),
+                        __fmul_rn(__fmul_rn(h4.z, inv2), w4.z), __fmul_rn(__fmul_rn(h4.w, inv2), w4.w));
+      }
+      __syncthreads();
+      xsrc = bo;
+    } else {
+      xsrc = br;
+    }
+  }
+  auto ldx4 = [&](const float *p) -> float4 {
+    if constexpr (PRO) return *reinterpret_cast<const float4 *>(p);
+    else return __ldg(reinterpret_cast<const float4 *>(p));
+  };
+
   // ---- stage x: x' = x - mu, scaled by 2^(S - pos) into the padded layout ----
   // One global read of x (held in registers up to kXv float4 per thread and row),
   // one (sum, max|x|) reduction for all MT rows giving mu and S (S leaves one
@@ -205,14 +298,14 @@ __global__ void __launch_bounds__(THREADS, THREADS == kThreads ? kResident : 1) 
       sx[m] = 0.0;
       mx[m] = 0.0f;
       const bool live = m0 + m < a.M;
-      const float *xr = a.x + (size_t)(m0 + m) * a.ldx;
+      const float *xr = PRO ? xsrc : a.x + (size_t)(m0 + m) * a.ldx;
 #pragma unroll
       for (int i = 0; i < kXv; ++i) {
         const int k = (tid + i * THREADS) * 4;
-        xv[m][i] = (live && k < a.K) ? __ldg(reinterpret_cast<const float4 *>(xr + k)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        xv[m][i] = (live && k < a.K) ? ldx4(xr + k) : make_float4(0.f, 0.f, 0.f, 0.f);
       }
       for (int k = (tid + kXv * THREADS) * 4; live && k < a.K; k += THREADS * 4) {
-        const float4 v = __ldg(reinterpret_cast<const float4 *>(xr + k));
+        const float4 v = ldx4(xr + k);
         sx[m] += ((double)v.x + (double)v.y) + ((double)v.z + (double)v.w);
         mx[m] = fmaxf(mx[m], fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
       }
@@ -249,7 +342,7 @@ __global__ void __launch_bounds__(THREADS, THREADS == kThreads ? kResident : 1) 
       int S = 125 - e;
       S = max(22, min(126, S));  // 2^(149-S) stays a normal f32 for the epilogue
       float *xm = xs + (size_t)m * xs_mstride;
-      const float *xr = a.x + (size_t)(m0 + m) * a.ldx;
+      const float *xr = PRO ? xsrc : a.x + (size_t)(m0 + m) * a.ldx;
       auto put = [&](int k, float4 v) {
         float o[4] = {0.f, 0.f, 0.f, 0.f};
         if (live) {
@@ -266,7 +359,7 @@ __global__ void __launch_bounds__(THREADS, THREADS == kThreads ? kResident : 1) 
         if (k < a.K) put(k, xv[m][i]);
       }
       for (int k = (tid + kXv * THREADS) * 4; k < a.K; k += THREADS * 4)
-        put(k, live ? __ldg(reinterpret_cast<const float4 *>(xr + k)) : make_float4(0.f, 0.f, 0.f, 0.f));
+        put(k, live ? ldx4(xr + k) : make_float4(0.f, 0.f, 0.f, 0.f));
       if (tid == 0) {
         mu_s[m] = mu;
         const double sxp = live ? sum - (double)a.K * (double)mu : 0.0;
@@ -462,9 +555,9 @@ __global__ void __launch_bounds__(THREADS, THREADS == kThreads ? kResident : 1) 
   }
 }
 
-template <int BITS, bool SIGNED, int MT, int MODE, int THREADS, int R>
+template <int BITS, bool SIGNED, int MT, int MODE, int THREADS, int R, bool PRO>
 int launch_t(gq_ctx *ctx, const GemvArgs &a, dim3 grid, size_t smem) {
-  auto kern = gemv_q_kernel<BITS, SIGNED, MT, MODE, THREADS, R>;
+  auto kern = gemv_q_kernel<BITS, SIGNED, MT, MODE, THREADS, R, PRO>;
   static bool attr_set[64] = {};
   const int dev = ctx->device & 63;
   if (!attr_set[dev]) {
@@ -478,24 +571,25 @@ int launch_t(gq_ctx *ctx, const GemvArgs &a, dim3 grid, size_t smem) {
   return GQ_OK;
 }
 
-template <int BITS, bool SIGNED, int MT, int MODE>
+template <int BITS, bool SIGNED, int MT, int MODE, bool PRO>
 int launch_v(gq_ctx *ctx, bool wide, const GemvArgs &a, dim3 grid, size_t smem) {
-  if (wide) return launch_t<BITS, SIGNED, MT, MODE, kWideThreads, MT == 1 ? 2 : 1>(ctx, a, grid, smem);
-  return launch_t<BITS, SIGNED, MT, MODE, kThreads, 1>(ctx, a, grid, smem);
+  if (wide) return launch_t<BITS, SIGNED, MT, MODE, kWideThreads, MT == 1 ? 2 : 1, PRO>(ctx, a, grid, smem);
+  return launch_t<BITS, SIGNED, MT, MODE, kThreads, 1, PRO>(ctx, a, grid, smem);
 }
 
-template <int BITS, bool SIGNED, int MT>
+template <int BITS, bool SIGNED, int MT, bool PRO = false>
 int launch_mode(gq_ctx *ctx, int mode, bool wide, const GemvArgs &a, dim3 grid, size_t smem) {
   switch (mode) {
-    case 0: return launch_v<BITS, SIGNED, MT, 0>(ctx, wide, a, grid, smem);
-    case 1: return launch_v<BITS, SIGNED, MT, 1>(ctx, wide, a, grid, smem);
-    case 2: return launch_v<BITS, SIGNED, MT, 2>(ctx, wide, a, grid, smem);
-    default: return launch_v<BITS, SIGNED, MT, 3>(ctx, wide, a, grid, smem);
+    case 0: return launch_v<BITS, SIGNED, MT, 0, PRO>(ctx, wide, a, grid, smem);
+    case 1: return launch_v<BITS, SIGNED, MT, 1, PRO>(ctx, wide, a, grid, smem);
+    case 2: return launch_v<BITS, SIGNED, MT, 2, PRO>(ctx, wide, a, grid, smem);
+    default: return launch_v<BITS, SIGNED, MT, 3, PRO>(ctx, wide, a, grid, smem);
   }
 }
 
 template <int BITS, bool SIGNED>
-int launch_mt(gq_ctx *ctx, int mt, int mode, bool wide, const GemvArgs &a, dim3 grid, size_t smem) {
+int launch_mt(gq_ctx *ctx, int mt, int mode, bool wide, const GemvArgs &a, dim3 grid, size_t smem, bool pro) {
+  if (pro) return launch_mode<BITS, SIGNED, 1, true>(ctx, mode, wide, a, grid, smem);
   if (mt == 1) return launch_mode<BITS, SIGNED, 1>(ctx, mode, wide, a, grid, smem);
   if (mt == 2) return launch_mode<BITS, SIGNED, 2>(ctx, mode, wide, a, grid, smem);
   return launch_mode<BITS, SIGNED, 4>(ctx, mode, wide, a, grid, smem);
@@ -504,8 +598,8 @@ int launch_mt(gq_ctx *ctx, int mt, int mode, bool wide, const GemvArgs &a, dim3 
 }  // namespace
 
 // Shared memory the kernel needs for a configuration (bytes).
-static size_t gemv_smem_bytes(int bits, int mt, int nw, int row_bytes, int tile_rows, int stages) {
-  return gemv_layout(bits, mt, nw, row_bytes, tile_rows, stages).total;
+static size_t gemv_smem_bytes(int bits, int mt, int nw, int row_bytes, int tile_rows, int stages, int pro_k = 0) {
+  return gemv_layout(bits, mt, nw, row_bytes, tile_rows, stages, pro_k).total;
 }
 
 // True when the CUDA-core GEMV handles this shape: whole 16-byte chunks per row,
@@ -532,19 +626,37 @@ bool gq_gemv_r1_supported(gq_ctx *ctx, const gq_qweight *w, int64_t m, int nw);
 int gq_gemv_r1_launch(gq_ctx *ctx, int mode, const float *x, const gq_qweight *w, const gq_qweight *w2,
                       const float *bs, int64_t b_off, float cap, float *y, int64_t y_col0);
 
-// mode: 0 plain, 1 geglu (w2 = up), 2 gelu * bs slice, 3 soft-cap.
-int gq_gemv_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq_qweight *w,
-                   const gq_qweight *w2, const float *bs, int64_t b_stride, int64_t b_off,
-                   float cap, float *y, int64_t ldy, int64_t y_col0) {
+// The norm prologue's inputs (one activation row; see GemvArgs::po).
+struct GemvPro {
+  const float *o, *r, *w1, *s, *w2;
+  float *h;
+  float eps;
+};
+
+// mode: 0 plain, 1 geglu (w2 = up), 2 gelu * bs slice, 3 soft-cap. pro: x made
+// in the kernel by the norm prologue (m = 1, x unused).
+static int gemv_launch_impl(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq_qweight *w,
+                            const gq_qweight *w2, const float *bs, int64_t b_stride, int64_t b_off,
+                            float cap, float *y, int64_t ldy, int64_t y_col0, const GemvPro *pro) {
   const int nw = (mode == 1) ? 2 : 1;
   // one activation row: the register-x kernel (gemv_r1.cu) where its shape rules hold
-  if (m == 1 && (uintptr_t)x % 16 == 0 && gq_gemv_r1_supported(ctx, w, m, nw))
+  if (!pro && m == 1 && (uintptr_t)x % 16 == 0 && gq_gemv_r1_supported(ctx, w, m, nw))
     return gq_gemv_r1_launch(ctx, mode, x, w, w2, bs, b_off, cap, y, y_col0);
-  const int mt = gemv_mt(ctx, w, m, nw);
+  const int mt = pro ? 1 : gemv_mt(ctx, w, m, nw);
+  const int pro_k = pro ? (int)((w->k + 3) & ~int64_t(3)) : 0;
   const int rb = (int)w->row_bytes;
   const int C = rb / 16;
   GemvArgs a = {};
   a.x = x;
+  if (pro) {
+    a.po = pro->o;
+    a.pr = pro->r;
+    a.pw1 = pro->w1;
+    a.ps = pro->s;
+    a.pw2 = pro->w2;
+    a.ph = pro->h;
+    a.peps = pro->eps;
+  }
   a.ldx = w->k;
   a.M = (int)m;
   a.K = (int)w->k;
@@ -593,7 +705,7 @@ int gq_gemv_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq_qw
     for (int l = 4; l <= max_lanes; l <<= 1) {
       if (C % l != 0) continue;
       const int rpp = warps * (32 / l) * R;
-      if ((size_t)rpp * rb * nw > 48 * 1024 || gemv_smem_bytes(w->bits, mt, nw, rb, rpp, 2) > cap) continue;
+      if ((size_t)rpp * rb * nw > 48 * 1024 || gemv_smem_bytes(w->bits, mt, nw, rb, rpp, 2, pro_k) > cap) continue;
       const int passes = (rows_per_cta + rpp - 1) / rpp;
       if (rows_per_cta >= (int)(0.85 * passes * rpp) || l == max_lanes) {
         lanes = l;
@@ -602,7 +714,7 @@ int gq_gemv_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq_qw
     }
     if (lanes < 0) {  // nothing fits the 48 KB stage budget: one pass per stage at max lanes
       lanes = max_lanes;
-      if (gemv_smem_bytes(w->bits, mt, nw, rb, warps * (32 / lanes) * R, 1) > cap) return false;
+      if (gemv_smem_bytes(w->bits, mt, nw, rb, warps * (32 / lanes) * R, 1, pro_k) > cap) return false;
     }
     const int rows_per_pass = warps * (32 / lanes) * R;
     // Stage size: whole passes, >= 24 KB per copy where the rows allow (large
@@ -613,11 +725,11 @@ int gq_gemv_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq_qw
     if (tile_rows > rows_per_cta) tile_rows = ((rows_per_cta + rows_per_pass - 1) / rows_per_pass) * rows_per_pass;
     const int ntiles = (rows_per_cta + tile_rows - 1) / tile_rows;
     stages = min(kMaxStages, ntiles);
-    smem = gemv_smem_bytes(w->bits, mt, nw, rb, tile_rows, stages);
+    smem = gemv_smem_bytes(w->bits, mt, nw, rb, tile_rows, stages, pro_k);
     while (smem > cap && (stages > 1 || tile_rows > rows_per_pass)) {
       if (stages > 2 || (stages > 1 && tile_rows == rows_per_pass)) --stages;
       else tile_rows -= rows_per_pass;
-      smem = gemv_smem_bytes(w->bits, mt, nw, rb, tile_rows, stages);
+      smem = gemv_smem_bytes(w->bits, mt, nw, rb, tile_rows, stages, pro_k);
     }
     return smem <= cap && tile_rows >= 1 && stages >= 1;
   };
@@ -641,8 +753,24 @@ int gq_gemv_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq_qw
   a.lanes = lanes;
   a.inv_k = 1.0 / (double)w->k;
   dim3 grid(gx, (unsigned)((m + mt - 1) / mt));
-  if (w->bits == 4) return launch_mt<4, false>(ctx, mt, mode, wide, a, grid, smem);
-  if (w->bits == 2) return launch_mt<2, false>(ctx, mt, mode, wide, a, grid, smem);
-  if (w->signed_i8) return launch_mt<8, true>(ctx, mt, mode, wide, a, grid, smem);
-  return launch_mt<8, false>(ctx, mt, mode, wide, a, grid, smem);
+  const bool p = pro != nullptr;
+  if (w->bits == 4) return launch_mt<4, false>(ctx, mt, mode, wide, a, grid, smem, p);
+  if (w->bits == 2) return launch_mt<2, false>(ctx, mt, mode, wide, a, grid, smem, p);
+  if (w->signed_i8) return launch_mt<8, true>(ctx, mt, mode, wide, a, grid, smem, p);
+  return launch_mt<8, false>(ctx, mt, mode, wide, a, grid, smem, p);
+}
+
+int gq_gemv_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq_qweight *w,
+                   const gq_qweight *w2, const float *bs, int64_t b_stride, int64_t b_off,
+                   float cap, float *y, int64_t ldy, int64_t y_col0) {
+  return gemv_launch_impl(ctx, mode, x, m, w, w2, bs, b_stride, b_off, cap, y, ldy, y_col0, nullptr);
+}
+
+// One activation row made by the norm prologue, then the streaming GEMV (modes 0-2;
+// bs: the MODE-2 row, its columns from b_off). Arguments checked by the caller.
+int gq_gemv_pro_launch(gq_ctx *ctx, int mode, const float *o, const float *r, const float *w1, const float *s,
+                       const float *w2n, float eps, float *h, const gq_qweight *w, const gq_qweight *wu,
+                       const float *bs, int64_t b_off, float *y) {
+  const GemvPro pro = {o, r, w1, s, w2n, h, eps};
+  return gemv_launch_impl(ctx, mode, nullptr, 1, w, wu, bs, 0, b_off, 0.0f, y, w->n, 0, &pro);
 }

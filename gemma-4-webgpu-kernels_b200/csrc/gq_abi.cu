@@ -22,6 +22,9 @@ int gq_gemv_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq_qw
                    const gq_qweight *w2, const float *bs, int64_t b_stride, int64_t b_off,
                    float cap, float *y, int64_t ldy, int64_t y_col0);
 int gq_scalar_linear_launch(gq_ctx *ctx, const float *x, int64_t m, const gq_qweight *w, float *y);
+int gq_gemv_pro_launch(gq_ctx *ctx, int mode, const float *o, const float *r, const float *w1, const float *s,
+                       const float *w2n, float eps, float *h, const gq_qweight *w, const gq_qweight *wu,
+                       const float *bs, int64_t b_off, float *y);
 // gemv_tcx.cu
 bool gq_gemv_tcx_supported(gq_ctx *ctx, const gq_qweight *w, const float *x, int64_t m, int nw);
 int gq_gemv_tcx_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq_qweight *w, const gq_qweight *w2,
@@ -532,6 +535,57 @@ int gq_linear_gelu_mul_cols(gq_ctx *ctx, const float *x, int64_t m, int64_t k, c
   if ((rc = scratch_get(ctx, 0, cnt, &g)) != GQ_OK) return rc;
   if ((rc = gq_linear(ctx, x, m, k, w, g)) != GQ_OK) return rc;
   return gq_elementwise_launch(ctx, 2, g, b, (int64_t)cnt, w->n, b_stride, b_offset, 0.0f, y);
+}
+
+namespace {
+bool ranges_overlap(const void *a, size_t na, const void *b, size_t nb) {
+  const uintptr_t pa = (uintptr_t)a, pb = (uintptr_t)b;
+  return na && nb && pa < pb + nb && pb < pa + na;
+}
+}  // namespace
+
+int gq_add_norm_linear(gq_ctx *ctx, int32_t mode, const float *x, const float *residual, int64_t k,
+                       const float *w_norm, float eps, const float *scale_by, const float *w_norm2, float *h_out,
+                       const gq_qweight *w, const gq_qweight *w_up, const float *b, int64_t b_offset, float *y) {
+  GQ_ENTER(ctx);
+  const char *what = "add_norm_linear";
+  if (mode < 0 || mode > 2) return gq_fail(ctx, GQ_ERR_INVALID_ARGUMENT, std::string(what) + ": mode not in 0..2");
+  if (!x || !residual || !w_norm || !h_out || !w || !y)
+    return gq_fail(ctx, GQ_ERR_INVALID_ARGUMENT, std::string(what) + ": null pointer");
+  if (k != w->k || k <= 0) return gq_fail(ctx, GQ_ERR_INVALID_ARGUMENT, std::string(what) + ": k differs from the weight's K");
+  if (mode == 1 && (!w_up || w_up->n != w->n || w_up->k != w->k || w_up->bits != w->bits ||
+                    w_up->signed_i8 != w->signed_i8 || w_up->group_size != w_up->k))
+    return gq_fail(ctx, GQ_ERR_INVALID_ARGUMENT, std::string(what) + ": geglu needs an up weight shaped as w");
+  if (mode == 2 && (!b || b_offset < 0)) return gq_fail(ctx, GQ_ERR_INVALID_ARGUMENT, std::string(what) + ": null b");
+  const size_t kb = (size_t)k * 4, yb = (size_t)w->n * 4;
+  if (ranges_overlap(h_out, kb, x, kb) || ranges_overlap(h_out, kb, residual, kb) || ranges_overlap(y, yb, h_out, kb) ||
+      ranges_overlap(y, yb, x, kb) || ranges_overlap(y, yb, residual, kb))
+    return gq_fail(ctx, GQ_ERR_INVALID_ARGUMENT, std::string(what) + ": h_out and y must not overlap the inputs");
+  if (w->n == 0) return GQ_OK;
+  const bool fused = k % 4 == 0 && k <= 4096 &&
+                     ((uintptr_t)x | (uintptr_t)residual | (uintptr_t)w_norm | (uintptr_t)h_out |
+                      (uintptr_t)(w_norm2 ? w_norm2 : w_norm)) % 16 == 0 &&
+                     gq_gemv_supported(ctx, w, 1, mode == 1 ? 2 : 1);
+  if (!fused) {
+    // the calls it fuses (the normalised row in the context workspace)
+    int rc;
+    const float *xn = h_out;
+    if (w_norm2) {
+      void *ws = nullptr;
+      if ((rc = gq_workspace(ctx, kb, &ws)) != GQ_OK) return rc;
+      if ((rc = gq_add_rms_norm_norm(ctx, residual, x, 1, k, w_norm, eps, scale_by, w_norm2, h_out,
+                                     static_cast<float *>(ws))) != GQ_OK)
+        return rc;
+      xn = static_cast<const float *>(ws);
+    } else if ((rc = gq_add_rms_norm(ctx, residual, x, 1, k, w_norm, eps, scale_by, h_out)) != GQ_OK) {
+      return rc;
+    }
+    if (mode == 1) return gq_linear_geglu(ctx, xn, 1, k, w, w_up, y);
+    if (mode == 2) return gq_linear_gelu_mul_cols(ctx, xn, 1, k, w, b, b_offset + w->n, b_offset, y);
+    return gq_linear(ctx, xn, 1, k, w, y);
+  }
+  return gq_gemv_pro_launch(ctx, mode, x, residual, w_norm, scale_by, w_norm2, eps, h_out, w, mode == 1 ? w_up : nullptr,
+                            b, b_offset, y);
 }
 
 namespace {

@@ -130,6 +130,8 @@ SIGNATURES = {
                                 c_void_p]),
     "gq_add_rms_norm_norm": (c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_float, c_void_p,
                                      c_void_p, c_void_p, c_void_p]),
+    "gq_add_norm_linear": (c_int, [c_void_p, c_int32, c_void_p, c_void_p, c_int64, c_void_p, c_float, c_void_p,
+                                   c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_void_p]),
     "gq_head_norm_rope": (c_int, [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p, c_float, c_void_p,
                                   c_float, c_int64, c_void_p, c_int64]),
     "gq_qkv_norm_rope": (

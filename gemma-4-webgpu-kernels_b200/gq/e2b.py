@@ -24,6 +24,7 @@ norm kernels and attends over slots [0, p]. Shared layers (the last
 from __future__ import annotations
 
 import math
+import os
 import zlib
 from ctypes import c_float, c_void_p
 from dataclasses import dataclass, field
@@ -202,7 +203,7 @@ class Decoder:
 
     def __init__(self, g, cfg: Config, weights: Optional[Weights], batch: int, cache_len: int,
                  capacity: Optional[int] = None, device_init_seed: Optional[int] = None, lm_shard=None,
-                 kv_device_seed: Optional[int] = None):
+                 kv_device_seed: Optional[int] = None, fuse_norms: Optional[bool] = None):
         import torch
 
         self.g, self.cfg, self.batch = g, cfg, batch
@@ -353,6 +354,14 @@ class Decoder:
         self.kpos = torch.arange(self.capacity, dtype=torch.int32, device=dev)
         self.rsqrt2 = torch.tensor([np.float32(1.0 / math.sqrt(2.0))], dtype=f32, device=dev)
         self.h, self.x = z(B, H), z(B, H)
+        # one sequence: the residual add + RMSNorm before gate|up, the PLE gate and
+        # the next layer's q(|k|v) run inside those projections (gq_add_norm_linear);
+        # the residual then alternates between h and h2 (the fused op must not
+        # write the row it reads). GQ_E2B_FUSE=0 keeps the separate norm launches.
+        if fuse_norms is None:
+            fuse_norms = batch == 1 and os.environ.get("GQ_E2B_FUSE", "1") != "0"
+        self.fuse_norms = bool(fuse_norms) and batch == 1
+        self.h2 = z(B, H)
         self.emb, self.proj, self.ple = z(B, L * P), z(B, L * P), z(B, L * P)
         self.q, self.qr, self.attn = z(B, dq), z(B, dq), z(B, dq)
         self.qkv = z(B, (c.heads_q + 2 * c.heads_kv) * c.global_head_dim)
@@ -394,6 +403,16 @@ class Decoder:
         S = p + 1
         # input norm of layer 0; later layers get theirs fused into the previous layer's last norm
         add("l0.input_norm", lib.gq_rms_norm, ctx, V(self.h), B, H, F("l0.input_ln"), eps, V(self.x), H)
+        fuse = self.fuse_norms
+        hc, halt = self.h, self.h2  # residual: current row, the other buffer
+
+        def fused(label, mode, w_norm, scale, w_norm2, w, w_up, b, b_off, y):
+            nonlocal hc, halt
+            add(label, lib.gq_add_norm_linear, ctx, mode, V(self.o), V(hc), H, F(w_norm), eps,
+                F(scale) if scale else None, F(w_norm2) if w_norm2 else None, V(halt), Q(w),
+                Q(w_up) if w_up else None, V(b) if b is not None else None, b_off, V(y))
+            hc, halt = halt, hc
+
         for i in range(L):
             pre = f"l{i}."
             dh = c.dh(i)
@@ -403,17 +422,29 @@ class Decoder:
             kvd = c.heads_kv * dh
             cstride = self.capacity * kvd
             # attention block (rust/src/model.rs:214-219, 233-300)
+            # the previous layer's closing norm (residual + PLE norm, layer scalar,
+            # this layer's input norm), fused into this layer's first projection
+            prev = f"l{i - 1}."
+            pro = fuse and i > 0
             if src == i:
                 # q|k|v in one GEMV, then the q and k norms + RoPE and the unweighted
                 # value norm (rust/src/model.rs:258-273) in one launch, k and v written
                 # straight into slot p of every sequence's cache
-                add(pre + "qkv_proj", lib.gq_linear, ctx, V(self.x), B, H, Q(pre + "qkv_proj"), V(self.qkv))
+                if pro:
+                    fused(pre + "qkv_proj", 0, prev + "ple_norm", prev + "layer_scalar", pre + "input_ln",
+                          pre + "qkv_proj", None, None, 0, self.qkv)
+                else:
+                    add(pre + "qkv_proj", lib.gq_linear, ctx, V(self.x), B, H, Q(pre + "qkv_proj"), V(self.qkv))
                 add(pre + "qkv_norm_rope", lib.gq_qkv_norm_rope, ctx, V(self.qkv), B, (c.heads_q + 2 * c.heads_kv) * dh,
                     c.heads_q, c.heads_kv, dh, F(pre + "q_norm"), F(pre + "k_norm"), eps, V(self.pos),
                     c_float(theta), rot, V(self.qr), c.heads_q * dh, c_void_p(kc.data_ptr() + 4 * p * kvd), cstride,
                     c_void_p(vc.data_ptr() + 4 * p * kvd), cstride)
             else:
-                add(pre + "q_proj", lib.gq_linear, ctx, V(self.x), B, H, Q(pre + "q_proj"), V(self.q))
+                if pro:
+                    fused(pre + "q_proj", 0, prev + "ple_norm", prev + "layer_scalar", pre + "input_ln",
+                          pre + "q_proj", None, None, 0, self.q)
+                else:
+                    add(pre + "q_proj", lib.gq_linear, ctx, V(self.x), B, H, Q(pre + "q_proj"), V(self.q))
                 add(pre + "q_norm_rope", lib.gq_head_norm_rope, ctx, V(self.q), B, c.heads_q, dh, F(pre + "q_norm"),
                     eps, V(self.pos), c_float(theta), rot, V(self.qr), c.heads_q * dh)
             add(pre + "attention", lib.gq_attention, ctx, V(self.qr), B, 1, c.heads_q, dh, V(kc), V(vc), S,
@@ -421,23 +452,34 @@ class Decoder:
                 GQ_ATTN_KPOS_IDENTITY, V(self.attn))
             add(pre + "o_proj", lib.gq_linear, ctx, V(self.attn), B, c.heads_q * dh, Q(pre + "o_proj"), V(self.o))
             # h = h + post_attn_norm(o), then x = pre_ffn_norm(h): one pass (rust/src/model.rs:219, 223)
-            add(pre + "post_attn", lib.gq_add_rms_norm_norm, ctx, V(self.h), V(self.o), B, H, F(pre + "post_attn_ln"),
-                eps, None, F(pre + "pre_ffn_ln"), V(self.h), V(self.x))
             # GeGLU MLP (rust/src/model.rs:221-227)
-            add(pre + "gate_up", lib.gq_linear_geglu, ctx, V(self.x), B, H, Q(pre + "gate"), Q(pre + "up"),
-                V(self.ff))
+            if fuse:
+                fused(pre + "gate_up", 1, pre + "post_attn_ln", None, pre + "pre_ffn_ln", pre + "gate", pre + "up",
+                      None, 0, self.ff)
+            else:
+                add(pre + "post_attn", lib.gq_add_rms_norm_norm, ctx, V(self.h), V(self.o), B, H,
+                    F(pre + "post_attn_ln"), eps, None, F(pre + "pre_ffn_ln"), V(self.h), V(self.x))
+                add(pre + "gate_up", lib.gq_linear_geglu, ctx, V(self.x), B, H, Q(pre + "gate"), Q(pre + "up"),
+                    V(self.ff))
             add(pre + "down", lib.gq_linear, ctx, V(self.ff), B, c.inter, Q(pre + "down"), V(self.o))
-            add(pre + "post_ffn", lib.gq_add_rms_norm, ctx, V(self.h), V(self.o), B, H, F(pre + "post_ffn_ln"), eps,
-                None, V(self.h))
-            # per-layer input injection + layer scalar (rust/src/model.rs:229-242)
-            add(pre + "ple_gate", lib.gq_linear_gelu_mul_cols, ctx, V(self.h), B, H, Q(pre + "ple_gate"),
-                V(self.ple), L * P, i * P, V(self.inj))
+            # h = h + post_ffn_norm(o); per-layer input injection + layer scalar (rust/src/model.rs:229-242)
+            if fuse:
+                fused(pre + "ple_gate", 2, pre + "post_ffn_ln", None, None, pre + "ple_gate", None, self.ple, i * P,
+                      self.inj)
+            else:
+                add(pre + "post_ffn", lib.gq_add_rms_norm, ctx, V(self.h), V(self.o), B, H, F(pre + "post_ffn_ln"),
+                    eps, None, V(self.h))
+                add(pre + "ple_gate", lib.gq_linear_gelu_mul_cols, ctx, V(self.h), B, H, Q(pre + "ple_gate"),
+                    V(self.ple), L * P, i * P, V(self.inj))
             add(pre + "ple_proj", lib.gq_linear, ctx, V(self.inj), B, P, Q(pre + "ple_proj"), V(self.o))
             # h = (h + ple_norm(inj)) * layer_scalar, then the next layer's input norm (or the
-            # final norm, rust/src/model.rs:183) of h: one pass
-            nxt = f"l{i + 1}.input_ln" if i + 1 < L else "final_norm"
-            add(pre + "ple_norm", lib.gq_add_rms_norm_norm, ctx, V(self.h), V(self.o), B, H, F(pre + "ple_norm"), eps,
-                F(pre + "layer_scalar"), F(nxt), V(self.h), V(self.x))
+            # final norm, rust/src/model.rs:183) of h: one pass (fused into the next layer's
+            # first projection when the norms are fused; the last one always here, into h)
+            if not fuse or i + 1 == L:
+                nxt = f"l{i + 1}.input_ln" if i + 1 < L else "final_norm"
+                add(pre + "ple_norm", lib.gq_add_rms_norm_norm, ctx, V(hc), V(self.o), B, H, F(pre + "ple_norm"),
+                    eps, F(pre + "layer_scalar"), F(nxt), V(self.h), V(self.x))
+                hc, halt = self.h, self.h2
         # lm_head with the soft-cap on the final-normed h (rust/src/model.rs:183-192)
         if self.peer is None:
             add("lm_head", lib.gq_linear_softcap, ctx, V(self.x), B, H, Q("lm_head"), c_float(c.lm_softcap),

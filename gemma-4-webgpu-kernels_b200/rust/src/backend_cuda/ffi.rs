@@ -166,6 +166,10 @@ extern "C" {
         w: *const f32, eps: f32, scale_by: *const f32, y: *mut f32) -> c_int;
     pub fn gq_add_rms_norm_norm(ctx: *mut GqCtx, residual: *const f32, x: *const f32, rows: i64, d: i64,
         w1: *const f32, eps: f32, scale_by: *const f32, w2: *const f32, h: *mut f32, xn: *mut f32) -> c_int;
+    // one decode row: residual add + RMSNorm fused into the projection that reads it
+    pub fn gq_add_norm_linear(ctx: *mut GqCtx, mode: i32, x: *const f32, residual: *const f32, k: i64,
+        w_norm: *const f32, eps: f32, scale_by: *const f32, w_norm2: *const f32, h_out: *mut f32,
+        w: *const GqQWeight, w_up: *const GqQWeight, b: *const f32, b_offset: i64, y: *mut f32) -> c_int;
     pub fn gq_head_norm_rope(ctx: *mut GqCtx, x: *const f32, t: i64, heads: i64, head_dim: i64, w: *const f32,
         eps: f32, positions: *const u32, theta: f32, rotary_dim: i64, y: *mut f32, y_tok_stride: i64) -> c_int;
     pub fn gq_qkv_norm_rope(ctx: *mut GqCtx, qkv: *const f32, t: i64, qkv_tok_stride: i64, hq: i64, hkv: i64,

@@ -416,6 +416,25 @@ int gq_add_rms_norm(gq_ctx *ctx, const float *residual, const float *x, int64_t 
 int gq_add_rms_norm_norm(gq_ctx *ctx, const float *residual, const float *x, int64_t rows, int64_t d, const float *w1,
                          float eps, const float *scale_by, const float *w2, float *h, float *xn);
 
+/* One decode row (m = 1): the residual add + RMSNorm that precedes a projection
+ * (rust/src/model.rs:219+223 before the MLP, :233 before the per-layer-input
+ * gate, :236 + the next layer's :214 before its q/k/v), fused into that
+ * projection's launch. h_out = (residual + rms_norm(x, w_norm)) * scale_by[0]
+ * (scale_by may be NULL), the row the projection reads is
+ * w_norm2 ? rms_norm(h_out, w_norm2) : h_out, and y = that row times w in
+ * `mode` 0 (gq_linear), 1 (gq_linear_geglu, w_up = up) or 2
+ * (gq_linear_gelu_mul_cols on b's columns from b_offset). h_out and the row
+ * equal gq_add_rms_norm / gq_add_rms_norm_norm bit for bit (k a multiple of 4,
+ * 16-byte aligned rows); y equals the CUDA-core GEMV's gq_linear of that row. Every
+ * CTA of the GEMV makes the row itself, so the separate norm launch goes away.
+ * Where that path does not apply (k not a multiple of 4 or above 4096, unaligned
+ * rows, a weight the streaming GEMV does not serve) the call runs the norm and
+ * the projection as their own calls, with the same results. k must equal w.k;
+ * h_out and y must not overlap x or residual (GQ_ERR_INVALID_ARGUMENT). */
+int gq_add_norm_linear(gq_ctx *ctx, int32_t mode, const float *x, const float *residual, int64_t k,
+                       const float *w_norm, float eps, const float *scale_by, const float *w_norm2, float *h_out,
+                       const gq_qweight *w, const gq_qweight *w_up, const float *b, int64_t b_offset, float *y);
+
 /* Backend::head_norm_rope (rust/src/backend.rs:148-154) and Backend::rope
  * (rust/src/backend.rs:118-119; CPU rust/src/backend_cpu.rs:248-268) on x [t, heads,
  * head_dim]: per-head weighted RMSNorm (head_norm_rope only), then the half-split

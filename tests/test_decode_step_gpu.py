@@ -343,6 +343,39 @@ def test_decode_step_graph_replay_matches_eager():
         g.close()
 
 
+@pytest.mark.parametrize("own_graph", [False, True])
+def test_decode_step_fused_norms_equal_separate(own_graph):
+    """One sequence: the residual + RMSNorm launches before gate|up, the PLE gate and
+    the next layer's q(|k|v) run inside those projections (gq_add_norm_linear). The
+    step matches the one with the separate norm launches (same norm arithmetic; the
+    PLE gate's GEMV variant differs, so to the GEMV bound) with three launches fewer
+    per layer (two in the last, whose closing norm feeds the lm_head), also
+    replayed from a graph."""
+    g = CudaBackend(0, own_stream=True)
+    try:
+        cfg = e2b.small_config(2048)
+        w = e2b.Weights(cfg, 11)
+        out, launches = [], []
+        for fuse in (False, True):
+            dec = e2b.Decoder(g, cfg, w, batch=1, cache_len=20, capacity=24, fuse_norms=fuse)
+            dec.set_ids([1500])
+            dec.run()
+            if own_graph:
+                graph = dec.record()
+                dec.logits.zero_()
+                g.flush()
+                g.replay(graph)
+                g.destroy_graph(graph)
+            out.append(dec.read(dec.logits))
+            launches.append(dec.launches)
+        assert launches[0] - launches[1] == 3 * cfg.layers - 1
+        assert rel(out[1], out[0]) <= 1e-5
+        want = e2b_ref.decode_step(cfg, w, [1500], 20, e2b_ref.kv_from_weights(cfg, w, 1, 20, 24))
+        check_logits(out[1], want)
+    finally:
+        g.close()
+
+
 _E2B_WEIGHTS = {}
 
 
