@@ -209,7 +209,6 @@ __global__ void __launch_bounds__(THREADS, THREADS == kThreads ? kResident : 1) 
   const float *xsrc = nullptr;
   if constexpr (PRO) {
     float *bo = reinterpret_cast<float *>(smem + L.pro_off), *br = bo + pro_k, *bw1 = br + pro_k, *bw2 = bw1 + pro_k;
-    float *inv_s = bw2 + pro_k;  // [2]
     const int n4 = a.K >> 2;
     const float4 one4 = make_float4(1.f, 1.f, 1.f, 1.f);
     for (int c = tid; c < n4; c += THREADS) {
@@ -220,33 +219,33 @@ __global__ void __launch_bounds__(THREADS, THREADS == kThreads ? kResident : 1) 
     }
     const float sc = a.ps ? __ldg(a.ps) : 1.0f;
     __syncthreads();
-    auto row_inv = [&](const float *v) {  // warp 0
+    // warp 0 alone forms the row (no block barrier between the two norms): lane l
+    // handles float4 chunks l, l + 32, ... of every row, the order in which the
+    // norm kernels accumulate their per-lane sums of squares
+    if (warp == 0) {
+      auto butterfly = [&](float v) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        return v;
+      };
+      auto inv_of = [&](float ss) { return __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, (float)a.K), a.peps))); };
       float ss = 0.0f;
       for (int c = lane; c < n4; c += 32) {
-        const float4 t = reinterpret_cast<const float4 *>(v)[c];
+        const float4 t = reinterpret_cast<const float4 *>(bo)[c];
         ss = __fadd_rn(ss, __fmul_rn(t.x, t.x));
         ss = __fadd_rn(ss, __fmul_rn(t.y, t.y));
         ss = __fadd_rn(ss, __fmul_rn(t.z, t.z));
         ss = __fadd_rn(ss, __fmul_rn(t.w, t.w));
       }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      return __fdiv_rn(1.0f, sqrtf(__fadd_rn(__fdiv_rn(ss, (float)a.K), a.peps)));
-    };
-    if (warp == 0) {
-      const float inv = row_inv(bo);
-      if (lane == 0) inv_s[0] = inv;
-    }
-    __syncthreads();
-    {
-      const float inv = inv_s[0];
-      const bool writer = blockIdx.x == 0 && blockIdx.y == 0;
+      const float inv = inv_of(butterfly(ss));
       auto one = [&](float xx, float ww, float rr) {
         float n = __fadd_rn(rr, __fmul_rn(__fmul_rn(xx, inv), ww));
         if (a.ps) n = __fmul_rn(n, sc);
         return n;
       };
-      for (int c = tid; c < n4; c += THREADS) {
+      const bool writer = blockIdx.x == 0 && blockIdx.y == 0;
+      float ss2 = 0.0f;
+      for (int c = lane; c < n4; c += 32) {
         const float4 o4 = reinterpret_cast<const float4 *>(bo)[c];
         const float4 w4 = reinterpret_cast<const float4 *>(bw1)[c];
         const float4 r4 = reinterpret_cast<const float4 *>(br)[c];
@@ -254,28 +253,24 @@ __global__ void __launch_bounds__(THREADS, THREADS == kThreads ? kResident : 1) 
                                       one(o4.w, w4.w, r4.w));
         reinterpret_cast<float4 *>(br)[c] = h4;
         if (writer) reinterpret_cast<float4 *>(a.ph)[c] = h4;
+        ss2 = __fadd_rn(ss2, __fmul_rn(h4.x, h4.x));
+        ss2 = __fadd_rn(ss2, __fmul_rn(h4.y, h4.y));
+        ss2 = __fadd_rn(ss2, __fmul_rn(h4.z, h4.z));
+        ss2 = __fadd_rn(ss2, __fmul_rn(h4.w, h4.w));
+      }
+      if (a.pw2) {
+        const float inv2 = inv_of(butterfly(ss2));
+        for (int c = lane; c < n4; c += 32) {
+          const float4 h4 = reinterpret_cast<const float4 *>(br)[c];
+          const float4 w4 = reinterpret_cast<const float4 *>(bw2)[c];
+          reinterpret_cast<float4 *>(bo)[c] =
+              make_float4(__fmul_rn(__fmul_rn(h4.x, inv2), w4.x), __fmul_rn(__fmul_rn(h4.y, inv2), w4.y),
+                          __fmul_rn(__fmul_rn(h4.z, inv2), w4.z), __fmul_rn(__fmul_rn(h4.w, inv2), w4.w));
+        }
       }
     }
     __syncthreads();
-    if (a.pw2) {
-      if (warp == 0) {
-        const float inv2 = row_inv(br);
-        if (lane == 0) inv_s[1] = inv2;
-      }
-      __syncthreads();
-      const float inv2 = inv_s[1];
-      for (int c = tid; c < n4; c += THREADS) {
-        const float4 h4 = reinterpret_cast<const float4 *>(br)[c];
-        const float4 w4 = reinterpret_cast<const float4 *>(bw2)[c];
-        reinterpret_cast<float4 *>(bo)[c] =
-            make_float4(__fmul_rn(__fmul_rn(h4.x, inv2), w4.x), __fmul_rn(__fmul_rn(h4.y, inv2), w4.y),
-                        __fmul_rn(__fmul_rn(h4.z, inv2), w4.z), __fmul_rn(__fmul_rn(h4.w, inv2), w4.w));
-      }
-      __syncthreads();
-      xsrc = bo;
-    } else {
-      xsrc = br;
-    }
+    xsrc = a.pw2 ? bo : br;
   }
   auto ldx4 = [&](const float *p) -> float4 {
     if constexpr (PRO) return *reinterpret_cast<const float4 *>(p);
