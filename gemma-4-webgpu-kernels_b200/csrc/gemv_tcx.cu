@@ -591,6 +591,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int t = 0; t < 4; ++t) {
           const int tok = t0 + t;
           if (!nok || tok >= a.M) continue;
+          if (KS > 1) {  // this split's exact partial sums, finalised after the cluster barrier
+#pragma unroll
+            for (int h = 0; h < NW; ++h) part[((size_t)h * a.M + tok) * a.tile_rows + nl] = T[h][t];
+            continue;
+          }
           float o;
           if (tok_bad[tok]) {
             o = __int_as_float(0x7fc00000);
@@ -832,7 +837,7 @@ int tcx_max_tile(int64_t m, int nw, bool wa) {
 // One tile of weight rows per CTA (tile_rows <= 0: the default, N / num_sms
 // rounded up to 16). Weights taller than num_sms tiles run as row slices of
 // num_sms * tile_rows rows. ks > 1 splits the K-blocks over a cluster of ks
-// CTAs per tile (one slice only, limb rows as A). Rings sized to the SM's
+// CTAs per tile (one slice only, either operand layout). Rings sized to the SM's
 // shared memory for the CTA's own K-blocks: the limb ring gets up to ~half of
 // it, the weight rings the rest.
 bool tcx_plan_with(const gq_ctx *ctx, const gq_qweight *w, int64_t m, int nw, bool wa, int tile_rows, int ks,
@@ -856,7 +861,7 @@ bool tcx_plan_with(const gq_ctx *ctx, const gq_qweight *w, int64_t m, int nw, bo
   p.gx = (int)((p.slice_rows + p.tile_rows - 1) / p.tile_rows);
   p.kblocks = (int)((w->k + kKB - 1) / kKB);
   // split-K: a cluster of ks CTAs per tile, every split non-empty, one slice
-  if (ks < 1 || ks > 8 || (ks > 1 && (wa || p.slice_rows < w->n || (int64_t)p.gx * ks > ctx->num_sms))) return false;
+  if (ks < 1 || ks > 8 || (ks > 1 && (p.slice_rows < w->n || (int64_t)p.gx * ks > ctx->num_sms))) return false;
   p.ksplit = ks;
   p.kb_per = (p.kblocks + ks - 1) / ks;
   if (ks > 1 && (int64_t)(ks - 1) * p.kb_per >= p.kblocks) return false;
@@ -943,12 +948,17 @@ bool tcx_plan_with(const gq_ctx *ctx, const gq_qweight *w, int64_t m, int nw, bo
 // count (and tile) when that plan fits.
 bool tcx_plan(const gq_ctx *ctx, const gq_qweight *w, int64_t m, int nw, bool wa, TcxPlan &p) {
   const char *e = getenv("GQ_TCX_SPLIT");
-  if (e && *e && !wa) {
+  if (e && *e) {
     int ks = atoi(e), tile = 0;
     const char *c = strchr(e, ':');
     if (c) tile = atoi(c + 1);
     if (ks >= 1 && tcx_plan_with(ctx, w, m, nw, wa, tile, ks, p)) return true;
-  } else if (!wa) {
+  } else if (wa) {
+    // weights as A (128-row tiles): split K until the clusters cover the SMs
+    const int64_t gx = (w->n + 127) / 128;
+    for (int ks = (int)std::min<int64_t>(8, std::max<int64_t>(1, ctx->num_sms / gx)); ks > 1; --ks)
+      if (tcx_plan_with(ctx, w, m, nw, wa, 128, ks, p)) return true;
+  } else {
     const int kb = (int)((w->k + kKB - 1) / kKB);
     if (kb >= 24) {
       if (tcx_plan_with(ctx, w, m, nw, wa, 64, 4, p) || tcx_plan_with(ctx, w, m, nw, wa, 32, 2, p)) return true;

@@ -158,6 +158,7 @@ def test_short_m_split_k_is_exact(g, monkeypatch, n, k, bits, signed, m, split):
     output is bit-identical to the unsplit kernel's (and within the FFMA bound
     of the oracle)."""
     monkeypatch.setenv("GQ_DECODE_TC", "2")
+    monkeypatch.setenv("GQ_TCX_WA", "0")
     w = synth.random_qweight(3700 + n + k + bits, n, k, bits, signed)
     x = synth.normal(3701 + m, m * k).reshape(m, k)
     gw, gx = g.quant_tensor(w), g.tensor(x, x.shape)
@@ -170,8 +171,36 @@ def test_short_m_split_k_is_exact(g, monkeypatch, n, k, bits, signed, m, split):
     assert rel_l2(got, oracle.linear(x, w)) <= REL_L2
 
 
-def test_short_m_split_k_fused_modes(g, monkeypatch):
+# (rows, K, bits, signed, M, splits) with the weights as the A operand (128-row
+# tiles): every plan below fits, so each runs split (grid = tiles x splits <= SMs)
+SPLITS_WA = [(1536, 6144, 2, False, 64, "8"), (1536, 6144, 2, False, 8, "8"), (2048, 1536, 8, True, 64, "6"),
+             (2048, 1536, 8, True, 5, "4"), (6144, 1536, 4, False, 40, "3"), (300, 640, 8, False, 16, "5"),
+             (1536, 2048, 8, True, 33, "8"), (77, 256, 4, False, 7, "2"), (2560, 1536, 8, True, 64, "6")]
+
+
+@pytest.mark.parametrize("n,k,bits,signed,m,split", SPLITS_WA)
+def test_short_m_split_k_weights_as_a_is_exact(g, monkeypatch, n, k, bits, signed, m, split):
+    """The same cluster split-K with weight rows as the MMA's A operand: each
+    thread's int64 limb sums for its weight row go to the shared partials, and
+    the cluster's finalisation gives the unsplit kernel's output bit for bit."""
     monkeypatch.setenv("GQ_DECODE_TC", "2")
+    monkeypatch.setenv("GQ_TCX_WA", "1")
+    w = synth.random_qweight(3750 + n + k + bits, n, k, bits, signed)
+    x = synth.normal(3751 + m, m * k).reshape(m, k)
+    gw, gx = g.quant_tensor(w), g.tensor(x, x.shape)
+    monkeypatch.setenv("GQ_TCX_SPLIT", "1")
+    base = g.readback(g.linear(gx, gw))
+    for sp in (split, ""):  # the forced split, then the default (automatic) one
+        monkeypatch.setenv("GQ_TCX_SPLIT", sp)
+        got = g.readback(g.linear(gx, gw))
+        assert np.array_equal(got, base), sp
+    assert rel_l2(base, oracle.linear(x, w)) <= REL_L2
+
+
+@pytest.mark.parametrize("wa", ["0", "1"])
+def test_short_m_split_k_fused_modes(g, monkeypatch, wa):
+    monkeypatch.setenv("GQ_DECODE_TC", "2")
+    monkeypatch.setenv("GQ_TCX_WA", wa)
     k = 1536
     x = synth.normal(3801, 40 * k).reshape(40, k)
     gx = g.tensor(x, x.shape)
@@ -184,7 +213,7 @@ def test_short_m_split_k_fused_modes(g, monkeypatch):
     wl = synth.random_qweight(3806, 2000, k, 8, True)
     gwl = g.quant_tensor(wl)
     outs = []
-    for split in ("1", "", "2:128", "4:32", "8:128"):
+    for split in ("1", "", "2:128", "4:32", "8:128", "3"):
         monkeypatch.setenv("GQ_TCX_SPLIT", split)
         outs.append((g.readback(g.linear_geglu(gx, wg, wu)),
                      g.readback(g.linear_gelu_mul_cols(gx, gwp, gb, 768)),
