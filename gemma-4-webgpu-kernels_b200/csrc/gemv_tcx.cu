@@ -49,6 +49,7 @@ constexpr int kMaxIss = 3;
 constexpr int kExpWarps = 4;
 constexpr int kMaxTok = 64;
 constexpr int kMaxK = 8192;
+constexpr int kXinSlots = 4;  // in-kernel limbs: 16-value groups a thread holds in registers
 
 struct TcxArgs {
   int M, K, N;
@@ -63,7 +64,9 @@ struct TcxArgs {
   const int *xexp;        // [M] per-row exponent s_m (X = rint(x * 2^s_m))
   const long long *sumx;  // [M] sum_k X
   const uint32_t *bad;    // [M] non-finite x row
-  const uint8_t *limbs;   // [kblocks][xa_rows][128 B] pre-swizzled A tiles
+  const uint8_t *limbs;   // [kblocks][xa_rows][128 B] pre-swizzled A tiles (pre-pass)
+  const float *x;         // [M, K] activations, read when xin
+  int xin;                // 1: the CTA makes its own limb tiles from x (no pre-pass)
   int tile_rows;          // MMA N: multiple of 16
   int mh;                 // 0: one M=64 MMA (<= 16 tokens); 1 or 2: M=128 halves
   int wa;                 // 1: weights are the A operand (M = 128 rows), limb rows the B operand (N = lrows)
@@ -90,7 +93,7 @@ __host__ __device__ inline TcxSmem tcx_layout(int xa_stages, int xa_tile, int ra
   L.mma_off = o;  o += (uint32_t)mma_stages * (uint32_t)mma_bytes;
   L.sc_off = o;   o += (uint32_t)((sc_bytes + 127) & ~127);
   L.bar_off = o;  o += (2 * kMaxRaw + 2 * kMaxMma + 2 * kMaxXa + 2 * kMaxIss + 2) * 8;
-  L.misc_off = o; o += 64 + kMaxTok * 24;
+  L.misc_off = o; o += 64 + kMaxTok * 36;
   L.total = o + 1024;
   return L;
 }
@@ -110,8 +113,6 @@ __device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
 __device__ __forceinline__ bool wait_phase(uint64_t *bar, uint32_t parity) {
   return gqd::mbar_try_wait(bar, parity) || gqd::mbar_wait_bounded(bar, parity);
 }
-// barrier among the 4 expander/epilogue warps only
-__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, %0;" ::"r"(kExpWarps * 32) : "memory"); }
 // all threads of every CTA of the cluster (release / acquire at cluster scope)
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
@@ -121,6 +122,12 @@ __device__ __forceinline__ uint32_t cluster_addr(const void *p, uint32_t rank) {
   uint32_t ra;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(gqd::smem_u32(p)), "r"(rank));
   return ra;
+}
+// a 32-bit value at a shared::cluster address
+__device__ __forceinline__ uint32_t ld_cluster_u32(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.shared::cluster.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+  return v;
 }
 // two 64-bit values at a shared::cluster address (16-byte aligned)
 __device__ __forceinline__ void ld_cluster_v2s64(uint32_t addr, long long &v0, long long &v1) {
@@ -277,6 +284,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   double *tok_pw = reinterpret_cast<double *>(smem + L.misc_off + 64);  // [kMaxTok] 2^-s
   long long *tok_zc = reinterpret_cast<long long *>(tok_pw + kMaxTok);  // [kMaxTok] ZP * sum X
   uint32_t *tok_bad = reinterpret_cast<uint32_t *>(tok_zc + kMaxTok);   // [kMaxTok]
+  uint32_t *rmax = tok_bad + kMaxTok;                                     // [kMaxTok] max|x| bits (xin)
+  int *tok_s = reinterpret_cast<int *>(rmax + kMaxTok);                   // [kMaxTok] exponent s (xin)
+  long long *tok_zs = reinterpret_cast<long long *>(tok_s + kMaxTok);     // [kMaxTok] split's ZP * sum X
   // split-K partials [NW][M][tile_rows] (int64), over the rings once every MMA has completed
   long long *part = reinterpret_cast<long long *>(smem);
 
@@ -304,6 +314,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     gqd::fence_mbar_init();
   }
   if (tid == 0) *abort_flag = 0;
+  if (tid < kMaxTok) {  // in-kernel limbs: row maxima and sums start at zero
+    rmax[tid] = 0u;
+    tok_zs[tid] = 0;
+  }
   __syncthreads();
 
   auto issue = [&](int r, int slot) {  // raw stage r (K-blocks r*kbr .. +kbr-1) into `slot`
@@ -440,6 +454,134 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  // ---- in-kernel limbs (xin): the CTA turns x into the resident A tiles of its
+  // own K-blocks, with the pre-pass kernel's arithmetic and layout. The row
+  // exponent needs max|x| over the whole row: each K split publishes its row
+  // maxima in shared memory and reads the others' over the cluster. Zero points
+  // are removed per split (exact integers), so the finalisation adds no term. ----
+  if (a.xin) {
+    // A row's groups (16 values each) occupy Gp lane slots: G rounded up to a power
+    // of two below 32, to a multiple of 32 above, so every row starts an aligned
+    // segment of S lanes and its maxima and sums reduce inside the segment. Thread
+    // t holds slots t, t + 256, t + 512 and t + 768 (the planner keeps M * Gp <= 1024),
+    // all loaded before the first use.
+    const int G = kblocks * 8;
+    const int Gp = G <= 8 ? 8 : G <= 16 ? 16 : (G + 31) & ~31;
+    const int S = min(Gp, 32), ngp = a.M * Gp;
+    const unsigned seg = S == 32 ? 0xffffffffu : (((1u << S) - 1u) << (lane & ~(S - 1)));
+    const bool lead = (lane & (S - 1)) == 0;
+    const int kx0 = kbase * kKB;
+    float4 v[kXinSlots][4];
+#pragma unroll
+    for (int i = 0; i < kXinSlots; ++i) {
+      const int slot = i * kThreads + tid, m = slot / Gp, j = slot - m * Gp, k = kx0 + j * 16;
+      if (slot < ngp && j < G && k < a.K) {
+        const float4 *src = reinterpret_cast<const float4 *>(a.x + (size_t)m * a.K + k);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) v[i][q] = __ldg(src + q);
+      } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) v[i][q] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    }
+    // keep the loaded values in registers until pass 2 (no reload after the barriers)
+#pragma unroll
+    for (int i = 0; i < kXinSlots; ++i)
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        asm volatile("" : "+f"(v[i][q].x), "+f"(v[i][q].y), "+f"(v[i][q].z), "+f"(v[i][q].w));
+#pragma unroll
+    for (int i = 0; i < kXinSlots; ++i) {
+      const int slot = i * kThreads + tid;
+      if (i * kThreads + warp * 32 >= ngp) break;  // warp-uniform: segments are whole
+      uint32_t mx = 0u;
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        mx = max(mx, max(max(__float_as_uint(v[i][q].x) & 0x7fffffffu, __float_as_uint(v[i][q].y) & 0x7fffffffu),
+                         max(__float_as_uint(v[i][q].z) & 0x7fffffffu, __float_as_uint(v[i][q].w) & 0x7fffffffu)));
+      mx = __reduce_max_sync(seg, mx);
+      if (lead && slot < ngp) atomicMax(&rmax[slot / Gp], mx);  // ngp is a multiple of S: segments are whole
+    }
+    __syncthreads();
+    if (KS > 1) cluster_sync_all();  // every split's row maxima are in place
+    if (tid < a.M) {
+      uint32_t mb = rmax[tid];
+      for (int q = 0; q < KS; ++q)
+        if (q != sidx) mb = max(mb, ld_cluster_u32(cluster_addr(&rmax[tid], (uint32_t)q)));
+      int e = 0;
+      if (mb != 0u && mb < 0x7f800000u) frexpf(__uint_as_float(mb), &e);
+      tok_s[tid] = 30 - e;
+      tok_bad[tid] = mb >= 0x7f800000u ? 1u : 0u;  // inf or NaN in the row
+      tok_pw[tid] = __longlong_as_double((long long)(1023 - (30 - e)) << 52);  // 2^-s
+    }
+    __syncthreads();
+    // pass 2: X = rint(x 2^s), four balanced byte digits, K permuted like the
+    // widened codes, written as the swizzled A tiles; row sums of X
+#pragma unroll
+    for (int i = 0; i < kXinSlots; ++i) {
+      const int slot = i * kThreads + tid, m = slot / Gp, j = slot - m * Gp;
+      if (i * kThreads + warp * 32 >= ngp) break;
+      long long part = 0;
+      if (slot < ngp && j < G) {
+        const int kb = j >> 3, c = j & 7;
+        const int sx = tok_s[m];
+        const float f1 = __int_as_float((sx / 2 + 127) << 23), f2 = __int_as_float((sx - sx / 2 + 127) << 23);
+        int X[16];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          X[4 * q + 0] = __float2int_rn(__fmul_rn(__fmul_rn(v[i][q].x, f1), f2));
+          X[4 * q + 1] = __float2int_rn(__fmul_rn(__fmul_rn(v[i][q].y, f1), f2));
+          X[4 * q + 2] = __float2int_rn(__fmul_rn(__fmul_rn(v[i][q].z, f1), f2));
+          X[4 * q + 3] = __float2int_rn(__fmul_rn(__fmul_rn(v[i][q].w, f1), f2));
+        }
+        uint32_t wv[16];
+#pragma unroll
+        for (int p = 0; p < 16; ++p) {
+          const int xv = X[perm16<BITS>(p)];
+          part += xv;
+          wv[p] = ((uint32_t)xv + 0x00808080u) ^ 0x00808080u;
+        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint32_t t01a = prmt(wv[4 * q], wv[4 * q + 1], 0x5140), t23a = prmt(wv[4 * q + 2], wv[4 * q + 3], 0x5140);
+          const uint32_t t01b = prmt(wv[4 * q], wv[4 * q + 1], 0x7362), t23b = prmt(wv[4 * q + 2], wv[4 * q + 3], 0x7362);
+          wv[4 * q] = prmt(t01a, t23a, 0x5410);
+          wv[4 * q + 1] = prmt(t01a, t23a, 0x7632);
+          wv[4 * q + 2] = prmt(t01b, t23b, 0x5410);
+          wv[4 * q + 3] = prmt(t01b, t23b, 0x7632);
+        }
+        uint8_t *tile = xa + (size_t)kb * xa_tile;
+#pragma unroll
+        for (int l = 0; l < 4; ++l) {
+          const int r = 4 * m + l;
+          *reinterpret_cast<uint4 *>(tile + r * 128 + ((c ^ (r & 7)) << 4)) =
+              make_uint4(wv[l], wv[4 + l], wv[8 + l], wv[12 + l]);
+        }
+      }
+      // |part| < 2^34: its 21-bit low and high halves sum exactly in 32 bits
+      const int lo = __reduce_add_sync(seg, (int)(part & 0x1fffff));
+      const int hi = __reduce_add_sync(seg, (int)(part >> 21));
+      if (lead && slot < ngp)
+        atomicAdd(reinterpret_cast<unsigned long long *>(&tok_zs[m]),
+                  (unsigned long long)(((long long)hi << 21) + (long long)lo));
+    }
+    {  // limb rows past 4M read as zero
+      const int pad = (int)(xa_tile >> 7) - 4 * a.M;
+      for (int i = tid; i < kblocks * pad * 8; i += kThreads) {
+        const int kb = i / (pad * 8), rem = i - kb * pad * 8;
+        *reinterpret_cast<uint4 *>(xa + (size_t)kb * xa_tile + (size_t)(4 * a.M) * 128 + (size_t)rem * 16) =
+            make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+    fence_proxy_async();  // the tiles are read by the tensor cores (async proxy)
+    __syncthreads();
+    if (tid < a.M) {
+      const long long z = ZP * tok_zs[tid];
+      tok_zc[tid] = KS > 1 ? 0 : z;   // unsplit: removed in the epilogue
+      tok_zs[tid] = KS > 1 ? z : 0;   // split: removed from this split's partials
+    }
+  }
+
   if (warp == 0) {
     // ---- TMA producer: limb tiles and weight refills, in K-block order ----
     if (lane == 0 && !*abort_flag) {
@@ -457,13 +599,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           issued = r + 1;
         }
         if (DIRECT) ord = base_ord + jj;
-        const int xslot = own * XI + (ord & (XI - 1));
-        if (ord >= XI && !wait_phase(&xa_empty[xslot], (uint32_t)((ord >> XL) - 1) & 1u)) {
-          ok = false;
-          break;
+        if (!a.xin) {
+          const int xslot = own * XI + (ord & (XI - 1));
+          if (ord >= XI && !wait_phase(&xa_empty[xslot], (uint32_t)((ord >> XL) - 1) & 1u)) {
+            ok = false;
+            break;
+          }
+          issue_x(xslot, g);
+          xi = g + 1;
         }
-        issue_x(xslot, g);
-        xi = g + 1;
         if (++jj == kbr) {
           jj = 0;
           ++r;
@@ -503,8 +647,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int ng = DIRECT ? min(kbr, kblocks - u * kbr) : 1;
         ok = wait_phase(DIRECT ? &raw_full[slot] : &mma_full[slot], (uint32_t)par);
         for (int j = 0; j < ng && ok; ++j) {
-          const int xslot = iss * XI + (ord & (XI - 1));
-          ok = wait_phase(&xa_full[xslot], (uint32_t)(ord >> XL) & 1u);
+          // limb tile of this K-block: resident tile g (xin) or the issuer's ring slot
+          const int xslot = a.xin ? (DIRECT ? u * kbr + j : u) : iss * XI + (ord & (XI - 1));
+          if (!a.xin) ok = wait_phase(&xa_full[xslot], (uint32_t)(ord >> XL) & 1u);
           ++ord;
           if (!ok) break;
           tc_fence_after();
@@ -531,7 +676,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
           first = false;
-          tc_commit(&xa_empty[xslot]);
+          if (!a.xin) tc_commit(&xa_empty[xslot]);
         }
         if (!ok) break;
         tc_commit(DIRECT ? &raw_empty[slot] : &mma_empty[slot]);
@@ -543,92 +688,103 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_commit(&done_bar[iss]);
       if (!gqd::mbar_wait_bounded(&done_bar[iss], 0)) *abort_flag = 1;
     }
-  } else {
-    // ---- warps 4-7: the rest of the widening, then the epilogue ----
-    if (!DIRECT) {
-      bool ok = exp_ok && !*abort_flag;
-      while (ok && er < total_raw) ok = expand_stage();
-      if (!ok) *abort_flag = 1;
+  } else if (!DIRECT) {
+    // ---- warps 4-7: the rest of the widening ----
+    bool ok = exp_ok && !*abort_flag;
+    while (ok && er < total_raw) ok = expand_stage();
+    if (!ok) *abort_flag = 1;
+  }
+
+  // ---- epilogue: all eight warps. Warp w reads TMEM lane quarter w % 4; the two
+  // warps of a quarter take alternate column (or token) groups, and each group's
+  // TMEM loads are all issued before one wait. ----
+  if (!a.xin && tid < a.M) {
+    tok_pw[tid] = __longlong_as_double((long long)(1023 - a.xexp[tid]) << 52);  // 2^-s
+    tok_zc[tid] = ZP * a.sumx[tid];
+    tok_bad[tid] = a.bad[tid];
+    tok_zs[tid] = 0;
+  }
+  __syncthreads();
+  // y of token tok, tile row nl (column n) from its exact sums (t0v: the weight, t1v: the up weight)
+  auto finish = [&](long long t0v, long long t1v, int tok, int nl, int n) -> float {
+    if (tok_bad[tok]) return __int_as_float(0x7fc00000);
+    const double pwt = tok_pw[tok];
+    const long long zct = tok_zc[tok];
+    const float v0 = __fmul_rn((float)((double)(t0v - zct) * pwt), scb[nl]);
+    if (MODE == 1) {
+      const float v1 = __fmul_rn((float)((double)(t1v - zct) * pwt), scb[a.tile_rows + nl]);
+      return __fmul_rn(gqd::gelu_tanh(v0), v1);
+    } else if (MODE == 2) {
+      return __fmul_rn(gqd::gelu_tanh(v0), a.bs[(size_t)tok * a.b_stride + a.b_off + n]);
+    } else if (MODE == 3) {
+      return a.cap > 0.0f ? __fmul_rn(a.cap, tanhf(__fdiv_rn(v0, a.cap))) : v0;
     }
-    if (et < a.M) {
-      tok_pw[et] = __longlong_as_double((long long)(1023 - a.xexp[et]) << 52);  // 2^-s
-      tok_zc[et] = ZP * a.sumx[et];
-      tok_bad[et] = a.bad[et];
-    }
-    epi_sync();
-    const int quarter = warp & 3, limb = lane & 3;
+    return v0;
+  };
+  {
+    const int quarter = warp & 3, half = warp >> 2;
     bool ok = !*abort_flag && wait_phase(sc_bar, 0u);
     for (int i = 0; i < NI; ++i) ok = ok && wait_phase(&acc_full[i], 0u);
     if (WA && __all_sync(0xffffffffu, ok)) {
-      // Thread et owns weight row et (TMEM lane et); columns 4*tok + limb hold the
-      // limb dot products of token tok, recombined here in int64.
+      // Thread (quarter, lane) owns weight row nl (TMEM lane nl); columns 4*tok + limb
+      // hold the limb dot products of token tok, recombined here in int64. The two
+      // warps of a quarter take alternate groups of 8 tokens.
       tc_fence_after();
-      const int nl = et, n = n_begin + nl;
+      const int nl = quarter * 32 + lane, n = n_begin + nl;
       const bool nok = n < n_end;
-      const float sc0 = scb[nl], sc1 = NW == 2 ? scb[a.tile_rows + nl] : 0.0f;
-      for (int t0 = 0; t0 < a.M; t0 += 4) {
-        long long T[NW][4];
+      for (int t0 = 8 * half; t0 < a.M; t0 += 16) {
+        long long T[NW][2][4];
 #pragma unroll
-        for (int h = 0; h < NW; ++h) {
-          uint32_t d[kMaxIss][16];
-          const uint32_t col = (uint32_t)(h * a.lrows + 4 * t0) + ((uint32_t)(quarter * 32) << 16);
+        for (int h = 0; h < NW; ++h)
 #pragma unroll
-          for (int i = 0; i < kMaxIss; ++i)
-            if (i < NI) tmem_ld16_nowait(tmem + col + (uint32_t)(i * acc_cols), d[i]);
+          for (int j = 0; j < 2; ++j)
 #pragma unroll
-          for (int t = 0; t < 4; ++t) T[h][t] = 0;
+            for (int t = 0; t < 4; ++t) T[h][j][t] = 0;
+        for (int i = 0; i < NI; ++i) {
+          uint32_t d[NW][2][16];
 #pragma unroll
-          for (int i = 0; i < kMaxIss; ++i)
-            if (i < NI) {
-              tmem_wait_ld16(d[i]);
+          for (int h = 0; h < NW; ++h)
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+              if (t0 + 4 * j < a.M)
+                tmem_ld16_nowait(tmem + (uint32_t)(i * acc_cols + h * a.lrows + 4 * (t0 + 4 * j)) +
+                                     ((uint32_t)(quarter * 32) << 16),
+                                 d[h][j]);
+#pragma unroll
+          for (int h = 0; h < NW; ++h)
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              tmem_wait_ld16(d[h][j]);
 #pragma unroll
               for (int t = 0; t < 4; ++t)
 #pragma unroll
-                for (int l = 0; l < 4; ++l) T[h][t] += (long long)(int32_t)d[i][4 * t + l] << (8 * l);
+                for (int l = 0; l < 4; ++l) T[h][j][t] += (long long)(int32_t)d[h][j][4 * t + l] << (8 * l);
             }
         }
 #pragma unroll
-        for (int t = 0; t < 4; ++t) {
-          const int tok = t0 + t;
-          if (!nok || tok >= a.M) continue;
-          if (KS > 1) {  // this split's exact partial sums, finalised after the cluster barrier
+        for (int j = 0; j < 2; ++j)
 #pragma unroll
-            for (int h = 0; h < NW; ++h) part[((size_t)h * a.M + tok) * a.tile_rows + nl] = T[h][t];
-            continue;
-          }
-          float o;
-          if (tok_bad[tok]) {
-            o = __int_as_float(0x7fc00000);
-          } else {
-            const double pwt = tok_pw[tok];
-            const long long zct = tok_zc[tok];
-            const float v0 = __fmul_rn((float)((double)(T[0][t] - zct) * pwt), sc0);
-            if (MODE == 1) {
-              const float v1 = __fmul_rn((float)((double)(T[NW - 1][t] - zct) * pwt), sc1);
-              o = __fmul_rn(gqd::gelu_tanh(v0), v1);
-            } else if (MODE == 2) {
-              o = __fmul_rn(gqd::gelu_tanh(v0), a.bs[(size_t)tok * a.b_stride + a.b_off + n]);
-            } else if (MODE == 3) {
-              o = a.cap > 0.0f ? __fmul_rn(a.cap, tanhf(__fdiv_rn(v0, a.cap))) : v0;
-            } else {
-              o = v0;
+          for (int t = 0; t < 4; ++t) {
+            const int tok = t0 + 4 * j + t;
+            if (!nok || tok >= a.M) continue;
+            if (KS > 1) {  // this split's exact partial sums, finalised after the cluster barrier
+#pragma unroll
+              for (int h = 0; h < NW; ++h) part[((size_t)h * a.M + tok) * a.tile_rows + nl] = T[h][j][t] - tok_zs[tok];
+              continue;
             }
+            a.y[(size_t)tok * a.ldy + a.y_col0 + n] = finish(T[0][j][t], T[NW - 1][j][t], tok, nl, n);
           }
-          a.y[(size_t)tok * a.ldy + a.y_col0 + n] = o;
-        }
       }
     } else if (!WA && __all_sync(0xffffffffu, ok)) {
       tc_fence_after();
+      const int limb = lane & 3;
+      const bool b1 = (lane & 1) != 0, b2 = (lane & 2) != 0;
       for (int hh = 0; hh < MH; ++hh) {
         // M=64: lane quarter q holds limb rows 16q.. in lanes 0-15 (tokens 4q..4q+3);
         // M=128: lane quarter q of half hh holds limb rows 128hh + 32q + lane.
         const int tok = a.mh == 0 ? 4 * quarter + ((lane >> 2) & 3) : 32 * hh + 8 * quarter + (lane >> 2);
         const bool lane_ok = (a.mh != 0 || lane < 16) && tok < a.M;
-        const int tk = min(tok, a.M - 1);
-        const double pwt = tok_pw[tk];
-        const long long zct = tok_zc[tk];
-        const bool badt = tok_bad[tk] != 0;
-        for (int c0 = 0; c0 < a.tile_rows; c0 += 8) {
+        for (int c0 = 8 * half; c0 < a.tile_rows; c0 += 16) {
           long long T[NW][2];
 #pragma unroll
           for (int h = 0; h < NW; ++h) {
@@ -637,24 +793,37 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int i = 0; i < kMaxIss; ++i)
               if (i < NI) tmem_ld8_nowait(tmem + col + (uint32_t)(i * MH * NW * a.tile_rows), d[i]);
-            int32_t dsum[8];
+            uint32_t r[8];
 #pragma unroll
-            for (int c = 0; c < 8; ++c) dsum[c] = 0;
+            for (int c = 0; c < 8; ++c) r[c] = 0;
 #pragma unroll
             for (int i = 0; i < kMaxIss; ++i)
               if (i < NI) {
                 tmem_wait_ld8(d[i]);
 #pragma unroll
-                for (int c = 0; c < 8; ++c) dsum[c] += (int32_t)d[i][c];
+                for (int c = 0; c < 8; ++c) r[c] += d[i][c];
               }
-            T[h][0] = T[h][1] = 0;
+            // The four lanes of a token hold limbs 0-3 of rows c0..c0+7: two 4x4
+            // transposes inside the lane group leave lane `limb` with the four limb
+            // sums of rows c0 + limb (r[0..3]) and c0 + 4 + limb (r[4..7]).
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {
-              long long v = (long long)dsum[c] << (8 * limb);
-              v += __shfl_xor_sync(0xffffffffu, v, 1);
-              v += __shfl_xor_sync(0xffffffffu, v, 2);
-              if (c == limb) T[h][0] = v;
-              if (c == 4 + limb) T[h][1] = v;
+            for (int q = 0; q < 8; q += 4) {
+              uint32_t t;
+              t = __shfl_xor_sync(0xffffffffu, b1 ? r[q] : r[q + 1], 1);
+              if (b1) r[q] = t; else r[q + 1] = t;
+              t = __shfl_xor_sync(0xffffffffu, b1 ? r[q + 2] : r[q + 3], 1);
+              if (b1) r[q + 2] = t; else r[q + 3] = t;
+              t = __shfl_xor_sync(0xffffffffu, b2 ? r[q] : r[q + 2], 2);
+              if (b2) r[q] = t; else r[q + 2] = t;
+              t = __shfl_xor_sync(0xffffffffu, b2 ? r[q + 1] : r[q + 3], 2);
+              if (b2) r[q + 1] = t; else r[q + 3] = t;
+            }
+#pragma unroll
+            for (int hr = 0; hr < 2; ++hr) {
+              long long v = 0;
+#pragma unroll
+              for (int l = 0; l < 4; ++l) v += (long long)(int32_t)r[4 * hr + l] << (8 * l);
+              T[h][hr] = v;
             }
           }
 #pragma unroll
@@ -664,33 +833,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!lane_ok || n >= n_end) continue;
             if (KS > 1) {  // this split's exact partial sums, finalised after the cluster barrier
 #pragma unroll
-              for (int h = 0; h < NW; ++h) part[((size_t)h * a.M + tok) * a.tile_rows + nl] = T[h][hr];
+              for (int h = 0; h < NW; ++h) part[((size_t)h * a.M + tok) * a.tile_rows + nl] = T[h][hr] - tok_zs[tok];
               continue;
             }
-            float o;
-            if (badt) {
-              o = __int_as_float(0x7fc00000);
-            } else {
-              const float v0 = __fmul_rn((float)((double)(T[0][hr] - zct) * pwt), scb[nl]);
-              if (MODE == 1) {
-                const float v1 = __fmul_rn((float)((double)(T[NW - 1][hr] - zct) * pwt), scb[a.tile_rows + nl]);
-                o = __fmul_rn(gqd::gelu_tanh(v0), v1);
-              } else if (MODE == 2) {
-                o = __fmul_rn(gqd::gelu_tanh(v0), a.bs[(size_t)tok * a.b_stride + a.b_off + n]);
-              } else if (MODE == 3) {
-                o = a.cap > 0.0f ? __fmul_rn(a.cap, tanhf(__fdiv_rn(v0, a.cap))) : v0;
-              } else {
-                o = v0;
-              }
-            }
-            a.y[(size_t)tok * a.ldy + a.y_col0 + n] = o;
+            a.y[(size_t)tok * a.ldy + a.y_col0 + n] = finish(T[0][hr], T[NW - 1][hr], tok, nl, n);
           }
         }
       }
     } else {
       *abort_flag = 1;
     }
-    tc_fence_before();
   }
 
   tc_fence_before();
@@ -733,25 +885,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int e = 0; e < 2; ++e) {
           const int nle = nl + e, n = n_begin + nle;
           if (nle >= r_hi) break;
-          float o;
-          if (tok_bad[tok]) {
-            o = __int_as_float(0x7fc00000);
-          } else {
-            const double pwt = tok_pw[tok];
-            const long long zct = tok_zc[tok];
-            const float v0 = __fmul_rn((float)((double)(T[0][e] - zct) * pwt), scb[nle]);
-            if (MODE == 1) {
-              const float v1 = __fmul_rn((float)((double)(T[NW - 1][e] - zct) * pwt), scb[a.tile_rows + nle]);
-              o = __fmul_rn(gqd::gelu_tanh(v0), v1);
-            } else if (MODE == 2) {
-              o = __fmul_rn(gqd::gelu_tanh(v0), a.bs[(size_t)tok * a.b_stride + a.b_off + n]);
-            } else if (MODE == 3) {
-              o = a.cap > 0.0f ? __fmul_rn(a.cap, tanhf(__fdiv_rn(v0, a.cap))) : v0;
-            } else {
-              o = v0;
-            }
-          }
-          a.y[(size_t)tok * a.ldy + a.y_col0 + n] = o;
+          a.y[(size_t)tok * a.ldy + a.y_col0 + n] = finish(T[0][e], T[NW - 1][e], tok, nle, n);
         }
       }
     }
@@ -824,6 +958,7 @@ struct TcxPlan {
   int tile_rows, mh, gx, slice_rows, kblocks, kbr, raw_stages, mma_stages, xa_stages, xi, raw_bytes, mma_bytes,
       xa_tile, issuers, tmem_cols;
   int ksplit, kb_per;
+  int xin;  // limb tiles made in the GEMV (all of a CTA's K-blocks resident), no pre-pass
   size_t smem;
 };
 
@@ -871,7 +1006,7 @@ bool tcx_plan_with(const gq_ctx *ctx, const gq_qweight *w, int64_t m, int nw, bo
   const size_t budget = ctx->smem_optin - 1024;
   // issuers: TMEM columns, work units; then the limb ring: XI >= 2 slots each
   const int units_hint = direct ? kbl : kbl;
-  p.issuers = std::max(1, std::min(std::min(kMaxIss, units_hint), 512 / acc_cols));
+  p.issuers = wa ? 1 : std::max(1, std::min(std::min(kMaxIss, units_hint), 512 / acc_cols));
   const size_t xa_budget = std::min<size_t>(budget / 2 + 16384, 131072);
   while (p.issuers > 1 && (size_t)p.issuers * 2 * p.xa_tile > xa_budget) --p.issuers;
   p.xi = (int)std::max<size_t>(2, std::min<size_t>(kMaxXa / p.issuers, xa_budget / ((size_t)p.issuers * p.xa_tile)));
@@ -933,7 +1068,45 @@ bool tcx_plan_with(const gq_ctx *ctx, const gq_qweight *w, int64_t m, int nw, bo
                                  sc_bytes);
     if ((size_t)nw * (size_t)m * (size_t)p.tile_rows * 8 > L.sc_off) return false;
   }
-  return p.tmem_cols <= 512 && p.smem <= budget;
+  p.xin = 0;
+  if (p.tmem_cols > 512 || p.smem > budget) return false;
+  // In-kernel limbs (GQ_TCX_XIN=1) when a CTA's share of x fits its threads'
+  // registers (four 16-value groups each): its K-blocks' limb tiles all stay
+  // resident (the weight rings shrink to make room) and the pre-pass launch goes
+  // away. Measured slower on B200 than the pre-pass (config-2 sweep at M = 8:
+  // 2.63 against 2.38 ms): a %globaltimer trace puts ~0.5 us on each converted
+  // group slot in the run-once conversion code, more than the launch it saves.
+  const char *xe = getenv("GQ_TCX_XIN");
+  const int gk = kbl * 8, gp = gk <= 8 ? 8 : gk <= 16 ? 16 : (gk + 31) / 32 * 32;  // lane slots of a row
+  if (xe && *xe == '1' && m * gp <= kThreads * kXinSlots) {
+    TcxPlan q = p;
+    q.xa_stages = kbl;
+    for (;;) {
+      const TcxSmem Lq = tcx_layout(q.xa_stages, q.xa_tile, q.raw_stages, q.raw_bytes, q.mma_stages, q.mma_bytes,
+                                    sc_bytes);
+      if (Lq.total <= budget && (ks == 1 || (size_t)nw * (size_t)m * (size_t)q.tile_rows * 8 <= Lq.sc_off)) {
+        q.smem = Lq.total;
+        q.xin = 1;
+        p = q;
+        break;
+      }
+      // shrink a weight ring, keeping every ring that wraps a multiple of the issuer count
+      int nm = q.mma_stages - 1;
+      nm -= nm % q.issuers;
+      if (!direct && nm >= std::max(2, q.issuers)) {
+        q.mma_stages = nm;
+        continue;
+      }
+      int nr = q.raw_stages - 1;
+      if (direct && nr < total_raw) nr -= nr % q.issuers;
+      if (nr >= std::min(2, total_raw) && (!direct || nr >= total_raw || nr >= q.issuers)) {
+        q.raw_stages = nr;
+        continue;
+      }
+      break;  // does not fit: keep the pre-pass plan
+    }
+  }
+  return true;
 }
 
 // Plan choice. The per-CTA cost grows with its K-block count (each K-block is
@@ -990,14 +1163,18 @@ cudaError_t launch_limbs(gq_ctx *ctx, const float *x, int64_t m, int64_t k, int6
                    (int)k, (int)kp, (int)m, xa_rows, limbs, xexp, sumx, bad);
 }
 
-// Operand layout. Default: limb rows as A (M = 64 / 128) and weight tiles of
-// 16..256 rows as N, one tile per SM. GQ_TCX_WA=1 selects weights as A (128-row
-// tiles, limb rows as N up to 256): full-size MMAs but 8-12x fewer CTAs; measured
-// slower on the E2B sweep (M = 32: 4.87 vs 3.35 ms, M = 64: 6.92 vs 4.13 ms).
-bool tcx_weights_as_a(int64_t m) {
+// Operand layout. Limb rows as A (M = 64 / 128) with weight tiles of 16..256
+// rows as N, one tile per SM; or weights as A (128-row tiles, limb rows as N up
+// to 256) with K split over a cluster so the grid still covers the SMs. Measured
+// per E2B projection (graph-replayed chains, one B200): the weights-as-A split
+// wins for one weight with long rows at small M (M = 8: 2-bit down 15.6 -> 12.5 us,
+// o_proj 12.6 -> 10.6 us; M = 16 likewise) and loses for the fused gate|up pair
+// (14.7 -> 24.7 us) and at M >= 32 (M = 64 gate|up 20.6 -> 39.1 us). GQ_TCX_WA=1|0
+// forces either layout.
+bool tcx_weights_as_a(int64_t m, const gq_qweight *w, int nw) {
   const char *e = getenv("GQ_TCX_WA");
-  (void)m;
-  return e && *e == '1';
+  if (e && *e) return *e == '1';
+  return nw == 1 && m <= 16 && w->k >= 2048;
 }
 
 // Rows [r0, r0 + n) of a weight as a weight of its own (same layout).
@@ -1019,7 +1196,7 @@ bool gq_gemv_tcx_supported(gq_ctx *ctx, const gq_qweight *w, const float *x, int
   if (w->row_bytes % 16 != 0 || (uintptr_t)w->bytes % 16 != 0 || (uintptr_t)x % 16 != 0) return false;
   if (gq_encode_fn() == nullptr) return false;
   TcxPlan p;
-  return tcx_plan(ctx, w, m, nw, tcx_weights_as_a(m), p);
+  return tcx_plan(ctx, w, m, nw, tcx_weights_as_a(m, w, nw), p);
 }
 
 int gq_gemv_tcx_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const gq_qweight *w, const gq_qweight *w2,
@@ -1027,24 +1204,31 @@ int gq_gemv_tcx_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const g
                        int64_t y_col0) {
   const int nw = (mode == 1) ? 2 : 1;
   TcxPlan p;
-  if (!tcx_plan(ctx, w, m, nw, tcx_weights_as_a(m), p))
+  if (!tcx_plan(ctx, w, m, nw, tcx_weights_as_a(m, w, nw), p))
     return gq_fail(ctx, GQ_ERR_UNSUPPORTED, "gemv_tcx: no stage configuration fits");
-  const int64_t kp = (int64_t)p.kblocks * kKB;
-  const int xa_rows = p.xa_tile / 128;
-  const size_t limb_bytes = ((size_t)p.kblocks * p.xa_tile + 255) & ~size_t(255);
-  void *wsp = nullptr;
-  int rc = gq_workspace(ctx, limb_bytes + (size_t)m * 16 + 256, &wsp);
-  if (rc != GQ_OK) return rc;
-  uint8_t *limbs = static_cast<uint8_t *>(wsp);
-  long long *sumx = reinterpret_cast<long long *>(limbs + limb_bytes);
-  int *xexp = reinterpret_cast<int *>(sumx + m);
-  uint32_t *bad = reinterpret_cast<uint32_t *>(xexp + m);
-  if (w->bits == 4) {
-    GQ_CUDA_TRY(ctx, launch_limbs<4>(ctx, x, m, w->k, kp, xa_rows, limbs, xexp, sumx, bad));
-  } else if (w->bits == 2) {
-    GQ_CUDA_TRY(ctx, launch_limbs<2>(ctx, x, m, w->k, kp, xa_rows, limbs, xexp, sumx, bad));
-  } else {
-    GQ_CUDA_TRY(ctx, launch_limbs<8>(ctx, x, m, w->k, kp, xa_rows, limbs, xexp, sumx, bad));
+  int rc = GQ_OK;
+  uint8_t *limbs = nullptr;
+  long long *sumx = nullptr;
+  int *xexp = nullptr;
+  uint32_t *bad = nullptr;
+  if (!p.xin) {  // the limb pre-pass: one launch before the GEMV
+    const int64_t kp = (int64_t)p.kblocks * kKB;
+    const int xa_rows = p.xa_tile / 128;
+    const size_t limb_bytes = ((size_t)p.kblocks * p.xa_tile + 255) & ~size_t(255);
+    void *wsp = nullptr;
+    rc = gq_workspace(ctx, limb_bytes + (size_t)m * 16 + 256, &wsp);
+    if (rc != GQ_OK) return rc;
+    limbs = static_cast<uint8_t *>(wsp);
+    sumx = reinterpret_cast<long long *>(limbs + limb_bytes);
+    xexp = reinterpret_cast<int *>(sumx + m);
+    bad = reinterpret_cast<uint32_t *>(xexp + m);
+    if (w->bits == 4) {
+      GQ_CUDA_TRY(ctx, launch_limbs<4>(ctx, x, m, w->k, kp, xa_rows, limbs, xexp, sumx, bad));
+    } else if (w->bits == 2) {
+      GQ_CUDA_TRY(ctx, launch_limbs<2>(ctx, x, m, w->k, kp, xa_rows, limbs, xexp, sumx, bad));
+    } else {
+      GQ_CUDA_TRY(ctx, launch_limbs<8>(ctx, x, m, w->k, kp, xa_rows, limbs, xexp, sumx, bad));
+    }
   }
   for (int64_t r0 = 0; r0 < w->n; r0 += p.slice_rows) {
     const int64_t rows = std::min<int64_t>(p.slice_rows, w->n - r0);
@@ -1070,6 +1254,8 @@ int gq_gemv_tcx_launch(gq_ctx *ctx, int mode, const float *x, int64_t m, const g
     a.sumx = sumx;
     a.bad = bad;
     a.limbs = limbs;
+    a.x = x;
+    a.xin = p.xin;
     a.tile_rows = p.tile_rows;
     a.mh = p.mh;
     a.wa = p.wa;

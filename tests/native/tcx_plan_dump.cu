@@ -1,6 +1,7 @@
 // Host-only harness for tests/test_tcx_plan_cpu.py: includes the short-M GEMV's
 // translation unit and prints its plans (no GPU is touched). Each line:
 // name m nw tile ks  tile_rows gx kb_per kblocks slice_rows issuers xi xa_stages tmem_cols smem part_bytes sc_off ok
+//   xin wa raw_stages mma_stages
 #include "../../gemma-4-webgpu-kernels_b200/csrc/gemv_tcx.cu"
 
 #include <cstdio>
@@ -30,12 +31,13 @@ int main() {
       w.group_size = sh.k;
       w.row_bytes = sh.bits == 8 ? sh.k : sh.k * sh.bits / 8;
       // tile 0 = default; ks 0 = the library's own choice (tcx_plan)
+      for (int wa : {0, 1})
       for (int tile : {0, 16, 32, 64, 128})
-        for (int ks : {0, 1, 2, 3, 4, 8}) {
-          if (ks == 0 && tile != 0) continue;
+        for (int ks : {0, 1, 2, 3, 4, 6, 8}) {
+          if ((ks == 0 || wa) && tile != 0) continue;
           TcxPlan p{};
-          const bool ok = ks == 0 ? tcx_plan(&ctx, &w, m, sh.nw, false, p)
-                                  : tcx_plan_with(&ctx, &w, m, sh.nw, false, tile, ks, p);
+          const bool ok = ks == 0 ? tcx_plan(&ctx, &w, m, sh.nw, wa != 0, p)
+                                  : tcx_plan_with(&ctx, &w, m, sh.nw, wa != 0, tile, ks, p);
           size_t sc_off = 0, part = 0;
           if (ok) {
             const TcxSmem L = tcx_layout(p.xa_stages, p.xa_tile, p.raw_stages, p.raw_bytes, p.mma_stages, p.mma_bytes,
@@ -43,9 +45,9 @@ int main() {
             sc_off = L.sc_off;
             part = (size_t)sh.nw * (size_t)m * (size_t)p.tile_rows * 8;
           }
-          printf("%s %d %d %d %d  %d %d %d %d %d %d %d %d %d %zu %zu %zu %d\n", sh.name, m, sh.nw, tile, ks, p.tile_rows,
-                 p.gx, p.kb_per, p.kblocks, p.slice_rows, p.issuers, p.xi, p.xa_stages, p.tmem_cols, p.smem, part,
-                 sc_off, ok ? 1 : 0);
+          printf("%s %d %d %d %d  %d %d %d %d %d %d %d %d %d %zu %zu %zu %d  %d %d %d %d\n", sh.name, m, sh.nw, tile, ks,
+                 p.tile_rows, p.gx, p.kb_per, p.kblocks, p.slice_rows, p.issuers, p.xi, p.xa_stages, p.tmem_cols,
+                 p.smem, part, sc_off, ok ? 1 : 0, ok ? p.xin : 0, wa, p.raw_stages, p.mma_stages);
         }
     }
   return 0;

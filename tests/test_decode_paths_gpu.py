@@ -197,6 +197,89 @@ def test_short_m_split_k_weights_as_a_is_exact(g, monkeypatch, n, k, bits, signe
     assert rel_l2(base, oracle.linear(x, w)) <= REL_L2
 
 
+# (rows, K, bits, signed, M, weights-as-A, splits): plans whose CTAs convert x into
+# their own limb tiles (no pre-pass launch), split and unsplit, both layouts
+XIN = [(2048, 1536, 8, True, 8, "0", ""), (6144, 1536, 4, False, 8, "0", ""), (1536, 6144, 2, False, 8, "0", ""),
+       (1536, 2048, 8, True, 16, "0", ""), (256, 1536, 8, True, 5, "0", ""), (1536, 256, 8, True, 64, "0", ""),
+       (2048, 1536, 8, True, 8, "1", ""), (1536, 6144, 2, False, 33, "1", ""), (300, 640, 8, False, 16, "1", ""),
+       (2048, 1536, 8, True, 64, "1", "6"), (77, 256, 4, False, 7, "0", ""), (40000, 1536, 8, True, 6, "0", "")]
+
+
+@pytest.mark.parametrize("n,k,bits,signed,m,wa,split", XIN)
+def test_short_m_in_kernel_limbs_equal_the_pre_pass(g, monkeypatch, n, k, bits, signed, m, wa, split):
+    """Limb tiles made inside the GEMV (row maxima exchanged over the K-split
+    cluster, zero points removed per split) give the pre-pass kernel's output bit
+    for bit: same exponent, same digits, same integer sums. Rows with an outlier,
+    tiny values and a non-finite entry included."""
+    monkeypatch.setenv("GQ_DECODE_TC", "2")
+    monkeypatch.setenv("GQ_TCX_WA", wa)
+    monkeypatch.setenv("GQ_TCX_SPLIT", split)
+    w = synth.random_qweight(3900 + n + k + bits + m, n, k, bits, signed)
+    x = synth.normal(3901 + m, m * k).reshape(m, k)
+    x[0, 5] = 300.0
+    x[m - 1] *= 1e-30
+    if m > 2:
+        x[1, k - 1] = np.inf
+    gw, gx = g.quant_tensor(w), g.tensor(x, x.shape)
+    monkeypatch.setenv("GQ_TCX_XIN", "0")
+    base = g.readback(g.linear(gx, gw))
+    monkeypatch.setenv("GQ_TCX_XIN", "1")
+    got = g.readback(g.linear(gx, gw))
+    assert np.array_equal(got, base, equal_nan=True)
+    ok = np.ones(m, bool)
+    if m > 2:
+        ok[1] = False
+        assert np.isnan(got.reshape(m, n)[1]).all()
+    assert rel_l2(got.reshape(m, n)[ok], oracle.linear(x[ok], w)) <= REL_L2
+
+
+def test_short_m_in_kernel_limbs_fused_modes(g, monkeypatch):
+    monkeypatch.setenv("GQ_DECODE_TC", "2")
+    k, m = 1536, 8
+    x = synth.normal(3951, m * k).reshape(m, k)
+    gx = g.tensor(x, x.shape)
+    wg = g.quant_tensor(synth.random_qweight(3952, 6144, k, 4, False))
+    wu = g.quant_tensor(synth.random_qweight(3953, 6144, k, 4, False))
+    gwp = g.quant_tensor(synth.random_qweight(3954, 256, k, 8, True))
+    b = synth.normal(3955, m * 8960).reshape(m, 8960)
+    gb = g.tensor(b, b.shape)
+    gwl = g.quant_tensor(synth.random_qweight(3956, 2000, k, 8, True))
+    outs = []
+    for wa in ("0", "1"):
+        monkeypatch.setenv("GQ_TCX_WA", wa)
+        for xin in ("0", "1"):
+            monkeypatch.setenv("GQ_TCX_XIN", xin)
+            outs.append((g.readback(g.linear_geglu(gx, wg, wu)),
+                         g.readback(g.linear_gelu_mul_cols(gx, gwp, gb, 768)),
+                         g.readback(g.linear_softcap(gx, gwl, 30.0))))
+    for o in outs[1:]:
+        for a, b0 in zip(o, outs[0]):
+            assert np.array_equal(a, b0)
+
+
+def test_short_m_in_kernel_limbs_launch_one_kernel(g, monkeypatch):
+    """With the in-kernel limbs an M = 8 projection is one launch (no limb pre-pass)."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+    monkeypatch.setenv("GQ_DECODE_TC", "2")
+    k, m = 1536, 8
+    x = synth.normal(3961, m * k).reshape(m, k)
+    gx = g.tensor(x, x.shape)
+    gw = g.quant_tensor(synth.random_qweight(3962, 2048, k, 8, True))
+    g.linear(gx, gw)
+    g.flush()
+    names = {}
+    for xin in ("1", "0"):
+        monkeypatch.setenv("GQ_TCX_XIN", xin)
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            g.linear(gx, gw)
+            g.flush()
+            torch.cuda.synchronize()
+        names[xin] = [e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA]
+    assert any("gemv_tcx_kernel" in nm for nm in names["1"]) and not any("xlimbs" in nm for nm in names["1"])
+    assert any("xlimbs" in nm for nm in names["0"])
+
+
 @pytest.mark.parametrize("wa", ["0", "1"])
 def test_short_m_split_k_fused_modes(g, monkeypatch, wa):
     monkeypatch.setenv("GQ_DECODE_TC", "2")
