@@ -411,6 +411,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     return true;
   };
 
+  // TMEM before the dependency wait (warp 1 has nothing else to do here): it
+  // can only wait on kernels that run ahead of this one, never on a dependent
+  // (the dependents launch after this CTA's launch_dependents, which follows).
+  // Measured: config-2 sweep at M = 8 2.29 -> 2.23 ms. (The same move in the
+  // M <= 2 GEMV cost its lm_head 40 us inside the M = 1 decode step, so that one
+  // allocates after the wait.)
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(gqd::smem_u32(tmem_slot)),
+                 "r"(a.tmem_cols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
   // ---- before the dependency wait: weights and scales only ----
   const int G_pre = DIRECT ? 0 : min(MS, kblocks);
   int issued = 0;
@@ -442,13 +454,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   gqd::griddep_launch_dependents();
   gqd::griddep_wait();  // the limbs come from the pre-pass
-
-  if (warp == 1) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(gqd::smem_u32(tmem_slot)),
-                 "r"(a.tmem_cols)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
