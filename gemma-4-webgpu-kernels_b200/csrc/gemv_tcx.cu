@@ -117,6 +117,9 @@ __device__ __forceinline__ bool wait_phase(uint64_t *bar, uint32_t parity) {
 __device__ __forceinline__ void cluster_sync_all() {
   asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
 }
+// the same barrier in two halves, so independent work can run between them
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire;" ::: "memory"); }
 // the shared::cluster address of this CTA's shared-memory location p in cluster CTA `rank`
 __device__ __forceinline__ uint32_t cluster_addr(const void *p, uint32_t rank) {
   uint32_t ra;
@@ -161,13 +164,30 @@ __global__ void xlimbs_kernel(const float *x, int K, int Kp, int M, int xa_rows,
   __shared__ float wmax[8];
   __shared__ uint32_t wbad[8];
   __shared__ long long wsum[8];
+  // each thread's 16-value groups (K <= 8192: at most two) stay in registers
+  // from the max pass to the conversion
+  constexpr int kG = kMaxK / 16 / kThreads;
+  float4 v[kG][4];
   float mx = 0.0f;
   uint32_t b = 0;
-  for (int k4 = tid; k4 < K / 4; k4 += kThreads) {
-    const float4 v = __ldg(xr + k4);
-    mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-    b |= !(isfinite(v.x) && isfinite(v.y) && isfinite(v.z) && isfinite(v.w));
+#pragma unroll
+  for (int j = 0; j < kG; ++j) {
+    const int gi = tid + j * kThreads;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) v[j][q] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (gi * 16 < K) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) v[j][q] = __ldg(xr + gi * 4 + q);
+    }
   }
+#pragma unroll
+  for (int j = 0; j < kG; ++j)
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float4 u = v[j][q];
+      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(u.x), fabsf(u.y)), fmaxf(fabsf(u.z), fabsf(u.w))));
+      b |= !(isfinite(u.x) && isfinite(u.y) && isfinite(u.z) && isfinite(u.w));
+    }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
@@ -190,23 +210,24 @@ __global__ void xlimbs_kernel(const float *x, int K, int Kp, int M, int xa_rows,
   const int s = 30 - e;
   const float f1 = __int_as_float((s / 2 + 127) << 23), f2 = __int_as_float((s - s / 2 + 127) << 23);
   long long part = 0;
-  for (int gi = tid; gi < Kp / 16; gi += kThreads) {
+#pragma unroll
+  for (int j = 0; j < kG; ++j) {
+    const int gi = tid + j * kThreads;
+    if (gi >= Kp / 16) break;
     int X[16];
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (gi * 16 < K) v = __ldg(xr + gi * 4 + q);
-      X[4 * q + 0] = __float2int_rn(__fmul_rn(__fmul_rn(v.x, f1), f2));
-      X[4 * q + 1] = __float2int_rn(__fmul_rn(__fmul_rn(v.y, f1), f2));
-      X[4 * q + 2] = __float2int_rn(__fmul_rn(__fmul_rn(v.z, f1), f2));
-      X[4 * q + 3] = __float2int_rn(__fmul_rn(__fmul_rn(v.w, f1), f2));
+      X[4 * q + 0] = __float2int_rn(__fmul_rn(__fmul_rn(v[j][q].x, f1), f2));
+      X[4 * q + 1] = __float2int_rn(__fmul_rn(__fmul_rn(v[j][q].y, f1), f2));
+      X[4 * q + 2] = __float2int_rn(__fmul_rn(__fmul_rn(v[j][q].z, f1), f2));
+      X[4 * q + 3] = __float2int_rn(__fmul_rn(__fmul_rn(v[j][q].w, f1), f2));
     }
     uint32_t wv[16];
 #pragma unroll
     for (int p = 0; p < 16; ++p) {
-      const int v = X[perm16<BITS>(p)];
-      part += v;
-      wv[p] = ((uint32_t)v + 0x00808080u) ^ 0x00808080u;
+      const int xv = X[perm16<BITS>(p)];
+      part += xv;
+      wv[p] = ((uint32_t)xv + 0x00808080u) ^ 0x00808080u;
     }
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
@@ -896,9 +917,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncthreads();
   }
+  // No CTA leaves (releasing its shared memory) while a cluster peer may still
+  // read it: every thread has finished its reads of the peers' partials here, so
+  // it arrives now and waits only at the exit, after the rest of the tail.
+  if (KS > 1) cluster_arrive();
   if (!*abort_flag && (a.peers.n > 0 || a.peers.signal)) gqd::push_to_peers(a.y, a.peers, a.M, a.ldy, a.y_col0 + c_lo, a.y_col0 + c_hi);
-  // no CTA leaves (releasing its shared memory) while a cluster peer may still read it
-  if (KS > 1) cluster_sync_all();
   if (*abort_flag) {
     if (tid == 0) gqd::report(a.err, GQ_DEVERR_WAIT_TIMEOUT);
     __syncthreads();
@@ -907,6 +930,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(a.tmem_cols) : "memory");
   }
+  if (KS > 1) cluster_wait();
 }
 
 }  // namespace
