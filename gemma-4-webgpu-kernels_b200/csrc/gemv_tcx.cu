@@ -20,9 +20,15 @@
 //    per SM are processed as row slices, one launch each, sharing the limbs;
 //  * the tile's scales come into shared memory by one bulk copy issued before
 //    the grid dependency wait;
-//  * epilogue warp q drains lane quarter q, recombines the limbs of each token in
-//    int64, removes the zero point exactly and converts once:
-//    y = f32(T * 2^-s_m) * scale[n].
+//  * all eight warps run the epilogue (warp w drains TMEM lane quarter w % 4),
+//    recombine the limbs of each token in int64, remove the zero point exactly
+//    and convert once: y = f32(T * 2^-s_m) * scale[n];
+//  * long rows split K over a thread-block cluster whose CTAs add their exact
+//    int64 partials over distributed shared memory (either operand layout; the
+//    weights-as-A one, 128-row tiles as the MMA's A, serves one long weight at
+//    M <= 16);
+//  * optionally (GQ_TCX_XIN=1) each CTA makes its own limb tiles from x instead
+//    of the pre-pass, bit for bit the same.
 // The limb matrix is small and shared by every CTA, so after the first CTAs it
 // streams from L2; the weights stream from HBM once for all M rows.
 // Every wait is bounded (GQ_DEVERR_WAIT_TIMEOUT); TMA copies in flight are
